@@ -1,0 +1,316 @@
+"""ctypes bindings for the parity checkers. TEST INFRASTRUCTURE ONLY.
+
+* ``Restated``: oracle/_build/libg4oracle.so, our C restatement (g4d_oracle.c). Built on
+  demand with gcc when missing, so it is available on any box.
+* ``Reference``: oracle/_ref/libg4ref.so, the reference's own CPU code (built here from the
+  read-only reference checkout; the prebuilt .so travels with the tree). ``available()``
+  says whether it is present.
+
+Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg may import this module.
+"""
+from __future__ import annotations
+
+import ctypes
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+RESTATED_SO = HERE / "_build" / "libg4oracle.so"
+REF_SO = HERE / "_ref" / "libg4ref.so"
+
+_u32p = ctypes.POINTER(ctypes.c_uint32)
+_vp = ctypes.c_void_p
+
+
+def _ptr(a):
+    return a.ctypes.data_as(_vp) if a is not None else None
+
+
+class Sampling(ctypes.Structure):
+    _fields_ = [("temperature", ctypes.c_float), ("top_p", ctypes.c_float), ("top_k", ctypes.c_int),
+                ("repetition_penalty", ctypes.c_float), ("has_seed", ctypes.c_int),
+                ("seed", ctypes.c_uint64)]
+
+    @classmethod
+    def greedy(cls):
+        return cls(0.0, 1.0, 0, 1.0, 0, 0)
+
+
+def build_restated(force: bool = False) -> Path:
+    if force or not RESTATED_SO.exists():
+        subprocess.run(["make", "-s", "-C", str(HERE), "restate"], check=True)
+    return RESTATED_SO
+
+
+def build_reference(ref_root: str = "/root/reference") -> Path | None:
+    """Builds oracle/_ref when the reference checkout is present; returns the .so or None."""
+    if Path(ref_root).is_dir():
+        subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REF_ROOT={ref_root}"], check=True)
+    return REF_SO if REF_SO.exists() else None
+
+
+_restated = None
+
+
+def restated_lib():
+    global _restated
+    if _restated is None:
+        lib = ctypes.CDLL(str(build_restated()))
+        lib.g4o_last_error.restype = ctypes.c_char_p
+        lib.g4o_open.restype = _vp
+        lib.g4o_open.argtypes = [ctypes.c_char_p, ctypes.c_int, ctypes.c_uint32, ctypes.c_int]
+        lib.g4o_close.argtypes = [_vp]
+        lib.g4o_info.argtypes = [_vp, _vp]
+        lib.g4o_length.argtypes = [_vp]
+        lib.g4o_length.restype = ctypes.c_uint32
+        lib.g4o_truncate.argtypes = [_vp, ctypes.c_uint32]
+        lib.g4o_forward.argtypes = [_vp, ctypes.c_uint32, ctypes.c_uint32, _vp, _vp]
+        lib.g4o_int4_gemm.argtypes = [_vp, _vp, _vp, ctypes.c_uint32, ctypes.c_uint32, _vp,
+                                      ctypes.c_uint32, _vp]
+        lib.g4o_int8_gemv.argtypes = [_vp, _vp, _vp, ctypes.c_uint32, ctypes.c_uint32, _vp, _vp]
+        lib.g4o_rmsnorm.argtypes = [_vp, _vp, ctypes.c_uint32, ctypes.c_float, _vp]
+        lib.g4o_attention.argtypes = [_vp, _vp, _vp] + [ctypes.c_uint32] * 6 + [ctypes.c_float, _vp]
+        lib.g4o_round_f16.restype = ctypes.c_float
+        lib.g4o_round_f16.argtypes = [ctypes.c_float]
+        lib.g4o_round_bf16.restype = ctypes.c_float
+        lib.g4o_round_bf16.argtypes = [ctypes.c_float]
+        lib.g4o_gelu_tanh.restype = ctypes.c_float
+        lib.g4o_gelu_tanh.argtypes = [ctypes.c_float]
+        lib.g4o_splitmix64.restype = ctypes.c_uint64
+        lib.g4o_splitmix64.argtypes = [ctypes.c_uint64]
+        lib.g4o_seed_for.restype = ctypes.c_uint64
+        lib.g4o_seed_for.argtypes = [ctypes.POINTER(Sampling), ctypes.c_int]
+        lib.g4o_validate_sampling.argtypes = [ctypes.POINTER(Sampling)]
+        lib.g4o_sample_token.restype = ctypes.c_uint32
+        lib.g4o_sample_token.argtypes = [_vp, ctypes.c_uint32, ctypes.POINTER(Sampling), ctypes.c_uint64]
+        lib.g4o_argmax.restype = ctypes.c_uint32
+        lib.g4o_argmax.argtypes = [_vp, ctypes.c_uint32]
+        lib.g4o_evaluate_verification.argtypes = [_vp, ctypes.c_int, _vp, ctypes.c_int, ctypes.c_uint32,
+                                                  ctypes.POINTER(Sampling), ctypes.c_uint64, _vp, _vp, _vp]
+        lib.g4o_mt64_seed.argtypes = [_vp, ctypes.c_uint64]
+        lib.g4o_mt64_uniform_float.restype = ctypes.c_float
+        lib.g4o_mt64_uniform_float.argtypes = [_vp]
+        lib.g4o_spec_generate.argtypes = [_vp, _vp, _vp, ctypes.c_int, ctypes.c_int, ctypes.c_int,
+                                          ctypes.POINTER(Sampling), ctypes.c_double, ctypes.c_int,
+                                          ctypes.c_int64, _vp, ctypes.c_int, ctypes.c_double,
+                                          ctypes.c_uint64, _vp, _vp, ctypes.c_int, _vp]
+        _restated = lib
+    return _restated
+
+
+KV_FP16, KV_BF16, KV_FP32 = 0, 1, 2
+
+
+class RestatedModel:
+    """Our C restatement of CpuReferenceRunner, with a truncatable KV cache."""
+
+    def __init__(self, path, kv_mode=KV_FP16, max_ctx=4096, cache_dequant=True):
+        self.lib = restated_lib()
+        self.h = self.lib.g4o_open(str(path).encode(), kv_mode, max_ctx, 1 if cache_dequant else 0)
+        if not self.h:
+            raise RuntimeError(self.lib.g4o_last_error().decode())
+        info = np.zeros(12, np.uint32)
+        self.lib.g4o_info(self.h, _ptr(info))
+        (self.num_layers, self.d_model, self.d_ff, self.q_heads, self.kv_heads, self.head_dim,
+         self.vocab, self.window, self.global_head_dim, self.global_kv_heads) = [int(x) for x in info[:10]]
+        self.global_mask = int(info[10]) | (int(info[11]) << 32)
+
+    def close(self):
+        if self.h:
+            self.lib.g4o_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    @property
+    def length(self):
+        return int(self.lib.g4o_length(self.h))
+
+    def truncate(self, n):
+        self.lib.g4o_truncate(self.h, n)
+
+    def forward(self, token, pos, want_hidden=False):
+        logits = np.empty(self.vocab, np.float32)
+        hidden = np.empty(self.d_model, np.float32) if want_hidden else None
+        if self.lib.g4o_forward(self.h, token, pos, _ptr(logits), _ptr(hidden)):
+            raise RuntimeError(self.lib.g4o_last_error().decode())
+        return (logits, hidden) if want_hidden else logits
+
+
+def spec_generate(target: RestatedModel, draft: RestatedModel | None, prompt, max_tokens,
+                  verify_width=5, sampling: Sampling | None = None, gate_min_accept=0.45,
+                  gate_window=24, stop_id=-1, replay_stream=None, mismatch_rate=0.0,
+                  mismatch_seed=0):
+    """Restated ForwardRunner::generate (src/runner.cpp:2120-2347). Returns
+    (tokens, rounds) with rounds = [(drafted, accepted, emitted), ...]."""
+    lib = restated_lib()
+    sp = sampling or Sampling.greedy()
+    prompt = np.ascontiguousarray(prompt, np.uint32)
+    out = np.zeros(max_tokens + 16, np.uint32)
+    max_rounds = max_tokens + 16
+    ri = np.zeros(3 * max_rounds, np.int32)
+    nr = ctypes.c_int(0)
+    rs = None if replay_stream is None else np.ascontiguousarray(replay_stream, np.uint32)
+    n = lib.g4o_spec_generate(target.h, draft.h if draft else None, _ptr(prompt), len(prompt),
+                              max_tokens, verify_width, ctypes.byref(sp), gate_min_accept,
+                              gate_window, stop_id, _ptr(rs), 0 if rs is None else len(rs),
+                              mismatch_rate, mismatch_seed, _ptr(out), _ptr(ri), max_rounds,
+                              ctypes.byref(nr))
+    if n < 0:
+        raise RuntimeError(lib.g4o_last_error().decode())
+    return out[:n].copy(), [tuple(int(v) for v in ri[3 * i:3 * i + 3]) for i in range(nr.value)]
+
+
+def int4_gemm(W, S, B, x):
+    """Restated GemmInt4Batch: W u32 [N][K/8], S/B u16 [N][K/64], x f32 [M][K] -> [M][N]."""
+    lib = restated_lib()
+    W = np.ascontiguousarray(W, np.uint32)
+    S = np.ascontiguousarray(S, np.uint16)
+    B = np.ascontiguousarray(B, np.uint16)
+    x = np.ascontiguousarray(x, np.float32)
+    N, K = W.shape[0], W.shape[1] * 8
+    M = x.shape[0]
+    out = np.empty((M, N), np.float32)
+    lib.g4o_int4_gemm(_ptr(W), _ptr(S), _ptr(B), N, K, _ptr(x), M, _ptr(out))
+    return out
+
+
+def int8_gemv(W, S, B, x):
+    lib = restated_lib()
+    W = np.ascontiguousarray(W, np.uint32)
+    N, K = W.shape[0], W.shape[1] * 4
+    out = np.empty(N, np.float32)
+    x = np.ascontiguousarray(x, np.float32)
+    lib.g4o_int8_gemv(_ptr(W), _ptr(np.ascontiguousarray(S, np.uint16)),
+                      _ptr(np.ascontiguousarray(B, np.uint16)), N, K, _ptr(x), _ptr(out))
+    return out
+
+
+def evaluate_verification(drafts, target_logits, sampling=None, base_seed=0, draft_logits=None):
+    lib = restated_lib()
+    sp = sampling or Sampling.greedy()
+    d = np.ascontiguousarray(drafts, np.uint32)
+    tl = np.ascontiguousarray(target_logits, np.float32)
+    dl = None if draft_logits is None else np.ascontiguousarray(draft_logits, np.float32)
+    out = np.zeros(len(d) + 1, np.uint32)
+    na = ctypes.c_uint32(0)
+    n = lib.g4o_evaluate_verification(_ptr(d), len(d), _ptr(tl), tl.shape[0], tl.shape[1],
+                                      ctypes.byref(sp), base_seed, _ptr(dl), _ptr(out), ctypes.byref(na))
+    return out[:n].tolist(), int(na.value)
+
+
+# ---------------------------------------------------------------- the reference's own code
+
+_ref = None
+
+
+def reference_available() -> bool:
+    return REF_SO.exists()
+
+
+def reference_lib():
+    global _ref
+    if _ref is None:
+        if not REF_SO.exists():
+            raise FileNotFoundError(f"{REF_SO} is not built (make -C oracle ref)")
+        lib = ctypes.CDLL(str(REF_SO))
+        lib.ref_last_error.restype = ctypes.c_char_p
+        lib.ref_open.restype = _vp
+        lib.ref_open.argtypes = [ctypes.c_char_p]
+        lib.ref_close.argtypes = [_vp]
+        lib.ref_vocab.argtypes = [_vp]
+        lib.ref_vocab.restype = ctypes.c_uint32
+        lib.ref_forward.argtypes = [_vp, ctypes.c_uint32, ctypes.c_uint32, _vp]
+        lib.ref_reset.argtypes = [_vp]
+        lib.ref_splitmix64.restype = ctypes.c_uint64
+        lib.ref_splitmix64.argtypes = [ctypes.c_uint64]
+        lib.ref_seed_for.restype = ctypes.c_uint64
+        lib.ref_seed_for.argtypes = [ctypes.c_float, ctypes.c_float, ctypes.c_int, ctypes.c_float,
+                                     ctypes.c_int, ctypes.c_uint64, ctypes.c_int]
+        lib.ref_sample_token.restype = ctypes.c_uint32
+        lib.ref_sample_token.argtypes = [_vp, ctypes.c_uint32, ctypes.c_float, ctypes.c_float, ctypes.c_int,
+                                         ctypes.c_float, ctypes.c_int, ctypes.c_uint64, ctypes.c_uint64]
+        lib.ref_validate_sampling.argtypes = [ctypes.c_float, ctypes.c_float, ctypes.c_int, ctypes.c_float]
+        lib.ref_evaluate_verification.argtypes = [_vp, ctypes.c_int, _vp, ctypes.c_int, ctypes.c_uint32,
+                                                  ctypes.c_float, ctypes.c_float, ctypes.c_int,
+                                                  ctypes.c_float, ctypes.c_int, ctypes.c_uint64,
+                                                  ctypes.c_uint64, _vp, _vp, _vp]
+        lib.ref_spec_generate.argtypes = [ctypes.c_char_p, ctypes.c_char_p, _vp, ctypes.c_int, ctypes.c_int,
+                                          ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.c_int,
+                                          ctypes.c_int, ctypes.c_uint64, ctypes.c_double, ctypes.c_int,
+                                          ctypes.c_int64, _vp, _vp, ctypes.c_int, _vp]
+        _ref = lib
+    return _ref
+
+
+class ReferenceModel:
+    """The reference's CpuReferenceRunner (append-only KV)."""
+
+    def __init__(self, path):
+        self.lib = reference_lib()
+        self.h = self.lib.ref_open(str(path).encode())
+        if not self.h:
+            raise RuntimeError(self.lib.ref_last_error().decode())
+        self.vocab = int(self.lib.ref_vocab(self.h))
+
+    def forward(self, token, pos):
+        out = np.empty(self.vocab, np.float32)
+        if self.lib.ref_forward(self.h, token, pos, _ptr(out)):
+            raise RuntimeError(self.lib.ref_last_error().decode())
+        return out
+
+    def reset(self):
+        self.lib.ref_reset(self.h)
+
+    def close(self):
+        if self.h:
+            self.lib.ref_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+def reference_spec_generate(target_path, draft_path, prompt, max_tokens, verify_width=5,
+                            sampling: Sampling | None = None, gate_min_accept=0.45,
+                            gate_window=24, stop_id=-1):
+    lib = reference_lib()
+    sp = sampling or Sampling.greedy()
+    prompt = np.ascontiguousarray(prompt, np.uint32)
+    out = np.zeros(max_tokens + 16, np.uint32)
+    max_rounds = max_tokens + 16
+    ri = np.zeros(3 * max_rounds, np.int32)
+    nr = ctypes.c_int(0)
+    n = lib.ref_spec_generate(str(target_path).encode(),
+                              None if draft_path is None else str(draft_path).encode(),
+                              _ptr(prompt), len(prompt), max_tokens, verify_width, sp.temperature,
+                              sp.top_p, sp.top_k, sp.has_seed, sp.seed, gate_min_accept, gate_window,
+                              stop_id, _ptr(out), _ptr(ri), max_rounds, ctypes.byref(nr))
+    if n < 0:
+        raise RuntimeError(lib.ref_last_error().decode())
+    return out[:n].copy(), [tuple(int(v) for v in ri[3 * i:3 * i + 3]) for i in range(nr.value)]
+
+
+def reference_evaluate_verification(drafts, target_logits, sampling=None, base_seed=0, draft_logits=None):
+    lib = reference_lib()
+    sp = sampling or Sampling.greedy()
+    d = np.ascontiguousarray(drafts, np.uint32)
+    tl = np.ascontiguousarray(target_logits, np.float32)
+    dl = None if draft_logits is None else np.ascontiguousarray(draft_logits, np.float32)
+    out = np.zeros(len(d) + 1, np.uint32)
+    na = ctypes.c_uint32(0)
+    n = lib.ref_evaluate_verification(_ptr(d), len(d), _ptr(tl), tl.shape[0], tl.shape[1],
+                                      sp.temperature, sp.top_p, sp.top_k, sp.repetition_penalty,
+                                      sp.has_seed, sp.seed, base_seed, _ptr(dl), _ptr(out), ctypes.byref(na))
+    if n < 0:
+        raise RuntimeError(lib.ref_last_error().decode())
+    return out[:n].tolist(), int(na.value)

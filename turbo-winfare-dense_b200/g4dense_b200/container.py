@@ -1,0 +1,204 @@
+"""Synthetic `.g4dense` v3 container writer and header reader.
+
+The on-disk contract is the reference's: a 4096-byte packed ``G4DenseHeader``
+(include/g4dense/format.hpp:26-110) followed by 4096-aligned blocks.
+
+* Embedding block (src/cpu_reference.cpp:260-285, 610-614): packed INT4 words
+  ``[V][d/8]`` u32 (nibble c%8 of word c/8 at bits 4*(c%8), low nibble first), bf16
+  scales ``[V][d/64]``, bf16 biases ``[V][d/64]``, then the bf16 final-norm weight
+  ``[d]``. The LM head is tied: ``lm_head_offset == embed_offset``
+  (tools/make_synthetic_model.py:189-191).
+* Layer block (src/cpu_reference.cpp:324-395, src/runner.cpp:271-370): bf16 norms
+  in, post-attn, pre-FFN, post-FFN (each ``[d]``), q_norm and k_norm (each
+  ``[head_dim]`` of that layer's geometry), one bf16 ``layer_scalar``; then for each
+  of q, k, v (absent on global layers), o, gate, up, down: zero-pad to a 16-byte
+  boundary relative to the layer start, then W, scales, biases.
+
+Value distributions are BASELINE config 0's, drawn from ``numpy.random.default_rng(seed)``
+in this fixed order: embedding (nibble bytes, scales, biases), final norm, then per layer
+the six norms in file order, then per projection (nibble bytes, scales, biases).
+Nibbles are uniform in 0..15 (uniform random bytes), scales are |N(0, 0.02)|, biases
+N(0, 0.01), norm weights 1 + N(0, 0.05); all non-quantized values are rounded to bf16
+(round-to-nearest-even). ``layer_scalar`` is 1/sqrt(2L) as in
+tools/make_synthetic_model.py:143. Embeddings are INT4 because the format has no bf16
+embedding block.
+"""
+from __future__ import annotations
+
+import dataclasses
+import hashlib
+import struct
+from pathlib import Path
+
+import numpy as np
+
+HEADER_SIZE = 4096
+ALIGNMENT = 4096
+MAGIC = 0x4734444E
+VERSION = 3
+QUANT_AFFINE_INT4_G64 = 1
+GROUP = 64
+# The packed header layout of G4DenseHeader (include/g4dense/format.hpp:26-110).
+HEADER_FMT = "<IIIIIIIIIIIIIIQffffQQQQ60Q60Q32sIIIIIIQQ60IIIff2696s"
+assert struct.calcsize(HEADER_FMT) == HEADER_SIZE
+
+
+@dataclasses.dataclass
+class ModelSpec:
+    num_layers: int
+    d_model: int
+    d_ff: int
+    num_q_heads: int
+    num_kv_heads: int
+    head_dim: int
+    vocab_size: int
+    sliding_window: int = 1024
+    global_layer_mask: int = 0
+    global_head_dim: int = 0
+    global_kv_heads: int = 0
+    rope_theta_local: float = 10000.0
+    rope_theta_global: float = 1000000.0
+    softcap: float = 30.0
+
+    def layer_geometry(self, l: int):
+        """(head_dim, q_heads, kv_heads, is_global) -- resolve_layer_geometry,
+        include/g4dense/format.hpp:229-241."""
+        is_global = bool((self.global_layer_mask >> l) & 1)
+        hd, kvh = self.head_dim, self.num_kv_heads
+        if is_global:
+            hd = self.global_head_dim or 512
+            kvh = self.global_kv_heads or 4
+        return hd, self.num_q_heads, kvh, is_global
+
+    def layer_projections(self, l: int):
+        """[(name, rows, cols)] in file order (src/cpu_reference.cpp:383-395)."""
+        hd, qh, kvh, is_global = self.layer_geometry(l)
+        d, f = self.d_model, self.d_ff
+        out = [("q", qh * hd, d), ("k", kvh * hd, d)]
+        if not is_global:
+            out.append(("v", kvh * hd, d))
+        out += [("o", d, qh * hd), ("gate", f, d), ("up", f, d), ("down", d, f)]
+        return out
+
+
+# the tiny target / drafter pair.
+CONFIG0_TARGET = ModelSpec(num_layers=4, d_model=256, d_ff=1024, num_q_heads=4, num_kv_heads=1,
+                           head_dim=64, vocab_size=4096)
+CONFIG0_DRAFT = ModelSpec(num_layers=2, d_model=128, d_ff=512, num_q_heads=2, num_kv_heads=1,
+                          head_dim=64, vocab_size=4096)
+# Gemma-4-31B shape (docs/FORWARD_PASS.md constants): global layers every 6th from 5.
+GEMMA4_31B = ModelSpec(num_layers=60, d_model=5376, d_ff=21504, num_q_heads=32, num_kv_heads=16,
+                       head_dim=256, vocab_size=262144, sliding_window=1024,
+                       global_layer_mask=0x0820820820820820, global_head_dim=512, global_kv_heads=4)
+# Gemma-4-E2B-shaped drafter used by BASELINE config 3 (no PLE, no KV sharing).
+E2B_DRAFT = ModelSpec(num_layers=35, d_model=1536, d_ff=6144, num_q_heads=8, num_kv_heads=1,
+                      head_dim=256, vocab_size=262144, sliding_window=512)
+
+
+def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    """Round-to-nearest-even float32 -> bf16 bit patterns (uint16)."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    rounded = (u + 0x7FFF + ((u >> 16) & 1)) >> 16
+    return rounded.astype(np.uint16)
+
+
+def bf16_bits_to_f32(b: np.ndarray) -> np.ndarray:
+    return (b.astype(np.uint32) << 16).view(np.float32)
+
+
+def random_quant_block(rng: np.random.Generator, rows: int, cols: int):
+    """Raw INT4 G64 block: (packed u32 [rows][cols/8], scales u16 [rows][cols/64],
+    biases u16 [rows][cols/64]) with config-0 distributions."""
+    assert cols % GROUP == 0
+    nib = rng.integers(0, 256, size=rows * cols // 2, dtype=np.uint8)
+    packed = nib.view(np.uint32).reshape(rows, cols // 8)
+    g = cols // GROUP
+    scales = f32_to_bf16_bits(np.abs(rng.standard_normal(rows * g, dtype=np.float32)) * 0.02)
+    biases = f32_to_bf16_bits(rng.standard_normal(rows * g, dtype=np.float32) * 0.01)
+    return packed, scales.reshape(rows, g), biases.reshape(rows, g)
+
+
+def _norm(rng, n):
+    return f32_to_bf16_bits(1.0 + rng.standard_normal(n, dtype=np.float32) * 0.05)
+
+
+def _pad(buf: bytearray, align: int):
+    rem = len(buf) % align
+    if rem:
+        buf += b"\x00" * (align - rem)
+
+
+def build_container(spec: ModelSpec, seed: int = 0) -> bytes:
+    """Returns the full container bytes for `spec` drawn from seed `seed`."""
+    rng = np.random.default_rng(seed)
+    d, V = spec.d_model, spec.vocab_size
+
+    embed = bytearray()
+    p, s, b = random_quant_block(rng, V, d)
+    embed += p.tobytes() + s.tobytes() + b.tobytes()
+    embed += _norm(rng, d).tobytes()
+    _pad(embed, ALIGNMENT)
+
+    layers = []
+    scalar = f32_to_bf16_bits(np.array([1.0 / np.sqrt(2.0 * spec.num_layers)], dtype=np.float32))
+    for l in range(spec.num_layers):
+        hd, _, _, _ = spec.layer_geometry(l)
+        ld = bytearray()
+        for _ in range(4):
+            ld += _norm(rng, d).tobytes()
+        ld += _norm(rng, hd).tobytes()
+        ld += _norm(rng, hd).tobytes()
+        ld += scalar.tobytes()
+        for _, rows, cols in spec.layer_projections(l):
+            _pad(ld, 16)
+            p, s, b = random_quant_block(rng, rows, cols)
+            ld += p.tobytes() + s.tobytes() + b.tobytes()
+        _pad(ld, ALIGNMENT)
+        layers.append(bytes(ld))
+
+    payload = bytearray(embed)
+    offsets = [0] * 60
+    sizes = [0] * 60
+    cur = HEADER_SIZE + len(payload)
+    for l, ld in enumerate(layers):
+        offsets[l] = cur
+        sizes[l] = len(ld)
+        payload += ld
+        cur += len(ld)
+    sha = hashlib.sha256(bytes(payload)).digest()
+    layer_d_ff = [spec.d_ff] * spec.num_layers + [0] * (60 - spec.num_layers)
+    header = struct.pack(
+        HEADER_FMT, MAGIC, VERSION, QUANT_AFFINE_INT4_G64, spec.num_layers, d, spec.d_ff,
+        spec.num_q_heads, spec.num_kv_heads, spec.head_dim, V, spec.sliding_window, GROUP,
+        1, 1, spec.global_layer_mask, spec.rope_theta_local, spec.rope_theta_global, 1.0,
+        spec.softcap, HEADER_SIZE, len(embed), HEADER_SIZE, len(embed), *offsets, *sizes, sha,
+        spec.global_head_dim or (spec.head_dim if spec.global_layer_mask == 0 else 512),
+        spec.global_kv_heads or (spec.num_kv_heads if spec.global_layer_mask == 0 else 4),
+        0, 0, 0, 0, 0, 0, *layer_d_ff, 0, 0, 0.0, 0.0, b"\x00" * 2696)
+    return header + bytes(payload)
+
+
+def write_container(path, spec: ModelSpec, seed: int = 0) -> Path:
+    path = Path(path)
+    path.parent.mkdir(parents=True, exist_ok=True)
+    data = build_container(spec, seed)
+    tmp = path.with_suffix(path.suffix + ".tmp")
+    tmp.write_bytes(data)
+    tmp.replace(path)
+    return path
+
+
+def read_header(path) -> dict:
+    with open(path, "rb") as f:
+        raw = f.read(HEADER_SIZE)
+    v = struct.unpack(HEADER_FMT, raw)
+    keys = ["magic", "version", "quant_type", "num_layers", "d_model", "d_ff", "num_q_heads",
+            "num_kv_heads", "head_dim", "vocab_size", "sliding_window", "quant_group_size",
+            "scale_dtype", "tied_embeddings", "global_layer_mask", "rope_theta_local",
+            "rope_theta_global", "rope_scaling", "final_logit_softcapping", "embed_offset",
+            "embed_size", "lm_head_offset", "lm_head_size"]
+    h = dict(zip(keys, v[:23]))
+    h["layer_offsets"] = list(v[23:83])
+    h["layer_sizes"] = list(v[83:143])
+    h["global_head_dim"], h["global_kv_heads"] = v[144], v[145]
+    return h
