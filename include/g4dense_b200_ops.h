@@ -1,0 +1,46 @@
+/* Kernel-level C ABI of the B200 speculative-decode library (libg4dense_b200.so).
+ *
+ * These entry points expose single hot-path operators on caller-owned DEVICE buffers, so a
+ * host that already manages CUDA memory can bind them the way the reference's host binds its
+ * compute shaders. All pointers are device pointers unless stated otherwise; `stream` is a
+ * cudaStream_t (NULL = legacy default stream). Functions return 0 on success or a CUDA error
+ * code, with a message in g4b_last_error() (thread-local), mirroring the reference's
+ * g4dense_engine_last_error convention (src/c_api.cpp:28-31).
+ */
+#ifndef G4DENSE_B200_OPS_H
+#define G4DENSE_B200_OPS_H
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define G4B_API __attribute__((visibility("default")))
+
+G4B_API const char* g4b_last_error(void);
+
+/* A prepared INT4 G64 affine matrix. Replaces the reference's weight binding for
+ * GemvInt4 / GemmInt4Batch (shaders/GemvInt4.hlsl:24-25, shaders/GemmInt4Batch.hlsl:296-301):
+ * W [N][K/8] u32 (nibble c%8 of word c/8, low nibble first), S and B [N][K/64] bf16, all in
+ * the container's row-major layout. The matrix is repacked once into the B200 streaming
+ * layout; the source buffers may be freed afterwards. K must be a multiple of 64. */
+typedef struct g4b_qmat g4b_qmat;
+G4B_API int g4b_qmat_create(const uint32_t* W, const uint16_t* S, const uint16_t* B, int N, int K,
+                            void* stream, g4b_qmat** out);
+G4B_API void g4b_qmat_destroy(g4b_qmat* q);
+
+/* out[m][n] = sum_k (q[n][k] * s + b) * x[m][k] for m < M <= 16: the batched verify GEMM
+ * (shaders/GemmInt4Batch.hlsl:64-143; M = 1 is GemvInt4, shaders/GemvInt4.hlsl:31-54).
+ * x is fp32 [M][ldx], out fp32 [M][ldo]. Launches two kernels: fragment preparation and the
+ * GEMM. Calls on one matrix must be stream-ordered (they share the matrix's workspace). */
+G4B_API int g4b_qmat_gemm(g4b_qmat* q, const float* x, int ldx, int M, float* out, int ldo, void* stream);
+/* The two halves of g4b_qmat_gemm, for timing the GEMM kernel alone. */
+G4B_API int g4b_qmat_prepare_input(g4b_qmat* q, const float* x, int ldx, int M, void* stream);
+G4B_API int g4b_qmat_run(g4b_qmat* q, int M, float* out, int ldo, void* stream);
+/* out4 = {N, K, grid CTAs at M=5, split-K slots per row group} */
+G4B_API int g4b_qmat_info(const g4b_qmat* q, int* out4);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,61 @@
+// Producer side of the B-frag activation layout (see common.cuh). Every kernel that
+// feeds a verify GEMM (input norm, post-attention norm, GeGLU, attention output,
+// final norm) ends by calling bfrag_store_group, so activations are converted once and
+// the GEMM streams ready-made tensor-core fragments.
+#pragma once
+#include "common.cuh"
+
+namespace g4b {
+
+// Converts one (row m, 64-group gi) held by a warp -- lane l owns columns 2l and 2l+1 of
+// the group -- into fragments and the group's {E, Y} record. `stage` is 128 halves of
+// per-warp shared scratch. All 32 lanes must call it.
+__device__ __forceinline__ void bfrag_store_group(const BFragView& v, int M, int m, int gi,
+                                                  float x0, float x1, __half* stage) {
+    const int lane = threadIdx.x & 31;
+    const BMode md = bmode_for(M);
+    const float amax = warp_max(fmaxf(fabsf(x0), fabsf(x1)));
+    int e = 0;
+    frexpf(amax, &e);  // amax = f * 2^e, f in [0.5, 1)
+    const float E = ldexpf(1.0f, e - 11);
+    const float invE = ldexpf(1.0f, 11 - e);
+    const float s0 = x0 * invE, s1 = x1 * invE;
+    const __half h0 = __float2half_rn(s0), h1 = __float2half_rn(s1);
+    const __half l0 = __float2half_rn(s0 - __half2float(h0));
+    const __half l1 = __float2half_rn(s1 - __half2float(h1));
+    const float y = warp_sum((__half2float(h0) + __half2float(l0)) + (__half2float(h1) + __half2float(l1)));
+    stage[2 * lane] = h0;
+    stage[2 * lane + 1] = h1;
+    stage[64 + 2 * lane] = l0;
+    stage[64 + 2 * lane + 1] = l1;
+    __syncwarp();
+    if (lane < 16) {
+        const int kb = lane >> 3, part = (lane >> 2) & 1, t = lane & 3;
+        const __half* src = stage + part * 64 + kb * 32 + 8 * t;
+        int tile, n;
+        if (md.packed) { tile = 0; n = m + 4 * part; }
+        else if (md.nb == 2) { tile = part; n = m; }
+        else { tile = 2 * (m >> 3) + part; n = m & 7; }
+        const __half sixteenth = __float2half(0.0625f);
+        auto pk = [](__half a, __half b) {
+            return (uint32_t)__half_as_ushort(a) | ((uint32_t)__half_as_ushort(b) << 16);
+        };
+        uint4 o;
+        o.x = pk(src[0], src[4]);
+        o.y = pk(__hmul(src[1], sixteenth), __hmul(src[5], sixteenth));
+        o.z = pk(src[2], src[6]);
+        o.w = pk(__hmul(src[3], sixteenth), __hmul(src[7], sixteenth));
+        v.frag[((size_t)(gi * 2 + kb) * md.nb + tile) * 32 + n * 4 + t] = o;
+    } else if (lane == 16) {
+        const float Y = y * 5.9604644775390625e-08f;  // 2^-24
+        if (md.packed) {
+            v.gsum[(size_t)gi * 8 + m] = make_float2(E, Y);
+            v.gsum[(size_t)gi * 8 + m + 4] = make_float2(E, 0.0f);
+        } else {
+            v.gsum[((size_t)gi * md.nacc + (m >> 3)) * 8 + (m & 7)] = make_float2(E, Y);
+        }
+    }
+    __syncwarp();
+}
+
+}  // namespace g4b

@@ -1,0 +1,119 @@
+// Shared device-side definitions for the B200 speculative-decode kernels (sm_100a).
+//
+// Data formats in HBM (all fully resident):
+//
+// 1. Packed INT4 G64 weight matrix ("vgemm layout"), repacked once at load from the
+//    container's row-major form (W [N][K/8] u32, scales/biases [N][K/64] bf16;
+//    src/cpu_reference.cpp:367-381). Rows are grouped in warp row groups of 64 rows
+//    (four 16-row MMA tiles) and K in 128-column k-tiles. Each (row group, k-tile) is one
+//    contiguous 4608-byte block:
+//      [r 0..3][half 0..1][lane 0..31] uint4   nibble words, 4096 B
+//      [r 0..3][g 0..7] uint4                  bf16 scale/bias pairs, 512 B
+//    Lane (g = lane/4, t = lane%4) of half h holds the words of rows g and g+8 covering
+//    k = 32*kk + 8t .. +7 for kk = 2h and 2h+1, in the order {row g kk=2h, row g+8 kk=2h,
+//    row g kk=2h+1, row g+8 kk=2h+1}: exactly the A-fragment words that lane needs for
+//    mma.m16n8k16, so one 128-bit load per half feeds eight MMAs with no shuffles.
+//    The scale/bias uint4 for (r, g) is {s(g,G0)|b(g,G0)<<16, s(g+8,G0)|b(g+8,G0)<<16,
+//    s(g,G1)|b(g,G1)<<16, s(g+8,G1)|b(g+8,G1)<<16} for the two 64-groups G0, G1 of the
+//    k-tile. Blocks are ordered [row group][k-tile], so a warp streams one row group's
+//    k-range from contiguous memory. Rows beyond N and columns beyond K are zero.
+//
+// 2. Activation fragments ("B-frag layout") for the verify GEMM's B operand. An activation
+//    matrix x [M][K] (M <= 16 verify/prefill rows) is stored as fp16 hi/lo pairs of
+//    x / E, where E is a power of two chosen per (64-group, row) so |x/E| < 2^11:
+//      frag[K/32][NB][32 lanes] uint4, gsum[K/64][NACC][8 cols] float2 {E, Y}
+//    NB/NACC depend on M (see BMode). Y = 2^-24 * sum of the group's (hi+lo) values;
+//    the per-group epilogue adds E*(s*P + b*Y), which restates q*s+b dequantization
+//    exactly: sum_k (q s + b) x = s * sum q x + b * sum x.
+//
+// 3. INT4 nibbles enter the tensor core as IEEE fp16 SUBNORMALS: the bit pattern q (or
+//    16q for odd nibbles) is the value q * 2^-24, so a single AND turns two nibbles into
+//    an exact fp16x2 operand; the 2^24 (and 1/16) factors are folded into the activation
+//    fragments and the final scale.
+#pragma once
+#include <cuda_fp16.h>
+#include <cstdint>
+
+namespace g4b {
+
+constexpr int kRowsPerTile = 16;         // MMA M
+constexpr int kTilesPerWarp = 4;         // row tiles per warp
+constexpr int kWarpRows = kRowsPerTile * kTilesPerWarp;  // 64
+constexpr int kKTile = 128;              // k-tile width
+constexpr int kKTileBytes = 4608;        // one (row group, k-tile) block
+constexpr int kNibBytes = 4096;
+constexpr int kMaxM = 16;                // verify / prefill rows per pass
+
+// B-operand mode for M rows.
+struct BMode {
+    int nb;      // B tiles per k32 block
+    int nacc;    // accumulator column tiles
+    bool packed; // M <= 4: hi in columns 0..3, lo in columns 4..7 of one tile
+};
+__host__ __device__ inline BMode bmode_for(int M) {
+    if (M <= 4) return {1, 1, true};
+    if (M <= 8) return {2, 1, false};
+    return {4, 2, false};
+}
+__host__ __device__ inline size_t bfrag_frag_bytes(int K, int M) {
+    return (size_t)(K / 32) * bmode_for(M).nb * 512;
+}
+__host__ __device__ inline size_t bfrag_gsum_bytes(int K, int M) {
+    return (size_t)(K / 64) * bmode_for(M).nacc * 8 * sizeof(float2);
+}
+// Capacity of one B-frag buffer for K columns at the maximum M.
+__host__ __device__ inline size_t bfrag_capacity(int K) {
+    return bfrag_frag_bytes(K, kMaxM) + bfrag_gsum_bytes(K, kMaxM);
+}
+
+struct BFragView {
+    uint4* frag;   // [K/32][nb][32]
+    float2* gsum;  // [K/64][nacc][8]
+};
+__host__ __device__ inline BFragView bfrag_view(void* base, int K, int M) {
+    BFragView v;
+    v.frag = reinterpret_cast<uint4*>(base);
+    v.gsum = reinterpret_cast<float2*>(reinterpret_cast<char*>(base) + bfrag_frag_bytes(K, M));
+    return v;
+}
+
+__device__ __forceinline__ float bf16_lo(uint32_t v) { return __uint_as_float(v << 16); }
+__device__ __forceinline__ float bf16_hi(uint32_t v) { return __uint_as_float(v & 0xFFFF0000u); }
+__device__ __forceinline__ float bf16_to_f32(uint16_t v) { return __uint_as_float((uint32_t)v << 16); }
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// Block-wide sum for blockDim.x <= 1024; `red` needs 32 floats of shared memory.
+__device__ __forceinline__ float block_sum(float v, float* red) {
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    v = warp_sum(v);
+    __syncthreads();
+    if (lane == 0) red[wid] = v;
+    __syncthreads();
+    const int nw = (blockDim.x + 31) >> 5;
+    float t = (threadIdx.x < nw) ? red[threadIdx.x] : 0.0f;
+    if (wid == 0) t = warp_sum(t);
+    if (threadIdx.x == 0) red[0] = t;
+    __syncthreads();
+    const float r = red[0];
+    __syncthreads();
+    return r;
+}
+
+// Programmatic dependent launch: wait for the producing kernel's writes / let the next
+// kernel start its independent prologue (weight prefetch) early.
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void pdl_launch_dependents() {
+    asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+}  // namespace g4b

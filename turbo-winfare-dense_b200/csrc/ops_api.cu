@@ -1,0 +1,119 @@
+// Kernel-level C ABI (include/g4dense_b200_ops.h): prepared INT4 G64 matrices and the
+// verify GEMM on caller-owned device buffers.
+#include "g4dense_b200_ops.h"
+
+#include <cstdio>
+#include <string>
+
+#include "common.cuh"
+#include "kernels.h"
+#include "vgemm.h"
+
+namespace {
+thread_local std::string g_err;
+int fail(cudaError_t e, const char* where) {
+    g_err = std::string(where) + ": " + cudaGetErrorString(e);
+    return (int)e;
+}
+int fail_msg(const char* msg) {
+    g_err = msg;
+    return (int)cudaErrorInvalidValue;
+}
+}  // namespace
+
+struct g4b_qmat {
+    int N, K, ktiles, n_wrg, n_crg;
+    void* w;          // repacked weights
+    void* bfrag;      // B fragments for one input of up to 16 rows
+    float* part;      // split-K partials
+    int* counters;    // split-K arrival counters
+    int max_slots;    // slots per row group sized for the largest grid
+};
+
+extern "C" {
+
+const char* g4b_last_error(void) { return g_err.c_str(); }
+
+int g4b_qmat_create(const uint32_t* W, const uint16_t* S, const uint16_t* B, int N, int K, void* stream,
+                    g4b_qmat** out) {
+    if (!out || !W || !S || !B || N <= 0 || K <= 0 || K % 64) return fail_msg("g4b_qmat_create: bad arguments");
+    cudaStream_t st = (cudaStream_t)stream;
+    auto* q = new g4b_qmat{};
+    q->N = N;
+    q->K = K;
+    q->ktiles = (K + 127) / 128;
+    q->n_wrg = (N + 63) / 64;
+    q->n_crg = (q->n_wrg + 3) / 4;
+    cudaError_t e;
+    if ((e = cudaMalloc(&q->w, g4b_qmat_bytes(N, K))) != cudaSuccess) { delete q; return fail(e, "cudaMalloc(weights)"); }
+    if ((e = g4b_repack(W, S, B, N, K, q->w, st)) != cudaSuccess) { g4b_qmat_destroy(q); return fail(e, "repack"); }
+    const int Kp = q->ktiles * 128;
+    if ((e = cudaMalloc(&q->bfrag, g4b::bfrag_capacity(Kp))) != cudaSuccess) { g4b_qmat_destroy(q); return fail(e, "cudaMalloc(bfrag)"); }
+    int grid_max = 0;
+    for (int M : {1, 5, 16}) grid_max = std::max(grid_max, vgemm_grid(M, q->n_crg, q->ktiles));
+    int slots = 0;
+    for (int M : {1, 5, 16}) slots = std::max(slots, vgemm_max_slots(vgemm_grid(M, q->n_crg, q->ktiles), q->n_crg, q->ktiles));
+    q->max_slots = slots;
+    const size_t part_bytes = (size_t)q->n_crg * slots * g4b::kMaxM * 256 * sizeof(float);
+    if ((e = cudaMalloc(&q->part, part_bytes)) != cudaSuccess) { g4b_qmat_destroy(q); return fail(e, "cudaMalloc(part)"); }
+    if ((e = cudaMalloc(&q->counters, q->n_crg * sizeof(int))) != cudaSuccess) { g4b_qmat_destroy(q); return fail(e, "cudaMalloc(counters)"); }
+    if ((e = cudaMemsetAsync(q->counters, 0, q->n_crg * sizeof(int), st)) != cudaSuccess) { g4b_qmat_destroy(q); return fail(e, "memset"); }
+    if ((e = cudaStreamSynchronize(st)) != cudaSuccess) { g4b_qmat_destroy(q); return fail(e, "g4b_qmat_create"); }
+    *out = q;
+    return 0;
+}
+
+void g4b_qmat_destroy(g4b_qmat* q) {
+    if (!q) return;
+    cudaFree(q->w);
+    cudaFree(q->bfrag);
+    cudaFree(q->part);
+    cudaFree(q->counters);
+    delete q;
+}
+
+int g4b_qmat_prepare_input(g4b_qmat* q, const float* x, int ldx, int M, void* stream) {
+    if (!q || !x || M < 1 || M > g4b::kMaxM || ldx < q->K) return fail_msg("g4b_qmat_prepare_input: bad arguments");
+    cudaError_t e = g4b_bfrag_from_f32(x, ldx, M, q->K, q->bfrag, (cudaStream_t)stream, false);
+    return e == cudaSuccess ? 0 : fail(e, "bfrag_from_f32");
+}
+
+int g4b_qmat_run(g4b_qmat* q, int M, float* out, int ldo, void* stream) {
+    if (!q || !out || M < 1 || M > g4b::kMaxM || ldo < q->N) return fail_msg("g4b_qmat_run: bad arguments");
+    const int Kp = q->ktiles * 128;
+    const g4b::BFragView v = g4b::bfrag_view(q->bfrag, Kp, M);
+    VgemmParams p{};
+    p.w = q->w;
+    p.bfrag = v.frag;
+    p.gsum = v.gsum;
+    p.out = out;
+    p.ldo = ldo;
+    p.N = q->N;
+    p.M = M;
+    p.n_wrg = q->n_wrg;
+    p.n_crg = q->n_crg;
+    p.ktiles = q->ktiles;
+    p.part = q->part;
+    p.counters = q->counters;
+    const int grid = vgemm_grid(M, q->n_crg, q->ktiles);
+    p.max_slots = q->max_slots;
+    if (vgemm_max_slots(grid, q->n_crg, q->ktiles) > q->max_slots) return fail_msg("g4b_qmat_run: slot overflow");
+    cudaError_t e = vgemm_launch(p, grid, (cudaStream_t)stream, false);
+    return e == cudaSuccess ? 0 : fail(e, "vgemm_launch");
+}
+
+int g4b_qmat_gemm(g4b_qmat* q, const float* x, int ldx, int M, float* out, int ldo, void* stream) {
+    int rc = g4b_qmat_prepare_input(q, x, ldx, M, stream);
+    return rc ? rc : g4b_qmat_run(q, M, out, ldo, stream);
+}
+
+int g4b_qmat_info(const g4b_qmat* q, int* out4) {
+    if (!q || !out4) return fail_msg("g4b_qmat_info: bad arguments");
+    out4[0] = q->N;
+    out4[1] = q->K;
+    out4[2] = vgemm_grid(5, q->n_crg, q->ktiles);
+    out4[3] = q->max_slots;
+    return 0;
+}
+
+}  // extern "C"

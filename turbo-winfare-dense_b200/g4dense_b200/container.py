@@ -106,15 +106,24 @@ def bf16_bits_to_f32(b: np.ndarray) -> np.ndarray:
     return (b.astype(np.uint32) << 16).view(np.float32)
 
 
-def random_quant_block(rng: np.random.Generator, rows: int, cols: int):
+def random_quant_block(rng: np.random.Generator, rows: int, cols: int, centered: bool = False):
     """Raw INT4 G64 block: (packed u32 [rows][cols/8], scales u16 [rows][cols/64],
-    biases u16 [rows][cols/64]) with config-0 distributions."""
+    biases u16 [rows][cols/64]) with config-0 distributions.
+
+    ``centered`` subtracts 7.5 * scale from each bias, making every group's dequantized
+    weights zero-mean. BASELINE's distributions give the weights a large positive mean, which
+    makes the greedy token stream nearly input-independent; the centered variant is a test
+    aid that exercises input-dependent tokens with the same format and value ranges."""
     assert cols % GROUP == 0
     nib = rng.integers(0, 256, size=rows * cols // 2, dtype=np.uint8)
     packed = nib.view(np.uint32).reshape(rows, cols // 8)
     g = cols // GROUP
-    scales = f32_to_bf16_bits(np.abs(rng.standard_normal(rows * g, dtype=np.float32)) * 0.02)
-    biases = f32_to_bf16_bits(rng.standard_normal(rows * g, dtype=np.float32) * 0.01)
+    s32 = np.abs(rng.standard_normal(rows * g, dtype=np.float32)) * 0.02
+    scales = f32_to_bf16_bits(s32)
+    b32 = rng.standard_normal(rows * g, dtype=np.float32) * 0.01
+    if centered:
+        b32 = b32 - 7.5 * bf16_bits_to_f32(scales)
+    biases = f32_to_bf16_bits(b32)
     return packed, scales.reshape(rows, g), biases.reshape(rows, g)
 
 
@@ -128,13 +137,14 @@ def _pad(buf: bytearray, align: int):
         buf += b"\x00" * (align - rem)
 
 
-def build_container(spec: ModelSpec, seed: int = 0) -> bytes:
-    """Returns the full container bytes for `spec` drawn from seed `seed`."""
+def build_container(spec: ModelSpec, seed: int = 0, centered: bool = False) -> bytes:
+    """Returns the full container bytes for `spec` drawn from seed `seed` (see
+    random_quant_block for ``centered``)."""
     rng = np.random.default_rng(seed)
     d, V = spec.d_model, spec.vocab_size
 
     embed = bytearray()
-    p, s, b = random_quant_block(rng, V, d)
+    p, s, b = random_quant_block(rng, V, d, centered)
     embed += p.tobytes() + s.tobytes() + b.tobytes()
     embed += _norm(rng, d).tobytes()
     _pad(embed, ALIGNMENT)
@@ -151,7 +161,7 @@ def build_container(spec: ModelSpec, seed: int = 0) -> bytes:
         ld += scalar.tobytes()
         for _, rows, cols in spec.layer_projections(l):
             _pad(ld, 16)
-            p, s, b = random_quant_block(rng, rows, cols)
+            p, s, b = random_quant_block(rng, rows, cols, centered)
             ld += p.tobytes() + s.tobytes() + b.tobytes()
         _pad(ld, ALIGNMENT)
         layers.append(bytes(ld))
@@ -178,10 +188,10 @@ def build_container(spec: ModelSpec, seed: int = 0) -> bytes:
     return header + bytes(payload)
 
 
-def write_container(path, spec: ModelSpec, seed: int = 0) -> Path:
+def write_container(path, spec: ModelSpec, seed: int = 0, centered: bool = False) -> Path:
     path = Path(path)
     path.parent.mkdir(parents=True, exist_ok=True)
-    data = build_container(spec, seed)
+    data = build_container(spec, seed, centered)
     tmp = path.with_suffix(path.suffix + ".tmp")
     tmp.write_bytes(data)
     tmp.replace(path)
