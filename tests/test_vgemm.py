@@ -47,6 +47,7 @@ def check_gemm(N, K, M, seed=0, centered=False, x_scale=1.0):
     out = torch.full((M, N), float("nan"), device=dev)
     q.gemm(xt, out)
     torch.cuda.synchronize()
+    q.check_error()
     got = out.cpu().numpy()
     ref = O.int4_gemm(W, S, B, x)
     mass = np.abs(x.astype(np.float64)) @ np.abs(dequant(W, S, B)).T
@@ -57,7 +58,7 @@ def check_gemm(N, K, M, seed=0, centered=False, x_scale=1.0):
     out2 = torch.full((M, N), float("nan"), device=dev)
     q.gemm(xt, out2)
     torch.cuda.synchronize()
-    assert np.array_equal(out2.cpu().numpy(), got), "second launch differs (counter reset / determinism)"
+    assert np.array_equal(out2.cpu().numpy(), got), "second launch differs (determinism)"
     q.close()
     return err.max()
 

@@ -26,8 +26,8 @@ struct g4b_qmat {
     void* w;          // repacked weights
     void* bfrag;      // B fragments for one input of up to 16 rows
     float* part;      // split-K partials
-    int* counters;    // split-K arrival counters
-    int max_slots;    // slots per row group sized for the largest grid
+    int max_slots;    // slots per row group sized for every M
+    int* err;         // device error word of the bounded waits
 };
 
 extern "C" {
@@ -41,23 +41,19 @@ int g4b_qmat_create(const uint32_t* W, const uint16_t* S, const uint16_t* B, int
     auto* q = new g4b_qmat{};
     q->N = N;
     q->K = K;
-    q->ktiles = (K + 127) / 128;
+    q->ktiles = vgemm_ktiles(K);
     q->n_wrg = (N + 63) / 64;
-    q->n_crg = (q->n_wrg + 3) / 4;
+    q->n_crg = vgemm_n_crg(N);
     cudaError_t e;
-    if ((e = cudaMalloc(&q->w, g4b_qmat_bytes(N, K))) != cudaSuccess) { delete q; return fail(e, "cudaMalloc(weights)"); }
+    if ((e = cudaMalloc(&q->w, vgemm_weight_bytes(N, K))) != cudaSuccess) { delete q; return fail(e, "cudaMalloc(weights)"); }
     if ((e = g4b_repack(W, S, B, N, K, q->w, st)) != cudaSuccess) { g4b_qmat_destroy(q); return fail(e, "repack"); }
     const int Kp = q->ktiles * 128;
     if ((e = cudaMalloc(&q->bfrag, g4b::bfrag_capacity(Kp))) != cudaSuccess) { g4b_qmat_destroy(q); return fail(e, "cudaMalloc(bfrag)"); }
-    int grid_max = 0;
-    for (int M : {1, 5, 16}) grid_max = std::max(grid_max, vgemm_grid(M, q->n_crg, q->ktiles));
-    int slots = 0;
-    for (int M : {1, 5, 16}) slots = std::max(slots, vgemm_max_slots(vgemm_grid(M, q->n_crg, q->ktiles), q->n_crg, q->ktiles));
-    q->max_slots = slots;
-    const size_t part_bytes = (size_t)q->n_crg * slots * g4b::kMaxM * 256 * sizeof(float);
+    q->max_slots = vgemm_plan_slots(q->n_crg, q->ktiles);
+    const size_t part_bytes = (size_t)q->n_crg * q->max_slots * g4b::kMaxM * 256 * sizeof(float);
     if ((e = cudaMalloc(&q->part, part_bytes)) != cudaSuccess) { g4b_qmat_destroy(q); return fail(e, "cudaMalloc(part)"); }
-    if ((e = cudaMalloc(&q->counters, q->n_crg * sizeof(int))) != cudaSuccess) { g4b_qmat_destroy(q); return fail(e, "cudaMalloc(counters)"); }
-    if ((e = cudaMemsetAsync(q->counters, 0, q->n_crg * sizeof(int), st)) != cudaSuccess) { g4b_qmat_destroy(q); return fail(e, "memset"); }
+    if ((e = cudaMalloc(&q->err, sizeof(int))) != cudaSuccess) { g4b_qmat_destroy(q); return fail(e, "cudaMalloc(err)"); }
+    if ((e = cudaMemsetAsync(q->err, 0, sizeof(int), st)) != cudaSuccess) { g4b_qmat_destroy(q); return fail(e, "memset"); }
     if ((e = cudaStreamSynchronize(st)) != cudaSuccess) { g4b_qmat_destroy(q); return fail(e, "g4b_qmat_create"); }
     *out = q;
     return 0;
@@ -68,7 +64,7 @@ void g4b_qmat_destroy(g4b_qmat* q) {
     cudaFree(q->w);
     cudaFree(q->bfrag);
     cudaFree(q->part);
-    cudaFree(q->counters);
+    cudaFree(q->err);
     delete q;
 }
 
@@ -78,28 +74,40 @@ int g4b_qmat_prepare_input(g4b_qmat* q, const float* x, int ldx, int M, void* st
     return e == cudaSuccess ? 0 : fail(e, "bfrag_from_f32");
 }
 
-int g4b_qmat_run(g4b_qmat* q, int M, float* out, int ldo, void* stream) {
-    if (!q || !out || M < 1 || M > g4b::kMaxM || ldo < q->N) return fail_msg("g4b_qmat_run: bad arguments");
+static PartView qmat_view(const g4b_qmat* q, int M) {
+    PartView v;
+    v.part = q->part;
+    v.max_slots = q->max_slots;
+    v.n_crg = q->n_crg;
+    v.ktiles = q->ktiles;
+    v.grid = vgemm_grid(M, q->n_crg, q->ktiles);
+    return v;
+}
+
+// GEMM kernel only: leaves the split-K partials in the matrix's workspace.
+int g4b_qmat_run_partial(g4b_qmat* q, int M, void* stream) {
+    if (!q || M < 1 || M > g4b::kMaxM) return fail_msg("g4b_qmat_run_partial: bad arguments");
     const int Kp = q->ktiles * 128;
     const g4b::BFragView v = g4b::bfrag_view(q->bfrag, Kp, M);
     VgemmParams p{};
     p.w = q->w;
     p.bfrag = v.frag;
     p.gsum = v.gsum;
-    p.out = out;
-    p.ldo = ldo;
+    p.out = qmat_view(q, M);
     p.N = q->N;
     p.M = M;
     p.n_wrg = q->n_wrg;
-    p.n_crg = q->n_crg;
-    p.ktiles = q->ktiles;
-    p.part = q->part;
-    p.counters = q->counters;
-    const int grid = vgemm_grid(M, q->n_crg, q->ktiles);
-    p.max_slots = q->max_slots;
-    if (vgemm_max_slots(grid, q->n_crg, q->ktiles) > q->max_slots) return fail_msg("g4b_qmat_run: slot overflow");
-    cudaError_t e = vgemm_launch(p, grid, (cudaStream_t)stream, false);
+    p.err = q->err;
+    cudaError_t e = vgemm_launch(p, (cudaStream_t)stream, false);
     return e == cudaSuccess ? 0 : fail(e, "vgemm_launch");
+}
+
+int g4b_qmat_run(g4b_qmat* q, int M, float* out, int ldo, void* stream) {
+    if (!q || !out || M < 1 || M > g4b::kMaxM || ldo < q->N) return fail_msg("g4b_qmat_run: bad arguments");
+    int rc = g4b_qmat_run_partial(q, M, stream);
+    if (rc) return rc;
+    cudaError_t e = vgemm_reduce(qmat_view(q, M), M, q->N, out, ldo, (cudaStream_t)stream, false);
+    return e == cudaSuccess ? 0 : fail(e, "vgemm_reduce");
 }
 
 int g4b_qmat_gemm(g4b_qmat* q, const float* x, int ldx, int M, float* out, int ldo, void* stream) {
@@ -113,6 +121,15 @@ int g4b_qmat_info(const g4b_qmat* q, int* out4) {
     out4[1] = q->K;
     out4[2] = vgemm_grid(5, q->n_crg, q->ktiles);
     out4[3] = q->max_slots;
+    return 0;
+}
+
+int g4b_qmat_check_error(g4b_qmat* q) {
+    if (!q) return fail_msg("g4b_qmat_check_error: null handle");
+    int h = 0;
+    cudaError_t e = cudaMemcpy(&h, q->err, sizeof(int), cudaMemcpyDeviceToHost);
+    if (e != cudaSuccess) return fail(e, "g4b_qmat_check_error");
+    if (h) return fail_msg("verify GEMM: a bounded wait gave up (weights or fragments never arrived)");
     return 0;
 }
 

@@ -6,7 +6,13 @@
 
 namespace g4b {
 
-// One thread per (row group, k-tile, r, half, lane) output uint4.
+// Block index of warp row group wrg (= 4*crg + w) at k-tile kt: [crg][kt][w].
+__device__ __forceinline__ long long block_index(long long wrg, int kt, int ktiles) {
+    return ((wrg >> 2) * ktiles + kt) * 4 + (wrg & 3);
+}
+
+// One thread per (row group, k-tile, r, half, lane) output uint4; n_wrg is padded to whole
+// 256-row CTA groups and rows past N are zero.
 __global__ void repack_nibbles(const uint32_t* __restrict__ W, int N, int K, int ktiles, int n_wrg,
                                uint4* __restrict__ out) {
     const long long total = (long long)n_wrg * ktiles * 256;
@@ -29,7 +35,8 @@ __global__ void repack_nibbles(const uint32_t* __restrict__ W, int N, int K, int
             const int word = kt * 16 + kk * 4 + t;
             v[j] = (row < N && word < wpr) ? W[row * wpr + word] : 0u;
         }
-        out[blk * (kKTileBytes / 16) + (r * 2 + half) * 32 + lane] = make_uint4(v[0], v[1], v[2], v[3]);
+        out[block_index(wrg, kt, ktiles) * (kKTileBytes / 16) + (r * 2 + half) * 32 + lane] =
+            make_uint4(v[0], v[1], v[2], v[3]);
     }
 }
 
@@ -58,21 +65,21 @@ __global__ void repack_scales(const uint16_t* __restrict__ S, const uint16_t* __
             }
             v[j] = s | (b << 16);
         }
-        out[blk * (kKTileBytes / 16) + 256 + r * 8 + g] = make_uint4(v[0], v[1], v[2], v[3]);
+        out[block_index(wrg, kt, ktiles) * (kKTileBytes / 16) + 256 + r * 8 + g] = make_uint4(v[0], v[1], v[2], v[3]);
     }
 }
 
 }  // namespace g4b
 
 size_t g4b_qmat_bytes(int N, int K) {
-    const int n_wrg = (N + 63) / 64, ktiles = (K + 127) / 128;
+    const int n_wrg = (N + 255) / 256 * 4, ktiles = (K + 127) / 128;
     return (size_t)n_wrg * ktiles * g4b::kKTileBytes;
 }
 
 cudaError_t g4b_repack(const uint32_t* W, const uint16_t* S, const uint16_t* B, int N, int K, void* out,
                        cudaStream_t st) {
     if (N <= 0 || K <= 0 || K % 64) return cudaErrorInvalidValue;
-    const int n_wrg = (N + 63) / 64, ktiles = (K + 127) / 128;
+    const int n_wrg = (N + 255) / 256 * 4, ktiles = (K + 127) / 128;
     g4b::repack_nibbles<<<1184, 256, 0, st>>>(W, N, K, ktiles, n_wrg, reinterpret_cast<uint4*>(out));
     g4b::repack_scales<<<592, 256, 0, st>>>(S, B, N, K, ktiles, n_wrg, reinterpret_cast<uint4*>(out));
     return cudaGetLastError();

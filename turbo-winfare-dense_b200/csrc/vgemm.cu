@@ -4,20 +4,25 @@
 //
 // The op is HBM-bound (0.5625 B per weight; 3.5-56 flop/B for M = 1..16), so the kernel is
 // organised around streaming the packed weights once at full bandwidth:
-//   * weights stream in the vgemm layout (common.cuh) with 128-bit non-allocating loads,
-//     one k-tile ahead in registers, so every warp keeps 4.5 KB in flight;
+//   * each warp owns a 4-stage ring of 4608-byte k-tile blocks in shared memory, filled by
+//     TMA bulk copies (cp.async.bulk, one per block, completion on a per-stage mbarrier).
+//     The first stages are issued before griddepcontrol.wait, so under programmatic
+//     dependent launch the weight stream starts while the previous kernel is still draining;
 //   * nibbles become exact fp16-subnormal tensor-core operands with one AND each, and
-//     mma.sync m16n8k16 (fp32 accumulate) does the multiply-adds -- the activations ride as
-//     fp16 hi/lo pairs, which keeps fp32-level accuracy (|error| ~ 2^-22 relative) where a
-//     bf16 dequantisation would give ~2^-9;
+//     mma.sync m16n8k16 (fp32 accumulate) does the multiply-adds; the activations ride as
+//     fp16 hi/lo pairs (B-frag layout, common.cuh), keeping fp32-level accuracy;
 //   * scale and bias are applied per 64-group in fp32 from the group partial sums;
-//   * work is split stream-K style: CTA c owns a contiguous range of (row group, k-tile)
-//     units, so every CTA streams the same number of bytes whatever the shape. Row groups
-//     split across CTAs are reduced deterministically (fixed slot order) by the last CTA
-//     to finish, which also resets the group's arrival counter for the next launch.
-// tcgen05 is deliberately not used here: at M <= 16 the tensor work is a few percent of the
+//   * work is split stream-K style: CTA c owns the contiguous unit range
+//     [c*T/G, (c+1)*T/G) of (256-row group, k-tile) units, so every CTA streams the same
+//     number of bytes whatever the shape. Each CTA writes one partial per row group it
+//     touches into a fixed slot; consumers add the slots in order (deterministic);
+//   * activation fragments for the CTA's k-range are double-buffered in shared memory by
+//     bulk copies, one chunk ahead.
+// tcgen05 is deliberately not used here: at M <= 16 the tensor work is a small part of the
 // issue budget and the binding resource is HBM bandwidth.
 #include "common.cuh"
+#include "launch.cuh"
+#include "tma.cuh"
 #include "vgemm.h"
 
 #include <algorithm>
@@ -28,19 +33,14 @@ namespace g4b {
 constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
 constexpr int kCtaRows = kWarps * kWarpRows;  // 256
-constexpr int kBChunk = 8;                    // k-tiles of B fragments staged at a time
-
-__device__ __forceinline__ uint4 ldg_stream(const uint4* p) {
-    uint4 r;
-    asm volatile("ld.global.nc.L1::no_allocate.L2::256B.v4.u32 {%0,%1,%2,%3}, [%4];"
-                 : "=r"(r.x), "=r"(r.y), "=r"(r.z), "=r"(r.w)
-                 : "l"(p));
-    return r;
-}
+constexpr int kStages = 3;                    // weight ring depth per warp
+constexpr int kBlockU4 = kKTileBytes / 16;    // 288 uint4 per block
 
 __device__ __forceinline__ void mma16816(float* d, uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
                                          uint32_t b0, uint32_t b1, const float* c) {
-    asm volatile(
+    // Not volatile: the MMA has no side effects, and letting the compiler interleave
+    // independent row tiles hides the tensor pipe's fixed latency.
+    asm(
         "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
         "{%10,%11,%12,%13};"
         : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
@@ -48,35 +48,27 @@ __device__ __forceinline__ void mma16816(float* d, uint32_t a0, uint32_t a1, uin
           "f"(c[3]));
 }
 
-__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
-    const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
-    asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem));
-}
-__device__ __forceinline__ void cp_async_wait_all() {
-    asm volatile("cp.async.commit_group;\ncp.async.wait_group 0;" ::: "memory");
-}
-
-struct KTileRegs {
-    uint4 nib[kTilesPerWarp][2];
-    uint4 sb[kTilesPerWarp];
+// k-tiles of activation fragments per staged chunk: 8 KB of fragments per chunk.
+template <int NB>
+struct Chunk {
+    static constexpr int kt = 4 / NB > 0 ? 4 / NB : 1;
+    static constexpr int frag_u4 = kt * 4 * NB * 32;
 };
 
-__device__ __forceinline__ void load_ktile(KTileRegs& R, const uint4* blk, int lane) {
-#pragma unroll
-    for (int r = 0; r < kTilesPerWarp; ++r) {
-        R.nib[r][0] = ldg_stream(blk + (r * 2 + 0) * 32 + lane);
-        R.nib[r][1] = ldg_stream(blk + (r * 2 + 1) * 32 + lane);
-    }
-#pragma unroll
-    for (int r = 0; r < kTilesPerWarp; ++r) R.sb[r] = ldg_stream(blk + 256 + r * 8 + (lane >> 2));
-}
-
-// One k-tile for one warp: 4 row tiles x 128 k. P = group partials, acc = totals.
+// One k-tile for one warp: 4 row tiles x 128 k, weights from the shared-memory ring.
 template <int NB, int NACC, bool PACKED>
-__device__ __forceinline__ void compute_ktile(const KTileRegs& R, const uint4* bsm, const float4* gsm,
+__device__ __forceinline__ void compute_ktile(const uint4* __restrict__ blk, const uint4* __restrict__ bsm,
+                                              const float4* __restrict__ gsm,
                                               float (&acc)[kTilesPerWarp][NACC][4], int lane) {
     constexpr uint32_t M0 = 0x000F000Fu, M1 = 0x00F000F0u;
     const float zero[4] = {0.f, 0.f, 0.f, 0.f};
+    uint4 nib[kTilesPerWarp][2], sb[kTilesPerWarp];
+#pragma unroll
+    for (int r = 0; r < kTilesPerWarp; ++r) {
+        nib[r][0] = blk[(r * 2 + 0) * 32 + lane];
+        nib[r][1] = blk[(r * 2 + 1) * 32 + lane];
+        sb[r] = blk[256 + r * 8 + (lane >> 2)];
+    }
     float P[kTilesPerWarp][NACC][4];
 #pragma unroll
     for (int kk = 0; kk < 4; ++kk) {
@@ -84,26 +76,27 @@ __device__ __forceinline__ void compute_ktile(const KTileRegs& R, const uint4* b
 #pragma unroll
         for (int nb = 0; nb < NB; ++nb) bf[nb] = bsm[(kk * NB + nb) * 32 + lane];
         const bool first = (kk & 1) == 0;
+        // Row tiles innermost: consecutive MMAs are independent, so the four accumulation
+        // chains of a warp overlap in the tensor pipe.
 #pragma unroll
-        for (int r = 0; r < kTilesPerWarp; ++r) {
-            const uint4& h = R.nib[r][kk >> 1];
-            const uint32_t wg = (kk & 1) ? h.z : h.x;
-            const uint32_t wg8 = (kk & 1) ? h.w : h.y;
-            const uint32_t wg2 = wg >> 8, wg82 = wg8 >> 8;
+        for (int step = 0; step < 2; ++step) {
 #pragma unroll
-            for (int a = 0; a < NACC; ++a) {
-                // step A: k slots {0,4} and 16x{1,5}
-                mma16816(P[r][a], wg & M0, wg8 & M0, wg & M1, wg8 & M1, bf[PACKED ? 0 : 2 * a].x,
-                         bf[PACKED ? 0 : 2 * a].y, first ? zero : P[r][a]);
-                if (!PACKED)
-                    mma16816(P[r][a], wg & M0, wg8 & M0, wg & M1, wg8 & M1, bf[2 * a + 1].x,
-                             bf[2 * a + 1].y, P[r][a]);
-                // step B: k slots {2,6} and 16x{3,7}
-                mma16816(P[r][a], wg2 & M0, wg82 & M0, wg2 & M1, wg82 & M1, bf[PACKED ? 0 : 2 * a].z,
-                         bf[PACKED ? 0 : 2 * a].w, P[r][a]);
-                if (!PACKED)
-                    mma16816(P[r][a], wg2 & M0, wg82 & M0, wg2 & M1, wg82 & M1, bf[2 * a + 1].z,
-                             bf[2 * a + 1].w, P[r][a]);
+            for (int part = 0; part < (PACKED ? 1 : 2); ++part) {
+#pragma unroll
+                for (int a = 0; a < NACC; ++a) {
+                    const uint4& b = bf[PACKED ? 0 : 2 * a + part];
+                    const uint32_t b0 = step ? b.z : b.x, b1 = step ? b.w : b.y;
+#pragma unroll
+                    for (int r = 0; r < kTilesPerWarp; ++r) {
+                        const uint4& h = nib[r][kk >> 1];
+                        uint32_t wg = (kk & 1) ? h.z : h.x;
+                        uint32_t wg8 = (kk & 1) ? h.w : h.y;
+                        if (step) { wg >>= 8; wg8 >>= 8; }
+                        // step 0: k slots {0,4} and 16x{1,5}; step 1: {2,6} and 16x{3,7}
+                        mma16816(P[r][a], wg & M0, wg8 & M0, wg & M1, wg8 & M1, b0, b1,
+                                 (first && step == 0 && part == 0) ? zero : P[r][a]);
+                    }
+                }
             }
         }
         if (kk & 1) {
@@ -114,8 +107,8 @@ __device__ __forceinline__ void compute_ktile(const KTileRegs& R, const uint4* b
                 const float4 ey = gsm[(G * NACC + a) * 4 + (lane & 3)];  // {E0, Y0, E1, Y1}
 #pragma unroll
                 for (int r = 0; r < kTilesPerWarp; ++r) {
-                    const uint32_t sbg = G ? R.sb[r].z : R.sb[r].x;
-                    const uint32_t sbg8 = G ? R.sb[r].w : R.sb[r].y;
+                    const uint32_t sbg = G ? sb[r].z : sb[r].x;
+                    const uint32_t sbg8 = G ? sb[r].w : sb[r].y;
                     const float s0 = bf16_lo(sbg), b0 = bf16_hi(sbg);
                     const float s8 = bf16_lo(sbg8), b8 = bf16_hi(sbg8);
                     acc[r][a][0] = fmaf(ey.x, fmaf(b0, ey.y, s0 * P[r][a][0]), acc[r][a][0]);
@@ -128,159 +121,177 @@ __device__ __forceinline__ void compute_ktile(const KTileRegs& R, const uint4* b
     }
 }
 
-// First CTA whose unit range contains unit x (ranges are floor(c*T/G) .. floor((c+1)*T/G)).
-__device__ __forceinline__ long long cta_of_unit(long long x, long long T, long long G) {
-    return ((x + 1) * G + T - 1) / T - 1;
-}
-
-// Stages the B fragments and {E, Y} records of k-tiles [kt, kt + kBChunk) into shared
-// memory when kt starts a chunk. Called uniformly by every warp of the CTA.
-template <int NB, int NACC>
-__device__ __forceinline__ void stage_bfrags(const VgemmParams& p, uint4* bsm, float4* gsm, int kt,
-                                             int kt0, int kt1) {
-    if ((kt - kt0) % kBChunk != 0) return;
-    const int ce = min(kt1, kt + kBChunk);
-    __syncthreads();
-    const int nf = (ce - kt) * 4 * NB * 32;  // uint4 count
-    const uint4* fsrc = p.bfrag + (size_t)kt * 4 * NB * 32;
-    for (int i = threadIdx.x; i < nf; i += kThreads) cp_async16(bsm + i, fsrc + i);
-    const int ng = (ce - kt) * 2 * NACC * 4;  // float4 count
-    const float4* gsrc = reinterpret_cast<const float4*>(p.gsum) + (size_t)kt * 2 * NACC * 4;
-    for (int i = threadIdx.x; i < ng; i += kThreads) cp_async16(gsm + i, gsrc + i);
-    cp_async_wait_all();
-    __syncthreads();
-}
-
 template <int NB, int NACC, bool PACKED>
 __global__ void __launch_bounds__(kThreads, NACC == 2 ? 2 : 3) vgemm_kernel(VgemmParams p) {
-    extern __shared__ __align__(16) unsigned char smem_raw[];
-    uint4* bsm = reinterpret_cast<uint4*>(smem_raw);  // [kBChunk*4][NB][32]
-    float4* gsm = reinterpret_cast<float4*>(smem_raw + kBChunk * 4 * NB * 512);  // [kBChunk*2][NACC][4]
-    __shared__ int s_last;
+    extern __shared__ __align__(128) unsigned char smem_raw[];
+    constexpr int kFragU4 = Chunk<NB>::frag_u4;
+    constexpr int kGsumF4 = Chunk<NB>::kt * 2 * NACC * 4;
+    constexpr int kBufU4 = kFragU4 + kGsumF4;
+    uint4* ring = reinterpret_cast<uint4*>(smem_raw);                 // [warp][stage][288]
+    uint4* bbuf = ring + kWarps * kStages * kBlockU4;                 // [2][kBufU4]
+    uint64_t* wbar = reinterpret_cast<uint64_t*>(bbuf + 2 * kBufU4);  // [warp][stage]
+    uint64_t* bbar = wbar + kWarps * kStages;                         // [2]
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const long long T = (long long)p.n_crg * p.ktiles;
-    const long long G = gridDim.x;
-    const long long c = blockIdx.x;
-    long long u = c * T / G;
-    const long long u_end = (c + 1) * T / G;
+    const int ktiles = p.out.ktiles;
+    const int T = p.out.n_crg * ktiles;
+    const int G = gridDim.x;
+    const int c = blockIdx.x;
+    const int u_begin = (int)((long long)c * T / G), u_end = (int)((long long)(c + 1) * T / G);
+    const int n_units = u_end - u_begin;
     const uint4* wbase = reinterpret_cast<const uint4*>(p.w);
 
-    bool waited = false;
-    while (u < u_end) {
-        const int crg = (int)(u / p.ktiles);
-        const int kt0 = (int)(u % p.ktiles);
-        const int kt1 = (int)min((long long)p.ktiles, (long long)kt0 + (u_end - u));
-        const int wrg = crg * kWarps + warp;
-        const bool active = wrg < p.n_wrg;
-        const uint4* wrow = wbase + ((size_t)wrg * p.ktiles) * (kKTileBytes / 16);
-
-        float acc[kTilesPerWarp][NACC][4];
-#pragma unroll
-        for (int r = 0; r < kTilesPerWarp; ++r)
-#pragma unroll
-            for (int a = 0; a < NACC; ++a)
-#pragma unroll
-                for (int i = 0; i < 4; ++i) acc[r][a][i] = 0.f;
-
-        KTileRegs ra, rb;
-        if (active) load_ktile(ra, wrow + (size_t)kt0 * (kKTileBytes / 16), lane);
-        if (!waited) {
-            // Weights do not depend on the previous kernel; activations and outputs do.
-            pdl_wait();
-            waited = true;
-        }
-        // Two k-tiles per trip so the double buffer never needs register copies. kBChunk is
-        // even, so chunk boundaries only fall on the first half of a trip.
-        for (int kt = kt0; kt < kt1; kt += 2) {
-            stage_bfrags<NB, NACC>(p, bsm, gsm, kt, kt0, kt1);
-            const int ci = (kt - kt0) % kBChunk;
-            if (active) {
-                if (kt + 1 < kt1) load_ktile(rb, wrow + (size_t)(kt + 1) * (kKTileBytes / 16), lane);
-                compute_ktile<NB, NACC, PACKED>(ra, bsm + ci * 4 * NB * 32, gsm + ci * 2 * NACC * 4, acc, lane);
-            }
-            if (kt + 1 >= kt1) break;
-            if (active) {
-                if (kt + 2 < kt1) load_ktile(ra, wrow + (size_t)(kt + 2) * (kKTileBytes / 16), lane);
-                compute_ktile<NB, NACC, PACKED>(rb, bsm + (ci + 1) * 4 * NB * 32, gsm + (ci + 1) * 2 * NACC * 4, acc, lane);
-            }
-        }
-
-        // ---- segment epilogue ----
-        const bool full = (kt0 == 0 && kt1 == p.ktiles);
-        const float kScale = 16777216.0f;  // 2^24
-        const int g = lane >> 2, t = lane & 3;
-        int slot = 0, nslots = 1;
-        if (!full) {
-            const long long lo = cta_of_unit((long long)crg * p.ktiles, T, G);
-            const long long hi = cta_of_unit((long long)(crg + 1) * p.ktiles - 1, T, G);
-            slot = (int)(c - lo);
-            nslots = (int)(hi - lo + 1);
-        }
-        if (active) {
-#pragma unroll
-            for (int r = 0; r < kTilesPerWarp; ++r) {
-#pragma unroll
-                for (int a = 0; a < NACC; ++a) {
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        float v = acc[r][a][i];
-                        if (PACKED) v += __shfl_xor_sync(0xffffffffu, v, 2);
-                        acc[r][a][i] = v * kScale;
-                    }
-                    if (PACKED && t >= 2) continue;
-#pragma unroll
-                    for (int i = 0; i < 4; ++i) {
-                        const int m = a * 8 + 2 * t + (i & 1);
-                        const int nl = warp * kWarpRows + r * 16 + g + ((i >> 1) << 3);
-                        const int n = crg * kCtaRows + nl;
-                        if (m >= p.M) continue;
-                        if (full) {
-                            if (n < p.N) p.out[(size_t)m * p.ldo + n] = acc[r][a][i];
-                        } else {
-                            p.part[(((size_t)crg * p.max_slots + slot) * kMaxM + m) * kCtaRows + nl] = acc[r][a][i];
-                        }
-                    }
-                }
-            }
-        }
-        if (!full) {
-            __threadfence();
-            __syncthreads();
-            if (threadIdx.x == 0) {
-                const int prev = atomicAdd(p.counters + crg, 1);
-                s_last = (prev == nslots - 1);
-            }
-            __syncthreads();
-            if (s_last) {
-                __threadfence();
-                const float* base = p.part + (size_t)crg * p.max_slots * kMaxM * kCtaRows;
-                for (int i = threadIdx.x; i < p.M * kCtaRows; i += kThreads) {
-                    const int m = i / kCtaRows, nl = i % kCtaRows;
-                    const int n = crg * kCtaRows + nl;
-                    float s = 0.f;
-                    for (int sl = 0; sl < nslots; ++sl)
-                        s += __ldcg(base + ((size_t)sl * kMaxM + m) * kCtaRows + nl);
-                    if (n < p.N) p.out[(size_t)m * p.ldo + n] = s;
-                }
-                if (threadIdx.x == 0) p.counters[crg] = 0;
-            }
-        }
-        u += (kt1 - kt0);
+    if (lane == 0)
+        for (int s = 0; s < kStages; ++s) mbar_init(&wbar[warp * kStages + s], 1);
+    if (threadIdx.x == 0) {
+        mbar_init(&bbar[0], 1);
+        mbar_init(&bbar[1], 1);
     }
-    if (!waited) pdl_wait();
+    mbar_init_fence();
+    __syncthreads();
+
+    // Unit cursors advance incrementally: no integer division inside the streaming loop.
+    struct Cursor {
+        int u, crg, kt;
+    };
+    auto advance = [&](Cursor& q) {
+        ++q.u;
+        if (++q.kt == ktiles) { q.kt = 0; ++q.crg; }
+    };
+    auto active = [&](const Cursor& q) { return q.crg * kWarps + warp < p.n_wrg; };
+    auto issue_w = [&](const Cursor& q, int i) {  // lane 0: unit q (the CTA's i-th) into stage i % kStages
+        uint64_t* bar = &wbar[warp * kStages + (i % kStages)];
+        mbar_expect_tx(bar, kKTileBytes);
+        bulk_g2s(ring + (warp * kStages + (i % kStages)) * kBlockU4,
+                 wbase + ((size_t)q.u * kWarps + warp) * kBlockU4, kKTileBytes, bar);
+    };
+    struct ChunkRec {
+        int s, kt, len;
+    };
+    auto make_chunk = [&](int s0, int kt0) {
+        ChunkRec r;
+        r.s = s0;
+        r.kt = kt0;
+        r.len = min(min(Chunk<NB>::kt, ktiles - kt0), u_end - s0);
+        return r;
+    };
+    auto next_chunk = [&](const ChunkRec& r) {
+        const int kt = r.kt + r.len == ktiles ? 0 : r.kt + r.len;
+        return make_chunk(r.s + r.len, kt);
+    };
+    auto issue_b = [&](const ChunkRec& r, int buf) {  // thread 0: activation fragments of a chunk
+        const uint32_t fb = (uint32_t)r.len * 4 * NB * 512, gb = (uint32_t)r.len * 2 * NACC * 64;
+        mbar_expect_tx(&bbar[buf], fb + gb);
+        bulk_g2s(bbuf + buf * kBufU4, p.bfrag + (size_t)r.kt * 4 * NB * 32, fb, &bbar[buf]);
+        bulk_g2s(bbuf + buf * kBufU4 + kFragU4, reinterpret_cast<const float4*>(p.gsum) + (size_t)r.kt * 2 * NACC * 4,
+                 gb, &bbar[buf]);
+    };
+
+    Cursor cur{u_begin, u_begin / ktiles, u_begin % ktiles};
+    Cursor pre = cur;  // the unit kStages ahead of `cur`
+    // Weight prefetch does not depend on the previous kernel: issue it before the wait.
+    for (int i = 0; i < kStages; ++i) {
+        if (i < n_units && lane == 0 && active(pre)) issue_w(pre, i);
+        advance(pre);
+    }
+    pdl_wait();
+
+    ChunkRec chk = make_chunk(cur.u, cur.kt);
+    ChunkRec nxt = next_chunk(chk);
+    int ch = 0;
+    if (threadIdx.x == 0 && n_units > 0) {
+        issue_b(chk, 0);
+        if (nxt.s < u_end) issue_b(nxt, 1);
+    }
+    bool failed = n_units > 0 && !mbar_wait(&bbar[0], 0);
+    uint32_t wphase = 0;  // bit s: parity of the next completion of stage s
+
+    float acc[kTilesPerWarp][NACC][4];
+#pragma unroll
+    for (int r = 0; r < kTilesPerWarp; ++r)
+#pragma unroll
+        for (int a = 0; a < NACC; ++a)
+#pragma unroll
+            for (int i = 0; i < 4; ++i) acc[r][a][i] = 0.f;
+    int seg_crg = cur.crg;
+    const int g = lane >> 2, t = lane & 3;
+
+    auto flush_segment = [&](int crg) {
+        const int lo = vgemm_cta_of_unit((long long)crg * ktiles, T, G);
+        const int slot = c - lo;
+        const bool act = crg * kWarps + warp < p.n_wrg;
+        float* dst = p.out.part + ((size_t)crg * p.out.max_slots + slot) * kMaxM * kCtaRows;
+#pragma unroll
+        for (int r = 0; r < kTilesPerWarp; ++r) {
+#pragma unroll
+            for (int a = 0; a < NACC; ++a) {
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    float v = acc[r][a][i];
+                    if (PACKED) v += __shfl_xor_sync(0xffffffffu, v, 2);
+                    v *= 16777216.0f;  // 2^24: the subnormal operand scale
+                    const int m = a * 8 + 2 * t + (i & 1);
+                    const int nl = warp * kWarpRows + r * 16 + g + ((i >> 1) << 3);
+                    if (act && !failed && (!PACKED || t < 2) && m < p.M) dst[m * kCtaRows + nl] = v;
+                    acc[r][a][i] = 0.f;
+                }
+            }
+        }
+    };
+
+    for (int i = 0; i < n_units; ++i) {
+        if (cur.u == chk.s + chk.len) {
+            // Next chunk: everyone is done with chunk ch, so its buffer's successor may load.
+            __syncthreads();
+            ++ch;
+            chk = nxt;
+            nxt = next_chunk(chk);
+            if (threadIdx.x == 0 && nxt.s < u_end && !failed) {
+                fence_proxy_async();  // generic reads of that buffer precede the bulk write
+                issue_b(nxt, (ch + 1) & 1);
+            }
+            if (!failed && !mbar_wait(&bbar[ch & 1], (ch >> 1) & 1)) failed = true;
+        }
+        if (cur.crg != seg_crg) {
+            flush_segment(seg_crg);
+            seg_crg = cur.crg;
+        }
+        const int stage = i % kStages;
+        if (active(cur)) {
+            uint64_t* bar = &wbar[warp * kStages + stage];
+            if (!failed && !mbar_wait(bar, (wphase >> stage) & 1)) failed = true;
+            wphase ^= 1u << stage;
+            if (!failed) {
+                const int off = cur.u - chk.s;
+                const uint4* bsm = bbuf + (ch & 1) * kBufU4 + off * 4 * NB * 32;
+                const float4* gsm = reinterpret_cast<const float4*>(bbuf + (ch & 1) * kBufU4 + kFragU4) + off * 2 * NACC * 4;
+                compute_ktile<NB, NACC, PACKED>(ring + (warp * kStages + stage) * kBlockU4, bsm, gsm, acc, lane);
+            }
+        }
+        __syncwarp();
+        if (lane == 0 && !failed && i + kStages < n_units && active(pre)) {
+            fence_proxy_async();
+            issue_w(pre, i + kStages);
+        }
+        advance(cur);
+        advance(pre);
+    }
+    if (n_units > 0) flush_segment(seg_crg);
+    if (failed && p.err) atomicExch(p.err, 1);
 }
 
-template <int NB, int NACC, bool PACKED>
-static size_t smem_bytes() {
-    return (size_t)kBChunk * 4 * NB * 512 + (size_t)kBChunk * 2 * NACC * 4 * sizeof(float4);
+template <int NB, int NACC>
+static constexpr size_t smem_bytes() {
+    return (size_t)kWarps * kStages * kKTileBytes +
+           2 * ((size_t)Chunk<NB>::frag_u4 * 16 + (size_t)Chunk<NB>::kt * 2 * NACC * 64) +
+           (kWarps * kStages + 2) * sizeof(uint64_t);
 }
 
 template <int NB, int NACC, bool PACKED>
 static int max_ctas_per_sm() {
     static int cached = -1;
     if (cached < 0) {
-        const size_t sm = smem_bytes<NB, NACC, PACKED>();
+        const size_t sm = smem_bytes<NB, NACC>();
         cudaFuncSetAttribute(vgemm_kernel<NB, NACC, PACKED>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
         int n = 0;
         cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, vgemm_kernel<NB, NACC, PACKED>, kThreads, sm);
@@ -300,18 +311,24 @@ static int sm_count() {
 }
 
 template <int NB, int NACC, bool PACKED>
-static cudaError_t launch_t(VgemmParams p, int grid, cudaStream_t st, bool pdl) {
-    cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(grid);
-    cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = smem_bytes<NB, NACC, PACKED>();
-    cfg.stream = st;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-    attr[0].val.programmaticStreamSerializationAllowed = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, vgemm_kernel<NB, NACC, PACKED>, p);
+static cudaError_t launch_t(const VgemmParams& p, cudaStream_t st, bool pdl) {
+    max_ctas_per_sm<NB, NACC, PACKED>();  // sets the dynamic shared memory attribute once
+    return launch(vgemm_kernel<NB, NACC, PACKED>, dim3(p.out.grid), dim3(kThreads), smem_bytes<NB, NACC>(), st,
+                  pdl, p);
+}
+
+__global__ void vgemm_reduce_kernel(PartView v, int M, int N, float* out, int ldo) {
+    pdl_wait();
+    const int n4 = (N + 3) / 4;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < M * n4; i += gridDim.x * blockDim.x) {
+        const int m = i / n4, n = (i % n4) * 4;
+        const float4 s = vgemm_part_get4(v, m, n);
+        float* o = out + (size_t)m * ldo + n;
+        o[0] = s.x;
+        if (n + 1 < N) o[1] = s.y;
+        if (n + 2 < N) o[2] = s.z;
+        if (n + 3 < N) o[3] = s.w;
+    }
 }
 
 }  // namespace g4b
@@ -336,10 +353,23 @@ int vgemm_max_slots(int grid, int n_crg, int ktiles) {
     return (int)((ktiles + min_units - 1) / min_units + 1);
 }
 
-cudaError_t vgemm_launch(const VgemmParams& p, int grid, cudaStream_t st, bool pdl) {
+int vgemm_plan_slots(int n_crg, int ktiles) {
+    int s = 0;
+    for (int M : {1, 5, 16}) s = std::max(s, vgemm_max_slots(vgemm_grid(M, n_crg, ktiles), n_crg, ktiles));
+    return s;
+}
+
+cudaError_t vgemm_launch(const VgemmParams& p, cudaStream_t st, bool pdl) {
     if (p.M < 1 || p.M > kMaxM) return cudaErrorInvalidValue;
+    if (vgemm_max_slots(p.out.grid, p.out.n_crg, p.out.ktiles) > p.out.max_slots) return cudaErrorInvalidValue;
     const BMode md = bmode_for(p.M);
-    if (md.packed) return launch_t<1, 1, true>(p, grid, st, pdl);
-    if (md.nb == 2) return launch_t<2, 1, false>(p, grid, st, pdl);
-    return launch_t<4, 2, false>(p, grid, st, pdl);
+    if (md.packed) return launch_t<1, 1, true>(p, st, pdl);
+    if (md.nb == 2) return launch_t<2, 1, false>(p, st, pdl);
+    return launch_t<4, 2, false>(p, st, pdl);
+}
+
+cudaError_t vgemm_reduce(const PartView& v, int M, int N, float* out, int ldo, cudaStream_t st, bool pdl) {
+    const int n = M * ((N + 3) / 4);
+    const int blocks = std::min(1184, (n + 255) / 256);
+    return launch(vgemm_reduce_kernel, dim3(blocks), dim3(256), 0, st, pdl, v, M, N, out, ldo);
 }

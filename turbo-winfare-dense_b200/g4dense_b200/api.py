@@ -29,6 +29,8 @@ def lib():
         L.g4b_qmat_prepare_input.argtypes = [_vp, _vp, ctypes.c_int, ctypes.c_int, _vp]
         L.g4b_qmat_run.argtypes = [_vp, ctypes.c_int, _vp, ctypes.c_int, _vp]
         L.g4b_qmat_info.argtypes = [_vp, _vp]
+        L.g4b_qmat_run_partial.argtypes = [_vp, ctypes.c_int, _vp]
+        L.g4b_qmat_check_error.argtypes = [_vp]
         _bind_engine(L)
         _lib = L
     return _lib
@@ -84,6 +86,12 @@ class QMat:
 
     def run(self, M, out, stream=None):
         _check(lib().g4b_qmat_run(self.h, M, _dptr(out), out.shape[1], _stream(stream)), "g4b_qmat_run")
+
+    def run_partial(self, M, stream=None):
+        _check(lib().g4b_qmat_run_partial(self.h, M, _stream(stream)), "g4b_qmat_run_partial")
+
+    def check_error(self):
+        _check(lib().g4b_qmat_check_error(self.h), "g4b_qmat_check_error")
 
     def info(self):
         o = np.zeros(4, np.int32)
