@@ -794,10 +794,12 @@ int g4o_spec_generate(g4o_model* tgt, g4o_model* drf, const uint32_t* prompt, in
     if (drf && verify_width > 0) {
         g4o_truncate(drf, 0);
         size_t consumed = 0;
-        const uint32_t K = verify_width < 8 ? (uint32_t)verify_width : 8u;
+        /* The reference caps K at 8 (kGemmMaxBatch); the B200 engine at 16, which BASELINE's k = 8
+         * configuration needs. Widths <= 8 behave identically. */
+        const uint32_t K = verify_width < 16 ? (uint32_t)verify_width : 16u;
         float* verify = (float*)malloc(sizeof(float) * V * K);
         float* dlog = (float*)malloc(sizeof(float) * V * K);
-        uint32_t drafts[8], acc_toks[9];
+        uint32_t drafts[16], acc_toks[17];
         uint32_t drafted_total = 0, accepted_total = 0;
         int drafting = 1;
         uint32_t pending = g4o_sample_token(logits, V, sp, g4o_seed_for(sp, (int)(hn - 1)));

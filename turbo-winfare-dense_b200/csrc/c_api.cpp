@@ -1,0 +1,389 @@
+// The engine's C ABI (include/g4dense/c_api.h). Exceptions never cross it: failures return
+// nullptr / -1 with a thread-local message, as src/c_api.cpp does.
+#include "g4dense/c_api.h"
+
+#include <atomic>
+#include <cstdlib>
+#include <cstring>
+#include <memory>
+#include <sstream>
+#include <string>
+#include <vector>
+
+#include "runner.h"
+
+#ifdef G4B_HAVE_NCCL
+#include <nccl.h>
+#endif
+
+namespace {
+
+thread_local std::string g_last_error;
+void set_error(const std::string& m) { g_last_error = m; }
+void clear_error() { g_last_error.clear(); }
+
+struct EngineHandle {
+    std::unique_ptr<g4b::Engine> engine;
+    std::atomic<bool> cancel{false};
+    std::string last_response, last_telemetry;
+    std::vector<uint32_t> last_tokens;
+    int last_stop_reason{0};
+    int draft_k{0};
+    int64_t stop_token{-1};
+    std::vector<uint32_t> replay;
+    double mismatch_rate{0};
+    uint64_t mismatch_seed{0};
+    double gate_min_accept{0.45};
+    int gate_window{24};
+    void* nccl_comm{nullptr};
+    ~EngineHandle() {
+        engine.reset();
+#ifdef G4B_HAVE_NCCL
+        if (nccl_comm) ncclCommDestroy((ncclComm_t)nccl_comm);
+#endif
+    }
+};
+
+// Model geometries for device-generated weights, with an optional ":layers=N" override.
+bool preset_header(const std::string& spec, g4b::G4DenseHeader& h) {
+    std::string name = spec;
+    int layers = -1;
+    const size_t colon = spec.find(':');
+    if (colon != std::string::npos) {
+        name = spec.substr(0, colon);
+        const std::string rest = spec.substr(colon + 1);
+        if (rest.rfind("layers=", 0) == 0) layers = std::atoi(rest.c_str() + 7);
+    }
+    std::memset(&h, 0, sizeof(h));
+    h.rope_theta_local = 10000.0f;
+    h.rope_theta_global = 1000000.0f;
+    h.rope_scaling = 1.0f;
+    h.final_logit_softcapping = 30.0f;
+    h.scale_dtype = 1;
+    if (name == "gemma4-31b") {
+        // docs/FORWARD_PASS.md constants: global layers every 6th from layer 5.
+        h.num_layers = 60; h.d_model = 5376; h.d_ff = 21504; h.num_q_heads = 32; h.num_kv_heads = 16;
+        h.head_dim = 256; h.vocab_size = 262144; h.sliding_window = 1024;
+        h.global_layer_mask = 0x0820820820820820ull; h.global_head_dim = 512; h.global_kv_heads = 4;
+    } else if (name == "gemma4-e2b") {
+        h.num_layers = 35; h.d_model = 1536; h.d_ff = 6144; h.num_q_heads = 8; h.num_kv_heads = 1;
+        h.head_dim = 256; h.vocab_size = 262144; h.sliding_window = 512;
+    } else if (name == "config0-target") {
+        h.num_layers = 4; h.d_model = 256; h.d_ff = 1024; h.num_q_heads = 4; h.num_kv_heads = 1;
+        h.head_dim = 64; h.vocab_size = 4096; h.sliding_window = 1024;
+    } else if (name == "config0-draft") {
+        h.num_layers = 2; h.d_model = 128; h.d_ff = 512; h.num_q_heads = 2; h.num_kv_heads = 1;
+        h.head_dim = 64; h.vocab_size = 4096; h.sliding_window = 1024;
+    } else {
+        return false;
+    }
+    if (layers > 0 && layers <= 60) {
+        h.num_layers = (uint32_t)layers;
+        h.global_layer_mask &= (layers == 64) ? ~0ull : ((1ull << layers) - 1);
+    }
+    for (uint32_t l = 0; l < h.num_layers; ++l) h.layer_d_ff[l] = h.d_ff;
+    return true;
+}
+
+g4b::GenerationOptions to_gen(const EngineHandle* e, const G4DenseGenerationOptions* o) {
+    g4b::GenerationOptions g;
+    if (o) {
+        g.max_tokens = o->max_tokens;
+        g.sampling.temperature = o->temperature;
+        g.sampling.top_p = o->top_p;
+        g.sampling.top_k = o->top_k;
+        g.sampling.repetition_penalty = o->repetition_penalty;
+        g.sampling.has_seed = o->has_seed != 0;
+        g.sampling.seed = o->seed;
+    }
+    g.speculative_enabled = e->draft_k > 0 && e->engine->draft() != nullptr;
+    g.draft_k = (uint32_t)std::max(0, e->draft_k);
+    g.stop_token = e->stop_token;
+    g.replay = e->replay;
+    g.mismatch_rate = e->mismatch_rate;
+    g.mismatch_seed = e->mismatch_seed;
+    g.gate_min_accept = e->gate_min_accept;
+    g.gate_window = e->gate_window;
+    return g;
+}
+
+}  // namespace
+
+extern "C" {
+
+G4DENSE_API const char* g4dense_engine_last_error(void) { return g_last_error.c_str(); }
+
+G4DENSE_API void g4dense_options_default(G4DenseGenerationOptions* out) {
+    if (!out) return;
+    out->max_tokens = 512;
+    out->temperature = 0.2f;
+    out->top_p = 0.95f;
+    out->top_k = 64;
+    out->repetition_penalty = 1.0f;
+    out->has_seed = 0;
+    out->seed = 0;
+    out->system_prompt = nullptr;
+    out->stop_strings = nullptr;
+    out->stop_count = 0;
+    out->tier_id = 1;
+}
+
+G4DENSE_API void g4dense_config_default(G4DenseEngineConfig* c) {
+    if (!c) return;
+    std::memset(c, 0, sizeof(*c));
+    c->max_context = 4096;
+    c->tp_size = 1;
+    c->device = -1;
+    c->gate_min_accept = 0.45;
+    c->gate_window = 24;
+}
+
+G4DENSE_API int g4dense_nccl_unique_id(void* out128) {
+    clear_error();
+#ifdef G4B_HAVE_NCCL
+    ncclUniqueId id;
+    if (ncclGetUniqueId(&id) != ncclSuccess) {
+        set_error("ncclGetUniqueId failed");
+        return -1;
+    }
+    std::memcpy(out128, &id, sizeof(id));
+    return 0;
+#else
+    (void)out128;
+    set_error("built without NCCL");
+    return -1;
+#endif
+}
+
+G4DENSE_API void* g4dense_engine_create_ex(const G4DenseEngineConfig* cfg) {
+    clear_error();
+    if (!cfg) {
+        set_error("null config");
+        return nullptr;
+    }
+    try {
+        if (cfg->device >= 0) g4b::cuda_check(cudaSetDevice(cfg->device), "cudaSetDevice");
+        int ndev = 0;
+        g4b::cuda_check(cudaGetDeviceCount(&ndev), "cudaGetDeviceCount");
+        auto h = std::make_unique<EngineHandle>();
+        g4b::ModelOptions mo;
+        mo.max_context = cfg->max_context > 0 ? cfg->max_context : 4096;
+        mo.kv_bf16 = cfg->kv_bf16;
+        mo.rank = cfg->tp_rank;
+        mo.tp = cfg->tp_size > 0 ? cfg->tp_size : 1;
+        if (const char* g = std::getenv("G4DENSE_NO_GRAPHS")) mo.use_graphs = std::atoi(g) == 0;
+        if (mo.tp > 1) {
+#ifdef G4B_HAVE_NCCL
+            if (!cfg->nccl_unique_id) throw std::invalid_argument("tensor parallelism needs an NCCL unique id");
+            ncclUniqueId id;
+            std::memcpy(&id, cfg->nccl_unique_id, sizeof(id));
+            ncclComm_t comm;
+            if (ncclCommInitRank(&comm, mo.tp, id, mo.rank) != ncclSuccess)
+                throw std::runtime_error("ncclCommInitRank failed");
+            h->nccl_comm = comm;
+            mo.nccl_comm = comm;
+#else
+            throw std::invalid_argument("built without NCCL");
+#endif
+        }
+        auto target = std::make_unique<g4b::DeviceModel>(mo);
+        if (cfg->container_path && *cfg->container_path) {
+            target->load_container(cfg->container_path);
+        } else if (cfg->synthetic_preset) {
+            g4b::G4DenseHeader gh;
+            if (!preset_header(cfg->synthetic_preset, gh)) throw std::invalid_argument("unknown synthetic preset");
+            target->load_synthetic(gh, cfg->synthetic_seed, cfg->synthetic_centered != 0);
+        } else {
+            throw std::invalid_argument("no target container or synthetic preset");
+        }
+        const cudaStream_t st = target->stream();
+        h->engine = std::make_unique<g4b::Engine>(std::move(target));
+        if ((cfg->draft_path && *cfg->draft_path) || cfg->draft_preset) {
+            // The drafter stays whole on every rank (it is small); it shares the target's stream.
+            g4b::ModelOptions dopt;
+            dopt.max_context = mo.max_context;
+            dopt.kv_bf16 = mo.kv_bf16;
+            dopt.stream = st;
+            dopt.use_graphs = mo.use_graphs;
+            auto d = std::make_unique<g4b::DeviceModel>(dopt);
+            if (cfg->draft_path && *cfg->draft_path) {
+                d->load_container(cfg->draft_path);
+            } else {
+                g4b::G4DenseHeader dh;
+                if (!preset_header(cfg->draft_preset, dh)) throw std::invalid_argument("unknown drafter preset");
+                d->load_synthetic(dh, cfg->draft_seed, cfg->synthetic_centered != 0);
+            }
+            h->engine->set_draft(std::move(d));
+        }
+        h->draft_k = cfg->draft_k;
+        h->gate_min_accept = cfg->gate_min_accept;
+        h->gate_window = cfg->gate_window;
+        return h.release();
+    } catch (const std::exception& e) {
+        set_error(e.what());
+        return nullptr;
+    }
+}
+
+G4DENSE_API void* g4dense_engine_create(const char* container_path) {
+    G4DenseEngineConfig c;
+    g4dense_config_default(&c);
+    const std::string path = (container_path && *container_path) ? container_path : "gemma-4-31b-dense.g4dense";
+    c.container_path = path.c_str();
+    // Speculation is opt-in, as in the reference; these environment variables enable it
+    // without changing the signature.
+    if (const char* d = std::getenv("G4DENSE_DRAFT_MODEL")) c.draft_path = d;
+    if (const char* k = std::getenv("G4DENSE_SPEC_K")) c.draft_k = std::atoi(k);
+    if (const char* m = std::getenv("G4DENSE_SPEC_GATE_MIN_ACCEPT")) c.gate_min_accept = std::atof(m);
+    if (const char* w = std::getenv("G4DENSE_SPEC_GATE_WINDOW")) c.gate_window = std::max(0, std::atoi(w));
+    return g4dense_engine_create_ex(&c);
+}
+
+G4DENSE_API void g4dense_engine_destroy(void* handle) { delete static_cast<EngineHandle*>(handle); }
+
+G4DENSE_API const char* g4dense_engine_generate(void* handle, const char* prompt, int max_tokens) {
+    clear_error();
+    (void)max_tokens;
+    if (!handle || !prompt) {
+        set_error("Invalid handle or null prompt");
+        return nullptr;
+    }
+    set_error("text prompts need the reference tokenizer (tokenizer.json), which this engine does not load; "
+              "use g4dense_engine_generate_tokens");
+    return nullptr;
+}
+
+G4DENSE_API const char* g4dense_engine_generate_ex(void* handle, const char* messages_json,
+                                                   const G4DenseGenerationOptions* opts, G4DenseTokenCallback on_token,
+                                                   void* user) {
+    clear_error();
+    (void)opts;
+    (void)on_token;
+    (void)user;
+    if (!handle || !messages_json) {
+        set_error("Invalid handle or null messages");
+        return nullptr;
+    }
+    set_error("chat messages need the reference tokenizer (tokenizer.json), which this engine does not load; "
+              "use g4dense_engine_generate_tokens");
+    return nullptr;
+}
+
+G4DENSE_API const char* g4dense_engine_generate_tokens(void* handle, const unsigned int* prompt_ids, int n_prompt,
+                                                       const G4DenseGenerationOptions* opts,
+                                                       G4DenseTokenCallback on_token, void* user) {
+    clear_error();
+    if (!handle || !prompt_ids || n_prompt <= 0) {
+        set_error("Invalid handle or empty prompt");
+        return nullptr;
+    }
+    auto* e = static_cast<EngineHandle*>(handle);
+    try {
+        e->cancel.store(false);
+        const g4b::GenerationOptions g = to_gen(e, opts);
+        std::vector<uint32_t> prompt(prompt_ids, prompt_ids + n_prompt);
+        int idx = 0;
+        auto cb = [&](uint32_t t) {
+            if (!on_token) return true;
+            return on_token(user, idx++, t, "") != 0;
+        };
+        e->last_tokens = e->engine->generate(prompt, g, cb, &e->cancel);
+        const g4b::GenStats& s = e->engine->last_stats();
+        e->last_stop_reason = s.stop_reason;
+        std::ostringstream ss;
+        ss << "{\"tokens\": " << e->last_tokens.size() << ", \"drafted\": " << s.drafted << ", \"accepted\": "
+           << s.accepted << ", \"rounds\": " << s.rounds << ", \"ttft_ms\": " << s.ttft_ms << ", \"total_ms\": "
+           << s.total_ms << "}";
+        e->last_response = ss.str();
+        return e->last_response.c_str();
+    } catch (const std::exception& ex) {
+        set_error(ex.what());
+        return nullptr;
+    }
+}
+
+G4DENSE_API int g4dense_engine_last_tokens(void* handle, unsigned int* out, int cap) {
+    if (!handle || !out || cap < 0) return 0;
+    auto* e = static_cast<EngineHandle*>(handle);
+    const int n = std::min<int>(cap, (int)e->last_tokens.size());
+    std::memcpy(out, e->last_tokens.data(), (size_t)n * sizeof(unsigned int));
+    return n;
+}
+
+G4DENSE_API int g4dense_engine_last_rounds(void* handle, int* out, int cap_triples) {
+    if (!handle || !out || cap_triples < 0) return 0;
+    auto* e = static_cast<EngineHandle*>(handle);
+    const auto& ri = e->engine->last_stats().round_info;
+    const int n = std::min<int>(cap_triples, (int)ri.size() / 3);
+    std::memcpy(out, ri.data(), (size_t)n * 3 * sizeof(int));
+    return n;
+}
+
+G4DENSE_API int g4dense_engine_forward_batch(void* handle, const unsigned int* token_ids, int batch, int base_position,
+                                             float* out_logits, int all_positions) {
+    clear_error();
+    if (!handle || !token_ids || batch <= 0 || base_position < 0) {
+        set_error("Invalid arguments");
+        return -1;
+    }
+    try {
+        static_cast<EngineHandle*>(handle)->engine->forward_batch(token_ids, (uint32_t)batch, (uint32_t)base_position,
+                                                                  out_logits, all_positions != 0);
+        return 0;
+    } catch (const std::exception& e) {
+        set_error(e.what());
+        return -1;
+    }
+}
+
+G4DENSE_API int g4dense_engine_set_decode_options(void* handle, long long stop_token, int draft_k,
+                                                  const unsigned int* replay, int replay_len, double mismatch_rate,
+                                                  unsigned long long mismatch_seed) {
+    clear_error();
+    if (!handle || replay_len < 0 || mismatch_rate < 0 || mismatch_rate > 1) {
+        set_error("Invalid arguments");
+        return -1;
+    }
+    auto* e = static_cast<EngineHandle*>(handle);
+    e->stop_token = stop_token;
+    if (draft_k >= 0) e->draft_k = draft_k;
+    e->replay.assign(replay, replay ? replay + replay_len : replay);
+    e->mismatch_rate = mismatch_rate;
+    e->mismatch_seed = mismatch_seed;
+    return 0;
+}
+
+G4DENSE_API const char* g4dense_engine_get_telemetry(void* handle) {
+    if (!handle) return "{}";
+    auto* e = static_cast<EngineHandle*>(handle);
+    try {
+        e->last_telemetry = e->engine->telemetry_json();
+    } catch (const std::exception& ex) {
+        e->last_telemetry = "{}";
+    }
+    return e->last_telemetry.c_str();
+}
+
+G4DENSE_API int g4dense_engine_last_stop_reason(void* handle) {
+    if (!handle) return 0;
+    return static_cast<EngineHandle*>(handle)->last_stop_reason;
+}
+
+G4DENSE_API int g4dense_engine_switch_tier(void* handle, int tier_id) {
+    clear_error();
+    if (!handle) {
+        set_error("Null handle");
+        return -1;
+    }
+    if (tier_id < 0) {
+        set_error("Invalid tier id");
+        return -1;
+    }
+    return 0;
+}
+
+G4DENSE_API void g4dense_engine_stop(void* handle) {
+    if (handle) static_cast<EngineHandle*>(handle)->cancel.store(true);
+}
+
+}  // extern "C"

@@ -1,0 +1,114 @@
+// LM head epilogue and on-device greedy acceptance.
+//
+// Restates, for the tied INT4 head (src/cpu_reference.cpp:635-665): logits = softcap(z) with
+// softcap(z) = 30*tanh(z/30), then the greedy target token per row = argmax with ties to
+// the LOWEST index (src/sampling.cpp:297-304, shaders/ArgmaxReduce.hlsl:15-62). The argmax is
+// taken over the softcapped values, as the reference's sample_token sees them, so saturated
+// ties resolve exactly as on the CPU.
+//
+// Greedy acceptance (src/speculator.cpp:53-69, 138-146): with the verify batch
+// [pending, d1 .. d_{M-1}], draft d_{i+1} is accepted while it equals argmax(row i); the
+// emitted tokens are argmax(row 0 .. row n_acc), i.e. the accepted drafts followed by the
+// correction or bonus token.
+#include "common.cuh"
+#include "kernels.h"
+#include "launch.cuh"
+#include "model_dev.h"
+
+#include <algorithm>
+
+namespace g4b {
+
+constexpr int kHeadChunk = 4096;
+
+__device__ __forceinline__ bool better(float v, uint32_t i, float bv, uint32_t bi) {
+    return v > bv || (v == bv && i < bi);
+}
+
+__global__ void head_chunks_kernel(GemmOut lm, int V, int M, float softcap, float* logits, int ldl,
+                                   float2* chunk_best) {
+    __shared__ float sv[32];
+    __shared__ uint32_t si[32];
+    pdl_wait();
+    const int chunk = blockIdx.x, m = blockIdx.y;
+    const int v0 = chunk * kHeadChunk, v1 = min(V, v0 + kHeadChunk);
+    float bv = -INFINITY;
+    uint32_t bi = 0xFFFFFFFFu;
+    for (int v = v0 + threadIdx.x; v < v1; v += blockDim.x) {
+        float z = gemm_out_get(lm, m, v);
+        if (softcap > 0.f) z = softcap * tanhf(z / softcap);
+        if (logits) logits[(size_t)m * ldl + v] = z;
+        if (better(z, (uint32_t)v, bv, bi)) { bv = z; bi = (uint32_t)v; }
+    }
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) {
+        const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+        const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+    }
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    if (lane == 0) { sv[wid] = bv; si[wid] = bi; }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        for (int w = 1; w < (int)(blockDim.x >> 5); ++w)
+            if (better(sv[w], si[w], bv, bi)) { bv = sv[w]; bi = si[w]; }
+        chunk_best[(size_t)m * gridDim.x + chunk] = make_float2(bv, __uint_as_float(bi));
+    }
+}
+
+__global__ void head_finalize_kernel(const float2* chunk_best, int nchunks, int M, StepParams* sp,
+                                     HeadResult* res, uint32_t* chain_out) {
+    __shared__ uint32_t am[16];
+    pdl_wait();
+    const int lane = threadIdx.x & 31, m = threadIdx.x >> 5;
+    if (m < M) {
+        float bv = -INFINITY;
+        uint32_t bi = 0xFFFFFFFFu;
+        for (int c = lane; c < nchunks; c += 32) {
+            const float2 e = chunk_best[(size_t)m * nchunks + c];
+            const uint32_t i = __float_as_uint(e.y);
+            if (better(e.x, i, bv, bi)) { bv = e.x; bi = i; }
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) {
+            const float ov = __shfl_xor_sync(0xffffffffu, bv, o);
+            const uint32_t oi = __shfl_xor_sync(0xffffffffu, bi, o);
+            if (better(ov, oi, bv, bi)) { bv = ov; bi = oi; }
+        }
+        if (lane == 0) am[m] = bi;
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        int n_acc = 0;
+        while (n_acc < M - 1 && sp->tokens[n_acc + 1] == am[n_acc]) ++n_acc;
+        res->n_accepted = n_acc;
+        res->n_emit = n_acc + 1;
+        for (int i = 0; i <= n_acc; ++i) res->tokens[i] = am[i];
+        for (int i = 0; i < M; ++i) res->argmax[i] = am[i];
+        if (chain_out) {
+            const uint32_t t = am[M - 1];
+            chain_out[sp->draft_step] = t;
+            sp->draft_step += 1;
+            sp->tokens[0] = t;
+            sp->base_pos += M;
+        }
+    }
+}
+
+}  // namespace g4b
+
+using namespace g4b;
+
+int g4b_head_chunks(int V) { return (V + kHeadChunk - 1) / kHeadChunk; }
+
+cudaError_t g4b_head_chunks_launch(const GemmOut& lm, int V, int M, float softcap, float* logits, int ldl,
+                                   float2* chunk_best, cudaStream_t st, bool pdl) {
+    return launch(head_chunks_kernel, dim3(g4b_head_chunks(V), M), dim3(256), 0, st, pdl, lm, V, M, softcap, logits,
+                  ldl, chunk_best);
+}
+
+cudaError_t g4b_head_finalize(const float2* chunk_best, int nchunks, int M, StepParams* sp, HeadResult* res,
+                              uint32_t* chain_out, cudaStream_t st, bool pdl) {
+    return launch(head_finalize_kernel, dim3(1), dim3(32 * 16), 0, st, pdl, chunk_best, nchunks, M, sp, res,
+                  chain_out);
+}

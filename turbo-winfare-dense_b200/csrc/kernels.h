@@ -3,6 +3,8 @@
 #include <cuda_runtime.h>
 #include <cstdint>
 
+#include "model_dev.h"
+
 // ---- repack.cu
 size_t g4b_qmat_bytes(int N, int K);
 cudaError_t g4b_repack(const uint32_t* W, const uint16_t* S, const uint16_t* B, int N, int K, void* out,
@@ -11,3 +13,37 @@ cudaError_t g4b_repack(const uint32_t* W, const uint16_t* S, const uint16_t* B, 
 // ---- rowops.cu
 // x fp32 [M][ldx] (K used columns) -> B fragments for a K-column GEMM input (K padded to 128).
 cudaError_t g4b_bfrag_from_f32(const float* x, int ldx, int M, int K, void* bfrag, cudaStream_t st, bool pdl);
+cudaError_t g4b_embed_norm(const g4b::StepParams* sp, const uint32_t* ew, const uint16_t* es, const uint16_t* eb,
+                           int V, int d, const uint16_t* w_in, float* h_out, void* bfrag, int M, cudaStream_t st,
+                           bool pdl);
+cudaError_t g4b_qkv_epi(const g4b::QkvEpiArgs& a, cudaStream_t st, bool pdl);
+cudaError_t g4b_post_attn(const g4b::GemmOut& o, const float* h_in, float* h_out, const uint16_t* w_pa,
+                          const uint16_t* w_pf, int d, void* bfrag, int M, cudaStream_t st, bool pdl);
+cudaError_t g4b_geglu(const g4b::GemmOut& gu, int F, void* bfrag, int M, cudaStream_t st, bool pdl);
+cudaError_t g4b_post_ffn(const g4b::GemmOut& dn, const float* h_in, float* h_out, const uint16_t* w_pffn,
+                         float layer_scalar, const uint16_t* w_next, int d, void* bfrag, int M, cudaStream_t st,
+                         bool pdl);
+
+// ---- attention.cu
+// Splits of the key range per KV head chosen for the launch (fixed per captured graph).
+int g4b_attn_nsplit(int kvh, int M, int qh, int hd);
+cudaError_t g4b_attention(const g4b::AttnArgs& a, cudaStream_t st, bool pdl);
+// Combines the splits and writes the attention output [M][qh*hd] as B fragments.
+cudaError_t g4b_attn_combine(const g4b::AttnArgs& a, void* bfrag, cudaStream_t st, bool pdl);
+
+// ---- head.cu
+struct HeadResult {
+    int n_emit;          // tokens emitted by greedy acceptance (accepted drafts + 1)
+    int n_accepted;      // drafts accepted
+    uint32_t tokens[17]; // emitted ids
+    uint32_t argmax[16]; // per-row greedy target token
+};
+int g4b_head_chunks(int V);
+// Softcapped logits (written when `logits` is non-null) and per-chunk (max, index).
+cudaError_t g4b_head_chunks_launch(const g4b::GemmOut& lm, int V, int M, float softcap, float* logits, int ldl,
+                                   float2* chunk_best, cudaStream_t st, bool pdl);
+// Per-row argmax (ties to the lowest index) and greedy acceptance of sp->tokens[1..M-1]
+// against argmax[0..M-2]. With chain_out (drafter steps) the last row's argmax also becomes
+// the next pass's input: sp->tokens[0] = t, sp->base_pos += M, chain_out[sp->draft_step++] = t.
+cudaError_t g4b_head_finalize(const float2* chunk_best, int nchunks, int M, g4b::StepParams* sp, HeadResult* res,
+                              uint32_t* chain_out, cudaStream_t st, bool pdl);

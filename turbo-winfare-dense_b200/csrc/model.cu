@@ -1,0 +1,631 @@
+// DeviceModel: residency, layout and the forward pass (see model.h).
+//
+// Per-layer kernel sequence for M rows (each arrow is one launch, PDL-chained and captured in
+// a CUDA graph per M):
+//   [qkv GEMM] -> qkv_epi (norms, RoPE, K/V ring) -> attention -> combine (o fragments)
+//   -> [o GEMM] -> post_attn (residual, pre-FFN norm) -> [gate|up GEMM] -> geglu
+//   -> [down GEMM] -> post_ffn (residual * layer_scalar, next input norm)
+// then [LM head GEMM] -> head_chunks (softcap, chunk argmax) -> head_finalize (argmax, greedy
+// acceptance). With tensor parallelism the o and down outputs are reduced across ranks with
+// one NCCL all-reduce each, and the head's chunk winners with one all-gather.
+#include "model.h"
+
+#include <fcntl.h>
+#include <sys/mman.h>
+#include <sys/stat.h>
+#include <unistd.h>
+
+#include <algorithm>
+#include <cmath>
+#include <cstring>
+#include <sstream>
+
+#include "common.cuh"
+#include "synth.h"
+#include "vgemm.h"
+
+#ifdef G4B_HAVE_NCCL
+#include <nccl.h>
+#endif
+
+namespace g4b {
+
+void cuda_check(cudaError_t e, const char* what) {
+    if (e != cudaSuccess) {
+        std::stringstream ss;
+        ss << what << ": " << cudaGetErrorString(e);
+        throw std::runtime_error(ss.str());
+    }
+}
+
+static int round_up(int x, int a) { return (x + a - 1) / a * a; }
+
+DeviceModel::DeviceModel(const ModelOptions& opt) : opt_(opt) {
+    if (opt_.tp < 1 || opt_.rank < 0 || opt_.rank >= opt_.tp) throw std::runtime_error("invalid tensor-parallel rank");
+#ifndef G4B_HAVE_NCCL
+    if (opt_.tp > 1) throw std::runtime_error("tensor parallelism needs the library built with NCCL");
+#endif
+    if (opt_.stream) {
+        stream_ = opt_.stream;
+        own_stream_ = false;
+    } else {
+        cuda_check(cudaStreamCreateWithFlags(&stream_, cudaStreamNonBlocking), "cudaStreamCreate");
+    }
+    cuda_check(cudaHostAlloc((void**)&sp_host_, kParamRing * sizeof(StepParams), cudaHostAllocDefault),
+               "cudaHostAlloc");
+    cuda_check(cudaHostAlloc((void**)&res_host_, sizeof(HeadResult), cudaHostAllocDefault), "cudaHostAlloc");
+}
+
+DeviceModel::~DeviceModel() {
+    if (stream_) cudaStreamSynchronize(stream_);
+    for (auto& kv : graphs_) cudaGraphExecDestroy(kv.second);
+    for (void* p : allocs_) cudaFree(p);
+    if (sp_host_) cudaFreeHost(sp_host_);
+    if (res_host_) cudaFreeHost(res_host_);
+    if (stream_ && own_stream_) cudaStreamDestroy(stream_);
+}
+
+void* DeviceModel::dmalloc(size_t bytes) {
+    void* p = nullptr;
+    cuda_check(cudaMalloc(&p, std::max<size_t>(bytes, 256)), "cudaMalloc");
+    allocs_.push_back(p);
+    return p;
+}
+
+uint16_t* DeviceModel::upload_u16(const uint16_t* src, size_t n) {
+    auto* d = static_cast<uint16_t*>(dmalloc(n * 2));
+    cuda_check(cudaMemcpy(d, src, n * 2, cudaMemcpyHostToDevice), "upload");
+    return d;
+}
+
+void DeviceModel::alloc_qw(QW& q, int N, int K) {
+    q.N = N;
+    q.K = K;
+    q.ktiles = vgemm_ktiles(K);
+    q.n_crg = vgemm_n_crg(N);
+    q.n_wrg = (N + 63) / 64;
+    q.max_slots = vgemm_plan_slots(q.n_crg, q.ktiles);
+    q.w = dmalloc(vgemm_weight_bytes(N, K));
+    weight_bytes_ += (uint64_t)N * K / 2 + (uint64_t)N * (K / 64) * 4;
+}
+
+// Raw matrix (device pointers, container layout) -> streaming layout.
+void DeviceModel::upload_qw(QW& q, const uint32_t* W, const uint16_t* S, const uint16_t* B, int N, int K) {
+    alloc_qw(q, N, K);
+    cuda_check(g4b_repack(W, S, B, N, K, q.w, stream_), "repack");
+}
+
+// ----------------------------------------------------------------------------- geometry
+
+namespace {
+
+struct QPtr {
+    const uint32_t* w;
+    const uint16_t* s;
+    const uint16_t* b;
+    int rows, cols;
+};
+
+// A contiguous row range [r0, r0+n) of a quantized matrix.
+struct RowRange {
+    const QPtr* m;
+    int r0, n;
+};
+
+// Local shard description of one layer.
+struct Shard {
+    int q0, qh_l, kv0, kvh_l, f0, F_l;
+};
+
+Shard make_shard(const LayerGeometry& g, int F, int rank, int tp) {
+    Shard s;
+    if (g.q_heads % tp) throw std::runtime_error("q_heads must divide by the tensor-parallel size");
+    if (F % tp || (F / tp) % 64) throw std::runtime_error("FFN width / tp must be a multiple of 64");
+    s.qh_l = g.q_heads / tp;
+    s.q0 = rank * s.qh_l;
+    const int gqa = g.q_heads / g.kv_heads;
+    s.kv0 = s.q0 / gqa;
+    s.kvh_l = (s.q0 + s.qh_l - 1) / gqa + 1 - s.kv0;
+    if (s.qh_l % s.kvh_l) throw std::runtime_error("uneven GQA split across ranks");
+    s.F_l = F / tp;
+    s.f0 = rank * s.F_l;
+    return s;
+}
+
+// Host gather of rows (several ranges, concatenated) and a 64-aligned column slice.
+void gather_host(const std::vector<RowRange>& ranges, int col0, int Kl, std::vector<uint32_t>& W,
+                 std::vector<uint16_t>& S, std::vector<uint16_t>& B) {
+    int N = 0;
+    for (auto& r : ranges) N += r.n;
+    W.resize((size_t)N * (Kl / 8));
+    S.resize((size_t)N * (Kl / 64));
+    B.resize((size_t)N * (Kl / 64));
+    size_t row = 0;
+    for (auto& r : ranges) {
+        const int K = r.m->cols;
+        for (int i = 0; i < r.n; ++i, ++row) {
+            const size_t src = (size_t)(r.r0 + i);
+            std::memcpy(&W[row * (Kl / 8)], r.m->w + src * (K / 8) + col0 / 8, (Kl / 8) * 4);
+            std::memcpy(&S[row * (Kl / 64)], r.m->s + src * (K / 64) + col0 / 64, (Kl / 64) * 2);
+            std::memcpy(&B[row * (Kl / 64)], r.m->b + src * (K / 64) + col0 / 64, (Kl / 64) * 2);
+        }
+    }
+}
+
+}  // namespace
+
+// ----------------------------------------------------------------------------- loading
+
+void DeviceModel::load_container(const std::string& path) {
+    if (loaded_) throw std::runtime_error("model already loaded");
+    const int fd = open(path.c_str(), O_RDONLY);
+    if (fd < 0) throw G4DenseFormatError("cannot open container " + path);
+    struct stat st;
+    if (fstat(fd, &st) != 0 || (size_t)st.st_size < sizeof(G4DenseHeader)) {
+        close(fd);
+        throw G4DenseFormatError("container file too small for header");
+    }
+    const size_t size = (size_t)st.st_size;
+    void* map = mmap(nullptr, size, PROT_READ, MAP_PRIVATE, fd, 0);
+    close(fd);
+    if (map == MAP_FAILED) throw G4DenseFormatError("mmap failed for " + path);
+    struct Unmap {
+        void* p;
+        size_t n;
+        ~Unmap() { munmap(p, n); }
+    } unmap{map, size};
+    const uint8_t* base = static_cast<const uint8_t*>(map);
+    std::memcpy(&h_, base, sizeof(G4DenseHeader));
+    validate_header(h_, size);
+
+    const int d = h_.d_model, V = h_.vocab_size;
+    // Embedding / tied head block (src/cpu_reference.cpp:260-285, 610-614).
+    const uint8_t* emb = base + h_.embed_offset;
+    const size_t ew = (size_t)V * (d / 8) * 4, es = (size_t)V * (d / 64) * 2;
+    emb_w_ = static_cast<uint32_t*>(dmalloc(ew));
+    emb_s_ = static_cast<uint16_t*>(dmalloc(es));
+    emb_b_ = static_cast<uint16_t*>(dmalloc(es));
+    cuda_check(cudaMemcpy(emb_w_, emb, ew, cudaMemcpyHostToDevice), "upload embed");
+    cuda_check(cudaMemcpy(emb_s_, emb + ew, es, cudaMemcpyHostToDevice), "upload embed");
+    cuda_check(cudaMemcpy(emb_b_, emb + ew + es, es, cudaMemcpyHostToDevice), "upload embed");
+    final_norm_ = upload_u16(reinterpret_cast<const uint16_t*>(emb + ew + 2 * es), d);
+
+    layers_.resize(h_.num_layers);
+    for (uint32_t l = 0; l < h_.num_layers; ++l) build_layer_from_host(l, base + h_.layer_offsets[l]);
+    finalize_load();
+}
+
+void DeviceModel::build_layer_from_host(uint32_t l, const uint8_t* lp) {
+    const int d = h_.d_model;
+    DevLayer& L = layers_[l];
+    L.geo = resolve_layer_geometry(h_, l);
+    const int hd = L.geo.head_dim, F = layer_ffn_width(h_, l);
+    const Shard sh = make_shard(L.geo, F, opt_.rank, opt_.tp);
+    L.hd = hd;
+    L.qh = sh.qh_l;
+    L.kvh = sh.kvh_l;
+    L.F = sh.F_l;
+    L.has_v = L.geo.is_global ? 0 : 1;
+    L.rotated = L.geo.is_global ? 64 : hd / 2;
+    L.theta = L.geo.is_global ? h_.rope_theta_global : h_.rope_theta_local;
+    if (L.rotated > hd / 2) throw G4DenseFormatError("global layer head_dim too small for 64 rotary pairs");
+
+    // Norms + layer scalar (src/cpu_reference.cpp:324-356).
+    const uint16_t* n = reinterpret_cast<const uint16_t*>(lp);
+    L.in_norm = upload_u16(n, d);
+    L.pa_norm = upload_u16(n + d, d);
+    L.pf_norm = upload_u16(n + 2 * d, d);
+    L.pffn_norm = upload_u16(n + 3 * d, d);
+    L.q_norm = upload_u16(n + 4 * d, hd);
+    L.k_norm = upload_u16(n + 4 * d + hd, hd);
+    uint16_t scal;
+    std::memcpy(&scal, n + 4 * d + 2 * hd, 2);
+    const uint32_t sb = (uint32_t)scal << 16;
+    std::memcpy(&L.scalar, &sb, 4);
+
+    // Quant blocks (parse_quant_block, src/cpu_reference.cpp:367-381).
+    const uint8_t* p = reinterpret_cast<const uint8_t*>(n + 4 * d + 2 * hd + 1);
+    auto parse = [&](int rows, int cols) {
+        p += (16u - ((size_t)(p - lp) & 15u)) & 15u;
+        QPtr q{reinterpret_cast<const uint32_t*>(p), nullptr, nullptr, rows, cols};
+        const size_t wb = (size_t)rows * (cols / 8) * 4, sbytes = (size_t)rows * (cols / 64) * 2;
+        q.s = reinterpret_cast<const uint16_t*>(p + wb);
+        q.b = reinterpret_cast<const uint16_t*>(p + wb + sbytes);
+        p += wb + 2 * sbytes;
+        return q;
+    };
+    const int qrows = L.geo.q_heads * hd, kvrows = L.geo.kv_heads * hd;
+    const QPtr Wq = parse(qrows, d), Wk = parse(kvrows, d);
+    QPtr Wv{};
+    if (L.has_v) Wv = parse(kvrows, d);
+    const QPtr Wo = parse(d, qrows), Wg = parse(F, d), Wu = parse(F, d), Wd = parse(d, F);
+
+    std::vector<uint32_t> W;
+    std::vector<uint16_t> S, B;
+    auto up = [&](QW& q, const std::vector<RowRange>& rr, int col0, int Kl) {
+        gather_host(rr, col0, Kl, W, S, B);
+        const int N = (int)(S.size() / (Kl / 64));
+        uint32_t* dw = static_cast<uint32_t*>(dmalloc(W.size() * 4));
+        uint16_t* ds = static_cast<uint16_t*>(dmalloc(S.size() * 2));
+        uint16_t* db = static_cast<uint16_t*>(dmalloc(B.size() * 2));
+        cuda_check(cudaMemcpy(dw, W.data(), W.size() * 4, cudaMemcpyHostToDevice), "upload");
+        cuda_check(cudaMemcpy(ds, S.data(), S.size() * 2, cudaMemcpyHostToDevice), "upload");
+        cuda_check(cudaMemcpy(db, B.data(), B.size() * 2, cudaMemcpyHostToDevice), "upload");
+        upload_qw(q, dw, ds, db, N, Kl);
+        cuda_check(cudaStreamSynchronize(stream_), "repack");
+        // the raw staging copies are released right away
+        for (void* x : {(void*)dw, (void*)ds, (void*)db}) {
+            cudaFree(x);
+            allocs_.erase(std::find(allocs_.begin(), allocs_.end(), x));
+        }
+    };
+    std::vector<RowRange> qkv = {{&Wq, sh.q0 * hd, sh.qh_l * hd}, {&Wk, sh.kv0 * hd, sh.kvh_l * hd}};
+    if (L.has_v) qkv.push_back({&Wv, sh.kv0 * hd, sh.kvh_l * hd});
+    up(L.qkv, qkv, 0, d);
+    up(L.o, {{&Wo, 0, d}}, sh.q0 * hd, sh.qh_l * hd);
+    up(L.gateup, {{&Wg, sh.f0, sh.F_l}, {&Wu, sh.f0, sh.F_l}}, 0, d);
+    up(L.down, {{&Wd, 0, d}}, sh.f0, sh.F_l);
+}
+
+void DeviceModel::load_synthetic(const G4DenseHeader& geom, uint64_t seed, bool centered) {
+    if (loaded_) throw std::runtime_error("model already loaded");
+    h_ = geom;
+    h_.magic = G4DenseHeader::kMagic;
+    h_.version = G4DenseHeader::kVersion;
+    h_.quant_type = 1;
+    h_.quant_group_size = 64;
+    h_.tied_embeddings = 1;
+    const int d = h_.d_model, V = h_.vocab_size;
+    if (d % 64 || h_.num_layers == 0 || h_.num_layers > 60) throw G4DenseFormatError("invalid synthetic geometry");
+    // Embedding table (replicated) and final norm.
+    emb_w_ = static_cast<uint32_t*>(dmalloc((size_t)V * (d / 8) * 4));
+    emb_s_ = static_cast<uint16_t*>(dmalloc((size_t)V * (d / 64) * 2));
+    emb_b_ = static_cast<uint16_t*>(dmalloc((size_t)V * (d / 64) * 2));
+    cuda_check(g4b_synth_qblock(emb_w_, emb_s_, emb_b_, V, d, 0, 0, d, seed, 100000, centered, stream_), "synth");
+    final_norm_ = static_cast<uint16_t*>(dmalloc(d * 2));
+    cuda_check(g4b_synth_norm(final_norm_, d, seed, 200000, stream_), "synth");
+
+    // Staging for one fused raw matrix at a time.
+    size_t max_words = 0;
+    layers_.resize(h_.num_layers);
+    for (uint32_t l = 0; l < h_.num_layers; ++l) {
+        const LayerGeometry g = resolve_layer_geometry(h_, l);
+        const Shard sh = make_shard(g, layer_ffn_width(h_, l), opt_.rank, opt_.tp);
+        const size_t qkv_rows = (size_t)(sh.qh_l + (g.is_global ? 1 : 2) * sh.kvh_l) * g.head_dim;
+        max_words = std::max({max_words, qkv_rows * d / 8, (size_t)d * sh.qh_l * g.head_dim / 8,
+                              (size_t)2 * sh.F_l * d / 8, (size_t)d * sh.F_l / 8});
+    }
+    uint32_t* sw = static_cast<uint32_t*>(dmalloc(max_words * 4));
+    uint16_t* ss = static_cast<uint16_t*>(dmalloc(max_words / 8 * 2));
+    uint16_t* sbb = static_cast<uint16_t*>(dmalloc(max_words / 8 * 2));
+
+    for (uint32_t l = 0; l < h_.num_layers; ++l) {
+        DevLayer& L = layers_[l];
+        L.geo = resolve_layer_geometry(h_, l);
+        const int hd = L.geo.head_dim, F = layer_ffn_width(h_, l);
+        const Shard sh = make_shard(L.geo, F, opt_.rank, opt_.tp);
+        L.hd = hd;
+        L.qh = sh.qh_l;
+        L.kvh = sh.kvh_l;
+        L.F = sh.F_l;
+        L.has_v = L.geo.is_global ? 0 : 1;
+        L.rotated = L.geo.is_global ? 64 : hd / 2;
+        L.theta = L.geo.is_global ? h_.rope_theta_global : h_.rope_theta_local;
+        // layer_scalar = 1/sqrt(2L) rounded to bf16 (tools/make_synthetic_model.py:143)
+        const float sc = 1.0f / std::sqrt(2.0f * (float)h_.num_layers);
+        uint32_t u;
+        std::memcpy(&u, &sc, 4);
+        u = (u + 0x7FFFu + ((u >> 16) & 1u)) & 0xFFFF0000u;
+        std::memcpy(&L.scalar, &u, 4);
+        const uint64_t t = (uint64_t)l * 16;
+        auto norm = [&](int n, uint64_t id) {
+            auto* p = static_cast<uint16_t*>(dmalloc(n * 2));
+            cuda_check(g4b_synth_norm(p, n, seed, t + id, stream_), "synth");
+            return p;
+        };
+        L.in_norm = norm(d, 8);
+        L.pa_norm = norm(d, 9);
+        L.pf_norm = norm(d, 10);
+        L.pffn_norm = norm(d, 11);
+        L.q_norm = norm(hd, 12);
+        L.k_norm = norm(hd, 13);
+        // Fused matrices: rows of each sub-matrix are generated from their global indices.
+        struct Part {
+            uint64_t id;
+            int row0_global, rows, Kg;
+        };
+        auto build = [&](QW& q, const std::vector<Part>& parts, int col0, int Kl) {
+            int r = 0;
+            for (const Part& pt : parts) {
+                cuda_check(g4b_synth_qblock(sw + (size_t)r * (Kl / 8), ss + (size_t)r * (Kl / 64),
+                                            sbb + (size_t)r * (Kl / 64), pt.rows, Kl, pt.row0_global, col0, pt.Kg, seed,
+                                            t + pt.id, centered, stream_),
+                           "synth");
+                r += pt.rows;
+            }
+            upload_qw(q, sw, ss, sbb, r, Kl);
+        };
+        std::vector<Part> qkv = {{0, sh.q0 * hd, sh.qh_l * hd, d}, {1, sh.kv0 * hd, sh.kvh_l * hd, d}};
+        if (L.has_v) qkv.push_back({2, sh.kv0 * hd, sh.kvh_l * hd, d});
+        build(L.qkv, qkv, 0, d);
+        build(L.o, {{3, 0, d, (int)L.geo.q_heads * hd}}, sh.q0 * hd, sh.qh_l * hd);
+        build(L.gateup, {{4, sh.f0, sh.F_l, d}, {5, sh.f0, sh.F_l, d}}, 0, d);
+        build(L.down, {{6, 0, d, F}}, sh.f0, sh.F_l);
+    }
+    cuda_check(cudaStreamSynchronize(stream_), "synthesize");
+    for (void* x : {(void*)sw, (void*)ss, (void*)sbb}) {
+        cudaFree(x);
+        allocs_.erase(std::find(allocs_.begin(), allocs_.end(), x));
+    }
+    finalize_load();
+}
+
+void DeviceModel::finalize_load() {
+    const int d = h_.d_model, V = h_.vocab_size;
+    if (V % opt_.tp) throw std::runtime_error("vocab must divide by the tensor-parallel size");
+    v_local_ = V / opt_.tp;
+    v_off_ = opt_.rank * v_local_;
+    upload_qw(lm_, emb_w_ + (size_t)v_off_ * (d / 8), emb_s_ + (size_t)v_off_ * (d / 64),
+              emb_b_ + (size_t)v_off_ * (d / 64), v_local_, d);
+    // KV rings: sliding layers keep window + 16 slots (a verify batch of up to 16 rows never
+    // overwrites a key an earlier row of the same batch still needs); full-attention layers
+    // keep max_context.
+    for (auto& L : layers_) {
+        L.cap = L.geo.is_global ? opt_.max_context
+                                : std::min<int>(opt_.max_context, (int)h_.sliding_window) + 16;
+        const size_t n = (size_t)L.cap * L.kvh * L.hd;
+        L.k_ring = static_cast<uint16_t*>(dmalloc(n * 2));
+        L.v_ring = static_cast<uint16_t*>(dmalloc(n * 2));
+        kv_bytes_ += n * 4;
+    }
+    init_buffers();
+    clear_kv();
+    cuda_check(cudaStreamSynchronize(stream_), "load");
+    loaded_ = true;
+}
+
+void DeviceModel::init_buffers() {
+    const int d = h_.d_model;
+    int max_attn_k = 0, max_F = 0, max_q = 0, max_hd = 0, max_qh = 0;
+    size_t part = 0;
+    auto consider = [&](const QW& q) { part = std::max(part, (size_t)q.n_crg * q.max_slots * kMaxM * 256); };
+    for (auto& L : layers_) {
+        max_attn_k = std::max(max_attn_k, L.qh * L.hd);
+        max_F = std::max(max_F, L.F);
+        max_q = std::max(max_q, L.qh * L.hd);
+        max_hd = std::max(max_hd, L.hd);
+        max_qh = std::max(max_qh, L.qh);
+        consider(L.qkv);
+        consider(L.o);
+        consider(L.gateup);
+        consider(L.down);
+    }
+    consider(lm_);
+    part_floats_ = part;
+    for (int i = 0; i < 2; ++i) hres_[i] = static_cast<float*>(dmalloc((size_t)kMaxM * d * 4));
+    bf_d_ = dmalloc(bfrag_capacity(round_up(d, 128)));
+    bf_attn_ = dmalloc(bfrag_capacity(round_up(max_attn_k, 128)));
+    bf_ff_ = dmalloc(bfrag_capacity(round_up(max_F, 128)));
+    part_ = static_cast<float*>(dmalloc(part * 4));
+    q_buf_ = static_cast<float*>(dmalloc((size_t)kMaxM * max_q * 4));
+    attn_part_floats_ = (size_t)64 * kMaxM * max_qh * max_hd;
+    o_part_ = static_cast<float*>(dmalloc(attn_part_floats_ * 4));
+    ml_part_ = static_cast<float2*>(dmalloc((size_t)64 * kMaxM * max_qh * sizeof(float2)));
+    y_ = static_cast<float*>(dmalloc((size_t)kMaxM * std::max(d, 2 * max_F) * 4));
+    chunk_best_ = static_cast<float2*>(dmalloc((size_t)opt_.tp * kMaxM * g4b_head_chunks(v_local_) * sizeof(float2)));
+    logits_ = static_cast<float*>(dmalloc((size_t)kMaxM * v_local_ * 4));
+    res_dev_ = static_cast<HeadResult*>(dmalloc(sizeof(HeadResult)));
+    sp_dev_ = static_cast<StepParams*>(dmalloc(4 * sizeof(StepParams)));
+    chain_dev_ = static_cast<uint32_t*>(dmalloc(64 * 4));
+    err_dev_ = static_cast<int*>(dmalloc(sizeof(int)));
+    cuda_check(cudaMemsetAsync(err_dev_, 0, sizeof(int), stream_), "memset");
+    cuda_check(cudaMemsetAsync(sp_dev_, 0, 4 * sizeof(StepParams), stream_), "memset");
+}
+
+void DeviceModel::clear_kv() {
+    for (auto& L : layers_) {
+        const size_t n = (size_t)L.cap * L.kvh * L.hd * 2;
+        cuda_check(cudaMemsetAsync(L.k_ring, 0, n, stream_), "memset kv");
+        cuda_check(cudaMemsetAsync(L.v_ring, 0, n, stream_), "memset kv");
+    }
+}
+
+uint64_t DeviceModel::pass_weight_bytes() const { return weight_bytes_; }
+
+// ----------------------------------------------------------------------------- forward
+
+PartView DeviceModel::part_view(const QW& q, int M) const {
+    PartView v;
+    v.part = part_;
+    v.max_slots = q.max_slots;
+    v.n_crg = q.n_crg;
+    v.ktiles = q.ktiles;
+    v.grid = vgemm_grid(M, q.n_crg, q.ktiles);
+    return v;
+}
+
+void DeviceModel::gemm(const QW& q, const void* bfrag, int M) {
+    const BFragView v = bfrag_view(const_cast<void*>(bfrag), q.ktiles * 128, M);
+    VgemmParams p{};
+    p.w = q.w;
+    p.bfrag = v.frag;
+    p.gsum = v.gsum;
+    p.out = part_view(q, M);
+    p.N = q.N;
+    p.M = M;
+    p.n_wrg = q.n_wrg;
+    p.err = err_dev_;
+    cuda_check(vgemm_launch(p, stream_, opt_.use_pdl), "vgemm");
+}
+
+void DeviceModel::enqueue_raw(int M, PassKind kind, bool want_logits, uint32_t* chain_out) {
+    const int d = h_.d_model;
+    const bool pdl = opt_.use_pdl;
+    StepParams* sp = sp_dev_ + (kind == PassKind::DraftStep ? 1 : 0);
+    int cur = 0;
+    cuda_check(g4b_embed_norm(sp, emb_w_, emb_s_, emb_b_, h_.vocab_size, d, layers_[0].in_norm, hres_[cur], bf_d_, M,
+                              stream_, false),
+               "embed_norm");
+    for (size_t l = 0; l < layers_.size(); ++l) {
+        DevLayer& L = layers_[l];
+        // Q/K/V
+        gemm(L.qkv, bf_d_, M);
+        QkvEpiArgs qa{};
+        qa.qkv.part = part_view(L.qkv, M);
+        qa.sp = sp;
+        qa.M = M;
+        qa.qh = L.qh;
+        qa.kvh = L.kvh;
+        qa.hd = L.hd;
+        qa.has_v = L.has_v;
+        qa.rotated = L.rotated;
+        qa.theta = L.theta;
+        qa.q_norm = L.q_norm;
+        qa.k_norm = L.k_norm;
+        qa.q_out = q_buf_;
+        qa.k_ring = L.k_ring;
+        qa.v_ring = L.v_ring;
+        qa.cap = L.cap;
+        qa.kv_bf16 = opt_.kv_bf16;
+        cuda_check(g4b_qkv_epi(qa, stream_, pdl), "qkv_epi");
+        // attention
+        AttnArgs aa{};
+        aa.q = q_buf_;
+        aa.k_ring = L.k_ring;
+        aa.v_ring = L.v_ring;
+        aa.sp = sp;
+        aa.M = M;
+        aa.qh = L.qh;
+        aa.kvh = L.kvh;
+        aa.hd = L.hd;
+        aa.cap = L.cap;
+        aa.window = L.geo.is_global ? 0 : (int)h_.sliding_window;
+        aa.kv_bf16 = opt_.kv_bf16;
+        aa.scale = 1.0f;
+        aa.nsplit = g4b_attn_nsplit(L.kvh, M, L.qh, L.hd);
+        aa.o_part = o_part_;
+        aa.ml_part = ml_part_;
+        cuda_check(g4b_attention(aa, stream_, pdl), "attention");
+        cuda_check(g4b_attn_combine(aa, bf_attn_, stream_, pdl), "attn_combine");
+        // o projection + post-attention norm / residual + pre-FFN norm
+        gemm(L.o, bf_attn_, M);
+        GemmOut oo{};
+        oo.part = part_view(L.o, M);
+#ifdef G4B_HAVE_NCCL
+        if (opt_.tp > 1) {
+            cuda_check(vgemm_reduce(oo.part, M, d, y_, d, stream_, pdl), "reduce");
+            if (ncclAllReduce(y_, y_, (size_t)M * d, ncclFloat, ncclSum, (ncclComm_t)opt_.nccl_comm, stream_) !=
+                ncclSuccess)
+                throw std::runtime_error("ncclAllReduce (attention) failed");
+            oo.part.part = nullptr;
+            oo.y = y_;
+            oo.ld = d;
+        }
+#endif
+        cuda_check(g4b_post_attn(oo, hres_[cur], hres_[1 - cur], L.pa_norm, L.pf_norm, d, bf_d_, M, stream_, pdl),
+                   "post_attn");
+        cur = 1 - cur;
+        // FFN
+        gemm(L.gateup, bf_d_, M);
+        GemmOut gu{};
+        gu.part = part_view(L.gateup, M);
+        cuda_check(g4b_geglu(gu, L.F, bf_ff_, M, stream_, pdl), "geglu");
+        gemm(L.down, bf_ff_, M);
+        GemmOut dn{};
+        dn.part = part_view(L.down, M);
+#ifdef G4B_HAVE_NCCL
+        if (opt_.tp > 1) {
+            cuda_check(vgemm_reduce(dn.part, M, d, y_, d, stream_, pdl), "reduce");
+            if (ncclAllReduce(y_, y_, (size_t)M * d, ncclFloat, ncclSum, (ncclComm_t)opt_.nccl_comm, stream_) !=
+                ncclSuccess)
+                throw std::runtime_error("ncclAllReduce (FFN) failed");
+            dn.part.part = nullptr;
+            dn.y = y_;
+            dn.ld = d;
+        }
+#endif
+        const uint16_t* w_next = (l + 1 < layers_.size()) ? layers_[l + 1].in_norm : final_norm_;
+        cuda_check(g4b_post_ffn(dn, hres_[cur], hres_[1 - cur], L.pffn_norm, L.scalar, w_next, d, bf_d_, M, stream_, pdl),
+                   "post_ffn");
+        cur = 1 - cur;
+    }
+    // LM head
+    gemm(lm_, bf_d_, M);
+    GemmOut lo{};
+    lo.part = part_view(lm_, M);
+    const int nch = g4b_head_chunks(v_local_);
+    cuda_check(g4b_head_chunks_launch(lo, v_local_, M, h_.final_logit_softcapping, want_logits ? logits_ : nullptr,
+                                      v_local_, chunk_best_, stream_, pdl),
+               "head_chunks");
+    cuda_check(g4b_head_finalize(chunk_best_, nch, M, sp, res_dev_, chain_out, stream_, pdl), "head_finalize");
+}
+
+void DeviceModel::enqueue(int M, PassKind kind, bool want_logits, uint32_t* chain_out) {
+    if (!loaded_) throw std::runtime_error("model not loaded");
+    if (M < 1 || M > kMaxM) throw std::runtime_error("batch width must be 1..16");
+    if (opt_.tp > 1 && h_.vocab_size % opt_.tp) throw std::runtime_error("vocab split");
+    if (!opt_.use_graphs) {
+        enqueue_raw(M, kind, want_logits, chain_out);
+        return;
+    }
+    const auto key = std::make_tuple(M, (int)kind, want_logits, (uintptr_t)chain_out);
+    auto it = graphs_.find(key);
+    if (it == graphs_.end()) {
+        cudaGraph_t g = nullptr;
+        cuda_check(cudaStreamBeginCapture(stream_, cudaStreamCaptureModeThreadLocal), "capture begin");
+        try {
+            enqueue_raw(M, kind, want_logits, chain_out);
+        } catch (...) {
+            cudaStreamEndCapture(stream_, &g);
+            if (g) cudaGraphDestroy(g);
+            throw;
+        }
+        cuda_check(cudaStreamEndCapture(stream_, &g), "capture end");
+        cudaGraphExec_t ge = nullptr;
+        const cudaError_t e = cudaGraphInstantiate(&ge, g, 0);
+        cudaGraphDestroy(g);
+        cuda_check(e, "graph instantiate");
+        it = graphs_.emplace(key, ge).first;
+    }
+    cuda_check(cudaGraphLaunch(it->second, stream_), "graph launch");
+}
+
+void DeviceModel::push_params(int slot, const StepParams& p) {
+    // A ring entry is reused only after the stream has drained every earlier copy.
+    if (sp_ring_ == kParamRing) {
+        cuda_check(cudaStreamSynchronize(stream_), "sync");
+        sp_ring_ = 0;
+    }
+    StepParams& s = sp_host_[sp_ring_++];
+    s = p;
+    cuda_check(cudaMemcpyAsync(sp_dev_ + slot, &s, sizeof(StepParams), cudaMemcpyHostToDevice, stream_), "params");
+}
+
+void DeviceModel::run_plain(int M, int base_pos, const uint32_t* tokens, bool want_logits) {
+    StepParams s;
+    std::memset(&s, 0, sizeof(s));
+    s.base_pos = base_pos;
+    for (int i = 0; i < M; ++i) {
+        uint32_t t = tokens[i];
+        if (t >= h_.vocab_size) t %= h_.vocab_size;
+        s.tokens[i] = t;
+    }
+    push_params(0, s);
+    enqueue(M, PassKind::Plain, want_logits, nullptr);
+}
+
+HeadResult DeviceModel::fetch_result() {
+    cuda_check(cudaMemcpyAsync(res_host_, res_dev_, sizeof(HeadResult), cudaMemcpyDeviceToHost, stream_), "result");
+    cuda_check(cudaStreamSynchronize(stream_), "sync");
+    sp_ring_ = 0;  // the stream is drained: the whole parameter ring is free again
+    return *res_host_;
+}
+
+void DeviceModel::check_device_error() {
+    int h = 0;
+    cuda_check(cudaMemcpyAsync(&h, err_dev_, sizeof(int), cudaMemcpyDeviceToHost, stream_), "err");
+    cuda_check(cudaStreamSynchronize(stream_), "sync");
+    if (h) throw std::runtime_error("a kernel's bounded wait gave up (weights or fragments never arrived)");
+}
+
+}  // namespace g4b

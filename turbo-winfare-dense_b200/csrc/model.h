@@ -1,0 +1,154 @@
+// A fully resident Gemma-4-shaped INT4 G64 model on one GPU (one tensor-parallel shard) and
+// its forward pass: ForwardRunner::forward_batch (src/runner.cpp:906-2059) rebuilt as a
+// captured CUDA graph of sm_100a kernels per batch width M.
+#pragma once
+#include <cuda_runtime.h>
+
+#include <cstdint>
+#include <map>
+#include <memory>
+#include <string>
+#include <tuple>
+#include <vector>
+
+#include "format.h"
+#include "kernels.h"
+#include "model_dev.h"
+
+namespace g4b {
+
+struct ModelOptions {
+    int max_context = 4096;  // KV capacity of full-attention layers
+    int kv_bf16 = 0;         // round K/V through bf16 instead of FP16
+    int rank = 0, tp = 1;    // tensor-parallel shard
+    void* nccl_comm = nullptr;  // ncclComm_t when tp > 1
+    bool use_graphs = true;
+    bool use_pdl = true;
+    cudaStream_t stream = nullptr;  // share a caller's stream (target and drafter do)
+};
+
+// One INT4 matrix in the vgemm streaming layout.
+struct QW {
+    void* w = nullptr;
+    int N = 0, K = 0, ktiles = 0, n_crg = 0, n_wrg = 0, max_slots = 0;
+};
+
+struct DevLayer {
+    LayerGeometry geo{};
+    int qh = 0, kvh = 0, hd = 0;  // local heads
+    int has_v = 0, rotated = 0;
+    float theta = 0.f, scalar = 1.f;
+    int F = 0;                    // local FFN width
+    QW qkv, o, gateup, down;
+    uint16_t *in_norm = nullptr, *pa_norm = nullptr, *pf_norm = nullptr, *pffn_norm = nullptr;
+    uint16_t *q_norm = nullptr, *k_norm = nullptr;
+    uint16_t *k_ring = nullptr, *v_ring = nullptr;
+    int cap = 0;
+};
+
+// Rows one pass processes at most (verify width, prefill chunk).
+constexpr int kBatchRows = 16;
+
+enum class PassKind { Plain = 0, DraftStep = 1 };
+
+class DeviceModel {
+   public:
+    explicit DeviceModel(const ModelOptions& opt);
+    ~DeviceModel();
+    DeviceModel(const DeviceModel&) = delete;
+    DeviceModel& operator=(const DeviceModel&) = delete;
+
+    // Reads a .g4dense v3 container (validated like src/format.cpp) and uploads this rank's
+    // shard.
+    void load_container(const std::string& path);
+    // Generates weights with the container's value distributions directly on the device
+    // for the geometry in `geom` (header fields only; offsets are ignored).
+    void load_synthetic(const G4DenseHeader& geom, uint64_t seed, bool centered);
+
+    const G4DenseHeader& header() const { return h_; }
+    int vocab_local() const { return v_local_; }
+    int max_context() const { return opt_.max_context; }
+    uint64_t weight_bytes() const { return weight_bytes_; }
+    uint64_t kv_bytes() const { return kv_bytes_; }
+    cudaStream_t stream() const { return stream_; }
+    const ModelOptions& options() const { return opt_; }
+
+    // Device step-parameter slots: 0 = plain passes, 1 = drafter chaining.
+    StepParams* step_params(int slot) { return sp_dev_ + slot; }
+    HeadResult* result_dev() { return res_dev_; }
+    float* logits_dev() { return logits_; }  // [16][vocab_local] when a pass asked for them
+    uint32_t* chain_dev() { return chain_dev_; }
+
+    // Enqueues one pass of M rows (1..16) on the model's stream (graph-replayed when enabled).
+    // The caller has already written the StepParams slot used by `kind`.
+    void enqueue(int M, PassKind kind, bool want_logits, uint32_t* chain_out);
+    // Stages `p` in a pinned ring and enqueues its copy into StepParams slot `slot`.
+    void push_params(int slot, const StepParams& p);
+    // Host helper: write StepParams slot 0 (base_pos, tokens) and enqueue a plain pass.
+    void run_plain(int M, int base_pos, const uint32_t* tokens, bool want_logits);
+    // Copies the result struct to host (synchronizes the stream).
+    HeadResult fetch_result();
+    void check_device_error();  // throws if a kernel's bounded wait gave up
+    void clear_kv();
+
+    // Timing hook: total verify-GEMM algorithmic weight bytes of one pass.
+    uint64_t pass_weight_bytes() const;
+
+   private:
+    void init_buffers();
+    void build_layer_from_host(uint32_t l, const uint8_t* layer_ptr);
+    void enqueue_raw(int M, PassKind kind, bool want_logits, uint32_t* chain_out);
+    void gemm(const QW& q, const void* bfrag, int M);
+    PartView part_view(const QW& q, int M) const;
+    void upload_qw(QW& q, const uint32_t* W, const uint16_t* S, const uint16_t* B, int N, int K);
+    void alloc_qw(QW& q, int N, int K);
+    uint16_t* upload_u16(const uint16_t* src, size_t n);
+    void* dmalloc(size_t bytes);
+    void finalize_load();
+
+    ModelOptions opt_;
+    G4DenseHeader h_{};
+    cudaStream_t stream_ = nullptr;
+    std::vector<void*> allocs_;
+    std::vector<DevLayer> layers_;
+    QW lm_;
+    int v_local_ = 0, v_off_ = 0;
+    uint32_t* emb_w_ = nullptr;
+    uint16_t *emb_s_ = nullptr, *emb_b_ = nullptr, *final_norm_ = nullptr;
+    // work buffers
+    float* hres_[2] = {nullptr, nullptr};
+    void* bf_d_ = nullptr;     // B fragments with K = d_model
+    void* bf_attn_ = nullptr;  // K = local q_heads * head_dim (max over layers)
+    void* bf_ff_ = nullptr;    // K = local FFN width
+    float* part_ = nullptr;
+    size_t part_floats_ = 0;
+    float* q_buf_ = nullptr;
+    float* o_part_ = nullptr;
+    float2* ml_part_ = nullptr;
+    size_t attn_part_floats_ = 0;
+    float* y_ = nullptr;  // all-reduce staging [16][max(d, ...)]
+    float2* chunk_best_ = nullptr;
+    float* logits_ = nullptr;
+    HeadResult* res_dev_ = nullptr;
+    StepParams* sp_dev_ = nullptr;
+    uint32_t* chain_dev_ = nullptr;
+    int* err_dev_ = nullptr;
+    uint64_t weight_bytes_ = 0, kv_bytes_ = 0;
+    bool loaded_ = false;
+    // staging for raw (container-layout) matrices before the repack
+    uint32_t* stage_w_ = nullptr;
+    uint16_t *stage_s_ = nullptr, *stage_b_ = nullptr;
+    size_t stage_words_ = 0;
+    std::map<std::tuple<int, int, bool, uintptr_t>, cudaGraphExec_t> graphs_;
+    bool pdl_in_graphs_ = true;
+    StepParams* sp_host_ = nullptr;  // pinned ring of kParamRing entries
+    int sp_ring_ = 0;
+    static constexpr int kParamRing = 256;
+    HeadResult* res_host_ = nullptr; // pinned
+    bool own_stream_ = true;
+};
+
+// cudaError_t -> exception with context.
+void cuda_check(cudaError_t e, const char* what);
+
+}  // namespace g4b

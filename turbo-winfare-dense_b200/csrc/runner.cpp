@@ -1,0 +1,325 @@
+#include "runner.h"
+
+#include <algorithm>
+#include <chrono>
+#include <cmath>
+#include <cstring>
+#include <sstream>
+#include <stdexcept>
+
+namespace g4b {
+
+namespace {
+double now_ms() {
+    return std::chrono::duration<double, std::milli>(std::chrono::steady_clock::now().time_since_epoch()).count();
+}
+
+// Config-3 oracle drafter: the proposal for history index n replays the target's stream, or,
+// with probability `rate` (a seeded coin per index), a different id.
+uint32_t replay_propose(const std::vector<uint32_t>& stream, size_t n_prompt, size_t hist_index, double rate,
+                        uint64_t seed, uint32_t vocab) {
+    const long long i = (long long)hist_index - (long long)n_prompt;
+    const uint32_t truth = (i >= 0 && i < (long long)stream.size()) ? stream[(size_t)i] : 0u;
+    const uint64_t h = splitmix64(seed + (uint64_t)hist_index);
+    const double u = (double)(h >> 11) * (1.0 / 9007199254740992.0);
+    if (u < rate) return (uint32_t)((truth + 1u + (uint32_t)(splitmix64(h) % (vocab - 1))) % vocab);
+    return truth;
+}
+}  // namespace
+
+void DraftRuntime::catch_up(const std::vector<uint32_t>& ctx) {
+    if (consumed_ > ctx.size()) consumed_ = 0;
+    while (consumed_ + 1 < ctx.size()) {
+        const int m = (int)std::min<size_t>(kBatchRows, ctx.size() - 1 - consumed_);
+        model_->run_plain(m, (int)consumed_, ctx.data() + consumed_, false);
+        consumed_ += m;
+    }
+}
+
+void Engine::forward_batch(const uint32_t* ids, uint32_t batch, uint32_t base, float* out_logits, bool all_positions) {
+    if (batch < 1 || batch > (uint32_t)kBatchRows) throw std::invalid_argument("forward_batch: batch must be 1..16");
+    if (out_logits && target_->options().tp > 1)
+        throw std::invalid_argument("forward_batch: host logits are not gathered across tensor-parallel ranks");
+    if (base + batch > (uint32_t)target_->max_context()) throw std::invalid_argument("forward_batch: context exceeds max_context");
+    target_->run_plain((int)batch, (int)base, ids, out_logits != nullptr);
+    if (out_logits) {
+        const size_t V = target_->vocab_local();
+        const size_t row0 = all_positions ? 0 : batch - 1;
+        const size_t rows = all_positions ? batch : 1;
+        cuda_check(cudaMemcpyAsync(out_logits, target_->logits_dev() + row0 * V, rows * V * sizeof(float),
+                                   cudaMemcpyDeviceToHost, target_->stream()),
+                   "logits");
+    }
+    cuda_check(cudaStreamSynchronize(target_->stream()), "forward_batch");
+}
+
+// Prefill in chunks of up to 16 positions (the reference chunks by 8, src/runner.cpp:2129-2133;
+// batched rows equal sequential positions, so the chunk width does not change results).
+// Returns the greedy next token; for sampled decoding fills *last_logits instead.
+uint32_t Engine::prefill(const std::vector<uint32_t>& toks, const GenerationOptions& opt, std::vector<float>* last) {
+    const bool greedy = opt.sampling.is_greedy();
+    const size_t n = toks.size();
+    int m_last = 1;
+    for (size_t i = 0; i < n; i += kBatchRows) {
+        const int m = (int)std::min<size_t>(kBatchRows, n - i);
+        const bool is_last = i + m == n;
+        target_->run_plain(m, (int)i, toks.data() + i, is_last && !greedy);
+        m_last = m;
+    }
+    const HeadResult r = target_->fetch_result();
+    if (!greedy) {
+        const size_t V = target_->vocab_local();
+        last->resize(V);
+        cuda_check(cudaMemcpy(last->data(), target_->logits_dev() + (size_t)(m_last - 1) * V, V * sizeof(float),
+                              cudaMemcpyDeviceToHost),
+                   "logits");
+    }
+    return r.argmax[m_last - 1];
+}
+
+std::vector<uint32_t> Engine::generate(const std::vector<uint32_t>& prompt, const GenerationOptions& opt,
+                                       const TokenCallback& on_token, const std::atomic<bool>* cancel) {
+    stats_ = GenStats{};
+    const double t0 = now_ms();
+    validate_sampling(opt.sampling);
+    const SamplingParams& sp = opt.sampling;
+    const bool greedy = sp.is_greedy();
+    DeviceModel& T = *target_;
+    const uint32_t V = T.header().vocab_size;
+    if (!greedy && T.options().tp > 1)
+        throw std::invalid_argument("sampled decoding needs full logits; tensor-parallel runs decode greedily");
+    std::vector<uint32_t> history;
+    for (uint32_t t : prompt) {
+        if (t >= V) {
+            // src/runner.cpp:2099-2109: small vocabularies wrap, large ones reject.
+            if (V <= 4096) t %= V;
+            else throw std::invalid_argument("token id " + std::to_string(t) + " exceeds model vocab size " + std::to_string(V));
+        }
+        history.push_back(t);
+    }
+    if (history.empty()) throw std::invalid_argument("generate: prompt is empty");
+    if (history.size() + (size_t)opt.max_tokens + 16 > (size_t)T.max_context())
+        throw std::invalid_argument("generate: prompt + max_tokens exceeds the KV capacity (max_context)");
+    if (opt.max_tokens <= 0) return {};
+
+    std::vector<uint32_t> out;
+    std::vector<float> logits;
+    const uint32_t first = prefill(history, opt, &logits);
+    stats_.ttft_ms = now_ms() - t0;
+    const double t_decode = now_ms();
+
+    int emitted = 0;
+    auto emit = [&](uint32_t t) -> bool {
+        out.push_back(t);
+        ++stats_.emitted;
+        if (on_token && !on_token(t)) {
+            stats_.stop_reason = 2;
+            return false;
+        }
+        if (opt.stop_token >= 0 && (int64_t)t == opt.stop_token) {
+            stats_.stop_reason = 1;
+            return false;
+        }
+        return true;
+    };
+    const bool spec = opt.speculative_enabled && draft_ && opt.draft_k > 0;
+
+    if (spec) {
+        DraftRuntime& D = *draft_;
+        DeviceModel& Dm = D.model();
+        if (Dm.header().vocab_size != V) throw std::invalid_argument("drafter vocabulary differs from the target's");
+        D.reset();
+        const uint32_t K = std::min<uint32_t>(opt.draft_k, kMaxDraftWidth);
+        uint32_t drafted_total = 0, accepted_total = 0;
+        bool drafting = true;
+        uint32_t pending = greedy ? first : sample_token(logits.data(), V, sp, seed_for(sp, (int)history.size() - 1));
+        history.push_back(pending);
+        ++emitted;
+        bool stop = !emit(pending);
+        std::vector<float> verify, dl;
+        while (!stop && emitted < opt.max_tokens) {
+            if (cancel && cancel->load()) {
+                stats_.stop_reason = 3;
+                break;
+            }
+            if (!drafting) {
+                // Gated: one target pass per token (src/runner.cpp:2219-2237).
+                T.run_plain(1, (int)history.size() - 1, &pending, !greedy);
+                const HeadResult r = T.fetch_result();
+                uint32_t nx = r.argmax[0];
+                if (!greedy) {
+                    verify.resize(V);
+                    cuda_check(cudaMemcpy(verify.data(), T.logits_dev(), V * 4, cudaMemcpyDeviceToHost), "logits");
+                    nx = sample_token(verify.data(), V, sp, seed_for(sp, (int)history.size()));
+                }
+                history.push_back(nx);
+                ++emitted;
+                ++stats_.gated_steps;
+                pending = nx;
+                if (!emit(nx)) break;
+                continue;
+            }
+            if (K < 2) break;  // K-1 = 0 drafts: the reference's round loop ends here
+            const double tr0 = now_ms();
+            D.catch_up(history);
+            const size_t len = history.size();
+            std::vector<uint32_t> emitted_now;
+            uint32_t n_acc = 0;
+            if (greedy) {
+                StepParams tp{}, dp{};
+                tp.base_pos = dp.base_pos = (int)len - 1;
+                tp.tokens[0] = dp.tokens[0] = pending;
+                const bool replay = !opt.replay.empty();
+                T.push_params(0, tp);
+                Dm.push_params(1, dp);
+                uint32_t* chain = replay ? Dm.chain_dev() : T.step_params(0)->tokens + 1;
+                for (uint32_t s = 0; s + 1 < K; ++s) Dm.enqueue(1, PassKind::DraftStep, false, chain);
+                if (replay) {
+                    for (uint32_t s = 0; s + 1 < K; ++s)
+                        tp.tokens[s + 1] = replay_propose(opt.replay, prompt.size(), len + s, opt.mismatch_rate,
+                                                          opt.mismatch_seed, V);
+                    T.push_params(0, tp);
+                }
+                T.enqueue((int)K, PassKind::Plain, false, nullptr);
+                const HeadResult r = T.fetch_result();
+                n_acc = (uint32_t)r.n_accepted;
+                emitted_now.assign(r.tokens, r.tokens + r.n_emit);
+            } else {
+                // Sampled: the reference's host RNG streams decide drafts and acceptance.
+                std::vector<uint32_t> drafts;
+                std::vector<std::vector<float>> draft_logits;
+                uint32_t cur = pending;
+                int pos = (int)len - 1;
+                for (uint32_t s = 0; s + 1 < K; ++s) {
+                    Dm.run_plain(1, pos++, &cur, true);
+                    dl.resize(V);
+                    cuda_check(cudaMemcpyAsync(dl.data(), Dm.logits_dev(), V * 4, cudaMemcpyDeviceToHost, Dm.stream()),
+                               "logits");
+                    cuda_check(cudaStreamSynchronize(Dm.stream()), "sync");
+                    const uint64_t ss = splitmix64(sp.has_seed ? (sp.seed + s) : (1337 + s));
+                    const uint32_t cand = sample_token(dl.data(), V, sp, ss);
+                    drafts.push_back(cand);
+                    draft_logits.push_back(dl);
+                    cur = cand;
+                }
+                std::vector<uint32_t> batch = {pending};
+                batch.insert(batch.end(), drafts.begin(), drafts.end());
+                T.run_plain((int)K, (int)len - 1, batch.data(), true);
+                verify.resize((size_t)K * V);
+                cuda_check(cudaMemcpyAsync(verify.data(), T.logits_dev(), (size_t)K * V * 4, cudaMemcpyDeviceToHost,
+                                           T.stream()),
+                           "logits");
+                cuda_check(cudaStreamSynchronize(T.stream()), "sync");
+                std::vector<const float*> per_pos;
+                for (uint32_t i = 0; i < K; ++i) per_pos.push_back(verify.data() + (size_t)i * V);
+                const SpeculativeEvaluation ev =
+                    speculator_.evaluate_verification(drafts, per_pos, V, sp, seed_for(sp, (int)len), draft_logits);
+                n_acc = ev.num_accepted;
+                emitted_now = ev.accepted_tokens;
+            }
+            const size_t forwarded = (len - 1) + (K - 1);
+            int this_emit = 0;
+            for (uint32_t t : emitted_now) {
+                if (emitted >= opt.max_tokens) {
+                    stop = true;
+                    break;
+                }
+                history.push_back(t);
+                ++emitted;
+                ++this_emit;
+                pending = t;
+                if (!emit(t)) {
+                    stop = true;
+                    break;
+                }
+            }
+            D.accept(history.size() - 1, forwarded);
+            ++stats_.rounds;
+            stats_.drafted += K - 1;
+            stats_.accepted += n_acc;
+            stats_.round_info.push_back((int)(K - 1));
+            stats_.round_info.push_back((int)n_acc);
+            stats_.round_info.push_back(this_emit);
+            stats_.verify_ms += now_ms() - tr0;
+            drafted_total += K - 1;
+            accepted_total += n_acc;
+            if (drafting && opt.gate_window >= 0 && drafted_total >= (uint32_t)opt.gate_window &&
+                (double)accepted_total / drafted_total < opt.gate_min_accept) {
+                drafting = false;
+                stats_.gated = true;
+            }
+        }
+    } else {
+        // Non-speculative loop (src/runner.cpp:2314-2344).
+        uint32_t next_greedy = first;
+        for (int step = 0; step < opt.max_tokens; ++step) {
+            if (cancel && cancel->load()) {
+                stats_.stop_reason = 3;
+                break;
+            }
+            const int pos = (int)history.size() - 1;
+            uint32_t nx = next_greedy;
+            if (!greedy) {
+                if (sp.repetition_penalty != 1.0f)
+                    apply_repetition_penalty(logits.data(), V, history, sp.repetition_penalty,
+                                             T.header().final_logit_softcapping);
+                nx = sample_token(logits.data(), V, sp, seed_for(sp, pos));
+            }
+            history.push_back(nx);
+            ++emitted;
+            if (!emit(nx)) break;
+            if (emitted >= opt.max_tokens) break;
+            T.run_plain(1, (int)history.size() - 1, &nx, !greedy);
+            const HeadResult r = T.fetch_result();
+            next_greedy = r.argmax[0];
+            if (!greedy) {
+                logits.resize(V);
+                cuda_check(cudaMemcpy(logits.data(), T.logits_dev(), V * 4, cudaMemcpyDeviceToHost), "logits");
+            }
+        }
+    }
+    T.check_device_error();
+    stats_.total_ms = now_ms() - t0;
+    stats_.decode_ms = now_ms() - t_decode;
+    return out;
+}
+
+std::string Engine::telemetry_json() const {
+    std::ostringstream ss;
+    ss.setf(std::ios::fixed);
+    ss.precision(2);
+    const GenStats& s = stats_;
+    const double tps = s.decode_ms > 0 ? (double)s.emitted / (s.decode_ms / 1000.0) : 0.0;
+    const double rate = s.drafted ? 100.0 * (double)s.accepted / (double)s.drafted : 0.0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceProp prop{};
+    cudaGetDeviceProperties(&prop, dev);
+    const G4DenseHeader& h = target_->header();
+    ss << "{\n";
+    ss << "  \"tps\": " << tps << ",\n";
+    ss << "  \"ttft_ms\": " << s.ttft_ms << ",\n";
+    ss << "  \"speculative_acceptance_rate\": " << rate << ",\n";
+    ss << "  \"max_context\": " << target_->max_context() << ",\n";
+    ss << "  \"gpu_name\": \"" << prop.name << "\",\n";
+    ss << "  \"has_draft\": " << (draft_ ? "true" : "false") << ",\n";
+    ss << "  \"speculative_drafted\": " << s.drafted << ",\n";
+    ss << "  \"speculative_accepted\": " << s.accepted << ",\n";
+    ss << "  \"drafting_gated\": " << (s.gated ? "true" : "false") << ",\n";
+    ss << "  \"total_tokens_generated\": " << s.emitted << ",\n";
+    ss << "  \"kv_cache_mb\": " << (double)target_->kv_bytes() / 1048576.0 << ",\n";
+    ss << "  \"layer_mb\": " << (double)target_->weight_bytes() / 1048576.0 / std::max(1u, h.num_layers) << ",\n";
+    ss << "  \"total_layers\": " << h.num_layers << ",\n";
+    ss << "  \"streamed_layers\": 0,\n";
+    ss << "  \"speculative_rounds\": " << s.rounds << ",\n";
+    ss << "  \"gated_steps\": " << s.gated_steps << ",\n";
+    ss << "  \"tensor_parallel\": " << target_->options().tp << ",\n";
+    ss << "  \"breakdown\": {\n";
+    ss << "    \"decode_ms\": " << s.decode_ms << ",\n";
+    ss << "    \"round_ms\": " << s.verify_ms << "\n";
+    ss << "  }\n";
+    ss << "}\n";
+    return ss.str();
+}
+
+}  // namespace g4b

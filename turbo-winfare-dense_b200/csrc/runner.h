@@ -1,0 +1,96 @@
+// The decode engine: ForwardRunner::forward_batch / generate (include/g4dense/runner.hpp:
+// 100-157, src/runner.cpp:2061-2347), DraftRuntime (include/g4dense/draft_runtime.hpp:19-54)
+// and the speculative round loop, over B200 DeviceModels. Prompts are token ids (the
+// reference's tokenizer and chat template sit outside this path).
+#pragma once
+#include <atomic>
+#include <cstdint>
+#include <functional>
+#include <memory>
+#include <string>
+#include <vector>
+
+#include "model.h"
+#include "sampling.h"
+
+namespace g4b {
+
+// Widest verify batch: the reference caps K at kGemmMaxBatch = 8
+// (include/g4dense/vk_pipeline.hpp:21); the B200 kernels take 16 rows, which BASELINE's
+// k = 8 configuration (K = 9) needs.
+constexpr uint32_t kMaxDraftWidth = 16;
+
+struct GenerationOptions {
+    int max_tokens{512};
+    SamplingParams sampling{};
+    bool speculative_enabled{false};  // off by default, as in the reference
+    uint32_t draft_k{6};              // verify width K (K-1 drafts), clamped to [2, 8]
+    int64_t stop_token{-1};           // < 0: no stop token
+    double gate_min_accept{0.45};     // adaptive gate (src/runner.cpp:2188-2195)
+    int gate_window{24};
+    // Config-3 "oracle drafter": the drafter model still runs its steps (cost), but the
+    // proposals replay `replay` (the target's own greedy stream after the prompt) with
+    // i.i.d. injected mismatches at `mismatch_rate`.
+    std::vector<uint32_t> replay;
+    double mismatch_rate{0.0};
+    uint64_t mismatch_seed{0};
+};
+
+struct GenStats {
+    uint64_t drafted{0}, accepted{0}, rounds{0}, gated_steps{0}, emitted{0};
+    double ttft_ms{0}, total_ms{0}, decode_ms{0}, draft_ms{0}, verify_ms{0};
+    bool gated{false};
+    std::vector<int> round_info;  // (drafted, accepted, emitted) per verify round
+    int stop_reason{0};           // 0 max_tokens, 1 stop token, 2 callback, 3 cancelled
+};
+
+using TokenCallback = std::function<bool(uint32_t token)>;
+
+// DraftRuntime: a second DeviceModel on the target's stream plus the bookkeeping of how much
+// of the context its KV cache holds (src/draft_runtime.cpp:46-103).
+class DraftRuntime {
+   public:
+    explicit DraftRuntime(std::unique_ptr<DeviceModel> m) : model_(std::move(m)) {}
+    DeviceModel& model() { return *model_; }
+    void reset() { consumed_ = 0; }
+    size_t consumed() const { return consumed_; }
+    // Feeds context[consumed, n-1) so the cache holds every token before the pending one.
+    void catch_up(const std::vector<uint32_t>& context);
+    // accept(): the reference sets consumed to the kept length; it is capped here at what the
+    // drafter actually forwarded, so a fully accepted round feeds its last draft next round.
+    void accept(size_t accepted_context_length, size_t forwarded) {
+        consumed_ = std::min(accepted_context_length, forwarded);
+    }
+    void set_consumed(size_t c) { consumed_ = c; }
+
+   private:
+    std::unique_ptr<DeviceModel> model_;
+    size_t consumed_{0};
+};
+
+class Engine {
+   public:
+    explicit Engine(std::unique_ptr<DeviceModel> target) : target_(std::move(target)) {}
+    DeviceModel& target() { return *target_; }
+    DraftRuntime* draft() { return draft_.get(); }
+    void set_draft(std::unique_ptr<DeviceModel> d) { draft_ = std::make_unique<DraftRuntime>(std::move(d)); }
+
+    // One pass over `batch` consecutive positions from base_position (runner.hpp:110-111).
+    // out_logits (host) receives the last row's logits, or all rows' when all_positions.
+    void forward_batch(const uint32_t* token_ids, uint32_t batch, uint32_t base_position, float* out_logits,
+                       bool all_positions = false);
+    // Generation from token ids; returns the emitted tokens.
+    std::vector<uint32_t> generate(const std::vector<uint32_t>& prompt, const GenerationOptions& opt,
+                                   const TokenCallback& on_token, const std::atomic<bool>* cancel = nullptr);
+    const GenStats& last_stats() const { return stats_; }
+    std::string telemetry_json() const;
+
+   private:
+    uint32_t prefill(const std::vector<uint32_t>& tokens, const GenerationOptions& opt, std::vector<float>* last_logits);
+    std::unique_ptr<DeviceModel> target_;
+    std::unique_ptr<DraftRuntime> draft_;
+    SpeculativeCoordinator speculator_;
+    GenStats stats_;
+};
+
+}  // namespace g4b

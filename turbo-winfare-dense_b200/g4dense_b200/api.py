@@ -36,17 +36,47 @@ def lib():
     return _lib
 
 
+class EngineConfig(ctypes.Structure):
+    """G4DenseEngineConfig (include/g4dense/c_api.h)."""
+    _fields_ = [("container_path", ctypes.c_char_p), ("synthetic_preset", ctypes.c_char_p),
+                ("synthetic_seed", ctypes.c_ulonglong), ("synthetic_centered", ctypes.c_int),
+                ("draft_path", ctypes.c_char_p), ("draft_preset", ctypes.c_char_p),
+                ("draft_seed", ctypes.c_ulonglong), ("draft_k", ctypes.c_int), ("max_context", ctypes.c_int),
+                ("kv_bf16", ctypes.c_int), ("tp_rank", ctypes.c_int), ("tp_size", ctypes.c_int),
+                ("nccl_unique_id", ctypes.c_void_p), ("device", ctypes.c_int),
+                ("gate_min_accept", ctypes.c_double), ("gate_window", ctypes.c_int)]
+
+
+TOKEN_CB = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_uint, ctypes.c_char_p)
+
+
 def _bind_engine(L):
-    """Binds the engine-level C API when the library exports it."""
-    if not hasattr(L, "g4dense_engine_create"):
-        return
+    """Binds the engine-level C API (include/g4dense/c_api.h)."""
     L.g4dense_engine_last_error.restype = ctypes.c_char_p
     L.g4dense_engine_create.restype = _vp
     L.g4dense_engine_create.argtypes = [ctypes.c_char_p]
+    L.g4dense_engine_create_ex.restype = _vp
+    L.g4dense_engine_create_ex.argtypes = [ctypes.POINTER(EngineConfig)]
+    L.g4dense_config_default.argtypes = [ctypes.POINTER(EngineConfig)]
     L.g4dense_engine_destroy.argtypes = [_vp]
     L.g4dense_engine_get_telemetry.restype = ctypes.c_char_p
     L.g4dense_engine_get_telemetry.argtypes = [_vp]
     L.g4dense_options_default.argtypes = [_vp]
+    L.g4dense_engine_generate.restype = ctypes.c_char_p
+    L.g4dense_engine_generate.argtypes = [_vp, ctypes.c_char_p, ctypes.c_int]
+    L.g4dense_engine_generate_ex.restype = ctypes.c_char_p
+    L.g4dense_engine_generate_ex.argtypes = [_vp, ctypes.c_char_p, _vp, TOKEN_CB, _vp]
+    L.g4dense_engine_generate_tokens.restype = ctypes.c_char_p
+    L.g4dense_engine_generate_tokens.argtypes = [_vp, _vp, ctypes.c_int, _vp, TOKEN_CB, _vp]
+    L.g4dense_engine_last_tokens.argtypes = [_vp, _vp, ctypes.c_int]
+    L.g4dense_engine_last_rounds.argtypes = [_vp, _vp, ctypes.c_int]
+    L.g4dense_engine_forward_batch.argtypes = [_vp, _vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int]
+    L.g4dense_engine_set_decode_options.argtypes = [_vp, ctypes.c_longlong, ctypes.c_int, _vp, ctypes.c_int,
+                                                    ctypes.c_double, ctypes.c_ulonglong]
+    L.g4dense_engine_last_stop_reason.argtypes = [_vp]
+    L.g4dense_engine_switch_tier.argtypes = [_vp, ctypes.c_int]
+    L.g4dense_engine_stop.argtypes = [_vp]
+    L.g4dense_nccl_unique_id.argtypes = [_vp]
 
 
 def _check(rc, what):
@@ -118,5 +148,99 @@ class GenOptions(ctypes.Structure):
                 ("stop_strings", ctypes.c_void_p), ("stop_count", ctypes.c_int), ("tier_id", ctypes.c_int)]
 
 
+def _eng_err(what):
+    raise RuntimeError(f"{what}: {lib().g4dense_engine_last_error().decode()}")
+
+
 class Engine:
-    """Placeholder until the engine C API is bound (see _bind_engine)."""
+    """The engine behind include/g4dense/c_api.h (greedy or sampled, optional drafter)."""
+
+    def __init__(self, target=None, preset=None, seed=0, centered=False, draft=None, draft_preset=None,
+                 draft_seed=1, draft_k=0, max_context=4096, kv_bf16=False, tp_rank=0, tp_size=1,
+                 nccl_id=None, device=-1, gate_min_accept=0.45, gate_window=24):
+        L = lib()
+        cfg = EngineConfig()
+        L.g4dense_config_default(ctypes.byref(cfg))
+        self._keep = []
+        def cstr(x):
+            if x is None:
+                return None
+            b = str(x).encode()
+            self._keep.append(b)
+            return b
+        cfg.container_path = cstr(target)
+        cfg.synthetic_preset = cstr(preset)
+        cfg.synthetic_seed = seed
+        cfg.synthetic_centered = 1 if centered else 0
+        cfg.draft_path = cstr(draft)
+        cfg.draft_preset = cstr(draft_preset)
+        cfg.draft_seed = draft_seed
+        cfg.draft_k = draft_k
+        cfg.max_context = max_context
+        cfg.kv_bf16 = 1 if kv_bf16 else 0
+        cfg.tp_rank, cfg.tp_size = tp_rank, tp_size
+        if nccl_id is not None:
+            self._nid = ctypes.create_string_buffer(bytes(nccl_id), 128)
+            cfg.nccl_unique_id = ctypes.cast(self._nid, ctypes.c_void_p)
+        cfg.device = device
+        cfg.gate_min_accept = gate_min_accept
+        cfg.gate_window = gate_window
+        self.h = L.g4dense_engine_create_ex(ctypes.byref(cfg))
+        if not self.h:
+            _eng_err("g4dense_engine_create_ex")
+
+    def set_decode_options(self, stop_token=-1, draft_k=-1, replay=None, mismatch_rate=0.0, mismatch_seed=0):
+        r = None if replay is None else np.ascontiguousarray(replay, np.uint32)
+        if lib().g4dense_engine_set_decode_options(self.h, stop_token, draft_k,
+                                                   None if r is None else r.ctypes.data_as(_vp),
+                                                   0 if r is None else len(r), mismatch_rate, mismatch_seed):
+            _eng_err("g4dense_engine_set_decode_options")
+
+    def generate(self, prompt, max_tokens, temperature=0.0, top_p=1.0, top_k=0, seed=None, callback=None):
+        o = GenOptions()
+        lib().g4dense_options_default(ctypes.byref(o))
+        o.max_tokens = max_tokens
+        o.temperature, o.top_p, o.top_k = temperature, top_p, top_k
+        o.repetition_penalty = 1.0
+        o.has_seed = 0 if seed is None else 1
+        o.seed = 0 if seed is None else seed
+        p = np.ascontiguousarray(prompt, np.uint32)
+        cb = TOKEN_CB(lambda u, i, t, d: int(callback(t)) if callback else 1)
+        r = lib().g4dense_engine_generate_tokens(self.h, p.ctypes.data_as(_vp), len(p), ctypes.byref(o), cb, None)
+        if r is None:
+            _eng_err("g4dense_engine_generate_tokens")
+        out = np.zeros(max_tokens + 32, np.uint32)
+        n = lib().g4dense_engine_last_tokens(self.h, out.ctypes.data_as(_vp), len(out))
+        return out[:n].copy()
+
+    def rounds(self, cap=4096):
+        buf = np.zeros(3 * cap, np.int32)
+        n = lib().g4dense_engine_last_rounds(self.h, buf.ctypes.data_as(_vp), cap)
+        return [tuple(int(v) for v in buf[3 * i:3 * i + 3]) for i in range(n)]
+
+    def forward_batch(self, tokens, base, vocab=None, all_positions=True):
+        t = np.ascontiguousarray(tokens, np.uint32)
+        out = None
+        if vocab is not None:
+            out = np.zeros((len(t) if all_positions else 1, vocab), np.float32)
+        rc = lib().g4dense_engine_forward_batch(self.h, t.ctypes.data_as(_vp), len(t), base,
+                                                None if out is None else out.ctypes.data_as(_vp),
+                                                1 if all_positions else 0)
+        if rc:
+            _eng_err("g4dense_engine_forward_batch")
+        return out
+
+    def telemetry(self):
+        import json
+        return json.loads(lib().g4dense_engine_get_telemetry(self.h).decode())
+
+    def close(self):
+        if getattr(self, "h", None):
+            lib().g4dense_engine_destroy(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
