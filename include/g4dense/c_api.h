@@ -117,6 +117,22 @@ G4DENSE_API int g4dense_engine_set_decode_options(void* handle, long long stop_t
 /* Per-round (drafted, accepted, emitted) triples of the last speculative generation. */
 G4DENSE_API int g4dense_engine_last_rounds(void* handle, int* out, int cap_triples);
 G4DENSE_API int g4dense_nccl_unique_id(void* out128);
+/* Statistics of the last generation: {emitted, decode device ms (CUDA events from the end of
+ * prefill), ttft ms, total ms, drafted, accepted, rounds, gated steps, kernel launches,
+ * host->device bytes, device->host bytes, decode wall ms}. Returns how many were written. */
+G4DENSE_API int g4dense_engine_last_stats(void* handle, double* out, int n);
+/* The adaptive drafting gate (src/runner.cpp:2188-2195): stop drafting once at least `window`
+ * drafts have been made and fewer than min_accept of them were accepted; window < 0 disables
+ * it. Defaults 0.45 / 24. */
+G4DENSE_API int g4dense_engine_set_gate(void* handle, double min_accept, int window);
+/* Device time (CUDA events) of one forward pass of `batch` rows on the target (which = 0) or
+ * the drafter (which = 1), averaged over `reps` back-to-back graph replays; -1 on error. */
+G4DENSE_API double g4dense_engine_time_pass(void* handle, int which, int batch, int reps);
+/* Times every verify GEMM of one `batch`-row target pass, `reps` passes back to back, with
+ * CUDA events; returns ms per pass (-1 on error), the pass's algorithmic GEMM bytes and the
+ * GEMM launches per pass. A measurement hook for the verify-GEMM bandwidth metric. */
+G4DENSE_API double g4dense_engine_profile_gemms(void* handle, int batch, int reps, unsigned long long* bytes,
+                                                int* launches);
 
 #ifdef __cplusplus
 }

@@ -167,6 +167,36 @@ def spec_generate(target: RestatedModel, draft: RestatedModel | None, prompt, ma
     return out[:n].copy(), [tuple(int(v) for v in ri[3 * i:3 * i + 3]) for i in range(nr.value)]
 
 
+def greedy_margins(path, prompt, tokens):
+    """Top-1 minus top-2 logit of the target along a given continuation (teacher-forced):
+    margins[i] belongs to the distribution that produced tokens[i]."""
+    m = RestatedModel(path)
+    prompt = [int(t) for t in prompt]
+    for p, t in enumerate(prompt[:-1]):
+        m.forward(t, p)
+    out = []
+    prev, pos = prompt[-1], len(prompt) - 1
+    for t in tokens:
+        s = np.sort(m.forward(prev, pos))[::-1]
+        out.append(float(s[0] - s[1]))
+        prev, pos = int(t), pos + 1
+    m.close()
+    return out
+
+
+def check_stream(got, want, margins, noise=0.05):
+    """Greedy streams must be identical until the oracle reaches a near-tie (top-2 margin
+    below the FP16-KV rounding noise, `noise`); a divergence is accepted only there.
+    Returns the number of positions compared."""
+    got, want = [int(t) for t in got], [int(t) for t in want]
+    for i, (a, b) in enumerate(zip(got, want)):
+        if a != b:
+            assert margins[i] < noise, f"stream diverges at {i} where the oracle's margin is {margins[i]:.4f}"
+            return i
+    assert len(got) == len(want), (len(got), len(want))
+    return len(got)
+
+
 def int4_gemm(W, S, B, x):
     """Restated GemmInt4Batch: W u32 [N][K/8], S/B u16 [N][K/64], x f32 [M][K] -> [M][N]."""
     lib = restated_lib()

@@ -41,7 +41,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnArgs a) {
     uint16_t* v_s = k_s + kAttnKeys * kstride;                              // [32][hd]
     float* p_s = reinterpret_cast<float*>(v_s + kAttnKeys * hd);            // [16][32]
 
-    pdl_wait();
+    pdl_enter();
     const int kvh_i = blockIdx.x, chunk = blockIdx.y, split = blockIdx.z;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int gqa = a.qh / a.kvh;
@@ -177,7 +177,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnArgs a) {
 // (row, 64-column group) of the [M][qh*hd] output, written as B fragments.
 __global__ void attn_combine_kernel(AttnArgs a, void* bfrag) {
     __shared__ __half stage[8][128];
-    pdl_wait();
+    pdl_enter();
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     const int K = a.qh * a.hd;
     const int ng = K / 64;

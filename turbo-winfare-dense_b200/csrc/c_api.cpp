@@ -382,6 +382,78 @@ G4DENSE_API int g4dense_engine_switch_tier(void* handle, int tier_id) {
     return 0;
 }
 
+G4DENSE_API int g4dense_engine_last_stats(void* handle, double* out, int n) {
+    if (!handle || !out) return 0;
+    const g4b::GenStats& s = static_cast<EngineHandle*>(handle)->engine->last_stats();
+    const double v[] = {(double)s.emitted, s.decode_gpu_ms, s.ttft_ms, s.total_ms, (double)s.drafted,
+                        (double)s.accepted, (double)s.rounds, (double)s.gated_steps, (double)s.launches,
+                        (double)s.h2d_bytes, (double)s.d2h_bytes, s.decode_ms};
+    const int m = std::min<int>(n, (int)(sizeof(v) / sizeof(v[0])));
+    for (int i = 0; i < m; ++i) out[i] = v[i];
+    return m;
+}
+
+G4DENSE_API double g4dense_engine_profile_gemms(void* handle, int batch, int reps, unsigned long long* bytes,
+                                                int* launches) {
+    clear_error();
+    if (!handle || batch < 1 || batch > 16 || reps < 1) {
+        set_error("Invalid arguments");
+        return -1.0;
+    }
+    try {
+        uint64_t b = 0;
+        const double ms = static_cast<EngineHandle*>(handle)->engine->target().profile_gemms(batch, reps, &b, launches);
+        if (bytes) *bytes = b;
+        return ms;
+    } catch (const std::exception& e) {
+        set_error(e.what());
+        return -1.0;
+    }
+}
+
+G4DENSE_API int g4dense_engine_set_gate(void* handle, double min_accept, int window) {
+    clear_error();
+    if (!handle) {
+        set_error("Null handle");
+        return -1;
+    }
+    auto* e = static_cast<EngineHandle*>(handle);
+    e->gate_min_accept = min_accept;
+    e->gate_window = window;
+    return 0;
+}
+
+G4DENSE_API double g4dense_engine_time_pass(void* handle, int which, int batch, int reps) {
+    clear_error();
+    if (!handle || batch < 1 || batch > 16 || reps < 1) {
+        set_error("Invalid arguments");
+        return -1.0;
+    }
+    try {
+        auto* e = static_cast<EngineHandle*>(handle);
+        g4b::DeviceModel* m = which == 0 ? &e->engine->target()
+                                         : (e->engine->draft() ? &e->engine->draft()->model() : nullptr);
+        if (!m) throw std::invalid_argument("no drafter loaded");
+        std::vector<uint32_t> toks(batch, 1);
+        m->run_plain(batch, 0, toks.data(), false);  // warm (captures the graph)
+        cudaEvent_t a, b;
+        g4b::cuda_check(cudaEventCreate(&a), "event");
+        g4b::cuda_check(cudaEventCreate(&b), "event");
+        g4b::cuda_check(cudaEventRecord(a, m->stream()), "event");
+        for (int r = 0; r < reps; ++r) m->enqueue(batch, g4b::PassKind::Plain, false, nullptr);
+        g4b::cuda_check(cudaEventRecord(b, m->stream()), "event");
+        g4b::cuda_check(cudaEventSynchronize(b), "event");
+        float ms = 0.f;
+        cudaEventElapsedTime(&ms, a, b);
+        cudaEventDestroy(a);
+        cudaEventDestroy(b);
+        return (double)ms / reps;
+    } catch (const std::exception& ex) {
+        set_error(ex.what());
+        return -1.0;
+    }
+}
+
 G4DENSE_API void g4dense_engine_stop(void* handle) {
     if (handle) static_cast<EngineHandle*>(handle)->cancel.store(true);
 }

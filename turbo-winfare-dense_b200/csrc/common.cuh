@@ -115,5 +115,12 @@ __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;"
 __device__ __forceinline__ void pdl_launch_dependents() {
     asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
 }
+// Kernel entry under PDL: let the next kernel in the stream launch now (it only runs its
+// own prologue until it waits in turn), then wait for this kernel's producer to finish.
+// Every kernel calls this before touching anything a predecessor wrote.
+__device__ __forceinline__ void pdl_enter() {
+    pdl_launch_dependents();
+    pdl_wait();
+}
 
 }  // namespace g4b

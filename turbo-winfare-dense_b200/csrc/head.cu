@@ -29,7 +29,7 @@ __global__ void head_chunks_kernel(GemmOut lm, int V, int M, float softcap, floa
                                    float2* chunk_best) {
     __shared__ float sv[32];
     __shared__ uint32_t si[32];
-    pdl_wait();
+    pdl_enter();
     const int chunk = blockIdx.x, m = blockIdx.y;
     const int v0 = chunk * kHeadChunk, v1 = min(V, v0 + kHeadChunk);
     float bv = -INFINITY;
@@ -59,7 +59,7 @@ __global__ void head_chunks_kernel(GemmOut lm, int V, int M, float softcap, floa
 __global__ void head_finalize_kernel(const float2* chunk_best, int nchunks, int M, StepParams* sp,
                                      HeadResult* res, uint32_t* chain_out) {
     __shared__ uint32_t am[16];
-    pdl_wait();
+    pdl_enter();
     const int lane = threadIdx.x & 31, m = threadIdx.x >> 5;
     if (m < M) {
         float bv = -INFINITY;

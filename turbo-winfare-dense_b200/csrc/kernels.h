@@ -17,12 +17,14 @@ cudaError_t g4b_embed_norm(const g4b::StepParams* sp, const uint32_t* ew, const 
                            int V, int d, const uint16_t* w_in, float* h_out, void* bfrag, int M, cudaStream_t st,
                            bool pdl);
 cudaError_t g4b_qkv_epi(const g4b::QkvEpiArgs& a, cudaStream_t st, bool pdl);
-cudaError_t g4b_post_attn(const g4b::GemmOut& o, const float* h_in, float* h_out, const uint16_t* w_pa,
-                          const uint16_t* w_pf, int d, void* bfrag, int M, cudaStream_t st, bool pdl);
 cudaError_t g4b_geglu(const g4b::GemmOut& gu, int F, void* bfrag, int M, cudaStream_t st, bool pdl);
-cudaError_t g4b_post_ffn(const g4b::GemmOut& dn, const float* h_in, float* h_out, const uint16_t* w_pffn,
-                         float layer_scalar, const uint16_t* w_next, int d, void* bfrag, int M, cudaStream_t st,
-                         bool pdl);
+// Norm/residual epilogue (post-attention with out_scale = 1, post-FFN with the layer scalar):
+// h_out = (h_in + rmsnorm(o)*w1) * out_scale; x = rmsnorm(h_out)*w2 -> B fragments.
+// y_buf [16][d] and stats [16][chunks] are scratch.
+int g4b_rowepi_chunks(int d);
+cudaError_t g4b_rowepi(const g4b::GemmOut& o, const float* h_in, float* h_out, const uint16_t* w1, float out_scale,
+                       const uint16_t* w2, int d, float* y_buf, float4* stats, void* bfrag, int M, cudaStream_t st,
+                       bool pdl);
 
 // ---- attention.cu
 // Splits of the key range per KV head chosen for the launch (fixed per captured graph).

@@ -412,6 +412,8 @@ void DeviceModel::init_buffers() {
     o_part_ = static_cast<float*>(dmalloc(attn_part_floats_ * 4));
     ml_part_ = static_cast<float2*>(dmalloc((size_t)64 * kMaxM * max_qh * sizeof(float2)));
     y_ = static_cast<float*>(dmalloc((size_t)kMaxM * std::max(d, 2 * max_F) * 4));
+    ybuf_ = static_cast<float*>(dmalloc((size_t)kMaxM * d * 4));
+    stats_ = static_cast<float4*>(dmalloc((size_t)kMaxM * g4b_rowepi_chunks(d) * sizeof(float4)));
     chunk_best_ = static_cast<float2*>(dmalloc((size_t)opt_.tp * kMaxM * g4b_head_chunks(v_local_) * sizeof(float2)));
     logits_ = static_cast<float*>(dmalloc((size_t)kMaxM * v_local_ * 4));
     res_dev_ = static_cast<HeadResult*>(dmalloc(sizeof(HeadResult)));
@@ -431,6 +433,54 @@ void DeviceModel::clear_kv() {
 }
 
 uint64_t DeviceModel::pass_weight_bytes() const { return weight_bytes_; }
+
+int DeviceModel::kernels_per_pass(int M) const {
+    (void)M;
+    // embed_norm; per layer 4 GEMMs + qkv_epi + attention + combine + 2x2 norm/residual
+    // phases + geglu (+ 2 slot reductions under TP); LM head GEMM + head_chunks + finalize
+    const int per_layer = 12 + (opt_.tp > 1 ? 2 : 0);
+    return 1 + per_layer * (int)layers_.size() + 3;
+}
+
+double DeviceModel::profile_gemms(int M, int reps, uint64_t* bytes, int* gemm_launches) {
+    if (!loaded_) throw std::runtime_error("model not loaded");
+    uint64_t b = 0;
+    int n = 0;
+    auto alg = [&](const QW& q) {
+        b += (uint64_t)q.N * q.K / 2 + (uint64_t)q.N * (q.K / 64) * 4 + 4ull * M * q.K + 4ull * M * q.N;
+        ++n;
+    };
+    for (auto& L : layers_) {
+        alg(L.qkv);
+        alg(L.o);
+        alg(L.gateup);
+        alg(L.down);
+    }
+    alg(lm_);
+    cudaEvent_t e0, e1;
+    cuda_check(cudaEventCreate(&e0), "event");
+    cuda_check(cudaEventCreate(&e1), "event");
+    cuda_check(cudaEventRecord(e0, stream_), "event");
+    for (int r = 0; r < reps; ++r) {
+        for (auto& L : layers_) {
+            gemm(L.qkv, bf_d_, M);
+            gemm(L.o, bf_attn_, M);
+            gemm(L.gateup, bf_d_, M);
+            gemm(L.down, bf_ff_, M);
+        }
+        gemm(lm_, bf_d_, M);
+    }
+    cuda_check(cudaEventRecord(e1, stream_), "event");
+    cuda_check(cudaEventSynchronize(e1), "event");
+    float ms = 0.f;
+    cuda_check(cudaEventElapsedTime(&ms, e0, e1), "event");
+    cudaEventDestroy(e0);
+    cudaEventDestroy(e1);
+    launches_ += (uint64_t)n * reps;
+    if (bytes) *bytes = b;
+    if (gemm_launches) *gemm_launches = n;
+    return (double)ms / reps;
+}
 
 // ----------------------------------------------------------------------------- forward
 
@@ -522,7 +572,8 @@ void DeviceModel::enqueue_raw(int M, PassKind kind, bool want_logits, uint32_t* 
             oo.ld = d;
         }
 #endif
-        cuda_check(g4b_post_attn(oo, hres_[cur], hres_[1 - cur], L.pa_norm, L.pf_norm, d, bf_d_, M, stream_, pdl),
+        cuda_check(g4b_rowepi(oo, hres_[cur], hres_[1 - cur], L.pa_norm, 1.0f, L.pf_norm, d, ybuf_, stats_, bf_d_, M,
+                              stream_, pdl),
                    "post_attn");
         cur = 1 - cur;
         // FFN
@@ -545,7 +596,8 @@ void DeviceModel::enqueue_raw(int M, PassKind kind, bool want_logits, uint32_t* 
         }
 #endif
         const uint16_t* w_next = (l + 1 < layers_.size()) ? layers_[l + 1].in_norm : final_norm_;
-        cuda_check(g4b_post_ffn(dn, hres_[cur], hres_[1 - cur], L.pffn_norm, L.scalar, w_next, d, bf_d_, M, stream_, pdl),
+        cuda_check(g4b_rowepi(dn, hres_[cur], hres_[1 - cur], L.pffn_norm, L.scalar, w_next, d, ybuf_, stats_, bf_d_, M,
+                              stream_, pdl),
                    "post_ffn");
         cur = 1 - cur;
     }
@@ -564,6 +616,7 @@ void DeviceModel::enqueue(int M, PassKind kind, bool want_logits, uint32_t* chai
     if (!loaded_) throw std::runtime_error("model not loaded");
     if (M < 1 || M > kMaxM) throw std::runtime_error("batch width must be 1..16");
     if (opt_.tp > 1 && h_.vocab_size % opt_.tp) throw std::runtime_error("vocab split");
+    launches_ += kernels_per_pass(M);
     if (!opt_.use_graphs) {
         enqueue_raw(M, kind, want_logits, chain_out);
         return;
@@ -599,6 +652,7 @@ void DeviceModel::push_params(int slot, const StepParams& p) {
     StepParams& s = sp_host_[sp_ring_++];
     s = p;
     cuda_check(cudaMemcpyAsync(sp_dev_ + slot, &s, sizeof(StepParams), cudaMemcpyHostToDevice, stream_), "params");
+    h2d_bytes_ += sizeof(StepParams);
 }
 
 void DeviceModel::run_plain(int M, int base_pos, const uint32_t* tokens, bool want_logits) {
@@ -616,6 +670,7 @@ void DeviceModel::run_plain(int M, int base_pos, const uint32_t* tokens, bool wa
 
 HeadResult DeviceModel::fetch_result() {
     cuda_check(cudaMemcpyAsync(res_host_, res_dev_, sizeof(HeadResult), cudaMemcpyDeviceToHost, stream_), "result");
+    d2h_bytes_ += sizeof(HeadResult);
     cuda_check(cudaStreamSynchronize(stream_), "sync");
     sp_ring_ = 0;  // the stream is drained: the whole parameter ring is free again
     return *res_host_;

@@ -93,6 +93,16 @@ class DeviceModel {
 
     // Timing hook: total verify-GEMM algorithmic weight bytes of one pass.
     uint64_t pass_weight_bytes() const;
+    // Kernel launches of one pass of M rows, and the running count of launches enqueued.
+    int kernels_per_pass(int M) const;
+    uint64_t launches() const { return launches_; }
+    // Times every verify GEMM of one M-row pass (PDL-chained, `reps` times back to back) with
+    // CUDA events on the model's stream. Returns milliseconds per pass; *bytes receives the
+    // algorithmic bytes of one pass's GEMMs (packed weights + fp32 activations + outputs).
+    double profile_gemms(int M, int reps, uint64_t* bytes, int* gemm_launches);
+    // Host<->device bytes moved by the per-pass parameter and result copies so far.
+    uint64_t h2d_bytes() const { return h2d_bytes_; }
+    uint64_t d2h_bytes() const { return d2h_bytes_; }
 
    private:
     void init_buffers();
@@ -127,6 +137,8 @@ class DeviceModel {
     float2* ml_part_ = nullptr;
     size_t attn_part_floats_ = 0;
     float* y_ = nullptr;  // all-reduce staging [16][max(d, ...)]
+    float* ybuf_ = nullptr;    // norm/residual epilogue scratch [16][d]
+    float4* stats_ = nullptr;  // [16][chunks]
     float2* chunk_best_ = nullptr;
     float* logits_ = nullptr;
     HeadResult* res_dev_ = nullptr;
@@ -146,6 +158,7 @@ class DeviceModel {
     static constexpr int kParamRing = 256;
     HeadResult* res_host_ = nullptr; // pinned
     bool own_stream_ = true;
+    uint64_t launches_ = 0, h2d_bytes_ = 0, d2h_bytes_ = 0;
 };
 
 // cudaError_t -> exception with context.

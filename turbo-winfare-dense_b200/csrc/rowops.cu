@@ -1,20 +1,24 @@
 // Row-wise kernels around the verify GEMM. Each consumes a GEMM's split-K slots (or an
-// all-reduced matrix), applies the layer's elementwise/normalisation step in fp32 exactly as
-// src/cpu_reference.cpp orders it, and produces the next GEMM's B fragments, so no
+// all-reduced matrix), applies the layer's elementwise/normalisation step in fp32 in the
+// order src/cpu_reference.cpp uses, and produces the next GEMM's B fragments, so no
 // activation is ever converted twice:
 //   embed_norm   token gather x sqrt(d) (src/cpu_reference.cpp:260-291) + input RMSNorm
 //   qkv_epi      q/k RMSNorm*w + NeoX RoPE, v unweighted RMSNorm (raw k on layers without
 //                v_proj), K/V rounded and written to the ring (:398-498, QKVEpilogue.hlsl,
-//                KVWrite.hlsl)
-//   post_attn    h += rmsnorm(o)*w_post_attn; x = rmsnorm(h)*w_pre_ffn (:560-567)
+//                KVWrite.hlsl) -- one warp per (row, head)
+//   rowepi       post-attention: h += rmsnorm(o)*w_post_attn; x = rmsnorm(h)*w_pre_ffn
+//                (:560-567); post-FFN: h = (h + rmsnorm(down)*w_post_ffn) * layer_scalar,
+//                then the next layer's input norm or the final norm (:583-629). Two wide
+//                phases: phase 1 sums the split-K slots and gathers per-chunk statistics,
+//                phase 2 derives both RMS factors and finishes every column in parallel.
 //   geglu        gelu_tanh(gate) * up (:568-581, GeGLU.hlsl)
-//   post_ffn     h = (h + rmsnorm(down)*w_post_ffn) * layer_scalar (:583-593), then the next
-//                layer's input norm, or the final norm before the LM head (:610-629)
 #include "bfrag.cuh"
 #include "common.cuh"
 #include "kernels.h"
 #include "launch.cuh"
 #include "model_dev.h"
+
+#include <algorithm>
 
 namespace g4b {
 
@@ -41,17 +45,12 @@ __device__ __forceinline__ uint16_t bf16_bits_rne(float f) {
     return (uint16_t)(u >> 16);
 }
 
-__device__ __forceinline__ float kv_decode(uint16_t b, int bf16) {
-    return bf16 ? __uint_as_float((uint32_t)b << 16) : __half2float(__ushort_as_half(b));
-}
-
 // 1 / sqrt(mean + eps) with IEEE sqrt and division, as the reference computes it.
 __device__ __forceinline__ float inv_rms(float sumsq, int n) {
     return 1.0f / sqrtf(sumsq / (float)n + 1e-6f);
 }
 
-// Writes a full row x[0..K) (K a multiple of 64, in shared memory) as B fragments, one warp
-// per 64-group.
+// Writes a full row x[0..K) (in shared memory) as B fragments, one warp per 64-group.
 __device__ __forceinline__ void row_to_bfrags(const float* xs, int K, int M, int m, void* bfrag, __half* stage) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     const int Kp = (K + 127) / 128 * 128;
@@ -69,13 +68,12 @@ __global__ void embed_norm_kernel(const StepParams* __restrict__ sp, const uint3
                                   const uint16_t* __restrict__ es, const uint16_t* __restrict__ eb, int V, int d,
                                   const uint16_t* __restrict__ w_in, float* __restrict__ h_out, void* bfrag, int M) {
     extern __shared__ float smem[];
-    float* xs = smem;                                       // [d]
-    __half* stage = reinterpret_cast<__half*>(xs + d);      // [warps][128]
+    float* xs = smem;                                   // [d]
+    __half* stage = reinterpret_cast<__half*>(xs + d);  // [warps][128]
     __shared__ float red[32];
-    pdl_wait();
+    pdl_enter();
     const int m = blockIdx.x;
-    uint32_t tok = sp->tokens[m];
-    tok %= (uint32_t)V;
+    const uint32_t tok = sp->tokens[m] % (uint32_t)V;
     const float scale = sqrtf((float)d);
     const uint32_t* wr = ew + (size_t)tok * (d / 8);
     const uint16_t* sr = es + (size_t)tok * (d / 64);
@@ -96,96 +94,166 @@ __global__ void embed_norm_kernel(const StepParams* __restrict__ sp, const uint3
 
 // ---------------------------------------------------------------- Q/K/V epilogue
 
-// One block per (row m, head): heads [0, qh) are query heads, [qh, qh + kvh) KV heads.
+// One warp per (row m, head): heads [0, qh) are query heads, [qh, qh + kvh) KV heads. Lane l
+// holds elements l + 32j, so the NeoX partner of element i (i + hd/2) lives in the same lane.
+constexpr int kMaxHdPerLane = 16;  // head_dim <= 512
+
 __global__ void qkv_epi_kernel(QkvEpiArgs a) {
-    extern __shared__ float smem[];
-    float* xs = smem;          // [hd]
-    float* vs = smem + a.hd;   // [hd]
-    __shared__ float red[32];
-    pdl_wait();
-    const int m = blockIdx.x, head = blockIdx.y;
-    const int hd = a.hd;
+    pdl_enter();
+    const int lane = threadIdx.x & 31;
+    const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+    const int heads = a.qh + a.kvh;
+    if (w >= a.M * heads) return;
+    const int m = w / heads, head = w % heads;
+    const int hd = a.hd, np = hd / 32;
     const int pos = a.sp->base_pos + m;
     const int nq = a.qh * hd, nk = a.kvh * hd;
     const bool is_q = head < a.qh;
     const int kvh = head - a.qh;
     const int row0 = is_q ? head * hd : nq + kvh * hd;
+    float x[kMaxHdPerLane];
     float ss = 0.f;
-    for (int i = threadIdx.x; i < hd; i += blockDim.x) {
-        const float v = gemm_out_get(a.qkv, m, row0 + i);
-        xs[i] = v;
-        ss += v * v;
-    }
-    const float r = inv_rms(block_sum(ss, red), hd);
+#pragma unroll
+    for (int j = 0; j < kMaxHdPerLane; ++j)
+        if (j < np) {
+            x[j] = gemm_out_get(a.qkv, m, row0 + lane + 32 * j);
+            ss += x[j] * x[j];
+        }
+    const float r = inv_rms(warp_sum(ss), hd);
     if (!is_q) {
         // V: unweighted norm of v_proj, or of the RAW k on layers without v_proj.
+        float v[kMaxHdPerLane];
         float vss = 0.f;
-        for (int i = threadIdx.x; i < hd; i += blockDim.x) {
-            const float v = a.has_v ? gemm_out_get(a.qkv, m, nq + nk + kvh * hd + i) : xs[i];
-            vs[i] = v;
-            vss += v * v;
-        }
-        const float rv = inv_rms(block_sum(vss, red), hd);
+#pragma unroll
+        for (int j = 0; j < kMaxHdPerLane; ++j)
+            if (j < np) {
+                v[j] = a.has_v ? gemm_out_get(a.qkv, m, nq + nk + kvh * hd + lane + 32 * j) : x[j];
+                vss += v[j] * v[j];
+            }
+        const float rv = inv_rms(warp_sum(vss), hd);
         uint16_t* vd = a.v_ring + ((size_t)(pos % a.cap) * a.kvh + kvh) * hd;
-        for (int i = threadIdx.x; i < hd; i += blockDim.x) {
-            const float v = vs[i] * rv;
-            vd[i] = a.kv_bf16 ? bf16_bits_rne(v) : f16_bits_like_reference(v);
+#pragma unroll
+        for (int j = 0; j < kMaxHdPerLane; ++j)
+            if (j < np) {
+                const float t = v[j] * rv;
+                vd[lane + 32 * j] = a.kv_bf16 ? bf16_bits_rne(t) : f16_bits_like_reference(t);
+            }
+    }
+    const uint16_t* wn = is_q ? a.q_norm : a.k_norm;
+#pragma unroll
+    for (int j = 0; j < kMaxHdPerLane; ++j)
+        if (j < np) x[j] = x[j] * r * bf16_to_f32(wn[lane + 32 * j]);
+    // NeoX rotary on `rotated` pairs (i, i + hd/2).
+    const int half_j = hd / 64;
+#pragma unroll
+    for (int j = 0; j < kMaxHdPerLane / 2; ++j) {
+        const int p = lane + 32 * j;
+        if (j < half_j && p < a.rotated) {
+            const float freq = 1.0f / powf(a.theta, (float)(2 * p) / (float)hd);
+            const float ang = (float)pos * freq;
+            const float c = cosf(ang), s = sinf(ang);
+            const float x0 = x[j], x1 = x[j + half_j];
+            x[j] = x0 * c - x1 * s;
+            x[j + half_j] = x0 * s + x1 * c;
         }
     }
-    const uint16_t* w = is_q ? a.q_norm : a.k_norm;
-    __syncthreads();
-    for (int i = threadIdx.x; i < hd; i += blockDim.x) xs[i] = xs[i] * r * bf16_to_f32(w[i]);
-    __syncthreads();
-    // NeoX rotary on `rotated` pairs (i, i + hd/2).
-    const int half = hd / 2;
-    for (int p = threadIdx.x; p < a.rotated; p += blockDim.x) {
-        const float freq = 1.0f / powf(a.theta, (float)(2 * p) / (float)hd);
-        const float ang = (float)pos * freq;
-        const float c = cosf(ang), s = sinf(ang);
-        const float x0 = xs[p], x1 = xs[p + half];
-        xs[p] = x0 * c - x1 * s;
-        xs[p + half] = x0 * s + x1 * c;
-    }
-    __syncthreads();
     if (is_q) {
         float* qd = a.q_out + ((size_t)m * a.qh + head) * hd;
-        for (int i = threadIdx.x; i < hd; i += blockDim.x) qd[i] = xs[i];
+#pragma unroll
+        for (int j = 0; j < kMaxHdPerLane; ++j)
+            if (j < np) qd[lane + 32 * j] = x[j];
     } else {
         uint16_t* kd = a.k_ring + ((size_t)(pos % a.cap) * a.kvh + kvh) * hd;
-        for (int i = threadIdx.x; i < hd; i += blockDim.x)
-            kd[i] = a.kv_bf16 ? bf16_bits_rne(xs[i]) : f16_bits_like_reference(xs[i]);
+#pragma unroll
+        for (int j = 0; j < kMaxHdPerLane; ++j)
+            if (j < np) kd[lane + 32 * j] = a.kv_bf16 ? bf16_bits_rne(x[j]) : f16_bits_like_reference(x[j]);
     }
 }
 
-// ---------------------------------------------------------------- post-attention
+// ---------------------------------------------------------------- norm/residual epilogues
 
-__global__ void post_attn_kernel(GemmOut o, const float* __restrict__ h_in, float* __restrict__ h_out,
-                                 const uint16_t* __restrict__ w_pa, const uint16_t* __restrict__ w_pf, int d,
-                                 void* bfrag, int M) {
-    extern __shared__ float smem[];
-    float* ys = smem;                                   // [d]
-    __half* stage = reinterpret_cast<__half*>(ys + d);  // [warps][128]
-    __shared__ float red[32];
-    pdl_wait();
-    const int m = blockIdx.x;
-    float ss = 0.f;
-    for (int c = threadIdx.x; c < d; c += blockDim.x) {
-        const float v = gemm_out_get(o, m, c);
-        ys[c] = v;
-        ss += v * v;
+// Block of 4 warps, one 64-column group per warp: 256 columns per block, grid (chunks, M).
+constexpr int kEpiWarps = 4;
+constexpr int kEpiCols = kEpiWarps * 64;
+
+// Phase 1: y = GEMM output (slot sums); per-chunk sums of y^2, h^2, h*c and c^2 with
+// c = y * w1, from which phase 2 obtains both RMS factors without another pass.
+__global__ void rowepi_phase1_kernel(GemmOut o, const float* __restrict__ h_in, const uint16_t* __restrict__ w1, int d,
+                                     float* __restrict__ y_buf, float4* __restrict__ stats) {
+    __shared__ float4 red[kEpiWarps];
+    pdl_enter();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int m = blockIdx.y, chunk = blockIdx.x;
+    const int c0 = chunk * kEpiCols + warp * 64 + 2 * lane;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        const int c = c0 + j;
+        if (c < d) {
+            const float y = gemm_out_get(o, m, c);
+            const float h = h_in[(size_t)m * d + c];
+            const float cc = y * bf16_to_f32(w1[c]);
+            y_buf[(size_t)m * d + c] = y;
+            acc.x += y * y;
+            acc.y += h * h;
+            acc.z += h * cc;
+            acc.w += cc * cc;
+        }
     }
-    const float r1 = inv_rms(block_sum(ss, red), d);
-    float ss2 = 0.f;
-    for (int c = threadIdx.x; c < d; c += blockDim.x) {
-        const float hn = h_in[(size_t)m * d + c] + ys[c] * r1 * bf16_to_f32(w_pa[c]);
-        h_out[(size_t)m * d + c] = hn;
-        ys[c] = hn;
-        ss2 += hn * hn;
-    }
-    const float r2 = inv_rms(block_sum(ss2, red), d);
-    for (int c = threadIdx.x; c < d; c += blockDim.x) ys[c] = ys[c] * r2 * bf16_to_f32(w_pf[c]);
+    acc.x = warp_sum(acc.x);
+    acc.y = warp_sum(acc.y);
+    acc.z = warp_sum(acc.z);
+    acc.w = warp_sum(acc.w);
+    if (lane == 0) red[warp] = acc;
     __syncthreads();
-    row_to_bfrags(ys, d, M, m, bfrag, stage);
+    if (threadIdx.x == 0) {
+        float4 t = red[0];
+        for (int i = 1; i < kEpiWarps; ++i) {
+            t.x += red[i].x; t.y += red[i].y; t.z += red[i].z; t.w += red[i].w;
+        }
+        stats[(size_t)m * gridDim.x + chunk] = t;
+    }
+}
+
+// Phase 2: r1 = 1/rms(y); h' = (h + (y*r1)*w1) * out_scale; r2 = 1/rms(h') from the phase-1
+// sums; x = (h'*r2)*w2 written as B fragments of the next GEMM.
+__global__ void rowepi_phase2_kernel(const float* __restrict__ y_buf, const float4* __restrict__ stats,
+                                     const float* __restrict__ h_in, float* __restrict__ h_out,
+                                     const uint16_t* __restrict__ w1, const uint16_t* __restrict__ w2,
+                                     float out_scale, int d, void* bfrag, int M) {
+    __shared__ __half stage[kEpiWarps][128];
+    pdl_enter();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int m = blockIdx.y, chunk = blockIdx.x;
+    const int nch = gridDim.x;
+    // Every warp reduces the row's chunk sums in the same fixed order.
+    float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int i = lane; i < nch; i += 32) {
+        const float4 s = stats[(size_t)m * nch + i];
+        t.x += s.x; t.y += s.y; t.z += s.z; t.w += s.w;
+    }
+    t.x = warp_sum(t.x);
+    t.y = warp_sum(t.y);
+    t.z = warp_sum(t.z);
+    t.w = warp_sum(t.w);
+    const float r1 = inv_rms(t.x, d);
+    const float s2 = out_scale * out_scale * (t.y + 2.0f * r1 * t.z + r1 * r1 * t.w);
+    const float r2 = inv_rms(fmaxf(s2, 0.f), d);
+    const int gi = chunk * kEpiWarps + warp;
+    const int Kp = (d + 127) / 128 * 128;
+    if (gi * 64 >= Kp) return;
+    float x[2] = {0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < 2; ++j) {
+        const int c = gi * 64 + 2 * lane + j;
+        if (c < d) {
+            const float a = __fmul_rn(__fmul_rn(y_buf[(size_t)m * d + c], r1), bf16_to_f32(w1[c]));
+            const float hn = __fmul_rn(__fadd_rn(h_in[(size_t)m * d + c], a), out_scale);
+            h_out[(size_t)m * d + c] = hn;
+            x[j] = __fmul_rn(__fmul_rn(hn, r2), bf16_to_f32(w2[c]));
+        }
+    }
+    bfrag_store_group(bfrag_view(bfrag, Kp, M), M, m, gi, x[0], x[1], stage[warp]);
 }
 
 // ---------------------------------------------------------------- GeGLU
@@ -199,7 +267,7 @@ __device__ __forceinline__ float gelu_tanh_dev(float x) {
 // One warp per (row, 64-group) of the F-wide activation; gate rows [0, F), up rows [F, 2F).
 __global__ void geglu_kernel(GemmOut gu, int F, void* bfrag, int M) {
     __shared__ __half stage[8][128];
-    pdl_wait();
+    pdl_enter();
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     const int Fp = (F + 127) / 128 * 128;
     const int ng = Fp / 64;
@@ -214,43 +282,12 @@ __global__ void geglu_kernel(GemmOut gu, int F, void* bfrag, int M) {
     }
 }
 
-// ---------------------------------------------------------------- post-FFN
-
-__global__ void post_ffn_kernel(GemmOut dn, const float* __restrict__ h_in, float* __restrict__ h_out,
-                                const uint16_t* __restrict__ w_pffn, float layer_scalar,
-                                const uint16_t* __restrict__ w_next, int d, void* bfrag, int M) {
-    extern __shared__ float smem[];
-    float* ys = smem;
-    __half* stage = reinterpret_cast<__half*>(ys + d);
-    __shared__ float red[32];
-    pdl_wait();
-    const int m = blockIdx.x;
-    float ss = 0.f;
-    for (int c = threadIdx.x; c < d; c += blockDim.x) {
-        const float v = gemm_out_get(dn, m, c);
-        ys[c] = v;
-        ss += v * v;
-    }
-    const float r1 = inv_rms(block_sum(ss, red), d);
-    float ss2 = 0.f;
-    for (int c = threadIdx.x; c < d; c += blockDim.x) {
-        const float hn = (h_in[(size_t)m * d + c] + ys[c] * r1 * bf16_to_f32(w_pffn[c])) * layer_scalar;
-        h_out[(size_t)m * d + c] = hn;
-        ys[c] = hn;
-        ss2 += hn * hn;
-    }
-    const float r2 = inv_rms(block_sum(ss2, red), d);
-    for (int c = threadIdx.x; c < d; c += blockDim.x) ys[c] = ys[c] * r2 * bf16_to_f32(w_next[c]);
-    __syncthreads();
-    row_to_bfrags(ys, d, M, m, bfrag, stage);
-}
-
 // ---------------------------------------------------------------- plain conversion
 
 // x [M][ldx] fp32 -> B fragments. One warp per (row, 64-group); groups past K are zeros.
 __global__ void bfrag_from_f32_kernel(const float* __restrict__ x, int ldx, int M, int K, void* bfrag) {
     __shared__ __half stage[8][128];
-    pdl_wait();
+    pdl_enter();
     const int lane = threadIdx.x & 31, wib = threadIdx.x >> 5;
     const int Kp = (K + 127) / 128 * 128;
     const int ngroups = Kp / 64;
@@ -287,25 +324,23 @@ cudaError_t g4b_embed_norm(const StepParams* sp, const uint32_t* ew, const uint1
 }
 
 cudaError_t g4b_qkv_epi(const QkvEpiArgs& a, cudaStream_t st, bool pdl) {
-    return launch(qkv_epi_kernel, dim3(a.M, a.qh + a.kvh), dim3(128), (size_t)2 * a.hd * sizeof(float), st, pdl, a);
+    if (a.hd % 64 || a.hd > 32 * kMaxHdPerLane || a.rotated > a.hd / 2) return cudaErrorInvalidValue;
+    return launch(qkv_epi_kernel, dim3(grid_for_warps(a.M * (a.qh + a.kvh))), dim3(256), 0, st, pdl, a);
 }
 
-cudaError_t g4b_post_attn(const GemmOut& o, const float* h_in, float* h_out, const uint16_t* w_pa,
-                          const uint16_t* w_pf, int d, void* bfrag, int M, cudaStream_t st, bool pdl) {
-    const int th = 512;
-    return launch(post_attn_kernel, dim3(M), dim3(th), row_smem(d, th), st, pdl, o, h_in, h_out, w_pa, w_pf, d,
-                  bfrag, M);
+int g4b_rowepi_chunks(int d) { return ((d + 127) / 128 * 128 + kEpiCols - 1) / kEpiCols; }
+
+cudaError_t g4b_rowepi(const GemmOut& o, const float* h_in, float* h_out, const uint16_t* w1, float out_scale,
+                       const uint16_t* w2, int d, float* y_buf, float4* stats, void* bfrag, int M, cudaStream_t st,
+                       bool pdl) {
+    const dim3 grid(g4b_rowepi_chunks(d), M);
+    cudaError_t e = launch(rowepi_phase1_kernel, grid, dim3(kEpiWarps * 32), 0, st, pdl, o, h_in, w1, d, y_buf, stats);
+    if (e != cudaSuccess) return e;
+    return launch(rowepi_phase2_kernel, grid, dim3(kEpiWarps * 32), 0, st, pdl, (const float*)y_buf,
+                  (const float4*)stats, h_in, h_out, w1, w2, out_scale, d, bfrag, M);
 }
 
 cudaError_t g4b_geglu(const GemmOut& gu, int F, void* bfrag, int M, cudaStream_t st, bool pdl) {
     const int ng = (F + 127) / 128 * 2;
     return launch(geglu_kernel, dim3(grid_for_warps(M * ng)), dim3(256), 0, st, pdl, gu, F, bfrag, M);
-}
-
-cudaError_t g4b_post_ffn(const GemmOut& dn, const float* h_in, float* h_out, const uint16_t* w_pffn,
-                         float layer_scalar, const uint16_t* w_next, int d, void* bfrag, int M, cudaStream_t st,
-                         bool pdl) {
-    const int th = 512;
-    return launch(post_ffn_kernel, dim3(M), dim3(th), row_smem(d, th), st, pdl, dn, h_in, h_out, w_pffn,
-                  layer_scalar, w_next, d, bfrag, M);
 }

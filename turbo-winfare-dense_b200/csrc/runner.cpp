@@ -104,9 +104,17 @@ std::vector<uint32_t> Engine::generate(const std::vector<uint32_t>& prompt, cons
 
     std::vector<uint32_t> out;
     std::vector<float> logits;
+    const uint64_t l0 = T.launches() + (draft_ ? draft_->model().launches() : 0);
+    const uint64_t h0 = T.h2d_bytes() + (draft_ ? draft_->model().h2d_bytes() : 0);
+    const uint64_t d0 = T.d2h_bytes() + (draft_ ? draft_->model().d2h_bytes() : 0);
     const uint32_t first = prefill(history, opt, &logits);
+    stats_.h2d_bytes += history.size() * sizeof(uint32_t);
     stats_.ttft_ms = now_ms() - t0;
     const double t_decode = now_ms();
+    cudaEvent_t ev0 = nullptr, ev1 = nullptr;
+    cuda_check(cudaEventCreate(&ev0), "event");
+    cuda_check(cudaEventCreate(&ev1), "event");
+    cuda_check(cudaEventRecord(ev0, T.stream()), "event");
 
     int emitted = 0;
     auto emit = [&](uint32_t t) -> bool {
@@ -278,9 +286,19 @@ std::vector<uint32_t> Engine::generate(const std::vector<uint32_t>& prompt, cons
             }
         }
     }
+    cuda_check(cudaEventRecord(ev1, T.stream()), "event");
+    cuda_check(cudaEventSynchronize(ev1), "event");
+    float dms = 0.f;
+    cuda_check(cudaEventElapsedTime(&dms, ev0, ev1), "event");
+    cudaEventDestroy(ev0);
+    cudaEventDestroy(ev1);
+    stats_.decode_gpu_ms = dms;
     T.check_device_error();
     stats_.total_ms = now_ms() - t0;
     stats_.decode_ms = now_ms() - t_decode;
+    stats_.launches = T.launches() + (draft_ ? draft_->model().launches() : 0) - l0;
+    stats_.h2d_bytes += T.h2d_bytes() + (draft_ ? draft_->model().h2d_bytes() : 0) - h0;
+    stats_.d2h_bytes += T.d2h_bytes() + (draft_ ? draft_->model().d2h_bytes() : 0) - d0 + out.size() * sizeof(uint32_t);
     return out;
 }
 

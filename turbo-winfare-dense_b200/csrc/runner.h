@@ -39,6 +39,9 @@ struct GenerationOptions {
 struct GenStats {
     uint64_t drafted{0}, accepted{0}, rounds{0}, gated_steps{0}, emitted{0};
     double ttft_ms{0}, total_ms{0}, decode_ms{0}, draft_ms{0}, verify_ms{0};
+    double decode_gpu_ms{0};        // device time from the end of prefill to the last token (CUDA events)
+    uint64_t launches{0};           // kernels enqueued by this generation (target + drafter)
+    uint64_t h2d_bytes{0}, d2h_bytes{0};  // host<->device copies of this generation
     bool gated{false};
     std::vector<int> round_info;  // (drafted, accepted, emitted) per verify round
     int stop_reason{0};           // 0 max_tokens, 1 stop token, 2 callback, 3 cancelled

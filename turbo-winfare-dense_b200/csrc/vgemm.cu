@@ -189,6 +189,8 @@ __global__ void __launch_bounds__(kThreads, NACC == 2 ? 2 : 3) vgemm_kernel(Vgem
 
     Cursor cur{u_begin, u_begin / ktiles, u_begin % ktiles};
     Cursor pre = cur;  // the unit kStages ahead of `cur`
+    // Let the next kernel launch now; its CTAs run only their own prologue until they wait.
+    pdl_launch_dependents();
     // Weight prefetch does not depend on the previous kernel: issue it before the wait.
     for (int i = 0; i < kStages; ++i) {
         if (i < n_units && lane == 0 && active(pre)) issue_w(pre, i);
@@ -318,7 +320,7 @@ static cudaError_t launch_t(const VgemmParams& p, cudaStream_t st, bool pdl) {
 }
 
 __global__ void vgemm_reduce_kernel(PartView v, int M, int N, float* out, int ldo) {
-    pdl_wait();
+    pdl_enter();
     const int n4 = (N + 3) / 4;
     for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < M * n4; i += gridDim.x * blockDim.x) {
         const int m = i / n4, n = (i % n4) * 4;

@@ -53,13 +53,23 @@ __device__ __forceinline__ int vgemm_nslots(const PartView& v, int crg) {
     const int hi = vgemm_cta_of_unit((long long)(crg + 1) * v.ktiles - 1, T, v.grid);
     return hi - lo + 1;
 }
-// Sum of slots for output (m, n), fixed slot order (deterministic).
+// Sum of slots for output (m, n), fixed slot order (deterministic). Loads are issued eight
+// at a time before they are added, so a long slot list costs a few memory round trips
+// rather than one per slot.
 __device__ __forceinline__ float vgemm_part_get(const PartView& v, int m, int n) {
     const int crg = n >> 8, nl = n & 255;
     const int ns = vgemm_nslots(v, crg);
     const float* p = v.part + ((size_t)crg * v.max_slots * 16 + m) * 256 + nl;
     float s = 0.f;
-    for (int i = 0; i < ns; ++i) s += __ldcg(p + (size_t)i * 16 * 256);
+    int i = 0;
+    for (; i + 8 <= ns; i += 8) {
+        float t[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) t[j] = __ldcg(p + (size_t)(i + j) * 16 * 256);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s += t[j];
+    }
+    for (; i < ns; ++i) s += __ldcg(p + (size_t)i * 16 * 256);
     return s;
 }
 // Four consecutive outputs n..n+3 (n % 4 == 0).
@@ -68,7 +78,17 @@ __device__ __forceinline__ float4 vgemm_part_get4(const PartView& v, int m, int 
     const int ns = vgemm_nslots(v, crg);
     const float4* p = reinterpret_cast<const float4*>(v.part + ((size_t)crg * v.max_slots * 16 + m) * 256 + nl);
     float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int i = 0; i < ns; ++i) {
+    int i = 0;
+    for (; i + 8 <= ns; i += 8) {
+        float4 t[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) t[j] = __ldcg(p + (size_t)(i + j) * 16 * 64);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            s.x += t[j].x; s.y += t[j].y; s.z += t[j].z; s.w += t[j].w;
+        }
+    }
+    for (; i < ns; ++i) {
         const float4 t = __ldcg(p + (size_t)i * 16 * 64);
         s.x += t.x; s.y += t.y; s.z += t.z; s.w += t.w;
     }

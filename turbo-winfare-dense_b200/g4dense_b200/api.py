@@ -77,6 +77,13 @@ def _bind_engine(L):
     L.g4dense_engine_switch_tier.argtypes = [_vp, ctypes.c_int]
     L.g4dense_engine_stop.argtypes = [_vp]
     L.g4dense_nccl_unique_id.argtypes = [_vp]
+    L.g4dense_engine_last_stats.argtypes = [_vp, _vp, ctypes.c_int]
+    L.g4dense_engine_set_gate.argtypes = [_vp, ctypes.c_double, ctypes.c_int]
+    L.g4dense_engine_time_pass.restype = ctypes.c_double
+    L.g4dense_engine_time_pass.argtypes = [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int]
+    L.g4dense_engine_profile_gemms.restype = ctypes.c_double
+    L.g4dense_engine_profile_gemms.argtypes = [_vp, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_ulonglong),
+                                               ctypes.POINTER(ctypes.c_int)]
 
 
 def _check(rc, what):
@@ -229,6 +236,32 @@ class Engine:
         if rc:
             _eng_err("g4dense_engine_forward_batch")
         return out
+
+    STAT_KEYS = ("emitted", "decode_gpu_ms", "ttft_ms", "total_ms", "drafted", "accepted", "rounds",
+                 "gated_steps", "launches", "h2d_bytes", "d2h_bytes", "decode_wall_ms")
+
+    def stats(self):
+        buf = np.zeros(len(self.STAT_KEYS), np.float64)
+        n = lib().g4dense_engine_last_stats(self.h, buf.ctypes.data_as(_vp), len(buf))
+        return dict(zip(self.STAT_KEYS[:n], buf[:n].tolist()))
+
+    def set_gate(self, min_accept=0.45, window=24):
+        if lib().g4dense_engine_set_gate(self.h, min_accept, window):
+            _eng_err("g4dense_engine_set_gate")
+
+    def time_pass(self, which, batch, reps=5):
+        ms = lib().g4dense_engine_time_pass(self.h, which, batch, reps)
+        if ms < 0:
+            _eng_err("g4dense_engine_time_pass")
+        return ms
+
+    def profile_gemms(self, batch, reps=3):
+        b = ctypes.c_ulonglong(0)
+        n = ctypes.c_int(0)
+        ms = lib().g4dense_engine_profile_gemms(self.h, batch, reps, ctypes.byref(b), ctypes.byref(n))
+        if ms < 0:
+            _eng_err("g4dense_engine_profile_gemms")
+        return ms, int(b.value), int(n.value)
 
     def telemetry(self):
         import json
