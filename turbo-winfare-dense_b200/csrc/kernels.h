@@ -27,11 +27,9 @@ cudaError_t g4b_rowepi(const g4b::GemmOut& o, const float* h_in, float* h_out, c
                        bool pdl);
 
 // ---- attention.cu
-// Splits of the key range per KV head chosen for the launch (fixed per captured graph).
-int g4b_attn_nsplit(int kvh, int M, int qh, int hd);
-cudaError_t g4b_attention(const g4b::AttnArgs& a, cudaStream_t st, bool pdl);
-// Combines the splits and writes the attention output [M][qh*hd] as B fragments.
-cudaError_t g4b_attn_combine(const g4b::AttnArgs& a, void* bfrag, cudaStream_t st, bool pdl);
+// Attention of M rows over the KV ring; writes the output [M][qh*hd] as the o-projection's
+// B fragments. One 8-CTA cluster per (KV head, 16 query rows), key splits combined in DSMEM.
+cudaError_t g4b_attention(const g4b::AttnArgs& a, void* bfrag, cudaStream_t st, bool pdl);
 
 // ---- head.cu
 struct HeadResult {

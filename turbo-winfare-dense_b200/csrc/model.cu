@@ -386,15 +386,13 @@ void DeviceModel::finalize_load() {
 
 void DeviceModel::init_buffers() {
     const int d = h_.d_model;
-    int max_attn_k = 0, max_F = 0, max_q = 0, max_hd = 0, max_qh = 0;
+    int max_attn_k = 0, max_F = 0, max_q = 0;
     size_t part = 0;
     auto consider = [&](const QW& q) { part = std::max(part, (size_t)q.n_crg * q.max_slots * kMaxM * 256); };
     for (auto& L : layers_) {
         max_attn_k = std::max(max_attn_k, L.qh * L.hd);
         max_F = std::max(max_F, L.F);
         max_q = std::max(max_q, L.qh * L.hd);
-        max_hd = std::max(max_hd, L.hd);
-        max_qh = std::max(max_qh, L.qh);
         consider(L.qkv);
         consider(L.o);
         consider(L.gateup);
@@ -408,9 +406,6 @@ void DeviceModel::init_buffers() {
     bf_ff_ = dmalloc(bfrag_capacity(round_up(max_F, 128)));
     part_ = static_cast<float*>(dmalloc(part * 4));
     q_buf_ = static_cast<float*>(dmalloc((size_t)kMaxM * max_q * 4));
-    attn_part_floats_ = (size_t)64 * kMaxM * max_qh * max_hd;
-    o_part_ = static_cast<float*>(dmalloc(attn_part_floats_ * 4));
-    ml_part_ = static_cast<float2*>(dmalloc((size_t)64 * kMaxM * max_qh * sizeof(float2)));
     y_ = static_cast<float*>(dmalloc((size_t)kMaxM * std::max(d, 2 * max_F) * 4));
     ybuf_ = static_cast<float*>(dmalloc((size_t)kMaxM * d * 4));
     stats_ = static_cast<float4*>(dmalloc((size_t)kMaxM * g4b_rowepi_chunks(d) * sizeof(float4)));
@@ -436,9 +431,9 @@ uint64_t DeviceModel::pass_weight_bytes() const { return weight_bytes_; }
 
 int DeviceModel::kernels_per_pass(int M) const {
     (void)M;
-    // embed_norm; per layer 4 GEMMs + qkv_epi + attention + combine + 2x2 norm/residual
-    // phases + geglu (+ 2 slot reductions under TP); LM head GEMM + head_chunks + finalize
-    const int per_layer = 12 + (opt_.tp > 1 ? 2 : 0);
+    // embed_norm; per layer 4 GEMMs + qkv_epi + attention + 2x2 norm/residual phases +
+    // geglu (+ 2 slot reductions under TP); LM head GEMM + head_chunks + finalize
+    const int per_layer = 11 + (opt_.tp > 1 ? 2 : 0);
     return 1 + per_layer * (int)layers_.size() + 3;
 }
 
@@ -552,11 +547,7 @@ void DeviceModel::enqueue_raw(int M, PassKind kind, bool want_logits, uint32_t* 
         aa.window = L.geo.is_global ? 0 : (int)h_.sliding_window;
         aa.kv_bf16 = opt_.kv_bf16;
         aa.scale = 1.0f;
-        aa.nsplit = g4b_attn_nsplit(L.kvh, M, L.qh, L.hd);
-        aa.o_part = o_part_;
-        aa.ml_part = ml_part_;
-        cuda_check(g4b_attention(aa, stream_, pdl), "attention");
-        cuda_check(g4b_attn_combine(aa, bf_attn_, stream_, pdl), "attn_combine");
+        cuda_check(g4b_attention(aa, bf_attn_, stream_, pdl), "attention");
         // o projection + post-attention norm / residual + pre-FFN norm
         gemm(L.o, bf_attn_, M);
         GemmOut oo{};

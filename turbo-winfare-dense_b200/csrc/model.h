@@ -133,9 +133,6 @@ class DeviceModel {
     float* part_ = nullptr;
     size_t part_floats_ = 0;
     float* q_buf_ = nullptr;
-    float* o_part_ = nullptr;
-    float2* ml_part_ = nullptr;
-    size_t attn_part_floats_ = 0;
     float* y_ = nullptr;  // all-reduce staging [16][max(d, ...)]
     float* ybuf_ = nullptr;    // norm/residual epilogue scratch [16][d]
     float4* stats_ = nullptr;  // [16][chunks]

@@ -28,6 +28,30 @@ struct GemmOut {
 __device__ __forceinline__ float gemm_out_get(const GemmOut& o, int m, int n) {
     return o.part.part ? vgemm_part_get(o.part, m, n) : o.y[(size_t)m * o.ld + n];
 }
+// Columns n and n+1 (n even): one slot lookup, 8-byte loads, loads batched across slots.
+__device__ __forceinline__ float2 gemm_out_pair(const GemmOut& o, int m, int n) {
+    if (!o.part.part) return *reinterpret_cast<const float2*>(o.y + (size_t)m * o.ld + n);
+    const SlotRow r = vgemm_slot_row(o.part, m, n >> 8);
+    const float2* p = reinterpret_cast<const float2*>(r.p + (n & 255));
+    float2 s = make_float2(0.f, 0.f);
+    int i = 0;
+    for (; i + 8 <= r.ns; i += 8) {
+        float2 t[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) t[j] = __ldcg(p + (size_t)(i + j) * 2048);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+            s.x += t[j].x;
+            s.y += t[j].y;
+        }
+    }
+    for (; i < r.ns; ++i) {
+        const float2 t = __ldcg(p + (size_t)i * 2048);
+        s.x += t.x;
+        s.y += t.y;
+    }
+    return s;
+}
 #endif
 
 struct QkvEpiArgs {
@@ -52,9 +76,6 @@ struct AttnArgs {
     int M, qh, kvh, hd, cap, window;  // window 0: full attention
     int kv_bf16;
     float scale;
-    int nsplit;
-    float* o_part;           // [nsplit][M*qh][hd] unnormalised
-    float2* ml_part;         // [nsplit][M*qh] {running max, running sum}
 };
 
 }  // namespace g4b

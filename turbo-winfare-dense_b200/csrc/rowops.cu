@@ -111,25 +111,45 @@ __global__ void qkv_epi_kernel(QkvEpiArgs a) {
     const bool is_q = head < a.qh;
     const int kvh = head - a.qh;
     const int row0 = is_q ? head * hd : nq + kvh * hd;
-    float x[kMaxHdPerLane];
-    float ss = 0.f;
+    // A head spans at most two 256-row groups of the GEMM output: look their slots up once.
+    auto load_head = [&](int r0, float* dst) {
+        float ss = 0.f;
+        if (a.qkv.part.part) {
+            const SlotRow s0 = vgemm_slot_row(a.qkv.part, m, r0 >> 8);
+            const SlotRow s1 = vgemm_slot_row(a.qkv.part, m, (r0 + hd - 1) >> 8);
 #pragma unroll
-    for (int j = 0; j < kMaxHdPerLane; ++j)
-        if (j < np) {
-            x[j] = gemm_out_get(a.qkv, m, row0 + lane + 32 * j);
-            ss += x[j] * x[j];
+            for (int j = 0; j < kMaxHdPerLane; ++j)
+                if (j < np) {
+                    const int row = r0 + lane + 32 * j;
+                    dst[j] = vgemm_slot_sum(((row >> 8) == (r0 >> 8)) ? s0 : s1, row & 255);
+                    ss += dst[j] * dst[j];
+                }
+        } else {
+#pragma unroll
+            for (int j = 0; j < kMaxHdPerLane; ++j)
+                if (j < np) {
+                    dst[j] = a.qkv.y[(size_t)m * a.qkv.ld + r0 + lane + 32 * j];
+                    ss += dst[j] * dst[j];
+                }
         }
-    const float r = inv_rms(warp_sum(ss), hd);
+        return ss;
+    };
+    float x[kMaxHdPerLane];
+    const float r = inv_rms(warp_sum(load_head(row0, x)), hd);
     if (!is_q) {
         // V: unweighted norm of v_proj, or of the RAW k on layers without v_proj.
         float v[kMaxHdPerLane];
         float vss = 0.f;
+        if (a.has_v) {
+            vss = load_head(nq + nk + kvh * hd, v);
+        } else {
 #pragma unroll
-        for (int j = 0; j < kMaxHdPerLane; ++j)
-            if (j < np) {
-                v[j] = a.has_v ? gemm_out_get(a.qkv, m, nq + nk + kvh * hd + lane + 32 * j) : x[j];
-                vss += v[j] * v[j];
-            }
+            for (int j = 0; j < kMaxHdPerLane; ++j)
+                if (j < np) {
+                    v[j] = x[j];
+                    vss += v[j] * v[j];
+                }
+        }
         const float rv = inv_rms(warp_sum(vss), hd);
         uint16_t* vd = a.v_ring + ((size_t)(pos % a.cap) * a.kvh + kvh) * hd;
 #pragma unroll
@@ -186,11 +206,13 @@ __global__ void rowepi_phase1_kernel(GemmOut o, const float* __restrict__ h_in, 
     const int m = blockIdx.y, chunk = blockIdx.x;
     const int c0 = chunk * kEpiCols + warp * 64 + 2 * lane;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float2 y2 = make_float2(0.f, 0.f);
+    if (c0 < d) y2 = gemm_out_pair(o, m, c0);
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
         const int c = c0 + j;
         if (c < d) {
-            const float y = gemm_out_get(o, m, c);
+            const float y = j ? y2.y : y2.x;
             const float h = h_in[(size_t)m * d + c];
             const float cc = y * bf16_to_f32(w1[c]);
             y_buf[(size_t)m * d + c] = y;
@@ -276,8 +298,11 @@ __global__ void geglu_kernel(GemmOut gu, int F, void* bfrag, int M) {
         const int m = w / ng, gi = w % ng;
         const int k = gi * 64 + 2 * lane;
         float x0 = 0.f, x1 = 0.f;
-        if (k < F) x0 = gelu_tanh_dev(gemm_out_get(gu, m, k)) * gemm_out_get(gu, m, F + k);
-        if (k + 1 < F) x1 = gelu_tanh_dev(gemm_out_get(gu, m, k + 1)) * gemm_out_get(gu, m, F + k + 1);
+        if (k < F) {
+            const float2 g = gemm_out_pair(gu, m, k), u = gemm_out_pair(gu, m, F + k);
+            x0 = gelu_tanh_dev(g.x) * u.x;
+            x1 = gelu_tanh_dev(g.y) * u.y;
+        }
         bfrag_store_group(v, M, m, gi, x0, x1, stage[wib]);
     }
 }
@@ -325,7 +350,9 @@ cudaError_t g4b_embed_norm(const StepParams* sp, const uint32_t* ew, const uint1
 
 cudaError_t g4b_qkv_epi(const QkvEpiArgs& a, cudaStream_t st, bool pdl) {
     if (a.hd % 64 || a.hd > 32 * kMaxHdPerLane || a.rotated > a.hd / 2) return cudaErrorInvalidValue;
-    return launch(qkv_epi_kernel, dim3(grid_for_warps(a.M * (a.qh + a.kvh))), dim3(256), 0, st, pdl, a);
+    // Two warps per block: the heads spread over as many SMs as possible.
+    const int warps = a.M * (a.qh + a.kvh);
+    return launch(qkv_epi_kernel, dim3((warps + 1) / 2), dim3(64), 0, st, pdl, a);
 }
 
 int g4b_rowepi_chunks(int d) { return ((d + 127) / 128 * 128 + kEpiCols - 1) / kEpiCols; }

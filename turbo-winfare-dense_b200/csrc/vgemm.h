@@ -47,11 +47,40 @@ cudaError_t vgemm_reduce(const PartView& v, int M, int N, float* out, int ldo, c
 __device__ __forceinline__ int vgemm_cta_of_unit(long long x, long long T, long long G) {
     return (int)(((x + 1) * G + T - 1) / T - 1);
 }
+// Same formula in 32-bit arithmetic: (x+1)*G stays below 2^31 for every launch this library
+// makes (T = row groups x k-tiles < 2^17, G <= 16 x 148 CTAs).
+__device__ __forceinline__ int vgemm_cta_of_unit32(int x, int T, int G) { return ((x + 1) * G + T - 1) / T - 1; }
 __device__ __forceinline__ int vgemm_nslots(const PartView& v, int crg) {
-    const long long T = (long long)v.n_crg * v.ktiles;
-    const int lo = vgemm_cta_of_unit((long long)crg * v.ktiles, T, v.grid);
-    const int hi = vgemm_cta_of_unit((long long)(crg + 1) * v.ktiles - 1, T, v.grid);
+    const int T = v.n_crg * v.ktiles;
+    const int lo = vgemm_cta_of_unit32(crg * v.ktiles, T, v.grid);
+    const int hi = vgemm_cta_of_unit32((crg + 1) * v.ktiles - 1, T, v.grid);
     return hi - lo + 1;
+}
+// Slot 0 of row m in CTA row group crg, and the slot count; slot s of column nl is at
+// p[s * 4096 + nl].
+struct SlotRow {
+    const float* p;
+    int ns;
+};
+__device__ __forceinline__ SlotRow vgemm_slot_row(const PartView& v, int m, int crg) {
+    SlotRow r;
+    r.p = v.part + ((size_t)crg * v.max_slots * 16 + m) * 256;
+    r.ns = vgemm_nslots(v, crg);
+    return r;
+}
+__device__ __forceinline__ float vgemm_slot_sum(const SlotRow& r, int nl) {
+    const float* p = r.p + nl;
+    float s = 0.f;
+    int i = 0;
+    for (; i + 8 <= r.ns; i += 8) {
+        float t[8];
+#pragma unroll
+        for (int j = 0; j < 8; ++j) t[j] = __ldcg(p + (size_t)(i + j) * 4096);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) s += t[j];
+    }
+    for (; i < r.ns; ++i) s += __ldcg(p + (size_t)i * 4096);
+    return s;
 }
 // Sum of slots for output (m, n), fixed slot order (deterministic). Loads are issued eight
 // at a time before they are added, so a long slot list costs a few memory round trips
