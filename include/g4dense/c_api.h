@@ -125,9 +125,11 @@ G4DENSE_API int g4dense_engine_last_stats(void* handle, double* out, int n);
  * drafts have been made and fewer than min_accept of them were accepted; window < 0 disables
  * it. Defaults 0.45 / 24. */
 G4DENSE_API int g4dense_engine_set_gate(void* handle, double min_accept, int window);
-/* Device time (CUDA events) of one forward pass of `batch` rows on the target (which = 0) or
- * the drafter (which = 1), averaged over `reps` back-to-back graph replays; -1 on error. */
-G4DENSE_API double g4dense_engine_time_pass(void* handle, int which, int batch, int reps);
+/* Device time (CUDA events) of one forward pass of `batch` rows at positions pos..pos+batch-1
+ * on the target (which = 0) or the drafter (which = 1), averaged over `reps` back-to-back graph
+ * replays; attention spans the pos earlier cache entries. Overwrites those rows of the KV
+ * cache. -1 on error. */
+G4DENSE_API double g4dense_engine_time_pass(void* handle, int which, int batch, int pos, int reps);
 /* Times every verify GEMM of one `batch`-row target pass, `reps` passes back to back, with
  * CUDA events; returns ms per pass (-1 on error), the pass's algorithmic GEMM bytes and the
  * GEMM launches per pass. A measurement hook for the verify-GEMM bandwidth metric. */

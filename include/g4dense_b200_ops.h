@@ -37,7 +37,8 @@ G4B_API int g4b_qmat_gemm(g4b_qmat* q, const float* x, int ldx, int M, float* ou
 /* The two halves of g4b_qmat_gemm, for timing the GEMM kernel alone. */
 G4B_API int g4b_qmat_prepare_input(g4b_qmat* q, const float* x, int ldx, int M, void* stream);
 G4B_API int g4b_qmat_run(g4b_qmat* q, int M, float* out, int ldo, void* stream);
-/* The GEMM kernel alone, leaving split-K partials in the matrix's workspace (for timing). */
+/* The GEMM kernel without its in-kernel split-K sum, leaving the partials in the matrix's
+ * workspace (for timing the weight stream alone). */
 G4B_API int g4b_qmat_run_partial(g4b_qmat* q, int M, void* stream);
 /* Synchronizes and reports whether any launch on q hit a bounded-wait timeout. */
 G4B_API int g4b_qmat_check_error(g4b_qmat* q);

@@ -40,9 +40,10 @@ def check_logits(got, ref, where):
     srt = np.sort(ref)[::-1]
     if srt[0] - srt[1] >= tie:
         assert int(np.argmax(got)) == int(np.argmax(ref)), where
-        top = np.argsort(-ref, kind="stable")[:5]
+        # Top-5 order, where every gap down to the 6th logit exceeds the noise bar.
+        top = np.argsort(-ref, kind="stable")[:6]
         if np.all(np.diff(ref[top]) <= -tie):
-            assert list(np.argsort(-got, kind="stable")[:5]) == list(top), where
+            assert list(np.argsort(-got, kind="stable")[:5]) == list(top[:5]), where
 
 
 @pytest.mark.parametrize("variant", ["target", "target_centered"])
@@ -58,6 +59,42 @@ def test_forward_batch_matches_oracle(built_lib, config0, variant):
         for i in range(m):
             check_logits(got[i], want[pos + i], f"{variant} position {pos + i} (batch {m})")
         pos += m
+    e.close()
+
+
+def test_bf16_kv_mode_matches_oracle(built_lib, config0):
+    """Long-context mode: K/V rounded through bf16 (the oracle's BF16 KV mode); the attention
+    kernel then runs its bf16 tensor-core variant."""
+    path = config0["target"]
+    e = engine(path, kv_bf16=True)
+    ref = O.RestatedModel(path, kv_mode=O.KV_BF16)
+    toks = np.random.default_rng(13).integers(0, 4096, 24)
+    want = [ref.forward(int(t), p) for p, t in enumerate(toks)]
+    pos = 0
+    for m in [16, 1, 7]:
+        got = e.forward_batch(toks[pos:pos + m], pos, vocab=4096, all_positions=True)
+        for i in range(m):
+            check_logits(got[i], want[pos + i], f"bf16 KV position {pos + i} (batch {m})")
+        pos += m
+    e.close()
+
+
+@pytest.mark.parametrize("variant", ["baseline", "centered"])
+def test_31b_attention_geometry_matches_oracle(built_lib, geom31, variant):
+    """head_dim 256 / 512, GQA 2 and 4, a sliding window shorter than the context (ring wrap)
+    and a full-attention layer long enough that every key split spans several tiles."""
+    path = geom31[variant]
+    e = engine(path, max_context=512)
+    ref = O.RestatedModel(path, max_ctx=512)
+    toks = np.random.default_rng(14).integers(0, 4096, 330)
+    want = [ref.forward(int(t), p) for p, t in enumerate(toks)]
+    pos = 0
+    for m in [16] * 18 + [5, 1, 9, 16, 11]:
+        got = e.forward_batch(toks[pos:pos + m], pos, vocab=4096, all_positions=True)
+        for i in range(m):
+            check_logits(got[i], want[pos + i], f"{variant} position {pos + i} (batch {m})")
+        pos += m
+    assert pos == len(toks)
     e.close()
 
 

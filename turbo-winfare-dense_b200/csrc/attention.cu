@@ -3,13 +3,18 @@
 // head's query heads (the reference dispatches one group per (row, query head), re-reading
 // the cache M * q_heads/kv_heads times).
 //
-// Grid: one thread-block cluster of kSplits CTAs per (KV head, chunk of 16 query rows); CTA
-// r of the cluster takes the r-th share of the batch's key range. Each CTA streams 32-key
-// tiles of K and V into shared memory (cp.async, double-buffered), each warp owns two query
-// rows, scores are fp32 dot products of the fp32 query with the rounded K, and an online
-// softmax (running max / sum) accumulates the unnormalised output. The cluster's partial
-// results are then combined through distributed shared memory -- no global round trip --
-// and written directly as the o-projection's B fragments.
+// Grid: one thread-block cluster of kSplits CTAs per (KV head, chunk of 16 query rows); CTA r
+// of the cluster takes the r-th share of the batch's key range. Per 32-key tile (K and V
+// double-buffered in shared memory by cp.async):
+//   * S = Q K^T on the tensor cores (mma.sync m16n8k16, fp32 accumulate). The cached K is
+//     exact in the MMA's input type (FP16, or bf16 in long-context mode); the fp32 query is
+//     split into 2 (FP16) or 3 (bf16) terms q = q1 + q2 (+ q3) after a power-of-two row
+//     scaling, so the scores carry the fp32 query's precision. Warp w computes keys 8w..8w+7;
+//   * an online softmax per row (running max / sum in fp32, exp of the fp32 scores);
+//   * O += P V on the tensor cores with P (scaled by 2^14) split the same way; warp w owns
+//     columns [w*hd/4, (w+1)*hd/4) of the output.
+// The cluster's partial results are then combined through distributed shared memory and
+// written directly as the o-projection's B fragments.
 //
 // Row m of the batch sits at position base+m and sees keys [max(0, base+m+1-window),
 // base+m+1) (all keys from 0 on full-attention layers): the reference's per-row causal span
@@ -20,7 +25,6 @@
 #include "bfrag.cuh"
 #include "common.cuh"
 #include "kernels.h"
-#include "launch.cuh"
 #include "model_dev.h"
 
 #include <algorithm>
@@ -29,71 +33,120 @@ namespace cg = cooperative_groups;
 
 namespace g4b {
 
-constexpr int kAttnKeys = 32;    // keys per tile (one per lane)
-constexpr int kAttnRows = 16;    // query rows per CTA (two per warp)
-constexpr int kAttnThreads = 256;
-constexpr int kSplits = 8;       // CTAs per cluster = key splits
+constexpr int kAttnKeys = 32;  // keys per tile
+constexpr int kAttnRows = 16;  // query rows per CTA (the MMA's M)
+constexpr int kAttnWarps = 4;
+constexpr int kAttnThreads = kAttnWarps * 32;
+constexpr int kSplits = 8;               // CTAs per cluster = key splits
+constexpr int kPStride = kAttnKeys + 8;  // halves per P row (conflict-free ldmatrix)
+constexpr int kSStride = kAttnKeys + 4;  // floats per S row
+constexpr float kPScale = 16384.0f;      // P is split after scaling by 2^14
 
-__device__ __forceinline__ float2 kv_pair(uint32_t bits2, int bf16) {
-    if (bf16) return make_float2(__uint_as_float(bits2 << 16), __uint_as_float(bits2 & 0xFFFF0000u));
-    return __half22float2(*reinterpret_cast<const __half2*>(&bits2));
+template <bool BF16>
+struct AttnTypes;
+template <>
+struct AttnTypes<false> {
+    static constexpr int kTerms = 2;
+    static __device__ __forceinline__ uint16_t to_bits(float x) { return __half_as_ushort(__float2half_rn(x)); }
+    static __device__ __forceinline__ float from_bits(uint16_t b) { return __half2float(__ushort_as_half(b)); }
+};
+template <>
+struct AttnTypes<true> {
+    static constexpr int kTerms = 3;
+    static __device__ __forceinline__ uint16_t to_bits(float x) {
+        return __bfloat16_as_ushort(__float2bfloat16_rn(x));
+    }
+    static __device__ __forceinline__ float from_bits(uint16_t b) { return __uint_as_float((uint32_t)b << 16); }
+};
+
+template <bool BF16>
+__device__ __forceinline__ void mma_tc(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
+    if constexpr (BF16) {
+        asm("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    } else {
+        asm("mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+            "{%0,%1,%2,%3};"
+            : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+            : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
+    }
 }
 
+__device__ __forceinline__ void ldsm_x4(uint32_t (&r)[4], const void* p) {
+    const uint32_t s = (uint32_t)__cvta_generic_to_shared(p);
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(s));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
+    const uint32_t s = (uint32_t)__cvta_generic_to_shared(p);
+    asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+                 : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
+                 : "r"(s));
+}
 __device__ __forceinline__ void cp16(void* smem, const void* gmem) {
     const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem));
 }
 
+// Shared memory plan (KS = hd + 8 halves per Q/K/V row: conflict-free ldmatrix rows).
 struct AttnSmem {
-    float* q;        // [16][hd]; reused for this CTA's partial output after the key loop
-    uint16_t* k[2];  // [32][hd + 8]
-    uint16_t* v[2];  // [32][hd]
-    float* p;        // [16][32]
-    float2* ml;      // [16] running {max, sum}
+    uint16_t* q;     // [terms][16][KS]
+    uint16_t* kv;    // 2 buffers x {K [32][KS], V [32][KS]}
+    uint16_t* p;     // [terms][16][kPStride]
+    float* s;        // [16][kSStride]
+    float* corr;     // [16]
+    float* qscale;   // [16] 2^-e of the row's query scaling
+    float2* ml;      // [16] {running max, running sum}
+    float* o;        // [16][hd] partial output after the key loop (aliases the K/V tiles)
 };
 
-__device__ __forceinline__ AttnSmem attn_smem(unsigned char* raw, int hd) {
+inline size_t attn_smem_bytes(int hd, int terms) {
+    const size_t ks = hd + 8;
+    return (size_t)terms * kAttnRows * ks * 2 + 4 * (size_t)kAttnKeys * ks * 2 +
+           (size_t)terms * kAttnRows * kPStride * 2 + kAttnRows * kSStride * 4 + kAttnRows * 4 * 2 + kAttnRows * 8;
+}
+
+__device__ __forceinline__ AttnSmem attn_smem(unsigned char* raw, int hd, int terms) {
     AttnSmem s;
-    s.q = reinterpret_cast<float*>(raw);
-    uint16_t* kv = reinterpret_cast<uint16_t*>(s.q + kAttnRows * hd);
-    const int ktile = kAttnKeys * (hd + 8), vtile = kAttnKeys * hd;
-    s.k[0] = kv;
-    s.v[0] = kv + ktile;
-    s.k[1] = kv + ktile + vtile;
-    s.v[1] = kv + 2 * ktile + vtile;
-    s.p = reinterpret_cast<float*>(kv + 2 * (ktile + vtile));
-    s.ml = reinterpret_cast<float2*>(s.p + kAttnRows * kAttnKeys);
+    const int ks = hd + 8;
+    uint16_t* h = reinterpret_cast<uint16_t*>(raw);
+    s.q = h;
+    h += terms * kAttnRows * ks;
+    s.kv = h;
+    s.o = reinterpret_cast<float*>(h);  // 16 * hd * 4 bytes <= 4 * 32 * ks * 2
+    h += 4 * kAttnKeys * ks;
+    s.p = h;
+    h += terms * kAttnRows * kPStride;
+    s.s = reinterpret_cast<float*>(h);
+    s.corr = s.s + kAttnRows * kSStride;
+    s.qscale = s.corr + kAttnRows;
+    s.ml = reinterpret_cast<float2*>(s.qscale + kAttnRows);
     return s;
 }
 
+template <bool BF16, int HD>
 __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnArgs a, void* bfrag) {
+    using Ty = AttnTypes<BF16>;
+    constexpr int kTerms = Ty::kTerms;
+    constexpr int KS = HD + 8;
+    constexpr int kColsPerWarp = HD / kAttnWarps;  // PV output columns per warp
+    constexpr int kNT = kColsPerWarp / 8;          // PV n-tiles per warp
     extern __shared__ __align__(16) unsigned char smem_raw[];
-    __shared__ __half stage[kAttnThreads / 32][128];
+    __shared__ __half stage[kAttnWarps][128];
     cg::cluster_group cluster = cg::this_cluster();
-    const int hd = a.hd;
-    const int kstride = hd + 8;
-    AttnSmem sm = attn_smem(smem_raw, hd);
+    AttnSmem sm = attn_smem(smem_raw, HD, kTerms);
 
     pdl_enter();
     const int split = (int)cluster.block_rank();
     const int kvh_i = blockIdx.y, chunk = blockIdx.z;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+    const int g = lane >> 2, t4 = lane & 3;
     const int gqa = a.qh / a.kvh;
     const int R = a.M * gqa;
     const int base = a.sp->base_pos;
-
-    // Stage this chunk's query rows.
-    for (int i = threadIdx.x; i < kAttnRows * hd; i += kAttnThreads) {
-        const int r = i / hd, d = i % hd;
-        const int qr = chunk * kAttnRows + r;
-        float v = 0.f;
-        if (qr < R) {
-            const int m = qr / gqa, qhead = kvh_i * gqa + qr % gqa;
-            v = a.q[((size_t)m * a.qh + qhead) * hd + d];
-        }
-        sm.q[i] = v;
-    }
-    __syncthreads();  // q is complete before any warp reads it or (empty split) overwrites it
 
     // Key range of the whole batch, then this split's share.
     const int kmin = a.window ? max(0, base + 1 - a.window) : 0;
@@ -101,173 +154,229 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnArgs a, voi
     const int per = (kmax - kmin + kSplits - 1) / kSplits;
     const int ks = kmin + split * per, ke = min(kmax, ks + per);
 
-    int row_lo[2], row_hi[2];
-    bool row_ok[2];
-#pragma unroll
-    for (int j = 0; j < 2; ++j) {
-        const int qr = chunk * kAttnRows + warp * 2 + j;
-        row_ok[j] = qr < R;
-        const int end = base + (row_ok[j] ? qr / gqa : 0) + 1;
-        row_hi[j] = min(end, ke);
-        row_lo[j] = max(a.window ? max(0, end - a.window) : 0, ks);
-    }
-    const int npair = hd / 64;  // dim pairs per lane: d = 2*lane + 64*i
-    float o[2][8][2];
-#pragma unroll
-    for (int j = 0; j < 2; ++j)
-#pragma unroll
-        for (int i = 0; i < 8; ++i) o[j][i][0] = o[j][i][1] = 0.f;
-    float m_run[2] = {-INFINITY, -INFINITY}, l_run[2] = {0.f, 0.f};
-
-    const int chunks_per_row = hd / 8;
     auto load_tile = [&](int t0, int buf) {
         const int nt = min(kAttnKeys, ke - t0);
-        for (int i = threadIdx.x; i < kAttnKeys * chunks_per_row; i += kAttnThreads) {
-            const int j = i / chunks_per_row, c8 = i % chunks_per_row;
+        for (int i = threadIdx.x; i < kAttnKeys * (HD / 8); i += kAttnThreads) {
+            const int j = i / (HD / 8), c8 = i % (HD / 8);
+            uint16_t* kd = sm.kv + (2 * buf * kAttnKeys + j) * KS + c8 * 8;
+            uint16_t* vd = kd + kAttnKeys * KS;
             if (j < nt) {
-                const size_t src = ((size_t)((t0 + j) % a.cap) * a.kvh + kvh_i) * hd + c8 * 8;
-                cp16(sm.k[buf] + j * kstride + c8 * 8, a.k_ring + src);
-                cp16(sm.v[buf] + j * hd + c8 * 8, a.v_ring + src);
+                const size_t src = ((size_t)((t0 + j) % a.cap) * a.kvh + kvh_i) * HD + c8 * 8;
+                cp16(kd, a.k_ring + src);
+                cp16(vd, a.v_ring + src);
+            } else {  // keys past the range: zeros, so P = 0 meets finite V
+                *reinterpret_cast<uint4*>(kd) = make_uint4(0, 0, 0, 0);
+                *reinterpret_cast<uint4*>(vd) = make_uint4(0, 0, 0, 0);
             }
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
+    if (ks < ke) load_tile(ks, 0);
+
+    // Stage the query rows: warp w takes rows 4w..4w+3. Scaling by 2^(15-e) puts the row's
+    // max |q| in [2^14, 2^15); the scaled row is then split into terms of the MMA type.
+    for (int rr = 0; rr < 4; ++rr) {
+        const int r = warp * 4 + rr;
+        const int qr = chunk * kAttnRows + r;
+        float x[HD / 32];
+        float amax = 0.f;
+        const float* src = nullptr;
+        if (qr < R) {
+            const int m = qr / gqa, qhead = kvh_i * gqa + qr % gqa;
+            src = a.q + ((size_t)m * a.qh + qhead) * HD;
+        }
+#pragma unroll
+        for (int j = 0; j < HD / 32; ++j) {
+            x[j] = src ? src[lane + 32 * j] : 0.f;
+            amax = fmaxf(amax, fabsf(x[j]));
+        }
+        amax = warp_max(amax);
+        int e = 0;
+        frexpf(amax, &e);
+        const float sc = amax > 0.f ? ldexpf(1.0f, 15 - e) : 1.0f;
+        if (lane == 0) sm.qscale[r] = amax > 0.f ? ldexpf(1.0f, e - 15) : 1.0f;
+#pragma unroll
+        for (int j = 0; j < HD / 32; ++j) {
+            float rem = x[j] * sc;
+#pragma unroll
+            for (int tt = 0; tt < kTerms; ++tt) {
+                const uint16_t b = Ty::to_bits(rem);
+                sm.q[(tt * kAttnRows + r) * KS + lane + 32 * j] = b;
+                rem -= Ty::from_bits(b);
+            }
+        }
+    }
+    // Softmax state: warp w owns rows 4w..4w+3 (every lane keeps the same copy).
+    float m_run[4], l_run[4];
+    int row_lo[4], row_hi[4];
+#pragma unroll
+    for (int rr = 0; rr < 4; ++rr) {
+        m_run[rr] = -INFINITY;
+        l_run[rr] = 0.f;
+        const int qr = chunk * kAttnRows + warp * 4 + rr;
+        if (qr < R) {
+            const int end = base + qr / gqa + 1;
+            row_hi[rr] = end;
+            row_lo[rr] = a.window ? max(0, end - a.window) : 0;
+        } else {
+            row_hi[rr] = row_lo[rr] = 0;  // empty span: the row stays masked
+        }
+    }
+    float acc[kNT][4];
+#pragma unroll
+    for (int n = 0; n < kNT; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
 
     int buf = 0;
-    if (ks < ke) load_tile(ks, 0);
     for (int t0 = ks; t0 < ke; t0 += kAttnKeys, buf ^= 1) {
-        const int nt = min(kAttnKeys, ke - t0);
-        // Prefetch the next tile into the other buffer, then wait for this one.
-        if (t0 + kAttnKeys < ke) {
-            load_tile(t0 + kAttnKeys, buf ^ 1);
-            asm volatile("cp.async.wait_group 1;" ::: "memory");
-        } else {
-            asm volatile("cp.async.wait_group 0;" ::: "memory");
+        asm volatile("cp.async.wait_group 0;" ::: "memory");
+        __syncthreads();  // tile t0 (and the staged q) visible; every warp is past the last PV
+        if (t0 + kAttnKeys < ke) load_tile(t0 + kAttnKeys, buf ^ 1);
+
+        // S[16 rows][keys 8w..8w+7] = sum over terms of Q_t K^T.
+        {
+            float s[4] = {0.f, 0.f, 0.f, 0.f};
+            const uint16_t* kb = sm.kv + (2 * buf * kAttnKeys + warp * 8 + (lane & 7)) * KS + (lane >> 3) * 8;
+            const uint16_t* qb = sm.q + (lane & 15) * KS + (lane >> 4) * 8;
+#pragma unroll 4
+            for (int k0 = 0; k0 < HD; k0 += 32) {
+                uint32_t b[4];
+                ldsm_x4(b, kb + k0);  // k-steps k0 and k0 + 16
+#pragma unroll
+                for (int tt = 0; tt < kTerms; ++tt) {
+                    uint32_t q0[4], q1[4];
+                    ldsm_x4(q0, qb + tt * kAttnRows * KS + k0);
+                    ldsm_x4(q1, qb + tt * kAttnRows * KS + k0 + 16);
+                    mma_tc<BF16>(s, q0, b[0], b[1]);
+                    mma_tc<BF16>(s, q1, b[2], b[3]);
+                }
+            }
+            float* sr = sm.s + g * kSStride + warp * 8 + 2 * t4;
+            sr[0] = s[0];
+            sr[1] = s[1];
+            sr[8 * kSStride] = s[2];
+            sr[8 * kSStride + 1] = s[3];
         }
         __syncthreads();
 
-        // Scores: lane = key, two rows per warp.
-        float s[2] = {0.f, 0.f};
-        const uint16_t* kr = sm.k[buf] + lane * kstride;
-        for (int d = 0; d < hd; d += 8) {
-            const uint4 kb = *reinterpret_cast<const uint4*>(kr + d);
-            const float2 k01 = kv_pair(kb.x, a.kv_bf16), k23 = kv_pair(kb.y, a.kv_bf16);
-            const float2 k45 = kv_pair(kb.z, a.kv_bf16), k67 = kv_pair(kb.w, a.kv_bf16);
+        // Online softmax: lane = key of the tile.
 #pragma unroll
-            for (int j = 0; j < 2; ++j) {
-                const float4 qa = *reinterpret_cast<const float4*>(sm.q + (warp * 2 + j) * hd + d);
-                const float4 qb = *reinterpret_cast<const float4*>(sm.q + (warp * 2 + j) * hd + d + 4);
-                s[j] += qa.x * k01.x + qa.y * k01.y + qa.z * k23.x + qa.w * k23.y + qb.x * k45.x + qb.y * k45.y +
-                        qb.z * k67.x + qb.w * k67.y;
-            }
-        }
-#pragma unroll
-        for (int j = 0; j < 2; ++j) {
-            const int t = t0 + lane;
-            const bool valid = row_ok[j] && lane < nt && t >= row_lo[j] && t < row_hi[j];
-            const float sc = valid ? s[j] * a.scale : -INFINITY;
-            const float mt = warp_max(sc);
-            const float m_new = fmaxf(m_run[j], mt);
+        for (int rr = 0; rr < 4; ++rr) {
+            const int r = warp * 4 + rr;
+            const int tk = t0 + lane;
+            const bool valid = lane < ke - t0 && tk >= row_lo[rr] && tk < row_hi[rr];
+            const float sc = valid ? sm.s[r * kSStride + lane] * sm.qscale[r] * a.scale : -INFINITY;
+            const float m_new = fmaxf(m_run[rr], warp_max(sc));
             float p = 0.f, corr = 1.f;
             if (m_new != -INFINITY) {
                 p = valid ? expf(sc - m_new) : 0.f;
-                corr = expf(m_run[j] - m_new);  // 0 on the first contributing tile
+                corr = expf(m_run[rr] - m_new);  // 0 on the first contributing tile
             }
-            l_run[j] = l_run[j] * corr + warp_sum(p);
-            m_run[j] = m_new;
+            l_run[rr] = l_run[rr] * corr + warp_sum(p);
+            m_run[rr] = m_new;
+            float rem = p * kPScale;
 #pragma unroll
-            for (int i = 0; i < 8; ++i)
-                if (i < npair) {
-                    o[j][i][0] *= corr;
-                    o[j][i][1] *= corr;
-                }
-            sm.p[(warp * 2 + j) * kAttnKeys + lane] = p;
-        }
-        __syncwarp();
-        for (int jk = 0; jk < nt; ++jk) {
-            const float p0 = sm.p[(warp * 2) * kAttnKeys + jk];
-            const float p1 = sm.p[(warp * 2 + 1) * kAttnKeys + jk];
-            const uint32_t* vr = reinterpret_cast<const uint32_t*>(sm.v[buf] + jk * hd);
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-                if (i < npair) {
-                    const float2 v = kv_pair(vr[lane + 32 * i], a.kv_bf16);
-                    o[0][i][0] += p0 * v.x;
-                    o[0][i][1] += p0 * v.y;
-                    o[1][i][0] += p1 * v.x;
-                    o[1][i][1] += p1 * v.y;
-                }
+            for (int tt = 0; tt < kTerms; ++tt) {
+                const uint16_t b = Ty::to_bits(rem);
+                sm.p[(tt * kAttnRows + r) * kPStride + lane] = b;
+                rem -= Ty::from_bits(b);
             }
+            if (lane == 0) sm.corr[r] = corr;
         }
-        __syncthreads();  // the buffer is refilled on the next trip
-    }
+        __syncthreads();
 
-    // Publish this split's partial result in shared memory (the query staging area).
+        // O[16][warp's columns] = O * corr + sum over terms of P_t V.
+        {
+            const float c0 = sm.corr[g], c1 = sm.corr[g + 8];
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-        float* op = sm.q + (warp * 2 + j) * hd;
+            for (int n = 0; n < kNT; ++n) {
+                acc[n][0] *= c0;
+                acc[n][1] *= c0;
+                acc[n][2] *= c1;
+                acc[n][3] *= c1;
+            }
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-            if (i < npair) *reinterpret_cast<float2*>(op + 2 * lane + 64 * i) = make_float2(o[j][i][0], o[j][i][1]);
-        if (lane == 0) sm.ml[warp * 2 + j] = make_float2(m_run[j], l_run[j]);
+            for (int kk = 0; kk < kAttnKeys; kk += 16) {
+                uint32_t pa[kTerms][4];
+#pragma unroll
+                for (int tt = 0; tt < kTerms; ++tt)
+                    ldsm_x4(pa[tt], sm.p + (tt * kAttnRows + (lane & 15)) * kPStride + kk + (lane >> 4) * 8);
+                const uint16_t* vb = sm.kv + ((2 * buf + 1) * kAttnKeys + kk + (lane & 7) + ((lane >> 3) & 1) * 8) * KS +
+                                     warp * kColsPerWarp + (lane >> 4) * 8;
+#pragma unroll
+                for (int n = 0; n < kNT; n += 2) {
+                    uint32_t b[4];
+                    ldsm_x4_t(b, vb + n * 8);  // n-tiles n and n + 1
+#pragma unroll
+                    for (int tt = 0; tt < kTerms; ++tt) {
+                        mma_tc<BF16>(acc[n], pa[tt], b[0], b[1]);
+                        mma_tc<BF16>(acc[n + 1], pa[tt], b[2], b[3]);
+                    }
+                }
+            }
+        }
     }
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    __syncthreads();  // every warp is done with the K/V tiles: sm.o may overwrite them
+
+    // This split's partial result: unnormalised O (P's 2^14 scale removed) and {m, l}.
+#pragma unroll
+    for (int n = 0; n < kNT; ++n) {
+        const int col = warp * kColsPerWarp + n * 8 + 2 * t4;
+        *reinterpret_cast<float2*>(sm.o + g * HD + col) = make_float2(acc[n][0] / kPScale, acc[n][1] / kPScale);
+        *reinterpret_cast<float2*>(sm.o + (g + 8) * HD + col) = make_float2(acc[n][2] / kPScale, acc[n][3] / kPScale);
+    }
+    if (lane == 0)
+#pragma unroll
+        for (int rr = 0; rr < 4; ++rr) sm.ml[warp * 4 + rr] = make_float2(m_run[rr], l_run[rr]);
     cluster.sync();
 
-    // Combine across the cluster: CTA r owns rows 2r, 2r+1 of the chunk; one warp per
-    // (row, 64-column group).
-    const int ngroups = hd / 64;
-    const int K = a.qh * hd;
+    // Combine across the cluster: out = sum_s e^(m_s - M) O_s / sum_s e^(m_s - M) l_s, one warp
+    // per (row, 64-column group), the items spread over the cluster's CTAs.
+    constexpr int kGroups = HD / 64;
+    const int K = a.qh * HD;
     const BFragView bv = bfrag_view(bfrag, (K + 127) / 128 * 128, a.M);
-    for (int w = warp; w < 2 * ngroups; w += kAttnThreads / 32) {
-        const int r = split * 2 + w / ngroups, g = w % ngroups;
+    for (int w = split * kAttnWarps + warp; w < kAttnRows * kGroups; w += kSplits * kAttnWarps) {
+        const int r = w / kGroups, gi = w % kGroups;
         const int qr = chunk * kAttnRows + r;
         if (qr >= R) continue;  // warp-uniform
         float mx = -INFINITY;
-        for (int s = 0; s < kSplits; ++s) {
-            const float2* rml = cluster.map_shared_rank(sm.ml, s);
-            mx = fmaxf(mx, rml[r].x);
-        }
+        for (int s = 0; s < kSplits; ++s) mx = fmaxf(mx, cluster.map_shared_rank(sm.ml, s)[r].x);
         float n0 = 0.f, n1 = 0.f, den = 0.f;
         for (int s = 0; s < kSplits; ++s) {
             const float2 ml = cluster.map_shared_rank(sm.ml, s)[r];
             if (ml.y <= 0.f) continue;
             const float wgt = expf(ml.x - mx);
-            const float2 op = *reinterpret_cast<const float2*>(cluster.map_shared_rank(sm.q, s) + r * hd + g * 64 + 2 * lane);
+            const float2 op =
+                *reinterpret_cast<const float2*>(cluster.map_shared_rank(sm.o, s) + r * HD + gi * 64 + 2 * lane);
             n0 += wgt * op.x;
             n1 += wgt * op.y;
             den += wgt * ml.y;
         }
         const float inv = den > 0.f ? 1.0f / den : 0.f;
         const int m = qr / gqa, qhead = kvh_i * gqa + qr % gqa;
-        bfrag_store_group(bv, a.M, m, (qhead * hd) / 64 + g, n0 * inv, n1 * inv, stage[warp]);
+        bfrag_store_group(bv, a.M, m, (qhead * HD) / 64 + gi, n0 * inv, n1 * inv, stage[warp]);
     }
     // A K that is not a multiple of 128 leaves one pad group per row: zero fragments.
     if ((K & 127) && blockIdx.y == 0 && blockIdx.z == 0 && split == 0)
-        for (int m = warp; m < a.M; m += kAttnThreads / 32) bfrag_store_group(bv, a.M, m, K / 64, 0.f, 0.f, stage[warp]);
+        for (int m = warp; m < a.M; m += kAttnWarps) bfrag_store_group(bv, a.M, m, K / 64, 0.f, 0.f, stage[warp]);
     cluster.sync();  // keep every CTA's shared memory alive until all remote reads are done
 }
 
-static size_t attn_smem_bytes(int hd) {
-    return (size_t)kAttnRows * hd * 4 + 2 * ((size_t)kAttnKeys * (hd + 8) * 2 + (size_t)kAttnKeys * hd * 2) +
-           kAttnRows * kAttnKeys * 4 + kAttnRows * sizeof(float2);
-}
-
-}  // namespace g4b
-
-using namespace g4b;
-
-cudaError_t g4b_attention(const AttnArgs& a, void* bfrag, cudaStream_t st, bool pdl) {
-    if (a.hd % 64 || a.hd > 512 || a.qh % a.kvh) return cudaErrorInvalidValue;
-    const int chunks = (a.M * (a.qh / a.kvh) + kAttnRows - 1) / kAttnRows;
+template <bool BF16, int HD>
+static cudaError_t launch_attn(const AttnArgs& a, void* bfrag, cudaStream_t st, bool pdl) {
+    const size_t smem = attn_smem_bytes(HD, BF16 ? 3 : 2);
     static bool attr_set = false;
     if (!attr_set) {
-        cudaFuncSetAttribute(attention_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)attn_smem_bytes(512));
+        const cudaError_t e = cudaFuncSetAttribute(attention_kernel<BF16, HD>,
+                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+        if (e != cudaSuccess) return e;
         attr_set = true;
     }
+    const int chunks = (a.M * (a.qh / a.kvh) + kAttnRows - 1) / kAttnRows;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(kSplits, a.kvh, chunks);
     cfg.blockDim = dim3(kAttnThreads);
-    cfg.dynamicSmemBytes = attn_smem_bytes(a.hd);
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = st;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -278,5 +387,25 @@ cudaError_t g4b_attention(const AttnArgs& a, void* bfrag, cudaStream_t st, bool 
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 2 : 1;
-    return cudaLaunchKernelEx(&cfg, attention_kernel, a, bfrag);
+    return cudaLaunchKernelEx(&cfg, attention_kernel<BF16, HD>, a, bfrag);
+}
+
+template <int HD>
+static cudaError_t launch_hd(const AttnArgs& a, void* bfrag, cudaStream_t st, bool pdl) {
+    return a.kv_bf16 ? launch_attn<true, HD>(a, bfrag, st, pdl) : launch_attn<false, HD>(a, bfrag, st, pdl);
+}
+
+}  // namespace g4b
+
+using namespace g4b;
+
+cudaError_t g4b_attention(const AttnArgs& a, void* bfrag, cudaStream_t st, bool pdl) {
+    if (a.kvh < 1 || a.qh % a.kvh || a.M < 1 || a.M > kMaxM) return cudaErrorInvalidValue;
+    switch (a.hd) {
+        case 64: return launch_hd<64>(a, bfrag, st, pdl);
+        case 128: return launch_hd<128>(a, bfrag, st, pdl);
+        case 256: return launch_hd<256>(a, bfrag, st, pdl);
+        case 512: return launch_hd<512>(a, bfrag, st, pdl);
+        default: return cudaErrorInvalidValue;
+    }
 }

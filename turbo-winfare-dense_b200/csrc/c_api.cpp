@@ -423,9 +423,9 @@ G4DENSE_API int g4dense_engine_set_gate(void* handle, double min_accept, int win
     return 0;
 }
 
-G4DENSE_API double g4dense_engine_time_pass(void* handle, int which, int batch, int reps) {
+G4DENSE_API double g4dense_engine_time_pass(void* handle, int which, int batch, int pos, int reps) {
     clear_error();
-    if (!handle || batch < 1 || batch > 16 || reps < 1) {
+    if (!handle || batch < 1 || batch > 16 || reps < 1 || pos < 0) {
         set_error("Invalid arguments");
         return -1.0;
     }
@@ -434,8 +434,9 @@ G4DENSE_API double g4dense_engine_time_pass(void* handle, int which, int batch, 
         g4b::DeviceModel* m = which == 0 ? &e->engine->target()
                                          : (e->engine->draft() ? &e->engine->draft()->model() : nullptr);
         if (!m) throw std::invalid_argument("no drafter loaded");
+        if (pos + batch > m->max_context()) throw std::invalid_argument("pos + batch exceeds the KV capacity");
         std::vector<uint32_t> toks(batch, 1);
-        m->run_plain(batch, 0, toks.data(), false);  // warm (captures the graph)
+        m->run_plain(batch, pos, toks.data(), false);  // warm (captures the graph)
         cudaEvent_t a, b;
         g4b::cuda_check(cudaEventCreate(&a), "event");
         g4b::cuda_check(cudaEventCreate(&b), "event");

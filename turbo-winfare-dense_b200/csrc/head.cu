@@ -34,11 +34,38 @@ __global__ void head_chunks_kernel(GemmOut lm, int V, int M, float softcap, floa
     const int v0 = chunk * kHeadChunk, v1 = min(V, v0 + kHeadChunk);
     float bv = -INFINITY;
     uint32_t bi = 0xFFFFFFFFu;
-    for (int v = v0 + threadIdx.x; v < v1; v += blockDim.x) {
-        float z = gemm_out_get(lm, m, v);
-        if (softcap > 0.f) z = softcap * tanhf(z / softcap);
-        if (logits) logits[(size_t)m * ldl + v] = z;
-        if (better(z, (uint32_t)v, bv, bi)) { bv = z; bi = (uint32_t)v; }
+    // Four 256-wide column blocks per batch; with split-K partials each block is its own row
+    // group, and all of a batch's slot loads are issued together.
+    for (int b0 = v0; b0 < v1; b0 += 4 * 256) {
+        float z[4];
+        if (lm.part.part) {
+            const float* pj[4];
+            int nsj[4], nsmax = 0;
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int v = b0 + j * 256 + threadIdx.x;
+                const int crg = (b0 >> 8) + j;
+                pj[j] = slot_base(lm.part, m, crg) + threadIdx.x;
+                nsj[j] = v < v1 ? slot_count(lm.part, crg) : 0;
+                nsmax = max(nsmax, nsj[j]);
+            }
+            slot_sums_each<4, 4>(pj, nsj, nsmax, z);
+        } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int v = b0 + j * 256 + threadIdx.x;
+                z[j] = v < v1 ? lm.y[(size_t)m * lm.ld + v] : 0.f;
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int v = b0 + j * 256 + threadIdx.x;
+            if (v >= v1) continue;
+            float zz = z[j];
+            if (softcap > 0.f) zz = softcap * tanhf(zz / softcap);
+            if (logits) logits[(size_t)m * ldl + v] = zz;
+            if (better(zz, (uint32_t)v, bv, bi)) { bv = zz; bi = (uint32_t)v; }
+        }
     }
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) {
@@ -103,6 +130,8 @@ int g4b_head_chunks(int V) { return (V + kHeadChunk - 1) / kHeadChunk; }
 
 cudaError_t g4b_head_chunks_launch(const GemmOut& lm, int V, int M, float softcap, float* logits, int ldl,
                                    float2* chunk_best, cudaStream_t st, bool pdl) {
+    // 256 threads, one column per thread per 256-wide block: blocks must align to row groups.
+    static_assert(kHeadChunk % 256 == 0, "head chunk");
     return launch(head_chunks_kernel, dim3(g4b_head_chunks(V), M), dim3(256), 0, st, pdl, lm, V, M, softcap, logits,
                   ldl, chunk_best);
 }

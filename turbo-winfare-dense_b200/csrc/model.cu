@@ -388,7 +388,12 @@ void DeviceModel::init_buffers() {
     const int d = h_.d_model;
     int max_attn_k = 0, max_F = 0, max_q = 0;
     size_t part = 0;
-    auto consider = [&](const QW& q) { part = std::max(part, (size_t)q.n_crg * q.max_slots * kMaxM * 256); };
+    int max_n = d, max_crg = 0;
+    auto consider = [&](const QW& q) {
+        part = std::max(part, (size_t)q.n_crg * q.max_slots * kMaxM * 256);
+        max_crg = std::max(max_crg, q.n_crg);
+        if (&q != &lm_) max_n = std::max(max_n, q.N);
+    };
     for (auto& L : layers_) {
         max_attn_k = std::max(max_attn_k, L.qh * L.hd);
         max_F = std::max(max_F, L.F);
@@ -406,8 +411,10 @@ void DeviceModel::init_buffers() {
     bf_ff_ = dmalloc(bfrag_capacity(round_up(max_F, 128)));
     part_ = static_cast<float*>(dmalloc(part * 4));
     q_buf_ = static_cast<float*>(dmalloc((size_t)kMaxM * max_q * 4));
-    y_ = static_cast<float*>(dmalloc((size_t)kMaxM * std::max(d, 2 * max_F) * 4));
+    y_ = static_cast<float*>(dmalloc((size_t)kMaxM * max_n * 4));
     ybuf_ = static_cast<float*>(dmalloc((size_t)kMaxM * d * 4));
+    cnt_ = static_cast<unsigned*>(dmalloc((size_t)max_crg * sizeof(unsigned)));
+    cuda_check(cudaMemset(cnt_, 0, (size_t)max_crg * sizeof(unsigned)), "memset");
     stats_ = static_cast<float4*>(dmalloc((size_t)kMaxM * g4b_rowepi_chunks(d) * sizeof(float4)));
     chunk_best_ = static_cast<float2*>(dmalloc((size_t)opt_.tp * kMaxM * g4b_head_chunks(v_local_) * sizeof(float2)));
     logits_ = static_cast<float*>(dmalloc((size_t)kMaxM * v_local_ * 4));
@@ -432,8 +439,8 @@ uint64_t DeviceModel::pass_weight_bytes() const { return weight_bytes_; }
 int DeviceModel::kernels_per_pass(int M) const {
     (void)M;
     // embed_norm; per layer 4 GEMMs + qkv_epi + attention + 2x2 norm/residual phases +
-    // geglu (+ 2 slot reductions under TP); LM head GEMM + head_chunks + finalize
-    const int per_layer = 11 + (opt_.tp > 1 ? 2 : 0);
+    // geglu; LM head GEMM + head_chunks + finalize (NCCL's all-reduce kernels not counted)
+    const int per_layer = 11;
     return 1 + per_layer * (int)layers_.size() + 3;
 }
 
@@ -458,12 +465,12 @@ double DeviceModel::profile_gemms(int M, int reps, uint64_t* bytes, int* gemm_la
     cuda_check(cudaEventRecord(e0, stream_), "event");
     for (int r = 0; r < reps; ++r) {
         for (auto& L : layers_) {
-            gemm(L.qkv, bf_d_, M);
-            gemm(L.o, bf_attn_, M);
-            gemm(L.gateup, bf_d_, M);
-            gemm(L.down, bf_ff_, M);
+            gemm(L.qkv, bf_d_, M, nullptr);
+            gemm(L.o, bf_attn_, M, tp_out());
+            gemm(L.gateup, bf_d_, M, nullptr);
+            gemm(L.down, bf_ff_, M, tp_out());
         }
-        gemm(lm_, bf_d_, M);
+        gemm(lm_, bf_d_, M, nullptr);
     }
     cuda_check(cudaEventRecord(e1, stream_), "event");
     cuda_check(cudaEventSynchronize(e1), "event");
@@ -489,7 +496,11 @@ PartView DeviceModel::part_view(const QW& q, int M) const {
     return v;
 }
 
-void DeviceModel::gemm(const QW& q, const void* bfrag, int M) {
+GemmOut DeviceModel::partials(const QW& q, int M) const { return GemmOut{part_view(q, M), nullptr, q.N}; }
+
+float* DeviceModel::tp_out() const { return opt_.tp > 1 ? y_ : nullptr; }
+
+void DeviceModel::gemm(const QW& q, const void* bfrag, int M, float* y) {
     const BFragView v = bfrag_view(const_cast<void*>(bfrag), q.ktiles * 128, M);
     VgemmParams p{};
     p.w = q.w;
@@ -500,6 +511,9 @@ void DeviceModel::gemm(const QW& q, const void* bfrag, int M) {
     p.M = M;
     p.n_wrg = q.n_wrg;
     p.err = err_dev_;
+    p.y = y;  // nullptr: leave the partial slots to the consumer
+    p.ldy = q.N;
+    p.cnt = cnt_;
     cuda_check(vgemm_launch(p, stream_, opt_.use_pdl), "vgemm");
 }
 
@@ -514,9 +528,9 @@ void DeviceModel::enqueue_raw(int M, PassKind kind, bool want_logits, uint32_t* 
     for (size_t l = 0; l < layers_.size(); ++l) {
         DevLayer& L = layers_[l];
         // Q/K/V
-        gemm(L.qkv, bf_d_, M);
+        gemm(L.qkv, bf_d_, M, nullptr);
         QkvEpiArgs qa{};
-        qa.qkv.part = part_view(L.qkv, M);
+        qa.qkv = partials(L.qkv, M);
         qa.sp = sp;
         qa.M = M;
         qa.qh = L.qh;
@@ -549,18 +563,16 @@ void DeviceModel::enqueue_raw(int M, PassKind kind, bool want_logits, uint32_t* 
         aa.scale = 1.0f;
         cuda_check(g4b_attention(aa, bf_attn_, stream_, pdl), "attention");
         // o projection + post-attention norm / residual + pre-FFN norm
-        gemm(L.o, bf_attn_, M);
-        GemmOut oo{};
-        oo.part = part_view(L.o, M);
+        // Under tensor parallelism the o and down GEMMs finish their own split-K sum into y_,
+        // which is then all-reduced in place; otherwise the epilogue sums the slots.
+        gemm(L.o, bf_attn_, M, tp_out());
+        GemmOut oo = partials(L.o, M);
 #ifdef G4B_HAVE_NCCL
         if (opt_.tp > 1) {
-            cuda_check(vgemm_reduce(oo.part, M, d, y_, d, stream_, pdl), "reduce");
             if (ncclAllReduce(y_, y_, (size_t)M * d, ncclFloat, ncclSum, (ncclComm_t)opt_.nccl_comm, stream_) !=
                 ncclSuccess)
                 throw std::runtime_error("ncclAllReduce (attention) failed");
-            oo.part.part = nullptr;
-            oo.y = y_;
-            oo.ld = d;
+            oo = GemmOut{PartView{}, y_, d};
         }
 #endif
         cuda_check(g4b_rowepi(oo, hres_[cur], hres_[1 - cur], L.pa_norm, 1.0f, L.pf_norm, d, ybuf_, stats_, bf_d_, M,
@@ -568,22 +580,16 @@ void DeviceModel::enqueue_raw(int M, PassKind kind, bool want_logits, uint32_t* 
                    "post_attn");
         cur = 1 - cur;
         // FFN
-        gemm(L.gateup, bf_d_, M);
-        GemmOut gu{};
-        gu.part = part_view(L.gateup, M);
-        cuda_check(g4b_geglu(gu, L.F, bf_ff_, M, stream_, pdl), "geglu");
-        gemm(L.down, bf_ff_, M);
-        GemmOut dn{};
-        dn.part = part_view(L.down, M);
+        gemm(L.gateup, bf_d_, M, nullptr);
+        cuda_check(g4b_geglu(partials(L.gateup, M), L.F, bf_ff_, M, stream_, pdl), "geglu");
+        gemm(L.down, bf_ff_, M, tp_out());
+        GemmOut dn = partials(L.down, M);
 #ifdef G4B_HAVE_NCCL
         if (opt_.tp > 1) {
-            cuda_check(vgemm_reduce(dn.part, M, d, y_, d, stream_, pdl), "reduce");
             if (ncclAllReduce(y_, y_, (size_t)M * d, ncclFloat, ncclSum, (ncclComm_t)opt_.nccl_comm, stream_) !=
                 ncclSuccess)
                 throw std::runtime_error("ncclAllReduce (FFN) failed");
-            dn.part.part = nullptr;
-            dn.y = y_;
-            dn.ld = d;
+            dn = GemmOut{PartView{}, y_, d};
         }
 #endif
         const uint16_t* w_next = (l + 1 < layers_.size()) ? layers_[l + 1].in_norm : final_norm_;
@@ -593,9 +599,8 @@ void DeviceModel::enqueue_raw(int M, PassKind kind, bool want_logits, uint32_t* 
         cur = 1 - cur;
     }
     // LM head
-    gemm(lm_, bf_d_, M);
-    GemmOut lo{};
-    lo.part = part_view(lm_, M);
+    gemm(lm_, bf_d_, M, nullptr);
+    const GemmOut lo = partials(lm_, M);
     const int nch = g4b_head_chunks(v_local_);
     cuda_check(g4b_head_chunks_launch(lo, v_local_, M, h_.final_logit_softcapping, want_logits ? logits_ : nullptr,
                                       v_local_, chunk_best_, stream_, pdl),

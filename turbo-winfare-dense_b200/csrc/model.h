@@ -108,8 +108,11 @@ class DeviceModel {
     void init_buffers();
     void build_layer_from_host(uint32_t l, const uint8_t* layer_ptr);
     void enqueue_raw(int M, PassKind kind, bool want_logits, uint32_t* chain_out);
-    void gemm(const QW& q, const void* bfrag, int M);
+    // One verify GEMM; y == nullptr leaves split-K partials for the consumer (partials()).
+    void gemm(const QW& q, const void* bfrag, int M, float* y);
     PartView part_view(const QW& q, int M) const;
+    GemmOut partials(const QW& q, int M) const;
+    float* tp_out() const;  // dense output for GEMMs followed by an all-reduce, else nullptr
     void upload_qw(QW& q, const uint32_t* W, const uint16_t* S, const uint16_t* B, int N, int K);
     void alloc_qw(QW& q, int N, int K);
     uint16_t* upload_u16(const uint16_t* src, size_t n);
@@ -133,8 +136,9 @@ class DeviceModel {
     float* part_ = nullptr;
     size_t part_floats_ = 0;
     float* q_buf_ = nullptr;
-    float* y_ = nullptr;  // all-reduce staging [16][max(d, ...)]
+    float* y_ = nullptr;       // dense GEMM output ahead of an all-reduce [16][max N]
     float* ybuf_ = nullptr;    // norm/residual epilogue scratch [16][d]
+    unsigned* cnt_ = nullptr;  // split-K arrival counters of the GEMM running on stream_
     float4* stats_ = nullptr;  // [16][chunks]
     float2* chunk_best_ = nullptr;
     float* logits_ = nullptr;

@@ -16,8 +16,9 @@ struct StepParams {
     uint32_t tokens[16];
 };
 
-// A GEMM output as its consumers see it: split-K slots (part.part != nullptr) or a plain
-// fp32 [M][ld] matrix (after a tensor-parallel all-reduce).
+// A GEMM output as its consumers see it: split-K partial slots (part.part != nullptr), summed
+// by the consumer in slot order, or a dense fp32 [M][ld] matrix (a GEMM that finished its own
+// sum, e.g. ahead of a tensor-parallel all-reduce).
 struct GemmOut {
     PartView part;
     const float* y;
@@ -25,30 +26,75 @@ struct GemmOut {
 };
 
 #ifdef __CUDACC__
-__device__ __forceinline__ float gemm_out_get(const GemmOut& o, int m, int n) {
-    return o.part.part ? vgemm_part_get(o.part, m, n) : o.y[(size_t)m * o.ld + n];
+// Slot 0 of row m in row group crg (slot s is 4096 floats further) and the slot count: the
+// CTAs whose unit ranges [c*T/G, (c+1)*T/G) meet the group's units.
+__device__ __forceinline__ const float* slot_base(const PartView& v, int m, int crg) {
+    return v.part + ((size_t)crg * v.max_slots * 16 + m) * 256;
 }
-// Columns n and n+1 (n even): one slot lookup, 8-byte loads, loads batched across slots.
+__device__ __forceinline__ int slot_count(const PartView& v, int crg) {
+    const int T = v.n_crg * v.ktiles;
+    return vgemm_cta_of_unit32((crg + 1) * v.ktiles - 1, T, v.grid) - vgemm_cta_of_unit32(crg * v.ktiles, T, v.grid) + 1;
+}
+// out[j] = sum over s < ns, in slot order, of p[s * 4096 + j * stride]. The loads of a batch
+// (B slots x NE elements) are all issued before any is added: a few memory round trips in
+// total rather than one per slot.
+template <int NE, int B>
+__device__ __forceinline__ void slot_sums(const float* p, int stride, int ns, float (&out)[NE]) {
+#pragma unroll
+    for (int j = 0; j < NE; ++j) out[j] = 0.f;
+    for (int s0 = 0; s0 < ns; s0 += B) {
+        float v[B][NE];
+#pragma unroll
+        for (int k = 0; k < B; ++k)
+#pragma unroll
+            for (int j = 0; j < NE; ++j)
+                if (s0 + k < ns) v[k][j] = __ldcg(p + (size_t)(s0 + k) * 4096 + j * stride);
+#pragma unroll
+        for (int k = 0; k < B; ++k)
+#pragma unroll
+            for (int j = 0; j < NE; ++j)
+                if (s0 + k < ns) out[j] += v[k][j];
+    }
+}
+// Per-element variant: element j has its own slot-0 pointer p[j] and slot count ns[j]
+// (elements may sit in different row groups); nsmax = max ns[j]. Same slot order.
+template <int NE, int B>
+__device__ __forceinline__ void slot_sums_each(const float* const (&p)[NE], const int (&ns)[NE], int nsmax,
+                                               float (&out)[NE]) {
+#pragma unroll
+    for (int j = 0; j < NE; ++j) out[j] = 0.f;
+    for (int s0 = 0; s0 < nsmax; s0 += B) {
+        float v[B][NE];
+#pragma unroll
+        for (int k = 0; k < B; ++k)
+#pragma unroll
+            for (int j = 0; j < NE; ++j)
+                if (s0 + k < ns[j]) v[k][j] = __ldcg(p[j] + (size_t)(s0 + k) * 4096);
+#pragma unroll
+        for (int k = 0; k < B; ++k)
+#pragma unroll
+            for (int j = 0; j < NE; ++j)
+                if (s0 + k < ns[j]) out[j] += v[k][j];
+    }
+}
+// Columns n, n+1 (n even) of row m.
 __device__ __forceinline__ float2 gemm_out_pair(const GemmOut& o, int m, int n) {
     if (!o.part.part) return *reinterpret_cast<const float2*>(o.y + (size_t)m * o.ld + n);
-    const SlotRow r = vgemm_slot_row(o.part, m, n >> 8);
-    const float2* p = reinterpret_cast<const float2*>(r.p + (n & 255));
+    const int crg = n >> 8;
+    const float2* p = reinterpret_cast<const float2*>(slot_base(o.part, m, crg) + (n & 255));
+    const int ns = slot_count(o.part, crg);
     float2 s = make_float2(0.f, 0.f);
-    int i = 0;
-    for (; i + 8 <= r.ns; i += 8) {
-        float2 t[8];
+    for (int s0 = 0; s0 < ns; s0 += 16) {
+        float2 v[16];
 #pragma unroll
-        for (int j = 0; j < 8; ++j) t[j] = __ldcg(p + (size_t)(i + j) * 2048);
+        for (int k = 0; k < 16; ++k)
+            if (s0 + k < ns) v[k] = __ldcg(p + (size_t)(s0 + k) * 2048);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) {
-            s.x += t[j].x;
-            s.y += t[j].y;
-        }
-    }
-    for (; i < r.ns; ++i) {
-        const float2 t = __ldcg(p + (size_t)i * 2048);
-        s.x += t.x;
-        s.y += t.y;
+        for (int k = 0; k < 16; ++k)
+            if (s0 + k < ns) {
+                s.x += v[k].x;
+                s.y += v[k].y;
+            }
     }
     return s;
 }

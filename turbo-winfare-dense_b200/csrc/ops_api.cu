@@ -26,6 +26,7 @@ struct g4b_qmat {
     void* w;          // repacked weights
     void* bfrag;      // B fragments for one input of up to 16 rows
     float* part;      // split-K partials
+    unsigned* cnt;    // split-K arrival counters [n_crg], zero between launches
     int max_slots;    // slots per row group sized for every M
     int* err;         // device error word of the bounded waits
 };
@@ -52,6 +53,8 @@ int g4b_qmat_create(const uint32_t* W, const uint16_t* S, const uint16_t* B, int
     q->max_slots = vgemm_plan_slots(q->n_crg, q->ktiles);
     const size_t part_bytes = (size_t)q->n_crg * q->max_slots * g4b::kMaxM * 256 * sizeof(float);
     if ((e = cudaMalloc(&q->part, part_bytes)) != cudaSuccess) { g4b_qmat_destroy(q); return fail(e, "cudaMalloc(part)"); }
+    if ((e = cudaMalloc(&q->cnt, q->n_crg * sizeof(unsigned))) != cudaSuccess) { g4b_qmat_destroy(q); return fail(e, "cudaMalloc(cnt)"); }
+    if ((e = cudaMemsetAsync(q->cnt, 0, q->n_crg * sizeof(unsigned), st)) != cudaSuccess) { g4b_qmat_destroy(q); return fail(e, "memset"); }
     if ((e = cudaMalloc(&q->err, sizeof(int))) != cudaSuccess) { g4b_qmat_destroy(q); return fail(e, "cudaMalloc(err)"); }
     if ((e = cudaMemsetAsync(q->err, 0, sizeof(int), st)) != cudaSuccess) { g4b_qmat_destroy(q); return fail(e, "memset"); }
     if ((e = cudaStreamSynchronize(st)) != cudaSuccess) { g4b_qmat_destroy(q); return fail(e, "g4b_qmat_create"); }
@@ -64,6 +67,7 @@ void g4b_qmat_destroy(g4b_qmat* q) {
     cudaFree(q->w);
     cudaFree(q->bfrag);
     cudaFree(q->part);
+    cudaFree(q->cnt);
     cudaFree(q->err);
     delete q;
 }
@@ -84,11 +88,8 @@ static PartView qmat_view(const g4b_qmat* q, int M) {
     return v;
 }
 
-// GEMM kernel only: leaves the split-K partials in the matrix's workspace.
-int g4b_qmat_run_partial(g4b_qmat* q, int M, void* stream) {
-    if (!q || M < 1 || M > g4b::kMaxM) return fail_msg("g4b_qmat_run_partial: bad arguments");
-    const int Kp = q->ktiles * 128;
-    const g4b::BFragView v = g4b::bfrag_view(q->bfrag, Kp, M);
+static VgemmParams qmat_params(g4b_qmat* q, int M) {
+    const g4b::BFragView v = g4b::bfrag_view(q->bfrag, q->ktiles * 128, M);
     VgemmParams p{};
     p.w = q->w;
     p.bfrag = v.frag;
@@ -98,16 +99,24 @@ int g4b_qmat_run_partial(g4b_qmat* q, int M, void* stream) {
     p.M = M;
     p.n_wrg = q->n_wrg;
     p.err = q->err;
-    cudaError_t e = vgemm_launch(p, (cudaStream_t)stream, false);
+    return p;
+}
+
+// GEMM kernel without its split-K sum: leaves the partials in the matrix's workspace.
+int g4b_qmat_run_partial(g4b_qmat* q, int M, void* stream) {
+    if (!q || M < 1 || M > g4b::kMaxM) return fail_msg("g4b_qmat_run_partial: bad arguments");
+    cudaError_t e = vgemm_launch(qmat_params(q, M), (cudaStream_t)stream, false);
     return e == cudaSuccess ? 0 : fail(e, "vgemm_launch");
 }
 
 int g4b_qmat_run(g4b_qmat* q, int M, float* out, int ldo, void* stream) {
     if (!q || !out || M < 1 || M > g4b::kMaxM || ldo < q->N) return fail_msg("g4b_qmat_run: bad arguments");
-    int rc = g4b_qmat_run_partial(q, M, stream);
-    if (rc) return rc;
-    cudaError_t e = vgemm_reduce(qmat_view(q, M), M, q->N, out, ldo, (cudaStream_t)stream, false);
-    return e == cudaSuccess ? 0 : fail(e, "vgemm_reduce");
+    VgemmParams p = qmat_params(q, M);
+    p.y = out;
+    p.ldy = ldo;
+    p.cnt = q->cnt;
+    cudaError_t e = vgemm_launch(p, (cudaStream_t)stream, false);
+    return e == cudaSuccess ? 0 : fail(e, "vgemm_launch");
 }
 
 int g4b_qmat_gemm(g4b_qmat* q, const float* x, int ldx, int M, float* out, int ldo, void* stream) {

@@ -111,27 +111,40 @@ __global__ void qkv_epi_kernel(QkvEpiArgs a) {
     const bool is_q = head < a.qh;
     const int kvh = head - a.qh;
     const int row0 = is_q ? head * hd : nq + kvh * hd;
-    // A head spans at most two 256-row groups of the GEMM output: look their slots up once.
+    // Lane l reads elements l + 32j of the head; every slot load of a batch is in flight
+    // together.
     auto load_head = [&](int r0, float* dst) {
         float ss = 0.f;
         if (a.qkv.part.part) {
-            const SlotRow s0 = vgemm_slot_row(a.qkv.part, m, r0 >> 8);
-            const SlotRow s1 = vgemm_slot_row(a.qkv.part, m, (r0 + hd - 1) >> 8);
+            const float* pj[kMaxHdPerLane];
+            int nsj[kMaxHdPerLane];
+            int nsmax = 0, prev_crg = -1, prev_ns = 0;
+#pragma unroll
+            for (int j = 0; j < kMaxHdPerLane; ++j) {
+                const int row = r0 + lane + 32 * (j < np ? j : 0);
+                const int crg = row >> 8;
+                if (crg != prev_crg) {
+                    prev_crg = crg;
+                    prev_ns = slot_count(a.qkv.part, crg);
+                }
+                pj[j] = slot_base(a.qkv.part, m, crg) + (row & 255);
+                nsj[j] = j < np ? prev_ns : 0;
+                nsmax = max(nsmax, nsj[j]);
+            }
+            float v[kMaxHdPerLane];
+            slot_sums_each<kMaxHdPerLane, 4>(pj, nsj, nsmax, v);
 #pragma unroll
             for (int j = 0; j < kMaxHdPerLane; ++j)
-                if (j < np) {
-                    const int row = r0 + lane + 32 * j;
-                    dst[j] = vgemm_slot_sum(((row >> 8) == (r0 >> 8)) ? s0 : s1, row & 255);
-                    ss += dst[j] * dst[j];
-                }
+                if (j < np) dst[j] = v[j];
         } else {
+            const float* src = a.qkv.y + (size_t)m * a.qkv.ld + r0 + lane;
 #pragma unroll
             for (int j = 0; j < kMaxHdPerLane; ++j)
-                if (j < np) {
-                    dst[j] = a.qkv.y[(size_t)m * a.qkv.ld + r0 + lane + 32 * j];
-                    ss += dst[j] * dst[j];
-                }
+                if (j < np) dst[j] = src[32 * j];
         }
+#pragma unroll
+        for (int j = 0; j < kMaxHdPerLane; ++j)
+            if (j < np) ss += dst[j] * dst[j];
         return ss;
     };
     float x[kMaxHdPerLane];
@@ -196,8 +209,8 @@ __global__ void qkv_epi_kernel(QkvEpiArgs a) {
 constexpr int kEpiWarps = 4;
 constexpr int kEpiCols = kEpiWarps * 64;
 
-// Phase 1: y = GEMM output (slot sums); per-chunk sums of y^2, h^2, h*c and c^2 with
-// c = y * w1, from which phase 2 obtains both RMS factors without another pass.
+// Phase 1: y = GEMM output (slot sums) into y_buf; per-chunk sums of y^2, h^2, h*c and c^2
+// with c = y * w1, from which phase 2 obtains both RMS factors without another pass.
 __global__ void rowepi_phase1_kernel(GemmOut o, const float* __restrict__ h_in, const uint16_t* __restrict__ w1, int d,
                                      float* __restrict__ y_buf, float4* __restrict__ stats) {
     __shared__ float4 red[kEpiWarps];
@@ -207,7 +220,10 @@ __global__ void rowepi_phase1_kernel(GemmOut o, const float* __restrict__ h_in, 
     const int c0 = chunk * kEpiCols + warp * 64 + 2 * lane;
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     float2 y2 = make_float2(0.f, 0.f);
-    if (c0 < d) y2 = gemm_out_pair(o, m, c0);
+    if (c0 < d) {
+        y2 = gemm_out_pair(o, m, c0);
+        *reinterpret_cast<float2*>(y_buf + (size_t)m * d + c0) = y2;
+    }
 #pragma unroll
     for (int j = 0; j < 2; ++j) {
         const int c = c0 + j;
@@ -215,7 +231,6 @@ __global__ void rowepi_phase1_kernel(GemmOut o, const float* __restrict__ h_in, 
             const float y = j ? y2.y : y2.x;
             const float h = h_in[(size_t)m * d + c];
             const float cc = y * bf16_to_f32(w1[c]);
-            y_buf[(size_t)m * d + c] = y;
             acc.x += y * y;
             acc.y += h * h;
             acc.z += h * cc;
@@ -360,6 +375,7 @@ int g4b_rowepi_chunks(int d) { return ((d + 127) / 128 * 128 + kEpiCols - 1) / k
 cudaError_t g4b_rowepi(const GemmOut& o, const float* h_in, float* h_out, const uint16_t* w1, float out_scale,
                        const uint16_t* w2, int d, float* y_buf, float4* stats, void* bfrag, int M, cudaStream_t st,
                        bool pdl) {
+    if ((o.ld | d) & 1) return cudaErrorInvalidValue;  // float2 loads
     const dim3 grid(g4b_rowepi_chunks(d), M);
     cudaError_t e = launch(rowepi_phase1_kernel, grid, dim3(kEpiWarps * 32), 0, st, pdl, o, h_in, w1, d, y_buf, stats);
     if (e != cudaSuccess) return e;
@@ -368,6 +384,7 @@ cudaError_t g4b_rowepi(const GemmOut& o, const float* h_in, float* h_out, const 
 }
 
 cudaError_t g4b_geglu(const GemmOut& gu, int F, void* bfrag, int M, cudaStream_t st, bool pdl) {
+    if ((gu.ld | F) & 1) return cudaErrorInvalidValue;  // float2 loads
     const int ng = (F + 127) / 128 * 2;
     return launch(geglu_kernel, dim3(grid_for_warps(M * ng)), dim3(256), 0, st, pdl, gu, F, bfrag, M);
 }

@@ -15,7 +15,8 @@
 //   * work is split stream-K style: CTA c owns the contiguous unit range
 //     [c*T/G, (c+1)*T/G) of (256-row group, k-tile) units, so every CTA streams the same
 //     number of bytes whatever the shape. Each CTA writes one partial per row group it
-//     touches into a fixed slot; consumers add the slots in order (deterministic);
+//     touches into a fixed slot; the last CTA to arrive on a row group adds its slots in
+//     slot order (deterministic) and writes the dense output;
 //   * activation fragments for the CTA's k-range are double-buffered in shared memory by
 //     bulk copies, one chunk ahead.
 // tcgen05 is deliberately not used here: at M <= 16 the tensor work is a small part of the
@@ -121,6 +122,70 @@ __device__ __forceinline__ void compute_ktile(const uint4* __restrict__ blk, con
     }
 }
 
+// y[m][crg*256 + j] = sum over slots s = 0..ns-1, in slot order, of part[crg][s][m][j]. One
+// CTA of 128 threads over M x 64 float4 columns; every load of a batch (8 slots of one
+// column when M <= 2, else 4 slots of 4 columns) is issued before any is added.
+__device__ __forceinline__ void vgemm_sum_slots(const VgemmParams& p, int crg, int ns) {
+    const float4* src = reinterpret_cast<const float4*>(p.out.part) + (size_t)crg * p.out.max_slots * kMaxM * 64;
+    const int items = p.M * 64;
+    auto store = [&](int it, const float4& v) {
+        const int n = crg * kCtaRows + (it & 63) * 4;
+        float* o = p.y + (size_t)(it >> 6) * p.ldy + n;
+        if (n < p.N) o[0] = v.x;
+        if (n + 1 < p.N) o[1] = v.y;
+        if (n + 2 < p.N) o[2] = v.z;
+        if (n + 3 < p.N) o[3] = v.w;
+    };
+    auto add = [](float4& a, const float4& b) {
+        a.x += b.x;
+        a.y += b.y;
+        a.z += b.z;
+        a.w += b.w;
+    };
+    if (items <= kThreads) {
+        const int it = threadIdx.x;
+        if (it >= items) return;
+        float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int s0 = 0; s0 < ns; s0 += 8) {
+            float4 v[8];
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+                if (s0 + k < ns) v[k] = __ldcg(src + ((size_t)(s0 + k) * kMaxM + (it >> 6)) * 64 + (it & 63));
+#pragma unroll
+            for (int k = 0; k < 8; ++k)
+                if (s0 + k < ns) add(sum, v[k]);
+        }
+        store(it, sum);
+        return;
+    }
+    for (int base = 0; base < items; base += 4 * kThreads) {
+        float4 sum[4];
+#pragma unroll
+        for (int j = 0; j < 4; ++j) sum[j] = make_float4(0.f, 0.f, 0.f, 0.f);
+        for (int s0 = 0; s0 < ns; s0 += 4) {
+            float4 v[4][4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                const int it = base + j * kThreads + threadIdx.x;
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    if (it < items && s0 + k < ns)
+                        v[j][k] = __ldcg(src + ((size_t)(s0 + k) * kMaxM + (it >> 6)) * 64 + (it & 63));
+            }
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    if (base + j * kThreads + (int)threadIdx.x < items && s0 + k < ns) add(sum[j], v[j][k]);
+        }
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+            const int it = base + j * kThreads + threadIdx.x;
+            if (it < items) store(it, sum[j]);
+        }
+    }
+}
+
 template <int NB, int NACC, bool PACKED>
 __global__ void __launch_bounds__(kThreads, NACC == 2 ? 2 : 3) vgemm_kernel(VgemmParams p) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
@@ -131,6 +196,10 @@ __global__ void __launch_bounds__(kThreads, NACC == 2 ? 2 : 3) vgemm_kernel(Vgem
     uint4* bbuf = ring + kWarps * kStages * kBlockU4;                 // [2][kBufU4]
     uint64_t* wbar = reinterpret_cast<uint64_t*>(bbuf + 2 * kBufU4);  // [warp][stage]
     uint64_t* bbar = wbar + kWarps * kStages;                         // [2]
+    // Row groups this CTA must finish (it arrived last on them): bit i = first row group of
+    // the CTA's range + i. The sums run after the streaming loop, when the accumulators are
+    // dead, so their loads can all be in flight at once.
+    __shared__ unsigned s_lastmask;
 
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int ktiles = p.out.ktiles;
@@ -147,6 +216,7 @@ __global__ void __launch_bounds__(kThreads, NACC == 2 ? 2 : 3) vgemm_kernel(Vgem
         mbar_init(&bbar[0], 1);
         mbar_init(&bbar[1], 1);
     }
+    if (threadIdx.x == 0) s_lastmask = 0;
     mbar_init_fence();
     __syncthreads();
 
@@ -218,11 +288,16 @@ __global__ void __launch_bounds__(kThreads, NACC == 2 ? 2 : 3) vgemm_kernel(Vgem
     int seg_crg = cur.crg;
     const int g = lane >> 2, t = lane & 3;
 
+    const int first_crg = cur.crg;
     auto flush_segment = [&](int crg) {
-        const int lo = vgemm_cta_of_unit((long long)crg * ktiles, T, G);
-        const int slot = c - lo;
+        const int lo = vgemm_cta_of_unit32(crg * ktiles, T, G);
+        const int hi = vgemm_cta_of_unit32((crg + 1) * ktiles - 1, T, G);
+        const bool direct = p.y != nullptr && lo == hi;  // this CTA owns the whole row group
         const bool act = crg * kWarps + warp < p.n_wrg;
-        float* dst = p.out.part + ((size_t)crg * p.out.max_slots + slot) * kMaxM * kCtaRows;
+        float* dst = direct ? p.y + (size_t)crg * kCtaRows
+                            : p.out.part + ((size_t)crg * p.out.max_slots + (c - lo)) * kMaxM * kCtaRows;
+        const int ld = direct ? p.ldy : kCtaRows;
+        const int nmax = direct ? p.N - crg * kCtaRows : kCtaRows;
 #pragma unroll
         for (int r = 0; r < kTilesPerWarp; ++r) {
 #pragma unroll
@@ -234,10 +309,17 @@ __global__ void __launch_bounds__(kThreads, NACC == 2 ? 2 : 3) vgemm_kernel(Vgem
                     v *= 16777216.0f;  // 2^24: the subnormal operand scale
                     const int m = a * 8 + 2 * t + (i & 1);
                     const int nl = warp * kWarpRows + r * 16 + g + ((i >> 1) << 3);
-                    if (act && !failed && (!PACKED || t < 2) && m < p.M) dst[m * kCtaRows + nl] = v;
+                    if (act && !failed && (!PACKED || t < 2) && m < p.M && nl < nmax) dst[(size_t)m * ld + nl] = v;
                     acc[r][a][i] = 0.f;
                 }
             }
+        }
+        if (p.y && !direct) {
+            // Publish this slot and count the arrival; the last arrival owns the sum.
+            __threadfence();
+            __syncthreads();
+            if (threadIdx.x == 0 && atomicAdd(p.cnt + crg, 1u) == (unsigned)(hi - lo))
+                s_lastmask |= 1u << (crg - first_crg);
         }
     };
 
@@ -279,6 +361,19 @@ __global__ void __launch_bounds__(kThreads, NACC == 2 ? 2 : 3) vgemm_kernel(Vgem
         advance(pre);
     }
     if (n_units > 0) flush_segment(seg_crg);
+    if (p.y) {
+        __syncthreads();
+        unsigned mask = s_lastmask;
+        if (mask) __threadfence();
+        while (mask) {
+            const int crg = first_crg + __ffs(mask) - 1;
+            mask &= mask - 1;
+            const int lo = vgemm_cta_of_unit32(crg * ktiles, T, G);
+            const int hi = vgemm_cta_of_unit32((crg + 1) * ktiles - 1, T, G);
+            vgemm_sum_slots(p, crg, hi - lo + 1);
+            if (threadIdx.x == 0) p.cnt[crg] = 0;  // every CTA of the group has arrived
+        }
+    }
     if (failed && p.err) atomicExch(p.err, 1);
 }
 
@@ -319,20 +414,6 @@ static cudaError_t launch_t(const VgemmParams& p, cudaStream_t st, bool pdl) {
                   pdl, p);
 }
 
-__global__ void vgemm_reduce_kernel(PartView v, int M, int N, float* out, int ldo) {
-    pdl_enter();
-    const int n4 = (N + 3) / 4;
-    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < M * n4; i += gridDim.x * blockDim.x) {
-        const int m = i / n4, n = (i % n4) * 4;
-        const float4 s = vgemm_part_get4(v, m, n);
-        float* o = out + (size_t)m * ldo + n;
-        o[0] = s.x;
-        if (n + 1 < N) o[1] = s.y;
-        if (n + 2 < N) o[2] = s.z;
-        if (n + 3 < N) o[3] = s.w;
-    }
-}
-
 }  // namespace g4b
 
 using namespace g4b;
@@ -363,15 +444,15 @@ int vgemm_plan_slots(int n_crg, int ktiles) {
 
 cudaError_t vgemm_launch(const VgemmParams& p, cudaStream_t st, bool pdl) {
     if (p.M < 1 || p.M > kMaxM) return cudaErrorInvalidValue;
+    if (p.y && (!p.cnt || p.ldy < p.N)) return cudaErrorInvalidValue;
+    // A CTA records the row groups it must finish in a 32-bit mask: its unit range may touch
+    // at most 32 of them (n_crg / grid + 2 bounds the count).
+    if (p.y && p.out.n_crg / p.out.grid + 2 > 32) return cudaErrorInvalidValue;
+    // The kernel's 32-bit unit-to-CTA arithmetic needs (T + 1) * G < 2^31.
+    if (((long long)p.out.n_crg * p.out.ktiles + 1) * p.out.grid >= (1ll << 31)) return cudaErrorInvalidValue;
     if (vgemm_max_slots(p.out.grid, p.out.n_crg, p.out.ktiles) > p.out.max_slots) return cudaErrorInvalidValue;
     const BMode md = bmode_for(p.M);
     if (md.packed) return launch_t<1, 1, true>(p, st, pdl);
     if (md.nb == 2) return launch_t<2, 1, false>(p, st, pdl);
     return launch_t<4, 2, false>(p, st, pdl);
-}
-
-cudaError_t vgemm_reduce(const PartView& v, int M, int N, float* out, int ldo, cudaStream_t st, bool pdl) {
-    const int n = M * ((N + 3) / 4);
-    const int blocks = std::min(1184, (n + 255) / 256);
-    return launch(vgemm_reduce_kernel, dim3(blocks), dim3(256), 0, st, pdl, v, M, N, out, ldo);
 }

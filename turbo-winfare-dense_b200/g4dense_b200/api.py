@@ -80,7 +80,7 @@ def _bind_engine(L):
     L.g4dense_engine_last_stats.argtypes = [_vp, _vp, ctypes.c_int]
     L.g4dense_engine_set_gate.argtypes = [_vp, ctypes.c_double, ctypes.c_int]
     L.g4dense_engine_time_pass.restype = ctypes.c_double
-    L.g4dense_engine_time_pass.argtypes = [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int]
+    L.g4dense_engine_time_pass.argtypes = [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]
     L.g4dense_engine_profile_gemms.restype = ctypes.c_double
     L.g4dense_engine_profile_gemms.argtypes = [_vp, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_ulonglong),
                                                ctypes.POINTER(ctypes.c_int)]
@@ -249,8 +249,8 @@ class Engine:
         if lib().g4dense_engine_set_gate(self.h, min_accept, window):
             _eng_err("g4dense_engine_set_gate")
 
-    def time_pass(self, which, batch, reps=5):
-        ms = lib().g4dense_engine_time_pass(self.h, which, batch, reps)
+    def time_pass(self, which, batch, reps=5, pos=0):
+        ms = lib().g4dense_engine_time_pass(self.h, which, batch, pos, reps)
         if ms < 0:
             _eng_err("g4dense_engine_time_pass")
         return ms
