@@ -5,7 +5,7 @@
 //   embed_norm   token gather x sqrt(d) (src/cpu_reference.cpp:260-291) + input RMSNorm
 //   qkv_epi      q/k RMSNorm*w + NeoX RoPE, v unweighted RMSNorm (raw k on layers without
 //                v_proj), K/V rounded and written to the ring (:398-498, QKVEpilogue.hlsl,
-//                KVWrite.hlsl) -- one warp per (row, head)
+//                KVWrite.hlsl) -- one CTA per (row, head), one thread per rotary pair
 //   rowepi       post-attention: h += rmsnorm(o)*w_post_attn; x = rmsnorm(h)*w_pre_ffn
 //                (:560-567); post-FFN: h = (h + rmsnorm(down)*w_post_ffn) * layer_scalar,
 //                then the next layer's input norm or the final norm (:583-629). Two wide
@@ -94,112 +94,70 @@ __global__ void embed_norm_kernel(const StepParams* __restrict__ sp, const uint3
 
 // ---------------------------------------------------------------- Q/K/V epilogue
 
-// One warp per (row m, head): heads [0, qh) are query heads, [qh, qh + kvh) KV heads. Lane l
-// holds elements l + 32j, so the NeoX partner of element i (i + hd/2) lives in the same lane.
-constexpr int kMaxHdPerLane = 16;  // head_dim <= 512
+// One CTA per (row m, head): heads [0, qh) are query heads, [qh, qh + kvh) KV heads. Thread i
+// (blockDim = hd/2) holds the NeoX pair (i, i + hd/2) -- its two elements and their rotation
+// stay in registers, every slot load of the pair is in flight together, and the per-head RMS
+// is a block reduction. Restates the reference's q/k/v norms, RoPE and FP16 cache rounding
+// (src/cpu_reference.cpp:452-498).
+
+// Elements r0 + i and r0 + i + half of row m.
+__device__ __forceinline__ float2 load_pair(const GemmOut& o, int m, int r0, int half) {
+    const int i = threadIdx.x;
+    if (!o.part.part) {
+        const float* src = o.y + (size_t)m * o.ld + r0 + i;
+        return make_float2(src[0], src[half]);
+    }
+    const int ra = r0 + i, rb = r0 + i + half;
+    const float* pj[2] = {slot_base(o.part, m, ra >> 8) + (ra & 255), slot_base(o.part, m, rb >> 8) + (rb & 255)};
+    const int nsa = slot_count(o.part, ra >> 8);
+    const int nsb = (rb >> 8) == (ra >> 8) ? nsa : slot_count(o.part, rb >> 8);
+    const int nsj[2] = {nsa, nsb};
+    float v[2];
+    slot_sums_each<2, 8>(pj, nsj, max(nsa, nsb), v);
+    return make_float2(v[0], v[1]);
+}
 
 __global__ void qkv_epi_kernel(QkvEpiArgs a) {
+    __shared__ float red[32];
     pdl_enter();
-    const int lane = threadIdx.x & 31;
-    const int w = blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
     const int heads = a.qh + a.kvh;
-    if (w >= a.M * heads) return;
-    const int m = w / heads, head = w % heads;
-    const int hd = a.hd, np = hd / 32;
+    const int m = blockIdx.x / heads, head = blockIdx.x % heads;
+    const int hd = a.hd, half = hd / 2, i = threadIdx.x;
     const int pos = a.sp->base_pos + m;
     const int nq = a.qh * hd, nk = a.kvh * hd;
     const bool is_q = head < a.qh;
     const int kvh = head - a.qh;
-    const int row0 = is_q ? head * hd : nq + kvh * hd;
-    // Lane l reads elements l + 32j of the head; every slot load of a batch is in flight
-    // together.
-    auto load_head = [&](int r0, float* dst) {
-        float ss = 0.f;
-        if (a.qkv.part.part) {
-            const float* pj[kMaxHdPerLane];
-            int nsj[kMaxHdPerLane];
-            int nsmax = 0, prev_crg = -1, prev_ns = 0;
-#pragma unroll
-            for (int j = 0; j < kMaxHdPerLane; ++j) {
-                const int row = r0 + lane + 32 * (j < np ? j : 0);
-                const int crg = row >> 8;
-                if (crg != prev_crg) {
-                    prev_crg = crg;
-                    prev_ns = slot_count(a.qkv.part, crg);
-                }
-                pj[j] = slot_base(a.qkv.part, m, crg) + (row & 255);
-                nsj[j] = j < np ? prev_ns : 0;
-                nsmax = max(nsmax, nsj[j]);
-            }
-            float v[kMaxHdPerLane];
-            slot_sums_each<kMaxHdPerLane, 4>(pj, nsj, nsmax, v);
-#pragma unroll
-            for (int j = 0; j < kMaxHdPerLane; ++j)
-                if (j < np) dst[j] = v[j];
-        } else {
-            const float* src = a.qkv.y + (size_t)m * a.qkv.ld + r0 + lane;
-#pragma unroll
-            for (int j = 0; j < kMaxHdPerLane; ++j)
-                if (j < np) dst[j] = src[32 * j];
-        }
-#pragma unroll
-        for (int j = 0; j < kMaxHdPerLane; ++j)
-            if (j < np) ss += dst[j] * dst[j];
-        return ss;
-    };
-    float x[kMaxHdPerLane];
-    const float r = inv_rms(warp_sum(load_head(row0, x)), hd);
+    float2 x = load_pair(a.qkv, m, is_q ? head * hd : nq + kvh * hd, half);
+    const float r = inv_rms(block_sum(x.x * x.x + x.y * x.y, red), hd);
     if (!is_q) {
         // V: unweighted norm of v_proj, or of the RAW k on layers without v_proj.
-        float v[kMaxHdPerLane];
-        float vss = 0.f;
-        if (a.has_v) {
-            vss = load_head(nq + nk + kvh * hd, v);
-        } else {
-#pragma unroll
-            for (int j = 0; j < kMaxHdPerLane; ++j)
-                if (j < np) {
-                    v[j] = x[j];
-                    vss += v[j] * v[j];
-                }
-        }
-        const float rv = inv_rms(warp_sum(vss), hd);
+        const float2 v = a.has_v ? load_pair(a.qkv, m, nq + nk + kvh * hd, half) : x;
+        const float rv = inv_rms(block_sum(v.x * v.x + v.y * v.y, red), hd);
         uint16_t* vd = a.v_ring + ((size_t)(pos % a.cap) * a.kvh + kvh) * hd;
-#pragma unroll
-        for (int j = 0; j < kMaxHdPerLane; ++j)
-            if (j < np) {
-                const float t = v[j] * rv;
-                vd[lane + 32 * j] = a.kv_bf16 ? bf16_bits_rne(t) : f16_bits_like_reference(t);
-            }
+        const float t0 = v.x * rv, t1 = v.y * rv;
+        vd[i] = a.kv_bf16 ? bf16_bits_rne(t0) : f16_bits_like_reference(t0);
+        vd[i + half] = a.kv_bf16 ? bf16_bits_rne(t1) : f16_bits_like_reference(t1);
     }
     const uint16_t* wn = is_q ? a.q_norm : a.k_norm;
-#pragma unroll
-    for (int j = 0; j < kMaxHdPerLane; ++j)
-        if (j < np) x[j] = x[j] * r * bf16_to_f32(wn[lane + 32 * j]);
-    // NeoX rotary on `rotated` pairs (i, i + hd/2).
-    const int half_j = hd / 64;
-#pragma unroll
-    for (int j = 0; j < kMaxHdPerLane / 2; ++j) {
-        const int p = lane + 32 * j;
-        if (j < half_j && p < a.rotated) {
-            const float freq = 1.0f / powf(a.theta, (float)(2 * p) / (float)hd);
-            const float ang = (float)pos * freq;
-            const float c = cosf(ang), s = sinf(ang);
-            const float x0 = x[j], x1 = x[j + half_j];
-            x[j] = x0 * c - x1 * s;
-            x[j + half_j] = x0 * s + x1 * c;
-        }
+    x.x = x.x * r * bf16_to_f32(wn[i]);
+    x.y = x.y * r * bf16_to_f32(wn[i + half]);
+    // NeoX rotary on the first `rotated` pairs.
+    if (i < a.rotated) {
+        const float freq = 1.0f / powf(a.theta, (float)(2 * i) / (float)hd);
+        const float ang = (float)pos * freq;
+        const float c = cosf(ang), s = sinf(ang);
+        const float x0 = x.x, x1 = x.y;
+        x.x = x0 * c - x1 * s;
+        x.y = x0 * s + x1 * c;
     }
     if (is_q) {
         float* qd = a.q_out + ((size_t)m * a.qh + head) * hd;
-#pragma unroll
-        for (int j = 0; j < kMaxHdPerLane; ++j)
-            if (j < np) qd[lane + 32 * j] = x[j];
+        qd[i] = x.x;
+        qd[i + half] = x.y;
     } else {
         uint16_t* kd = a.k_ring + ((size_t)(pos % a.cap) * a.kvh + kvh) * hd;
-#pragma unroll
-        for (int j = 0; j < kMaxHdPerLane; ++j)
-            if (j < np) kd[lane + 32 * j] = a.kv_bf16 ? bf16_bits_rne(x[j]) : f16_bits_like_reference(x[j]);
+        kd[i] = a.kv_bf16 ? bf16_bits_rne(x.x) : f16_bits_like_reference(x.x);
+        kd[i + half] = a.kv_bf16 ? bf16_bits_rne(x.y) : f16_bits_like_reference(x.y);
     }
 }
 
@@ -364,10 +322,8 @@ cudaError_t g4b_embed_norm(const StepParams* sp, const uint32_t* ew, const uint1
 }
 
 cudaError_t g4b_qkv_epi(const QkvEpiArgs& a, cudaStream_t st, bool pdl) {
-    if (a.hd % 64 || a.hd > 32 * kMaxHdPerLane || a.rotated > a.hd / 2) return cudaErrorInvalidValue;
-    // Two warps per block: the heads spread over as many SMs as possible.
-    const int warps = a.M * (a.qh + a.kvh);
-    return launch(qkv_epi_kernel, dim3((warps + 1) / 2), dim3(64), 0, st, pdl, a);
+    if (a.hd % 64 || a.hd > 1024 || a.rotated > a.hd / 2) return cudaErrorInvalidValue;
+    return launch(qkv_epi_kernel, dim3(a.M * (a.qh + a.kvh)), dim3(a.hd / 2), 0, st, pdl, a);
 }
 
 int g4b_rowepi_chunks(int d) { return ((d + 127) / 128 * 128 + kEpiCols - 1) / kEpiCols; }
