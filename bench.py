@@ -11,7 +11,8 @@ uniform-random prompt (seed 0) and 256 generated tokens per request.
 Acceptance is set by config 3's oracle drafter: the drafter model runs its k steps (cost) and
 its proposals replay the target's own greedy stream with i.i.d. injected mismatches. The
 headline uses a 0.25 mismatch rate; the line also carries the {0, 0.25, 0.5, 1.0} sweep and
-the natural random-weight drafter (which the adaptive gate switches off after 24 drafts).
+the natural random-weight drafter (which the adaptive gate switches off after 24 drafts). The
+adaptive gate is off for the replay runs, whose acceptance the replay sets.
 
 One step = one generation request. `value` = decoded tokens / device decode time (CUDA events
 on the engine's stream from the end of prefill to the last token, max over ranks); `e2e` =
@@ -98,6 +99,18 @@ def clocks_stop(proc, path, device):
 
 # ------------------------------------------------------------------------- reference arm
 
+def reduce_max(values, world):
+    """Element-wise max over ranks (device timings are reported as the slowest rank's)."""
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor(values, dtype=torch.float64)
+    if world > 1:
+        if dist.get_backend() == "nccl":
+            t = t.cuda()
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return [float(x) for x in t.cpu()]
+
+
 def reference_sample(steps, warmup):
     """Times the reference's CpuReferenceRunner on a 2-layer 31B-shaped container."""
     from g4dense_b200 import container as C
@@ -171,6 +184,7 @@ def run_b200(args, rank, world):
     eng.set_decode_options(draft_k=0)
     stream = eng.generate(prompt, GEN_LEN)
     ar = eng.stats()
+    eng.set_gate(0.45, -1)  # replay runs: acceptance is set by the replay, not gated
     eng.set_decode_options(draft_k=VERIFY_WIDTH, replay=stream, mismatch_rate=MISMATCH, mismatch_seed=7)
 
     matches = []
@@ -201,10 +215,7 @@ def run_b200(args, rank, world):
     dec_ms = sum(s["decode_gpu_ms"] for s in stats)
     dec_tokens = sum(s["emitted"] - 1 for s in stats)
     emitted = sum(s["emitted"] for s in stats)
-    vals = torch.tensor([dec_ms, wall], dtype=torch.float64, device="cuda")
-    if world > 1:
-        dist.all_reduce(vals, op=dist.ReduceOp.MAX)
-    dec_ms, wall = float(vals[0]), float(vals[1])
+    dec_ms, wall = reduce_max([dec_ms, wall], world)
     value = dec_tokens / (dec_ms / 1000.0)
     e2e = emitted / wall
 
@@ -215,6 +226,7 @@ def run_b200(args, rank, world):
         s = one()
         sweep[str(rate)] = {"tok_s": (s["emitted"] - 1) / (s["decode_gpu_ms"] / 1000.0),
                             "acceptance": s["accepted"] / max(1.0, s["drafted"]), "rounds": int(s["rounds"])}
+    eng.set_gate(0.45, 24)  # the natural drafter runs under the reference's default gate
     eng.set_decode_options(draft_k=VERIFY_WIDTH)
     eng.generate(prompt, GEN_LEN)
     s = eng.stats()
@@ -238,7 +250,7 @@ def run_b200(args, rank, world):
         "ms_per_step": dec_ms / args.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
         "dtype": "int4-g64 weights, fp32 activations/accumulation, fp16 KV", "data": "synthetic",
         "config": {"workload": "config3: 31B-shaped target + E2B-shaped drafter, greedy speculative decode k=4 "
-                               "(verify width 5), oracle drafter at mismatch rate 0.25",
+                               "(verify width 5), oracle drafter at mismatch rate 0.25, adaptive gate off",
                    "prompt_tokens": PROMPT_LEN, "generated_tokens": GEN_LEN, "kv_context": 4096,
                    "parallelism": f"tp{world}", "weights_gb": 17.3,
                    "l2": "each verify pass streams 17.3 GB of weights, > 126 MB L2"},

@@ -1,0 +1,46 @@
+"""One rank of the tensor-parallel parity test (launched by test_tp.py under torchrun).
+
+argv: target container, drafter container ("-" for none), verify width, prompt length,
+tokens to generate, output directory. Writes rank<r>.json with the greedy stream and the
+per-round records."""
+import json
+import os
+import sys
+from pathlib import Path
+
+REPO = Path(__file__).resolve().parent.parent
+sys.path[:0] = [str(REPO), str(REPO / "turbo-winfare-dense_b200")]
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+import torch.distributed as dist  # noqa: E402
+
+
+def main():
+    target, draft, width, plen, n, out = sys.argv[1:7]
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    import datetime
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120))
+    from g4dense_b200 import Engine
+    from g4dense_b200.api import lib
+    buf = np.zeros(128, np.uint8)
+    if rank == 0:
+        lib().g4dense_nccl_unique_id(buf.ctypes.data)
+    t = torch.from_numpy(buf).cuda()
+    dist.broadcast(t, 0)
+    nid = t.cpu().numpy().tobytes()
+    e = Engine(target=target, draft=None if draft == "-" else draft, draft_k=int(width) if draft != "-" else 0,
+               tp_rank=rank, tp_size=world, nccl_id=nid, device=local)
+    prompt = np.random.default_rng(0).integers(0, 4096, int(plen))
+    toks = e.generate(prompt, int(n))
+    rounds = e.rounds()
+    e.close()
+    Path(out, f"rank{rank}.json").write_text(json.dumps({"tokens": toks.tolist(), "rounds": rounds}))
+    dist.barrier()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -25,8 +25,9 @@ __device__ __forceinline__ bool better(float v, uint32_t i, float bv, uint32_t b
     return v > bv || (v == bv && i < bi);
 }
 
+// chunk_best[m][chunk] = {best softcapped logit, its GLOBAL vocabulary index (v + v_off)}.
 __global__ void head_chunks_kernel(GemmOut lm, int V, int M, float softcap, float* logits, int ldl,
-                                   float2* chunk_best) {
+                                   float2* chunk_best, int v_off) {
     __shared__ float sv[32];
     __shared__ uint32_t si[32];
     pdl_enter();
@@ -64,7 +65,8 @@ __global__ void head_chunks_kernel(GemmOut lm, int V, int M, float softcap, floa
             float zz = z[j];
             if (softcap > 0.f) zz = softcap * tanhf(zz / softcap);
             if (logits) logits[(size_t)m * ldl + v] = zz;
-            if (better(zz, (uint32_t)v, bv, bi)) { bv = zz; bi = (uint32_t)v; }
+            const uint32_t gv = (uint32_t)(v + v_off);
+            if (better(zz, gv, bv, bi)) { bv = zz; bi = gv; }
         }
     }
 #pragma unroll
@@ -83,7 +85,9 @@ __global__ void head_chunks_kernel(GemmOut lm, int V, int M, float softcap, floa
     }
 }
 
-__global__ void head_finalize_kernel(const float2* chunk_best, int nchunks, int M, StepParams* sp,
+// chunk_best is [nranks][M][nchunks] (one slice per tensor-parallel rank's vocabulary range);
+// the order is total (value, then lowest index), so the result does not depend on the split.
+__global__ void head_finalize_kernel(const float2* chunk_best, int nchunks, int nranks, int M, StepParams* sp,
                                      HeadResult* res, uint32_t* chain_out) {
     __shared__ uint32_t am[16];
     pdl_enter();
@@ -91,8 +95,9 @@ __global__ void head_finalize_kernel(const float2* chunk_best, int nchunks, int 
     if (m < M) {
         float bv = -INFINITY;
         uint32_t bi = 0xFFFFFFFFu;
-        for (int c = lane; c < nchunks; c += 32) {
-            const float2 e = chunk_best[(size_t)m * nchunks + c];
+        for (int c = lane; c < nranks * nchunks; c += 32) {
+            const int r = c / nchunks;
+            const float2 e = chunk_best[((size_t)r * M + m) * nchunks + c % nchunks];
             const uint32_t i = __float_as_uint(e.y);
             if (better(e.x, i, bv, bi)) { bv = e.x; bi = i; }
         }
@@ -129,15 +134,15 @@ using namespace g4b;
 int g4b_head_chunks(int V) { return (V + kHeadChunk - 1) / kHeadChunk; }
 
 cudaError_t g4b_head_chunks_launch(const GemmOut& lm, int V, int M, float softcap, float* logits, int ldl,
-                                   float2* chunk_best, cudaStream_t st, bool pdl) {
+                                   float2* chunk_best, int v_off, cudaStream_t st, bool pdl) {
     // 256 threads, one column per thread per 256-wide block: blocks must align to row groups.
     static_assert(kHeadChunk % 256 == 0, "head chunk");
     return launch(head_chunks_kernel, dim3(g4b_head_chunks(V), M), dim3(256), 0, st, pdl, lm, V, M, softcap, logits,
-                  ldl, chunk_best);
+                  ldl, chunk_best, v_off);
 }
 
-cudaError_t g4b_head_finalize(const float2* chunk_best, int nchunks, int M, StepParams* sp, HeadResult* res,
-                              uint32_t* chain_out, cudaStream_t st, bool pdl) {
-    return launch(head_finalize_kernel, dim3(1), dim3(32 * 16), 0, st, pdl, chunk_best, nchunks, M, sp, res,
+cudaError_t g4b_head_finalize(const float2* chunk_best, int nchunks, int nranks, int M, StepParams* sp,
+                              HeadResult* res, uint32_t* chain_out, cudaStream_t st, bool pdl) {
+    return launch(head_finalize_kernel, dim3(1), dim3(32 * 16), 0, st, pdl, chunk_best, nchunks, nranks, M, sp, res,
                   chain_out);
 }

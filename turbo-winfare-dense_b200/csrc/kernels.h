@@ -39,11 +39,13 @@ struct HeadResult {
     uint32_t argmax[16]; // per-row greedy target token
 };
 int g4b_head_chunks(int V);
-// Softcapped logits (written when `logits` is non-null) and per-chunk (max, index).
+// Softcapped logits (written when `logits` is non-null) and per-chunk (max, global index =
+// local index + v_off) into chunk_best [M][chunks].
 cudaError_t g4b_head_chunks_launch(const g4b::GemmOut& lm, int V, int M, float softcap, float* logits, int ldl,
-                                   float2* chunk_best, cudaStream_t st, bool pdl);
+                                   float2* chunk_best, int v_off, cudaStream_t st, bool pdl);
 // Per-row argmax (ties to the lowest index) and greedy acceptance of sp->tokens[1..M-1]
 // against argmax[0..M-2]. With chain_out (drafter steps) the last row's argmax also becomes
 // the next pass's input: sp->tokens[0] = t, sp->base_pos += M, chain_out[sp->draft_step++] = t.
-cudaError_t g4b_head_finalize(const float2* chunk_best, int nchunks, int M, g4b::StepParams* sp, HeadResult* res,
-                              uint32_t* chain_out, cudaStream_t st, bool pdl);
+// chunk_best holds nranks slices [M][nchunks] (tensor-parallel vocabulary ranges).
+cudaError_t g4b_head_finalize(const float2* chunk_best, int nchunks, int nranks, int M, g4b::StepParams* sp,
+                              HeadResult* res, uint32_t* chain_out, cudaStream_t st, bool pdl);

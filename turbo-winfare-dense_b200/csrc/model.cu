@@ -601,11 +601,21 @@ void DeviceModel::enqueue_raw(int M, PassKind kind, bool want_logits, uint32_t* 
     // LM head
     gemm(lm_, bf_d_, M, nullptr);
     const GemmOut lo = partials(lm_, M);
+    // Under tensor parallelism each rank ranks its own vocabulary slice; the per-chunk bests
+    // (global indices) are all-gathered and every rank finalizes the same argmax.
     const int nch = g4b_head_chunks(v_local_);
+    const size_t slice = (size_t)M * nch;
+    float2* mine = chunk_best_ + (size_t)opt_.rank * slice;
     cuda_check(g4b_head_chunks_launch(lo, v_local_, M, h_.final_logit_softcapping, want_logits ? logits_ : nullptr,
-                                      v_local_, chunk_best_, stream_, pdl),
+                                      v_local_, mine, v_off_, stream_, pdl),
                "head_chunks");
-    cuda_check(g4b_head_finalize(chunk_best_, nch, M, sp, res_dev_, chain_out, stream_, pdl), "head_finalize");
+#ifdef G4B_HAVE_NCCL
+    if (opt_.tp > 1 && ncclAllGather(mine, chunk_best_, slice * 2, ncclFloat, (ncclComm_t)opt_.nccl_comm, stream_) !=
+                           ncclSuccess)
+        throw std::runtime_error("ncclAllGather (LM head) failed");
+#endif
+    cuda_check(g4b_head_finalize(chunk_best_, nch, opt_.tp, M, sp, res_dev_, chain_out, stream_, pdl),
+               "head_finalize");
 }
 
 void DeviceModel::enqueue(int M, PassKind kind, bool want_logits, uint32_t* chain_out) {
