@@ -238,10 +238,12 @@ def run_b200(args, rank, world):
     ms, gbytes, glaunch = eng.profile_gemms(VERIFY_WIDTH, reps=5)
     achieved = gbytes / (ms / 1000.0) / 1e9
     peak, peak_kind = peaks()
-    traffic = None
-    tf = REPO / "profiles" / "vgemm_traffic.json"
+    traffic = None  # DRAM bytes per 5-row pass from the committed ncu summary
+    tf = REPO / "profiles" / "vgemm_31b_shapes_m5.md"
     if tf.exists():
-        traffic = json.loads(tf.read_text()).get("dram_bytes_per_launch")
+        for ln in tf.read_text().splitlines():
+            if ln.startswith("traffic_bytes_per_pass:"):
+                traffic = int(ln.split(":")[1])
 
     if rank != 0:
         return 0
@@ -260,6 +262,8 @@ def run_b200(args, rank, world):
         "roofline": {"bound": "hbm", "kernel": "vgemm (verify GEMM, M=5)", "achieved": achieved, "peak": peak,
                      "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak, "traffic": traffic,
                      "algorithmic_bytes_per_pass": gbytes, "launches_per_pass": glaunch,
+                     "traffic_per": "pass (sum of dram__bytes_read+write over the pass's GEMM launches, ncu; "
+                                    "profiles/vgemm_31b_shapes_m5.md)",
                      "ms_per_pass": ms},
         "acceptance_sweep": sweep,
         "autoregressive_tok_s": ar_tok_s,

@@ -1,0 +1,100 @@
+"""Profiling drivers: run one piece of the hot path inside a CUDA profiler range so an external
+profiler started with `--profile-from-start off` sees exactly that piece.
+
+    python -m g4dense_b200.profile pass  --which target|draft --batch M --pos P
+        one forward pass of the 31B-shaped target (or the E2B-shaped drafter) with M rows at
+        positions P..P+M-1 (attention spans P earlier cache entries), after 5 timed warm
+        passes; prints their mean CUDA-event time.
+    python -m g4dense_b200.profile gemms [--only NAME] [--batch M]
+        each distinct verify-GEMM shape of the 31B pass once (the kernel as the pass runs it:
+        split-K slots left for the consuming epilogue), through the g4b_qmat C-ABI.
+
+Synthetic weights; nothing here is on the product path."""
+from __future__ import annotations
+
+import argparse
+import ctypes
+import json
+import sys
+
+import numpy as np
+
+# (name, N, K) of every distinct verify GEMM in a Gemma-4-31B pass (50 sliding + 10 global
+# layers + the tied LM head).
+GEMM_SHAPES = [("qkv_sliding", 16384, 5376), ("qkv_global", 18432, 5376), ("o_sliding", 5376, 8192),
+               ("o_global", 5376, 16384), ("gateup", 43008, 5376), ("down", 5376, 21504),
+               ("lm_head", 262144, 5376)]
+# Launches of each shape per pass.
+GEMM_COUNTS = {"qkv_sliding": 50, "qkv_global": 10, "o_sliding": 50, "o_global": 10, "gateup": 60, "down": 60,
+               "lm_head": 1}
+
+
+def _profiler():
+    cu = ctypes.CDLL("libcuda.so.1")
+    return cu.cuProfilerStart, cu.cuProfilerStop
+
+
+def run_pass(which, batch, pos):
+    from .api import Engine
+    if which == "target":
+        e = Engine(preset="gemma4-31b", seed=0, max_context=4096, device=0)
+    else:
+        e = Engine(preset="gemma4-e2b", seed=1, max_context=4096, device=0)
+    ms = e.time_pass(0, batch, 5, pos=pos)
+    start, stop = _profiler()
+    start()
+    e.time_pass(0, batch, 1, pos=pos)
+    stop()
+    e.close()
+    print(json.dumps({"which": which, "batch": batch, "pos": pos, "ms_per_pass": ms}))
+
+
+def run_gemms(only, batch):
+    import torch
+    from .api import QMat
+    rng = np.random.default_rng(0)
+    mats = []
+    for name, N, K in GEMM_SHAPES:
+        if only and name != only:
+            continue
+        W = torch.from_numpy(rng.integers(0, 2**32, (N, K // 8), dtype=np.uint32).view(np.int32)).cuda()
+        S = torch.full((N, K // 64), 0x3C00, dtype=torch.int16, device="cuda")
+        B = torch.zeros((N, K // 64), dtype=torch.int16, device="cuda")
+        q = QMat(W, S, B)
+        del W, S, B
+        x = torch.randn(batch, K, device="cuda")
+        y = torch.empty(batch, N, device="cuda")
+        q.gemm(x, y)
+        mats.append((name, q))
+    torch.cuda.synchronize()
+    start, stop = _profiler()
+    start()
+    for _, q in mats:
+        q.run_partial(batch)
+    torch.cuda.synchronize()
+    stop()
+    for _, q in mats:
+        q.check_error()
+    print(json.dumps({"gemms": [n for n, _ in mats], "batch": batch}))
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser(prog="python -m g4dense_b200.profile")
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    p = sub.add_parser("pass")
+    p.add_argument("--which", choices=["target", "draft"], default="target")
+    p.add_argument("--batch", type=int, default=5)
+    p.add_argument("--pos", type=int, default=768)
+    g = sub.add_parser("gemms")
+    g.add_argument("--only", default=None)
+    g.add_argument("--batch", type=int, default=5)
+    a = ap.parse_args(argv)
+    if a.cmd == "pass":
+        run_pass(a.which, a.batch, a.pos)
+    else:
+        run_gemms(a.only, a.batch)
+    return 0
+
+
+if __name__ == "__main__":
+    sys.exit(main())
