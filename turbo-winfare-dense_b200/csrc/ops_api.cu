@@ -3,6 +3,7 @@
 #include "g4dense_b200_ops.h"
 
 #include <cstdio>
+#include <mutex>
 #include <string>
 
 #include "common.cuh"
@@ -117,6 +118,73 @@ int g4b_qmat_run(g4b_qmat* q, int M, float* out, int ldo, void* stream) {
     p.cnt = q->cnt;
     cudaError_t e = vgemm_launch(p, (cudaStream_t)stream, false);
     return e == cudaSuccess ? 0 : fail(e, "vgemm_launch");
+}
+
+// ---------------------------------------------------------------- allocation-free run
+
+namespace {
+// Library-owned split-K scratch of g4b_qmat_run_noalloc: 8 MiB of partial slots and one
+// arrival counter per 256-row group. Static device memory is part of the module image, so
+// using it allocates nothing at call time.
+constexpr size_t kNoAllocPartFloats = (size_t)2 << 20;  // 8 MiB
+constexpr int kNoAllocCounters = 4096;                 // N <= 4096 * 256 rows
+__device__ __align__(256) float g_noalloc_part[kNoAllocPartFloats];
+__device__ __align__(256) unsigned g_noalloc_cnt[kNoAllocCounters];
+
+struct NoAllocScratch {
+    float* part = nullptr;
+    unsigned* cnt = nullptr;
+};
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+NoAllocScratch g_noalloc[kMaxDevices];  // symbol addresses, looked up once per device
+}  // namespace
+
+int g4b_qmat_run_noalloc(g4b_qmat* q, int M, float* out, int ldo, void* stream) {
+    if (!q || !out || M < 1 || M > g4b::kMaxM || ldo < q->N) return fail_msg("g4b_qmat_run_noalloc: bad arguments");
+    int dev = 0;
+    cudaError_t e = cudaGetDevice(&dev);
+    if (e != cudaSuccess) return fail(e, "g4b_qmat_run_noalloc: cudaGetDevice");
+    if (dev < 0 || dev >= kMaxDevices) return fail_msg("g4b_qmat_run_noalloc: device ordinal out of range");
+    NoAllocScratch sc;
+    {
+        std::lock_guard<std::mutex> lock(g_noalloc_mu);
+        NoAllocScratch& slot = g_noalloc[dev];
+        if (!slot.part) {
+            void* part = nullptr;
+            void* cnt = nullptr;
+            if ((e = cudaGetSymbolAddress(&part, g_noalloc_part)) != cudaSuccess ||
+                (e = cudaGetSymbolAddress(&cnt, g_noalloc_cnt)) != cudaSuccess)
+                return fail(e, "g4b_qmat_run_noalloc: cudaGetSymbolAddress");
+            slot.part = static_cast<float*>(part);
+            slot.cnt = static_cast<unsigned*>(cnt);
+        }
+        sc = slot;
+    }
+    VgemmParams p = qmat_params(q, M);
+    // Exactly the slots this launch needs (the matrix's own workspace is sized for every M).
+    const int slots = vgemm_max_slots(p.out.grid, q->n_crg, q->ktiles);
+    const size_t need = (size_t)q->n_crg * slots * g4b::kMaxM * 256;
+    if (need > kNoAllocPartFloats || q->n_crg > kNoAllocCounters) {
+        char msg[256];
+        std::snprintf(msg, sizeof msg,
+                      "g4b_qmat_run_noalloc: this matrix needs %.1f MiB of split-K scratch at M = %d (%d row groups x "
+                      "%d slots); the static buffer holds 8 MiB and %d row groups -- use g4b_qmat_run",
+                      need * 4.0 / (1 << 20), M, q->n_crg, slots, kNoAllocCounters);
+        return fail_msg(msg);
+    }
+    p.out.part = sc.part;
+    p.out.max_slots = slots;
+    p.y = out;
+    p.ldy = ldo;
+    p.cnt = sc.cnt;
+    const cudaStream_t st = (cudaStream_t)stream;
+    // The arrival counters must start at zero; a complete launch leaves them at zero, a failed
+    // one may not, so they are cleared on the stream first.
+    if ((e = cudaMemsetAsync(sc.cnt, 0, (size_t)q->n_crg * sizeof(unsigned), st)) != cudaSuccess)
+        return fail(e, "g4b_qmat_run_noalloc: clearing counters");
+    e = vgemm_launch(p, st, false);
+    return e == cudaSuccess ? 0 : fail(e, "g4b_qmat_run_noalloc: vgemm_launch");
 }
 
 int g4b_qmat_gemm(g4b_qmat* q, const float* x, int ldx, int M, float* out, int ldo, void* stream) {

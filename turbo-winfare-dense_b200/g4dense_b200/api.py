@@ -30,6 +30,7 @@ def lib():
         L.g4b_qmat_run.argtypes = [_vp, ctypes.c_int, _vp, ctypes.c_int, _vp]
         L.g4b_qmat_info.argtypes = [_vp, _vp]
         L.g4b_qmat_run_partial.argtypes = [_vp, ctypes.c_int, _vp]
+        L.g4b_qmat_run_noalloc.argtypes = [_vp, ctypes.c_int, _vp, ctypes.c_int, _vp]
         L.g4b_qmat_check_error.argtypes = [_vp]
         _bind_engine(L)
         _lib = L
@@ -123,6 +124,11 @@ class QMat:
 
     def run(self, M, out, stream=None):
         _check(lib().g4b_qmat_run(self.h, M, _dptr(out), out.shape[1], _stream(stream)), "g4b_qmat_run")
+
+    def run_noalloc(self, M, out, stream=None):
+        """g4b_qmat_run with the library's static split-K scratch (allocates nothing)."""
+        _check(lib().g4b_qmat_run_noalloc(self.h, M, _dptr(out), out.shape[1], _stream(stream)),
+               "g4b_qmat_run_noalloc")
 
     def run_partial(self, M, stream=None):
         _check(lib().g4b_qmat_run_partial(self.h, M, _stream(stream)), "g4b_qmat_run_partial")
