@@ -3,16 +3,18 @@
 // head's query heads (the reference dispatches one group per (row, query head), re-reading
 // the cache M * q_heads/kv_heads times).
 //
-// Grid: one thread-block cluster of kSplits CTAs per (KV head, chunk of 16 query rows); CTA r
-// of the cluster takes the r-th share of the batch's key range. Per 32-key tile (K and V
-// double-buffered in shared memory by cp.async):
-//   * S = Q K^T on the tensor cores (mma.sync m16n8k16, fp32 accumulate). The cached K is
-//     exact in the MMA's input type (FP16, or bf16 in long-context mode); the fp32 query is
-//     split into 2 (FP16) or 3 (bf16) terms q = q1 + q2 (+ q3) after a power-of-two row
-//     scaling, so the scores carry the fp32 query's precision. Warp w computes keys 8w..8w+7;
-//   * an online softmax per row (running max / sum in fp32, exp of the fp32 scores);
-//   * O += P V on the tensor cores with P (scaled by 2^14) split the same way; warp w owns
-//     columns [w*hd/4, (w+1)*hd/4) of the output.
+// Grid: one thread-block cluster of S CTAs per (KV head, chunk of 16 query rows); CTA r of the
+// cluster takes the r-th share of the batch's key range, in 64-key tiles. S (16, 12 or 8) is
+// the largest size whose clusters all fit on the GPU at once (one wave). Per tile:
+//   * K and V land in shared memory by cp.async;
+//   * S = Q K^T on the tensor cores (mma.sync m16n8k16, fp32 accumulate), warp w taking keys
+//     8w..8w+7. The cached K is exact in the MMA's input type (FP16, or bf16 in long-context
+//     mode); the fp32 query is split into 2 (FP16) or 3 (bf16) terms q = q1 + q2 (+ q3) after
+//     a power-of-two row scaling, so the scores carry the fp32 query's precision;
+//   * an online softmax per row (running max / sum in fp32, exp of the fp32 scores), warp w
+//     taking rows 2w, 2w+1;
+//   * O += P V on the tensor cores with P (scaled by 2^14) split the same way, warp w owning
+//     columns [w*hd/8, (w+1)*hd/8) of the output.
 // The cluster's partial results are then combined through distributed shared memory and
 // written directly as the o-projection's B fragments.
 //
@@ -33,14 +35,15 @@ namespace cg = cooperative_groups;
 
 namespace g4b {
 
-constexpr int kAttnKeys = 32;  // keys per tile
+constexpr int kAttnKeys = 64;  // keys per tile
 constexpr int kAttnRows = 16;  // query rows per CTA (the MMA's M)
-constexpr int kAttnWarps = 4;
+constexpr int kAttnWarps = 8;
 constexpr int kAttnThreads = kAttnWarps * 32;
-constexpr int kSplits = 8;               // CTAs per cluster = key splits
 constexpr int kPStride = kAttnKeys + 8;  // halves per P row (conflict-free ldmatrix)
 constexpr int kSStride = kAttnKeys + 4;  // floats per S row
 constexpr float kPScale = 16384.0f;      // P is split after scaling by 2^14
+
+constexpr int kMaxSplits = 16;  // largest cluster (non-portable size; B200 allows 16)
 
 template <bool BF16>
 struct AttnTypes;
@@ -86,6 +89,10 @@ __device__ __forceinline__ void ldsm_x4_t(uint32_t (&r)[4], const void* p) {
                  : "=r"(r[0]), "=r"(r[1]), "=r"(r[2]), "=r"(r[3])
                  : "r"(s));
 }
+__device__ __forceinline__ void ldsm_x2_t(uint32_t& r0, uint32_t& r1, const void* p) {
+    const uint32_t s = (uint32_t)__cvta_generic_to_shared(p);
+    asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(s));
+}
 __device__ __forceinline__ void cp16(void* smem, const void* gmem) {
     const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem));
@@ -94,18 +101,19 @@ __device__ __forceinline__ void cp16(void* smem, const void* gmem) {
 // Shared memory plan (KS = hd + 8 halves per Q/K/V row: conflict-free ldmatrix rows).
 struct AttnSmem {
     uint16_t* q;     // [terms][16][KS]
-    uint16_t* kv;    // 2 buffers x {K [32][KS], V [32][KS]}
+    uint16_t* k;     // [64][KS]
+    uint16_t* v;     // [64][KS]
     uint16_t* p;     // [terms][16][kPStride]
     float* s;        // [16][kSStride]
     float* corr;     // [16]
     float* qscale;   // [16] 2^-e of the row's query scaling
     float2* ml;      // [16] {running max, running sum}
-    float* o;        // [16][hd] partial output after the key loop (aliases the K/V tiles)
+    float* o;        // [16][hd] partial output after the key loop (aliases the K/V tile)
 };
 
 inline size_t attn_smem_bytes(int hd, int terms) {
     const size_t ks = hd + 8;
-    return (size_t)terms * kAttnRows * ks * 2 + 4 * (size_t)kAttnKeys * ks * 2 +
+    return (size_t)terms * kAttnRows * ks * 2 + 2 * (size_t)kAttnKeys * ks * 2 +
            (size_t)terms * kAttnRows * kPStride * 2 + kAttnRows * kSStride * 4 + kAttnRows * 4 * 2 + kAttnRows * 8;
 }
 
@@ -115,9 +123,10 @@ __device__ __forceinline__ AttnSmem attn_smem(unsigned char* raw, int hd, int te
     uint16_t* h = reinterpret_cast<uint16_t*>(raw);
     s.q = h;
     h += terms * kAttnRows * ks;
-    s.kv = h;
-    s.o = reinterpret_cast<float*>(h);  // 16 * hd * 4 bytes <= 4 * 32 * ks * 2
-    h += 4 * kAttnKeys * ks;
+    s.k = h;
+    s.v = h + kAttnKeys * ks;
+    s.o = reinterpret_cast<float*>(h);  // 16 * hd * 4 bytes <= 2 * 64 * ks * 2
+    h += 2 * kAttnKeys * ks;
     s.p = h;
     h += terms * kAttnRows * kPStride;
     s.s = reinterpret_cast<float*>(h);
@@ -128,12 +137,14 @@ __device__ __forceinline__ AttnSmem attn_smem(unsigned char* raw, int hd, int te
 }
 
 template <bool BF16, int HD>
-__global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnArgs a, void* bfrag) {
+__global__ void __launch_bounds__(kAttnThreads, HD <= 256 ? 2 : 1) attention_kernel(AttnArgs a, void* bfrag) {
     using Ty = AttnTypes<BF16>;
     constexpr int kTerms = Ty::kTerms;
     constexpr int KS = HD + 8;
     constexpr int kColsPerWarp = HD / kAttnWarps;  // PV output columns per warp
     constexpr int kNT = kColsPerWarp / 8;          // PV n-tiles per warp
+    constexpr int kChunks = HD / 8;                // 16-byte chunks per K/V row
+    constexpr int kKeyStep = kAttnThreads / kChunks;
     extern __shared__ __align__(16) unsigned char smem_raw[];
     __shared__ __half stage[kAttnWarps][128];
     cg::cluster_group cluster = cg::this_cluster();
@@ -141,6 +152,7 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnArgs a, voi
 
     pdl_enter();
     const int split = (int)cluster.block_rank();
+    const int nsplit = (int)cluster.num_blocks();
     const int kvh_i = blockIdx.y, chunk = blockIdx.z;
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
     const int g = lane >> 2, t4 = lane & 3;
@@ -151,17 +163,22 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnArgs a, voi
     // Key range of the whole batch, then this split's share.
     const int kmin = a.window ? max(0, base + 1 - a.window) : 0;
     const int kmax = base + a.M;
-    const int per = (kmax - kmin + kSplits - 1) / kSplits;
+    const int per = (kmax - kmin + nsplit - 1) / nsplit;
     const int ks = kmin + split * per, ke = min(kmax, ks + per);
 
-    auto load_tile = [&](int t0, int buf) {
+    // Each thread copies one 16-byte column chunk c8 of keys j0, j0 + kKeyStep, ...
+    const int c8 = threadIdx.x % kChunks, j0 = threadIdx.x / kChunks;
+    const size_t head_off = (size_t)kvh_i * HD + c8 * 8;
+    auto load_tile = [&](int t0) {
         const int nt = min(kAttnKeys, ke - t0);
-        for (int i = threadIdx.x; i < kAttnKeys * (HD / 8); i += kAttnThreads) {
-            const int j = i / (HD / 8), c8 = i % (HD / 8);
-            uint16_t* kd = sm.kv + (2 * buf * kAttnKeys + j) * KS + c8 * 8;
-            uint16_t* vd = kd + kAttnKeys * KS;
+        const int slot0 = t0 % a.cap;
+        for (int j = j0; j < kAttnKeys; j += kKeyStep) {
+            uint16_t* kd = sm.k + j * KS + c8 * 8;
+            uint16_t* vd = sm.v + j * KS + c8 * 8;
             if (j < nt) {
-                const size_t src = ((size_t)((t0 + j) % a.cap) * a.kvh + kvh_i) * HD + c8 * 8;
+                int slot = slot0 + j;
+                if (slot >= a.cap) slot %= a.cap;
+                const size_t src = (size_t)slot * a.kvh * HD + head_off;
                 cp16(kd, a.k_ring + src);
                 cp16(vd, a.v_ring + src);
             } else {  // keys past the range: zeros, so P = 0 meets finite V
@@ -171,12 +188,13 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnArgs a, voi
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
-    if (ks < ke) load_tile(ks, 0);
+    if (ks < ke) load_tile(ks);
 
-    // Stage the query rows: warp w takes rows 4w..4w+3. Scaling by 2^(15-e) puts the row's
+    // Stage the query rows: warp w takes rows 2w, 2w+1. Scaling by 2^(15-e) puts the row's
     // max |q| in [2^14, 2^15); the scaled row is then split into terms of the MMA type.
-    for (int rr = 0; rr < 4; ++rr) {
-        const int r = warp * 4 + rr;
+#pragma unroll
+    for (int rr = 0; rr < 2; ++rr) {
+        const int r = warp * 2 + rr;
         const int qr = chunk * kAttnRows + r;
         float x[HD / 32];
         float amax = 0.f;
@@ -206,14 +224,14 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnArgs a, voi
             }
         }
     }
-    // Softmax state: warp w owns rows 4w..4w+3 (every lane keeps the same copy).
-    float m_run[4], l_run[4];
-    int row_lo[4], row_hi[4];
+    // Softmax state: warp w owns rows 2w, 2w+1 (every lane keeps the same copy).
+    float m_run[2], l_run[2];
+    int row_lo[2], row_hi[2];
 #pragma unroll
-    for (int rr = 0; rr < 4; ++rr) {
+    for (int rr = 0; rr < 2; ++rr) {
         m_run[rr] = -INFINITY;
         l_run[rr] = 0.f;
-        const int qr = chunk * kAttnRows + warp * 4 + rr;
+        const int qr = chunk * kAttnRows + warp * 2 + rr;
         if (qr < R) {
             const int end = base + qr / gqa + 1;
             row_hi[rr] = end;
@@ -226,16 +244,14 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnArgs a, voi
 #pragma unroll
     for (int n = 0; n < kNT; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
 
-    int buf = 0;
-    for (int t0 = ks; t0 < ke; t0 += kAttnKeys, buf ^= 1) {
+    for (int t0 = ks; t0 < ke; t0 += kAttnKeys) {
         asm volatile("cp.async.wait_group 0;" ::: "memory");
-        __syncthreads();  // tile t0 (and the staged q) visible; every warp is past the last PV
-        if (t0 + kAttnKeys < ke) load_tile(t0 + kAttnKeys, buf ^ 1);
+        __syncthreads();  // tile t0 (and the staged q) visible
 
         // S[16 rows][keys 8w..8w+7] = sum over terms of Q_t K^T.
         {
             float s[4] = {0.f, 0.f, 0.f, 0.f};
-            const uint16_t* kb = sm.kv + (2 * buf * kAttnKeys + warp * 8 + (lane & 7)) * KS + (lane >> 3) * 8;
+            const uint16_t* kb = sm.k + (warp * 8 + (lane & 7)) * KS + (lane >> 3) * 8;
             const uint16_t* qb = sm.q + (lane & 15) * KS + (lane >> 4) * 8;
 #pragma unroll 4
             for (int k0 = 0; k0 < HD; k0 += 32) {
@@ -258,27 +274,36 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnArgs a, voi
         }
         __syncthreads();
 
-        // Online softmax: lane = key of the tile.
+        // Online softmax: keys lane and lane + 32 of the tile.
 #pragma unroll
-        for (int rr = 0; rr < 4; ++rr) {
-            const int r = warp * 4 + rr;
-            const int tk = t0 + lane;
-            const bool valid = lane < ke - t0 && tk >= row_lo[rr] && tk < row_hi[rr];
-            const float sc = valid ? sm.s[r * kSStride + lane] * sm.qscale[r] * a.scale : -INFINITY;
-            const float m_new = fmaxf(m_run[rr], warp_max(sc));
-            float p = 0.f, corr = 1.f;
+        for (int rr = 0; rr < 2; ++rr) {
+            const int r = warp * 2 + rr;
+            float sc[2];
+            bool valid[2];
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                const int kl = lane + 32 * h, tk = t0 + kl;
+                valid[h] = tk < ke && tk >= row_lo[rr] && tk < row_hi[rr];
+                sc[h] = valid[h] ? sm.s[r * kSStride + kl] * sm.qscale[r] * a.scale : -INFINITY;
+            }
+            const float m_new = fmaxf(m_run[rr], warp_max(fmaxf(sc[0], sc[1])));
+            float p[2] = {0.f, 0.f}, corr = 1.f;
             if (m_new != -INFINITY) {
-                p = valid ? expf(sc - m_new) : 0.f;
+                p[0] = valid[0] ? expf(sc[0] - m_new) : 0.f;
+                p[1] = valid[1] ? expf(sc[1] - m_new) : 0.f;
                 corr = expf(m_run[rr] - m_new);  // 0 on the first contributing tile
             }
-            l_run[rr] = l_run[rr] * corr + warp_sum(p);
+            l_run[rr] = l_run[rr] * corr + warp_sum(p[0] + p[1]);
             m_run[rr] = m_new;
-            float rem = p * kPScale;
 #pragma unroll
-            for (int tt = 0; tt < kTerms; ++tt) {
-                const uint16_t b = Ty::to_bits(rem);
-                sm.p[(tt * kAttnRows + r) * kPStride + lane] = b;
-                rem -= Ty::from_bits(b);
+            for (int h = 0; h < 2; ++h) {
+                float rem = p[h] * kPScale;
+#pragma unroll
+                for (int tt = 0; tt < kTerms; ++tt) {
+                    const uint16_t b = Ty::to_bits(rem);
+                    sm.p[(tt * kAttnRows + r) * kPStride + lane + 32 * h] = b;
+                    rem -= Ty::from_bits(b);
+                }
             }
             if (lane == 0) sm.corr[r] = corr;
         }
@@ -300,23 +325,32 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnArgs a, voi
 #pragma unroll
                 for (int tt = 0; tt < kTerms; ++tt)
                     ldsm_x4(pa[tt], sm.p + (tt * kAttnRows + (lane & 15)) * kPStride + kk + (lane >> 4) * 8);
-                const uint16_t* vb = sm.kv + ((2 * buf + 1) * kAttnKeys + kk + (lane & 7) + ((lane >> 3) & 1) * 8) * KS +
-                                     warp * kColsPerWarp + (lane >> 4) * 8;
+                if constexpr (kNT == 1) {
+                    uint32_t b0, b1;
+                    ldsm_x2_t(b0, b1, sm.v + (kk + (lane & 7) + ((lane >> 3) & 1) * 8) * KS + warp * kColsPerWarp);
 #pragma unroll
-                for (int n = 0; n < kNT; n += 2) {
-                    uint32_t b[4];
-                    ldsm_x4_t(b, vb + n * 8);  // n-tiles n and n + 1
+                    for (int tt = 0; tt < kTerms; ++tt) mma_tc<BF16>(acc[0], pa[tt], b0, b1);
+                } else {
+                    const uint16_t* vb = sm.v + (kk + (lane & 7) + ((lane >> 3) & 1) * 8) * KS + warp * kColsPerWarp +
+                                         (lane >> 4) * 8;
 #pragma unroll
-                    for (int tt = 0; tt < kTerms; ++tt) {
-                        mma_tc<BF16>(acc[n], pa[tt], b[0], b[1]);
-                        mma_tc<BF16>(acc[n + 1], pa[tt], b[2], b[3]);
+                    for (int n = 0; n < kNT; n += 2) {
+                        uint32_t b[4];
+                        ldsm_x4_t(b, vb + n * 8);  // n-tiles n and n + 1
+#pragma unroll
+                        for (int tt = 0; tt < kTerms; ++tt) {
+                            mma_tc<BF16>(acc[n], pa[tt], b[0], b[1]);
+                            mma_tc<BF16>(acc[n + 1], pa[tt], b[2], b[3]);
+                        }
                     }
                 }
             }
         }
+        __syncthreads();  // the tile buffers are refilled next
+        if (t0 + kAttnKeys < ke) load_tile(t0 + kAttnKeys);
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
-    __syncthreads();  // every warp is done with the K/V tiles: sm.o may overwrite them
+    __syncthreads();  // every warp is done with the K/V tile: sm.o may overwrite it
 
     // This split's partial result: unnormalised O (P's 2^14 scale removed) and {m, l}.
 #pragma unroll
@@ -327,30 +361,44 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnArgs a, voi
     }
     if (lane == 0)
 #pragma unroll
-        for (int rr = 0; rr < 4; ++rr) sm.ml[warp * 4 + rr] = make_float2(m_run[rr], l_run[rr]);
+        for (int rr = 0; rr < 2; ++rr) sm.ml[warp * 2 + rr] = make_float2(m_run[rr], l_run[rr]);
     cluster.sync();
 
     // Combine across the cluster: out = sum_s e^(m_s - M) O_s / sum_s e^(m_s - M) l_s, one warp
-    // per (row, 64-column group), the items spread over the cluster's CTAs.
+    // per (row, 64-column group), the items spread over the cluster's CTAs. Each warp loads
+    // every split's {m, l} and partial output before combining, so the remote reads overlap.
     constexpr int kGroups = HD / 64;
     const int K = a.qh * HD;
     const BFragView bv = bfrag_view(bfrag, (K + 127) / 128 * 128, a.M);
-    for (int w = split * kAttnWarps + warp; w < kAttnRows * kGroups; w += kSplits * kAttnWarps) {
+    for (int w = split * kAttnWarps + warp; w < kAttnRows * kGroups; w += nsplit * kAttnWarps) {
         const int r = w / kGroups, gi = w % kGroups;
         const int qr = chunk * kAttnRows + r;
         if (qr >= R) continue;  // warp-uniform
+        float2 ml[kMaxSplits];
+#pragma unroll
+        for (int s = 0; s < kMaxSplits; ++s)
+            ml[s] = s < nsplit ? cluster.map_shared_rank(sm.ml, s)[r] : make_float2(-INFINITY, 0.f);
         float mx = -INFINITY;
-        for (int s = 0; s < kSplits; ++s) mx = fmaxf(mx, cluster.map_shared_rank(sm.ml, s)[r].x);
+#pragma unroll
+        for (int s = 0; s < kMaxSplits; ++s) mx = fmaxf(mx, ml[s].x);
         float n0 = 0.f, n1 = 0.f, den = 0.f;
-        for (int s = 0; s < kSplits; ++s) {
-            const float2 ml = cluster.map_shared_rank(sm.ml, s)[r];
-            if (ml.y <= 0.f) continue;
-            const float wgt = expf(ml.x - mx);
-            const float2 op =
-                *reinterpret_cast<const float2*>(cluster.map_shared_rank(sm.o, s) + r * HD + gi * 64 + 2 * lane);
-            n0 += wgt * op.x;
-            n1 += wgt * op.y;
-            den += wgt * ml.y;
+#pragma unroll
+        for (int s0 = 0; s0 < kMaxSplits; s0 += 8) {
+            if (s0 >= nsplit) break;
+            float2 op[8];
+#pragma unroll
+            for (int s = 0; s < 8; ++s)
+                if (s0 + s < nsplit)
+                    op[s] = *reinterpret_cast<const float2*>(cluster.map_shared_rank(sm.o, s0 + s) + r * HD + gi * 64 +
+                                                             2 * lane);
+#pragma unroll
+            for (int s = 0; s < 8; ++s) {
+                if (s0 + s >= nsplit || ml[s0 + s].y <= 0.f) continue;
+                const float wgt = expf(ml[s0 + s].x - mx);
+                n0 += wgt * op[s].x;
+                n1 += wgt * op[s].y;
+                den += wgt * ml[s0 + s].y;
+            }
         }
         const float inv = den > 0.f ? 1.0f / den : 0.f;
         const int m = qr / gqa, qhead = kvh_i * gqa + qr % gqa;
@@ -363,30 +411,65 @@ __global__ void __launch_bounds__(kAttnThreads) attention_kernel(AttnArgs a, voi
 }
 
 template <bool BF16, int HD>
-static cudaError_t launch_attn(const AttnArgs& a, void* bfrag, cudaStream_t st, bool pdl) {
-    const size_t smem = attn_smem_bytes(HD, BF16 ? 3 : 2);
-    static bool attr_set = false;
-    if (!attr_set) {
-        const cudaError_t e = cudaFuncSetAttribute(attention_kernel<BF16, HD>,
-                                                   cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-        if (e != cudaSuccess) return e;
-        attr_set = true;
-    }
+static cudaLaunchConfig_t attn_config(const AttnArgs& a, int splits, cudaStream_t st, cudaLaunchAttribute* attr,
+                                      bool pdl) {
     const int chunks = (a.M * (a.qh / a.kvh) + kAttnRows - 1) / kAttnRows;
     cudaLaunchConfig_t cfg = {};
-    cfg.gridDim = dim3(kSplits, a.kvh, chunks);
+    cfg.gridDim = dim3(splits, a.kvh, chunks);
     cfg.blockDim = dim3(kAttnThreads);
-    cfg.dynamicSmemBytes = smem;
+    cfg.dynamicSmemBytes = attn_smem_bytes(HD, BF16 ? 3 : 2);
     cfg.stream = st;
-    cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = kSplits;
+    attr[0].val.clusterDim.x = splits;
     attr[0].val.clusterDim.y = 1;
     attr[0].val.clusterDim.z = 1;
     attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 2 : 1;
+    return cfg;
+}
+
+// Largest cluster size in {16, 12, 8} whose clusters all fit on the GPU at once; the occupancy
+// query is made once per (kernel, size).
+template <bool BF16, int HD>
+static int attn_splits(int clusters) {
+    static int max_active[3] = {-1, -1, -1};
+    const int sizes[3] = {16, 12, 8};
+    for (int i = 0; i < 3; ++i) {
+        if (max_active[i] < 0) {
+            AttnArgs probe{};
+            probe.M = 1;
+            probe.qh = probe.kvh = 1;
+            cudaLaunchAttribute attr[2];
+            cudaLaunchConfig_t cfg = attn_config<BF16, HD>(probe, sizes[i], nullptr, attr, false);
+            int n = 0;
+            if (cudaOccupancyMaxActiveClusters(&n, attention_kernel<BF16, HD>, &cfg) != cudaSuccess) {
+                cudaGetLastError();
+                n = 0;
+            }
+            max_active[i] = n;
+        }
+        if (max_active[i] >= clusters) return sizes[i];
+    }
+    return 8;
+}
+
+template <bool BF16, int HD>
+static cudaError_t launch_attn(const AttnArgs& a, void* bfrag, cudaStream_t st, bool pdl) {
+    static bool attr_set = false;
+    if (!attr_set) {
+        cudaError_t e = cudaFuncSetAttribute(attention_kernel<BF16, HD>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             (int)attn_smem_bytes(HD, BF16 ? 3 : 2));
+        if (e == cudaSuccess)
+            e = cudaFuncSetAttribute(attention_kernel<BF16, HD>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e != cudaSuccess) return e;
+        attr_set = true;
+    }
+    const int chunks = (a.M * (a.qh / a.kvh) + kAttnRows - 1) / kAttnRows;
+    const int splits = attn_splits<BF16, HD>(a.kvh * chunks);
+    cudaLaunchAttribute attr[2];
+    cudaLaunchConfig_t cfg = attn_config<BF16, HD>(a, splits, st, attr, pdl);
     return cudaLaunchKernelEx(&cfg, attention_kernel<BF16, HD>, a, bfrag);
 }
 

@@ -20,11 +20,8 @@ cudaError_t g4b_qkv_epi(const g4b::QkvEpiArgs& a, cudaStream_t st, bool pdl);
 cudaError_t g4b_geglu(const g4b::GemmOut& gu, int F, void* bfrag, int M, cudaStream_t st, bool pdl);
 // Norm/residual epilogue (post-attention with out_scale = 1, post-FFN with the layer scalar):
 // h_out = (h_in + rmsnorm(o)*w1) * out_scale; x = rmsnorm(h_out)*w2 -> B fragments.
-// y_buf [16][d] and stats [16][chunks] are scratch.
-int g4b_rowepi_chunks(int d);
 cudaError_t g4b_rowepi(const g4b::GemmOut& o, const float* h_in, float* h_out, const uint16_t* w1, float out_scale,
-                       const uint16_t* w2, int d, float* y_buf, float4* stats, void* bfrag, int M, cudaStream_t st,
-                       bool pdl);
+                       const uint16_t* w2, int d, void* bfrag, int M, cudaStream_t st, bool pdl);
 
 // ---- attention.cu
 // Attention of M rows over the KV ring; writes the output [M][qh*hd] as the o-projection's

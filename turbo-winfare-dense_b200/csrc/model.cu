@@ -412,10 +412,8 @@ void DeviceModel::init_buffers() {
     part_ = static_cast<float*>(dmalloc(part * 4));
     q_buf_ = static_cast<float*>(dmalloc((size_t)kMaxM * max_q * 4));
     y_ = static_cast<float*>(dmalloc((size_t)kMaxM * max_n * 4));
-    ybuf_ = static_cast<float*>(dmalloc((size_t)kMaxM * d * 4));
     cnt_ = static_cast<unsigned*>(dmalloc((size_t)max_crg * sizeof(unsigned)));
     cuda_check(cudaMemset(cnt_, 0, (size_t)max_crg * sizeof(unsigned)), "memset");
-    stats_ = static_cast<float4*>(dmalloc((size_t)kMaxM * g4b_rowepi_chunks(d) * sizeof(float4)));
     chunk_best_ = static_cast<float2*>(dmalloc((size_t)opt_.tp * kMaxM * g4b_head_chunks(v_local_) * sizeof(float2)));
     logits_ = static_cast<float*>(dmalloc((size_t)kMaxM * v_local_ * 4));
     res_dev_ = static_cast<HeadResult*>(dmalloc(sizeof(HeadResult)));
@@ -438,9 +436,9 @@ uint64_t DeviceModel::pass_weight_bytes() const { return weight_bytes_; }
 
 int DeviceModel::kernels_per_pass(int M) const {
     (void)M;
-    // embed_norm; per layer 4 GEMMs + qkv_epi + attention + 2x2 norm/residual phases +
+    // embed_norm; per layer 4 GEMMs + qkv_epi + attention + 2 norm/residual epilogues +
     // geglu; LM head GEMM + head_chunks + finalize (NCCL's all-reduce kernels not counted)
-    const int per_layer = 11;
+    const int per_layer = 9;
     return 1 + per_layer * (int)layers_.size() + 3;
 }
 
@@ -575,8 +573,7 @@ void DeviceModel::enqueue_raw(int M, PassKind kind, bool want_logits, uint32_t* 
             oo = GemmOut{PartView{}, y_, d};
         }
 #endif
-        cuda_check(g4b_rowepi(oo, hres_[cur], hres_[1 - cur], L.pa_norm, 1.0f, L.pf_norm, d, ybuf_, stats_, bf_d_, M,
-                              stream_, pdl),
+        cuda_check(g4b_rowepi(oo, hres_[cur], hres_[1 - cur], L.pa_norm, 1.0f, L.pf_norm, d, bf_d_, M, stream_, pdl),
                    "post_attn");
         cur = 1 - cur;
         // FFN
@@ -593,8 +590,8 @@ void DeviceModel::enqueue_raw(int M, PassKind kind, bool want_logits, uint32_t* 
         }
 #endif
         const uint16_t* w_next = (l + 1 < layers_.size()) ? layers_[l + 1].in_norm : final_norm_;
-        cuda_check(g4b_rowepi(dn, hres_[cur], hres_[1 - cur], L.pffn_norm, L.scalar, w_next, d, ybuf_, stats_, bf_d_, M,
-                              stream_, pdl),
+        cuda_check(g4b_rowepi(dn, hres_[cur], hres_[1 - cur], L.pffn_norm, L.scalar, w_next, d, bf_d_, M, stream_,
+                              pdl),
                    "post_ffn");
         cur = 1 - cur;
     }

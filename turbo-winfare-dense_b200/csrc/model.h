@@ -137,9 +137,7 @@ class DeviceModel {
     size_t part_floats_ = 0;
     float* q_buf_ = nullptr;
     float* y_ = nullptr;       // dense GEMM output ahead of an all-reduce [16][max N]
-    float* ybuf_ = nullptr;    // norm/residual epilogue scratch [16][d]
     unsigned* cnt_ = nullptr;  // split-K arrival counters of the GEMM running on stream_
-    float4* stats_ = nullptr;  // [16][chunks]
     float2* chunk_best_ = nullptr;
     float* logits_ = nullptr;
     HeadResult* res_dev_ = nullptr;

@@ -8,10 +8,12 @@
 //                KVWrite.hlsl) -- one CTA per (row, head), one thread per rotary pair
 //   rowepi       post-attention: h += rmsnorm(o)*w_post_attn; x = rmsnorm(h)*w_pre_ffn
 //                (:560-567); post-FFN: h = (h + rmsnorm(down)*w_post_ffn) * layer_scalar,
-//                then the next layer's input norm or the final norm (:583-629). Two wide
-//                phases: phase 1 sums the split-K slots and gathers per-chunk statistics,
-//                phase 2 derives both RMS factors and finishes every column in parallel.
+//                then the next layer's input norm or the final norm (:583-629). One 8-CTA
+//                cluster per row: slot sums and statistics, a DSMEM reduction of the two
+//                RMS factors, then every column finished in parallel.
 //   geglu        gelu_tanh(gate) * up (:568-581, GeGLU.hlsl)
+#include <cooperative_groups.h>
+
 #include "bfrag.cuh"
 #include "common.cuh"
 #include "kernels.h"
@@ -19,6 +21,8 @@
 #include "model_dev.h"
 
 #include <algorithm>
+
+namespace cg = cooperative_groups;
 
 namespace g4b {
 
@@ -163,36 +167,48 @@ __global__ void qkv_epi_kernel(QkvEpiArgs a) {
 
 // ---------------------------------------------------------------- norm/residual epilogues
 
-// Block of 4 warps, one 64-column group per warp: 256 columns per block, grid (chunks, M).
-constexpr int kEpiWarps = 4;
-constexpr int kEpiCols = kEpiWarps * 64;
+// One 16-CTA cluster per row; CTA r owns 64-column groups [r*gpc, (r+1)*gpc) of the row (gpc =
+// ceil(groups / 8)), each warp up to kEpiGroupsPerWarp of them, held in registers from start
+// to finish. Phase 1 sums the split-K slots and the per-CTA sums of y^2, h^2, h*c and c^2
+// (c = y * w1); the cluster adds the CTA sums in rank order through distributed shared
+// memory, so every CTA derives the same two RMS factors; phase 2 finishes its columns.
+constexpr int kEpiClusters = 16;     // non-portable cluster size (B200 allows 16)
+constexpr int kEpiWarps = 8;
+constexpr int kEpiGroupsPerWarp = 2;  // d <= 16 CTAs x 8 warps x 2 groups x 64 = 16384
 
-// Phase 1: y = GEMM output (slot sums) into y_buf; per-chunk sums of y^2, h^2, h*c and c^2
-// with c = y * w1, from which phase 2 obtains both RMS factors without another pass.
-__global__ void rowepi_phase1_kernel(GemmOut o, const float* __restrict__ h_in, const uint16_t* __restrict__ w1, int d,
-                                     float* __restrict__ y_buf, float4* __restrict__ stats) {
+__global__ void __launch_bounds__(kEpiWarps * 32) rowepi_kernel(GemmOut o, const float* __restrict__ h_in,
+                                                                 float* __restrict__ h_out,
+                                                                 const uint16_t* __restrict__ w1, float out_scale,
+                                                                 const uint16_t* __restrict__ w2, int d, void* bfrag,
+                                                                 int M) {
     __shared__ float4 red[kEpiWarps];
+    __shared__ float4 cta_sum;
+    __shared__ __half stage[kEpiWarps][128];
+    cg::cluster_group cluster = cg::this_cluster();
     pdl_enter();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int m = blockIdx.y, chunk = blockIdx.x;
-    const int c0 = chunk * kEpiCols + warp * 64 + 2 * lane;
+    const int rank = (int)cluster.block_rank();
+    const int m = blockIdx.y;
+    const int Kp = (d + 127) / 128 * 128;
+    const int ngp = Kp / 64;
+    const int gpc = (ngp + kEpiClusters - 1) / kEpiClusters;
+    const int g_end = min(ngp, (rank + 1) * gpc);
+
+    float2 y[kEpiGroupsPerWarp], h[kEpiGroupsPerWarp];
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    float2 y2 = make_float2(0.f, 0.f);
-    if (c0 < d) {
-        y2 = gemm_out_pair(o, m, c0);
-        *reinterpret_cast<float2*>(y_buf + (size_t)m * d + c0) = y2;
-    }
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-        const int c = c0 + j;
-        if (c < d) {
-            const float y = j ? y2.y : y2.x;
-            const float h = h_in[(size_t)m * d + c];
-            const float cc = y * bf16_to_f32(w1[c]);
-            acc.x += y * y;
-            acc.y += h * h;
-            acc.z += h * cc;
-            acc.w += cc * cc;
+    for (int j = 0; j < kEpiGroupsPerWarp; ++j) {
+        const int gi = rank * gpc + warp + kEpiWarps * j;
+        const int c0 = gi * 64 + 2 * lane;
+        y[j] = h[j] = make_float2(0.f, 0.f);
+        if (gi < g_end && c0 < d) {
+            y[j] = gemm_out_pair(o, m, c0);
+            h[j] = *reinterpret_cast<const float2*>(h_in + (size_t)m * d + c0);
+            const float ca = y[j].x * bf16_to_f32(w1[c0]), cb = y[j].y * bf16_to_f32(w1[c0 + 1]);
+            acc.x += y[j].x * y[j].x + y[j].y * y[j].y;
+            acc.y += h[j].x * h[j].x + h[j].y * h[j].y;
+            acc.z += h[j].x * ca + h[j].y * cb;
+            acc.w += ca * ca + cb * cb;
         }
     }
     acc.x = warp_sum(acc.x);
@@ -206,49 +222,40 @@ __global__ void rowepi_phase1_kernel(GemmOut o, const float* __restrict__ h_in, 
         for (int i = 1; i < kEpiWarps; ++i) {
             t.x += red[i].x; t.y += red[i].y; t.z += red[i].z; t.w += red[i].w;
         }
-        stats[(size_t)m * gridDim.x + chunk] = t;
+        cta_sum = t;
     }
-}
-
-// Phase 2: r1 = 1/rms(y); h' = (h + (y*r1)*w1) * out_scale; r2 = 1/rms(h') from the phase-1
-// sums; x = (h'*r2)*w2 written as B fragments of the next GEMM.
-__global__ void rowepi_phase2_kernel(const float* __restrict__ y_buf, const float4* __restrict__ stats,
-                                     const float* __restrict__ h_in, float* __restrict__ h_out,
-                                     const uint16_t* __restrict__ w1, const uint16_t* __restrict__ w2,
-                                     float out_scale, int d, void* bfrag, int M) {
-    __shared__ __half stage[kEpiWarps][128];
-    pdl_enter();
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int m = blockIdx.y, chunk = blockIdx.x;
-    const int nch = gridDim.x;
-    // Every warp reduces the row's chunk sums in the same fixed order.
-    float4 t = make_float4(0.f, 0.f, 0.f, 0.f);
-    for (int i = lane; i < nch; i += 32) {
-        const float4 s = stats[(size_t)m * nch + i];
-        t.x += s.x; t.y += s.y; t.z += s.z; t.w += s.w;
+    cluster.sync();
+    float4 u[kEpiClusters];
+#pragma unroll
+    for (int r = 0; r < kEpiClusters; ++r) u[r] = *cluster.map_shared_rank(&cta_sum, r);  // all in flight
+    float4 t = u[0];
+#pragma unroll
+    for (int r = 1; r < kEpiClusters; ++r) {
+        t.x += u[r].x; t.y += u[r].y; t.z += u[r].z; t.w += u[r].w;
     }
-    t.x = warp_sum(t.x);
-    t.y = warp_sum(t.y);
-    t.z = warp_sum(t.z);
-    t.w = warp_sum(t.w);
+    cluster.sync();  // every CTA has read the others' sums before any of them exits
     const float r1 = inv_rms(t.x, d);
     const float s2 = out_scale * out_scale * (t.y + 2.0f * r1 * t.z + r1 * r1 * t.w);
     const float r2 = inv_rms(fmaxf(s2, 0.f), d);
-    const int gi = chunk * kEpiWarps + warp;
-    const int Kp = (d + 127) / 128 * 128;
-    if (gi * 64 >= Kp) return;
-    float x[2] = {0.f, 0.f};
+    const BFragView bv = bfrag_view(bfrag, Kp, M);
 #pragma unroll
-    for (int j = 0; j < 2; ++j) {
-        const int c = gi * 64 + 2 * lane + j;
-        if (c < d) {
-            const float a = __fmul_rn(__fmul_rn(y_buf[(size_t)m * d + c], r1), bf16_to_f32(w1[c]));
-            const float hn = __fmul_rn(__fadd_rn(h_in[(size_t)m * d + c], a), out_scale);
-            h_out[(size_t)m * d + c] = hn;
-            x[j] = __fmul_rn(__fmul_rn(hn, r2), bf16_to_f32(w2[c]));
+    for (int j = 0; j < kEpiGroupsPerWarp; ++j) {
+        const int gi = rank * gpc + warp + kEpiWarps * j;
+        if (gi >= g_end) continue;  // warp-uniform
+        float x[2] = {0.f, 0.f};
+#pragma unroll
+        for (int e = 0; e < 2; ++e) {
+            const int c = gi * 64 + 2 * lane + e;
+            if (c < d) {
+                const float yy = e ? y[j].y : y[j].x, hh = e ? h[j].y : h[j].x;
+                const float a = __fmul_rn(__fmul_rn(yy, r1), bf16_to_f32(w1[c]));
+                const float hn = __fmul_rn(__fadd_rn(hh, a), out_scale);
+                h_out[(size_t)m * d + c] = hn;
+                x[e] = __fmul_rn(__fmul_rn(hn, r2), bf16_to_f32(w2[c]));
+            }
         }
+        bfrag_store_group(bv, M, m, gi, x[0], x[1], stage[warp]);
     }
-    bfrag_store_group(bfrag_view(bfrag, Kp, M), M, m, gi, x[0], x[1], stage[warp]);
 }
 
 // ---------------------------------------------------------------- GeGLU
@@ -326,17 +333,31 @@ cudaError_t g4b_qkv_epi(const QkvEpiArgs& a, cudaStream_t st, bool pdl) {
     return launch(qkv_epi_kernel, dim3(a.M * (a.qh + a.kvh)), dim3(a.hd / 2), 0, st, pdl, a);
 }
 
-int g4b_rowepi_chunks(int d) { return ((d + 127) / 128 * 128 + kEpiCols - 1) / kEpiCols; }
-
 cudaError_t g4b_rowepi(const GemmOut& o, const float* h_in, float* h_out, const uint16_t* w1, float out_scale,
-                       const uint16_t* w2, int d, float* y_buf, float4* stats, void* bfrag, int M, cudaStream_t st,
-                       bool pdl) {
+                       const uint16_t* w2, int d, void* bfrag, int M, cudaStream_t st, bool pdl) {
     if ((o.ld | d) & 1) return cudaErrorInvalidValue;  // float2 loads
-    const dim3 grid(g4b_rowepi_chunks(d), M);
-    cudaError_t e = launch(rowepi_phase1_kernel, grid, dim3(kEpiWarps * 32), 0, st, pdl, o, h_in, w1, d, y_buf, stats);
-    if (e != cudaSuccess) return e;
-    return launch(rowepi_phase2_kernel, grid, dim3(kEpiWarps * 32), 0, st, pdl, (const float*)y_buf,
-                  (const float4*)stats, h_in, h_out, w1, w2, out_scale, d, bfrag, M);
+    const int ngp = (d + 127) / 128 * 2;
+    if ((ngp + kEpiClusters - 1) / kEpiClusters > kEpiWarps * kEpiGroupsPerWarp) return cudaErrorInvalidValue;
+    static bool attr_set = false;
+    if (!attr_set) {
+        const cudaError_t e = cudaFuncSetAttribute(rowepi_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        if (e != cudaSuccess) return e;
+        attr_set = true;
+    }
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(kEpiClusters, M);
+    cfg.blockDim = dim3(kEpiWarps * 32);
+    cfg.stream = st;
+    cudaLaunchAttribute attr[2];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = kEpiClusters;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    attr[1].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[1].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = pdl ? 2 : 1;
+    return cudaLaunchKernelEx(&cfg, rowepi_kernel, o, h_in, h_out, w1, out_scale, w2, d, bfrag, M);
 }
 
 cudaError_t g4b_geglu(const GemmOut& gu, int F, void* bfrag, int M, cudaStream_t st, bool pdl) {

@@ -1,7 +1,7 @@
 """Profiling drivers: run one piece of the hot path inside a CUDA profiler range so an external
 profiler started with `--profile-from-start off` sees exactly that piece.
 
-    python -m g4dense_b200.profile pass  --which target|draft --batch M --pos P
+    python -m g4dense_b200.profile pass  --which target|draft --batch M --pos P [--layers L]
         one forward pass of the 31B-shaped target (or the E2B-shaped drafter) with M rows at
         positions P..P+M-1 (attention spans P earlier cache entries), after 5 timed warm
         passes; prints their mean CUDA-event time.
@@ -34,10 +34,11 @@ def _profiler():
     return cu.cuProfilerStart, cu.cuProfilerStop
 
 
-def run_pass(which, batch, pos):
+def run_pass(which, batch, pos, layers=0):
     from .api import Engine
     if which == "target":
-        e = Engine(preset="gemma4-31b", seed=0, max_context=4096, device=0)
+        preset = "gemma4-31b" + (f":layers={layers}" if layers else "")
+        e = Engine(preset=preset, seed=0, max_context=4096, device=0)
     else:
         e = Engine(preset="gemma4-e2b", seed=1, max_context=4096, device=0)
     ms = e.time_pass(0, batch, 5, pos=pos)
@@ -85,12 +86,13 @@ def main(argv=None):
     p.add_argument("--which", choices=["target", "draft"], default="target")
     p.add_argument("--batch", type=int, default=5)
     p.add_argument("--pos", type=int, default=768)
+    p.add_argument("--layers", type=int, default=0, help="target layers (0 = all 60); a small case for ncu")
     g = sub.add_parser("gemms")
     g.add_argument("--only", default=None)
     g.add_argument("--batch", type=int, default=5)
     a = ap.parse_args(argv)
     if a.cmd == "pass":
-        run_pass(a.which, a.batch, a.pos)
+        run_pass(a.which, a.batch, a.pos, a.layers)
     else:
         run_gemms(a.only, a.batch)
     return 0
