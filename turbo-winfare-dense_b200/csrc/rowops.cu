@@ -19,40 +19,13 @@
 #include "kernels.h"
 #include "launch.cuh"
 #include "model_dev.h"
+#include "rowmath.cuh"
 
 #include <algorithm>
 
 namespace cg = cooperative_groups;
 
 namespace g4b {
-
-// FP16 round trip of the reference oracle (src/cpu_reference.cpp:51-84): round to nearest
-// even for normal halves, values below the smallest normal half become signed zero, values
-// at or above 2^16 become infinity. Returns the half's bit pattern.
-__device__ __forceinline__ uint16_t f16_bits_like_reference(float f) {
-    const uint32_t x = __float_as_uint(f);
-    const uint32_t sign = (x >> 16) & 0x8000u;
-    const int e = (int)((x >> 23) & 0xFFu) - 127 + 15;
-    const uint32_t man = x & 0x7FFFFFu;
-    if (e <= 0) return (uint16_t)sign;
-    if (e >= 31) return (uint16_t)(sign | 0x7C00u);
-    const uint32_t round_bit = (man >> 12) & 1u;
-    const uint32_t sticky = (man & 0xFFFu) != 0u;
-    uint32_t v = sign | ((uint32_t)e << 10) | (man >> 13);
-    if (round_bit && (sticky || (v & 1u))) ++v;
-    return (uint16_t)v;
-}
-
-__device__ __forceinline__ uint16_t bf16_bits_rne(float f) {
-    uint32_t u = __float_as_uint(f);
-    u += 0x7FFFu + ((u >> 16) & 1u);
-    return (uint16_t)(u >> 16);
-}
-
-// 1 / sqrt(mean + eps) with IEEE sqrt and division, as the reference computes it.
-__device__ __forceinline__ float inv_rms(float sumsq, int n) {
-    return 1.0f / sqrtf(sumsq / (float)n + 1e-6f);
-}
 
 // Writes a full row x[0..K) (in shared memory) as B fragments, one warp per 64-group.
 __device__ __forceinline__ void row_to_bfrags(const float* xs, int K, int M, int m, void* bfrag, __half* stage) {
@@ -259,12 +232,6 @@ __global__ void __launch_bounds__(kEpiWarps * 32) rowepi_kernel(GemmOut o, const
 }
 
 // ---------------------------------------------------------------- GeGLU
-
-__device__ __forceinline__ float gelu_tanh_dev(float x) {
-    const float k = 0.7978845608028654f;
-    const float inner = k * (x + 0.044715f * x * x * x);
-    return 0.5f * x * (1.0f + tanhf(inner));
-}
 
 // One warp per (row, 64-group) of the F-wide activation; gate rows [0, F), up rows [F, 2F).
 __global__ void geglu_kernel(GemmOut gu, int F, void* bfrag, int M) {
