@@ -8,9 +8,9 @@
 //                KVWrite.hlsl) -- one CTA per (row, head), one thread per rotary pair
 //   rowepi       post-attention: h += rmsnorm(o)*w_post_attn; x = rmsnorm(h)*w_pre_ffn
 //                (:560-567); post-FFN: h = (h + rmsnorm(down)*w_post_ffn) * layer_scalar,
-//                then the next layer's input norm or the final norm (:583-629). One 8-CTA
-//                cluster per row: slot sums and statistics, a DSMEM reduction of the two
-//                RMS factors, then every column finished in parallel.
+//                then the next layer's input norm or the final norm (:583-629). One CTA
+//                (narrow rows) or one 16-CTA cluster (wide rows, DSMEM reduction) per row:
+//                slot sums and statistics, the two RMS factors, then every column.
 //   geglu        gelu_tanh(gate) * up (:568-581, GeGLU.hlsl)
 #include <cooperative_groups.h>
 
@@ -140,38 +140,41 @@ __global__ void qkv_epi_kernel(QkvEpiArgs a) {
 
 // ---------------------------------------------------------------- norm/residual epilogues
 
-// One 16-CTA cluster per row; CTA r owns 64-column groups [r*gpc, (r+1)*gpc) of the row (gpc =
-// ceil(groups / 8)), each warp up to kEpiGroupsPerWarp of them, held in registers from start
-// to finish. Phase 1 sums the split-K slots and the per-CTA sums of y^2, h^2, h*c and c^2
-// (c = y * w1); the cluster adds the CTA sums in rank order through distributed shared
-// memory, so every CTA derives the same two RMS factors; phase 2 finishes its columns.
+// Rows of up to 32 64-column groups (d <= 2048): one CTA per row, one warp per group, the
+// statistics reduced in the CTA. Wider rows: one 16-CTA cluster per row; CTA r owns groups
+// [r*gpc, (r+1)*gpc) (gpc = ceil(groups / 16)), each warp up to kEpiGroupsPerWarp of them, and
+// the cluster adds the CTA sums in rank order through distributed shared memory, so every CTA
+// derives the same two RMS factors. In both forms a warp holds its columns in registers from
+// start to finish: phase 1 sums the split-K slots and the sums of y^2, h^2, h*c and c^2
+// (c = y * w1); phase 2 finishes the columns.
 constexpr int kEpiClusters = 16;     // non-portable cluster size (B200 allows 16)
-constexpr int kEpiWarps = 8;
+constexpr int kEpiWarps = 8;         // warps per CTA in the cluster form
 constexpr int kEpiGroupsPerWarp = 2;  // d <= 16 CTAs x 8 warps x 2 groups x 64 = 16384
+constexpr int kEpiMaxWarps = 32;
 
-__global__ void __launch_bounds__(kEpiWarps * 32) rowepi_kernel(GemmOut o, const float* __restrict__ h_in,
-                                                                 float* __restrict__ h_out,
-                                                                 const uint16_t* __restrict__ w1, float out_scale,
-                                                                 const uint16_t* __restrict__ w2, int d, void* bfrag,
-                                                                 int M) {
-    __shared__ float4 red[kEpiWarps];
+template <bool CLUSTER>
+__global__ void __launch_bounds__(kEpiMaxWarps * 32) rowepi_kernel(GemmOut o, const float* __restrict__ h_in,
+                                                                    float* __restrict__ h_out,
+                                                                    const uint16_t* __restrict__ w1, float out_scale,
+                                                                    const uint16_t* __restrict__ w2, int d,
+                                                                    void* bfrag, int M) {
+    __shared__ float4 red[kEpiMaxWarps];
     __shared__ float4 cta_sum;
-    __shared__ __half stage[kEpiWarps][128];
-    cg::cluster_group cluster = cg::this_cluster();
+    __shared__ __half stage[kEpiMaxWarps][128];
     pdl_enter();
-    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
-    const int rank = (int)cluster.block_rank();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int rank = CLUSTER ? (int)cg::this_cluster().block_rank() : 0;
     const int m = blockIdx.y;
     const int Kp = (d + 127) / 128 * 128;
     const int ngp = Kp / 64;
-    const int gpc = (ngp + kEpiClusters - 1) / kEpiClusters;
+    const int gpc = CLUSTER ? (ngp + kEpiClusters - 1) / kEpiClusters : ngp;
     const int g_end = min(ngp, (rank + 1) * gpc);
 
     float2 y[kEpiGroupsPerWarp], h[kEpiGroupsPerWarp];
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int j = 0; j < kEpiGroupsPerWarp; ++j) {
-        const int gi = rank * gpc + warp + kEpiWarps * j;
+        const int gi = rank * gpc + warp + nw * j;
         const int c0 = gi * 64 + 2 * lane;
         y[j] = h[j] = make_float2(0.f, 0.f);
         if (gi < g_end && c0 < d) {
@@ -192,28 +195,35 @@ __global__ void __launch_bounds__(kEpiWarps * 32) rowepi_kernel(GemmOut o, const
     __syncthreads();
     if (threadIdx.x == 0) {
         float4 t = red[0];
-        for (int i = 1; i < kEpiWarps; ++i) {
+        for (int i = 1; i < nw; ++i) {
             t.x += red[i].x; t.y += red[i].y; t.z += red[i].z; t.w += red[i].w;
         }
         cta_sum = t;
     }
-    cluster.sync();
-    float4 u[kEpiClusters];
+    float4 t;
+    if constexpr (CLUSTER) {
+        cg::cluster_group cluster = cg::this_cluster();
+        cluster.sync();
+        float4 u[kEpiClusters];
 #pragma unroll
-    for (int r = 0; r < kEpiClusters; ++r) u[r] = *cluster.map_shared_rank(&cta_sum, r);  // all in flight
-    float4 t = u[0];
+        for (int r = 0; r < kEpiClusters; ++r) u[r] = *cluster.map_shared_rank(&cta_sum, r);  // all in flight
+        t = u[0];
 #pragma unroll
-    for (int r = 1; r < kEpiClusters; ++r) {
-        t.x += u[r].x; t.y += u[r].y; t.z += u[r].z; t.w += u[r].w;
+        for (int r = 1; r < kEpiClusters; ++r) {
+            t.x += u[r].x; t.y += u[r].y; t.z += u[r].z; t.w += u[r].w;
+        }
+        cluster.sync();  // every CTA has read the others' sums before any of them exits
+    } else {
+        __syncthreads();
+        t = cta_sum;
     }
-    cluster.sync();  // every CTA has read the others' sums before any of them exits
     const float r1 = inv_rms(t.x, d);
     const float s2 = out_scale * out_scale * (t.y + 2.0f * r1 * t.z + r1 * r1 * t.w);
     const float r2 = inv_rms(fmaxf(s2, 0.f), d);
     const BFragView bv = bfrag_view(bfrag, Kp, M);
 #pragma unroll
     for (int j = 0; j < kEpiGroupsPerWarp; ++j) {
-        const int gi = rank * gpc + warp + kEpiWarps * j;
+        const int gi = rank * gpc + warp + nw * j;
         if (gi >= g_end) continue;  // warp-uniform
         float x[2] = {0.f, 0.f};
 #pragma unroll
@@ -304,10 +314,14 @@ cudaError_t g4b_rowepi(const GemmOut& o, const float* h_in, float* h_out, const 
                        const uint16_t* w2, int d, void* bfrag, int M, cudaStream_t st, bool pdl) {
     if ((o.ld | d) & 1) return cudaErrorInvalidValue;  // float2 loads
     const int ngp = (d + 127) / 128 * 2;
+    if (ngp <= kEpiMaxWarps)  // one CTA per row, one warp per group
+        return launch(rowepi_kernel<false>, dim3(1, M), dim3(ngp * 32), 0, st, pdl, o, h_in, h_out, w1, out_scale, w2,
+                      d, bfrag, M);
     if ((ngp + kEpiClusters - 1) / kEpiClusters > kEpiWarps * kEpiGroupsPerWarp) return cudaErrorInvalidValue;
     static bool attr_set = false;
     if (!attr_set) {
-        const cudaError_t e = cudaFuncSetAttribute(rowepi_kernel, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
+        const cudaError_t e =
+            cudaFuncSetAttribute(rowepi_kernel<true>, cudaFuncAttributeNonPortableClusterSizeAllowed, 1);
         if (e != cudaSuccess) return e;
         attr_set = true;
     }
@@ -324,7 +338,7 @@ cudaError_t g4b_rowepi(const GemmOut& o, const float* h_in, float* h_out, const 
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 2 : 1;
-    return cudaLaunchKernelEx(&cfg, rowepi_kernel, o, h_in, h_out, w1, out_scale, w2, d, bfrag, M);
+    return cudaLaunchKernelEx(&cfg, rowepi_kernel<true>, o, h_in, h_out, w1, out_scale, w2, d, bfrag, M);
 }
 
 cudaError_t g4b_geglu(const GemmOut& gu, int F, void* bfrag, int M, cudaStream_t st, bool pdl) {
