@@ -56,6 +56,16 @@ G4B_API int g4b_qmat_run_partial(g4b_qmat* q, int M, void* stream);
 G4B_API int g4b_qmat_run_noalloc(g4b_qmat* q, int M, float* out, int ldo, void* stream);
 /* Synchronizes and reports whether any launch on q hit a bounded-wait timeout. */
 G4B_API int g4b_qmat_check_error(g4b_qmat* q);
+/* INT8 G64 affine GEMV, the reference's GemvInt8 (shaders/GemvInt8.hlsl:13-33, row dot
+ * shaders/Common.hlsli:225-269): out[r] = sum_k (W[r][k] * s + b) * x[k] for r < rows, with W
+ * [rows][K] u8, S and B [rows][K/64] bf16, x [K] fp32, out [rows] fp32. K a multiple of 64; W and
+ * x 16-byte aligned. */
+G4B_API int g4b_gemv_int8(const uint8_t* W, const uint16_t* S, const uint16_t* B, const float* x, float* out,
+                          int rows, int K, void* stream);
+/* Attention output gate, the reference's AttnGate (shaders/AttnGate.hlsl:15-32):
+ * out[m][c] = ctx[m][c] * sigmoid(gate[m][c]) for c < n, m < batch; strides in floats. */
+G4B_API int g4b_attn_gate(const float* ctx, const float* gate, float* out, int n, int batch, int ctx_stride,
+                          int gate_stride, int out_stride, void* stream);
 /* out4 = {N, K, grid CTAs at M=5, split-K slots per row group} */
 G4B_API int g4b_qmat_info(const g4b_qmat* q, int* out4);
 

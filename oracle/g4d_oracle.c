@@ -141,6 +141,15 @@ void g4o_int8_gemv(const uint32_t* W, const uint16_t* S, const uint16_t* B, uint
     }
 }
 
+/* Attention output gate: out = ctx * (1 / (1 + exp(-gate))) (src/cpu_reference.cpp:550-556,
+ * shaders/AttnGate.hlsl:15-32). */
+void g4o_attn_gate(const float* ctx, const float* gate, float* out, uint32_t n) {
+    for (uint32_t i = 0; i < n; ++i) {
+        const float sig = 1.0f / (1.0f + expf(-gate[i]));
+        out[i] = ctx[i] * sig;
+    }
+}
+
 /* rms_norm, src/cpu_reference.cpp:141-150 (w == NULL: rms_norm_no_scale, :153-162). */
 static void rms_norm_f(const float* x, const float* w, uint32_t n, float eps, float* out) {
     float ss = 0.0f;

@@ -55,6 +55,7 @@ float g4o_gelu_tanh(float x);
 /* out[m][r] = sum_c (q*s+b) * x[m][c]; sequential fp32 sum per row, as cpu_reference gemv. */
 void g4o_int4_gemm(const uint32_t* W, const uint16_t* S, const uint16_t* B, uint32_t rows,
                    uint32_t cols, const float* x, uint32_t M, float* out);
+void g4o_attn_gate(const float* ctx, const float* gate, float* out, uint32_t n);
 void g4o_int8_gemv(const uint32_t* W, const uint16_t* S, const uint16_t* B, uint32_t rows,
                    uint32_t cols, const float* x, float* out);
 void g4o_rmsnorm(const float* x, const uint16_t* w_bf16, uint32_t n, float eps, float* out);

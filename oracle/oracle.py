@@ -70,6 +70,7 @@ def restated_lib():
         lib.g4o_int4_gemm.argtypes = [_vp, _vp, _vp, ctypes.c_uint32, ctypes.c_uint32, _vp,
                                       ctypes.c_uint32, _vp]
         lib.g4o_int8_gemv.argtypes = [_vp, _vp, _vp, ctypes.c_uint32, ctypes.c_uint32, _vp, _vp]
+        lib.g4o_attn_gate.argtypes = [_vp, _vp, _vp, ctypes.c_uint32]
         lib.g4o_rmsnorm.argtypes = [_vp, _vp, ctypes.c_uint32, ctypes.c_float, _vp]
         lib.g4o_attention.argtypes = [_vp, _vp, _vp] + [ctypes.c_uint32] * 6 + [ctypes.c_float, _vp]
         lib.g4o_round_f16.restype = ctypes.c_float
@@ -219,6 +220,15 @@ def int8_gemv(W, S, B, x):
     x = np.ascontiguousarray(x, np.float32)
     lib.g4o_int8_gemv(_ptr(W), _ptr(np.ascontiguousarray(S, np.uint16)),
                       _ptr(np.ascontiguousarray(B, np.uint16)), N, K, _ptr(x), _ptr(out))
+    return out
+
+
+def attn_gate(ctx, gate):
+    lib = restated_lib()
+    ctx = np.ascontiguousarray(ctx, np.float32)
+    gate = np.ascontiguousarray(gate, np.float32)
+    out = np.empty_like(ctx)
+    lib.g4o_attn_gate(_ptr(ctx), _ptr(gate), _ptr(out), ctx.size)
     return out
 
 

@@ -199,11 +199,12 @@ G4DENSE_API void* g4dense_engine_create_ex(const G4DenseEngineConfig* cfg) {
         const cudaStream_t st = target->stream();
         h->engine = std::make_unique<g4b::Engine>(std::move(target));
         if ((cfg->draft_path && *cfg->draft_path) || cfg->draft_preset) {
-            // The drafter stays whole on every rank (it is small); it shares the target's stream.
+            // The drafter stays whole on every rank (it is small) and runs on its own stream, so
+            // its prompt catch-up overlaps the target's prefill; the engine orders the two
+            // streams with events where a round's passes depend on each other.
             g4b::ModelOptions dopt;
             dopt.max_context = mo.max_context;
             dopt.kv_bf16 = mo.kv_bf16;
-            dopt.stream = st;
             dopt.use_graphs = mo.use_graphs;
             auto d = std::make_unique<g4b::DeviceModel>(dopt);
             if (cfg->draft_path && *cfg->draft_path) {

@@ -46,3 +46,11 @@ cudaError_t g4b_head_chunks_launch(const g4b::GemmOut& lm, int V, int M, float s
 // chunk_best holds nranks slices [M][nchunks] (tensor-parallel vocabulary ranges).
 cudaError_t g4b_head_finalize(const float2* chunk_best, int nchunks, int nranks, int M, g4b::StepParams* sp,
                               HeadResult* res, uint32_t* chain_out, cudaStream_t st, bool pdl);
+
+// ---- side.cu: INT8 G64 GEMV (one row per warp) and the attention output gate
+namespace g4b {
+cudaError_t gemv_int8_launch(const uint8_t* W, const uint16_t* S, const uint16_t* B, const float* x, float* out,
+                             int rows, int K, cudaStream_t st);
+cudaError_t attn_gate_launch(const float* ctx, const float* gate, float* out, int n, int batch, int ctx_stride,
+                             int gate_stride, int out_stride, cudaStream_t st);
+}  // namespace g4b

@@ -154,7 +154,7 @@ class DeviceModel {
     bool pdl_in_graphs_ = true;
     StepParams* sp_host_ = nullptr;  // pinned ring of kParamRing entries
     int sp_ring_ = 0;
-    static constexpr int kParamRing = 256;
+    static constexpr int kParamRing = 4096;  // no host stall in a 30k-token prefill
     HeadResult* res_host_ = nullptr; // pinned
     bool own_stream_ = true;
     uint64_t launches_ = 0, h2d_bytes_ = 0, d2h_bytes_ = 0;

@@ -201,6 +201,26 @@ int g4b_qmat_info(const g4b_qmat* q, int* out4) {
     return 0;
 }
 
+int g4b_gemv_int8(const uint8_t* W, const uint16_t* S, const uint16_t* B, const float* x, float* out, int rows,
+                  int K, void* stream) {
+    if (!W || !S || !B || !x || !out || rows <= 0 || K <= 0 || K % 64)
+        return fail_msg("g4b_gemv_int8: bad arguments (K must be a positive multiple of 64)");
+    if ((reinterpret_cast<uintptr_t>(W) | reinterpret_cast<uintptr_t>(x)) & 15)
+        return fail_msg("g4b_gemv_int8: W and x must be 16-byte aligned");
+    const cudaError_t e = g4b::gemv_int8_launch(W, S, B, x, out, rows, K, (cudaStream_t)stream);
+    return e == cudaSuccess ? 0 : fail(e, "g4b_gemv_int8");
+}
+
+int g4b_attn_gate(const float* ctx, const float* gate, float* out, int n, int batch, int ctx_stride, int gate_stride,
+                  int out_stride, void* stream) {
+    if (!ctx || !gate || !out || n <= 0 || batch < 0 || ctx_stride < n || gate_stride < n || out_stride < n)
+        return fail_msg("g4b_attn_gate: bad arguments");
+    if (batch == 0) return 0;
+    const cudaError_t e =
+        g4b::attn_gate_launch(ctx, gate, out, n, batch, ctx_stride, gate_stride, out_stride, (cudaStream_t)stream);
+    return e == cudaSuccess ? 0 : fail(e, "g4b_attn_gate");
+}
+
 int g4b_qmat_check_error(g4b_qmat* q) {
     if (!q) return fail_msg("g4b_qmat_check_error: null handle");
     int h = 0;

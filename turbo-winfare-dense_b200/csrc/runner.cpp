@@ -36,6 +36,15 @@ void DraftRuntime::catch_up(const std::vector<uint32_t>& ctx) {
     }
 }
 
+void Engine::order(cudaStream_t from, cudaStream_t to) {
+    if (from == to) return;
+    if (!order_ev_[0])
+        for (auto& e : order_ev_) cuda_check(cudaEventCreateWithFlags(&e, cudaEventDisableTiming), "event");
+    cudaEvent_t e = order_ev_[order_i_ ^= 1];  // alternate: a recorded event is reused one edge later
+    cuda_check(cudaEventRecord(e, from), "event record");
+    cuda_check(cudaStreamWaitEvent(to, e, 0), "stream wait");
+}
+
 void Engine::forward_batch(const uint32_t* ids, uint32_t batch, uint32_t base, float* out_logits, bool all_positions) {
     if (batch < 1 || batch > (uint32_t)kBatchRows) throw std::invalid_argument("forward_batch: batch must be 1..16");
     if (out_logits && target_->options().tp > 1)
@@ -107,7 +116,15 @@ std::vector<uint32_t> Engine::generate(const std::vector<uint32_t>& prompt, cons
     const uint64_t l0 = T.launches() + (draft_ ? draft_->model().launches() : 0);
     const uint64_t h0 = T.h2d_bytes() + (draft_ ? draft_->model().h2d_bytes() : 0);
     const uint64_t d0 = T.d2h_bytes() + (draft_ ? draft_->model().d2h_bytes() : 0);
+    const bool spec = opt.speculative_enabled && draft_ && opt.draft_k > 0;
+    if (spec) {
+        // The drafter's pass over the prompt is prefill work: queue it on the drafter's stream
+        // first so it runs alongside the target's prefill.
+        draft_->reset();
+        draft_->catch_up(history);
+    }
     const uint32_t first = prefill(history, opt, &logits);
+    if (spec) order(draft_->model().stream(), T.stream());  // decode starts after both prefills
     stats_.h2d_bytes += history.size() * sizeof(uint32_t);
     stats_.ttft_ms = now_ms() - t0;
     const double t_decode = now_ms();
@@ -130,13 +147,10 @@ std::vector<uint32_t> Engine::generate(const std::vector<uint32_t>& prompt, cons
         }
         return true;
     };
-    const bool spec = opt.speculative_enabled && draft_ && opt.draft_k > 0;
-
     if (spec) {
         DraftRuntime& D = *draft_;
         DeviceModel& Dm = D.model();
         if (Dm.header().vocab_size != V) throw std::invalid_argument("drafter vocabulary differs from the target's");
-        D.reset();
         const uint32_t K = std::min<uint32_t>(opt.draft_k, kMaxDraftWidth);
         uint32_t drafted_total = 0, accepted_total = 0;
         bool drafting = true;
@@ -179,6 +193,9 @@ std::vector<uint32_t> Engine::generate(const std::vector<uint32_t>& prompt, cons
                 tp.tokens[0] = dp.tokens[0] = pending;
                 const bool replay = !opt.replay.empty();
                 T.push_params(0, tp);
+                // The drafter's steps write their tokens into the target's step parameters:
+                // after the target's parameter copy, and before the verify pass reads them.
+                order(T.stream(), Dm.stream());
                 Dm.push_params(1, dp);
                 uint32_t* chain = replay ? Dm.chain_dev() : T.step_params(0)->tokens + 1;
                 for (uint32_t s = 0; s + 1 < K; ++s) Dm.enqueue(1, PassKind::DraftStep, false, chain);
@@ -188,6 +205,7 @@ std::vector<uint32_t> Engine::generate(const std::vector<uint32_t>& prompt, cons
                                                           opt.mismatch_seed, V);
                     T.push_params(0, tp);
                 }
+                order(Dm.stream(), T.stream());  // replay too: the verify waits for the drafts
                 T.enqueue((int)K, PassKind::Plain, false, nullptr);
                 const HeadResult r = T.fetch_result();
                 n_acc = (uint32_t)r.n_accepted;

@@ -74,6 +74,12 @@ class DraftRuntime {
 class Engine {
    public:
     explicit Engine(std::unique_ptr<DeviceModel> target) : target_(std::move(target)) {}
+    ~Engine() {
+        for (auto e : order_ev_)
+            if (e) cudaEventDestroy(e);
+    }
+    Engine(const Engine&) = delete;
+    Engine& operator=(const Engine&) = delete;
     DeviceModel& target() { return *target_; }
     DraftRuntime* draft() { return draft_.get(); }
     void set_draft(std::unique_ptr<DeviceModel> d) { draft_ = std::make_unique<DraftRuntime>(std::move(d)); }
@@ -90,8 +96,13 @@ class Engine {
 
    private:
     uint32_t prefill(const std::vector<uint32_t>& tokens, const GenerationOptions& opt, std::vector<float>* last_logits);
+    // Makes `to` wait for the work queued on `from` so far.
+    void order(cudaStream_t from, cudaStream_t to);
+
     std::unique_ptr<DeviceModel> target_;
     std::unique_ptr<DraftRuntime> draft_;
+    cudaEvent_t order_ev_[2] = {nullptr, nullptr};
+    int order_i_ = 0;
     SpeculativeCoordinator speculator_;
     GenStats stats_;
 };

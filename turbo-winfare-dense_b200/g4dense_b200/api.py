@@ -31,6 +31,8 @@ def lib():
         L.g4b_qmat_info.argtypes = [_vp, _vp]
         L.g4b_qmat_run_partial.argtypes = [_vp, ctypes.c_int, _vp]
         L.g4b_qmat_run_noalloc.argtypes = [_vp, ctypes.c_int, _vp, ctypes.c_int, _vp]
+        L.g4b_gemv_int8.argtypes = [_vp, _vp, _vp, _vp, _vp, ctypes.c_int, ctypes.c_int, _vp]
+        L.g4b_attn_gate.argtypes = [_vp, _vp, _vp] + [ctypes.c_int] * 5 + [_vp]
         L.g4b_qmat_check_error.argtypes = [_vp]
         _bind_engine(L)
         _lib = L
@@ -99,6 +101,19 @@ def _dptr(t):
 
 def _stream(stream):
     return ctypes.c_void_p(stream.cuda_stream if stream is not None else 0)
+
+
+def gemv_int8(W, S, B, x, out, stream=None):
+    """out[r] = sum_k (W[r][k] * s + b) * x[k]: W uint8 [rows][K], S/B bf16 bits [rows][K/64],
+    x fp32 [K], out fp32 [rows] (torch CUDA tensors)."""
+    _check(lib().g4b_gemv_int8(_dptr(W), _dptr(S), _dptr(B), _dptr(x), _dptr(out), W.shape[0], W.shape[1],
+                               _stream(stream)), "g4b_gemv_int8")
+
+
+def attn_gate(ctx, gate, out, stream=None):
+    """out = ctx * sigmoid(gate) over [batch][n] fp32 torch CUDA tensors (row strides honoured)."""
+    _check(lib().g4b_attn_gate(_dptr(ctx), _dptr(gate), _dptr(out), ctx.shape[1], ctx.shape[0], ctx.stride(0),
+                               gate.stride(0), out.stride(0), _stream(stream)), "g4b_attn_gate")
 
 
 class QMat:
