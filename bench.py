@@ -245,8 +245,6 @@ def run_b200(args, rank, world):
             if ln.startswith("traffic_bytes_per_pass:"):
                 traffic = int(ln.split(":")[1])
 
-    if rank != 0:
-        return 0
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": dec_ms / args.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
@@ -274,14 +272,49 @@ def run_b200(args, rank, world):
     }
     if clocks:
         line["clocks"] = clocks
+    long_ctx = args.long_context and world == 1  # (a second TP engine would need its own NCCL id)
+    if long_ctx:
+        eng.close()
+        line["long_context"] = long_context(args, eng_factory=lambda: Engine(
+            preset="gemma4-31b", seed=0, draft_preset="gemma4-e2b", draft_seed=1, draft_k=9, max_context=32768,
+            kv_bf16=True, device=local), world=world)
+    if rank != 0:
+        if not long_ctx:
+            eng.close()
+        return 0
     if world == 1 and not args.no_cpu_baseline:
         try:
             line["cpu_baseline"] = reference_sample(1, 1)
         except Exception as e:  # the baseline is reported, never required
             line["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
     print(json.dumps(line), flush=True)
-    eng.close()
+    if not long_ctx:
+        eng.close()
     return 0
+
+
+def long_context(args, eng_factory, world):
+    """BASELINE config 4 at TP 1: 32768-token bf16 KV filled by a 30000-token prefill, verify width
+    9 (k = 8), greedy (natural drafter, gate off) and temperature-0.8 rejection sampling."""
+    import gc
+    gc.collect()
+    eng = eng_factory()
+    prompt = np.random.default_rng(4).integers(0, 262144, 30000).astype(np.uint32)
+    eng.set_gate(0.45, -1)
+    out = {"prompt_tokens": 30000, "kv_context": 32768, "kv": "bf16", "verify_width": 9}
+    eng.generate(prompt, 32)
+    s = eng.stats()
+    out["greedy"] = {"tokens": int(s["emitted"]), "decode_tok_s": (s["emitted"] - 1) / (s["decode_gpu_ms"] / 1000.0),
+                     "prefill_s": s["ttft_ms"] / 1000.0, "acceptance": s["accepted"] / max(1.0, s["drafted"])}
+    if world == 1:
+        eng.generate(prompt, 16, temperature=0.8, seed=7)
+        s = eng.stats()
+        out["sampled_t0.8"] = {"tokens": int(s["emitted"]),
+                               "decode_tok_s": (s["emitted"] - 1) / (s["decode_gpu_ms"] / 1000.0),
+                               "acceptance": s["accepted"] / max(1.0, s["drafted"])}
+    out["verify_pass_ms_at_30000"] = eng.time_pass(0, 9, 3, pos=30000)
+    eng.close()
+    return out
 
 
 def main():
@@ -291,6 +324,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--long-context", action="store_true", help="also run BASELINE config 4 (about a minute more)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
