@@ -88,7 +88,7 @@ __global__ void head_chunks_kernel(GemmOut lm, int V, int M, float softcap, floa
 // chunk_best is [nranks][M][nchunks] (one slice per tensor-parallel rank's vocabulary range);
 // the order is total (value, then lowest index), so the result does not depend on the split.
 __global__ void head_finalize_kernel(const float2* chunk_best, int nchunks, int nranks, int M, StepParams* sp,
-                                     HeadResult* res, uint32_t* chain_out) {
+                                     HeadResult* res, uint32_t* chain_out, unsigned* tp_seq) {
     __shared__ uint32_t am[16];
     pdl_enter();
     const int lane = threadIdx.x & 31, m = threadIdx.x >> 5;
@@ -124,6 +124,7 @@ __global__ void head_finalize_kernel(const float2* chunk_best, int nchunks, int 
             sp->tokens[0] = t;
             sp->base_pos += M;
         }
+        if (tp_seq) *tp_seq += 1;  // the pass is complete on this rank
     }
 }
 
@@ -142,7 +143,7 @@ cudaError_t g4b_head_chunks_launch(const GemmOut& lm, int V, int M, float softca
 }
 
 cudaError_t g4b_head_finalize(const float2* chunk_best, int nchunks, int nranks, int M, StepParams* sp,
-                              HeadResult* res, uint32_t* chain_out, cudaStream_t st, bool pdl) {
+                              HeadResult* res, uint32_t* chain_out, unsigned* tp_seq, cudaStream_t st, bool pdl) {
     return launch(head_finalize_kernel, dim3(1), dim3(32 * 16), 0, st, pdl, chunk_best, nchunks, nranks, M, sp, res,
-                  chain_out);
+                  chain_out, tp_seq);
 }

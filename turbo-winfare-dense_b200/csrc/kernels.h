@@ -20,8 +20,11 @@ cudaError_t g4b_qkv_epi(const g4b::QkvEpiArgs& a, cudaStream_t st, bool pdl);
 cudaError_t g4b_geglu(const g4b::GemmOut& gu, int F, void* bfrag, int M, cudaStream_t st, bool pdl);
 // Norm/residual epilogue (post-attention with out_scale = 1, post-FFN with the layer scalar):
 // h_out = (h_in + rmsnorm(o)*w1) * out_scale; x = rmsnorm(h_out)*w2 -> B fragments.
-cudaError_t g4b_rowepi(const g4b::GemmOut& o, const float* h_in, float* h_out, const uint16_t* w1, float out_scale,
-                       const uint16_t* w2, int d, void* bfrag, int M, cudaStream_t st, bool pdl);
+// Under tensor parallelism (tg.n > 1) y is the rank-ordered sum of every rank's dense partial
+// (TpGather); otherwise o's slots or dense matrix.
+cudaError_t g4b_rowepi(const g4b::GemmOut& o, const g4b::TpGather& tg, const float* h_in, float* h_out,
+                       const uint16_t* w1, float out_scale, const uint16_t* w2, int d, void* bfrag, int M,
+                       cudaStream_t st, bool pdl);
 
 // ---- attention.cu
 // Attention of M rows over the KV ring; writes the output [M][qh*hd] as the o-projection's
@@ -44,8 +47,9 @@ cudaError_t g4b_head_chunks_launch(const g4b::GemmOut& lm, int V, int M, float s
 // against argmax[0..M-2]. With chain_out (drafter steps) the last row's argmax also becomes
 // the next pass's input: sp->tokens[0] = t, sp->base_pos += M, chain_out[sp->draft_step++] = t.
 // chunk_best holds nranks slices [M][nchunks] (tensor-parallel vocabulary ranges).
+// tp_seq (tensor parallelism, else nullptr) counts completed passes for the peer-memory sums.
 cudaError_t g4b_head_finalize(const float2* chunk_best, int nchunks, int nranks, int M, g4b::StepParams* sp,
-                              HeadResult* res, uint32_t* chain_out, cudaStream_t st, bool pdl);
+                              HeadResult* res, uint32_t* chain_out, unsigned* tp_seq, cudaStream_t st, bool pdl);
 
 // ---- side.cu: INT8 G64 GEMV (one row per warp) and the attention output gate
 namespace g4b {

@@ -58,6 +58,7 @@ DeviceModel::DeviceModel(const ModelOptions& opt) : opt_(opt) {
 
 DeviceModel::~DeviceModel() {
     if (stream_) cudaStreamSynchronize(stream_);
+    for (void* p : tp_ipc_open_) cudaIpcCloseMemHandle(p);
     for (auto& kv : graphs_) cudaGraphExecDestroy(kv.second);
     for (void* p : allocs_) cudaFree(p);
     if (sp_host_) cudaFreeHost(sp_host_);
@@ -422,6 +423,61 @@ void DeviceModel::init_buffers() {
     err_dev_ = static_cast<int*>(dmalloc(sizeof(int)));
     cuda_check(cudaMemsetAsync(err_dev_, 0, sizeof(int), stream_), "memset");
     cuda_check(cudaMemsetAsync(sp_dev_, 0, 4 * sizeof(StepParams), stream_), "memset");
+    if (opt_.tp > 1) init_tp_peers();
+}
+
+void DeviceModel::init_tp_peers() {
+#ifdef G4B_HAVE_NCCL
+    if (opt_.tp > kMaxTp) throw std::runtime_error("tensor parallelism supports at most 8 ranks");
+    const int d = h_.d_model;
+    const size_t ybytes = (size_t)2 * kMaxM * d * sizeof(float);
+    // One cudaMalloc holds both parities and the two flag words (IPC maps whole allocations).
+    void* base = dmalloc(ybytes + 256);
+    cuda_check(cudaMemset(base, 0, ybytes + 256), "memset");
+    tp_buf_ = static_cast<float*>(base);
+    tp_flags_ = reinterpret_cast<unsigned*>(static_cast<char*>(base) + ybytes);
+    tp_seq_ = static_cast<unsigned*>(dmalloc(sizeof(unsigned)));
+    cuda_check(cudaMemset(tp_seq_, 0, sizeof(unsigned)), "memset");
+    // Exchange the allocations' IPC handles over the communicator and map every peer's.
+    cudaIpcMemHandle_t mine;
+    cuda_check(cudaIpcGetMemHandle(&mine, base), "cudaIpcGetMemHandle");
+    const size_t hb = sizeof(cudaIpcMemHandle_t);
+    char* dh = static_cast<char*>(dmalloc(hb * opt_.tp));
+    cuda_check(cudaMemcpy(dh + hb * opt_.rank, &mine, hb, cudaMemcpyHostToDevice), "handle");
+    if (ncclAllGather(dh + hb * opt_.rank, dh, hb, ncclChar, (ncclComm_t)opt_.nccl_comm, stream_) != ncclSuccess)
+        throw std::runtime_error("ncclAllGather (IPC handles) failed");
+    std::vector<cudaIpcMemHandle_t> all(opt_.tp);
+    cuda_check(cudaStreamSynchronize(stream_), "sync");
+    cuda_check(cudaMemcpy(all.data(), dh, hb * opt_.tp, cudaMemcpyDeviceToHost), "handles");
+    for (int r = 0; r < opt_.tp; ++r) {
+        void* p = base;
+        if (r != opt_.rank) {
+            cuda_check(cudaIpcOpenMemHandle(&p, all[r], cudaIpcMemLazyEnablePeerAccess),
+                       "cudaIpcOpenMemHandle (the ranks' GPUs need peer access)");
+            tp_ipc_open_.push_back(p);
+        }
+        tp_peer_y_[r] = static_cast<float*>(p);
+        tp_peer_flags_[r] = reinterpret_cast<unsigned*>(static_cast<char*>(p) + ybytes);
+    }
+#endif
+}
+
+TpGather DeviceModel::tp_gather(int step, int parity) const {
+    TpGather g{};
+    g.n = opt_.tp;
+    g.rank = opt_.rank;
+    g.step = step;
+    g.err = err_dev_;
+    if (opt_.tp > 1) {
+        const size_t off = (size_t)parity * kMaxM * h_.d_model;
+        for (int r = 0; r < opt_.tp; ++r) {
+            g.y[r] = tp_peer_y_[r] + off;
+            g.flag[r] = tp_peer_flags_[r] + parity;
+        }
+        g.own_flag = tp_flags_ + parity;
+        g.seq = tp_seq_;
+    }
+    return g;
 }
 
 void DeviceModel::clear_kv() {
@@ -464,9 +520,10 @@ double DeviceModel::profile_gemms(int M, int reps, uint64_t* bytes, int* gemm_la
     for (int r = 0; r < reps; ++r) {
         for (auto& L : layers_) {
             gemm(L.qkv, bf_d_, M, nullptr);
-            gemm(L.o, bf_attn_, M, tp_out());
+            // Under TP the dense output goes to y_: peers may still read this rank's partial buffers.
+            gemm(L.o, bf_attn_, M, opt_.tp > 1 ? y_ : nullptr);
             gemm(L.gateup, bf_d_, M, nullptr);
-            gemm(L.down, bf_ff_, M, tp_out());
+            gemm(L.down, bf_ff_, M, opt_.tp > 1 ? y_ : nullptr);
         }
         gemm(lm_, bf_d_, M, nullptr);
     }
@@ -496,7 +553,9 @@ PartView DeviceModel::part_view(const QW& q, int M) const {
 
 GemmOut DeviceModel::partials(const QW& q, int M) const { return GemmOut{part_view(q, M), nullptr, q.N}; }
 
-float* DeviceModel::tp_out() const { return opt_.tp > 1 ? y_ : nullptr; }
+float* DeviceModel::tp_out(int parity) const {
+    return opt_.tp > 1 ? tp_buf_ + (size_t)parity * kMaxM * h_.d_model : nullptr;
+}
 
 void DeviceModel::gemm(const QW& q, const void* bfrag, int M, float* y) {
     const BFragView v = bfrag_view(const_cast<void*>(bfrag), q.ktiles * 128, M);
@@ -561,37 +620,25 @@ void DeviceModel::enqueue_raw(int M, PassKind kind, bool want_logits, uint32_t* 
         aa.scale = 1.0f;
         cuda_check(g4b_attention(aa, bf_attn_, stream_, pdl), "attention");
         // o projection + post-attention norm / residual + pre-FFN norm
-        // Under tensor parallelism the o and down GEMMs finish their own split-K sum into y_,
-        // which is then all-reduced in place; otherwise the epilogue sums the slots.
-        gemm(L.o, bf_attn_, M, tp_out());
+        // Under tensor parallelism the o and down GEMMs finish their own split-K sum into this
+        // rank's peer-mapped partial buffer and the norm epilogue sums the ranks' partials
+        // over NVLink (TpGather); otherwise the epilogue sums the slots.
+        gemm(L.o, bf_attn_, M, tp_out(0));
         GemmOut oo = partials(L.o, M);
-#ifdef G4B_HAVE_NCCL
-        if (opt_.tp > 1) {
-            if (ncclAllReduce(y_, y_, (size_t)M * d, ncclFloat, ncclSum, (ncclComm_t)opt_.nccl_comm, stream_) !=
-                ncclSuccess)
-                throw std::runtime_error("ncclAllReduce (attention) failed");
-            oo = GemmOut{PartView{}, y_, d};
-        }
-#endif
-        cuda_check(g4b_rowepi(oo, hres_[cur], hres_[1 - cur], L.pa_norm, 1.0f, L.pf_norm, d, bf_d_, M, stream_, pdl),
+        if (opt_.tp > 1) oo = GemmOut{PartView{}, nullptr, d};
+        cuda_check(g4b_rowepi(oo, tp_gather(2 * (int)l, 0), hres_[cur], hres_[1 - cur], L.pa_norm, 1.0f, L.pf_norm, d,
+                              bf_d_, M, stream_, pdl),
                    "post_attn");
         cur = 1 - cur;
         // FFN
         gemm(L.gateup, bf_d_, M, nullptr);
         cuda_check(g4b_geglu(partials(L.gateup, M), L.F, bf_ff_, M, stream_, pdl), "geglu");
-        gemm(L.down, bf_ff_, M, tp_out());
+        gemm(L.down, bf_ff_, M, tp_out(1));
         GemmOut dn = partials(L.down, M);
-#ifdef G4B_HAVE_NCCL
-        if (opt_.tp > 1) {
-            if (ncclAllReduce(y_, y_, (size_t)M * d, ncclFloat, ncclSum, (ncclComm_t)opt_.nccl_comm, stream_) !=
-                ncclSuccess)
-                throw std::runtime_error("ncclAllReduce (FFN) failed");
-            dn = GemmOut{PartView{}, y_, d};
-        }
-#endif
+        if (opt_.tp > 1) dn = GemmOut{PartView{}, nullptr, d};
         const uint16_t* w_next = (l + 1 < layers_.size()) ? layers_[l + 1].in_norm : final_norm_;
-        cuda_check(g4b_rowepi(dn, hres_[cur], hres_[1 - cur], L.pffn_norm, L.scalar, w_next, d, bf_d_, M, stream_,
-                              pdl),
+        cuda_check(g4b_rowepi(dn, tp_gather(2 * (int)l + 1, 1), hres_[cur], hres_[1 - cur], L.pffn_norm, L.scalar,
+                              w_next, d, bf_d_, M, stream_, pdl),
                    "post_ffn");
         cur = 1 - cur;
     }
@@ -611,7 +658,8 @@ void DeviceModel::enqueue_raw(int M, PassKind kind, bool want_logits, uint32_t* 
                            ncclSuccess)
         throw std::runtime_error("ncclAllGather (LM head) failed");
 #endif
-    cuda_check(g4b_head_finalize(chunk_best_, nch, opt_.tp, M, sp, res_dev_, chain_out, stream_, pdl),
+    cuda_check(g4b_head_finalize(chunk_best_, nch, opt_.tp, M, sp, res_dev_, chain_out, opt_.tp > 1 ? tp_seq_ : nullptr,
+                                 stream_, pdl),
                "head_finalize");
 }
 

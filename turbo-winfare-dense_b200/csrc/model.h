@@ -106,13 +106,15 @@ class DeviceModel {
 
    private:
     void init_buffers();
+    void init_tp_peers();  // tensor parallelism: peer-mapped partial buffers and flags
+    TpGather tp_gather(int step, int parity) const;
     void build_layer_from_host(uint32_t l, const uint8_t* layer_ptr);
     void enqueue_raw(int M, PassKind kind, bool want_logits, uint32_t* chain_out);
     // One verify GEMM; y == nullptr leaves split-K partials for the consumer (partials()).
     void gemm(const QW& q, const void* bfrag, int M, float* y);
     PartView part_view(const QW& q, int M) const;
     GemmOut partials(const QW& q, int M) const;
-    float* tp_out() const;  // dense output for GEMMs followed by an all-reduce, else nullptr
+    float* tp_out(int parity) const;  // under TP: this rank's partial buffer of that parity, else nullptr
     void upload_qw(QW& q, const uint32_t* W, const uint16_t* S, const uint16_t* B, int N, int K);
     void alloc_qw(QW& q, int N, int K);
     uint16_t* upload_u16(const uint16_t* src, size_t n);
@@ -136,7 +138,15 @@ class DeviceModel {
     float* part_ = nullptr;
     size_t part_floats_ = 0;
     float* q_buf_ = nullptr;
-    float* y_ = nullptr;       // dense GEMM output ahead of an all-reduce [16][max N]
+    float* y_ = nullptr;       // dense GEMM output [16][max N]
+    // tensor parallelism: this rank's [2 parities][16][d] partials + [2] flags (IPC-exported),
+    // the peers' mappings, and the pass counter that makes every step's epoch distinct
+    float* tp_buf_ = nullptr;
+    unsigned* tp_flags_ = nullptr;
+    unsigned* tp_seq_ = nullptr;
+    float* tp_peer_y_[kMaxTp] = {};
+    unsigned* tp_peer_flags_[kMaxTp] = {};
+    std::vector<void*> tp_ipc_open_;
     unsigned* cnt_ = nullptr;  // split-K arrival counters of the GEMM running on stream_
     float2* chunk_best_ = nullptr;
     float* logits_ = nullptr;

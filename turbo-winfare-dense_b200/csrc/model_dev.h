@@ -114,6 +114,22 @@ struct QkvEpiArgs {
     int kv_bf16;             // 1: round K/V through bf16 instead of FP16 (long-context mode)
 };
 
+// Tensor-parallel sum of one step's dense partial outputs over peer memory (NVLink). Every rank
+// writes its partial [M][ld] into its own buffer y[rank] and, once the consuming kernel starts
+// (so the partial is complete), publishes epoch = seq * 256 + step + 1 in its flag word; each
+// consumer waits (bounded) for every rank's flag and adds the ranks' partials in rank order,
+// so all ranks compute identical sums. Two buffer/flag parities alternate between the o and the
+// down projection, so a buffer is rewritten only after every rank has consumed it.
+constexpr int kMaxTp = 8;
+struct TpGather {
+    const float* y[kMaxTp];        // each rank's partial buffer for this step (peer-mapped)
+    const unsigned* flag[kMaxTp];  // each rank's flag word for this step's parity (peer-mapped)
+    unsigned* own_flag;            // this rank's flag word
+    const unsigned* seq;           // passes completed on this rank (advanced by head_finalize)
+    int n, rank, step;             // ranks (1: no gather), this rank, step index within a pass
+    int* err;                      // set to 3 if a peer's flag never arrived
+};
+
 struct AttnArgs {
     const float* q;          // [M][qh][hd]
     const uint16_t* k_ring;

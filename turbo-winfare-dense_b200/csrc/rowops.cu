@@ -20,6 +20,7 @@
 #include "launch.cuh"
 #include "model_dev.h"
 #include "rowmath.cuh"
+#include "tma.cuh"
 
 #include <algorithm>
 
@@ -152,8 +153,50 @@ constexpr int kEpiWarps = 8;         // warps per CTA in the cluster form
 constexpr int kEpiGroupsPerWarp = 2;  // d <= 16 CTAs x 8 warps x 2 groups x 64 = 16384
 constexpr int kEpiMaxWarps = 32;
 
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+    unsigned v;
+    asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// Tensor parallelism: publish this rank's flag (its partial is complete once this kernel
+// runs) and wait, bounded, for every peer's.
+__device__ void tp_sync(const TpGather& tg, bool publisher) {
+    if (threadIdx.x == 0) {
+        const unsigned epoch = *tg.seq * 256u + (unsigned)tg.step + 1u;
+        if (publisher) {
+            __threadfence_system();
+            asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(tg.own_flag), "r"(epoch) : "memory");
+        }
+        for (int r = 0; r < tg.n; ++r) {
+            if (r == tg.rank) continue;
+            const uint64_t t0 = global_ns();
+            while ((int)(ld_acquire_sys(tg.flag[r]) - epoch) < 0) {
+                if (global_ns() - t0 > kWaitLimitNs) {
+                    atomicExch(tg.err, 3);
+                    break;
+                }
+            }
+        }
+    }
+    __syncthreads();
+}
+
+// Columns c, c+1 of row m summed over the ranks in rank order (peer partials bypass the caches).
+__device__ __forceinline__ float2 tp_pair(const TpGather& tg, int m, int ld, int c) {
+    float2 s = make_float2(0.f, 0.f);
+    for (int r = 0; r < tg.n; ++r) {
+        const float2* p = reinterpret_cast<const float2*>(tg.y[r] + (size_t)m * ld + c);
+        const float2 v = r == tg.rank ? __ldcg(p) : __ldcv(p);
+        s.x += v.x;
+        s.y += v.y;
+    }
+    return s;
+}
+
 template <bool CLUSTER>
-__global__ void __launch_bounds__(kEpiMaxWarps * 32) rowepi_kernel(GemmOut o, const float* __restrict__ h_in,
+__global__ void __launch_bounds__(kEpiMaxWarps * 32) rowepi_kernel(GemmOut o, TpGather tg,
+                                                                    const float* __restrict__ h_in,
                                                                     float* __restrict__ h_out,
                                                                     const uint16_t* __restrict__ w1, float out_scale,
                                                                     const uint16_t* __restrict__ w2, int d,
@@ -162,6 +205,7 @@ __global__ void __launch_bounds__(kEpiMaxWarps * 32) rowepi_kernel(GemmOut o, co
     __shared__ float4 cta_sum;
     __shared__ __half stage[kEpiMaxWarps][128];
     pdl_enter();
+    if (tg.n > 1) tp_sync(tg, blockIdx.x == 0 && blockIdx.y == 0);
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     const int rank = CLUSTER ? (int)cg::this_cluster().block_rank() : 0;
     const int m = blockIdx.y;
@@ -178,7 +222,7 @@ __global__ void __launch_bounds__(kEpiMaxWarps * 32) rowepi_kernel(GemmOut o, co
         const int c0 = gi * 64 + 2 * lane;
         y[j] = h[j] = make_float2(0.f, 0.f);
         if (gi < g_end && c0 < d) {
-            y[j] = gemm_out_pair(o, m, c0);
+            y[j] = tg.n > 1 ? tp_pair(tg, m, o.ld, c0) : gemm_out_pair(o, m, c0);
             h[j] = *reinterpret_cast<const float2*>(h_in + (size_t)m * d + c0);
             const float ca = y[j].x * bf16_to_f32(w1[c0]), cb = y[j].y * bf16_to_f32(w1[c0 + 1]);
             acc.x += y[j].x * y[j].x + y[j].y * y[j].y;
@@ -310,13 +354,14 @@ cudaError_t g4b_qkv_epi(const QkvEpiArgs& a, cudaStream_t st, bool pdl) {
     return launch(qkv_epi_kernel, dim3(a.M * (a.qh + a.kvh)), dim3(a.hd / 2), 0, st, pdl, a);
 }
 
-cudaError_t g4b_rowepi(const GemmOut& o, const float* h_in, float* h_out, const uint16_t* w1, float out_scale,
-                       const uint16_t* w2, int d, void* bfrag, int M, cudaStream_t st, bool pdl) {
+cudaError_t g4b_rowepi(const GemmOut& o, const TpGather& tg, const float* h_in, float* h_out, const uint16_t* w1,
+                       float out_scale, const uint16_t* w2, int d, void* bfrag, int M, cudaStream_t st, bool pdl) {
     if ((o.ld | d) & 1) return cudaErrorInvalidValue;  // float2 loads
+    if (tg.n < 1 || tg.n > kMaxTp) return cudaErrorInvalidValue;
     const int ngp = (d + 127) / 128 * 2;
     if (ngp <= kEpiMaxWarps)  // one CTA per row, one warp per group
-        return launch(rowepi_kernel<false>, dim3(1, M), dim3(ngp * 32), 0, st, pdl, o, h_in, h_out, w1, out_scale, w2,
-                      d, bfrag, M);
+        return launch(rowepi_kernel<false>, dim3(1, M), dim3(ngp * 32), 0, st, pdl, o, tg, h_in, h_out, w1, out_scale,
+                      w2, d, bfrag, M);
     if ((ngp + kEpiClusters - 1) / kEpiClusters > kEpiWarps * kEpiGroupsPerWarp) return cudaErrorInvalidValue;
     static bool attr_set = false;
     if (!attr_set) {
@@ -338,7 +383,7 @@ cudaError_t g4b_rowepi(const GemmOut& o, const float* h_in, float* h_out, const 
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 2 : 1;
-    return cudaLaunchKernelEx(&cfg, rowepi_kernel<true>, o, h_in, h_out, w1, out_scale, w2, d, bfrag, M);
+    return cudaLaunchKernelEx(&cfg, rowepi_kernel<true>, o, tg, h_in, h_out, w1, out_scale, w2, d, bfrag, M);
 }
 
 cudaError_t g4b_geglu(const GemmOut& gu, int F, void* bfrag, int M, cudaStream_t st, bool pdl) {
