@@ -29,16 +29,18 @@ G4B_API int g4b_qmat_create(const uint32_t* W, const uint16_t* S, const uint16_t
                             void* stream, g4b_qmat** out);
 G4B_API void g4b_qmat_destroy(g4b_qmat* q);
 
-/* out[m][n] = sum_k (q[n][k] * s + b) * x[m][k] for m < M <= 16: the batched verify GEMM
+/* out[m][n] = sum_k (q[n][k] * s + b) * x[m][k] for m < M <= 128: the batched INT4 GEMM
  * (shaders/GemmInt4Batch.hlsl:64-143; M = 1 is GemvInt4, shaders/GemvInt4.hlsl:31-54).
- * x is fp32 [M][ldx], out fp32 [M][ldo]. Launches two kernels: fragment preparation and the
- * GEMM. Calls on one matrix must be stream-ordered (they share the matrix's workspace). */
+ * M <= 16 runs the HBM-streaming verify GEMM; 17 <= M <= 128 (prefill chunks) the tcgen05
+ * tensor-core GEMM. x is fp32 [M][ldx], out fp32 [M][ldo]. Launches two kernels: activation
+ * preparation and the GEMM. Calls on one matrix must be stream-ordered (they share the
+ * matrix's workspace). */
 G4B_API int g4b_qmat_gemm(g4b_qmat* q, const float* x, int ldx, int M, float* out, int ldo, void* stream);
 /* The two halves of g4b_qmat_gemm, for timing the GEMM kernel alone. */
 G4B_API int g4b_qmat_prepare_input(g4b_qmat* q, const float* x, int ldx, int M, void* stream);
 G4B_API int g4b_qmat_run(g4b_qmat* q, int M, float* out, int ldo, void* stream);
-/* The GEMM kernel without its in-kernel split-K sum, leaving the partials in the matrix's
- * workspace (for timing the weight stream alone). */
+/* The verify GEMM kernel (M <= 16) without its in-kernel split-K sum, leaving the partials in
+ * the matrix's workspace (for timing the weight stream alone). */
 G4B_API int g4b_qmat_run_partial(g4b_qmat* q, int M, void* stream);
 /* g4b_qmat_run without any allocation: the same kernel, grid and slot order (bit-identical
  * output), but the split-K scratch -- partial slots and per-row-group arrival counters -- is a

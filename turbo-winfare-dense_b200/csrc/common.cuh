@@ -30,6 +30,14 @@
 //    16q for odd nibbles) is the value q * 2^-24, so a single AND turns two nibbles into
 //    an exact fp16x2 operand; the 2^24 (and 1/16) factors are folded into the activation
 //    fragments and the final scale.
+//
+// 4. Wide activation layout, for passes of 17..128 rows (prefill chunks) feeding the
+//    tcgen05 prefill GEMM (pgemm.cu). Same hi/lo split and {E, Y} records as (2), stored
+//    as ready-made shared-memory images of the MMA's B operand: per 64-group g, a 16 KB hi
+//    tile and a 16 KB lo tile of 128 rows x 64 fp16 in the 128-byte-swizzled K-major form
+//    (row m at byte m*128, 16-byte chunk c of the row at chunk position c ^ (m % 8)):
+//      hi[K/64][16384 B], lo[K/64][16384 B], gsum[K/64][128 rows] float2 {E, Y}
+//    so one bulk copy per tile lands it in shared memory exactly as the MMA reads it.
 #pragma once
 #include <cuda_fp16.h>
 #include <cstdint>
@@ -42,7 +50,9 @@ constexpr int kWarpRows = kRowsPerTile * kTilesPerWarp;  // 64
 constexpr int kKTile = 128;              // k-tile width
 constexpr int kKTileBytes = 4608;        // one (row group, k-tile) block
 constexpr int kNibBytes = 4096;
-constexpr int kMaxM = 16;                // verify / prefill rows per pass
+constexpr int kMaxM = 16;                // rows of a verify pass (B-frag layout)
+constexpr int kPrefillRows = 128;        // rows of a prefill pass (wide layout)
+constexpr int kWideTileBytes = kPrefillRows * 128;  // one 64-group's hi (or lo) tile
 
 // B-operand mode for M rows.
 struct BMode {
@@ -61,19 +71,32 @@ __host__ __device__ inline size_t bfrag_frag_bytes(int K, int M) {
 __host__ __device__ inline size_t bfrag_gsum_bytes(int K, int M) {
     return (size_t)(K / 64) * bmode_for(M).nacc * 8 * sizeof(float2);
 }
-// Capacity of one B-frag buffer for K columns at the maximum M.
+// Bytes of the wide layout (M > kMaxM) for K columns.
+__host__ __device__ inline size_t wide_bytes(int K) {
+    return (size_t)(K / 64) * (2 * kWideTileBytes + kPrefillRows * sizeof(float2));
+}
+// Capacity of one activation buffer for K columns at any M (either layout).
 __host__ __device__ inline size_t bfrag_capacity(int K) {
-    return bfrag_frag_bytes(K, kMaxM) + bfrag_gsum_bytes(K, kMaxM);
+    const size_t narrow = bfrag_frag_bytes(K, kMaxM) + bfrag_gsum_bytes(K, kMaxM);
+    const size_t wide = wide_bytes(K);
+    return narrow > wide ? narrow : wide;
 }
 
 struct BFragView {
-    uint4* frag;   // [K/32][nb][32]
-    float2* gsum;  // [K/64][nacc][8]
+    uint4* frag;      // B-frag layout: [K/32][nb][32];  wide layout: the hi tiles
+    float2* gsum;     // B-frag layout: [K/64][nacc][8]; wide layout: [K/64][128]
+    uint32_t lo_off;  // wide layout: bytes from a group's hi tile to its lo tile; 0 = B-frag layout
 };
 __host__ __device__ inline BFragView bfrag_view(void* base, int K, int M) {
     BFragView v;
     v.frag = reinterpret_cast<uint4*>(base);
-    v.gsum = reinterpret_cast<float2*>(reinterpret_cast<char*>(base) + bfrag_frag_bytes(K, M));
+    if (M > kMaxM) {
+        v.lo_off = (uint32_t)((K / 64) * kWideTileBytes);
+        v.gsum = reinterpret_cast<float2*>(reinterpret_cast<char*>(base) + 2 * (size_t)v.lo_off);
+    } else {
+        v.lo_off = 0;
+        v.gsum = reinterpret_cast<float2*>(reinterpret_cast<char*>(base) + bfrag_frag_bytes(K, M));
+    }
     return v;
 }
 

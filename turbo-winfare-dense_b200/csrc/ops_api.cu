@@ -8,6 +8,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "pgemm.h"
 #include "vgemm.h"
 
 namespace {
@@ -30,6 +31,11 @@ struct g4b_qmat {
     unsigned* cnt;    // split-K arrival counters [n_crg], zero between launches
     int max_slots;    // slots per row group sized for every M
     int* err;         // device error word of the bounded waits
+    // prefill GEMM (17..128 rows): its weight layout, split-K slots and tile counters
+    void* pw;
+    float* ppart;
+    unsigned* pcnt;
+    int n_tiles, pmax_slots;
 };
 
 extern "C" {
@@ -57,6 +63,13 @@ int g4b_qmat_create(const uint32_t* W, const uint16_t* S, const uint16_t* B, int
     if ((e = cudaMalloc(&q->cnt, q->n_crg * sizeof(unsigned))) != cudaSuccess) { g4b_qmat_destroy(q); return fail(e, "cudaMalloc(cnt)"); }
     if ((e = cudaMemsetAsync(q->cnt, 0, q->n_crg * sizeof(unsigned), st)) != cudaSuccess) { g4b_qmat_destroy(q); return fail(e, "memset"); }
     if ((e = cudaMalloc(&q->err, sizeof(int))) != cudaSuccess) { g4b_qmat_destroy(q); return fail(e, "cudaMalloc(err)"); }
+    q->n_tiles = pgemm_n_tiles(N);
+    q->pmax_slots = pgemm_max_slots(q->n_tiles, K / 64, pgemm_grid(q->n_tiles, K / 64));
+    if ((e = cudaMalloc(&q->pw, pgemm_weight_bytes(N, K))) != cudaSuccess) { g4b_qmat_destroy(q); return fail(e, "cudaMalloc(prefill weights)"); }
+    if ((e = pgemm_repack(W, S, B, N, K, q->pw, st)) != cudaSuccess) { g4b_qmat_destroy(q); return fail(e, "prefill repack"); }
+    if ((e = cudaMalloc(&q->ppart, pgemm_part_floats(q->n_tiles, q->pmax_slots) * sizeof(float))) != cudaSuccess) { g4b_qmat_destroy(q); return fail(e, "cudaMalloc(prefill part)"); }
+    if ((e = cudaMalloc(&q->pcnt, q->n_tiles * sizeof(unsigned))) != cudaSuccess) { g4b_qmat_destroy(q); return fail(e, "cudaMalloc(prefill cnt)"); }
+    if ((e = cudaMemsetAsync(q->pcnt, 0, q->n_tiles * sizeof(unsigned), st)) != cudaSuccess) { g4b_qmat_destroy(q); return fail(e, "memset"); }
     if ((e = cudaMemsetAsync(q->err, 0, sizeof(int), st)) != cudaSuccess) { g4b_qmat_destroy(q); return fail(e, "memset"); }
     if ((e = cudaStreamSynchronize(st)) != cudaSuccess) { g4b_qmat_destroy(q); return fail(e, "g4b_qmat_create"); }
     *out = q;
@@ -70,11 +83,15 @@ void g4b_qmat_destroy(g4b_qmat* q) {
     cudaFree(q->part);
     cudaFree(q->cnt);
     cudaFree(q->err);
+    cudaFree(q->pw);
+    cudaFree(q->ppart);
+    cudaFree(q->pcnt);
     delete q;
 }
 
 int g4b_qmat_prepare_input(g4b_qmat* q, const float* x, int ldx, int M, void* stream) {
-    if (!q || !x || M < 1 || M > g4b::kMaxM || ldx < q->K) return fail_msg("g4b_qmat_prepare_input: bad arguments");
+    if (!q || !x || M < 1 || M > g4b::kPrefillRows || ldx < q->K)
+        return fail_msg("g4b_qmat_prepare_input: bad arguments");
     cudaError_t e = g4b_bfrag_from_f32(x, ldx, M, q->K, q->bfrag, (cudaStream_t)stream, false);
     return e == cudaSuccess ? 0 : fail(e, "bfrag_from_f32");
 }
@@ -111,7 +128,25 @@ int g4b_qmat_run_partial(g4b_qmat* q, int M, void* stream) {
 }
 
 int g4b_qmat_run(g4b_qmat* q, int M, float* out, int ldo, void* stream) {
-    if (!q || !out || M < 1 || M > g4b::kMaxM || ldo < q->N) return fail_msg("g4b_qmat_run: bad arguments");
+    if (!q || !out || M < 1 || M > g4b::kPrefillRows || ldo < q->N) return fail_msg("g4b_qmat_run: bad arguments");
+    if (M > g4b::kMaxM) {
+        PgemmParams pp{};
+        pp.w = q->pw;
+        pp.act = q->bfrag;
+        pp.g_layout = q->ktiles * 2;
+        pp.y = out;
+        pp.ldy = ldo;
+        pp.part = q->ppart;
+        pp.cnt = q->pcnt;
+        pp.N = q->N;
+        pp.K = q->K;
+        pp.M = M;
+        pp.n_tiles = q->n_tiles;
+        pp.max_slots = q->pmax_slots;
+        pp.err = q->err;
+        cudaError_t e = pgemm_launch(pp, (cudaStream_t)stream, false);
+        return e == cudaSuccess ? 0 : fail(e, "pgemm_launch");
+    }
     VgemmParams p = qmat_params(q, M);
     p.y = out;
     p.ldy = ldo;
@@ -226,7 +261,7 @@ int g4b_qmat_check_error(g4b_qmat* q) {
     int h = 0;
     cudaError_t e = cudaMemcpy(&h, q->err, sizeof(int), cudaMemcpyDeviceToHost);
     if (e != cudaSuccess) return fail(e, "g4b_qmat_check_error");
-    if (h) return fail_msg("verify GEMM: a bounded wait gave up (weights or fragments never arrived)");
+    if (h) return fail_msg("INT4 GEMM: a bounded wait gave up (weights or fragments never arrived)");
     return 0;
 }
 
