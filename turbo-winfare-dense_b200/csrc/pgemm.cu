@@ -48,7 +48,8 @@ constexpr int kThreadsP = (kMmaWarp + 1) * 32;     // 448
 constexpr int kMaxRegs = (512 / ((kThreadsP / 32 + 3) / 4)) / 8 * 8;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kAccCols = 128;          // one fp32 accumulator: 128 activation rows
-constexpr uint32_t kACol0 = 2 * kAccCols;   // A buffers after the two accumulators
+constexpr int kAccBufs = 3;                 // accumulators in flight between MMA and epilogue
+constexpr uint32_t kACol0 = kAccBufs * kAccCols;  // A buffers after the accumulators
 constexpr uint32_t kACols = 32;             // 64 fp16 of a weight row
 constexpr int kErrPgemm = 6;
 
@@ -63,7 +64,7 @@ constexpr uint32_t kStageBytes = (kOffEY + kPrefillRows * 8 + 1023) / 1024 * 102
 struct Bars {
     uint64_t full[kStages], empty[kStages];
     uint64_t conv[kADepth], a_empty[kADepth];
-    uint64_t acc_full[2], acc_empty[2];
+    uint64_t acc_full[kAccBufs], acc_empty[kAccBufs];
     uint64_t done;
     uint32_t tmem_base;
     int abort;
@@ -80,7 +81,7 @@ __device__ __forceinline__ long long cta_of_unit(long long u, long long T, int C
 __device__ __forceinline__ bool pg_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* err) {
     if (mbar_try_wait(bar, parity)) return true;
     const uint64_t t0 = global_ns();
-    while (!mbar_try_wait(bar, parity)) {
+    while (!mbar_try_wait_sleep(bar, parity, 1000000u)) {
         if (*abort) return false;
         if (global_ns() - t0 > kWaitLimitNs) {
             *abort = 1;
@@ -117,7 +118,7 @@ __global__ void __maxnreg__(kMaxRegs) pgemm_kernel(PgemmParams p) {
             mbar_init(&bars.conv[a], kConvWarps);
             mbar_init(&bars.a_empty[a], 1);
         }
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < kAccBufs; ++b) {
             mbar_init(&bars.acc_full[b], 1);
             mbar_init(&bars.acc_empty[b], kEpiWarps);
         }
@@ -182,10 +183,10 @@ __global__ void __maxnreg__(kMaxRegs) pgemm_kernel(PgemmParams p) {
         if (lane == 0) {
             const uint32_t idesc = tc::idesc_f16(kPgemmTileRows, nmma);
             for (int i = 0; i < n; ++i) {
-                const int s = i % kStages, a = i % kADepth, b = i & 1;
+                const int s = i % kStages, a = i % kADepth, b = i % kAccBufs;
                 bool ok = pg_wait(&bars.full[s], (i / kStages) & 1, abort, p.err);
                 ok = ok && pg_wait(&bars.conv[a], (i / kADepth) & 1, abort, p.err);
-                ok = ok && (i < 2 || pg_wait(&bars.acc_empty[b], ((i >> 1) + 1) & 1, abort, p.err));
+                ok = ok && (i < kAccBufs || pg_wait(&bars.acc_empty[b], ((i / kAccBufs) + 1) & 1, abort, p.err));
                 tc::fence_after_sync();
                 if (ok) {
                     const uint32_t d = tmem + b * kAccCols;
@@ -248,25 +249,25 @@ __global__ void __maxnreg__(kMaxRegs) pgemm_kernel(PgemmParams p) {
         for (int i = 0; i < n; ++i) {
             const long long u = u0 + i;
             const int t = (int)(u / G), g = (int)(u - (long long)t * G);
-            const int s = i % kStages, b = i & 1;
-            bool ok = pg_wait(&bars.acc_full[b], (i >> 1) & 1, abort, p.err);
+            const int s = i % kStages, b = i % kAccBufs;
+            bool ok = pg_wait(&bars.acc_full[b], (i / kAccBufs) & 1, abort, p.err);
             ok = ok && pg_wait(&bars.full[s], (i / kStages) & 1, abort, p.err);
             ok = __all_sync(0xffffffffu, ok);
             tc::fence_after_sync();
-            if (ok) {
+            if (ok && c0 < nmma) {  // warp-uniform
                 const uint32_t sbw = *reinterpret_cast<const uint32_t*>(stage(s) + kOffSB + r * 4);
                 const float sc = bf16_lo(sbw), bi = bf16_hi(sbw);
-                const float2* eyv = reinterpret_cast<const float2*>(stage(s) + kOffEY) + c0;
+                const float4* eyv = reinterpret_cast<const float4*>(stage(s) + kOffEY) + c0 / 2;
 #pragma unroll
-                for (int jc = 0; jc < kEpiCols / 8; ++jc) {
-                    if (c0 + 8 * jc >= nmma) break;  // warp-uniform
-                    float P[8];
-                    tc::ld8(tl + b * kAccCols + 8 * jc, P);
+                for (int jc = 0; jc < kEpiCols; jc += 16) {
+                    float P[16];
+                    tc::ld16(tl + b * kAccCols + jc, P);
                     tc::wait_ld();
 #pragma unroll
-                    for (int j = 0; j < 8; ++j) {
-                        const float2 e = eyv[8 * jc + j];
-                        acc[8 * jc + j] = fmaf(e.x, fmaf(bi, e.y, sc * P[j]), acc[8 * jc + j]);
+                    for (int j = 0; j < 16; j += 2) {
+                        const float4 e = eyv[(jc + j) / 2];  // {E, Y} of columns jc+j, jc+j+1
+                        acc[jc + j] = fmaf(e.x, fmaf(bi, e.y, sc * P[j]), acc[jc + j]);
+                        acc[jc + j + 1] = fmaf(e.z, fmaf(bi, e.w, sc * P[j + 1]), acc[jc + j + 1]);
                     }
                 }
             }

@@ -8,6 +8,11 @@ profiler started with `--profile-from-start off` sees exactly that piece.
     python -m g4dense_b200.profile gemms [--only NAME] [--batch M]
         each distinct verify-GEMM shape of the 31B pass once (the kernel as the pass runs it:
         split-K slots left for the consuming epilogue), through the g4b_qmat C-ABI.
+    python -m g4dense_b200.profile pgemm [--only NAME] [--batch M] [--reps R]
+        each distinct GEMM shape of a 31B prefill chunk of M (17..128) rows on the tcgen05
+        prefill GEMM: CUDA-event time per launch (mean of R after 3 warm launches), the
+        algorithmic rate 2*M*N*K / time, and the weighted sum over one prefill pass; then
+        one launch per shape inside the profiler range.
 
 Synthetic weights; nothing here is on the product path."""
 from __future__ import annotations
@@ -79,6 +84,50 @@ def run_gemms(only, batch):
     print(json.dumps({"gemms": [n for n, _ in mats], "batch": batch}))
 
 
+def _make_qmat(rng, N, K):
+    import torch
+    from .api import QMat
+    W = torch.from_numpy(rng.integers(0, 2**32, (N, K // 8), dtype=np.uint32).view(np.int32)).cuda()
+    S = torch.full((N, K // 64), 0x3C00, dtype=torch.int16, device="cuda")
+    B = torch.zeros((N, K // 64), dtype=torch.int16, device="cuda")
+    return QMat(W, S, B)
+
+
+def run_pgemm(only, batch, reps):
+    import torch
+    rng = np.random.default_rng(0)
+    rows, mats = [], []
+    pass_us = 0.0
+    for name, N, K in GEMM_SHAPES:
+        if (only and name != only) or (not only and name == "lm_head"):
+            continue  # a prefill chunk ranks only its last row: the LM head runs on one row
+        q = _make_qmat(rng, N, K)
+        x = torch.randn(batch, K, device="cuda")
+        y = torch.empty(batch, N, device="cuda")
+        q.prepare(x)
+        for _ in range(3):
+            q.run(batch, y)
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record()
+        for _ in range(reps):
+            q.run(batch, y)
+        ev1.record()
+        torch.cuda.synchronize()
+        q.check_error()
+        us = ev0.elapsed_time(ev1) * 1000.0 / reps
+        tflops = 2.0 * batch * N * K / (us * 1e-6) / 1e12
+        pass_us += us * GEMM_COUNTS[name]
+        rows.append({"gemm": name, "N": N, "K": K, "us": round(us, 2), "tflops": round(tflops, 1)})
+        mats.append((q, y))
+    start, stop = _profiler()
+    start()
+    for q, y in mats:
+        q.run(batch, y)
+    torch.cuda.synchronize()
+    stop()
+    print(json.dumps({"batch": batch, "shapes": rows, "prefill_pass_gemm_ms": round(pass_us / 1000.0, 3)}))
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser(prog="python -m g4dense_b200.profile")
     sub = ap.add_subparsers(dest="cmd", required=True)
@@ -90,9 +139,15 @@ def main(argv=None):
     g = sub.add_parser("gemms")
     g.add_argument("--only", default=None)
     g.add_argument("--batch", type=int, default=5)
+    pg = sub.add_parser("pgemm")
+    pg.add_argument("--only", default=None)
+    pg.add_argument("--batch", type=int, default=128)
+    pg.add_argument("--reps", type=int, default=20)
     a = ap.parse_args(argv)
     if a.cmd == "pass":
         run_pass(a.which, a.batch, a.pos, a.layers)
+    elif a.cmd == "pgemm":
+        run_pgemm(a.only, a.batch, a.reps)
     else:
         run_gemms(a.only, a.batch)
     return 0
