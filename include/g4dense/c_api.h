@@ -105,8 +105,10 @@ G4DENSE_API const char* g4dense_engine_generate_tokens(void* handle, const unsig
 /* Copies up to `cap` ids of the last generation into out; returns the count. */
 G4DENSE_API int g4dense_engine_last_tokens(void* handle, unsigned int* out, int cap);
 /* ForwardRunner::forward_batch (include/g4dense/runner.hpp:110-111): one pass over `batch`
- * (1..16) positions from base_position; out_logits (host, may be NULL) receives the last
- * row's softcapped logits, or all rows' when all_positions != 0. Returns 0 or -1. */
+ * positions from base_position; out_logits (host, may be NULL) receives the last row's
+ * softcapped logits, or all rows' when all_positions != 0. 1..16 rows run the verify pass;
+ * 17..128 rows a tensor-core prefill chunk, which returns the last row only (all_positions
+ * with more than 16 rows is an error). Returns 0 or -1. */
 G4DENSE_API int g4dense_engine_forward_batch(void* handle, const unsigned int* token_ids, int batch,
                                              int base_position, float* out_logits, int all_positions);
 /* Greedy decoding knobs beyond G4DenseGenerationOptions (additive): stop token id, and the
@@ -127,8 +129,8 @@ G4DENSE_API int g4dense_engine_last_stats(void* handle, double* out, int n);
 G4DENSE_API int g4dense_engine_set_gate(void* handle, double min_accept, int window);
 /* Device time (CUDA events) of one forward pass of `batch` rows at positions pos..pos+batch-1
  * on the target (which = 0) or the drafter (which = 1), averaged over `reps` back-to-back graph
- * replays; attention spans the pos earlier cache entries. Overwrites those rows of the KV
- * cache. -1 on error. */
+ * replays; attention spans the pos earlier cache entries. batch 1..16 times a verify pass,
+ * 17..128 a tensor-core prefill chunk. Overwrites those rows of the KV cache. -1 on error. */
 G4DENSE_API double g4dense_engine_time_pass(void* handle, int which, int batch, int pos, int reps);
 /* Times every verify GEMM of one `batch`-row target pass, `reps` passes back to back, with
  * CUDA events; returns ms per pass (-1 on error), the pass's algorithmic GEMM bytes and the

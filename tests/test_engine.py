@@ -198,3 +198,75 @@ def test_callback_stop_and_telemetry(built_lib, config0):
     assert lib().g4dense_engine_generate(e.h, b"hello", 4) is None
     assert b"tokenizer" in lib().g4dense_engine_last_error()
     e.close()
+
+
+def _prefill_then_verify(e, ref_rows, toks, chunks, where):
+    """Feeds `toks` in `chunks`: chunks above 16 rows are tensor-core prefill passes (last row's
+    logits checked), the rest verify passes (every row checked)."""
+    pos = 0
+    for m in chunks:
+        if m > 16:
+            got = e.forward_batch(toks[pos:pos + m], pos, vocab=4096, all_positions=False)
+            check_logits(got[0], ref_rows[pos + m - 1], f"{where} prefill chunk at {pos} (rows {m}), last row")
+        else:
+            got = e.forward_batch(toks[pos:pos + m], pos, vocab=4096, all_positions=True)
+            for i in range(m):
+                check_logits(got[i], ref_rows[pos + i], f"{where} position {pos + i} (batch {m})")
+        pos += m
+    assert pos == len(toks)
+
+
+@pytest.mark.parametrize("variant", ["target", "target_centered"])
+def test_prefill_chunks_match_oracle(built_lib, config0, variant):
+    """Tensor-core prefill chunks (17..128 rows) against the oracle: the chunk's last-row logits,
+    then verify passes that read the K/V the chunks wrote."""
+    path = config0[variant]
+    e = engine(path)
+    ref = O.RestatedModel(path)
+    toks = np.random.default_rng(21).integers(0, 4096, 330)
+    want = [ref.forward(int(t), p) for p, t in enumerate(toks)]
+    _prefill_then_verify(e, want, toks, [128, 17, 100, 64, 16, 5], variant)
+    e.close()
+
+
+def test_prefill_chunks_bf16_kv(built_lib, config0):
+    path = config0["target"]
+    e = engine(path, kv_bf16=True)
+    ref = O.RestatedModel(path, kv_mode=O.KV_BF16)
+    toks = np.random.default_rng(22).integers(0, 4096, 200)
+    want = [ref.forward(int(t), p) for p, t in enumerate(toks)]
+    _prefill_then_verify(e, want, toks, [128, 56, 16], "bf16 KV")
+    e.close()
+
+
+def test_prefill_chunks_31b_geometry(built_lib, geom31):
+    """head_dim 256 / 512, GQA 2 and 4 and a 48-key sliding window far shorter than a 128-row
+    chunk: the ring holds window + 128 slots so a chunk never overwrites a key it still reads.
+    BASELINE-distribution weights only: over 400 positions the zero-mean model turns one-ulp
+    FP16 K/V rounding differences into logit moves beyond 2e-2 on the verify path alone (seen
+    from position ~100 with this sequence), so there it would test the rounding, not the kernels;
+    the zero-mean model's prefill chunks are covered on config 0 above."""
+    variant = "baseline"
+    path = geom31[variant]
+    e = engine(path, max_context=512)
+    ref = O.RestatedModel(path, max_ctx=512)
+    toks = np.random.default_rng(23).integers(0, 4096, 420)
+    want = [ref.forward(int(t), p) for p, t in enumerate(toks)]
+    _prefill_then_verify(e, want, toks, [128, 128, 97, 49, 16, 2], variant)
+    e.close()
+
+
+def test_long_prompt_streams_match_oracle(built_lib, config0):
+    """A 300-token prompt is prefilled in tensor-core chunks (128, 128, then 44 rows as verify
+    passes); the greedy streams that follow must still equal the oracle's bit for bit."""
+    tgt, drf = config0["target"], config0["draft"]
+    prompt = np.random.default_rng(24).integers(0, 4096, 300)
+    T = O.RestatedModel(tgt)
+    for name, dpath in (("no_spec", None), ("spec_k4", drf)):
+        D = O.RestatedModel(dpath) if dpath else None
+        want_tokens, want_rounds = O.spec_generate(T, D, prompt, 32, verify_width=5)
+        e = engine(tgt, draft=dpath, draft_k=5 if dpath else 0)
+        got = e.generate(prompt, 32)
+        assert got.tolist() == want_tokens.tolist(), f"{name} tokens"
+        assert e.rounds() == want_rounds, f"{name} rounds"
+        e.close()

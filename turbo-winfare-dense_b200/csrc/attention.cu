@@ -483,7 +483,7 @@ static cudaError_t launch_hd(const AttnArgs& a, void* bfrag, cudaStream_t st, bo
 using namespace g4b;
 
 cudaError_t g4b_attention(const AttnArgs& a, void* bfrag, cudaStream_t st, bool pdl) {
-    if (a.kvh < 1 || a.qh % a.kvh || a.M < 1 || a.M > kMaxM) return cudaErrorInvalidValue;
+    if (a.kvh < 1 || a.qh % a.kvh || a.M < 1 || a.M > kPrefillRows) return cudaErrorInvalidValue;
     switch (a.hd) {
         case 64: return launch_hd<64>(a, bfrag, st, pdl);
         case 128: return launch_hd<128>(a, bfrag, st, pdl);

@@ -426,7 +426,7 @@ G4DENSE_API int g4dense_engine_set_gate(void* handle, double min_accept, int win
 
 G4DENSE_API double g4dense_engine_time_pass(void* handle, int which, int batch, int pos, int reps) {
     clear_error();
-    if (!handle || batch < 1 || batch > 16 || reps < 1 || pos < 0) {
+    if (!handle || batch < 1 || batch > 128 || reps < 1 || pos < 0) {
         set_error("Invalid arguments");
         return -1.0;
     }
@@ -435,6 +435,7 @@ G4DENSE_API double g4dense_engine_time_pass(void* handle, int which, int batch, 
         g4b::DeviceModel* m = which == 0 ? &e->engine->target()
                                          : (e->engine->draft() ? &e->engine->draft()->model() : nullptr);
         if (!m) throw std::invalid_argument("no drafter loaded");
+        if (batch > m->max_rows()) throw std::invalid_argument("batch exceeds the model's rows per pass");
         if (pos + batch > m->max_context()) throw std::invalid_argument("pos + batch exceeds the KV capacity");
         std::vector<uint32_t> toks(batch, 1);
         m->run_plain(batch, pos, toks.data(), false);  // warm (captures the graph)

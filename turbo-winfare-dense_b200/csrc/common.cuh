@@ -42,6 +42,8 @@
 #include <cuda_fp16.h>
 #include <cstdint>
 
+#include "passrows.h"
+
 namespace g4b {
 
 constexpr int kRowsPerTile = 16;         // MMA M
@@ -50,8 +52,6 @@ constexpr int kWarpRows = kRowsPerTile * kTilesPerWarp;  // 64
 constexpr int kKTile = 128;              // k-tile width
 constexpr int kKTileBytes = 4608;        // one (row group, k-tile) block
 constexpr int kNibBytes = 4096;
-constexpr int kMaxM = 16;                // rows of a verify pass (B-frag layout)
-constexpr int kPrefillRows = 128;        // rows of a prefill pass (wide layout)
 constexpr int kWideTileBytes = kPrefillRows * 128;  // one 64-group's hi (or lo) tile
 
 // B-operand mode for M rows.

@@ -24,7 +24,8 @@ cudaError_t g4b_geglu(const g4b::GemmOut& gu, int F, void* bfrag, int M, cudaStr
 // (TpGather); otherwise o's slots or dense matrix.
 cudaError_t g4b_rowepi(const g4b::GemmOut& o, const g4b::TpGather& tg, const float* h_in, float* h_out,
                        const uint16_t* w1, float out_scale, const uint16_t* w2, int d, void* bfrag, int M,
-                       cudaStream_t st, bool pdl);
+                       cudaStream_t st, bool pdl,
+                       int frag_row0 = 0);
 
 // ---- attention.cu
 // Attention of M rows over the KV ring; writes the output [M][qh*hd] as the o-projection's

@@ -17,10 +17,12 @@
 
 #include <algorithm>
 #include <cmath>
+#include <cstddef>
 #include <cstring>
 #include <sstream>
 
 #include "common.cuh"
+#include "pgemm.h"
 #include "synth.h"
 #include "vgemm.h"
 
@@ -79,7 +81,7 @@ uint16_t* DeviceModel::upload_u16(const uint16_t* src, size_t n) {
     return d;
 }
 
-void DeviceModel::alloc_qw(QW& q, int N, int K) {
+void DeviceModel::alloc_qw(QW& q, int N, int K, bool prefill) {
     q.N = N;
     q.K = K;
     q.ktiles = vgemm_ktiles(K);
@@ -88,12 +90,19 @@ void DeviceModel::alloc_qw(QW& q, int N, int K) {
     q.max_slots = vgemm_plan_slots(q.n_crg, q.ktiles);
     q.w = dmalloc(vgemm_weight_bytes(N, K));
     weight_bytes_ += (uint64_t)N * K / 2 + (uint64_t)N * (K / 64) * 4;
+    if (prefill && opt_.prefill_tc) {
+        q.n_tiles = pgemm_n_tiles(N);
+        q.pmax_slots = pgemm_max_slots(q.n_tiles, K / 64, pgemm_grid(q.n_tiles, K / 64));
+        q.pw = dmalloc(pgemm_weight_bytes(N, K));
+    }
 }
 
-// Raw matrix (device pointers, container layout) -> streaming layout.
-void DeviceModel::upload_qw(QW& q, const uint32_t* W, const uint16_t* S, const uint16_t* B, int N, int K) {
-    alloc_qw(q, N, K);
+// Raw matrix (device pointers, container layout) -> streaming layout (+ prefill layout).
+void DeviceModel::upload_qw(QW& q, const uint32_t* W, const uint16_t* S, const uint16_t* B, int N, int K,
+                            bool prefill) {
+    alloc_qw(q, N, K, prefill);
     cuda_check(g4b_repack(W, S, B, N, K, q.w, stream_), "repack");
+    if (q.pw) cuda_check(pgemm_repack(W, S, B, N, K, q.pw, stream_), "prefill repack");
 }
 
 // ----------------------------------------------------------------------------- geometry
@@ -366,14 +375,15 @@ void DeviceModel::finalize_load() {
     if (V % opt_.tp) throw std::runtime_error("vocab must divide by the tensor-parallel size");
     v_local_ = V / opt_.tp;
     v_off_ = opt_.rank * v_local_;
+    // The LM head ranks one row of a prefill chunk (its last), so it needs no prefill layout.
     upload_qw(lm_, emb_w_ + (size_t)v_off_ * (d / 8), emb_s_ + (size_t)v_off_ * (d / 64),
-              emb_b_ + (size_t)v_off_ * (d / 64), v_local_, d);
-    // KV rings: sliding layers keep window + 16 slots (a verify batch of up to 16 rows never
-    // overwrites a key an earlier row of the same batch still needs); full-attention layers
-    // keep max_context.
+              emb_b_ + (size_t)v_off_ * (d / 64), v_local_, d, false);
+    // KV rings: sliding layers keep window + max_rows() slots (a batch of rows never overwrites
+    // a key an earlier row of the same batch still needs); full-attention layers keep
+    // max_context.
     for (auto& L : layers_) {
         L.cap = L.geo.is_global ? opt_.max_context
-                                : std::min<int>(opt_.max_context, (int)h_.sliding_window) + 16;
+                                : std::min<int>(opt_.max_context, (int)h_.sliding_window) + max_rows();
         const size_t n = (size_t)L.cap * L.kvh * L.hd;
         L.k_ring = static_cast<uint16_t*>(dmalloc(n * 2));
         L.v_ring = static_cast<uint16_t*>(dmalloc(n * 2));
@@ -388,12 +398,16 @@ void DeviceModel::finalize_load() {
 void DeviceModel::init_buffers() {
     const int d = h_.d_model;
     int max_attn_k = 0, max_F = 0, max_q = 0;
-    size_t part = 0;
-    int max_n = d, max_crg = 0;
+    size_t part = 0, ppart = 0;
+    int max_n = d, max_crg = 0, max_tiles = 0;
     auto consider = [&](const QW& q) {
         part = std::max(part, (size_t)q.n_crg * q.max_slots * kMaxM * 256);
         max_crg = std::max(max_crg, q.n_crg);
         if (&q != &lm_) max_n = std::max(max_n, q.N);
+        if (q.pw) {
+            ppart = std::max(ppart, pgemm_part_floats(q.n_tiles, q.pmax_slots));
+            max_tiles = std::max(max_tiles, q.n_tiles);
+        }
     };
     for (auto& L : layers_) {
         max_attn_k = std::max(max_attn_k, L.qh * L.hd);
@@ -406,13 +420,19 @@ void DeviceModel::init_buffers() {
     }
     consider(lm_);
     part_floats_ = part;
-    for (int i = 0; i < 2; ++i) hres_[i] = static_cast<float*>(dmalloc((size_t)kMaxM * d * 4));
+    const int rows = max_rows();
+    for (int i = 0; i < 2; ++i) hres_[i] = static_cast<float*>(dmalloc((size_t)rows * d * 4));
     bf_d_ = dmalloc(bfrag_capacity(round_up(d, 128)));
     bf_attn_ = dmalloc(bfrag_capacity(round_up(max_attn_k, 128)));
     bf_ff_ = dmalloc(bfrag_capacity(round_up(max_F, 128)));
     part_ = static_cast<float*>(dmalloc(part * 4));
-    q_buf_ = static_cast<float*>(dmalloc((size_t)kMaxM * max_q * 4));
-    y_ = static_cast<float*>(dmalloc((size_t)kMaxM * max_n * 4));
+    q_buf_ = static_cast<float*>(dmalloc((size_t)rows * max_q * 4));
+    y_ = static_cast<float*>(dmalloc((size_t)rows * max_n * 4));
+    if (max_tiles) {
+        ppart_ = static_cast<float*>(dmalloc(ppart * 4));
+        pcnt_ = static_cast<unsigned*>(dmalloc((size_t)max_tiles * sizeof(unsigned)));
+        cuda_check(cudaMemset(pcnt_, 0, (size_t)max_tiles * sizeof(unsigned)), "memset");
+    }
     cnt_ = static_cast<unsigned*>(dmalloc((size_t)max_crg * sizeof(unsigned)));
     cuda_check(cudaMemset(cnt_, 0, (size_t)max_crg * sizeof(unsigned)), "memset");
     chunk_best_ = static_cast<float2*>(dmalloc((size_t)opt_.tp * kMaxM * g4b_head_chunks(v_local_) * sizeof(float2)));
@@ -430,7 +450,7 @@ void DeviceModel::init_tp_peers() {
 #ifdef G4B_HAVE_NCCL
     if (opt_.tp > kMaxTp) throw std::runtime_error("tensor parallelism supports at most 8 ranks");
     const int d = h_.d_model;
-    const size_t ybytes = (size_t)2 * kMaxM * d * sizeof(float);
+    const size_t ybytes = (size_t)2 * max_rows() * d * sizeof(float);
     // One cudaMalloc holds both parities and the two flag words (IPC maps whole allocations).
     void* base = dmalloc(ybytes + 256);
     cuda_check(cudaMemset(base, 0, ybytes + 256), "memset");
@@ -469,7 +489,7 @@ TpGather DeviceModel::tp_gather(int step, int parity) const {
     g.step = step;
     g.err = err_dev_;
     if (opt_.tp > 1) {
-        const size_t off = (size_t)parity * kMaxM * h_.d_model;
+        const size_t off = (size_t)parity * max_rows() * h_.d_model;
         for (int r = 0; r < opt_.tp; ++r) {
             g.y[r] = tp_peer_y_[r] + off;
             g.flag[r] = tp_peer_flags_[r] + parity;
@@ -554,7 +574,7 @@ PartView DeviceModel::part_view(const QW& q, int M) const {
 GemmOut DeviceModel::partials(const QW& q, int M) const { return GemmOut{part_view(q, M), nullptr, q.N}; }
 
 float* DeviceModel::tp_out(int parity) const {
-    return opt_.tp > 1 ? tp_buf_ + (size_t)parity * kMaxM * h_.d_model : nullptr;
+    return opt_.tp > 1 ? tp_buf_ + (size_t)parity * max_rows() * h_.d_model : nullptr;
 }
 
 void DeviceModel::gemm(const QW& q, const void* bfrag, int M, float* y) {
@@ -574,7 +594,95 @@ void DeviceModel::gemm(const QW& q, const void* bfrag, int M, float* y) {
     cuda_check(vgemm_launch(p, stream_, opt_.use_pdl), "vgemm");
 }
 
+void DeviceModel::pgemm(const QW& q, const void* act, int M, float* y) {
+    PgemmParams p{};
+    p.w = q.pw;
+    p.act = act;
+    p.g_layout = q.ktiles * 2;
+    p.y = y;
+    p.ldy = q.N;
+    p.part = ppart_;
+    p.cnt = pcnt_;
+    p.N = q.N;
+    p.K = q.K;
+    p.M = M;
+    p.n_tiles = q.n_tiles;
+    p.max_slots = q.pmax_slots;
+    p.err = err_dev_;
+    cuda_check(pgemm_launch(p, stream_, opt_.use_pdl), "pgemm");
+}
+
+// A prefill chunk of 17..128 rows: the layer kernels of the verify pass with wide-layout
+// activations and the tensor-core GEMM (dense outputs), then the LM head on the chunk's last
+// row only -- the final norm writes that row alone, in the 1-row fragment layout.
+void DeviceModel::enqueue_prefill(int M, bool want_logits) {
+    const int d = h_.d_model;
+    const bool pdl = opt_.use_pdl;
+    StepParams* sp = sp_dev_;
+    int cur = 0;
+    cuda_check(g4b_embed_norm(sp, emb_w_, emb_s_, emb_b_, h_.vocab_size, d, layers_[0].in_norm, hres_[cur], bf_d_, M,
+                              stream_, false),
+               "embed_norm");
+    for (size_t l = 0; l < layers_.size(); ++l) {
+        DevLayer& L = layers_[l];
+        pgemm(L.qkv, bf_d_, M, y_);
+        QkvEpiArgs qa{};
+        qa.qkv = GemmOut{PartView{}, y_, L.qkv.N};
+        qa.sp = sp;
+        qa.M = M;
+        qa.qh = L.qh;
+        qa.kvh = L.kvh;
+        qa.hd = L.hd;
+        qa.has_v = L.has_v;
+        qa.rotated = L.rotated;
+        qa.theta = L.theta;
+        qa.q_norm = L.q_norm;
+        qa.k_norm = L.k_norm;
+        qa.q_out = q_buf_;
+        qa.k_ring = L.k_ring;
+        qa.v_ring = L.v_ring;
+        qa.cap = L.cap;
+        qa.kv_bf16 = opt_.kv_bf16;
+        cuda_check(g4b_qkv_epi(qa, stream_, pdl), "qkv_epi");
+        AttnArgs aa{};
+        aa.q = q_buf_;
+        aa.k_ring = L.k_ring;
+        aa.v_ring = L.v_ring;
+        aa.sp = sp;
+        aa.M = M;
+        aa.qh = L.qh;
+        aa.kvh = L.kvh;
+        aa.hd = L.hd;
+        aa.cap = L.cap;
+        aa.window = L.geo.is_global ? 0 : (int)h_.sliding_window;
+        aa.kv_bf16 = opt_.kv_bf16;
+        aa.scale = 1.0f;
+        cuda_check(g4b_attention(aa, bf_attn_, stream_, pdl), "attention");
+        float* yo = opt_.tp > 1 ? tp_out(0) : y_;
+        pgemm(L.o, bf_attn_, M, yo);
+        cuda_check(g4b_rowepi(GemmOut{PartView{}, yo, d}, tp_gather(2 * (int)l, 0), hres_[cur], hres_[1 - cur],
+                              L.pa_norm, 1.0f, L.pf_norm, d, bf_d_, M, stream_, pdl),
+                   "post_attn");
+        cur = 1 - cur;
+        pgemm(L.gateup, bf_d_, M, y_);
+        cuda_check(g4b_geglu(GemmOut{PartView{}, y_, L.gateup.N}, L.F, bf_ff_, M, stream_, pdl), "geglu");
+        float* yd = opt_.tp > 1 ? tp_out(1) : y_;
+        pgemm(L.down, bf_ff_, M, yd);
+        const bool last = l + 1 == layers_.size();
+        const uint16_t* w_next = last ? final_norm_ : layers_[l + 1].in_norm;
+        cuda_check(g4b_rowepi(GemmOut{PartView{}, yd, d}, tp_gather(2 * (int)l + 1, 1), hres_[cur], hres_[1 - cur],
+                              L.pffn_norm, L.scalar, w_next, d, bf_d_, M, stream_, pdl, last ? M - 1 : 0),
+                   "post_ffn");
+        cur = 1 - cur;
+    }
+    head(1, want_logits, nullptr, sp);
+}
+
 void DeviceModel::enqueue_raw(int M, PassKind kind, bool want_logits, uint32_t* chain_out) {
+    if (M > kMaxM) {
+        enqueue_prefill(M, want_logits);
+        return;
+    }
     const int d = h_.d_model;
     const bool pdl = opt_.use_pdl;
     StepParams* sp = sp_dev_ + (kind == PassKind::DraftStep ? 1 : 0);
@@ -642,7 +750,13 @@ void DeviceModel::enqueue_raw(int M, PassKind kind, bool want_logits, uint32_t* 
                    "post_ffn");
         cur = 1 - cur;
     }
-    // LM head
+    head(M, want_logits, chain_out, sp);
+}
+
+// LM head over the M rows whose final-norm fragments are in bf_d_ (verify layout), then the
+// softcapped chunk argmax and the row argmax / greedy acceptance.
+void DeviceModel::head(int M, bool want_logits, uint32_t* chain_out, StepParams* sp) {
+    const bool pdl = opt_.use_pdl;
     gemm(lm_, bf_d_, M, nullptr);
     const GemmOut lo = partials(lm_, M);
     // Under tensor parallelism each rank ranks its own vocabulary slice; the per-chunk bests
@@ -665,7 +779,8 @@ void DeviceModel::enqueue_raw(int M, PassKind kind, bool want_logits, uint32_t* 
 
 void DeviceModel::enqueue(int M, PassKind kind, bool want_logits, uint32_t* chain_out) {
     if (!loaded_) throw std::runtime_error("model not loaded");
-    if (M < 1 || M > kMaxM) throw std::runtime_error("batch width must be 1..16");
+    if (M < 1 || M > max_rows())
+        throw std::runtime_error("batch width must be 1.." + std::to_string(max_rows()));
     if (opt_.tp > 1 && h_.vocab_size % opt_.tp) throw std::runtime_error("vocab split");
     launches_ += kernels_per_pass(M);
     if (!opt_.use_graphs) {
@@ -694,7 +809,7 @@ void DeviceModel::enqueue(int M, PassKind kind, bool want_logits, uint32_t* chai
     cuda_check(cudaGraphLaunch(it->second, stream_), "graph launch");
 }
 
-void DeviceModel::push_params(int slot, const StepParams& p) {
+void DeviceModel::push_params(int slot, const StepParams& p, int ntok) {
     // A ring entry is reused only after the stream has drained every earlier copy.
     if (sp_ring_ == kParamRing) {
         cuda_check(cudaStreamSynchronize(stream_), "sync");
@@ -702,8 +817,9 @@ void DeviceModel::push_params(int slot, const StepParams& p) {
     }
     StepParams& s = sp_host_[sp_ring_++];
     s = p;
-    cuda_check(cudaMemcpyAsync(sp_dev_ + slot, &s, sizeof(StepParams), cudaMemcpyHostToDevice, stream_), "params");
-    h2d_bytes_ += sizeof(StepParams);
+    const size_t bytes = offsetof(StepParams, tokens) + (size_t)std::max(1, std::min(ntok, kPrefillRows)) * 4;
+    cuda_check(cudaMemcpyAsync(sp_dev_ + slot, &s, bytes, cudaMemcpyHostToDevice, stream_), "params");
+    h2d_bytes_ += bytes;
 }
 
 void DeviceModel::run_plain(int M, int base_pos, const uint32_t* tokens, bool want_logits) {
@@ -715,7 +831,7 @@ void DeviceModel::run_plain(int M, int base_pos, const uint32_t* tokens, bool wa
         if (t >= h_.vocab_size) t %= h_.vocab_size;
         s.tokens[i] = t;
     }
-    push_params(0, s);
+    push_params(0, s, std::max(M, kMaxM));
     enqueue(M, PassKind::Plain, want_logits, nullptr);
 }
 

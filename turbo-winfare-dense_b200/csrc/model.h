@@ -24,13 +24,18 @@ struct ModelOptions {
     void* nccl_comm = nullptr;  // ncclComm_t when tp > 1
     bool use_graphs = true;
     bool use_pdl = true;
+    // Keep a second copy of every layer matrix in the prefill GEMM's layout and run prompt
+    // chunks of 17..128 rows on the tcgen05 tensor cores (the weights take twice the memory).
+    bool prefill_tc = true;
     cudaStream_t stream = nullptr;  // share a caller's stream (target and drafter do)
 };
 
-// One INT4 matrix in the vgemm streaming layout.
+// One INT4 matrix in the vgemm streaming layout (and, for prefill, in the pgemm layout).
 struct QW {
     void* w = nullptr;
     int N = 0, K = 0, ktiles = 0, n_crg = 0, n_wrg = 0, max_slots = 0;
+    void* pw = nullptr;  // prefill-GEMM layout (nullptr: no tensor-core prefill for this matrix)
+    int n_tiles = 0, pmax_slots = 0;
 };
 
 struct DevLayer {
@@ -79,11 +84,17 @@ class DeviceModel {
     float* logits_dev() { return logits_; }  // [16][vocab_local] when a pass asked for them
     uint32_t* chain_dev() { return chain_dev_; }
 
-    // Enqueues one pass of M rows (1..16) on the model's stream (graph-replayed when enabled).
-    // The caller has already written the StepParams slot used by `kind`.
+    // Enqueues one pass of M rows on the model's stream (graph-replayed when enabled): 1..16
+    // rows run the verify path, 17..max_rows() (prefill chunks) the tensor-core path, which
+    // ranks only the last row (its result and logits are row 0). The caller has already
+    // written the StepParams slot used by `kind`.
     void enqueue(int M, PassKind kind, bool want_logits, uint32_t* chain_out);
-    // Stages `p` in a pinned ring and enqueues its copy into StepParams slot `slot`.
-    void push_params(int slot, const StepParams& p);
+    // Rows one pass may hold, and the result/logits row that holds a pass's last row.
+    int max_rows() const { return opt_.prefill_tc ? kPrefillRows : kMaxM; }
+    static int result_row(int M) { return M > kMaxM ? 0 : M - 1; }
+    // Stages `p` in a pinned ring and enqueues the copy of its first `ntok` tokens (and the
+    // scalar fields) into StepParams slot `slot`.
+    void push_params(int slot, const StepParams& p, int ntok = kMaxM);
     // Host helper: write StepParams slot 0 (base_pos, tokens) and enqueue a plain pass.
     void run_plain(int M, int base_pos, const uint32_t* tokens, bool want_logits);
     // Copies the result struct to host (synchronizes the stream).
@@ -112,11 +123,16 @@ class DeviceModel {
     void enqueue_raw(int M, PassKind kind, bool want_logits, uint32_t* chain_out);
     // One verify GEMM; y == nullptr leaves split-K partials for the consumer (partials()).
     void gemm(const QW& q, const void* bfrag, int M, float* y);
+    // One prefill GEMM (17..128 rows, wide-layout activations) into the dense y[M][q.N].
+    void pgemm(const QW& q, const void* act, int M, float* y);
+    void enqueue_prefill(int M, bool want_logits);
+    void head(int M, bool want_logits, uint32_t* chain_out, StepParams* sp);
     PartView part_view(const QW& q, int M) const;
     GemmOut partials(const QW& q, int M) const;
     float* tp_out(int parity) const;  // under TP: this rank's partial buffer of that parity, else nullptr
-    void upload_qw(QW& q, const uint32_t* W, const uint16_t* S, const uint16_t* B, int N, int K);
-    void alloc_qw(QW& q, int N, int K);
+    void upload_qw(QW& q, const uint32_t* W, const uint16_t* S, const uint16_t* B, int N, int K,
+                   bool prefill = true);
+    void alloc_qw(QW& q, int N, int K, bool prefill);
     uint16_t* upload_u16(const uint16_t* src, size_t n);
     void* dmalloc(size_t bytes);
     void finalize_load();
@@ -148,6 +164,8 @@ class DeviceModel {
     unsigned* tp_peer_flags_[kMaxTp] = {};
     std::vector<void*> tp_ipc_open_;
     unsigned* cnt_ = nullptr;  // split-K arrival counters of the GEMM running on stream_
+    float* ppart_ = nullptr;   // prefill GEMM split-K slots
+    unsigned* pcnt_ = nullptr; // prefill GEMM tile arrival counters
     float2* chunk_best_ = nullptr;
     float* logits_ = nullptr;
     HeadResult* res_dev_ = nullptr;

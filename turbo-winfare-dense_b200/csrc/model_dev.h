@@ -3,6 +3,7 @@
 #include <cuda_fp16.h>
 #include <cstdint>
 
+#include "passrows.h"
 #include "vgemm.h"
 
 namespace g4b {
@@ -13,7 +14,7 @@ namespace g4b {
 struct StepParams {
     int base_pos;
     int draft_step;  // drafter chaining: index of the next draft written to the chain list
-    uint32_t tokens[16];
+    uint32_t tokens[kPrefillRows];  // a verify pass uses the first 16, a prefill chunk up to 128
 };
 
 // A GEMM output as its consumers see it: split-K partial slots (part.part != nullptr), summed

@@ -246,9 +246,8 @@ __global__ void __maxnreg__(kMaxRegs) pgemm_kernel(PgemmParams p) {
         float acc[kEpiCols];
 #pragma unroll
         for (int j = 0; j < kEpiCols; ++j) acc[j] = 0.f;
-        for (int i = 0; i < n; ++i) {
-            const long long u = u0 + i;
-            const int t = (int)(u / G), g = (int)(u - (long long)t * G);
+        int t = (int)(u0 / G), g = (int)(u0 - (long long)t * G);  // unit u0 + i, advanced below
+        for (int i = 0; i < n; ++i, g = (g + 1 == G) ? 0 : g + 1, t += (g == 0)) {
             const int s = i % kStages, b = i % kAccBufs;
             bool ok = pg_wait(&bars.acc_full[b], (i / kAccBufs) & 1, abort, p.err);
             ok = ok && pg_wait(&bars.full[s], (i / kStages) & 1, abort, p.err);

@@ -200,7 +200,7 @@ __global__ void __launch_bounds__(kEpiMaxWarps * 32) rowepi_kernel(GemmOut o, Tp
                                                                     float* __restrict__ h_out,
                                                                     const uint16_t* __restrict__ w1, float out_scale,
                                                                     const uint16_t* __restrict__ w2, int d,
-                                                                    void* bfrag, int M) {
+                                                                    void* bfrag, int M, int frag_row0) {
     __shared__ float4 red[kEpiMaxWarps];
     __shared__ float4 cta_sum;
     __shared__ __half stage[kEpiMaxWarps][128];
@@ -264,7 +264,10 @@ __global__ void __launch_bounds__(kEpiMaxWarps * 32) rowepi_kernel(GemmOut o, Tp
     const float r1 = inv_rms(t.x, d);
     const float s2 = out_scale * out_scale * (t.y + 2.0f * r1 * t.z + r1 * r1 * t.w);
     const float r2 = inv_rms(fmaxf(s2, 0.f), d);
-    const BFragView bv = bfrag_view(bfrag, Kp, M);
+    // Fragments for rows frag_row0.. only, as rows 0.. of an (M - frag_row0)-row batch (a
+    // prefill chunk's final norm feeds the LM head its last row alone).
+    const int Mf = M - frag_row0, mf = m - frag_row0;
+    const BFragView bv = bfrag_view(bfrag, Kp, Mf);
 #pragma unroll
     for (int j = 0; j < kEpiGroupsPerWarp; ++j) {
         const int gi = rank * gpc + warp + nw * j;
@@ -281,7 +284,7 @@ __global__ void __launch_bounds__(kEpiMaxWarps * 32) rowepi_kernel(GemmOut o, Tp
                 x[e] = __fmul_rn(__fmul_rn(hn, r2), bf16_to_f32(w2[c]));
             }
         }
-        bfrag_store_group(bv, M, m, gi, x[0], x[1], stage[warp]);
+        if (mf >= 0) bfrag_store_group(bv, Mf, mf, gi, x[0], x[1], stage[warp]);  // block-uniform
     }
 }
 
@@ -355,13 +358,15 @@ cudaError_t g4b_qkv_epi(const QkvEpiArgs& a, cudaStream_t st, bool pdl) {
 }
 
 cudaError_t g4b_rowepi(const GemmOut& o, const TpGather& tg, const float* h_in, float* h_out, const uint16_t* w1,
-                       float out_scale, const uint16_t* w2, int d, void* bfrag, int M, cudaStream_t st, bool pdl) {
+                       float out_scale, const uint16_t* w2, int d, void* bfrag, int M, cudaStream_t st, bool pdl,
+                       int frag_row0) {
     if ((o.ld | d) & 1) return cudaErrorInvalidValue;  // float2 loads
+    if (frag_row0 < 0 || frag_row0 >= M) return cudaErrorInvalidValue;
     if (tg.n < 1 || tg.n > kMaxTp) return cudaErrorInvalidValue;
     const int ngp = (d + 127) / 128 * 2;
     if (ngp <= kEpiMaxWarps)  // one CTA per row, one warp per group
         return launch(rowepi_kernel<false>, dim3(1, M), dim3(ngp * 32), 0, st, pdl, o, tg, h_in, h_out, w1, out_scale,
-                      w2, d, bfrag, M);
+                      w2, d, bfrag, M, frag_row0);
     if ((ngp + kEpiClusters - 1) / kEpiClusters > kEpiWarps * kEpiGroupsPerWarp) return cudaErrorInvalidValue;
     static bool attr_set = false;
     if (!attr_set) {
@@ -383,7 +388,7 @@ cudaError_t g4b_rowepi(const GemmOut& o, const TpGather& tg, const float* h_in, 
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 2 : 1;
-    return cudaLaunchKernelEx(&cfg, rowepi_kernel<true>, o, tg, h_in, h_out, w1, out_scale, w2, d, bfrag, M);
+    return cudaLaunchKernelEx(&cfg, rowepi_kernel<true>, o, tg, h_in, h_out, w1, out_scale, w2, d, bfrag, M, frag_row0);
 }
 
 cudaError_t g4b_geglu(const GemmOut& gu, int F, void* bfrag, int M, cudaStream_t st, bool pdl) {

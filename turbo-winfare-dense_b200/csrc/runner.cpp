@@ -25,12 +25,20 @@ uint32_t replay_propose(const std::vector<uint32_t>& stream, size_t n_prompt, si
     if (u < rate) return (uint32_t)((truth + 1u + (uint32_t)(splitmix64(h) % (vocab - 1))) % vocab);
     return truth;
 }
+// Rows of the next prefill pass over `remaining` prompt positions: whole tensor-core chunks
+// (max_rows = 128) while more than kPrefillMinRows remain; a shorter tail runs as verify passes
+// of up to 16 rows, which cost less than a mostly empty tensor-core chunk.
+constexpr size_t kPrefillMinRows = 48;
+int next_chunk(size_t remaining, int max_rows) {
+    if (max_rows > kBatchRows && remaining > kPrefillMinRows) return (int)std::min<size_t>(remaining, max_rows);
+    return (int)std::min<size_t>(remaining, kBatchRows);
+}
 }  // namespace
 
 void DraftRuntime::catch_up(const std::vector<uint32_t>& ctx) {
     if (consumed_ > ctx.size()) consumed_ = 0;
     while (consumed_ + 1 < ctx.size()) {
-        const int m = (int)std::min<size_t>(kBatchRows, ctx.size() - 1 - consumed_);
+        const int m = next_chunk(ctx.size() - 1 - consumed_, model_->max_rows());
         model_->run_plain(m, (int)consumed_, ctx.data() + consumed_, false);
         consumed_ += m;
     }
@@ -46,14 +54,19 @@ void Engine::order(cudaStream_t from, cudaStream_t to) {
 }
 
 void Engine::forward_batch(const uint32_t* ids, uint32_t batch, uint32_t base, float* out_logits, bool all_positions) {
-    if (batch < 1 || batch > (uint32_t)kBatchRows) throw std::invalid_argument("forward_batch: batch must be 1..16");
+    // 1..16 rows run the verify pass (every row's logits available); 17..max_rows() run a
+    // tensor-core prefill chunk, which ranks only its last row.
+    if (batch < 1 || batch > (uint32_t)target_->max_rows())
+        throw std::invalid_argument("forward_batch: batch must be 1.." + std::to_string(target_->max_rows()));
+    if (batch > (uint32_t)kBatchRows && out_logits && all_positions)
+        throw std::invalid_argument("forward_batch: a batch of more than 16 rows returns the last row's logits only");
     if (out_logits && target_->options().tp > 1)
         throw std::invalid_argument("forward_batch: host logits are not gathered across tensor-parallel ranks");
     if (base + batch > (uint32_t)target_->max_context()) throw std::invalid_argument("forward_batch: context exceeds max_context");
     target_->run_plain((int)batch, (int)base, ids, out_logits != nullptr);
     if (out_logits) {
         const size_t V = target_->vocab_local();
-        const size_t row0 = all_positions ? 0 : batch - 1;
+        const size_t row0 = all_positions ? 0 : (size_t)DeviceModel::result_row((int)batch);
         const size_t rows = all_positions ? batch : 1;
         cuda_check(cudaMemcpyAsync(out_logits, target_->logits_dev() + row0 * V, rows * V * sizeof(float),
                                    cudaMemcpyDeviceToHost, target_->stream()),
@@ -62,28 +75,31 @@ void Engine::forward_batch(const uint32_t* ids, uint32_t batch, uint32_t base, f
     cuda_check(cudaStreamSynchronize(target_->stream()), "forward_batch");
 }
 
-// Prefill in chunks of up to 16 positions (the reference chunks by 8, src/runner.cpp:2129-2133;
-// batched rows equal sequential positions, so the chunk width does not change results).
-// Returns the greedy next token; for sampled decoding fills *last_logits instead.
+// Prefill in chunks of up to 128 positions on the tensor cores, the tail in 16-row verify
+// passes (the reference chunks by 8, src/runner.cpp:2129-2133; batched rows equal sequential
+// positions, so the chunk width does not change results). Returns the greedy next token; for
+// sampled decoding fills *last_logits instead.
 uint32_t Engine::prefill(const std::vector<uint32_t>& toks, const GenerationOptions& opt, std::vector<float>* last) {
     const bool greedy = opt.sampling.is_greedy();
     const size_t n = toks.size();
     int m_last = 1;
-    for (size_t i = 0; i < n; i += kBatchRows) {
-        const int m = (int)std::min<size_t>(kBatchRows, n - i);
+    for (size_t i = 0; i < n;) {
+        const int m = next_chunk(n - i, target_->max_rows());
         const bool is_last = i + m == n;
         target_->run_plain(m, (int)i, toks.data() + i, is_last && !greedy);
         m_last = m;
+        i += m;
     }
     const HeadResult r = target_->fetch_result();
+    const int row = DeviceModel::result_row(m_last);
     if (!greedy) {
         const size_t V = target_->vocab_local();
         last->resize(V);
-        cuda_check(cudaMemcpy(last->data(), target_->logits_dev() + (size_t)(m_last - 1) * V, V * sizeof(float),
+        cuda_check(cudaMemcpy(last->data(), target_->logits_dev() + (size_t)row * V, V * sizeof(float),
                               cudaMemcpyDeviceToHost),
                    "logits");
     }
-    return r.argmax[m_last - 1];
+    return r.argmax[row];
 }
 
 std::vector<uint32_t> Engine::generate(const std::vector<uint32_t>& prompt, const GenerationOptions& opt,

@@ -1,7 +1,8 @@
 // Thin inline-PTX wrappers for the sm_100a 5th-generation tensor core (tcgen05): tensor-memory
 // allocation, the MMA with its accumulator in tensor memory (TMEM), completion tracking through
 // mbarriers, and TMEM <-> register moves. Only the forms the prefill GEMM uses are wrapped:
-// cta_group::1, kind::f16 (fp16 inputs, fp32 accumulate), A from TMEM, B from shared memory.
+// cta_group::1, kind::f16 (fp16 inputs, fp32 accumulate), B from shared memory, A from shared
+// or tensor memory.
 //
 // TMEM addresses are (lane << 16) | column. A warp may only touch the 32 lanes of its
 // quadrant, lanes 32 * (warp % 4) .. +31.
@@ -39,6 +40,16 @@ __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_
         "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
         " tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n}" ::"r"(d_tmem),
         "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, issued by one thread.
+__device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate) {
+    asm volatile(
+        "{\n .reg .pred p;\n setp.ne.b32 p, %4, 0;\n"
+        " tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
         : "memory");
 }
 
