@@ -160,9 +160,10 @@ __global__ void __launch_bounds__(kAttnThreads, HD <= 256 ? 2 : 1) attention_ker
     const int R = a.M * gqa;
     const int base = a.sp->base_pos;
 
-    // Key range of the whole batch, then this split's share.
-    const int kmin = a.window ? max(0, base + 1 - a.window) : 0;
-    const int kmax = base + a.M;
+    // Key range of this chunk's rows (the union of their causal spans), then this split's share.
+    const int m_first = (chunk * kAttnRows) / gqa, m_last = min(a.M - 1, (chunk * kAttnRows + kAttnRows - 1) / gqa);
+    const int kmin = a.window ? max(0, base + m_first + 1 - a.window) : 0;
+    const int kmax = base + m_last + 1;
     const int per = (kmax - kmin + nsplit - 1) / nsplit;
     const int ks = kmin + split * per, ke = min(kmax, ks + per);
 
@@ -467,7 +468,10 @@ static cudaError_t launch_attn(const AttnArgs& a, void* bfrag, cudaStream_t st, 
         attr_set = true;
     }
     const int chunks = (a.M * (a.qh / a.kvh) + kAttnRows - 1) / kAttnRows;
-    const int splits = attn_splits<BF16, HD>(a.kvh * chunks);
+    // A verify pass has few clusters: split the keys as widely as one wave allows. A prefill
+    // chunk has hundreds of clusters already, so its keys are split in two only, which keeps the
+    // per-CTA loops long and the cross-CTA combine cheap.
+    const int splits = a.M > kMaxM ? 2 : attn_splits<BF16, HD>(a.kvh * chunks);
     cudaLaunchAttribute attr[2];
     cudaLaunchConfig_t cfg = attn_config<BF16, HD>(a, splits, st, attr, pdl);
     return cudaLaunchKernelEx(&cfg, attention_kernel<BF16, HD>, a, bfrag);

@@ -194,7 +194,7 @@ __device__ __forceinline__ float2 tp_pair(const TpGather& tg, int m, int ld, int
     return s;
 }
 
-template <bool CLUSTER>
+template <bool CLUSTER, int GPW = kEpiGroupsPerWarp>
 __global__ void __launch_bounds__(kEpiMaxWarps * 32) rowepi_kernel(GemmOut o, TpGather tg,
                                                                     const float* __restrict__ h_in,
                                                                     float* __restrict__ h_out,
@@ -214,10 +214,10 @@ __global__ void __launch_bounds__(kEpiMaxWarps * 32) rowepi_kernel(GemmOut o, Tp
     const int gpc = CLUSTER ? (ngp + kEpiClusters - 1) / kEpiClusters : ngp;
     const int g_end = min(ngp, (rank + 1) * gpc);
 
-    float2 y[kEpiGroupsPerWarp], h[kEpiGroupsPerWarp];
+    float2 y[GPW], h[GPW];
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-    for (int j = 0; j < kEpiGroupsPerWarp; ++j) {
+    for (int j = 0; j < GPW; ++j) {
         const int gi = rank * gpc + warp + nw * j;
         const int c0 = gi * 64 + 2 * lane;
         y[j] = h[j] = make_float2(0.f, 0.f);
@@ -269,7 +269,7 @@ __global__ void __launch_bounds__(kEpiMaxWarps * 32) rowepi_kernel(GemmOut o, Tp
     const int Mf = M - frag_row0, mf = m - frag_row0;
     const BFragView bv = bfrag_view(bfrag, Kp, Mf);
 #pragma unroll
-    for (int j = 0; j < kEpiGroupsPerWarp; ++j) {
+    for (int j = 0; j < GPW; ++j) {
         const int gi = rank * gpc + warp + nw * j;
         if (gi >= g_end) continue;  // warp-uniform
         float x[2] = {0.f, 0.f};
@@ -367,6 +367,11 @@ cudaError_t g4b_rowepi(const GemmOut& o, const TpGather& tg, const float* h_in, 
     if (ngp <= kEpiMaxWarps)  // one CTA per row, one warp per group
         return launch(rowepi_kernel<false>, dim3(1, M), dim3(ngp * 32), 0, st, pdl, o, tg, h_in, h_out, w1, out_scale,
                       w2, d, bfrag, M, frag_row0);
+    // A prefill chunk has rows enough to fill the GPU: one 32-warp CTA per row, each warp up to
+    // three groups, instead of a 16-CTA cluster per row.
+    if (M > kMaxM && ngp <= 3 * kEpiMaxWarps)
+        return launch(rowepi_kernel<false, 3>, dim3(1, M), dim3(kEpiMaxWarps * 32), 0, st, pdl, o, tg, h_in, h_out, w1,
+                      out_scale, w2, d, bfrag, M, frag_row0);
     if ((ngp + kEpiClusters - 1) / kEpiClusters > kEpiWarps * kEpiGroupsPerWarp) return cudaErrorInvalidValue;
     static bool attr_set = false;
     if (!attr_set) {
