@@ -199,22 +199,40 @@ std::vector<uint32_t> Engine::generate(const std::vector<uint32_t>& prompt, cons
             }
             if (K < 2) break;  // K-1 = 0 drafts: the reference's round loop ends here
             const double tr0 = now_ms();
-            D.catch_up(history);
             const size_t len = history.size();
+            // Greedy: context the drafter has not seen yet (one token after a fully accepted
+            // round) rides in the first drafting pass together with the pending token, so that
+            // round needs no separate catch-up pass. Batched rows equal sequential positions.
+            size_t unseen = 0;
+            if (greedy) {
+                if (D.consumed() > len - 1) D.set_consumed(0);
+                unseen = len - 1 - D.consumed();
+                if (unseen + 1 > (size_t)kBatchRows) {
+                    D.catch_up(history);
+                    unseen = 0;
+                }
+            } else {
+                D.catch_up(history);
+            }
             std::vector<uint32_t> emitted_now;
             uint32_t n_acc = 0;
             if (greedy) {
                 StepParams tp{}, dp{};
-                tp.base_pos = dp.base_pos = (int)len - 1;
-                tp.tokens[0] = dp.tokens[0] = pending;
+                tp.base_pos = (int)len - 1;
+                tp.tokens[0] = pending;
+                dp.base_pos = (int)(len - 1 - unseen);
+                for (size_t i = 0; i < unseen; ++i) dp.tokens[i] = history[len - 1 - unseen + i];
+                dp.tokens[unseen] = pending;
                 const bool replay = !opt.replay.empty();
                 T.push_params(0, tp);
                 // The drafter's steps write their tokens into the target's step parameters:
                 // after the target's parameter copy, and before the verify pass reads them.
                 order(T.stream(), Dm.stream());
-                Dm.push_params(1, dp);
+                Dm.push_params(1, dp, (int)unseen + 1);
                 uint32_t* chain = replay ? Dm.chain_dev() : T.step_params(0)->tokens + 1;
-                for (uint32_t s = 0; s + 1 < K; ++s) Dm.enqueue(1, PassKind::DraftStep, false, chain);
+                for (uint32_t s = 0; s + 1 < K; ++s)
+                    Dm.enqueue(s == 0 ? (int)unseen + 1 : 1, PassKind::DraftStep, false, chain);
+                D.set_consumed(len - 1);
                 if (replay) {
                     for (uint32_t s = 0; s + 1 < K; ++s)
                         tp.tokens[s + 1] = replay_propose(opt.replay, prompt.size(), len + s, opt.mismatch_rate,
