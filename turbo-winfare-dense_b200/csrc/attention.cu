@@ -170,26 +170,27 @@ __global__ void __launch_bounds__(kAttnThreads, HD <= 256 ? 2 : 1) attention_ker
     // Each thread copies one 16-byte column chunk c8 of keys j0, j0 + kKeyStep, ...
     const int c8 = threadIdx.x % kChunks, j0 = threadIdx.x / kChunks;
     const size_t head_off = (size_t)kvh_i * HD + c8 * 8;
-    auto load_tile = [&](int t0) {
+    // K and V tiles stream as separate cp.async groups so each overlaps the other's use: K of
+    // tile t+1 loads during the softmax and P V of tile t, V of tile t+1 during Q K^T of t+1.
+    auto load_half = [&](int t0, const uint16_t* ring, uint16_t* dst) {
         const int nt = min(kAttnKeys, ke - t0);
         const int slot0 = t0 % a.cap;
         for (int j = j0; j < kAttnKeys; j += kKeyStep) {
-            uint16_t* kd = sm.k + j * KS + c8 * 8;
-            uint16_t* vd = sm.v + j * KS + c8 * 8;
+            uint16_t* d = dst + j * KS + c8 * 8;
             if (j < nt) {
                 int slot = slot0 + j;
                 if (slot >= a.cap) slot %= a.cap;
-                const size_t src = (size_t)slot * a.kvh * HD + head_off;
-                cp16(kd, a.k_ring + src);
-                cp16(vd, a.v_ring + src);
+                cp16(d, ring + (size_t)slot * a.kvh * HD + head_off);
             } else {  // keys past the range: zeros, so P = 0 meets finite V
-                *reinterpret_cast<uint4*>(kd) = make_uint4(0, 0, 0, 0);
-                *reinterpret_cast<uint4*>(vd) = make_uint4(0, 0, 0, 0);
+                *reinterpret_cast<uint4*>(d) = make_uint4(0, 0, 0, 0);
             }
         }
         asm volatile("cp.async.commit_group;" ::: "memory");
     };
-    if (ks < ke) load_tile(ks);
+    if (ks < ke) {
+        load_half(ks, a.k_ring, sm.k);
+        load_half(ks, a.v_ring, sm.v);
+    }
 
     // Stage the query rows: warp w takes rows 2w, 2w+1. Scaling by 2^(15-e) puts the row's
     // max |q| in [2^14, 2^15); the scaled row is then split into terms of the MMA type.
@@ -246,8 +247,9 @@ __global__ void __launch_bounds__(kAttnThreads, HD <= 256 ? 2 : 1) attention_ker
     for (int n = 0; n < kNT; ++n) acc[n][0] = acc[n][1] = acc[n][2] = acc[n][3] = 0.f;
 
     for (int t0 = ks; t0 < ke; t0 += kAttnKeys) {
-        asm volatile("cp.async.wait_group 0;" ::: "memory");
-        __syncthreads();  // tile t0 (and the staged q) visible
+        const bool more = t0 + kAttnKeys < ke;
+        asm volatile("cp.async.wait_group 1;" ::: "memory");  // K of tile t0 (V may still land)
+        __syncthreads();  // K of tile t0 (and the staged q) visible
 
         // S[16 rows][keys 8w..8w+7] = sum over terms of Q_t K^T.
         {
@@ -273,7 +275,9 @@ __global__ void __launch_bounds__(kAttnThreads, HD <= 256 ? 2 : 1) attention_ker
             sr[8 * kSStride] = s[2];
             sr[8 * kSStride + 1] = s[3];
         }
-        __syncthreads();
+        __syncthreads();  // every warp is done with K of tile t0
+        if (more) load_half(t0 + kAttnKeys, a.k_ring, sm.k);
+        else asm volatile("cp.async.commit_group;" ::: "memory");  // keep the group count uniform
 
         // Online softmax: keys lane and lane + 32 of the tile.
 #pragma unroll
@@ -308,7 +312,8 @@ __global__ void __launch_bounds__(kAttnThreads, HD <= 256 ? 2 : 1) attention_ker
             }
             if (lane == 0) sm.corr[r] = corr;
         }
-        __syncthreads();
+        asm volatile("cp.async.wait_group 1;" ::: "memory");  // V of tile t0 (K of t0+1 may still land)
+        __syncthreads();  // P, the corrections and V of tile t0 visible
 
         // O[16][warp's columns] = O * corr + sum over terms of P_t V.
         {
@@ -347,8 +352,8 @@ __global__ void __launch_bounds__(kAttnThreads, HD <= 256 ? 2 : 1) attention_ker
                 }
             }
         }
-        __syncthreads();  // the tile buffers are refilled next
-        if (t0 + kAttnKeys < ke) load_tile(t0 + kAttnKeys);
+        __syncthreads();  // every warp is done with V of tile t0
+        if (more) load_half(t0 + kAttnKeys, a.v_ring, sm.v);
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
     __syncthreads();  // every warp is done with the K/V tile: sm.o may overwrite it
@@ -431,19 +436,22 @@ static cudaLaunchConfig_t attn_config(const AttnArgs& a, int splits, cudaStream_
     return cfg;
 }
 
-// Largest cluster size in {16, 12, 8} whose clusters all fit on the GPU at once; the occupancy
-// query is made once per (kernel, size).
+// Largest cluster size (key splits) whose clusters all fit on the GPU at once, so the launch is
+// one wave; the occupancy query is made once per (kernel, size). Sizes above 8 are non-portable
+// cluster sizes B200 allows.
+constexpr int kSplitSizes[] = {16, 12, 8, 7, 6, 5, 4, 3, 2, 1};
+constexpr int kNumSplitSizes = sizeof(kSplitSizes) / sizeof(kSplitSizes[0]);
 template <bool BF16, int HD>
 static int attn_splits(int clusters) {
-    static int max_active[3] = {-1, -1, -1};
-    const int sizes[3] = {16, 12, 8};
-    for (int i = 0; i < 3; ++i) {
-        if (max_active[i] < 0) {
+    static int max_active[kNumSplitSizes];
+    static bool queried = false;
+    if (!queried) {
+        for (int i = 0; i < kNumSplitSizes; ++i) {
             AttnArgs probe{};
             probe.M = 1;
             probe.qh = probe.kvh = 1;
             cudaLaunchAttribute attr[2];
-            cudaLaunchConfig_t cfg = attn_config<BF16, HD>(probe, sizes[i], nullptr, attr, false);
+            cudaLaunchConfig_t cfg = attn_config<BF16, HD>(probe, kSplitSizes[i], nullptr, attr, false);
             int n = 0;
             if (cudaOccupancyMaxActiveClusters(&n, attention_kernel<BF16, HD>, &cfg) != cudaSuccess) {
                 cudaGetLastError();
@@ -451,9 +459,11 @@ static int attn_splits(int clusters) {
             }
             max_active[i] = n;
         }
-        if (max_active[i] >= clusters) return sizes[i];
+        queried = true;
     }
-    return 8;
+    for (int i = 0; i < kNumSplitSizes; ++i)
+        if (max_active[i] >= clusters) return kSplitSizes[i];
+    return 1;
 }
 
 template <bool BF16, int HD>
