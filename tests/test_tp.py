@@ -1,8 +1,9 @@
-"""Tensor parallelism over NCCL: 2 ranks, one GPU each, run the config-0 target with query
-heads, FFN columns and the vocabulary split (KV heads replicated where there are fewer than
-ranks); the o-projection and down-projection outputs are all-reduced and the LM head's
-per-chunk bests all-gathered. Greedy token streams and round records must equal the oracle's
-(the reference has no multi-GPU path; its single-process CPU runner is the oracle)."""
+"""Tensor parallelism: 2 ranks, one GPU each, run the config-0 target with query heads, FFN
+columns and the vocabulary split (KV heads replicated where there are fewer than ranks); the
+o-projection and down-projection partials are summed across ranks over peer memory and the LM
+head's per-chunk bests all-gathered over NCCL. Greedy token streams and round records must equal
+the oracle's (the reference has no multi-GPU path; its single-process CPU runner is the oracle).
+A 200-token prompt also runs the tensor-core prefill (chunks of 128 and 72 rows) under TP."""
 from __future__ import annotations
 
 import json
@@ -27,12 +28,12 @@ def gpu_count():
         return 0
 
 
-@pytest.mark.parametrize("spec", ["no_spec", "spec_k5"])
-def test_tp2_streams_match_oracle(built_lib, config0, tmp_path, spec):
+@pytest.mark.parametrize("spec,plen", [("no_spec", 24), ("spec_k5", 24), ("spec_k5", 200)])
+def test_tp2_streams_match_oracle(built_lib, config0, tmp_path, spec, plen):
     if gpu_count() < 2:
         pytest.skip("needs 2 GPUs")
     tgt, drf = config0["target"], config0["draft"]
-    plen, n = 24, 48
+    n = 48
     prompt = np.random.default_rng(0).integers(0, 4096, plen)
     D = O.RestatedModel(drf) if spec == "spec_k5" else None
     want_tokens, want_rounds = O.spec_generate(O.RestatedModel(tgt), D, prompt, n, verify_width=5)
