@@ -263,6 +263,10 @@ def run_b200(args, rank, world):
                      "traffic_per": "pass (sum of dram__bytes_read+write over the pass's GEMM launches, ncu; "
                                     "profiles/vgemm_31b_shapes_m5.md)",
                      "ms_per_pass": ms},
+        "prefill": {"prompt_tokens": PROMPT_LEN,
+                    "ttft_ms": sum(s["ttft_ms"] for s in stats) / args.steps,
+                    "tok_s": PROMPT_LEN / (sum(s["ttft_ms"] for s in stats) / args.steps / 1000.0),
+                    "path": "tcgen05 prefill GEMM, chunks of 128 rows (target and drafter catch-up)"},
         "acceptance_sweep": sweep,
         "autoregressive_tok_s": ar_tok_s,
         "spec_stream_equals_greedy": all(matches),
