@@ -376,6 +376,11 @@ __global__ void __launch_bounds__(kAttnThreads, HD <= 256 ? 2 : 1) attention_ker
     constexpr int kGroups = HD / 64;
     const int K = a.qh * HD;
     const BFragView bv = bfrag_view(bfrag, (K + 127) / 128 * 128, a.M);
+    // Prefill rows (wide layout) take one static scale per row: every output is a convex
+    // combination of cached V rows, and V is RMS-normalised without a weight, so
+    // |o| <= max |v| <= sqrt(head_dim) (times the cache's rounding, well inside 1.01).
+    const bool wide = a.M > kMaxM;
+    const float wide_e = wide_row_scale(sqrtf((float)HD) * 1.01f), wide_inv = 1.0f / wide_e;
     for (int w = split * kAttnWarps + warp; w < kAttnRows * kGroups; w += nsplit * kAttnWarps) {
         const int r = w / kGroups, gi = w % kGroups;
         const int qr = chunk * kAttnRows + r;
@@ -408,11 +413,19 @@ __global__ void __launch_bounds__(kAttnThreads, HD <= 256 ? 2 : 1) attention_ker
         }
         const float inv = den > 0.f ? 1.0f / den : 0.f;
         const int m = qr / gqa, qhead = kvh_i * gqa + qr % gqa;
-        bfrag_store_group(bv, a.M, m, (qhead * HD) / 64 + gi, n0 * inv, n1 * inv, stage[warp]);
+        if (wide) {
+            wide_store_group(bv, m, (qhead * HD) / 64 + gi, n0 * inv, n1 * inv, wide_inv);
+            if (lane == 0 && qhead == 0 && gi == 0) bv.erow[m] = wide_e;
+        } else {
+            bfrag_store_group(bv, a.M, m, (qhead * HD) / 64 + gi, n0 * inv, n1 * inv, stage[warp]);
+        }
     }
     // A K that is not a multiple of 128 leaves one pad group per row: zero fragments.
     if ((K & 127) && blockIdx.y == 0 && blockIdx.z == 0 && split == 0)
-        for (int m = warp; m < a.M; m += kAttnWarps) bfrag_store_group(bv, a.M, m, K / 64, 0.f, 0.f, stage[warp]);
+        for (int m = warp; m < a.M; m += kAttnWarps) {
+            if (wide) wide_store_group(bv, m, K / 64, 0.f, 0.f, wide_inv);
+            else bfrag_store_group(bv, a.M, m, K / 64, 0.f, 0.f, stage[warp]);
+        }
     cluster.sync();  // keep every CTA's shared memory alive until all remote reads are done
 }
 

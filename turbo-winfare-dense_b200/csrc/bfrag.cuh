@@ -1,16 +1,36 @@
-// Producer side of the B-frag activation layout (see common.cuh). Every kernel that
-// feeds a verify GEMM (input norm, post-attention norm, GeGLU, attention output,
-// final norm) ends by calling bfrag_store_group, so activations are converted once and
-// the GEMM streams ready-made tensor-core fragments.
+// Producer side of the activation layouts (see common.cuh). Every kernel that feeds a GEMM
+// (input norm, post-attention norm, GeGLU, attention output, final norm) ends by calling
+// bfrag_store_group (verify rows) or wide_store_group (prefill rows), so activations are
+// converted once and the GEMM streams ready-made tensor-core operands.
 #pragma once
 #include "common.cuh"
 
 namespace g4b {
 
+// Wide layout (prefill rows): one (row m, 64-group gi) held by a warp, lane l owning columns
+// 2l and 2l+1, scaled by the row's 1/E (wide_row_scale), split into hi/lo fp16 tiles, plus the
+// group's Y record. Lane l's columns sit in 16-byte chunk l/4 of row m, stored at chunk
+// position (l/4) ^ (m % 8) of the row's 128 bytes. The caller writes erow[m] = E once. All 32
+// lanes must call it.
+__device__ __forceinline__ void wide_store_group(const BFragView& v, int m, int gi, float x0, float x1,
+                                                 float inv_e) {
+    const int lane = threadIdx.x & 31;
+    const float s0 = x0 * inv_e, s1 = x1 * inv_e;
+    const __half h0 = __float2half_rn(s0), h1 = __float2half_rn(s1);
+    const __half l0 = __float2half_rn(s0 - __half2float(h0));
+    const __half l1 = __float2half_rn(s1 - __half2float(h1));
+    const float y = warp_sum((__half2float(h0) + __half2float(l0)) + (__half2float(h1) + __half2float(l1)));
+    auto pk = [](__half a, __half b) { return (uint32_t)__half_as_ushort(a) | ((uint32_t)__half_as_ushort(b) << 16); };
+    char* hi = reinterpret_cast<char*>(v.frag) + (size_t)gi * kWideTileBytes;
+    const uint32_t off = (uint32_t)m * 128 + ((((uint32_t)lane >> 2) ^ ((uint32_t)m & 7)) << 4) + (lane & 3) * 4;
+    *reinterpret_cast<uint32_t*>(hi + off) = pk(h0, h1);
+    *reinterpret_cast<uint32_t*>(hi + v.lo_off + off) = pk(l0, l1);
+    if (lane == 0) v.ysum[(size_t)gi * kPrefillRows + m] = y * 5.9604644775390625e-08f;  // 2^-24
+}
+
 // Converts one (row m, 64-group gi) held by a warp -- lane l owns columns 2l and 2l+1 of
-// the group -- into fragments (B-frag layout for M <= 16 rows, wide layout above) and the
-// group's {E, Y} record. `stage` is 128 halves of per-warp shared scratch (B-frag layout
-// only). All 32 lanes must call it.
+// the group -- into B fragments of an M <= 16-row batch and the group's {E, Y} record.
+// `stage` is 128 halves of per-warp shared scratch. All 32 lanes must call it.
 __device__ __forceinline__ void bfrag_store_group(const BFragView& v, int M, int m, int gi,
                                                   float x0, float x1, __half* stage) {
     const int lane = threadIdx.x & 31;
@@ -25,19 +45,6 @@ __device__ __forceinline__ void bfrag_store_group(const BFragView& v, int M, int
     const __half l0 = __float2half_rn(s0 - __half2float(h0));
     const __half l1 = __float2half_rn(s1 - __half2float(h1));
     const float y = warp_sum((__half2float(h0) + __half2float(l0)) + (__half2float(h1) + __half2float(l1)));
-    if (M > kMaxM) {
-        // Wide layout: lane l's columns 2l, 2l+1 sit in 16-byte chunk l/4 of row m, stored at
-        // chunk position (l/4) ^ (m % 8) of the row's 128 bytes.
-        auto pk = [](__half a, __half b) {
-            return (uint32_t)__half_as_ushort(a) | ((uint32_t)__half_as_ushort(b) << 16);
-        };
-        char* hi = reinterpret_cast<char*>(v.frag) + (size_t)gi * kWideTileBytes;
-        const uint32_t off = (uint32_t)m * 128 + ((((uint32_t)lane >> 2) ^ ((uint32_t)m & 7)) << 4) + (lane & 3) * 4;
-        *reinterpret_cast<uint32_t*>(hi + off) = pk(h0, h1);
-        *reinterpret_cast<uint32_t*>(hi + v.lo_off + off) = pk(l0, l1);
-        if (lane == 0) v.gsum[(size_t)gi * kPrefillRows + m] = make_float2(E, y * 5.9604644775390625e-08f);
-        return;
-    }
     stage[2 * lane] = h0;
     stage[2 * lane + 1] = h1;
     stage[64 + 2 * lane] = l0;

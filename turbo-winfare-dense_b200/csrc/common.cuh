@@ -32,11 +32,13 @@
 //    fragments and the final scale.
 //
 // 4. Wide activation layout, for passes of 17..128 rows (prefill chunks) feeding the
-//    tcgen05 prefill GEMM (pgemm.cu). Same hi/lo split and {E, Y} records as (2), stored
-//    as ready-made shared-memory images of the MMA's B operand: per 64-group g, a 16 KB hi
-//    tile and a 16 KB lo tile of 128 rows x 64 fp16 in the 128-byte-swizzled K-major form
-//    (row m at byte m*128, 16-byte chunk c of the row at chunk position c ^ (m % 8)):
-//      hi[K/64][16384 B], lo[K/64][16384 B], gsum[K/64][128 rows] float2 {E, Y}
+//    tcgen05 prefill GEMM (pgemm.cu). The same fp16 hi/lo split, but with ONE power-of-two
+//    scale E per row (|x/E| < 2^11 for the row's largest element), so the GEMM can add the
+//    groups' scaled sums and apply E once per output. Stored as ready-made shared-memory images
+//    of the MMA's B operand: per 64-group g, a 16 KB hi tile and a 16 KB lo tile of 128 rows x
+//    64 fp16 in the 128-byte-swizzled K-major form (row m at byte m*128, 16-byte chunk c of the
+//    row at chunk position c ^ (m % 8)), then the groups' Y records and the rows' scales:
+//      hi[K/64][16384 B], lo[K/64][16384 B], ysum[K/64][128 rows] float, erow[128] float
 //    so one bulk copy per tile lands it in shared memory exactly as the MMA reads it.
 #pragma once
 #include <cuda_fp16.h>
@@ -73,7 +75,7 @@ __host__ __device__ inline size_t bfrag_gsum_bytes(int K, int M) {
 }
 // Bytes of the wide layout (M > kMaxM) for K columns.
 __host__ __device__ inline size_t wide_bytes(int K) {
-    return (size_t)(K / 64) * (2 * kWideTileBytes + kPrefillRows * sizeof(float2));
+    return (size_t)(K / 64) * (2 * kWideTileBytes + kPrefillRows * sizeof(float)) + kPrefillRows * sizeof(float);
 }
 // Capacity of one activation buffer for K columns at any M (either layout).
 __host__ __device__ inline size_t bfrag_capacity(int K) {
@@ -84,20 +86,32 @@ __host__ __device__ inline size_t bfrag_capacity(int K) {
 
 struct BFragView {
     uint4* frag;      // B-frag layout: [K/32][nb][32];  wide layout: the hi tiles
-    float2* gsum;     // B-frag layout: [K/64][nacc][8]; wide layout: [K/64][128]
+    float2* gsum;     // B-frag layout: [K/64][nacc][8] {E, Y}
     uint32_t lo_off;  // wide layout: bytes from a group's hi tile to its lo tile; 0 = B-frag layout
+    float* ysum;      // wide layout: [K/64][128] Y records
+    float* erow;      // wide layout: [128] row scales E
 };
 __host__ __device__ inline BFragView bfrag_view(void* base, int K, int M) {
     BFragView v;
     v.frag = reinterpret_cast<uint4*>(base);
     if (M > kMaxM) {
         v.lo_off = (uint32_t)((K / 64) * kWideTileBytes);
-        v.gsum = reinterpret_cast<float2*>(reinterpret_cast<char*>(base) + 2 * (size_t)v.lo_off);
+        v.gsum = nullptr;
+        v.ysum = reinterpret_cast<float*>(reinterpret_cast<char*>(base) + 2 * (size_t)v.lo_off);
+        v.erow = v.ysum + (size_t)(K / 64) * kPrefillRows;
     } else {
         v.lo_off = 0;
         v.gsum = reinterpret_cast<float2*>(reinterpret_cast<char*>(base) + bfrag_frag_bytes(K, M));
+        v.ysum = v.erow = nullptr;
     }
     return v;
+}
+// Row scale of the wide layout for a row whose largest |x| is amax (a power of two, so the
+// scaled row stays below 2^11 and the hi/lo split is exact to ~2^-22 of amax).
+__device__ __forceinline__ float wide_row_scale(float amax) {
+    int e = 0;
+    frexpf(amax, &e);
+    return amax > 0.f ? ldexpf(1.0f, e - 11) : 1.0f;
 }
 
 __device__ __forceinline__ float bf16_lo(uint32_t v) { return __uint_as_float(v << 16); }
@@ -125,6 +139,23 @@ __device__ __forceinline__ float block_sum(float v, float* red) {
     const int nw = (blockDim.x + 31) >> 5;
     float t = (threadIdx.x < nw) ? red[threadIdx.x] : 0.0f;
     if (wid == 0) t = warp_sum(t);
+    if (threadIdx.x == 0) red[0] = t;
+    __syncthreads();
+    const float r = red[0];
+    __syncthreads();
+    return r;
+}
+
+// Block-wide max of non-negative values for blockDim.x <= 1024; `red` needs 32 floats.
+__device__ __forceinline__ float block_max(float v, float* red) {
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    v = warp_max(v);
+    __syncthreads();
+    if (lane == 0) red[wid] = v;
+    __syncthreads();
+    const int nw = (blockDim.x + 31) >> 5;
+    float t = (threadIdx.x < nw) ? red[threadIdx.x] : 0.0f;
+    if (wid == 0) t = warp_max(t);
     if (threadIdx.x == 0) red[0] = t;
     __syncthreads();
     const float r = red[0];

@@ -17,9 +17,10 @@
 //     rounded up to 16, K = 16): 4 k-slices x {hi, lo} activation terms per group into a
 //     double-buffered fp32 accumulator in tensor memory, and tcgen05.commit signals the
 //     epilogue and frees the stage;
-//   * 8 epilogue warps read the group's accumulator (tcgen05.ld) and apply the group's
-//     scale and bias in fp32, acc += E * (s * P + b * Y), the verify GEMM's per-group
-//     formula, so products stay exact and each group is summed in fp32;
+//   * 16 epilogue warps read the group's accumulator (tcgen05.ld) and apply the group's
+//     scale and bias in fp32, acc += s * P + b * Y (products stay exact, each group is summed
+//     in fp32); the activations' power-of-two scale is per row, so it is applied once, when
+//     the tile segment is written;
 //   * at the end of a tile segment the partial is written straight to the dense output when
 //     one CTA covers the whole tile; otherwise to a fixed slot, and the last CTA to arrive
 //     on the tile's counter adds the slots in slot order (deterministic).
@@ -53,13 +54,13 @@ constexpr uint32_t kACol0 = kAccBufs * kAccCols;  // A buffers after the accumul
 constexpr uint32_t kACols = 32;             // 64 fp16 of a weight row
 constexpr int kErrPgemm = 6;
 
-// Stage layout (bytes): hi tile, lo tile, weight nibbles, scale/bias, {E, Y}.
+// Stage layout (bytes): hi tile, lo tile, weight nibbles, scale/bias, the group's Y records.
 constexpr uint32_t kOffHi = 0;
 constexpr uint32_t kOffLo = kWideTileBytes;
 constexpr uint32_t kOffW = 2 * kWideTileBytes;
 constexpr uint32_t kOffSB = kOffW + 4096;
-constexpr uint32_t kOffEY = kOffSB + 512;
-constexpr uint32_t kStageBytes = (kOffEY + kPrefillRows * 8 + 1023) / 1024 * 1024;
+constexpr uint32_t kOffY = kOffSB + 512;
+constexpr uint32_t kStageBytes = (kOffY + kPrefillRows * 4 + 1023) / 1024 * 1024;
 
 struct Bars {
     uint64_t full[kStages], empty[kStages];
@@ -146,15 +147,15 @@ __global__ void __maxnreg__(kMaxRegs) pgemm_kernel(PgemmParams p) {
             const char* wsrc = static_cast<const char*>(p.w);
             const char* hi = static_cast<const char*>(p.act);
             const char* lo = hi + (size_t)p.g_layout * kWideTileBytes;
-            const char* ey = lo + (size_t)p.g_layout * kWideTileBytes;
-            const uint32_t act_bytes = (uint32_t)nmma * 128, ey_bytes = (uint32_t)nmma * 8;
-            const uint32_t tx = kPgemmBlockBytes + 2 * act_bytes + ey_bytes;
+            const char* ys = lo + (size_t)p.g_layout * kWideTileBytes;
+            const uint32_t act_bytes = (uint32_t)nmma * 128, y_bytes = (uint32_t)nmma * 4;
+            const uint32_t tx = kPgemmBlockBytes + 2 * act_bytes + y_bytes;
             auto copy_act = [&](int i) {
                 const int s = i % kStages;
                 const int g = (int)((u0 + i) % G);
                 bulk_g2s(stage(s) + kOffHi, hi + (size_t)g * kWideTileBytes, act_bytes, &bars.full[s]);
                 bulk_g2s(stage(s) + kOffLo, lo + (size_t)g * kWideTileBytes, act_bytes, &bars.full[s]);
-                bulk_g2s(stage(s) + kOffEY, ey + (size_t)g * kPrefillRows * 8, ey_bytes, &bars.full[s]);
+                bulk_g2s(stage(s) + kOffY, ys + (size_t)g * kPrefillRows * 4, y_bytes, &bars.full[s]);
             };
             auto copy_w = [&](int i) {
                 const int s = i % kStages;
@@ -256,17 +257,21 @@ __global__ void __maxnreg__(kMaxRegs) pgemm_kernel(PgemmParams p) {
             if (ok && c0 < nmma) {  // warp-uniform
                 const uint32_t sbw = *reinterpret_cast<const uint32_t*>(stage(s) + kOffSB + r * 4);
                 const float sc = bf16_lo(sbw), bi = bf16_hi(sbw);
-                const float4* eyv = reinterpret_cast<const float4*>(stage(s) + kOffEY) + c0 / 2;
+                const float4* yv = reinterpret_cast<const float4*>(stage(s) + kOffY) + c0 / 4;
+                // The rows' scales are per row, not per group: acc += s*P + b*Y here and the
+                // row's E is applied once when the segment is written.
 #pragma unroll
                 for (int jc = 0; jc < kEpiCols; jc += 16) {
                     float P[16];
                     tc::ld16(tl + b * kAccCols + jc, P);
                     tc::wait_ld();
 #pragma unroll
-                    for (int j = 0; j < 16; j += 2) {
-                        const float4 e = eyv[(jc + j) / 2];  // {E, Y} of columns jc+j, jc+j+1
-                        acc[jc + j] = fmaf(e.x, fmaf(bi, e.y, sc * P[j]), acc[jc + j]);
-                        acc[jc + j + 1] = fmaf(e.z, fmaf(bi, e.w, sc * P[j + 1]), acc[jc + j + 1]);
+                    for (int j = 0; j < 16; j += 4) {
+                        const float4 y4 = yv[(jc + j) / 4];  // Y of columns jc+j .. jc+j+3
+                        acc[jc + j] = fmaf(sc, P[j], fmaf(bi, y4.x, acc[jc + j]));
+                        acc[jc + j + 1] = fmaf(sc, P[j + 1], fmaf(bi, y4.y, acc[jc + j + 1]));
+                        acc[jc + j + 2] = fmaf(sc, P[j + 2], fmaf(bi, y4.z, acc[jc + j + 2]));
+                        acc[jc + j + 3] = fmaf(sc, P[j + 3], fmaf(bi, y4.w, acc[jc + j + 3]));
                     }
                 }
             }
@@ -279,6 +284,9 @@ __global__ void __maxnreg__(kMaxRegs) pgemm_kernel(PgemmParams p) {
             if (g != G - 1 && i != n - 1) continue;
             // ---- end of this CTA's segment of tile t
             const int row = t * kPgemmTileRows + r;
+            const float* erow = reinterpret_cast<const float*>(static_cast<const char*>(p.act) +
+                                                               2 * (size_t)p.g_layout * kWideTileBytes) +
+                                (size_t)p.g_layout * kPrefillRows + c0;
             const int e = t == bars.seg_tile[0] ? 0 : 1;
             const int count = (t == bars.seg_tile[0] || t == bars.seg_tile[1]) ? bars.seg_count[e] : 1;
             if (count == 1) {
@@ -286,7 +294,7 @@ __global__ void __maxnreg__(kMaxRegs) pgemm_kernel(PgemmParams p) {
                     float* yp = p.y + (size_t)c0 * p.ldy + row;
 #pragma unroll
                     for (int j = 0; j < kEpiCols; ++j, yp += p.ldy)
-                        if (c0 + j < p.M) *yp = acc[j] * 16777216.0f;
+                        if (c0 + j < p.M) *yp = acc[j] * (__ldg(erow + j) * 16777216.0f);
                 }
             } else {
                 // Every CTA of the tile writes its slot; the last to arrive re-reads all of them
@@ -324,7 +332,7 @@ __global__ void __maxnreg__(kMaxRegs) pgemm_kernel(PgemmParams p) {
                         float* yp = p.y + (size_t)c0 * p.ldy + row;
 #pragma unroll
                         for (int j = 0; j < kEpiCols; ++j, yp += p.ldy)
-                            if (c0 + j < p.M) *yp = acc[j] * 16777216.0f;
+                            if (c0 + j < p.M) *yp = acc[j] * (__ldg(erow + j) * 16777216.0f);
                     }
                     if (warp == kConvWarps && lane == 0) p.cnt[t] = 0;
                 }

@@ -28,15 +28,27 @@ namespace cg = cooperative_groups;
 
 namespace g4b {
 
-// Writes a full row x[0..K) (in shared memory) as B fragments, one warp per 64-group.
-__device__ __forceinline__ void row_to_bfrags(const float* xs, int K, int M, int m, void* bfrag, __half* stage) {
+// Writes a full row x[0..K) (in shared memory) as GEMM operands, one warp per 64-group: B
+// fragments for a verify batch, the wide layout (with the row's scale) for a prefill chunk.
+// Block-collective; `red` is 32 floats of shared scratch.
+__device__ __forceinline__ void row_to_bfrags(const float* xs, int K, int M, int m, void* bfrag, __half* stage,
+                                              float* red) {
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     const int Kp = (K + 127) / 128 * 128;
     const BFragView v = bfrag_view(bfrag, Kp, M);
+    float inv_e = 1.f;
+    if (M > kMaxM) {
+        float amax = 0.f;
+        for (int c = threadIdx.x; c < K; c += blockDim.x) amax = fmaxf(amax, fabsf(xs[c]));
+        const float E = wide_row_scale(block_max(amax, red));
+        inv_e = 1.0f / E;
+        if (threadIdx.x == 0) v.erow[m] = E;
+    }
     for (int gi = warp; gi < Kp / 64; gi += nw) {
         const int k = gi * 64 + 2 * lane;
         const float x0 = k < K ? xs[k] : 0.f, x1 = k + 1 < K ? xs[k + 1] : 0.f;
-        bfrag_store_group(v, M, m, gi, x0, x1, stage + warp * 128);
+        if (M > kMaxM) wide_store_group(v, m, gi, x0, x1, inv_e);
+        else bfrag_store_group(v, M, m, gi, x0, x1, stage + warp * 128);
     }
 }
 
@@ -67,7 +79,7 @@ __global__ void embed_norm_kernel(const StepParams* __restrict__ sp, const uint3
     const float r = inv_rms(block_sum(ss, red), d);
     for (int c = threadIdx.x; c < d; c += blockDim.x) xs[c] = xs[c] * r * bf16_to_f32(w_in[c]);
     __syncthreads();
-    row_to_bfrags(xs, d, M, m, bfrag, stage);
+    row_to_bfrags(xs, d, M, m, bfrag, stage, red);
 }
 
 // ---------------------------------------------------------------- Q/K/V epilogue
@@ -202,6 +214,7 @@ __global__ void __launch_bounds__(kEpiMaxWarps * 32) rowepi_kernel(GemmOut o, Tp
                                                                     const uint16_t* __restrict__ w2, int d,
                                                                     void* bfrag, int M, int frag_row0) {
     __shared__ float4 red[kEpiMaxWarps];
+    __shared__ float red_max[32];
     __shared__ float4 cta_sum;
     __shared__ __half stage[kEpiMaxWarps][128];
     pdl_enter();
@@ -268,11 +281,13 @@ __global__ void __launch_bounds__(kEpiMaxWarps * 32) rowepi_kernel(GemmOut o, Tp
     // prefill chunk's final norm feeds the LM head its last row alone).
     const int Mf = M - frag_row0, mf = m - frag_row0;
     const BFragView bv = bfrag_view(bfrag, Kp, Mf);
+    float xv[GPW][2];
+    float amax = 0.f;
 #pragma unroll
     for (int j = 0; j < GPW; ++j) {
         const int gi = rank * gpc + warp + nw * j;
+        xv[j][0] = xv[j][1] = 0.f;
         if (gi >= g_end) continue;  // warp-uniform
-        float x[2] = {0.f, 0.f};
 #pragma unroll
         for (int e = 0; e < 2; ++e) {
             const int c = gi * 64 + 2 * lane + e;
@@ -281,10 +296,23 @@ __global__ void __launch_bounds__(kEpiMaxWarps * 32) rowepi_kernel(GemmOut o, Tp
                 const float a = __fmul_rn(__fmul_rn(yy, r1), bf16_to_f32(w1[c]));
                 const float hn = __fmul_rn(__fadd_rn(hh, a), out_scale);
                 h_out[(size_t)m * d + c] = hn;
-                x[e] = __fmul_rn(__fmul_rn(hn, r2), bf16_to_f32(w2[c]));
+                xv[j][e] = __fmul_rn(__fmul_rn(hn, r2), bf16_to_f32(w2[c]));
+                amax = fmaxf(amax, fabsf(xv[j][e]));
             }
         }
-        if (mf >= 0) bfrag_store_group(bv, Mf, mf, gi, x[0], x[1], stage[warp]);  // block-uniform
+    }
+    float inv_e = 1.f;
+    if (Mf > kMaxM) {  // wide layout (one CTA holds the whole row): the row's scale first
+        const float E = wide_row_scale(block_max(amax, red_max));
+        inv_e = 1.0f / E;
+        if (threadIdx.x == 0) bv.erow[mf] = E;
+    }
+#pragma unroll
+    for (int j = 0; j < GPW; ++j) {
+        const int gi = rank * gpc + warp + nw * j;
+        if (gi >= g_end || mf < 0) continue;  // warp-uniform / block-uniform
+        if (Mf > kMaxM) wide_store_group(bv, mf, gi, xv[j][0], xv[j][1], inv_e);
+        else bfrag_store_group(bv, Mf, mf, gi, xv[j][0], xv[j][1], stage[warp]);
     }
 }
 
@@ -311,7 +339,62 @@ __global__ void geglu_kernel(GemmOut gu, int F, void* bfrag, int M) {
     }
 }
 
+// Prefill rows: one CTA per row, so the row's scale is known before the wide-layout stores.
+// Pass 1 finds max |gelu(g) u| over the row; pass 2 recomputes and stores (the inputs are in L2).
+__global__ void __launch_bounds__(1024) geglu_wide_kernel(GemmOut gu, int F, void* bfrag, int M) {
+    __shared__ float red[32];
+    pdl_enter();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int m = blockIdx.x;
+    const int Fp = (F + 127) / 128 * 128;
+    const int ng = Fp / 64;
+    const BFragView v = bfrag_view(bfrag, Fp, M);
+    auto value = [&](int k, float2& x) {
+        x = make_float2(0.f, 0.f);
+        if (k < F) {
+            const float2 g = gemm_out_pair(gu, m, k), u = gemm_out_pair(gu, m, F + k);
+            x.x = gelu_tanh_dev(g.x) * u.x;
+            x.y = gelu_tanh_dev(g.y) * u.y;
+        }
+    };
+    float amax = 0.f;
+    for (int gi = warp; gi < ng; gi += nw) {
+        float2 x;
+        value(gi * 64 + 2 * lane, x);
+        amax = fmaxf(amax, fmaxf(fabsf(x.x), fabsf(x.y)));
+    }
+    const float E = wide_row_scale(block_max(amax, red));
+    if (threadIdx.x == 0) v.erow[m] = E;
+    const float inv_e = 1.0f / E;
+    for (int gi = warp; gi < ng; gi += nw) {
+        float2 x;
+        value(gi * 64 + 2 * lane, x);
+        wide_store_group(v, m, gi, x.x, x.y, inv_e);
+    }
+}
+
 // ---------------------------------------------------------------- plain conversion
+
+// x [M][ldx] fp32 -> wide layout for 17..128 rows: one CTA per row (its scale first).
+__global__ void __launch_bounds__(1024) wide_from_f32_kernel(const float* __restrict__ x, int ldx, int M, int K,
+                                                             void* bfrag) {
+    __shared__ float red[32];
+    pdl_enter();
+    const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
+    const int m = blockIdx.x;
+    const int Kp = (K + 127) / 128 * 128;
+    const BFragView v = bfrag_view(bfrag, Kp, M);
+    const float* xr = x + (size_t)m * ldx;
+    float amax = 0.f;
+    for (int c = threadIdx.x; c < K; c += blockDim.x) amax = fmaxf(amax, fabsf(xr[c]));
+    const float E = wide_row_scale(block_max(amax, red));
+    if (threadIdx.x == 0) v.erow[m] = E;
+    const float inv_e = 1.0f / E;
+    for (int gi = warp; gi < Kp / 64; gi += nw) {
+        const int k = gi * 64 + 2 * lane;
+        wide_store_group(v, m, gi, k < K ? xr[k] : 0.f, k + 1 < K ? xr[k + 1] : 0.f, inv_e);
+    }
+}
 
 // x [M][ldx] fp32 -> B fragments. One warp per (row, 64-group); groups past K are zeros.
 __global__ void bfrag_from_f32_kernel(const float* __restrict__ x, int ldx, int M, int K, void* bfrag) {
@@ -338,6 +421,7 @@ using namespace g4b;
 static int grid_for_warps(int warps) { return std::max(1, std::min(1184, (warps + 7) / 8)); }
 
 cudaError_t g4b_bfrag_from_f32(const float* x, int ldx, int M, int K, void* bfrag, cudaStream_t st, bool pdl) {
+    if (M > kMaxM) return launch(wide_from_f32_kernel, dim3(M), dim3(1024), 0, st, pdl, x, ldx, M, K, bfrag);
     const int ngroups = (K + 127) / 128 * 2;
     return launch(bfrag_from_f32_kernel, dim3(grid_for_warps(M * ngroups)), dim3(256), 0, st, pdl, x, ldx, M, K,
                   bfrag);
@@ -372,6 +456,8 @@ cudaError_t g4b_rowepi(const GemmOut& o, const TpGather& tg, const float* h_in, 
     if (M > kMaxM && ngp <= 3 * kEpiMaxWarps)
         return launch(rowepi_kernel<false, 3>, dim3(1, M), dim3(kEpiMaxWarps * 32), 0, st, pdl, o, tg, h_in, h_out, w1,
                       out_scale, w2, d, bfrag, M, frag_row0);
+    // Beyond here the cluster form: a prefill chunk's wide layout needs the row in one CTA.
+    if (M - frag_row0 > kMaxM) return cudaErrorInvalidValue;
     if ((ngp + kEpiClusters - 1) / kEpiClusters > kEpiWarps * kEpiGroupsPerWarp) return cudaErrorInvalidValue;
     static bool attr_set = false;
     if (!attr_set) {
@@ -398,6 +484,7 @@ cudaError_t g4b_rowepi(const GemmOut& o, const TpGather& tg, const float* h_in, 
 
 cudaError_t g4b_geglu(const GemmOut& gu, int F, void* bfrag, int M, cudaStream_t st, bool pdl) {
     if ((gu.ld | F) & 1) return cudaErrorInvalidValue;  // float2 loads
+    if (M > kMaxM) return launch(geglu_wide_kernel, dim3(M), dim3(1024), 0, st, pdl, gu, F, bfrag, M);
     const int ng = (F + 127) / 128 * 2;
     return launch(geglu_kernel, dim3(grid_for_warps(M * ng)), dim3(256), 0, st, pdl, gu, F, bfrag, M);
 }
