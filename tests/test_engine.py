@@ -98,6 +98,25 @@ def test_31b_attention_geometry_matches_oracle(built_lib, geom31, variant):
     e.close()
 
 
+def test_31b_geometry_bf16_kv(built_lib, geom31):
+    """Long-context mode (bf16 K/V, three-term bf16 query/probability splits) on the 31B
+    attention geometry: head_dim 512 with its head-dimension-split scores, GQA 4, a wrapped
+    sliding ring. BASELINE-distribution weights."""
+    path = geom31["baseline"]
+    e = engine(path, max_context=512, kv_bf16=True)
+    ref = O.RestatedModel(path, max_ctx=512, kv_mode=O.KV_BF16)
+    toks = np.random.default_rng(15).integers(0, 4096, 200)
+    want = [ref.forward(int(t), p) for p, t in enumerate(toks)]
+    pos = 0
+    for m in [16] * 10 + [9, 1, 5, 16, 9]:
+        got = e.forward_batch(toks[pos:pos + m], pos, vocab=4096, all_positions=True)
+        for i in range(m):
+            check_logits(got[i], want[pos + i], f"bf16 KV position {pos + i} (batch {m})")
+        pos += m
+    assert pos == len(toks)
+    e.close()
+
+
 def test_batched_rows_equal_sequential(built_lib, config0):
     """tests/test_gpu_forward.cpp:205-260 / test_context_dependence.cpp: a batch of M rows
     computes what M single-row passes compute."""

@@ -226,6 +226,27 @@ __global__ void __launch_bounds__(kAttnThreads, HD <= 256 ? 2 : 1) attention_ker
             }
         }
     }
+    // head_dim 512: Q K^T is split by head dimension instead of by key. Warp w keeps its 64-dim
+    // slice of the query terms in registers for the whole key loop and multiplies it by the
+    // same slice of all 64 keys of a tile; the eight partial score tiles are then added in
+    // shared memory (in the Q staging buffer, free once the slices are in registers). Each
+    // tile's K is read from shared memory once instead of the query once per warp.
+    constexpr bool kSplitDims = HD == 512;
+    constexpr int kDimsPerWarp = HD / kAttnWarps;
+    uint32_t qf[kSplitDims ? kTerms : 1][kSplitDims ? kDimsPerWarp / 16 : 1][4];
+    float* sp = reinterpret_cast<float*>(sm.q);  // [warp][16 rows][64 keys], column-swizzled
+    auto sp_at = [&](int w, int row, int key) { return sp + (w * kAttnRows + row) * kAttnKeys + (key ^ ((row & 7) << 3)); };
+    if constexpr (kSplitDims) {
+        static_assert((size_t)kAttnWarps * kAttnRows * kAttnKeys * 4 <= (size_t)2 * kAttnRows * (HD + 8) * 2,
+                      "partial scores must fit the query staging buffer");
+        __syncthreads();  // the staged query terms are visible
+        const uint16_t* qb = sm.q + (lane & 15) * KS + warp * kDimsPerWarp + (lane >> 4) * 8;
+#pragma unroll
+        for (int tt = 0; tt < kTerms; ++tt)
+#pragma unroll
+            for (int kk = 0; kk < kDimsPerWarp / 16; ++kk) ldsm_x4(qf[tt][kk], qb + tt * kAttnRows * KS + kk * 16);
+        __syncthreads();  // every warp holds its slice: the buffer now takes partial scores
+    }
     // Softmax state: warp w owns rows 2w, 2w+1 (every lane keeps the same copy).
     float m_run[2], l_run[2];
     int row_lo[2], row_hi[2];
@@ -251,8 +272,28 @@ __global__ void __launch_bounds__(kAttnThreads, HD <= 256 ? 2 : 1) attention_ker
         asm volatile("cp.async.wait_group 1;" ::: "memory");  // K of tile t0 (V may still land)
         __syncthreads();  // K of tile t0 (and the staged q) visible
 
+        if constexpr (kSplitDims) {
+            // Partial S[16 rows][64 keys] over this warp's 64 dimensions.
+            float sj[kAttnKeys / 8][4];
+            const uint16_t* kb = sm.k + (lane & 7) * KS + warp * kDimsPerWarp + (lane >> 3) * 8;
+#pragma unroll
+            for (int j = 0; j < kAttnKeys / 8; ++j) {
+                sj[j][0] = sj[j][1] = sj[j][2] = sj[j][3] = 0.f;
+#pragma unroll
+                for (int kh = 0; kh < kDimsPerWarp / 32; ++kh) {
+                    uint32_t b[4];
+                    ldsm_x4(b, kb + (8 * j) * KS + kh * 32);  // dims +0..15 and +16..31 of keys 8j..8j+7
+#pragma unroll
+                    for (int tt = 0; tt < kTerms; ++tt) {
+                        mma_tc<BF16>(sj[j], qf[tt][2 * kh], b[0], b[1]);
+                        mma_tc<BF16>(sj[j], qf[tt][2 * kh + 1], b[2], b[3]);
+                    }
+                }
+                *reinterpret_cast<float2*>(sp_at(warp, g, 8 * j + 2 * t4)) = make_float2(sj[j][0], sj[j][1]);
+                *reinterpret_cast<float2*>(sp_at(warp, g + 8, 8 * j + 2 * t4)) = make_float2(sj[j][2], sj[j][3]);
+            }
+        } else {
         // S[16 rows][keys 8w..8w+7] = sum over terms of Q_t K^T.
-        {
             float s[4] = {0.f, 0.f, 0.f, 0.f};
             const uint16_t* kb = sm.k + (warp * 8 + (lane & 7)) * KS + (lane >> 3) * 8;
             const uint16_t* qb = sm.q + (lane & 15) * KS + (lane >> 4) * 8;
@@ -289,7 +330,15 @@ __global__ void __launch_bounds__(kAttnThreads, HD <= 256 ? 2 : 1) attention_ker
             for (int h = 0; h < 2; ++h) {
                 const int kl = lane + 32 * h, tk = t0 + kl;
                 valid[h] = tk < ke && tk >= row_lo[rr] && tk < row_hi[rr];
-                sc[h] = valid[h] ? sm.s[r * kSStride + kl] * sm.qscale[r] * a.scale : -INFINITY;
+                float sv;
+                if constexpr (kSplitDims) {
+                    sv = 0.f;
+#pragma unroll
+                    for (int w = 0; w < kAttnWarps; ++w) sv += *sp_at(w, r, kl);
+                } else {
+                    sv = sm.s[r * kSStride + kl];
+                }
+                sc[h] = valid[h] ? sv * sm.qscale[r] * a.scale : -INFINITY;
             }
             const float m_new = fmaxf(m_run[rr], warp_max(fmaxf(sc[0], sc[1])));
             float p[2] = {0.f, 0.f}, corr = 1.f;

@@ -153,8 +153,8 @@ __global__ void qkv_epi_kernel(QkvEpiArgs a) {
 
 // ---------------------------------------------------------------- norm/residual epilogues
 
-// Rows of up to 32 64-column groups (d <= 2048): one CTA per row, one warp per group, the
-// statistics reduced in the CTA. Wider rows: one 16-CTA cluster per row; CTA r owns groups
+// Narrow rows (d <= 1024, and prefill rows up to d = 6144): one CTA per row, the statistics
+// reduced in the CTA. Wider verify rows: one 16-CTA cluster per row; CTA r owns groups
 // [r*gpc, (r+1)*gpc) (gpc = ceil(groups / 16)), each warp up to kEpiGroupsPerWarp of them, and
 // the cluster adds the CTA sums in rank order through distributed shared memory, so every CTA
 // derives the same two RMS factors. In both forms a warp holds its columns in registers from
@@ -448,11 +448,16 @@ cudaError_t g4b_rowepi(const GemmOut& o, const TpGather& tg, const float* h_in, 
     if (frag_row0 < 0 || frag_row0 >= M) return cudaErrorInvalidValue;
     if (tg.n < 1 || tg.n > kMaxTp) return cudaErrorInvalidValue;
     const int ngp = (d + 127) / 128 * 2;
-    if (ngp <= kEpiMaxWarps)  // one CTA per row, one warp per group
+    // Rows of up to 16 groups (d <= 1024): one CTA per row, one warp per group. Wider verify
+    // rows spread their slot sums over a 16-CTA cluster (measured faster from d = 1536 up).
+    if (ngp <= 16)
         return launch(rowepi_kernel<false>, dim3(1, M), dim3(ngp * 32), 0, st, pdl, o, tg, h_in, h_out, w1, out_scale,
                       w2, d, bfrag, M, frag_row0);
-    // A prefill chunk has rows enough to fill the GPU: one 32-warp CTA per row, each warp up to
-    // three groups, instead of a 16-CTA cluster per row.
+    // A prefill chunk has rows enough to fill the GPU: one CTA per row (each warp up to three
+    // groups) instead of a 16-CTA cluster per row.
+    if (M > kMaxM && ngp <= kEpiMaxWarps)
+        return launch(rowepi_kernel<false>, dim3(1, M), dim3(ngp * 32), 0, st, pdl, o, tg, h_in, h_out, w1, out_scale,
+                      w2, d, bfrag, M, frag_row0);
     if (M > kMaxM && ngp <= 3 * kEpiMaxWarps)
         return launch(rowepi_kernel<false, 3>, dim3(1, M), dim3(kEpiMaxWarps * 32), 0, st, pdl, o, tg, h_in, h_out, w1,
                       out_scale, w2, d, bfrag, M, frag_row0);
