@@ -28,13 +28,60 @@ __device__ __forceinline__ void wide_store_group(const BFragView& v, int m, int 
     if (lane == 0) v.ysum[(size_t)gi * kPrefillRows + m] = y * 5.9604644775390625e-08f;  // 2^-24
 }
 
+// Digit modes (M = 5..16): the (row m, group gi) held by a warp as three 8-bit digit planes.
+// Lane l's values sit at k = 2l and 2l+1 of the group: k32 step l/16, fragment thread
+// t = (l%16)/4, byte i = l%4, register b0 (even k) or b1 (odd k). Bytes meet in `stage`
+// (192 bytes), then 24 lanes write one uint2 each.
+__device__ __forceinline__ void digits_store_group(const BFragView& v, int M, int m, int gi, float x0, float x1,
+                                                   __half* stage) {
+    const int lane = threadIdx.x & 31;
+    const int nt_count = bmode_for(M).nt;
+    const float amax = warp_max(fmaxf(fabsf(x0), fabsf(x1)));
+    int e = 0;
+    frexpf(amax, &e);  // |x| < 2^e
+    const float inv = ldexpf(1.0f, 22 - e);
+    const int v0 = __float2int_rn(x0 * inv), v1 = __float2int_rn(x1 * inv);  // |v| < 2^22
+    unsigned char* st = reinterpret_cast<unsigned char*>(stage);
+    // byte index: ((d * 2 + kk_sub) * 2 + par) * 16 + t * 4 + i
+    const int kk_sub = lane >> 4, t = (lane >> 2) & 3, i = lane & 3;
+    int r0 = v0, r1 = v1;
+#pragma unroll
+    for (int d = 0; d < 3; ++d) {
+        const int d0 = (int)(signed char)(r0 & 0xFF), d1 = (int)(signed char)(r1 & 0xFF);
+        st[((d * 2 + kk_sub) * 2 + 0) * 16 + t * 4 + i] = (unsigned char)d0;
+        st[((d * 2 + kk_sub) * 2 + 1) * 16 + t * 4 + i] = (unsigned char)d1;
+        r0 = (r0 - d0) >> 8;
+        r1 = (r1 - d1) >> 8;
+    }
+    const int ysum = warp_sum_int(v0 + v1);
+    __syncwarp();
+    if (lane < 24) {
+        const int d = lane >> 3, ks = (lane >> 2) & 1, tt = lane & 3;
+        const uint32_t* w = reinterpret_cast<const uint32_t*>(st);
+        const uint2 val = make_uint2(w[((d * 2 + ks) * 2 + 0) * 4 + tt], w[((d * 2 + ks) * 2 + 1) * 4 + tt]);
+        int nt, col;
+        digit_col(nt_count, m, d, nt, col);
+        const int kk = 2 * (gi & 1) + ks;  // k32 step within the 128-wide k-tile
+        uint2* frag = reinterpret_cast<uint2*>(v.frag);
+        frag[(((size_t)(gi >> 1) * 4 + kk) * nt_count + nt) * 32 + col * 4 + tt] = val;
+    } else if (lane == 24) {
+        v.gsum[(size_t)gi * kMaxM + m] = make_float2(ldexpf(1.0f, e - 22), (float)ysum);
+    }
+    __syncwarp();
+}
+
 // Converts one (row m, 64-group gi) held by a warp -- lane l owns columns 2l and 2l+1 of
-// the group -- into B fragments of an M <= 16-row batch and the group's {E, Y} record.
-// `stage` is 128 halves of per-warp shared scratch. All 32 lanes must call it.
+// the group -- into B operands of an M <= 16-row batch (fp16 fragments for M <= 4, integer
+// digits above) and the group's {E, Y} record. `stage` is 128 halves of per-warp shared
+// scratch. All 32 lanes must call it.
 __device__ __forceinline__ void bfrag_store_group(const BFragView& v, int M, int m, int gi,
                                                   float x0, float x1, __half* stage) {
     const int lane = threadIdx.x & 31;
     const BMode md = bmode_for(M);
+    if (md.nt) {
+        digits_store_group(v, M, m, gi, x0, x1, stage);
+        return;
+    }
     const float amax = warp_max(fmaxf(fabsf(x0), fabsf(x1)));
     int e = 0;
     frexpf(amax, &e);  // amax = f * 2^e, f in [0.5, 1)

@@ -30,6 +30,17 @@
 //    16q for odd nibbles) is the value q * 2^-24, so a single AND turns two nibbles into
 //    an exact fp16x2 operand; the 2^24 (and 1/16) factors are folded into the activation
 //    fragments and the final scale.
+//    M = 5..16 use format 5 below instead.
+//
+// 5. Integer digits (verify rows 5..16). Per (64-group, row) a power-of-two E puts the group's
+//    values on a 23-bit signed grid, v = rint(x / E) with |v| < 2^22, split into balanced
+//    base-256 digits v = d0 + 256 d1 + 65536 d2 (each in [-128, 127]). Digit d of row m is MMA
+//    column digit_col(m, d). For the k32 step kk, lane (g, t) of n-tile nt holds
+//      b0 = bytes i = 0..3 of column g at k = 32 kk + 8t + 2i, b1 = the same at k + 1
+//    which matches the A fragments the weight words give with two ANDs (even nibbles, odd
+//    nibbles). frag[K/32][nt][32 lanes] uint2, gsum[K/64][16 rows] float2 {E, Y = sum v}.
+//    The MMA sums q * d exactly in int32; the epilogue forms P = sum q v in fp32 and adds
+//    E * (s * P + b * Y).
 //
 // 4. Wide activation layout, for passes of 17..128 rows (prefill chunks) feeding the
 //    tcgen05 prefill GEMM (pgemm.cu). The same fp16 hi/lo split, but with ONE power-of-two
@@ -56,22 +67,48 @@ constexpr int kKTileBytes = 4608;        // one (row group, k-tile) block
 constexpr int kNibBytes = 4096;
 constexpr int kWideTileBytes = kPrefillRows * 128;  // one 64-group's hi (or lo) tile
 
-// B-operand mode for M rows.
+// B-operand mode for M rows. M <= 4 packs the fp16 hi and lo terms of every row into one
+// m16n8k16 tile. M = 5..16 uses integer digits instead (format 5): three signed 8-bit digits
+// per value, multiplied by the nibbles with mma.sync m16n8k32 (u8 x s8 -> s32), which does
+// twice the work per instruction of the fp16 MMA at the same issue rate on sm_100a.
 struct BMode {
-    int nb;      // B tiles per k32 block
-    int nacc;    // accumulator column tiles
+    int nb;      // fp16 modes: B tiles per k32 block
+    int nacc;    // fp16 modes: accumulator column tiles
     bool packed; // M <= 4: hi in columns 0..3, lo in columns 4..7 of one tile
+    int nt;      // digit modes: n-tiles of 8 digit columns (0 = fp16 mode)
 };
 __host__ __device__ inline BMode bmode_for(int M) {
-    if (M <= 4) return {1, 1, true};
-    if (M <= 8) return {2, 1, false};
-    return {4, 2, false};
+    if (M <= 4) return {1, 1, true, 0};
+    if (M <= 5) return {0, 0, false, 2};
+    if (M <= 8) return {0, 0, false, 3};
+    return {0, 0, false, 6};
 }
 __host__ __device__ inline size_t bfrag_frag_bytes(int K, int M) {
-    return (size_t)(K / 32) * bmode_for(M).nb * 512;
+    const BMode md = bmode_for(M);
+    return md.nt ? (size_t)(K / 32) * md.nt * 32 * 8 : (size_t)(K / 32) * md.nb * 512;
 }
 __host__ __device__ inline size_t bfrag_gsum_bytes(int K, int M) {
-    return (size_t)(K / 64) * bmode_for(M).nacc * 8 * sizeof(float2);
+    const BMode md = bmode_for(M);
+    return (size_t)(K / 64) * (md.nt ? kMaxM : md.nacc * 8) * sizeof(float2);
+}
+// Digit modes: the (n-tile, column) of digit d of activation row m. Columns are arranged so
+// that the quad thread t holding accumulator columns 2t, 2t+1 holds all three digits of rows
+// t, 4+t (and 8+t, 12+t with six tiles); with two tiles, row 4's digits sit in column 2d+1 of
+// tile 1 (threads 0..2) and are gathered with two shuffles.
+__host__ __device__ inline void digit_col(int nt_count, int m, int d, int& nt, int& col) {
+    if (nt_count == 2 && m == 4) {
+        nt = 1;
+        col = 2 * d + 1;
+        return;
+    }
+    const int blk = m >> 3, mm = m & 7, tt = mm & 3;
+    if (mm < 4) {
+        nt = 3 * blk + (d < 2 ? 0 : 1);
+        col = d < 2 ? 2 * tt + d : 2 * tt;
+    } else {
+        nt = 3 * blk + (d == 0 ? 1 : 2);
+        col = d == 0 ? 2 * tt + 1 : 2 * tt + (d - 1);
+    }
 }
 // Bytes of the wide layout (M > kMaxM) for K columns.
 __host__ __device__ inline size_t wide_bytes(int K) {
@@ -119,6 +156,11 @@ __device__ __forceinline__ float bf16_hi(uint32_t v) { return __uint_as_float(v 
 __device__ __forceinline__ float bf16_to_f32(uint16_t v) { return __uint_as_float((uint32_t)v << 16); }
 
 __device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    return v;
+}
+__device__ __forceinline__ int warp_sum_int(int v) {
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
     return v;

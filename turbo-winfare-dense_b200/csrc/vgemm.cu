@@ -102,11 +102,23 @@ __device__ __forceinline__ void vgemm_sum_slots(const VgemmParams& p, int crg, i
     }
 }
 
-template <int NB, int NACC, bool PACKED>
-__global__ void __launch_bounds__(kThreads, NACC == 2 ? 2 : 3) vgemm_kernel(VgemmParams p) {
+// Per-k-tile sizes of the staged activation operands: fp16 fragments (NT = 0) or integer
+// digits (NT n-tiles), and the k-tiles one 8 KB staging chunk holds.
+template <int NB, int NACC, int NT>
+struct BStage {
+    static constexpr int frag_u4_kt = NT ? 64 * NT : 4 * NB * 32;      // uint4 per k-tile
+    static constexpr int gsum_f4_kt = NT ? kMaxM : 2 * NACC * 4;       // float4 per k-tile
+    static constexpr int kt = 512 / frag_u4_kt > 0 ? 512 / frag_u4_kt : 1;
+    static constexpr int frag_u4 = kt * frag_u4_kt;
+    static constexpr int gsum_f4 = kt * gsum_f4_kt;
+};
+
+template <int NB, int NACC, bool PACKED, int NT>
+__global__ void __launch_bounds__(kThreads, (NACC == 2 || NT == 6) ? 2 : 3) vgemm_kernel(VgemmParams p) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
-    constexpr int kFragU4 = Chunk<NB>::frag_u4;
-    constexpr int kGsumF4 = Chunk<NB>::kt * 2 * NACC * 4;
+    using BS = BStage<NB, NACC, NT>;
+    constexpr int kFragU4 = BS::frag_u4;
+    constexpr int kGsumF4 = BS::gsum_f4;
     constexpr int kBufU4 = kFragU4 + kGsumF4;
     uint4* ring = reinterpret_cast<uint4*>(smem_raw);                 // [warp][stage][288]
     uint4* bbuf = ring + kWarps * kStages * kBlockU4;                 // [2][kBufU4]
@@ -158,7 +170,7 @@ __global__ void __launch_bounds__(kThreads, NACC == 2 ? 2 : 3) vgemm_kernel(Vgem
         ChunkRec r;
         r.s = s0;
         r.kt = kt0;
-        r.len = min(min(Chunk<NB>::kt, ktiles - kt0), u_end - s0);
+        r.len = min(min(BS::kt, ktiles - kt0), u_end - s0);
         return r;
     };
     auto next_chunk = [&](const ChunkRec& r) {
@@ -166,10 +178,10 @@ __global__ void __launch_bounds__(kThreads, NACC == 2 ? 2 : 3) vgemm_kernel(Vgem
         return make_chunk(r.s + r.len, kt);
     };
     auto issue_b = [&](const ChunkRec& r, int buf) {  // thread 0: activation fragments of a chunk
-        const uint32_t fb = (uint32_t)r.len * 4 * NB * 512, gb = (uint32_t)r.len * 2 * NACC * 64;
+        const uint32_t fb = (uint32_t)r.len * BS::frag_u4_kt * 16, gb = (uint32_t)r.len * BS::gsum_f4_kt * 16;
         mbar_expect_tx(&bbar[buf], fb + gb);
-        bulk_g2s(bbuf + buf * kBufU4, p.bfrag + (size_t)r.kt * 4 * NB * 32, fb, &bbar[buf]);
-        bulk_g2s(bbuf + buf * kBufU4 + kFragU4, reinterpret_cast<const float4*>(p.gsum) + (size_t)r.kt * 2 * NACC * 4,
+        bulk_g2s(bbuf + buf * kBufU4, p.bfrag + (size_t)r.kt * BS::frag_u4_kt, fb, &bbar[buf]);
+        bulk_g2s(bbuf + buf * kBufU4 + kFragU4, reinterpret_cast<const float4*>(p.gsum) + (size_t)r.kt * BS::gsum_f4_kt,
                  gb, &bbar[buf]);
     };
 
@@ -194,13 +206,18 @@ __global__ void __launch_bounds__(kThreads, NACC == 2 ? 2 : 3) vgemm_kernel(Vgem
     bool failed = n_units > 0 && !mbar_wait(&bbar[0], 0);
     uint32_t wphase = 0;  // bit s: parity of the next completion of stage s
 
-    float acc[kTilesPerWarp][NACC][4];
+    constexpr int kJ = DigitRows<NT ? NT : 2>::J;
+    float acc[kTilesPerWarp][NT ? 1 : NACC][4];          // fp16 modes
+    float accd[kTilesPerWarp][NT ? kJ : 1][2];           // digit modes
 #pragma unroll
-    for (int r = 0; r < kTilesPerWarp; ++r)
+    for (int r = 0; r < kTilesPerWarp; ++r) {
 #pragma unroll
-        for (int a = 0; a < NACC; ++a)
+        for (int a = 0; a < (NT ? 1 : NACC); ++a)
 #pragma unroll
             for (int i = 0; i < 4; ++i) acc[r][a][i] = 0.f;
+#pragma unroll
+        for (int j = 0; j < (NT ? kJ : 1); ++j) accd[r][j][0] = accd[r][j][1] = 0.f;
+    }
     int seg_crg = cur.crg;
     const int g = lane >> 2, t = lane & 3;
 
@@ -214,10 +231,26 @@ __global__ void __launch_bounds__(kThreads, NACC == 2 ? 2 : 3) vgemm_kernel(Vgem
                             : p.out.part + ((size_t)crg * p.out.max_slots + (c - lo)) * kMaxM * kCtaRows;
         const int ld = direct ? p.ldy : kCtaRows;
         const int nmax = direct ? p.N - crg * kCtaRows : kCtaRows;
+        if constexpr (NT > 0) {
+            // Thread t holds activation rows t, 4+t (8+t, 12+t); with two tiles its second
+            // row is row 4, valid on thread 0 only. No 2^24 factor: digits are integers.
+#pragma unroll
+            for (int r = 0; r < kTilesPerWarp; ++r)
+#pragma unroll
+                for (int j = 0; j < kJ; ++j)
+#pragma unroll
+                    for (int h = 0; h < 2; ++h) {
+                        const int m = (NT == 2 && j == 1) ? 4 : 4 * j + t;
+                        const bool mine = NT != 2 || j == 0 || t == 0;
+                        const int nl = warp * kWarpRows + r * 16 + g + 8 * h;
+                        if (act && !failed && mine && m < p.M && nl < nmax) dst[(size_t)m * ld + nl] = accd[r][j][h];
+                        accd[r][j][h] = 0.f;
+                    }
+        }
 #pragma unroll
         for (int r = 0; r < kTilesPerWarp; ++r) {
 #pragma unroll
-            for (int a = 0; a < NACC; ++a) {
+            for (int a = 0; a < (NT ? 0 : NACC); ++a) {
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
                     float v = acc[r][a][i];
@@ -263,9 +296,15 @@ __global__ void __launch_bounds__(kThreads, NACC == 2 ? 2 : 3) vgemm_kernel(Vgem
             wphase ^= 1u << stage;
             if (!failed) {
                 const int off = cur.u - chk.s;
-                const uint4* bsm = bbuf + (ch & 1) * kBufU4 + off * 4 * NB * 32;
-                const float4* gsm = reinterpret_cast<const float4*>(bbuf + (ch & 1) * kBufU4 + kFragU4) + off * 2 * NACC * 4;
-                compute_ktile<NB, NACC, PACKED>(ring + (warp * kStages + stage) * kBlockU4, bsm, gsm, acc, lane);
+                const uint4* bsm = bbuf + (ch & 1) * kBufU4 + off * BS::frag_u4_kt;
+                const float4* gsm = reinterpret_cast<const float4*>(bbuf + (ch & 1) * kBufU4 + kFragU4) +
+                                    off * BS::gsum_f4_kt;
+                if constexpr (NT > 0)
+                    compute_ktile_digits<NT>(ring + (warp * kStages + stage) * kBlockU4,
+                                             reinterpret_cast<const uint2*>(bsm), reinterpret_cast<const float2*>(gsm),
+                                             accd, lane);
+                else
+                    compute_ktile<NB, NACC, PACKED>(ring + (warp * kStages + stage) * kBlockU4, bsm, gsm, acc, lane);
             }
         }
         __syncwarp();
@@ -293,21 +332,21 @@ __global__ void __launch_bounds__(kThreads, NACC == 2 ? 2 : 3) vgemm_kernel(Vgem
     if (failed && p.err) atomicExch(p.err, 1);
 }
 
-template <int NB, int NACC>
+template <int NB, int NACC, int NT>
 static constexpr size_t smem_bytes() {
-    return (size_t)kWarps * kStages * kKTileBytes +
-           2 * ((size_t)Chunk<NB>::frag_u4 * 16 + (size_t)Chunk<NB>::kt * 2 * NACC * 64) +
+    using BS = BStage<NB, NACC, NT>;
+    return (size_t)kWarps * kStages * kKTileBytes + 2 * ((size_t)BS::frag_u4 * 16 + (size_t)BS::gsum_f4 * 16) +
            (kWarps * kStages + 2) * sizeof(uint64_t);
 }
 
-template <int NB, int NACC, bool PACKED>
+template <int NB, int NACC, bool PACKED, int NT>
 static int max_ctas_per_sm() {
     static int cached = -1;
     if (cached < 0) {
-        const size_t sm = smem_bytes<NB, NACC>();
-        cudaFuncSetAttribute(vgemm_kernel<NB, NACC, PACKED>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
+        const size_t sm = smem_bytes<NB, NACC, NT>();
+        cudaFuncSetAttribute(vgemm_kernel<NB, NACC, PACKED, NT>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)sm);
         int n = 0;
-        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, vgemm_kernel<NB, NACC, PACKED>, kThreads, sm);
+        cudaOccupancyMaxActiveBlocksPerMultiprocessor(&n, vgemm_kernel<NB, NACC, PACKED, NT>, kThreads, sm);
         cached = n > 0 ? n : 1;
     }
     return cached;
@@ -323,10 +362,10 @@ static int sm_count() {
     return n;
 }
 
-template <int NB, int NACC, bool PACKED>
+template <int NB, int NACC, bool PACKED, int NT>
 static cudaError_t launch_t(const VgemmParams& p, cudaStream_t st, bool pdl) {
-    max_ctas_per_sm<NB, NACC, PACKED>();  // sets the dynamic shared memory attribute once
-    return launch(vgemm_kernel<NB, NACC, PACKED>, dim3(p.out.grid), dim3(kThreads), smem_bytes<NB, NACC>(), st,
+    max_ctas_per_sm<NB, NACC, PACKED, NT>();  // sets the dynamic shared memory attribute once
+    return launch(vgemm_kernel<NB, NACC, PACKED, NT>, dim3(p.out.grid), dim3(kThreads), smem_bytes<NB, NACC, NT>(), st,
                   pdl, p);
 }
 
@@ -337,9 +376,10 @@ using namespace g4b;
 int vgemm_grid(int M, int n_crg, int ktiles) {
     const BMode md = bmode_for(M);
     int per_sm;
-    if (md.packed) per_sm = max_ctas_per_sm<1, 1, true>();
-    else if (md.nb == 2) per_sm = max_ctas_per_sm<2, 1, false>();
-    else per_sm = max_ctas_per_sm<4, 2, false>();
+    if (md.packed) per_sm = max_ctas_per_sm<1, 1, true, 0>();
+    else if (md.nt == 2) per_sm = max_ctas_per_sm<0, 0, false, 2>();
+    else if (md.nt == 3) per_sm = max_ctas_per_sm<0, 0, false, 3>();
+    else per_sm = max_ctas_per_sm<0, 0, false, 6>();
     const long long T = (long long)n_crg * ktiles;
     return (int)std::min<long long>(T, (long long)sm_count() * per_sm);
 }
@@ -368,7 +408,8 @@ cudaError_t vgemm_launch(const VgemmParams& p, cudaStream_t st, bool pdl) {
     if (((long long)p.out.n_crg * p.out.ktiles + 1) * p.out.grid >= (1ll << 31)) return cudaErrorInvalidValue;
     if (vgemm_max_slots(p.out.grid, p.out.n_crg, p.out.ktiles) > p.out.max_slots) return cudaErrorInvalidValue;
     const BMode md = bmode_for(p.M);
-    if (md.packed) return launch_t<1, 1, true>(p, st, pdl);
-    if (md.nb == 2) return launch_t<2, 1, false>(p, st, pdl);
-    return launch_t<4, 2, false>(p, st, pdl);
+    if (md.packed) return launch_t<1, 1, true, 0>(p, st, pdl);
+    if (md.nt == 2) return launch_t<0, 0, false, 2>(p, st, pdl);
+    if (md.nt == 3) return launch_t<0, 0, false, 3>(p, st, pdl);
+    return launch_t<0, 0, false, 6>(p, st, pdl);
 }
