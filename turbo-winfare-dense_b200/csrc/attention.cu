@@ -150,7 +150,7 @@ __global__ void __launch_bounds__(kAttnThreads, HD <= 256 ? 2 : 1) attention_ker
     cg::cluster_group cluster = cg::this_cluster();
     AttnSmem sm = attn_smem(smem_raw, HD, kTerms);
 
-    pdl_enter();
+    pdl_launch_dependents();
     const int split = (int)cluster.block_rank();
     const int nsplit = (int)cluster.num_blocks();
     const int kvh_i = blockIdx.y, chunk = blockIdx.z;
@@ -172,24 +172,43 @@ __global__ void __launch_bounds__(kAttnThreads, HD <= 256 ? 2 : 1) attention_ker
     const size_t head_off = (size_t)kvh_i * HD + c8 * 8;
     // K and V tiles stream as separate cp.async groups so each overlaps the other's use: K of
     // tile t+1 loads during the softmax and P V of tile t, V of tile t+1 during Q K^T of t+1.
-    auto load_half = [&](int t0, const uint16_t* ring, uint16_t* dst) {
+    // load_half copies the tile's keys at positions [plo, phi) and zero-fills the slots past
+    // the range (P = 0 there meets finite V); the caller commits the group.
+    auto load_half = [&](int t0, const uint16_t* ring, uint16_t* dst, int plo, int phi) {
         const int nt = min(kAttnKeys, ke - t0);
         const int slot0 = t0 % a.cap;
         for (int j = j0; j < kAttnKeys; j += kKeyStep) {
             uint16_t* d = dst + j * KS + c8 * 8;
             if (j < nt) {
+                if (t0 + j < plo || t0 + j >= phi) continue;
                 int slot = slot0 + j;
                 if (slot >= a.cap) slot %= a.cap;
                 cp16(d, ring + (size_t)slot * a.kvh * HD + head_off);
-            } else {  // keys past the range: zeros, so P = 0 meets finite V
+            } else if (plo == kmin) {
                 *reinterpret_cast<uint4*>(d) = make_uint4(0, 0, 0, 0);
             }
         }
-        asm volatile("cp.async.commit_group;" ::: "memory");
     };
+    auto commit = [] { asm volatile("cp.async.commit_group;" ::: "memory"); };
+    // The first tile's keys from earlier passes are fetched before waiting on the producer
+    // (the Q/K/V epilogue). Nothing in this pass changes them or base_pos: base_pos is written
+    // only by a pass's last kernel (head_finalize), every pass starts with a kernel launched
+    // without programmatic overlap, and this pass rewrites only the ring slots of positions
+    // base.. (a sliding ring keeps window + max rows slots, so those never alias a key a row
+    // still needs). The keys at base.. and the query rows are read after the wait. A prefill
+    // chunk (two waves of CTAs, several tiles each) keeps the plain order, in which Q K^T of the
+    // first tile waits for K alone.
+    const int early = a.M > kMaxM ? kmin : base;  // keys [kmin, early) are fetched early
     if (ks < ke) {
-        load_half(ks, a.k_ring, sm.k);
-        load_half(ks, a.v_ring, sm.v);
+        load_half(ks, a.k_ring, sm.k, kmin, early);
+        load_half(ks, a.v_ring, sm.v, kmin, early);
+    }
+    pdl_wait();
+    if (ks < ke) {
+        load_half(ks, a.k_ring, sm.k, early, kmax);
+        commit();
+        load_half(ks, a.v_ring, sm.v, early, kmax);
+        commit();
     }
 
     // Stage the query rows: warp w takes rows 2w, 2w+1. Scaling by 2^(15-e) puts the row's
@@ -317,8 +336,8 @@ __global__ void __launch_bounds__(kAttnThreads, HD <= 256 ? 2 : 1) attention_ker
             sr[8 * kSStride + 1] = s[3];
         }
         __syncthreads();  // every warp is done with K of tile t0
-        if (more) load_half(t0 + kAttnKeys, a.k_ring, sm.k);
-        else asm volatile("cp.async.commit_group;" ::: "memory");  // keep the group count uniform
+        if (more) load_half(t0 + kAttnKeys, a.k_ring, sm.k, kmin, kmax);
+        commit();  // (an empty group past the last tile keeps the group count uniform)
 
         // Online softmax: keys lane and lane + 32 of the tile.
 #pragma unroll
@@ -402,7 +421,10 @@ __global__ void __launch_bounds__(kAttnThreads, HD <= 256 ? 2 : 1) attention_ker
             }
         }
         __syncthreads();  // every warp is done with V of tile t0
-        if (more) load_half(t0 + kAttnKeys, a.v_ring, sm.v);
+        if (more) {
+            load_half(t0 + kAttnKeys, a.v_ring, sm.v, kmin, kmax);
+            commit();
+        }
     }
     asm volatile("cp.async.wait_group 0;" ::: "memory");
     __syncthreads();  // every warp is done with the K/V tile: sm.o may overwrite it

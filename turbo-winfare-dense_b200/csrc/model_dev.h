@@ -78,26 +78,61 @@ __device__ __forceinline__ void slot_sums_each(const float* const (&p)[NE], cons
                 if (s0 + k < ns[j]) out[j] += v[k][j];
     }
 }
-// Columns n, n+1 (n even) of row m.
-__device__ __forceinline__ float2 gemm_out_pair(const GemmOut& o, int m, int n) {
-    if (!o.part.part) return *reinterpret_cast<const float2*>(o.y + (size_t)m * o.ld + n);
-    const int crg = n >> 8;
-    const float2* p = reinterpret_cast<const float2*>(slot_base(o.part, m, crg) + (n & 255));
-    const int ns = slot_count(o.part, crg);
+// Columns n, n+1 (n even) of row m of a split-K output, summed over the slots [lo, hi) of their
+// row group in slot order.
+__device__ __forceinline__ float2 slot_pair_range(const PartView& v, int m, int n, int lo, int hi) {
+    const float2* p = reinterpret_cast<const float2*>(slot_base(v, m, n >> 8) + (n & 255));
     float2 s = make_float2(0.f, 0.f);
-    for (int s0 = 0; s0 < ns; s0 += 16) {
-        float2 v[16];
+    for (int s0 = lo; s0 < hi; s0 += 16) {
+        float2 t[16];
 #pragma unroll
         for (int k = 0; k < 16; ++k)
-            if (s0 + k < ns) v[k] = __ldcg(p + (size_t)(s0 + k) * 2048);
+            if (s0 + k < hi) t[k] = __ldcg(p + (size_t)(s0 + k) * 2048);
 #pragma unroll
         for (int k = 0; k < 16; ++k)
-            if (s0 + k < ns) {
-                s.x += v[k].x;
-                s.y += v[k].y;
+            if (s0 + k < hi) {
+                s.x += t[k].x;
+                s.y += t[k].y;
             }
     }
     return s;
+}
+// Column pairs (na, na+1) and (nb, nb+1) of row m, the slot loads of both in flight together
+// (each pair still summed in its own slot order).
+__device__ __forceinline__ void gemm_out_two_pairs(const GemmOut& o, int m, int na, int nb, float2& a, float2& b) {
+    if (!o.part.part) {
+        a = *reinterpret_cast<const float2*>(o.y + (size_t)m * o.ld + na);
+        b = *reinterpret_cast<const float2*>(o.y + (size_t)m * o.ld + nb);
+        return;
+    }
+    const float2* pa = reinterpret_cast<const float2*>(slot_base(o.part, m, na >> 8) + (na & 255));
+    const float2* pb = reinterpret_cast<const float2*>(slot_base(o.part, m, nb >> 8) + (nb & 255));
+    const int nsa = slot_count(o.part, na >> 8), nsb = slot_count(o.part, nb >> 8);
+    a = b = make_float2(0.f, 0.f);
+    for (int s0 = 0; s0 < max(nsa, nsb); s0 += 16) {
+        float2 ta[16], tb[16];
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            if (s0 + k < nsa) ta[k] = __ldcg(pa + (size_t)(s0 + k) * 2048);
+            if (s0 + k < nsb) tb[k] = __ldcg(pb + (size_t)(s0 + k) * 2048);
+        }
+#pragma unroll
+        for (int k = 0; k < 16; ++k) {
+            if (s0 + k < nsa) {
+                a.x += ta[k].x;
+                a.y += ta[k].y;
+            }
+            if (s0 + k < nsb) {
+                b.x += tb[k].x;
+                b.y += tb[k].y;
+            }
+        }
+    }
+}
+// Columns n, n+1 (n even) of row m.
+__device__ __forceinline__ float2 gemm_out_pair(const GemmOut& o, int m, int n) {
+    if (!o.part.part) return *reinterpret_cast<const float2*>(o.y + (size_t)m * o.ld + n);
+    return slot_pair_range(o.part, m, n, 0, slot_count(o.part, n >> 8));
 }
 #endif
 

@@ -90,10 +90,11 @@ __global__ void embed_norm_kernel(const StepParams* __restrict__ sp, const uint3
 // is a block reduction. Restates the reference's q/k/v norms, RoPE and FP16 cache rounding
 // (src/cpu_reference.cpp:452-498).
 
-// Elements r0 + i and r0 + i + half of row m.
+// Elements r0 + i and r0 + i + half of row m (DENSE: the GEMM wrote a dense matrix).
+template <bool DENSE>
 __device__ __forceinline__ float2 load_pair(const GemmOut& o, int m, int r0, int half) {
     const int i = threadIdx.x;
-    if (!o.part.part) {
+    if (DENSE) {
         const float* src = o.y + (size_t)m * o.ld + r0 + i;
         return make_float2(src[0], src[half]);
     }
@@ -103,42 +104,54 @@ __device__ __forceinline__ float2 load_pair(const GemmOut& o, int m, int r0, int
     const int nsb = (rb >> 8) == (ra >> 8) ? nsa : slot_count(o.part, rb >> 8);
     const int nsj[2] = {nsa, nsb};
     float v[2];
-    slot_sums_each<2, 8>(pj, nsj, max(nsa, nsb), v);
+    slot_sums_each<2, 16>(pj, nsj, max(nsa, nsb), v);
     return make_float2(v[0], v[1]);
 }
 
-__global__ void qkv_epi_kernel(QkvEpiArgs a) {
+// DENSE (a prefill chunk's dense GEMM output) is a separate instance: the slot sums' registers
+// would otherwise cut the CTAs resident per SM for the thousands of CTAs of a 128-row chunk.
+template <bool DENSE>
+__global__ void __launch_bounds__(256, 3) qkv_epi_kernel(QkvEpiArgs a) {
     __shared__ float red[32];
-    pdl_enter();
+    pdl_launch_dependents();
     const int heads = a.qh + a.kvh;
     const int m = blockIdx.x / heads, head = blockIdx.x % heads;
     const int hd = a.hd, half = hd / 2, i = threadIdx.x;
-    const int pos = a.sp->base_pos + m;
     const int nq = a.qh * hd, nk = a.kvh * hd;
     const bool is_q = head < a.qh;
     const int kvh = head - a.qh;
-    float2 x = load_pair(a.qkv, m, is_q ? head * hd : nq + kvh * hd, half);
+    // Before waiting on the GEMM: the norm weights and the rotation, which depend only on the
+    // position (base_pos is written by a pass's last kernel alone, and every pass starts with a
+    // kernel launched without programmatic overlap, so it is stable here).
+    const int pos = a.sp->base_pos + m;
+    const uint16_t* wn = is_q ? a.q_norm : a.k_norm;
+    const float wa = bf16_to_f32(wn[i]), wb = bf16_to_f32(wn[i + half]);
+    float rc = 1.f, rs = 0.f;
+    if (i < a.rotated) {
+        const float freq = 1.0f / powf(a.theta, (float)(2 * i) / (float)hd);
+        const float ang = (float)pos * freq;
+        rc = cosf(ang);
+        rs = sinf(ang);
+    }
+    pdl_wait();
+    float2 x = load_pair<DENSE>(a.qkv, m, is_q ? head * hd : nq + kvh * hd, half);
     const float r = inv_rms(block_sum(x.x * x.x + x.y * x.y, red), hd);
     if (!is_q) {
         // V: unweighted norm of v_proj, or of the RAW k on layers without v_proj.
-        const float2 v = a.has_v ? load_pair(a.qkv, m, nq + nk + kvh * hd, half) : x;
+        const float2 v = a.has_v ? load_pair<DENSE>(a.qkv, m, nq + nk + kvh * hd, half) : x;
         const float rv = inv_rms(block_sum(v.x * v.x + v.y * v.y, red), hd);
         uint16_t* vd = a.v_ring + ((size_t)(pos % a.cap) * a.kvh + kvh) * hd;
         const float t0 = v.x * rv, t1 = v.y * rv;
         vd[i] = a.kv_bf16 ? bf16_bits_rne(t0) : f16_bits_like_reference(t0);
         vd[i + half] = a.kv_bf16 ? bf16_bits_rne(t1) : f16_bits_like_reference(t1);
     }
-    const uint16_t* wn = is_q ? a.q_norm : a.k_norm;
-    x.x = x.x * r * bf16_to_f32(wn[i]);
-    x.y = x.y * r * bf16_to_f32(wn[i + half]);
+    x.x = x.x * r * wa;
+    x.y = x.y * r * wb;
     // NeoX rotary on the first `rotated` pairs.
     if (i < a.rotated) {
-        const float freq = 1.0f / powf(a.theta, (float)(2 * i) / (float)hd);
-        const float ang = (float)pos * freq;
-        const float c = cosf(ang), s = sinf(ang);
         const float x0 = x.x, x1 = x.y;
-        x.x = x0 * c - x1 * s;
-        x.y = x0 * s + x1 * c;
+        x.x = x0 * rc - x1 * rs;
+        x.y = x0 * rs + x1 * rc;
     }
     if (is_q) {
         float* qd = a.q_out + ((size_t)m * a.qh + head) * hd;
@@ -207,7 +220,7 @@ __device__ __forceinline__ float2 tp_pair(const TpGather& tg, int m, int ld, int
 }
 
 template <bool CLUSTER, int GPW = kEpiGroupsPerWarp>
-__global__ void __launch_bounds__(kEpiMaxWarps * 32) rowepi_kernel(GemmOut o, TpGather tg,
+__global__ void __launch_bounds__(CLUSTER ? kEpiWarps * 32 : kEpiMaxWarps * 32) rowepi_kernel(GemmOut o, TpGather tg,
                                                                     const float* __restrict__ h_in,
                                                                     float* __restrict__ h_out,
                                                                     const uint16_t* __restrict__ w1, float out_scale,
@@ -217,8 +230,7 @@ __global__ void __launch_bounds__(kEpiMaxWarps * 32) rowepi_kernel(GemmOut o, Tp
     __shared__ float red_max[32];
     __shared__ float4 cta_sum;
     __shared__ __half stage[kEpiMaxWarps][128];
-    pdl_enter();
-    if (tg.n > 1) tp_sync(tg, blockIdx.x == 0 && blockIdx.y == 0);
+    pdl_launch_dependents();
     const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5, nw = blockDim.x >> 5;
     const int rank = CLUSTER ? (int)cg::this_cluster().block_rank() : 0;
     const int m = blockIdx.y;
@@ -226,18 +238,64 @@ __global__ void __launch_bounds__(kEpiMaxWarps * 32) rowepi_kernel(GemmOut o, Tp
     const int ngp = Kp / 64;
     const int gpc = CLUSTER ? (ngp + kEpiClusters - 1) / kEpiClusters : ngp;
     const int g_end = min(ngp, (rank + 1) * gpc);
+    // The two norm weights of this thread's columns do not depend on the producer: load them
+    // before the wait (in the 1024-thread form, with its 64 registers, after it).
+    float2 wv1[GPW], wv2[GPW];
+    auto load_w = [&] {
+#pragma unroll
+        for (int j = 0; j < GPW; ++j) {
+            const int c0 = (rank * gpc + warp + nw * j) * 64 + 2 * lane;
+            wv1[j] = wv2[j] = make_float2(0.f, 0.f);
+            if (rank * gpc + warp + nw * j < g_end && c0 < d) {
+                wv1[j] = make_float2(bf16_to_f32(w1[c0]), bf16_to_f32(w1[c0 + 1]));
+                wv2[j] = make_float2(bf16_to_f32(w2[c0]), bf16_to_f32(w2[c0 + 1]));
+            }
+        }
+    };
+    constexpr bool kPreloadW = CLUSTER || GPW <= 2;
+    if constexpr (kPreloadW) load_w();
+    pdl_wait();
+    // Weight of column c (= (rank * gpc + warp + nw * j) * 64 + 2 * lane + e).
+    auto wt1 = [&](int j, int e, int c) { return kPreloadW ? (e ? wv1[j].y : wv1[j].x) : bf16_to_f32(w1[c]); };
+    auto wt2 = [&](int j, int e, int c) { return kPreloadW ? (e ? wv2[j].y : wv2[j].x) : bf16_to_f32(w2[c]); };
+    if (tg.n > 1) tp_sync(tg, blockIdx.x == 0 && blockIdx.y == 0);
 
     float2 y[GPW], h[GPW];
+    // A cluster CTA with at least twice as many warps as groups (d = 1536: 2 groups, 8 warps)
+    // spreads each group's split-K slots over wpg warps, so a long slot list (a down projection
+    // split 48 ways) costs one round of loads instead of several. Warp w sums share w / gpc of
+    // group w % gpc's slots; warp g < gpc then adds the shares in share order.
+    const int wpg = (CLUSTER && o.part.part && tg.n == 1) ? nw / gpc : 1;  // block-uniform
+    if (wpg >= 2) {
+        __shared__ float2 share_sum[kEpiWarps][32];
+        const int gl = warp % gpc, share = warp / gpc;
+        const int c0 = (rank * gpc + gl) * 64 + 2 * lane;
+        float2 ps = make_float2(0.f, 0.f);
+        if (share < wpg && rank * gpc + gl < g_end && c0 < d) {
+            const int ns = slot_count(o.part, c0 >> 8);
+            ps = slot_pair_range(o.part, m, c0, ns * share / wpg, ns * (share + 1) / wpg);
+        }
+        share_sum[warp][lane] = ps;
+        __syncthreads();
+        if (warp < gpc) {
+            y[0] = share_sum[warp][lane];
+            for (int s = 1; s < wpg; ++s) {
+                y[0].x += share_sum[warp + s * gpc][lane].x;
+                y[0].y += share_sum[warp + s * gpc][lane].y;
+            }
+        }
+    }
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
     for (int j = 0; j < GPW; ++j) {
         const int gi = rank * gpc + warp + nw * j;
         const int c0 = gi * 64 + 2 * lane;
-        y[j] = h[j] = make_float2(0.f, 0.f);
+        if (wpg < 2 || j > 0 || warp >= gpc) y[j] = make_float2(0.f, 0.f);
+        h[j] = make_float2(0.f, 0.f);
         if (gi < g_end && c0 < d) {
-            y[j] = tg.n > 1 ? tp_pair(tg, m, o.ld, c0) : gemm_out_pair(o, m, c0);
+            if (wpg < 2) y[j] = tg.n > 1 ? tp_pair(tg, m, o.ld, c0) : gemm_out_pair(o, m, c0);
             h[j] = *reinterpret_cast<const float2*>(h_in + (size_t)m * d + c0);
-            const float ca = y[j].x * bf16_to_f32(w1[c0]), cb = y[j].y * bf16_to_f32(w1[c0 + 1]);
+            const float ca = y[j].x * wt1(j, 0, c0), cb = y[j].y * wt1(j, 1, c0 + 1);
             acc.x += y[j].x * y[j].x + y[j].y * y[j].y;
             acc.y += h[j].x * h[j].x + h[j].y * h[j].y;
             acc.z += h[j].x * ca + h[j].y * cb;
@@ -293,10 +351,10 @@ __global__ void __launch_bounds__(kEpiMaxWarps * 32) rowepi_kernel(GemmOut o, Tp
             const int c = gi * 64 + 2 * lane + e;
             if (c < d) {
                 const float yy = e ? y[j].y : y[j].x, hh = e ? h[j].y : h[j].x;
-                const float a = __fmul_rn(__fmul_rn(yy, r1), bf16_to_f32(w1[c]));
+                const float a = __fmul_rn(__fmul_rn(yy, r1), wt1(j, e, c));
                 const float hn = __fmul_rn(__fadd_rn(hh, a), out_scale);
                 h_out[(size_t)m * d + c] = hn;
-                xv[j][e] = __fmul_rn(__fmul_rn(hn, r2), bf16_to_f32(w2[c]));
+                xv[j][e] = __fmul_rn(__fmul_rn(hn, r2), wt2(j, e, c));
                 amax = fmaxf(amax, fabsf(xv[j][e]));
             }
         }
@@ -331,7 +389,8 @@ __global__ void geglu_kernel(GemmOut gu, int F, void* bfrag, int M) {
         const int k = gi * 64 + 2 * lane;
         float x0 = 0.f, x1 = 0.f;
         if (k < F) {
-            const float2 g = gemm_out_pair(gu, m, k), u = gemm_out_pair(gu, m, F + k);
+            float2 g, u;
+            gemm_out_two_pairs(gu, m, k, F + k, g, u);
             x0 = gelu_tanh_dev(g.x) * u.x;
             x1 = gelu_tanh_dev(g.y) * u.y;
         }
@@ -349,10 +408,11 @@ __global__ void __launch_bounds__(1024) geglu_wide_kernel(GemmOut gu, int F, voi
     const int Fp = (F + 127) / 128 * 128;
     const int ng = Fp / 64;
     const BFragView v = bfrag_view(bfrag, Fp, M);
+    const float* yr = gu.y + (size_t)m * gu.ld;  // a prefill GEMM's dense output
     auto value = [&](int k, float2& x) {
         x = make_float2(0.f, 0.f);
         if (k < F) {
-            const float2 g = gemm_out_pair(gu, m, k), u = gemm_out_pair(gu, m, F + k);
+            const float2 g = *reinterpret_cast<const float2*>(yr + k), u = *reinterpret_cast<const float2*>(yr + F + k);
             x.x = gelu_tanh_dev(g.x) * u.x;
             x.y = gelu_tanh_dev(g.y) * u.y;
         }
@@ -438,7 +498,9 @@ cudaError_t g4b_embed_norm(const StepParams* sp, const uint32_t* ew, const uint1
 
 cudaError_t g4b_qkv_epi(const QkvEpiArgs& a, cudaStream_t st, bool pdl) {
     if (a.hd % 64 || a.hd > 1024 || a.rotated > a.hd / 2) return cudaErrorInvalidValue;
-    return launch(qkv_epi_kernel, dim3(a.M * (a.qh + a.kvh)), dim3(a.hd / 2), 0, st, pdl, a);
+    if (!a.qkv.part.part)
+        return launch(qkv_epi_kernel<true>, dim3(a.M * (a.qh + a.kvh)), dim3(a.hd / 2), 0, st, pdl, a);
+    return launch(qkv_epi_kernel<false>, dim3(a.M * (a.qh + a.kvh)), dim3(a.hd / 2), 0, st, pdl, a);
 }
 
 cudaError_t g4b_rowepi(const GemmOut& o, const TpGather& tg, const float* h_in, float* h_out, const uint16_t* w1,
@@ -489,7 +551,10 @@ cudaError_t g4b_rowepi(const GemmOut& o, const TpGather& tg, const float* h_in, 
 
 cudaError_t g4b_geglu(const GemmOut& gu, int F, void* bfrag, int M, cudaStream_t st, bool pdl) {
     if ((gu.ld | F) & 1) return cudaErrorInvalidValue;  // float2 loads
-    if (M > kMaxM) return launch(geglu_wide_kernel, dim3(M), dim3(1024), 0, st, pdl, gu, F, bfrag, M);
+    if (M > kMaxM) {  // prefill: the GEMM wrote a dense matrix
+        if (gu.part.part) return cudaErrorInvalidValue;
+        return launch(geglu_wide_kernel, dim3(M), dim3(1024), 0, st, pdl, gu, F, bfrag, M);
+    }
     const int ng = (F + 127) / 128 * 2;
     return launch(geglu_kernel, dim3(grid_for_warps(M * ng)), dim3(256), 0, st, pdl, gu, F, bfrag, M);
 }
