@@ -93,6 +93,15 @@ __device__ __forceinline__ void ldsm_x2_t(uint32_t& r0, uint32_t& r1, const void
     const uint32_t s = (uint32_t)__cvta_generic_to_shared(p);
     asm volatile("ldmatrix.sync.aligned.m8n8.x2.trans.shared.b16 {%0,%1}, [%2];" : "=r"(r0), "=r"(r1) : "r"(s));
 }
+__device__ __forceinline__ uint32_t smem_addr(const void* p) { return (uint32_t)__cvta_generic_to_shared(p); }
+// The float2 at shared-memory address `addr` of cluster CTA `rank` (distributed shared memory).
+__device__ __forceinline__ float2 ld_cluster_f2(uint32_t addr, int rank) {
+    uint32_t ra;
+    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(ra) : "r"(addr), "r"(rank));
+    float2 v;
+    asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(ra) : "memory");
+    return v;
+}
 __device__ __forceinline__ void cp16(void* smem, const void* gmem) {
     const uint32_t s = (uint32_t)__cvta_generic_to_shared(smem);
     asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(s), "l"(gmem));
@@ -456,31 +465,30 @@ __global__ void __launch_bounds__(kAttnThreads, HD <= 256 ? 2 : 1) attention_ker
         const int r = w / kGroups, gi = w % kGroups;
         const int qr = chunk * kAttnRows + r;
         if (qr >= R) continue;  // warp-uniform
-        float2 ml[kMaxSplits];
+        // Every split's {m, l} and partial output in one round of remote loads (32-bit cluster
+        // addresses keep the 32 loads in flight within the register budget).
+        float2 ml[kMaxSplits], op[kMaxSplits];
+        const uint32_t ml_addr = smem_addr(sm.ml + r), o_addr = smem_addr(sm.o + r * HD + gi * 64 + 2 * lane);
 #pragma unroll
-        for (int s = 0; s < kMaxSplits; ++s)
-            ml[s] = s < nsplit ? cluster.map_shared_rank(sm.ml, s)[r] : make_float2(-INFINITY, 0.f);
+        for (int s = 0; s < kMaxSplits; ++s) {
+            ml[s] = make_float2(-INFINITY, 0.f);
+            op[s] = make_float2(0.f, 0.f);
+            if (s < nsplit) {
+                ml[s] = ld_cluster_f2(ml_addr, s);
+                op[s] = ld_cluster_f2(o_addr, s);
+            }
+        }
         float mx = -INFINITY;
 #pragma unroll
         for (int s = 0; s < kMaxSplits; ++s) mx = fmaxf(mx, ml[s].x);
         float n0 = 0.f, n1 = 0.f, den = 0.f;
 #pragma unroll
-        for (int s0 = 0; s0 < kMaxSplits; s0 += 8) {
-            if (s0 >= nsplit) break;
-            float2 op[8];
-#pragma unroll
-            for (int s = 0; s < 8; ++s)
-                if (s0 + s < nsplit)
-                    op[s] = *reinterpret_cast<const float2*>(cluster.map_shared_rank(sm.o, s0 + s) + r * HD + gi * 64 +
-                                                             2 * lane);
-#pragma unroll
-            for (int s = 0; s < 8; ++s) {
-                if (s0 + s >= nsplit || ml[s0 + s].y <= 0.f) continue;
-                const float wgt = expf(ml[s0 + s].x - mx);
-                n0 += wgt * op[s].x;
-                n1 += wgt * op[s].y;
-                den += wgt * ml[s0 + s].y;
-            }
+        for (int s = 0; s < kMaxSplits; ++s) {
+            if (s >= nsplit || ml[s].y <= 0.f) continue;
+            const float wgt = expf(ml[s].x - mx);
+            n0 += wgt * op[s].x;
+            n1 += wgt * op[s].y;
+            den += wgt * ml[s].y;
         }
         const float inv = den > 0.f ? 1.0f / den : 0.f;
         const int m = qr / gqa, qhead = kvh_i * gqa + qr % gqa;

@@ -172,6 +172,23 @@ __device__ __forceinline__ float warp_max(float v) {
 }
 
 // Block-wide sum for blockDim.x <= 1024; `red` needs 32 floats of shared memory.
+// Two block-wide sums in one exchange: each warp's partials are added in warp order by every
+// thread. `red` (32 entries) must not be written again by the block without a barrier first.
+__device__ __forceinline__ float2 block_sum2(float2 v, float2* red) {
+    const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
+    v.x = warp_sum(v.x);
+    v.y = warp_sum(v.y);
+    if (lane == 0) red[wid] = v;
+    __syncthreads();
+    const int nw = (blockDim.x + 31) >> 5;
+    float2 t = red[0];
+    for (int i = 1; i < nw; ++i) {
+        t.x += red[i].x;
+        t.y += red[i].y;
+    }
+    return t;
+}
+
 __device__ __forceinline__ float block_sum(float v, float* red) {
     const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5;
     v = warp_sum(v);

@@ -112,7 +112,7 @@ __device__ __forceinline__ float2 load_pair(const GemmOut& o, int m, int r0, int
 // would otherwise cut the CTAs resident per SM for the thousands of CTAs of a 128-row chunk.
 template <bool DENSE>
 __global__ void __launch_bounds__(256, 3) qkv_epi_kernel(QkvEpiArgs a) {
-    __shared__ float red[32];
+    __shared__ float2 red2[32];
     pdl_launch_dependents();
     const int heads = a.qh + a.kvh;
     const int m = blockIdx.x / heads, head = blockIdx.x % heads;
@@ -134,12 +134,14 @@ __global__ void __launch_bounds__(256, 3) qkv_epi_kernel(QkvEpiArgs a) {
         rs = sinf(ang);
     }
     pdl_wait();
+    // A KV head's k and v rows load together and their two sums of squares share one
+    // reduction (V: unweighted norm of v_proj, or of the RAW k on layers without v_proj).
     float2 x = load_pair<DENSE>(a.qkv, m, is_q ? head * hd : nq + kvh * hd, half);
-    const float r = inv_rms(block_sum(x.x * x.x + x.y * x.y, red), hd);
+    const float2 v = !is_q && a.has_v ? load_pair<DENSE>(a.qkv, m, nq + nk + kvh * hd, half) : x;
+    const float2 ss = block_sum2(make_float2(x.x * x.x + x.y * x.y, v.x * v.x + v.y * v.y), red2);
+    const float r = inv_rms(ss.x, hd);
     if (!is_q) {
-        // V: unweighted norm of v_proj, or of the RAW k on layers without v_proj.
-        const float2 v = a.has_v ? load_pair<DENSE>(a.qkv, m, nq + nk + kvh * hd, half) : x;
-        const float rv = inv_rms(block_sum(v.x * v.x + v.y * v.y, red), hd);
+        const float rv = inv_rms(ss.y, hd);
         uint16_t* vd = a.v_ring + ((size_t)(pos % a.cap) * a.kvh + kvh) * hd;
         const float t0 = v.x * rv, t1 = v.y * rv;
         vd[i] = a.kv_bf16 ? bf16_bits_rne(t0) : f16_bits_like_reference(t0);
@@ -327,7 +329,10 @@ __global__ void __launch_bounds__(CLUSTER ? kEpiWarps * 32 : kEpiMaxWarps * 32) 
         for (int r = 1; r < kEpiClusters; ++r) {
             t.x += u[r].x; t.y += u[r].y; t.z += u[r].z; t.w += u[r].w;
         }
-        cluster.sync();  // every CTA has read the others' sums before any of them exits
+        // Every CTA must have read the others' sums before any of them exits: arrive once the
+        // sums are in registers (the operands tie the arrival to the loads' completion), wait
+        // at the end, so the barrier's latency overlaps the column work below.
+        asm volatile("barrier.cluster.arrive.release.aligned;" ::"f"(t.x), "f"(t.y), "f"(t.z), "f"(t.w) : "memory");
     } else {
         __syncthreads();
         t = cta_sum;
@@ -372,6 +377,7 @@ __global__ void __launch_bounds__(CLUSTER ? kEpiWarps * 32 : kEpiMaxWarps * 32) 
         if (Mf > kMaxM) wide_store_group(bv, mf, gi, xv[j][0], xv[j][1], inv_e);
         else bfrag_store_group(bv, Mf, mf, gi, xv[j][0], xv[j][1], stage[warp]);
     }
+    if constexpr (CLUSTER) asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
 
 // ---------------------------------------------------------------- GeGLU
