@@ -116,6 +116,10 @@ G4DENSE_API int g4dense_engine_forward_batch(void* handle, const unsigned int* t
 G4DENSE_API int g4dense_engine_set_decode_options(void* handle, long long stop_token, int draft_k,
                                                   const unsigned int* replay, int replay_len, double mismatch_rate,
                                                   unsigned long long mismatch_seed);
+/* Non-speculative sampled decoding (temperature > 0, no repetition penalty) draws each token on
+ * the device by default, as sample_token does on the host (src/sampling.cpp:92-169); on = 0
+ * selects the host draw over a copied logits row. Additive; returns 0 or -1. */
+G4DENSE_API int g4dense_engine_set_device_sampling(void* handle, int on);
 /* Per-round (drafted, accepted, emitted) triples of the last speculative generation. */
 G4DENSE_API int g4dense_engine_last_rounds(void* handle, int* out, int cap_triples);
 G4DENSE_API int g4dense_nccl_unique_id(void* out128);

@@ -9,6 +9,7 @@
  */
 #ifndef G4DENSE_B200_OPS_H
 #define G4DENSE_B200_OPS_H
+#include <stddef.h>
 #include <stdint.h>
 
 #ifdef __cplusplus
@@ -68,6 +69,17 @@ G4B_API int g4b_gemv_int8(const uint8_t* W, const uint16_t* S, const uint16_t* B
  * out[m][c] = ctx[m][c] * sigmoid(gate[m][c]) for c < n, m < batch; strides in floats. */
 G4B_API int g4b_attn_gate(const float* ctx, const float* gate, float* out, int n, int batch, int ctx_stride,
                           int gate_stride, int out_stride, void* stream);
+/* Token sampling on a device logits row, the reference's sample_token (src/sampling.cpp:92-169):
+ * greedy argmax (ties to the lowest index) when temperature <= 0; otherwise the top_k (or 256)
+ * largest logits, a top-p cut measured against the full-vocabulary softmax, and a
+ * temperature-scaled draw with the xorshift64* generator seeded with `seed` (the caller derives it
+ * as the reference's seed_for does, src/sampling.cpp:63-72). logits: fp32 [vocab] device memory,
+ * vocab <= 262144; top_k 0..256 (0 = 256-wide shortlist); top_p in (0, 1]. `workspace` is
+ * g4b_sample_workspace() bytes of device memory, used by one stream at a time; the token is
+ * written to out_token (device memory). Two kernel launches. */
+G4B_API size_t g4b_sample_workspace(void);
+G4B_API int g4b_sample_token(const float* logits, int vocab, float temperature, float top_p, int top_k,
+                             uint64_t seed, void* workspace, uint32_t* out_token, void* stream);
 /* out4 = {N, K, grid CTAs at M=5, split-K slots per row group} */
 G4B_API int g4b_qmat_info(const g4b_qmat* q, int* out4);
 

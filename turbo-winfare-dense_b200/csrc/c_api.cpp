@@ -33,6 +33,7 @@ struct EngineHandle {
     std::vector<uint32_t> replay;
     double mismatch_rate{0};
     uint64_t mismatch_seed{0};
+    bool device_sampling{true};
     double gate_min_accept{0.45};
     int gate_window{24};
     void* nccl_comm{nullptr};
@@ -102,6 +103,7 @@ g4b::GenerationOptions to_gen(const EngineHandle* e, const G4DenseGenerationOpti
     g.replay = e->replay;
     g.mismatch_rate = e->mismatch_rate;
     g.mismatch_seed = e->mismatch_seed;
+    g.device_sampling = e->device_sampling;
     g.gate_min_accept = e->gate_min_accept;
     g.gate_window = e->gate_window;
     return g;
@@ -351,6 +353,16 @@ G4DENSE_API int g4dense_engine_set_decode_options(void* handle, long long stop_t
     e->replay.assign(replay, replay ? replay + replay_len : replay);
     e->mismatch_rate = mismatch_rate;
     e->mismatch_seed = mismatch_seed;
+    return 0;
+}
+
+G4DENSE_API int g4dense_engine_set_device_sampling(void* handle, int on) {
+    clear_error();
+    if (!handle) {
+        set_error("Invalid arguments");
+        return -1;
+    }
+    static_cast<EngineHandle*>(handle)->device_sampling = on != 0;
     return 0;
 }
 

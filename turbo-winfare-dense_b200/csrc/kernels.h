@@ -52,6 +52,13 @@ cudaError_t g4b_head_chunks_launch(const g4b::GemmOut& lm, int V, int M, float s
 cudaError_t g4b_head_finalize(const float2* chunk_best, int nchunks, int nranks, int M, g4b::StepParams* sp,
                               HeadResult* res, uint32_t* chain_out, unsigned* tp_seq, cudaStream_t st, bool pdl);
 
+// ---- sample.cu: sample_token (src/sampling.cpp:92-169) over a device logits row. `work` is
+// g4b_sample_workspace_bytes() of device memory, private to one stream at a time; the token is
+// written to *out (device memory, may be null) and to the workspace.
+size_t g4b_sample_workspace_bytes();
+cudaError_t g4b_sample_launch(const float* logits, int V, float temperature, float top_p, int top_k,
+                              unsigned long long seed, void* work, unsigned* out, cudaStream_t st);
+
 // ---- side.cu: INT8 G64 GEMV (one row per warp) and the attention output gate
 namespace g4b {
 cudaError_t gemv_int8_launch(const uint8_t* W, const uint16_t* S, const uint16_t* B, const float* x, float* out,

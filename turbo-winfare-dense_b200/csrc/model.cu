@@ -835,6 +835,24 @@ void DeviceModel::run_plain(int M, int base_pos, const uint32_t* tokens, bool wa
     enqueue(M, PassKind::Plain, want_logits, nullptr);
 }
 
+uint32_t DeviceModel::sample_device(int row, float temperature, float top_p, int top_k, uint64_t seed) {
+    if (opt_.tp > 1) throw std::runtime_error("device sampling needs the full vocabulary on one rank");
+    if (!sample_work_) {
+        sample_work_ = dmalloc(g4b_sample_workspace_bytes());
+        sample_out_ = static_cast<uint32_t*>(dmalloc(sizeof(uint32_t)));
+    }
+    const int V = v_local_;
+    cuda_check(g4b_sample_launch(logits_ + (size_t)row * V, V, temperature, top_p, top_k, seed, sample_work_,
+                                 sample_out_, stream_),
+               "sample");
+    launches_ += 2;
+    cuda_check(cudaMemcpyAsync(&res_host_->tokens[0], sample_out_, sizeof(uint32_t), cudaMemcpyDeviceToHost, stream_),
+               "sampled token");
+    d2h_bytes_ += sizeof(uint32_t);
+    cuda_check(cudaStreamSynchronize(stream_), "sync");
+    return res_host_->tokens[0];
+}
+
 HeadResult DeviceModel::fetch_result() {
     cuda_check(cudaMemcpyAsync(res_host_, res_dev_, sizeof(HeadResult), cudaMemcpyDeviceToHost, stream_), "result");
     d2h_bytes_ += sizeof(HeadResult);

@@ -99,6 +99,10 @@ class DeviceModel {
     void run_plain(int M, int base_pos, const uint32_t* tokens, bool want_logits);
     // Copies the result struct to host (synchronizes the stream).
     HeadResult fetch_result();
+    // Draws a token on the device from logits row `row` of the last pass that asked for logits
+    // (sample_token, src/sampling.cpp:92-169, with the given seed) and returns it (synchronizes
+    // the stream; 4 bytes come back instead of the logits row).
+    uint32_t sample_device(int row, float temperature, float top_p, int top_k, uint64_t seed);
     void check_device_error();  // throws if a kernel's bounded wait gave up
     void clear_kv();
 
@@ -168,6 +172,8 @@ class DeviceModel {
     unsigned* pcnt_ = nullptr; // prefill GEMM tile arrival counters
     float2* chunk_best_ = nullptr;
     float* logits_ = nullptr;
+    void* sample_work_ = nullptr;      // device sampler workspace (allocated on first use)
+    uint32_t* sample_out_ = nullptr;   // device: the sampled token
     HeadResult* res_dev_ = nullptr;
     StepParams* sp_dev_ = nullptr;
     uint32_t* chain_dev_ = nullptr;

@@ -256,6 +256,19 @@ int g4b_attn_gate(const float* ctx, const float* gate, float* out, int n, int ba
     return e == cudaSuccess ? 0 : fail(e, "g4b_attn_gate");
 }
 
+size_t g4b_sample_workspace(void) { return g4b_sample_workspace_bytes(); }
+
+int g4b_sample_token(const float* logits, int vocab, float temperature, float top_p, int top_k, uint64_t seed,
+                     void* workspace, uint32_t* out_token, void* stream) {
+    if (!logits || !workspace || vocab < 1 || vocab > 262144 || top_k < 0 || top_k > 256 || !(top_p > 0.f) ||
+        top_p > 1.f || !(temperature >= 0.f))
+        return fail_msg("g4b_sample_token: bad arguments (vocab 1..262144, top_k 0..256, top_p in (0, 1], "
+                        "temperature >= 0)");
+    const cudaError_t e = g4b_sample_launch(logits, vocab, temperature, top_p, top_k, seed, workspace, out_token,
+                                            static_cast<cudaStream_t>(stream));
+    return e == cudaSuccess ? 0 : fail(e, "g4b_sample_token");
+}
+
 int g4b_qmat_check_error(g4b_qmat* q) {
     if (!q) return fail_msg("g4b_qmat_check_error: null handle");
     int h = 0;

@@ -92,7 +92,8 @@ uint32_t Engine::prefill(const std::vector<uint32_t>& toks, const GenerationOpti
     }
     const HeadResult r = target_->fetch_result();
     const int row = DeviceModel::result_row(m_last);
-    if (!greedy) {
+    last_row_ = row;
+    if (!greedy && last) {
         const size_t V = target_->vocab_local();
         last->resize(V);
         cuda_check(cudaMemcpy(last->data(), target_->logits_dev() + (size_t)row * V, V * sizeof(float),
@@ -139,7 +140,8 @@ std::vector<uint32_t> Engine::generate(const std::vector<uint32_t>& prompt, cons
         draft_->reset();
         draft_->catch_up(history);
     }
-    const uint32_t first = prefill(history, opt, &logits);
+    const bool dev_sample = !greedy && !spec && opt.device_sampling && sp.repetition_penalty == 1.0f;
+    const uint32_t first = prefill(history, opt, dev_sample ? nullptr : &logits);
     if (spec) order(draft_->model().stream(), T.stream());  // decode starts after both prefills
     stats_.h2d_bytes += history.size() * sizeof(uint32_t);
     stats_.ttft_ms = now_ms() - t0;
@@ -319,7 +321,9 @@ std::vector<uint32_t> Engine::generate(const std::vector<uint32_t>& prompt, cons
             }
             const int pos = (int)history.size() - 1;
             uint32_t nx = next_greedy;
-            if (!greedy) {
+            if (dev_sample) {
+                nx = T.sample_device(last_row_, sp.temperature, sp.top_p, sp.top_k, seed_for(sp, pos));
+            } else if (!greedy) {
                 if (sp.repetition_penalty != 1.0f)
                     apply_repetition_penalty(logits.data(), V, history, sp.repetition_penalty,
                                              T.header().final_logit_softcapping);
@@ -330,6 +334,8 @@ std::vector<uint32_t> Engine::generate(const std::vector<uint32_t>& prompt, cons
             if (!emit(nx)) break;
             if (emitted >= opt.max_tokens) break;
             T.run_plain(1, (int)history.size() - 1, &nx, !greedy);
+            last_row_ = 0;
+            if (dev_sample) continue;  // the next draw reads the logits on the device
             const HeadResult r = T.fetch_result();
             next_greedy = r.argmax[0];
             if (!greedy) {

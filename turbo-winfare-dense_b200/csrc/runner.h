@@ -34,6 +34,9 @@ struct GenerationOptions {
     std::vector<uint32_t> replay;
     double mismatch_rate{0.0};
     uint64_t mismatch_seed{0};
+    // Non-speculative sampled decoding draws each token on the device (sample.cu) instead of
+    // copying the logits row to the host; a repetition penalty keeps the host path.
+    bool device_sampling{true};
 };
 
 struct GenStats {
@@ -95,6 +98,8 @@ class Engine {
     std::string telemetry_json() const;
 
    private:
+    // Runs the prompt; returns the greedy next token. last_logits (may be null) receives the
+    // last position's logits on sampled runs; last_row_ names their row on the device.
     uint32_t prefill(const std::vector<uint32_t>& tokens, const GenerationOptions& opt, std::vector<float>* last_logits);
     // Makes `to` wait for the work queued on `from` so far.
     void order(cudaStream_t from, cudaStream_t to);
@@ -103,6 +108,7 @@ class Engine {
     std::unique_ptr<DraftRuntime> draft_;
     cudaEvent_t order_ev_[2] = {nullptr, nullptr};
     int order_i_ = 0;
+    int last_row_ = 0;  // device logits row of the last pass's final position
     SpeculativeCoordinator speculator_;
     GenStats stats_;
 };

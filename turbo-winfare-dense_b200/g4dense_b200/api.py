@@ -76,6 +76,10 @@ def _bind_engine(L):
     L.g4dense_engine_forward_batch.argtypes = [_vp, _vp, ctypes.c_int, ctypes.c_int, _vp, ctypes.c_int]
     L.g4dense_engine_set_decode_options.argtypes = [_vp, ctypes.c_longlong, ctypes.c_int, _vp, ctypes.c_int,
                                                     ctypes.c_double, ctypes.c_ulonglong]
+    L.g4dense_engine_set_device_sampling.argtypes = [_vp, ctypes.c_int]
+    L.g4b_sample_workspace.restype = ctypes.c_size_t
+    L.g4b_sample_token.argtypes = [_vp, ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.c_int,
+                                   ctypes.c_uint64, _vp, _vp, _vp]
     L.g4dense_engine_last_stop_reason.argtypes = [_vp]
     L.g4dense_engine_switch_tier.argtypes = [_vp, ctypes.c_int]
     L.g4dense_engine_stop.argtypes = [_vp]
@@ -114,6 +118,18 @@ def attn_gate(ctx, gate, out, stream=None):
     """out = ctx * sigmoid(gate) over [batch][n] fp32 torch CUDA tensors (row strides honoured)."""
     _check(lib().g4b_attn_gate(_dptr(ctx), _dptr(gate), _dptr(out), ctx.shape[1], ctx.shape[0], ctx.stride(0),
                                gate.stride(0), out.stride(0), _stream(stream)), "g4b_attn_gate")
+
+
+def sample_workspace_bytes():
+    return int(lib().g4b_sample_workspace())
+
+
+def sample_token(logits, temperature, top_p, top_k, seed, workspace, out, stream=None):
+    """Draws a token from the fp32 logits row (torch CUDA tensor) into out (uint32/int32 CUDA
+    tensor of one element) as the reference's sample_token does; workspace is a CUDA byte tensor
+    of sample_workspace_bytes()."""
+    _check(lib().g4b_sample_token(_dptr(logits), logits.numel(), temperature, top_p, top_k, seed & (2**64 - 1),
+                                  _dptr(workspace), _dptr(out), _stream(stream)), "g4b_sample_token")
 
 
 class QMat:
@@ -223,6 +239,10 @@ class Engine:
                                                    None if r is None else r.ctypes.data_as(_vp),
                                                    0 if r is None else len(r), mismatch_rate, mismatch_seed):
             _eng_err("g4dense_engine_set_decode_options")
+
+    def set_device_sampling(self, on):
+        if lib().g4dense_engine_set_device_sampling(self.h, 1 if on else 0):
+            _eng_err("g4dense_engine_set_device_sampling")
 
     def generate(self, prompt, max_tokens, temperature=0.0, top_p=1.0, top_k=0, seed=None, callback=None):
         o = GenOptions()
