@@ -276,6 +276,8 @@ def run_b200(args, rank, world):
     }
     if clocks:
         line["clocks"] = clocks
+    if world == 1:
+        line["mtp_drafter"] = mtp_drafter(eng, prompt, stream, args)
     long_ctx = args.long_context and world == 1  # (a second TP engine would need its own NCCL id)
     if long_ctx:
         eng.close()
@@ -319,6 +321,32 @@ def long_context(args, eng_factory, world):
     out["verify_pass_ms_at_30000"] = eng.time_pass(0, 9, 3, pos=30000)
     eng.close()
     return out
+
+
+def mtp_drafter(eng, prompt, stream, args):
+    """The same config-3 rounds with the MTP assistant drafter (src/mtp_runner.cpp; a synthetic
+    drafter of the 31B assistant's geometry: 4 layers, hidden 1024, attending the target's last
+    sliding and full-attention layers) in place of the E2B-shaped one. Same oracle drafter and
+    mismatch rate, so only the drafting cost differs."""
+    eng.close()
+    m = Engine(preset="gemma4-31b", seed=0, draft_preset="gemma4-31b-assistant", draft_seed=2,
+               draft_k=VERIFY_WIDTH, max_context=4096)
+    m.set_gate(0.45, -1)
+    m.set_decode_options(draft_k=VERIFY_WIDTH, replay=stream, mismatch_rate=MISMATCH, mismatch_seed=7)
+    ok = []
+    for _ in range(max(1, args.warmup)):
+        m.generate(prompt, GEN_LEN)
+    ms = tok = 0.0
+    for _ in range(2):
+        toks = m.generate(prompt, GEN_LEN)
+        ok.append(toks.tolist() == stream.tolist())
+        s = m.stats()
+        ms += s["decode_gpu_ms"]
+        tok += s["emitted"] - 1
+    step_ms = m.time_pass(2, 1, reps=20, pos=PROMPT_LEN + GEN_LEN)
+    m.close()
+    return {"tok_s": tok / (ms / 1000.0), "step_ms": step_ms, "spec_stream_equals_greedy": all(ok),
+            "workload": "config-3 rounds (k=4, mismatch 0.25) with the MTP assistant drafter instead of E2B"}
 
 
 def main():

@@ -120,6 +120,14 @@ G4DENSE_API int g4dense_engine_set_decode_options(void* handle, long long stop_t
  * the device by default, as sample_token does on the host (src/sampling.cpp:92-169); on = 0
  * selects the host draw over a copied logits row. Additive; returns 0 or -1. */
 G4DENSE_API int g4dense_engine_set_device_sampling(void* handle, int on);
+/* MtpRunner::generate_draft_tokens (src/mtp_runner.cpp:263-843) with greedy drafting, for an
+ * engine whose drafter is an MTP assistant (.g4mtp): k draft tokens from seed_token at position
+ * context_length - 1, starting from row hidden_row of the target's final normed hidden states of
+ * its last pass (the last prompt position after a prefill chunk of more than 16 rows is row 0;
+ * after a pass of M <= 16 rows, row M - 1). out_logits (host, may be NULL) receives [k][vocab].
+ * Additive; returns 0 or -1. */
+G4DENSE_API int g4dense_engine_mtp_draft(void* handle, unsigned int seed_token, int context_length, int hidden_row,
+                                         int k, unsigned int* out_tokens, float* out_logits);
 /* Per-round (drafted, accepted, emitted) triples of the last speculative generation. */
 G4DENSE_API int g4dense_engine_last_rounds(void* handle, int* out, int cap_triples);
 G4DENSE_API int g4dense_nccl_unique_id(void* out128);
@@ -134,7 +142,9 @@ G4DENSE_API int g4dense_engine_set_gate(void* handle, double min_accept, int win
 /* Device time (CUDA events) of one forward pass of `batch` rows at positions pos..pos+batch-1
  * on the target (which = 0) or the drafter (which = 1), averaged over `reps` back-to-back graph
  * replays; attention spans the pos earlier cache entries. batch 1..16 times a verify pass,
- * 17..128 a tensor-core prefill chunk. Overwrites those rows of the KV cache. -1 on error. */
+ * 17..128 a tensor-core prefill chunk. Overwrites those rows of the KV cache. which = 2 times one
+ * step of an MTP drafter (batch 1) whose query attends the target's pos cached positions. -1 on
+ * error. */
 G4DENSE_API double g4dense_engine_time_pass(void* handle, int which, int batch, int pos, int reps);
 /* Times every verify GEMM of one `batch`-row target pass, `reps` passes back to back, with
  * CUDA events; returns ms per pass (-1 on error), the pass's algorithmic GEMM bytes and the

@@ -543,6 +543,226 @@ int g4o_forward(g4o_model* m, uint32_t token, uint32_t pos, float* logits, float
     return 0;
 }
 
+/* ------------------------------------------------------------------ MTP assistant drafter */
+
+/* G4MtpHeader, include/g4dense/format.hpp:143-180 (packed, 4096 bytes). */
+#pragma pack(push, 1)
+typedef struct {
+    uint32_t magic, version, quant_type, num_layers, backbone_hidden_size, hidden_size, intermediate_size,
+        vocab_size, num_q_heads, num_kv_heads, head_dim, global_head_dim, global_kv_heads, sliding_window;
+    uint64_t global_layer_mask;
+    uint32_t quant_group_size, scale_dtype;
+    uint64_t embed_offset, embed_size, pre_proj_offset, pre_proj_size, post_proj_offset, post_proj_size,
+        norm_offset, norm_size;
+    uint64_t layer_offsets[8], layer_sizes[8];
+    uint8_t payload_sha256[32];
+    uint8_t reserved[3800];
+} g4o_mtp_header;
+#pragma pack(pop)
+
+typedef struct {
+    uint32_t is_global, qhd;
+    const uint16_t *in_norm, *post_attn_norm, *pre_ffn_norm, *post_ffn_norm, *q_norm;
+    float layer_scalar;
+    qmat q, o, gate, up, down;
+} mtp_layer;
+
+struct g4o_mtp {
+    g4o_mtp_header h;
+    const uint8_t* base;
+    size_t size;
+    qmat embed, pre, post;
+    const uint16_t* norm;
+    mtp_layer* layers;
+};
+
+/* MtpRunner::load_model + compute_layer_offsets, src/mtp_runner.cpp:92-234, with
+ * validate_mtp_header's checks (src/format.cpp:67-130). */
+g4o_mtp* g4o_mtp_open(const char* path) {
+    int fd = open(path, O_RDONLY);
+    if (fd < 0) { set_err("g4o_mtp_open: cannot open container"); return NULL; }
+    struct stat st;
+    if (fstat(fd, &st) != 0 || (size_t)st.st_size < sizeof(g4o_mtp_header)) {
+        close(fd);
+        set_err("g4o_mtp_open: container too small for header");
+        return NULL;
+    }
+    void* p = mmap(NULL, (size_t)st.st_size, PROT_READ, MAP_PRIVATE, fd, 0);
+    close(fd);
+    if (p == MAP_FAILED) { set_err("g4o_mtp_open: mmap failed"); return NULL; }
+    g4o_mtp* m = (g4o_mtp*)calloc(1, sizeof(g4o_mtp));
+    m->base = (const uint8_t*)p;
+    m->size = (size_t)st.st_size;
+    memcpy(&m->h, p, sizeof(g4o_mtp_header));
+    const g4o_mtp_header* h = &m->h;
+    int bad = h->magic != 0x47344D54u || h->version != 1 || h->num_layers == 0 || h->num_layers > 8 ||
+              !h->backbone_hidden_size || !h->hidden_size || !h->intermediate_size || !h->vocab_size ||
+              h->embed_offset % 4096 || h->pre_proj_offset % 4096 || h->post_proj_offset % 4096 ||
+              h->norm_offset % 4096;
+    for (uint32_t l = 0; !bad && l < h->num_layers; ++l)
+        bad = h->layer_offsets[l] % 4096 || !h->layer_sizes[l] || h->layer_offsets[l] + h->layer_sizes[l] > m->size;
+    if (bad) {
+        set_err("g4o_mtp_open: invalid header");
+        munmap(p, m->size);
+        free(m);
+        return NULL;
+    }
+    const uint32_t hs = h->hidden_size, bb = h->backbone_hidden_size, I = h->intermediate_size;
+    parse_qmat(m->base + h->embed_offset, m->base + h->embed_offset, h->vocab_size, hs, &m->embed);
+    parse_qmat(m->base + h->pre_proj_offset, m->base + h->pre_proj_offset, hs, 2 * bb, &m->pre);
+    parse_qmat(m->base + h->post_proj_offset, m->base + h->post_proj_offset, bb, hs, &m->post);
+    m->norm = (const uint16_t*)(m->base + h->norm_offset);
+    m->layers = (mtp_layer*)calloc(h->num_layers, sizeof(mtp_layer));
+    for (uint32_t l = 0; l < h->num_layers; ++l) {
+        mtp_layer* L = &m->layers[l];
+        const uint8_t* lp = m->base + h->layer_offsets[l];
+        L->is_global = (uint32_t)((h->global_layer_mask >> l) & 1ull);
+        L->qhd = L->is_global ? h->global_head_dim : h->head_dim;
+        const uint32_t qd = h->num_q_heads * L->qhd;
+        L->in_norm = (const uint16_t*)lp;
+        L->post_attn_norm = (const uint16_t*)(lp + hs * 2);
+        L->pre_ffn_norm = (const uint16_t*)(lp + hs * 4);
+        L->post_ffn_norm = (const uint16_t*)(lp + hs * 6);
+        L->q_norm = (const uint16_t*)(lp + hs * 8);
+        const uint8_t* sc = lp + hs * 8 + L->qhd * 2;
+        L->layer_scalar = g4o_bf16_to_f32(*(const uint16_t*)sc);
+        const uint8_t* q = sc + 2;
+        q = parse_qmat(lp, q, qd, hs, &L->q);
+        q = parse_qmat(lp, q, hs, qd, &L->o);
+        q = parse_qmat(lp, q, I, hs, &L->gate);
+        q = parse_qmat(lp, q, I, hs, &L->up);
+        parse_qmat(lp, q, hs, I, &L->down);
+    }
+    return m;
+}
+
+void g4o_mtp_close(g4o_mtp* m) {
+    if (!m) return;
+    free(m->layers);
+    munmap((void*)m->base, m->size);
+    free(m);
+}
+
+void g4o_mtp_info(const g4o_mtp* m, uint32_t* o) {
+    const g4o_mtp_header* h = &m->h;
+    o[0] = h->num_layers; o[1] = h->backbone_hidden_size; o[2] = h->hidden_size; o[3] = h->intermediate_size;
+    o[4] = h->vocab_size; o[5] = h->num_q_heads; o[6] = h->num_kv_heads; o[7] = h->head_dim;
+    o[8] = h->global_head_dim; o[9] = h->global_kv_heads; o[10] = h->sliding_window;
+    o[11] = (uint32_t)h->global_layer_mask;
+}
+
+/* MtpRunner::generate_draft_tokens, src/mtp_runner.cpp:263-843. Per step: x = [e(t); h] with
+ * e(t) the target's scaled token embedding (src/runner.cpp:2359-2380) and h the target's final
+ * normed hidden state (step 0) or the previous step's post-projection; hidden = W_pre x; the
+ * layers (q-only attention over the target's KV of its last sliding / last full-attention
+ * layer); final norm; post-projection (the next step's h) and the tied LM head (no softcap); the
+ * token drawn with sample_token and seed splitmix64(seed + step) (or 1337 + step).
+ *
+ * Two deliberate differences from the reference, both about positions:
+ *   - the reference attends [first, context_length), which includes the pending token's own
+ *     position; the target has not processed that token yet, so the slot holds the KV of a
+ *     rejected draft or of no token at all. Here the query at position context_length - 1 sees
+ *     the keys the target has processed, [max(0, context_length - 1 - window), context_length - 1)
+ *     on sliding layers and [0, context_length - 1) on full-attention layers;
+ *   - the donor layers, window, RoPE bases and rotated pairs are the target's own (its last
+ *     sliding and last full-attention layer; the reference hard-codes 58/59, 1024, 1e4/1e6 and
+ *     128/64 pairs, which are the 31B's values).
+ * Like the reference, every step uses the same query position and key range. */
+int g4o_mtp_draft(const g4o_mtp* mtp, const g4o_model* tgt, const float* target_hidden, uint32_t seed_token,
+                  uint32_t context_length, uint32_t k, const g4o_sampling* sp, uint32_t* out_tokens,
+                  float* out_logits) {
+    const g4o_mtp_header* h = &mtp->h;
+    const g4o_header* th = &tgt->h;
+    const uint32_t hs = h->hidden_size, bb = h->backbone_hidden_size, I = h->intermediate_size, V = h->vocab_size;
+    if (bb != th->d_model || V != th->vocab_size) { set_err("g4o_mtp_draft: drafter does not match the target"); return -1; }
+    if (context_length < 2 || context_length - 1 > tgt->len) { set_err("g4o_mtp_draft: bad context length"); return -1; }
+    int donor_local = -1, donor_global = -1;
+    for (uint32_t l = 0; l < th->num_layers; ++l) {
+        if ((th->global_layer_mask >> l) & 1ull) donor_global = (int)l;
+        else donor_local = (int)l;
+    }
+    float* x = (float*)malloc(sizeof(float) * 2 * bb);
+    float* hidden = (float*)malloc(sizeof(float) * hs);
+    float* norm = (float*)malloc(sizeof(float) * hs);
+    float* proj = (float*)malloc(sizeof(float) * hs);
+    float* wn = (float*)malloc(sizeof(float) * (hs > 512 ? hs : 512));
+    float* gbuf = (float*)malloc(sizeof(float) * I);
+    float* ubuf = (float*)malloc(sizeof(float) * I);
+    float* post = (float*)malloc(sizeof(float) * bb);
+    float* logits = (float*)malloc(sizeof(float) * V);
+    const float es = sqrtf((float)bb);
+    const uint32_t qpos = context_length - 1, kend = context_length - 1;
+    uint32_t tok = seed_token;
+    int rc = 0;
+    memcpy(post, target_hidden, sizeof(float) * bb);
+    for (uint32_t step = 0; step < k; ++step) {
+        if (tok >= V) tok %= V;
+        dequant_int4(tgt->embed.w + (size_t)tok * (bb / 8), tgt->embed.s + (size_t)tok * (bb / 64),
+                     tgt->embed.b + (size_t)tok * (bb / 64), 1, bb, x);
+        for (uint32_t i = 0; i < bb; ++i) x[i] *= es;
+        memcpy(x + bb, post, sizeof(float) * bb);
+        qgemv(&mtp->pre, x, hidden);
+        for (uint32_t l = 0; l < h->num_layers; ++l) {
+            const mtp_layer* L = &mtp->layers[l];
+            const int dl = L->is_global ? donor_global : donor_local;
+            if (dl < 0) { set_err("g4o_mtp_draft: target has no donor layer of this kind"); rc = -1; break; }
+            const layer_t* D = &tgt->layers[dl];
+            const uint32_t qhd = L->qhd, qd = h->num_q_heads * qhd;
+            if (D->hd != qhd || D->kvh != (L->is_global ? h->global_kv_heads : h->num_kv_heads)) {
+                set_err("g4o_mtp_draft: attention geometry differs from the donor layer");
+                rc = -1;
+                break;
+            }
+            float* qb = (float*)malloc(sizeof(float) * qd);
+            float* head_out = (float*)calloc(qd, sizeof(float));
+            float* qn = (float*)malloc(sizeof(float) * qhd);
+            bf16_vec(L->in_norm, hs, wn);
+            rms_norm_f(hidden, wn, hs, 1e-6f, norm);
+            qgemv(&L->q, norm, qb);
+            bf16_vec(L->q_norm, qhd, qn);
+            const float theta = L->is_global ? th->rope_theta_global : th->rope_theta_local;
+            const uint32_t rotated = L->is_global ? 64u : qhd / 2;
+            const uint32_t first = L->is_global ? 0 : (kend > th->sliding_window ? kend - th->sliding_window : 0);
+            float* scores = (float*)malloc(sizeof(float) * (kend - first + 1));
+            const uint32_t gqa = h->num_q_heads / D->kvh;
+            for (uint32_t hh = 0; hh < h->num_q_heads; ++hh) {
+                float* qv = qb + (size_t)hh * qhd;
+                rms_norm_f(qv, qn, qhd, 1e-6f, qv);
+                rope(qv, qhd, rotated, theta, qpos);
+                if (kend > first)
+                    attend_row(qv, D->kcache, D->vcache, D->kvh, hh / gqa, qhd, first, kend, 1.0f, scores,
+                               head_out + (size_t)hh * qhd);
+            }
+            free(scores);
+            qgemv(&L->o, head_out, proj);
+            bf16_vec(L->post_attn_norm, hs, wn);
+            rms_norm_f(proj, wn, hs, 1e-6f, proj);
+            for (uint32_t i = 0; i < hs; ++i) hidden[i] += proj[i];
+            bf16_vec(L->pre_ffn_norm, hs, wn);
+            rms_norm_f(hidden, wn, hs, 1e-6f, norm);
+            qgemv(&L->gate, norm, gbuf);
+            qgemv(&L->up, norm, ubuf);
+            for (uint32_t i = 0; i < I; ++i) gbuf[i] = g4o_gelu_tanh(gbuf[i]) * ubuf[i];
+            qgemv(&L->down, gbuf, proj);
+            bf16_vec(L->post_ffn_norm, hs, wn);
+            rms_norm_f(proj, wn, hs, 1e-6f, proj);
+            for (uint32_t i = 0; i < hs; ++i) hidden[i] = (hidden[i] + proj[i]) * L->layer_scalar;
+            free(qb); free(head_out); free(qn);
+        }
+        if (rc) break;
+        bf16_vec(mtp->norm, hs, wn);
+        rms_norm_f(hidden, wn, hs, 1e-6f, norm);
+        qgemv(&mtp->post, norm, post);
+        qgemv(&mtp->embed, norm, logits);
+        const uint64_t step_seed = g4o_splitmix64(sp->has_seed ? sp->seed + step : 1337u + step);
+        tok = g4o_sample_token(logits, V, sp, step_seed);
+        out_tokens[step] = tok;
+        if (out_logits) memcpy(out_logits + (size_t)step * V, logits, sizeof(float) * V);
+    }
+    free(x); free(hidden); free(norm); free(proj); free(wn); free(gbuf); free(ubuf); free(post); free(logits);
+    return rc;
+}
+
 /* ------------------------------------------------------------------ sampling */
 
 /* src/sampling.cpp:256-261 */

@@ -66,6 +66,20 @@ void g4o_attention(const float* q, const float* K, const float* V, uint32_t M, u
                    uint32_t kvh, uint32_t hd, uint32_t n_pos, uint32_t window, float scale,
                    float* out);
 
+/* ---- MTP "assistant" drafter (.g4mtp v1; src/mtp_runner.cpp) ---- */
+typedef struct g4o_mtp g4o_mtp;
+g4o_mtp* g4o_mtp_open(const char* path);
+void g4o_mtp_close(g4o_mtp* m);
+/* out[0..11] = num_layers, backbone, hidden, intermediate, vocab, q_heads, kv_heads, head_dim,
+ *              global_head_dim, global_kv_heads, sliding_window, global mask (low 32 bits) */
+void g4o_mtp_info(const g4o_mtp* m, uint32_t* out);
+/* k draft tokens (and, if out_logits is non-null, their [k][vocab] logits) from the target's
+ * final normed hidden state, the token at position context_length - 1 and the target's KV of
+ * positions below it. The target must hold at least context_length - 1 positions. */
+int g4o_mtp_draft(const g4o_mtp* mtp, const g4o_model* target, const float* target_hidden, uint32_t seed_token,
+                  uint32_t context_length, uint32_t k, const g4o_sampling* sp, uint32_t* out_tokens,
+                  float* out_logits);
+
 /* ---- sampling / acceptance (src/sampling.cpp, src/speculator.cpp) ---- */
 uint64_t g4o_splitmix64(uint64_t x);
 uint64_t g4o_seed_for(const g4o_sampling* p, int position);

@@ -97,6 +97,12 @@ def restated_lib():
                                           ctypes.POINTER(Sampling), ctypes.c_double, ctypes.c_int,
                                           ctypes.c_int64, _vp, ctypes.c_int, ctypes.c_double,
                                           ctypes.c_uint64, _vp, _vp, ctypes.c_int, _vp]
+        lib.g4o_mtp_open.restype = _vp
+        lib.g4o_mtp_open.argtypes = [ctypes.c_char_p]
+        lib.g4o_mtp_close.argtypes = [_vp]
+        lib.g4o_mtp_info.argtypes = [_vp, _vp]
+        lib.g4o_mtp_draft.argtypes = [_vp, _vp, _vp, ctypes.c_uint32, ctypes.c_uint32, ctypes.c_uint32,
+                                      ctypes.POINTER(Sampling), _vp, _vp]
         _restated = lib
     return _restated
 
@@ -142,6 +148,41 @@ class RestatedModel:
         if self.lib.g4o_forward(self.h, token, pos, _ptr(logits), _ptr(hidden)):
             raise RuntimeError(self.lib.g4o_last_error().decode())
         return (logits, hidden) if want_hidden else logits
+
+
+class RestatedMtp:
+    """Our C restatement of MtpRunner (src/mtp_runner.cpp) over a RestatedModel target."""
+
+    def __init__(self, path):
+        self.lib = restated_lib()
+        self.h = self.lib.g4o_mtp_open(str(path).encode())
+        if not self.h:
+            raise RuntimeError(self.lib.g4o_last_error().decode())
+        info = np.zeros(12, np.uint32)
+        self.lib.g4o_mtp_info(self.h, _ptr(info))
+        self.vocab = int(info[4])
+
+    def close(self):
+        if self.h:
+            self.lib.g4o_mtp_close(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def draft(self, target: RestatedModel, hidden, seed_token, context_length, k, sampling: Sampling | None = None):
+        """(tokens [k], logits [k][vocab]) drafted from the target's state."""
+        sp = sampling or Sampling.greedy()
+        toks = np.zeros(k, np.uint32)
+        logits = np.zeros((k, self.vocab), np.float32)
+        hid = np.ascontiguousarray(hidden, np.float32)
+        if self.lib.g4o_mtp_draft(self.h, target.h, _ptr(hid), seed_token, context_length, k, ctypes.byref(sp),
+                                  _ptr(toks), _ptr(logits)):
+            raise RuntimeError(self.lib.g4o_last_error().decode())
+        return toks, logits
 
 
 def spec_generate(target: RestatedModel, draft: RestatedModel | None, prompt, max_tokens,

@@ -3,6 +3,7 @@
 #include "g4dense/c_api.h"
 
 #include <atomic>
+#include <cstdio>
 #include <cstdlib>
 #include <cstring>
 #include <memory>
@@ -44,6 +45,33 @@ struct EngineHandle {
 #endif
     }
 };
+
+// MTP drafter geometries: the 31B's assistant (tools/convert_hf_assistant.py:49-66 defaults) and
+// "mtp-small", a 4-layer drafter sized for tests, with attention geometry taken from `t`.
+bool mtp_preset_header(const std::string& name, const g4b::G4DenseHeader& t, g4b::G4MtpHeader& m) {
+    std::memset(&m, 0, sizeof(m));
+    m.num_layers = 4;
+    m.backbone_hidden_size = t.d_model;
+    m.vocab_size = t.vocab_size;
+    m.num_kv_heads = t.num_kv_heads;
+    m.head_dim = t.head_dim;
+    m.global_head_dim = t.global_head_dim ? t.global_head_dim : 512;
+    m.global_kv_heads = t.global_kv_heads ? t.global_kv_heads : 4;
+    m.sliding_window = t.sliding_window;
+    m.global_layer_mask = 1ull << 3;  // sliding x3, then full attention
+    if (name == "gemma4-31b-assistant") {
+        m.hidden_size = 1024;
+        m.intermediate_size = 8192;
+        m.num_q_heads = 32;
+    } else if (name == "mtp-small") {
+        m.hidden_size = 128;
+        m.intermediate_size = 512;
+        m.num_q_heads = t.num_q_heads;
+    } else {
+        return false;
+    }
+    return true;
+}
 
 // Model geometries for device-generated weights, with an optional ":layers=N" override.
 bool preset_header(const std::string& spec, g4b::G4DenseHeader& h) {
@@ -200,7 +228,40 @@ G4DENSE_API void* g4dense_engine_create_ex(const G4DenseEngineConfig* cfg) {
         }
         const cudaStream_t st = target->stream();
         h->engine = std::make_unique<g4b::Engine>(std::move(target));
-        if ((cfg->draft_path && *cfg->draft_path) || cfg->draft_preset) {
+        bool mtp = false;
+        if (cfg->draft_path && *cfg->draft_path) {
+            if (FILE* f = std::fopen(cfg->draft_path, "rb")) {
+                uint32_t magic = 0;
+                if (std::fread(&magic, 4, 1, f) == 1) mtp = magic == g4b::G4MtpHeader::kMagic;
+                std::fclose(f);
+            }
+        } else if (cfg->draft_preset) {
+            mtp = std::strncmp(cfg->draft_preset, "mtp-", 4) == 0 ||
+                  std::strcmp(cfg->draft_preset, "gemma4-31b-assistant") == 0;
+        }
+        if (mtp) {
+            // The MTP assistant drafter (src/mtp_runner.cpp) reads the target's KV rings, embedding
+            // and final hidden states, so it shares the target's device and stream.
+            if (mo.tp != 1) throw std::invalid_argument("the MTP drafter runs without tensor parallelism");
+            g4b::DeviceModel& T = h->engine->target();
+            T.enable_hidden_out();
+            g4b::ModelOptions dopt;
+            dopt.max_context = mo.max_context;
+            dopt.kv_bf16 = mo.kv_bf16;
+            dopt.use_graphs = mo.use_graphs;
+            dopt.prefill_tc = false;
+            dopt.stream = st;
+            auto d = std::make_unique<g4b::DeviceModel>(dopt);
+            if (cfg->draft_path && *cfg->draft_path) {
+                d->load_mtp(cfg->draft_path, T);
+            } else {
+                g4b::G4MtpHeader mh;
+                if (!mtp_preset_header(cfg->draft_preset, T.header(), mh))
+                    throw std::invalid_argument("unknown MTP drafter preset");
+                d->load_mtp_synthetic(mh, cfg->draft_seed, cfg->synthetic_centered != 0, T);
+            }
+            h->engine->set_mtp(std::move(d));
+        } else if ((cfg->draft_path && *cfg->draft_path) || cfg->draft_preset) {
             // The drafter stays whole on every rank (it is small) and runs on its own stream, so
             // its prompt catch-up overlaps the target's prefill; the engine orders the two
             // streams with events where a round's passes depend on each other.
@@ -339,6 +400,43 @@ G4DENSE_API int g4dense_engine_forward_batch(void* handle, const unsigned int* t
     }
 }
 
+G4DENSE_API int g4dense_engine_mtp_draft(void* handle, unsigned int seed_token, int context_length, int hidden_row,
+                                         int k, unsigned int* out_tokens, float* out_logits) {
+    clear_error();
+    if (!handle || context_length < 2 || hidden_row < 0 || k < 1 || !out_tokens) {
+        set_error("Invalid arguments");
+        return -1;
+    }
+    try {
+        g4b::Engine& E = *static_cast<EngineHandle*>(handle)->engine;
+        g4b::DeviceModel* Mt = E.mtp();
+        if (!Mt) throw std::invalid_argument("no MTP drafter loaded");
+        if (hidden_row >= E.target().max_rows()) throw std::invalid_argument("hidden_row out of range");
+        const int V = (int)Mt->header().vocab_size;
+        uint32_t tok = seed_token;
+        for (int s = 0; s < k; ++s) {
+            g4b::StepParams p{};
+            p.base_pos = context_length - 2;
+            p.tokens[0] = tok;
+            p.aux = hidden_row;
+            Mt->push_params(1, p, 1);
+            Mt->enqueue(1, s == 0 ? g4b::PassKind::MtpFirst : g4b::PassKind::MtpNext, out_logits != nullptr, nullptr);
+            const HeadResult r = Mt->fetch_result();
+            tok = r.argmax[0];
+            out_tokens[s] = tok;
+            if (out_logits)
+                g4b::cuda_check(cudaMemcpy(out_logits + (size_t)s * V, Mt->logits_dev(), (size_t)V * 4,
+                                           cudaMemcpyDeviceToHost),
+                                "logits");
+        }
+        Mt->check_device_error();
+        return 0;
+    } catch (const std::exception& e) {
+        set_error(e.what());
+        return -1;
+    }
+}
+
 G4DENSE_API int g4dense_engine_set_decode_options(void* handle, long long stop_token, int draft_k,
                                                   const unsigned int* replay, int replay_len, double mismatch_rate,
                                                   unsigned long long mismatch_seed) {
@@ -444,6 +542,31 @@ G4DENSE_API double g4dense_engine_time_pass(void* handle, int which, int batch, 
     }
     try {
         auto* e = static_cast<EngineHandle*>(handle);
+        if (which == 2) {  // one MTP drafter step (batch 1) with the target's KV up to pos
+            g4b::DeviceModel* m = e->engine->mtp();
+            if (!m) throw std::invalid_argument("no MTP drafter loaded");
+            if (batch != 1 || pos < 1 || pos + 1 > e->engine->target().max_context())
+                throw std::invalid_argument("an MTP step is one row at a position inside the target's KV");
+            g4b::StepParams p{};
+            p.base_pos = pos - 1;
+            p.tokens[0] = 1;
+            m->push_params(1, p, 1);
+            m->enqueue(1, g4b::PassKind::MtpFirst, false, nullptr);  // warm (captures the graphs)
+            m->enqueue(1, g4b::PassKind::MtpNext, false, nullptr);
+            cudaEvent_t a, b;
+            g4b::cuda_check(cudaEventCreate(&a), "event");
+            g4b::cuda_check(cudaEventCreate(&b), "event");
+            g4b::cuda_check(cudaEventRecord(a, m->stream()), "event");
+            for (int r = 0; r < reps; ++r)
+                m->enqueue(1, r == 0 ? g4b::PassKind::MtpFirst : g4b::PassKind::MtpNext, false, nullptr);
+            g4b::cuda_check(cudaEventRecord(b, m->stream()), "event");
+            g4b::cuda_check(cudaEventSynchronize(b), "event");
+            float ms = 0.f;
+            cudaEventElapsedTime(&ms, a, b);
+            cudaEventDestroy(a);
+            cudaEventDestroy(b);
+            return (double)ms / reps;
+        }
         g4b::DeviceModel* m = which == 0 ? &e->engine->target()
                                          : (e->engine->draft() ? &e->engine->draft()->model() : nullptr);
         if (!m) throw std::invalid_argument("no drafter loaded");

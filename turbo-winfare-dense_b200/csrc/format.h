@@ -61,4 +61,30 @@ inline uint32_t layer_ffn_width(const G4DenseHeader& h, uint32_t l) {
 // checks this engine needs to run the model (Gemma-4 architecture, INT4 G64, no PLE).
 void validate_header(const G4DenseHeader& h, uint64_t file_size);
 
+// The .g4mtp v1 container of the MTP "assistant" drafter: G4MtpHeader of
+// include/g4dense/format.hpp:143-180 (packed, 4096 bytes).
+#pragma pack(push, 1)
+struct G4MtpHeader {
+    static constexpr uint32_t kMagic = 0x47344D54;  // 'G4MT'
+    static constexpr uint32_t kVersion = 1;
+    static constexpr uint64_t kAlign = 4096;
+    static constexpr uint32_t kMaxLayers = 8;
+
+    uint32_t magic, version, quant_type, num_layers, backbone_hidden_size, hidden_size, intermediate_size,
+        vocab_size, num_q_heads, num_kv_heads, head_dim, global_head_dim, global_kv_heads, sliding_window;
+    uint64_t global_layer_mask;
+    uint32_t quant_group_size, scale_dtype;
+    uint64_t embed_offset, embed_size, pre_proj_offset, pre_proj_size, post_proj_offset, post_proj_size,
+        norm_offset, norm_size;
+    uint64_t layer_offsets[8];
+    uint64_t layer_sizes[8];
+    uint8_t payload_sha256[32];
+    uint8_t reserved[3800];
+};
+#pragma pack(pop)
+static_assert(sizeof(G4MtpHeader) == 4096, "G4MtpHeader must be 4096 bytes");
+
+// validate_mtp_header (src/format.cpp:67-130), with the reference's messages.
+void validate_mtp_header(const G4MtpHeader& h, uint64_t file_size);
+
 }  // namespace g4b

@@ -88,7 +88,7 @@ __global__ void head_chunks_kernel(GemmOut lm, int V, int M, float softcap, floa
 // chunk_best is [nranks][M][nchunks] (one slice per tensor-parallel rank's vocabulary range);
 // the order is total (value, then lowest index), so the result does not depend on the split.
 __global__ void head_finalize_kernel(const float2* chunk_best, int nchunks, int nranks, int M, StepParams* sp,
-                                     HeadResult* res, uint32_t* chain_out, unsigned* tp_seq) {
+                                     HeadResult* res, uint32_t* chain_out, unsigned* tp_seq, int advance_pos) {
     __shared__ uint32_t am[16];
     pdl_enter();
     const int lane = threadIdx.x & 31, m = threadIdx.x >> 5;
@@ -122,7 +122,7 @@ __global__ void head_finalize_kernel(const float2* chunk_best, int nchunks, int 
             chain_out[sp->draft_step] = t;
             sp->draft_step += 1;
             sp->tokens[0] = t;
-            sp->base_pos += M;
+            if (advance_pos) sp->base_pos += M;  // the MTP drafter keeps its position
         }
         if (tp_seq) *tp_seq += 1;  // the pass is complete on this rank
     }
@@ -143,7 +143,8 @@ cudaError_t g4b_head_chunks_launch(const GemmOut& lm, int V, int M, float softca
 }
 
 cudaError_t g4b_head_finalize(const float2* chunk_best, int nchunks, int nranks, int M, StepParams* sp,
-                              HeadResult* res, uint32_t* chain_out, unsigned* tp_seq, cudaStream_t st, bool pdl) {
+                              HeadResult* res, uint32_t* chain_out, unsigned* tp_seq, cudaStream_t st, bool pdl,
+                              bool advance_pos) {
     return launch(head_finalize_kernel, dim3(1), dim3(32 * 16), 0, st, pdl, chunk_best, nchunks, nranks, M, sp, res,
-                  chain_out, tp_seq);
+                  chain_out, tp_seq, advance_pos ? 1 : 0);
 }

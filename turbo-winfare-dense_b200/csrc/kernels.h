@@ -17,15 +17,22 @@ cudaError_t g4b_embed_norm(const g4b::StepParams* sp, const uint32_t* ew, const 
                            int V, int d, const uint16_t* w_in, float* h_out, void* bfrag, int M, cudaStream_t st,
                            bool pdl);
 cudaError_t g4b_qkv_epi(const g4b::QkvEpiArgs& a, cudaStream_t st, bool pdl);
+// MTP drafter step input [e(t) * sqrt(bb); h] -> B fragments (one row, K = 2 * bb); h from
+// hidden[sp->aux] when hidden is set, else from the previous post-projection's output `post`.
+cudaError_t g4b_mtp_input(const g4b::StepParams* sp, const uint32_t* ew, const uint16_t* es, const uint16_t* eb,
+                          int V, int bb, const float* hidden, const g4b::GemmOut& post, void* bfrag, cudaStream_t st,
+                          bool pdl);
 cudaError_t g4b_geglu(const g4b::GemmOut& gu, int F, void* bfrag, int M, cudaStream_t st, bool pdl);
 // Norm/residual epilogue (post-attention with out_scale = 1, post-FFN with the layer scalar):
 // h_out = (h_in + rmsnorm(o)*w1) * out_scale; x = rmsnorm(h_out)*w2 -> B fragments.
 // Under tensor parallelism (tg.n > 1) y is the rank-ordered sum of every rank's dense partial
-// (TpGather); otherwise o's slots or dense matrix.
+// (TpGather); otherwise o's slots or dense matrix. w1 == nullptr adds o unnormalised and h_in ==
+// nullptr starts from zero (h_out = o: a projection's output becoming the residual stream).
+// x_out (optional) also receives x in fp32, [M - frag_row0][d].
 cudaError_t g4b_rowepi(const g4b::GemmOut& o, const g4b::TpGather& tg, const float* h_in, float* h_out,
                        const uint16_t* w1, float out_scale, const uint16_t* w2, int d, void* bfrag, int M,
                        cudaStream_t st, bool pdl,
-                       int frag_row0 = 0);
+                       int frag_row0 = 0, float* x_out = nullptr);
 
 // ---- attention.cu
 // Attention of M rows over the KV ring; writes the output [M][qh*hd] as the o-projection's
@@ -50,7 +57,8 @@ cudaError_t g4b_head_chunks_launch(const g4b::GemmOut& lm, int V, int M, float s
 // chunk_best holds nranks slices [M][nchunks] (tensor-parallel vocabulary ranges).
 // tp_seq (tensor parallelism, else nullptr) counts completed passes for the peer-memory sums.
 cudaError_t g4b_head_finalize(const float2* chunk_best, int nchunks, int nranks, int M, g4b::StepParams* sp,
-                              HeadResult* res, uint32_t* chain_out, unsigned* tp_seq, cudaStream_t st, bool pdl);
+                              HeadResult* res, uint32_t* chain_out, unsigned* tp_seq, cudaStream_t st, bool pdl,
+                              bool advance_pos = true);
 
 // ---- sample.cu: sample_token (src/sampling.cpp:92-169) over a device logits row. `work` is
 // g4b_sample_workspace_bytes() of device memory, private to one stream at a time; the token is

@@ -382,6 +382,7 @@ void DeviceModel::finalize_load() {
     // a key an earlier row of the same batch still needs); full-attention layers keep
     // max_context.
     for (auto& L : layers_) {
+        if (mtp_) break;  // the MTP drafter attends over its target's rings
         L.cap = L.geo.is_global ? opt_.max_context
                                 : std::min<int>(opt_.max_context, (int)h_.sliding_window) + max_rows();
         const size_t n = (size_t)L.cap * L.kvh * L.hd;
@@ -419,6 +420,7 @@ void DeviceModel::init_buffers() {
         consider(L.down);
     }
     consider(lm_);
+    if (mtp_) consider(pre_);
     part_floats_ = part;
     const int rows = max_rows();
     for (int i = 0; i < 2; ++i) hres_[i] = static_cast<float*>(dmalloc((size_t)rows * d * 4));
@@ -444,6 +446,10 @@ void DeviceModel::init_buffers() {
     cuda_check(cudaMemsetAsync(err_dev_, 0, sizeof(int), stream_), "memset");
     cuda_check(cudaMemsetAsync(sp_dev_, 0, 4 * sizeof(StepParams), stream_), "memset");
     if (opt_.tp > 1) init_tp_peers();
+    if (mtp_) {
+        bf_in_ = dmalloc(bfrag_capacity(round_up(pre_.K, 128)));
+        post_part_ = static_cast<float*>(dmalloc((size_t)post_.n_crg * post_.max_slots * kMaxM * 256 * 4));
+    }
 }
 
 void DeviceModel::init_tp_peers() {
@@ -502,6 +508,7 @@ TpGather DeviceModel::tp_gather(int step, int parity) const {
 
 void DeviceModel::clear_kv() {
     for (auto& L : layers_) {
+        if (!L.k_ring) continue;  // the MTP drafter has no rings of its own
         const size_t n = (size_t)L.cap * L.kvh * L.hd * 2;
         cuda_check(cudaMemsetAsync(L.k_ring, 0, n, stream_), "memset kv");
         cuda_check(cudaMemsetAsync(L.v_ring, 0, n, stream_), "memset kv");
@@ -512,6 +519,9 @@ uint64_t DeviceModel::pass_weight_bytes() const { return weight_bytes_; }
 
 int DeviceModel::kernels_per_pass(int M) const {
     (void)M;
+    // MTP step: input, pre-projection GEMM, its epilogue; per layer the 9 below; the
+    // post-projection and LM head GEMMs, head_chunks and finalize.
+    if (mtp_) return 3 + 9 * (int)layers_.size() + 4;
     // embed_norm; per layer 4 GEMMs + qkv_epi + attention + 2 norm/residual epilogues +
     // geglu; LM head GEMM + head_chunks + finalize (NCCL's all-reduce kernels not counted)
     const int per_layer = 9;
@@ -561,9 +571,9 @@ double DeviceModel::profile_gemms(int M, int reps, uint64_t* bytes, int* gemm_la
 
 // ----------------------------------------------------------------------------- forward
 
-PartView DeviceModel::part_view(const QW& q, int M) const {
+PartView DeviceModel::part_view(const QW& q, int M, float* part) const {
     PartView v;
-    v.part = part_;
+    v.part = part ? part : part_;
     v.max_slots = q.max_slots;
     v.n_crg = q.n_crg;
     v.ktiles = q.ktiles;
@@ -571,19 +581,21 @@ PartView DeviceModel::part_view(const QW& q, int M) const {
     return v;
 }
 
-GemmOut DeviceModel::partials(const QW& q, int M) const { return GemmOut{part_view(q, M), nullptr, q.N}; }
+GemmOut DeviceModel::partials(const QW& q, int M, float* part) const {
+    return GemmOut{part_view(q, M, part), nullptr, q.N};
+}
 
 float* DeviceModel::tp_out(int parity) const {
     return opt_.tp > 1 ? tp_buf_ + (size_t)parity * max_rows() * h_.d_model : nullptr;
 }
 
-void DeviceModel::gemm(const QW& q, const void* bfrag, int M, float* y) {
+void DeviceModel::gemm(const QW& q, const void* bfrag, int M, float* y, float* part) {
     const BFragView v = bfrag_view(const_cast<void*>(bfrag), q.ktiles * 128, M);
     VgemmParams p{};
     p.w = q.w;
     p.bfrag = v.frag;
     p.gsum = v.gsum;
-    p.out = part_view(q, M);
+    p.out = part_view(q, M, part);
     p.N = q.N;
     p.M = M;
     p.n_wrg = q.n_wrg;
@@ -671,7 +683,8 @@ void DeviceModel::enqueue_prefill(int M, bool want_logits) {
         const bool last = l + 1 == layers_.size();
         const uint16_t* w_next = last ? final_norm_ : layers_[l + 1].in_norm;
         cuda_check(g4b_rowepi(GemmOut{PartView{}, yd, d}, tp_gather(2 * (int)l + 1, 1), hres_[cur], hres_[1 - cur],
-                              L.pffn_norm, L.scalar, w_next, d, bf_d_, M, stream_, pdl, last ? M - 1 : 0),
+                              L.pffn_norm, L.scalar, w_next, d, bf_d_, M, stream_, pdl, last ? M - 1 : 0,
+                              last ? hidden_out_ : nullptr),
                    "post_ffn");
         cur = 1 - cur;
     }
@@ -679,6 +692,13 @@ void DeviceModel::enqueue_prefill(int M, bool want_logits) {
 }
 
 void DeviceModel::enqueue_raw(int M, PassKind kind, bool want_logits, uint32_t* chain_out) {
+    if (mtp_) {
+        if (M != 1 || (kind != PassKind::MtpFirst && kind != PassKind::MtpNext))
+            throw std::runtime_error("the MTP drafter runs one-row MtpFirst / MtpNext steps");
+        enqueue_mtp(kind == PassKind::MtpFirst, want_logits, chain_out);
+        return;
+    }
+    if (kind == PassKind::MtpFirst || kind == PassKind::MtpNext) throw std::runtime_error("not an MTP drafter");
     if (M > kMaxM) {
         enqueue_prefill(M, want_logits);
         return;
@@ -744,9 +764,10 @@ void DeviceModel::enqueue_raw(int M, PassKind kind, bool want_logits, uint32_t* 
         gemm(L.down, bf_ff_, M, tp_out(1));
         GemmOut dn = partials(L.down, M);
         if (opt_.tp > 1) dn = GemmOut{PartView{}, nullptr, d};
-        const uint16_t* w_next = (l + 1 < layers_.size()) ? layers_[l + 1].in_norm : final_norm_;
+        const bool last = l + 1 == layers_.size();
+        const uint16_t* w_next = last ? final_norm_ : layers_[l + 1].in_norm;
         cuda_check(g4b_rowepi(dn, tp_gather(2 * (int)l + 1, 1), hres_[cur], hres_[1 - cur], L.pffn_norm, L.scalar,
-                              w_next, d, bf_d_, M, stream_, pdl),
+                              w_next, d, bf_d_, M, stream_, pdl, 0, last ? hidden_out_ : nullptr),
                    "post_ffn");
         cur = 1 - cur;
     }
@@ -755,7 +776,7 @@ void DeviceModel::enqueue_raw(int M, PassKind kind, bool want_logits, uint32_t* 
 
 // LM head over the M rows whose final-norm fragments are in bf_d_ (verify layout), then the
 // softcapped chunk argmax and the row argmax / greedy acceptance.
-void DeviceModel::head(int M, bool want_logits, uint32_t* chain_out, StepParams* sp) {
+void DeviceModel::head(int M, bool want_logits, uint32_t* chain_out, StepParams* sp, bool advance_pos) {
     const bool pdl = opt_.use_pdl;
     gemm(lm_, bf_d_, M, nullptr);
     const GemmOut lo = partials(lm_, M);
@@ -773,7 +794,7 @@ void DeviceModel::head(int M, bool want_logits, uint32_t* chain_out, StepParams*
         throw std::runtime_error("ncclAllGather (LM head) failed");
 #endif
     cuda_check(g4b_head_finalize(chunk_best_, nch, opt_.tp, M, sp, res_dev_, chain_out, opt_.tp > 1 ? tp_seq_ : nullptr,
-                                 stream_, pdl),
+                                 stream_, pdl, advance_pos),
                "head_finalize");
 }
 
@@ -866,6 +887,327 @@ void DeviceModel::check_device_error() {
     cuda_check(cudaMemcpyAsync(&h, err_dev_, sizeof(int), cudaMemcpyDeviceToHost, stream_), "err");
     cuda_check(cudaStreamSynchronize(stream_), "sync");
     if (h) throw std::runtime_error("a kernel's bounded wait gave up (weights or fragments never arrived)");
+}
+
+// ----------------------------------------------------------------------------- MTP drafter
+
+void DeviceModel::enable_hidden_out() {
+    if (!loaded_) throw std::runtime_error("enable_hidden_out: model not loaded");
+    if (mtp_) throw std::runtime_error("enable_hidden_out: not a target model");
+    if (hidden_out_) return;
+    if (!graphs_.empty()) throw std::runtime_error("enable_hidden_out must precede the first captured pass");
+    hidden_out_ = static_cast<float*>(dmalloc((size_t)max_rows() * h_.d_model * 4));
+}
+
+// G4DenseHeader fields the shared forward code reads, from the MTP header: the drafter's own
+// widths, vocabulary and layer kinds; no softcap on its logits (src/mtp_runner.cpp:773-790).
+static G4DenseHeader mtp_as_dense(const G4MtpHeader& m) {
+    G4DenseHeader h{};
+    h.magic = G4DenseHeader::kMagic;
+    h.version = G4DenseHeader::kVersion;
+    h.quant_type = 1;
+    h.quant_group_size = 64;
+    h.num_layers = m.num_layers;
+    h.d_model = m.hidden_size;
+    h.d_ff = m.intermediate_size;
+    h.vocab_size = m.vocab_size;
+    h.num_q_heads = m.num_q_heads;
+    h.num_kv_heads = m.num_kv_heads;
+    h.head_dim = m.head_dim;
+    h.global_head_dim = m.global_head_dim;
+    h.global_kv_heads = m.global_kv_heads;
+    h.sliding_window = m.sliding_window;
+    h.global_layer_mask = m.global_layer_mask;
+    h.final_logit_softcapping = 0.f;
+    h.tied_embeddings = 1;
+    return h;
+}
+
+void DeviceModel::mtp_attach(DeviceModel& T) {
+    if (opt_.tp != 1 || T.opt_.tp != 1) throw std::runtime_error("the MTP drafter runs without tensor parallelism");
+    if (!T.loaded_ || T.mtp_) throw std::runtime_error("the MTP drafter needs a loaded target model");
+    if (mh_.backbone_hidden_size != T.h_.d_model || mh_.vocab_size != T.h_.vocab_size)
+        throw G4DenseFormatError("MTP drafter: backbone width or vocabulary differs from the target's");
+    // Donor layers: the target's last sliding and last full-attention layer (the 31B's 58 / 59,
+    // src/mtp_runner.cpp:368).
+    int donor_local = -1, donor_global = -1;
+    for (size_t l = 0; l < T.layers_.size(); ++l) (T.layers_[l].geo.is_global ? donor_global : donor_local) = (int)l;
+    for (size_t l = 0; l < layers_.size(); ++l) {
+        DevLayer& L = layers_[l];
+        const int dl = L.geo.is_global ? donor_global : donor_local;
+        if (dl < 0) throw G4DenseFormatError("MTP drafter: the target has no donor layer of this attention kind");
+        const DevLayer& D = T.layers_[dl];
+        const int want_kvh = L.geo.is_global ? (int)mh_.global_kv_heads : (int)mh_.num_kv_heads;
+        if (D.hd != L.hd || D.kvh != want_kvh || L.qh % D.kvh)
+            throw G4DenseFormatError("MTP drafter: attention geometry differs from the target's donor layer");
+        L.att_k = D.k_ring;
+        L.att_v = D.v_ring;
+        L.att_cap = D.cap;
+        L.att_kvh = D.kvh;
+        L.att_window = D.geo.is_global ? 0 : (int)T.h_.sliding_window;
+        // Rotation as on the donor: its bases and rotated pairs (the reference hard-codes the
+        // 31B's 1e4 / 1e6 and 128 / 64 pairs, src/mtp_runner.cpp:369-372).
+        L.theta = D.theta;
+        L.rotated = D.rotated;
+    }
+    donor_ = &T;
+    opt_.kv_bf16 = T.opt_.kv_bf16;
+}
+
+void DeviceModel::load_mtp(const std::string& path, DeviceModel& target) {
+    if (loaded_) throw std::runtime_error("model already loaded");
+    const int fd = open(path.c_str(), O_RDONLY);
+    if (fd < 0) throw G4DenseFormatError("MtpRunner: failed to open " + path);
+    struct stat st;
+    if (fstat(fd, &st) != 0 || (size_t)st.st_size < sizeof(G4MtpHeader)) {
+        close(fd);
+        throw G4DenseFormatError("MTP container too small for its header");
+    }
+    const size_t size = (size_t)st.st_size;
+    void* map = mmap(nullptr, size, PROT_READ, MAP_PRIVATE, fd, 0);
+    close(fd);
+    if (map == MAP_FAILED) throw G4DenseFormatError("MtpRunner: MapViewOfFile failed for " + path);
+    struct Unmap {
+        void* p;
+        size_t n;
+        ~Unmap() { munmap(p, n); }
+    } unmap{map, size};
+    const uint8_t* base = static_cast<const uint8_t*>(map);
+    std::memcpy(&mh_, base, sizeof(G4MtpHeader));
+    validate_mtp_header(mh_, size);
+    mtp_ = true;
+    h_ = mtp_as_dense(mh_);
+    const int hs = mh_.hidden_size, bb = mh_.backbone_hidden_size, I = mh_.intermediate_size, V = mh_.vocab_size;
+    auto sect = [&](uint64_t off, int rows, int cols) {
+        const uint8_t* p = base + off;
+        QPtr q{reinterpret_cast<const uint32_t*>(p), nullptr, nullptr, rows, cols};
+        const size_t wb = (size_t)rows * (cols / 8) * 4, sb = (size_t)rows * (cols / 64) * 2;
+        if (off + wb + 2 * sb > size) throw G4DenseFormatError("MTP section extends beyond the file");
+        q.s = reinterpret_cast<const uint16_t*>(p + wb);
+        q.b = reinterpret_cast<const uint16_t*>(p + wb + sb);
+        return q;
+    };
+    std::vector<uint32_t> W;
+    std::vector<uint16_t> S, B;
+    auto up = [&](QW& q, const std::vector<RowRange>& rr, int Kl) {
+        gather_host(rr, 0, Kl, W, S, B);
+        const int N = (int)(S.size() / (Kl / 64));
+        uint32_t* dw = static_cast<uint32_t*>(dmalloc(W.size() * 4));
+        uint16_t* ds = static_cast<uint16_t*>(dmalloc(S.size() * 2));
+        uint16_t* db = static_cast<uint16_t*>(dmalloc(B.size() * 2));
+        cuda_check(cudaMemcpy(dw, W.data(), W.size() * 4, cudaMemcpyHostToDevice), "upload");
+        cuda_check(cudaMemcpy(ds, S.data(), S.size() * 2, cudaMemcpyHostToDevice), "upload");
+        cuda_check(cudaMemcpy(db, B.data(), B.size() * 2, cudaMemcpyHostToDevice), "upload");
+        upload_qw(q, dw, ds, db, N, Kl, false);
+        cuda_check(cudaStreamSynchronize(stream_), "repack");
+        for (void* x : {(void*)dw, (void*)ds, (void*)db}) {
+            cudaFree(x);
+            allocs_.erase(std::find(allocs_.begin(), allocs_.end(), x));
+        }
+    };
+    // Tied LM head (the drafter's own [V][hidden] table), projections, final norm
+    // (MtpRunner::allocate_gpu_resources, src/mtp_runner.cpp:236-261).
+    const QPtr E = sect(mh_.embed_offset, V, hs), Pre = sect(mh_.pre_proj_offset, hs, 2 * bb),
+               Post = sect(mh_.post_proj_offset, bb, hs);
+    emb_w_ = static_cast<uint32_t*>(dmalloc((size_t)V * (hs / 8) * 4));
+    emb_s_ = static_cast<uint16_t*>(dmalloc((size_t)V * (hs / 64) * 2));
+    emb_b_ = static_cast<uint16_t*>(dmalloc((size_t)V * (hs / 64) * 2));
+    cuda_check(cudaMemcpy(emb_w_, E.w, (size_t)V * (hs / 8) * 4, cudaMemcpyHostToDevice), "upload");
+    cuda_check(cudaMemcpy(emb_s_, E.s, (size_t)V * (hs / 64) * 2, cudaMemcpyHostToDevice), "upload");
+    cuda_check(cudaMemcpy(emb_b_, E.b, (size_t)V * (hs / 64) * 2, cudaMemcpyHostToDevice), "upload");
+    up(pre_, {{&Pre, 0, hs}}, 2 * bb);
+    up(post_, {{&Post, 0, bb}}, hs);
+    if (mh_.norm_offset + (size_t)hs * 2 > size) throw G4DenseFormatError("MTP norm extends beyond the file");
+    final_norm_ = upload_u16(reinterpret_cast<const uint16_t*>(base + mh_.norm_offset), hs);
+    // Layers: MtpRunner::compute_layer_offsets (src/mtp_runner.cpp:175-234).
+    layers_.resize(mh_.num_layers);
+    for (uint32_t l = 0; l < mh_.num_layers; ++l) {
+        DevLayer& L = layers_[l];
+        const uint8_t* lp = base + mh_.layer_offsets[l];
+        L.geo = resolve_layer_geometry(h_, l);
+        L.hd = L.geo.head_dim;
+        L.qh = mh_.num_q_heads;
+        L.kvh = 0;  // q-only: the keys and values are the target's
+        L.F = I;
+        L.has_v = 0;
+        const int qd = L.qh * L.hd;
+        const uint16_t* n = reinterpret_cast<const uint16_t*>(lp);
+        L.in_norm = upload_u16(n, hs);
+        L.pa_norm = upload_u16(n + hs, hs);
+        L.pf_norm = upload_u16(n + 2 * hs, hs);
+        L.pffn_norm = upload_u16(n + 3 * hs, hs);
+        L.q_norm = upload_u16(n + 4 * hs, L.hd);
+        uint16_t scal;
+        std::memcpy(&scal, n + 4 * hs + L.hd, 2);
+        const uint32_t sb = (uint32_t)scal << 16;
+        std::memcpy(&L.scalar, &sb, 4);
+        const uint8_t* p = reinterpret_cast<const uint8_t*>(n + 4 * hs + L.hd + 1);
+        auto parse = [&](int rows, int cols) {
+            p += (16u - ((size_t)(p - lp) & 15u)) & 15u;
+            QPtr q{reinterpret_cast<const uint32_t*>(p), nullptr, nullptr, rows, cols};
+            const size_t wb = (size_t)rows * (cols / 8) * 4, sbytes = (size_t)rows * (cols / 64) * 2;
+            q.s = reinterpret_cast<const uint16_t*>(p + wb);
+            q.b = reinterpret_cast<const uint16_t*>(p + wb + sbytes);
+            p += wb + 2 * sbytes;
+            if ((size_t)(p - lp) > mh_.layer_sizes[l]) throw G4DenseFormatError("MTP layer shorter than its matrices");
+            return q;
+        };
+        const QPtr Wq = parse(qd, hs), Wo = parse(hs, qd), Wg = parse(I, hs), Wu = parse(I, hs), Wd = parse(hs, I);
+        up(L.qkv, {{&Wq, 0, qd}}, hs);
+        up(L.o, {{&Wo, 0, hs}}, qd);
+        up(L.gateup, {{&Wg, 0, I}, {&Wu, 0, I}}, hs);
+        up(L.down, {{&Wd, 0, hs}}, I);
+    }
+    mtp_attach(target);
+    finalize_load();
+}
+
+void DeviceModel::load_mtp_synthetic(const G4MtpHeader& geom, uint64_t seed, bool centered, DeviceModel& target) {
+    if (loaded_) throw std::runtime_error("model already loaded");
+    mh_ = geom;
+    mh_.magic = G4MtpHeader::kMagic;
+    mh_.version = G4MtpHeader::kVersion;
+    mh_.quant_type = 1;
+    mh_.quant_group_size = 64;
+    const int hs = mh_.hidden_size, bb = mh_.backbone_hidden_size, I = mh_.intermediate_size, V = mh_.vocab_size;
+    if (!mh_.num_layers || mh_.num_layers > G4MtpHeader::kMaxLayers || hs % 64 || bb % 64 || I % 64 || V < 1)
+        throw G4DenseFormatError("invalid synthetic MTP geometry");
+    mtp_ = true;
+    h_ = mtp_as_dense(mh_);
+    size_t max_words = (size_t)hs * 2 * bb / 8;
+    for (uint32_t l = 0; l < mh_.num_layers; ++l) {
+        const LayerGeometry g = resolve_layer_geometry(h_, l);
+        max_words = std::max({max_words, (size_t)g.q_heads * g.head_dim * hs / 8, (size_t)2 * I * hs / 8});
+    }
+    uint32_t* sw = static_cast<uint32_t*>(dmalloc(max_words * 4));
+    uint16_t* ss = static_cast<uint16_t*>(dmalloc(max_words / 8 * 2));
+    uint16_t* sbb = static_cast<uint16_t*>(dmalloc(max_words / 8 * 2));
+    auto build = [&](QW& q, const std::vector<std::pair<uint64_t, int>>& parts, int Kl) {
+        int r = 0;
+        for (const auto& pt : parts) {
+            cuda_check(g4b_synth_qblock(sw + (size_t)r * (Kl / 8), ss + (size_t)r * (Kl / 64), sbb + (size_t)r * (Kl / 64),
+                                        pt.second, Kl, 0, 0, Kl, seed, pt.first, centered, stream_),
+                       "synth");
+            r += pt.second;
+        }
+        upload_qw(q, sw, ss, sbb, r, Kl, false);
+    };
+    emb_w_ = static_cast<uint32_t*>(dmalloc((size_t)V * (hs / 8) * 4));
+    emb_s_ = static_cast<uint16_t*>(dmalloc((size_t)V * (hs / 64) * 2));
+    emb_b_ = static_cast<uint16_t*>(dmalloc((size_t)V * (hs / 64) * 2));
+    cuda_check(g4b_synth_qblock(emb_w_, emb_s_, emb_b_, V, hs, 0, 0, hs, seed, 100000, centered, stream_), "synth");
+    final_norm_ = static_cast<uint16_t*>(dmalloc(hs * 2));
+    cuda_check(g4b_synth_norm(final_norm_, hs, seed, 200000, stream_), "synth");
+    build(pre_, {{300000, hs}}, 2 * bb);
+    build(post_, {{300001, bb}}, hs);
+    layers_.resize(mh_.num_layers);
+    for (uint32_t l = 0; l < mh_.num_layers; ++l) {
+        DevLayer& L = layers_[l];
+        L.geo = resolve_layer_geometry(h_, l);
+        L.hd = L.geo.head_dim;
+        L.qh = mh_.num_q_heads;
+        L.kvh = 0;
+        L.F = I;
+        L.has_v = 0;
+        const float sc = 1.0f / std::sqrt(2.0f * (float)mh_.num_layers);
+        uint32_t u;
+        std::memcpy(&u, &sc, 4);
+        u = (u + 0x7FFFu + ((u >> 16) & 1u)) & 0xFFFF0000u;
+        std::memcpy(&L.scalar, &u, 4);
+        const uint64_t t = 400000 + (uint64_t)l * 16;
+        auto norm = [&](int n, uint64_t id) {
+            auto* p = static_cast<uint16_t*>(dmalloc(n * 2));
+            cuda_check(g4b_synth_norm(p, n, seed, t + id, stream_), "synth");
+            return p;
+        };
+        L.in_norm = norm(hs, 8);
+        L.pa_norm = norm(hs, 9);
+        L.pf_norm = norm(hs, 10);
+        L.pffn_norm = norm(hs, 11);
+        L.q_norm = norm(L.hd, 12);
+        build(L.qkv, {{t + 0, L.qh * L.hd}}, hs);
+        build(L.o, {{t + 3, hs}}, L.qh * L.hd);
+        build(L.gateup, {{t + 4, I}, {t + 5, I}}, hs);
+        build(L.down, {{t + 6, hs}}, I);
+    }
+    cuda_check(cudaStreamSynchronize(stream_), "synthesize");
+    for (void* x : {(void*)sw, (void*)ss, (void*)sbb}) {
+        cudaFree(x);
+        allocs_.erase(std::find(allocs_.begin(), allocs_.end(), x));
+    }
+    mtp_attach(target);
+    finalize_load();
+}
+
+// One MtpRunner::generate_draft_tokens step (src/mtp_runner.cpp:318-843) from StepParams slot 1:
+// tokens[0] is the input token, base_pos the last position the target has processed (its
+// keys, up to and including base_pos, are what the drafter attends; the query rotates at
+// base_pos + 1, the pending token's position) and aux the row of the target's normed hidden
+// states a round starts from. With chain_out the drafted token becomes the next step's input
+// and is appended to chain_out; the position stays (the reference keeps context_length).
+void DeviceModel::enqueue_mtp(bool first, bool want_logits, uint32_t* chain_out) {
+    if (!donor_ || !donor_->hidden_out_) throw std::runtime_error("MTP drafter: target hidden states not enabled");
+    const int hs = h_.d_model, bb = mh_.backbone_hidden_size;
+    const bool pdl = opt_.use_pdl;
+    StepParams* sp = sp_dev_ + 1;
+    DeviceModel& T = *donor_;
+    cuda_check(g4b_mtp_input(sp, T.emb_w_, T.emb_s_, T.emb_b_, T.h_.vocab_size, bb, first ? T.hidden_out_ : nullptr,
+                             partials(post_, 1, post_part_), bf_in_, stream_, false),
+               "mtp_input");
+    gemm(pre_, bf_in_, 1, nullptr);
+    int cur = 0;
+    const TpGather none = tp_gather(0, 0);
+    cuda_check(g4b_rowepi(partials(pre_, 1), none, nullptr, hres_[cur], nullptr, 1.0f, layers_[0].in_norm, hs, bf_d_, 1,
+                          stream_, pdl),
+               "mtp_pre");
+    for (size_t l = 0; l < layers_.size(); ++l) {
+        DevLayer& L = layers_[l];
+        gemm(L.qkv, bf_d_, 1, nullptr);
+        QkvEpiArgs qa{};
+        qa.qkv = partials(L.qkv, 1);
+        qa.sp = sp;
+        qa.M = 1;
+        qa.qh = L.qh;
+        qa.kvh = 0;
+        qa.hd = L.hd;
+        qa.rotated = L.rotated;
+        qa.theta = L.theta;
+        qa.q_norm = L.q_norm;
+        qa.q_out = q_buf_;
+        qa.kv_bf16 = opt_.kv_bf16;
+        qa.pos_offset = 1;
+        cuda_check(g4b_qkv_epi(qa, stream_, pdl), "mtp_q_epi");
+        AttnArgs aa{};
+        aa.q = q_buf_;
+        aa.k_ring = L.att_k;
+        aa.v_ring = L.att_v;
+        aa.sp = sp;
+        aa.M = 1;
+        aa.qh = L.qh;
+        aa.kvh = L.att_kvh;
+        aa.hd = L.hd;
+        aa.cap = L.att_cap;
+        aa.window = L.att_window;
+        aa.kv_bf16 = opt_.kv_bf16;
+        aa.scale = 1.0f;
+        cuda_check(g4b_attention(aa, bf_attn_, stream_, pdl), "mtp_attention");
+        gemm(L.o, bf_attn_, 1, nullptr);
+        cuda_check(g4b_rowepi(partials(L.o, 1), none, hres_[cur], hres_[1 - cur], L.pa_norm, 1.0f, L.pf_norm, hs, bf_d_,
+                              1, stream_, pdl),
+                   "mtp_post_attn");
+        cur = 1 - cur;
+        gemm(L.gateup, bf_d_, 1, nullptr);
+        cuda_check(g4b_geglu(partials(L.gateup, 1), L.F, bf_ff_, 1, stream_, pdl), "mtp_geglu");
+        gemm(L.down, bf_ff_, 1, nullptr);
+        const uint16_t* w_next = (l + 1 < layers_.size()) ? layers_[l + 1].in_norm : final_norm_;
+        cuda_check(g4b_rowepi(partials(L.down, 1), none, hres_[cur], hres_[1 - cur], L.pffn_norm, L.scalar, w_next, hs,
+                              bf_d_, 1, stream_, pdl),
+                   "mtp_post_ffn");
+        cur = 1 - cur;
+    }
+    // Post-projection (the next step's h) into its own slots, then the tied LM head.
+    gemm(post_, bf_d_, 1, nullptr, post_part_);
+    head(1, want_logits, chain_out, sp, false);
 }
 
 }  // namespace g4b

@@ -49,12 +49,15 @@ struct DevLayer {
     uint16_t *q_norm = nullptr, *k_norm = nullptr;
     uint16_t *k_ring = nullptr, *v_ring = nullptr;
     int cap = 0;
+    // MTP drafter layers attend over a donor layer of the target instead of their own ring.
+    const uint16_t *att_k = nullptr, *att_v = nullptr;
+    int att_cap = 0, att_kvh = 0, att_window = 0;
 };
 
 // Rows one pass processes at most (verify width, prefill chunk).
 constexpr int kBatchRows = 16;
 
-enum class PassKind { Plain = 0, DraftStep = 1 };
+enum class PassKind { Plain = 0, DraftStep = 1, MtpFirst = 2, MtpNext = 3 };
 
 class DeviceModel {
    public:
@@ -69,6 +72,18 @@ class DeviceModel {
     // Generates weights with the container's value distributions directly on the device
     // for the geometry in `geom` (header fields only; offsets are ignored).
     void load_synthetic(const G4DenseHeader& geom, uint64_t seed, bool centered);
+    // The MTP "assistant" drafter (src/mtp_runner.cpp) as a model of this class: a .g4mtp
+    // container (validated like src/format.cpp:67-130), or synthetic weights of that geometry.
+    // Its attention reads `target`'s KV rings (the target's last sliding and last full-attention
+    // layers) and its input the target's embedding table and final normed hidden states, so the
+    // target must outlive it, run tensor-parallel size 1, and have enable_hidden_out() set.
+    void load_mtp(const std::string& path, DeviceModel& target);
+    void load_mtp_synthetic(const G4MtpHeader& geom, uint64_t seed, bool centered, DeviceModel& target);
+    bool is_mtp() const { return mtp_; }
+    const G4MtpHeader& mtp_header() const { return mh_; }
+    // Makes every pass also write its final normed hidden rows in fp32 ([rows][d_model]; a prefill
+    // chunk's last row as row 0), the MTP drafter's input. Call before the first pass.
+    void enable_hidden_out();
 
     const G4DenseHeader& header() const { return h_; }
     int vocab_local() const { return v_local_; }
@@ -125,14 +140,16 @@ class DeviceModel {
     TpGather tp_gather(int step, int parity) const;
     void build_layer_from_host(uint32_t l, const uint8_t* layer_ptr);
     void enqueue_raw(int M, PassKind kind, bool want_logits, uint32_t* chain_out);
+    void enqueue_mtp(bool first, bool want_logits, uint32_t* chain_out);
+    void mtp_attach(DeviceModel& target);  // donor rings, geometry checks, buffers
     // One verify GEMM; y == nullptr leaves split-K partials for the consumer (partials()).
-    void gemm(const QW& q, const void* bfrag, int M, float* y);
+    void gemm(const QW& q, const void* bfrag, int M, float* y, float* part = nullptr);
     // One prefill GEMM (17..128 rows, wide-layout activations) into the dense y[M][q.N].
     void pgemm(const QW& q, const void* act, int M, float* y);
     void enqueue_prefill(int M, bool want_logits);
-    void head(int M, bool want_logits, uint32_t* chain_out, StepParams* sp);
-    PartView part_view(const QW& q, int M) const;
-    GemmOut partials(const QW& q, int M) const;
+    void head(int M, bool want_logits, uint32_t* chain_out, StepParams* sp, bool advance_pos = true);
+    PartView part_view(const QW& q, int M, float* part = nullptr) const;
+    GemmOut partials(const QW& q, int M, float* part = nullptr) const;
     float* tp_out(int parity) const;  // under TP: this rank's partial buffer of that parity, else nullptr
     void upload_qw(QW& q, const uint32_t* W, const uint16_t* S, const uint16_t* B, int N, int K,
                    bool prefill = true);
@@ -147,6 +164,15 @@ class DeviceModel {
     std::vector<void*> allocs_;
     std::vector<DevLayer> layers_;
     QW lm_;
+    // MTP drafter mode: pre-/post-projections, the target whose rings and embedding it reads,
+    // the post-projection's own split-K slots (they outlive the LM head's), its input fragments.
+    bool mtp_ = false;
+    G4MtpHeader mh_{};
+    DeviceModel* donor_ = nullptr;
+    QW pre_, post_;
+    float* post_part_ = nullptr;
+    void* bf_in_ = nullptr;
+    float* hidden_out_ = nullptr;  // final normed hidden rows (enable_hidden_out)
     int v_local_ = 0, v_off_ = 0;
     uint32_t* emb_w_ = nullptr;
     uint16_t *emb_s_ = nullptr, *emb_b_ = nullptr, *final_norm_ = nullptr;

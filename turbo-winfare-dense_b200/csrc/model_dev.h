@@ -14,6 +14,7 @@ namespace g4b {
 struct StepParams {
     int base_pos;
     int draft_step;  // drafter chaining: index of the next draft written to the chain list
+    int aux;         // MTP drafter: row of the target's normed hidden states a round starts from
     uint32_t tokens[kPrefillRows];  // a verify pass uses the first 16, a prefill chunk up to 128
 };
 
@@ -148,6 +149,7 @@ struct QkvEpiArgs {
     uint16_t* v_ring;
     int cap;
     int kv_bf16;             // 1: round K/V through bf16 instead of FP16 (long-context mode)
+    int pos_offset;          // rotary position = base_pos + row + pos_offset
 };
 
 // Tensor-parallel sum of one step's dense partial outputs over peer memory (NVLink). Every rank

@@ -82,6 +82,44 @@ __global__ void embed_norm_kernel(const StepParams* __restrict__ sp, const uint3
     row_to_bfrags(xs, d, M, m, bfrag, stage, red);
 }
 
+// ---------------------------------------------------------------- MTP drafter input
+
+// MtpRunner's step input (src/mtp_runner.cpp:318-327): x = [e(t) * sqrt(bb); h] as the
+// pre-projection's B fragments (one row, K = 2 * bb). e(t) is the target's dequantised embedding
+// row of sp->tokens[0] (ForwardRunner::get_token_embedding, src/runner.cpp:2359-2380); h is row
+// sp->aux of the target's final normed hidden states on a round's first step, else the previous
+// step's post-projection (its split-K slots).
+__global__ void mtp_input_kernel(const StepParams* __restrict__ sp, const uint32_t* __restrict__ ew,
+                                 const uint16_t* __restrict__ es, const uint16_t* __restrict__ eb, int V, int bb,
+                                 const float* __restrict__ hidden, GemmOut post, void* bfrag) {
+    extern __shared__ float smem[];
+    float* xs = smem;                                        // [2 * bb]
+    __half* stage = reinterpret_cast<__half*>(xs + 2 * bb);  // [warps][128]
+    __shared__ float red[32];
+    pdl_enter();
+    const uint32_t tok = sp->tokens[0] % (uint32_t)V;
+    const float scale = sqrtf((float)bb);
+    const uint32_t* wr = ew + (size_t)tok * (bb / 8);
+    const uint16_t* sr = es + (size_t)tok * (bb / 64);
+    const uint16_t* br = eb + (size_t)tok * (bb / 64);
+    for (int c = threadIdx.x; c < bb; c += blockDim.x) {
+        const uint32_t q = (wr[c >> 3] >> ((c & 7) * 4)) & 0xFu;
+        xs[c] = ((float)q * bf16_to_f32(sr[c >> 6]) + bf16_to_f32(br[c >> 6])) * scale;
+    }
+    if (hidden) {
+        const float* hr = hidden + (size_t)sp->aux * bb;
+        for (int c = threadIdx.x; c < bb; c += blockDim.x) xs[bb + c] = hr[c];
+    } else {
+        for (int c = 2 * threadIdx.x; c < bb; c += 2 * blockDim.x) {
+            const float2 v = gemm_out_pair(post, 0, c);
+            xs[bb + c] = v.x;
+            xs[bb + c + 1] = v.y;
+        }
+    }
+    __syncthreads();
+    row_to_bfrags(xs, 2 * bb, 1, 0, bfrag, stage, red);
+}
+
 // ---------------------------------------------------------------- Q/K/V epilogue
 
 // One CTA per (row m, head): heads [0, qh) are query heads, [qh, qh + kvh) KV heads. Thread i
@@ -123,7 +161,7 @@ __global__ void __launch_bounds__(256, 3) qkv_epi_kernel(QkvEpiArgs a) {
     // Before waiting on the GEMM: the norm weights and the rotation, which depend only on the
     // position (base_pos is written by a pass's last kernel alone, and every pass starts with a
     // kernel launched without programmatic overlap, so it is stable here).
-    const int pos = a.sp->base_pos + m;
+    const int pos = a.sp->base_pos + m + a.pos_offset;
     const uint16_t* wn = is_q ? a.q_norm : a.k_norm;
     const float wa = bf16_to_f32(wn[i]), wb = bf16_to_f32(wn[i + half]);
     float rc = 1.f, rs = 0.f;
@@ -227,7 +265,8 @@ __global__ void __launch_bounds__(CLUSTER ? kEpiWarps * 32 : kEpiMaxWarps * 32) 
                                                                     float* __restrict__ h_out,
                                                                     const uint16_t* __restrict__ w1, float out_scale,
                                                                     const uint16_t* __restrict__ w2, int d,
-                                                                    void* bfrag, int M, int frag_row0) {
+                                                                    void* bfrag, int M, int frag_row0,
+                                                                    float* __restrict__ x_out) {
     __shared__ float4 red[kEpiMaxWarps];
     __shared__ float red_max[32];
     __shared__ float4 cta_sum;
@@ -249,7 +288,7 @@ __global__ void __launch_bounds__(CLUSTER ? kEpiWarps * 32 : kEpiMaxWarps * 32) 
             const int c0 = (rank * gpc + warp + nw * j) * 64 + 2 * lane;
             wv1[j] = wv2[j] = make_float2(0.f, 0.f);
             if (rank * gpc + warp + nw * j < g_end && c0 < d) {
-                wv1[j] = make_float2(bf16_to_f32(w1[c0]), bf16_to_f32(w1[c0 + 1]));
+                wv1[j] = w1 ? make_float2(bf16_to_f32(w1[c0]), bf16_to_f32(w1[c0 + 1])) : make_float2(1.f, 1.f);
                 wv2[j] = make_float2(bf16_to_f32(w2[c0]), bf16_to_f32(w2[c0 + 1]));
             }
         }
@@ -258,7 +297,9 @@ __global__ void __launch_bounds__(CLUSTER ? kEpiWarps * 32 : kEpiMaxWarps * 32) 
     if constexpr (kPreloadW) load_w();
     pdl_wait();
     // Weight of column c (= (rank * gpc + warp + nw * j) * 64 + 2 * lane + e).
-    auto wt1 = [&](int j, int e, int c) { return kPreloadW ? (e ? wv1[j].y : wv1[j].x) : bf16_to_f32(w1[c]); };
+    auto wt1 = [&](int j, int e, int c) {
+        return kPreloadW ? (e ? wv1[j].y : wv1[j].x) : (w1 ? bf16_to_f32(w1[c]) : 1.f);
+    };
     auto wt2 = [&](int j, int e, int c) { return kPreloadW ? (e ? wv2[j].y : wv2[j].x) : bf16_to_f32(w2[c]); };
     if (tg.n > 1) tp_sync(tg, blockIdx.x == 0 && blockIdx.y == 0);
 
@@ -296,7 +337,7 @@ __global__ void __launch_bounds__(CLUSTER ? kEpiWarps * 32 : kEpiMaxWarps * 32) 
         h[j] = make_float2(0.f, 0.f);
         if (gi < g_end && c0 < d) {
             if (wpg < 2) y[j] = tg.n > 1 ? tp_pair(tg, m, o.ld, c0) : gemm_out_pair(o, m, c0);
-            h[j] = *reinterpret_cast<const float2*>(h_in + (size_t)m * d + c0);
+            if (h_in) h[j] = *reinterpret_cast<const float2*>(h_in + (size_t)m * d + c0);
             const float ca = y[j].x * wt1(j, 0, c0), cb = y[j].y * wt1(j, 1, c0 + 1);
             acc.x += y[j].x * y[j].x + y[j].y * y[j].y;
             acc.y += h[j].x * h[j].x + h[j].y * h[j].y;
@@ -337,7 +378,7 @@ __global__ void __launch_bounds__(CLUSTER ? kEpiWarps * 32 : kEpiMaxWarps * 32) 
         __syncthreads();
         t = cta_sum;
     }
-    const float r1 = inv_rms(t.x, d);
+    const float r1 = w1 ? inv_rms(t.x, d) : 1.f;  // plain mode: y enters the residual unnormalised
     const float s2 = out_scale * out_scale * (t.y + 2.0f * r1 * t.z + r1 * r1 * t.w);
     const float r2 = inv_rms(fmaxf(s2, 0.f), d);
     // Fragments for rows frag_row0.. only, as rows 0.. of an (M - frag_row0)-row batch (a
@@ -360,6 +401,7 @@ __global__ void __launch_bounds__(CLUSTER ? kEpiWarps * 32 : kEpiMaxWarps * 32) 
                 const float hn = __fmul_rn(__fadd_rn(hh, a), out_scale);
                 h_out[(size_t)m * d + c] = hn;
                 xv[j][e] = __fmul_rn(__fmul_rn(hn, r2), wt2(j, e, c));
+                if (x_out && mf >= 0) x_out[(size_t)mf * d + c] = xv[j][e];
                 amax = fmaxf(amax, fabsf(xv[j][e]));
             }
         }
@@ -502,6 +544,22 @@ cudaError_t g4b_embed_norm(const StepParams* sp, const uint32_t* ew, const uint1
                   bfrag, M);
 }
 
+cudaError_t g4b_mtp_input(const StepParams* sp, const uint32_t* ew, const uint16_t* es, const uint16_t* eb, int V,
+                          int bb, const float* hidden, const GemmOut& post, void* bfrag, cudaStream_t st, bool pdl) {
+    if (bb % 64) return cudaErrorInvalidValue;
+    const int th = 512;
+    const size_t smem = row_smem(2 * bb, th);
+    static bool attr_set = false;
+    if (!attr_set) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(mtp_input_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 96 * 1024);
+        if (e != cudaSuccess) return e;
+        attr_set = true;
+    }
+    if (smem > 96 * 1024) return cudaErrorInvalidValue;
+    return launch(mtp_input_kernel, dim3(1), dim3(th), smem, st, pdl, sp, ew, es, eb, V, bb, hidden, post, bfrag);
+}
+
 cudaError_t g4b_qkv_epi(const QkvEpiArgs& a, cudaStream_t st, bool pdl) {
     if (a.hd % 64 || a.hd > 1024 || a.rotated > a.hd / 2) return cudaErrorInvalidValue;
     if (!a.qkv.part.part)
@@ -511,7 +569,7 @@ cudaError_t g4b_qkv_epi(const QkvEpiArgs& a, cudaStream_t st, bool pdl) {
 
 cudaError_t g4b_rowepi(const GemmOut& o, const TpGather& tg, const float* h_in, float* h_out, const uint16_t* w1,
                        float out_scale, const uint16_t* w2, int d, void* bfrag, int M, cudaStream_t st, bool pdl,
-                       int frag_row0) {
+                       int frag_row0, float* x_out) {
     if ((o.ld | d) & 1) return cudaErrorInvalidValue;  // float2 loads
     if (frag_row0 < 0 || frag_row0 >= M) return cudaErrorInvalidValue;
     if (tg.n < 1 || tg.n > kMaxTp) return cudaErrorInvalidValue;
@@ -520,15 +578,15 @@ cudaError_t g4b_rowepi(const GemmOut& o, const TpGather& tg, const float* h_in, 
     // rows spread their slot sums over a 16-CTA cluster (measured faster from d = 1536 up).
     if (ngp <= 16)
         return launch(rowepi_kernel<false>, dim3(1, M), dim3(ngp * 32), 0, st, pdl, o, tg, h_in, h_out, w1, out_scale,
-                      w2, d, bfrag, M, frag_row0);
+                      w2, d, bfrag, M, frag_row0, x_out);
     // A prefill chunk has rows enough to fill the GPU: one CTA per row (each warp up to three
     // groups) instead of a 16-CTA cluster per row.
     if (M > kMaxM && ngp <= kEpiMaxWarps)
         return launch(rowepi_kernel<false>, dim3(1, M), dim3(ngp * 32), 0, st, pdl, o, tg, h_in, h_out, w1, out_scale,
-                      w2, d, bfrag, M, frag_row0);
+                      w2, d, bfrag, M, frag_row0, x_out);
     if (M > kMaxM && ngp <= 3 * kEpiMaxWarps)
         return launch(rowepi_kernel<false, 3>, dim3(1, M), dim3(kEpiMaxWarps * 32), 0, st, pdl, o, tg, h_in, h_out, w1,
-                      out_scale, w2, d, bfrag, M, frag_row0);
+                      out_scale, w2, d, bfrag, M, frag_row0, x_out);
     // Beyond here the cluster form: a prefill chunk's wide layout needs the row in one CTA.
     if (M - frag_row0 > kMaxM) return cudaErrorInvalidValue;
     if ((ngp + kEpiClusters - 1) / kEpiClusters > kEpiWarps * kEpiGroupsPerWarp) return cudaErrorInvalidValue;
@@ -552,7 +610,7 @@ cudaError_t g4b_rowepi(const GemmOut& o, const TpGather& tg, const float* h_in, 
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = pdl ? 2 : 1;
-    return cudaLaunchKernelEx(&cfg, rowepi_kernel<true>, o, tg, h_in, h_out, w1, out_scale, w2, d, bfrag, M, frag_row0);
+    return cudaLaunchKernelEx(&cfg, rowepi_kernel<true>, o, tg, h_in, h_out, w1, out_scale, w2, d, bfrag, M, frag_row0, x_out);
 }
 
 cudaError_t g4b_geglu(const GemmOut& gu, int F, void* bfrag, int M, cudaStream_t st, bool pdl) {

@@ -133,8 +133,8 @@ std::vector<uint32_t> Engine::generate(const std::vector<uint32_t>& prompt, cons
     const uint64_t l0 = T.launches() + (draft_ ? draft_->model().launches() : 0);
     const uint64_t h0 = T.h2d_bytes() + (draft_ ? draft_->model().h2d_bytes() : 0);
     const uint64_t d0 = T.d2h_bytes() + (draft_ ? draft_->model().d2h_bytes() : 0);
-    const bool spec = opt.speculative_enabled && draft_ && opt.draft_k > 0;
-    if (spec) {
+    const bool spec = opt.speculative_enabled && (draft_ || mtp_) && opt.draft_k > 0;
+    if (spec && draft_) {
         // The drafter's pass over the prompt is prefill work: queue it on the drafter's stream
         // first so it runs alongside the target's prefill.
         draft_->reset();
@@ -142,7 +142,8 @@ std::vector<uint32_t> Engine::generate(const std::vector<uint32_t>& prompt, cons
     }
     const bool dev_sample = !greedy && !spec && opt.device_sampling && sp.repetition_penalty == 1.0f;
     const uint32_t first = prefill(history, opt, dev_sample ? nullptr : &logits);
-    if (spec) order(draft_->model().stream(), T.stream());  // decode starts after both prefills
+    if (spec && draft_) order(draft_->model().stream(), T.stream());  // decode starts after both prefills
+    mtp_row_ = last_row_;  // the MTP drafter's first round starts from the prompt's last hidden state
     stats_.h2d_bytes += history.size() * sizeof(uint32_t);
     stats_.ttft_ms = now_ms() - t0;
     const double t_decode = now_ms();
@@ -166,8 +167,12 @@ std::vector<uint32_t> Engine::generate(const std::vector<uint32_t>& prompt, cons
         return true;
     };
     if (spec) {
-        DraftRuntime& D = *draft_;
-        DeviceModel& Dm = D.model();
+        // Two kinds of drafter: a separate model with its own KV (DraftRuntime) or the MTP
+        // assistant (src/mtp_runner.cpp), which reads the target's KV and hidden state and runs
+        // on the target's stream.
+        DraftRuntime* Dp = draft_.get();
+        DeviceModel* Mt = mtp_.get();
+        DeviceModel& Dm = Dp ? Dp->model() : *Mt;
         if (Dm.header().vocab_size != V) throw std::invalid_argument("drafter vocabulary differs from the target's");
         const uint32_t K = std::min<uint32_t>(opt.draft_k, kMaxDraftWidth);
         uint32_t drafted_total = 0, accepted_total = 0;
@@ -185,6 +190,7 @@ std::vector<uint32_t> Engine::generate(const std::vector<uint32_t>& prompt, cons
             if (!drafting) {
                 // Gated: one target pass per token (src/runner.cpp:2219-2237).
                 T.run_plain(1, (int)history.size() - 1, &pending, !greedy);
+                mtp_row_ = 0;
                 const HeadResult r = T.fetch_result();
                 uint32_t nx = r.argmax[0];
                 if (!greedy) {
@@ -206,19 +212,46 @@ std::vector<uint32_t> Engine::generate(const std::vector<uint32_t>& prompt, cons
             // round) rides in the first drafting pass together with the pending token, so that
             // round needs no separate catch-up pass. Batched rows equal sequential positions.
             size_t unseen = 0;
-            if (greedy) {
-                if (D.consumed() > len - 1) D.set_consumed(0);
-                unseen = len - 1 - D.consumed();
+            if (Dp && greedy) {
+                if (Dp->consumed() > len - 1) Dp->set_consumed(0);
+                unseen = len - 1 - Dp->consumed();
                 if (unseen + 1 > (size_t)kBatchRows) {
-                    D.catch_up(history);
+                    Dp->catch_up(history);
                     unseen = 0;
                 }
-            } else {
-                D.catch_up(history);
+            } else if (Dp) {
+                Dp->catch_up(history);
             }
             std::vector<uint32_t> emitted_now;
             uint32_t n_acc = 0;
-            if (greedy) {
+            if (greedy && Mt) {
+                // MTP round: the drafter's steps chain their tokens into the verify pass's step
+                // parameters on the device. Its query sits at the pending token's position and
+                // attends the keys the target has processed (positions up to len - 2).
+                StepParams tp{}, mp{};
+                tp.base_pos = (int)len - 1;
+                tp.tokens[0] = pending;
+                mp.base_pos = (int)len - 2;
+                mp.tokens[0] = pending;
+                mp.aux = mtp_row_;
+                const bool replay = !opt.replay.empty();
+                T.push_params(0, tp);
+                Mt->push_params(1, mp, 1);
+                uint32_t* chain = replay ? Mt->chain_dev() : T.step_params(0)->tokens + 1;
+                for (uint32_t s = 0; s + 1 < K; ++s)
+                    Mt->enqueue(1, s == 0 ? PassKind::MtpFirst : PassKind::MtpNext, false, chain);
+                if (replay) {
+                    for (uint32_t s = 0; s + 1 < K; ++s)
+                        tp.tokens[s + 1] = replay_propose(opt.replay, prompt.size(), len + s, opt.mismatch_rate,
+                                                          opt.mismatch_seed, V);
+                    T.push_params(0, tp);
+                }
+                T.enqueue((int)K, PassKind::Plain, false, nullptr);
+                const HeadResult r = T.fetch_result();
+                n_acc = (uint32_t)r.n_accepted;
+                emitted_now.assign(r.tokens, r.tokens + r.n_emit);
+            } else if (greedy) {
+                DraftRuntime& D = *Dp;
                 StepParams tp{}, dp{};
                 tp.base_pos = (int)len - 1;
                 tp.tokens[0] = pending;
@@ -253,7 +286,16 @@ std::vector<uint32_t> Engine::generate(const std::vector<uint32_t>& prompt, cons
                 uint32_t cur = pending;
                 int pos = (int)len - 1;
                 for (uint32_t s = 0; s + 1 < K; ++s) {
-                    Dm.run_plain(1, pos++, &cur, true);
+                    if (Mt) {
+                        StepParams mp{};
+                        mp.base_pos = (int)len - 2;
+                        mp.tokens[0] = cur;
+                        mp.aux = mtp_row_;
+                        Mt->push_params(1, mp, 1);
+                        Mt->enqueue(1, s == 0 ? PassKind::MtpFirst : PassKind::MtpNext, true, nullptr);
+                    } else {
+                        Dm.run_plain(1, pos++, &cur, true);
+                    }
                     dl.resize(V);
                     cuda_check(cudaMemcpyAsync(dl.data(), Dm.logits_dev(), V * 4, cudaMemcpyDeviceToHost, Dm.stream()),
                                "logits");
@@ -295,7 +337,8 @@ std::vector<uint32_t> Engine::generate(const std::vector<uint32_t>& prompt, cons
                     break;
                 }
             }
-            D.accept(history.size() - 1, forwarded);
+            if (Dp) Dp->accept(history.size() - 1, forwarded);
+            mtp_row_ = (int)n_acc;  // the verify row whose logits gave the round's last token
             ++stats_.rounds;
             stats_.drafted += K - 1;
             stats_.accepted += n_acc;

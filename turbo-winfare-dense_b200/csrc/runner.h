@@ -86,6 +86,9 @@ class Engine {
     DeviceModel& target() { return *target_; }
     DraftRuntime* draft() { return draft_.get(); }
     void set_draft(std::unique_ptr<DeviceModel> d) { draft_ = std::make_unique<DraftRuntime>(std::move(d)); }
+    // The MTP assistant drafter: a DeviceModel loaded with load_mtp*, on the target's stream.
+    void set_mtp(std::unique_ptr<DeviceModel> m) { mtp_ = std::move(m); }
+    DeviceModel* mtp() { return mtp_.get(); }
 
     // One pass over `batch` consecutive positions from base_position (runner.hpp:110-111).
     // out_logits (host) receives the last row's logits, or all rows' when all_positions.
@@ -106,6 +109,8 @@ class Engine {
 
     std::unique_ptr<DeviceModel> target_;
     std::unique_ptr<DraftRuntime> draft_;
+    std::unique_ptr<DeviceModel> mtp_;
+    int mtp_row_ = 0;  // row of the target's normed hidden states the next MTP round starts from
     cudaEvent_t order_ev_[2] = {nullptr, nullptr};
     int order_i_ = 0;
     int last_row_ = 0;  // device logits row of the last pass's final position

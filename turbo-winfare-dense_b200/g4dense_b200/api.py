@@ -77,6 +77,7 @@ def _bind_engine(L):
     L.g4dense_engine_set_decode_options.argtypes = [_vp, ctypes.c_longlong, ctypes.c_int, _vp, ctypes.c_int,
                                                     ctypes.c_double, ctypes.c_ulonglong]
     L.g4dense_engine_set_device_sampling.argtypes = [_vp, ctypes.c_int]
+    L.g4dense_engine_mtp_draft.argtypes = [_vp, ctypes.c_uint, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, _vp]
     L.g4b_sample_workspace.restype = ctypes.c_size_t
     L.g4b_sample_token.argtypes = [_vp, ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.c_int,
                                    ctypes.c_uint64, _vp, _vp, _vp]
@@ -277,6 +278,15 @@ class Engine:
         if rc:
             _eng_err("g4dense_engine_forward_batch")
         return out
+
+    def mtp_draft(self, seed_token, context_length, hidden_row, k, vocab):
+        """Greedy MTP drafting from the target's current state: (tokens [k], logits [k][vocab])."""
+        toks = np.zeros(k, np.uint32)
+        logits = np.zeros((k, vocab), np.float32)
+        if lib().g4dense_engine_mtp_draft(self.h, seed_token, context_length, hidden_row, k,
+                                          toks.ctypes.data_as(_vp), logits.ctypes.data_as(_vp)):
+            _eng_err("g4dense_engine_mtp_draft")
+        return toks, logits
 
     STAT_KEYS = ("emitted", "decode_gpu_ms", "ttft_ms", "total_ms", "drafted", "accepted", "rounds",
                  "gated_steps", "launches", "h2d_bytes", "d2h_bytes", "decode_wall_ms")

@@ -95,6 +95,122 @@ E2B_DRAFT = ModelSpec(num_layers=35, d_model=1536, d_ff=6144, num_q_heads=8, num
                       head_dim=256, vocab_size=262144, sliding_window=512)
 
 
+# A target with both layer kinds at config-0 scale: the MTP drafter's tests need a sliding and a
+# full-attention donor layer (the 31B's last two layers play that part for its assistant).
+MTP_TEST_TARGET = ModelSpec(num_layers=4, d_model=256, d_ff=1024, num_q_heads=4, num_kv_heads=2,
+                            head_dim=64, vocab_size=4096, sliding_window=64, global_layer_mask=0b1000,
+                            global_head_dim=128, global_kv_heads=1)
+
+
+# ---------------------------------------------------------------- .g4mtp (MTP assistant drafter)
+
+MTP_MAGIC = 0x47344D54  # 'G4MT'
+MTP_VERSION = 1
+MTP_MAX_LAYERS = 8
+# G4MtpHeader, include/g4dense/format.hpp:143-180 (packed, 4096 bytes).
+MTP_HEADER_FMT = "<14IQ2I8Q8Q8Q32s3800s"
+
+
+@dataclasses.dataclass
+class MtpSpec:
+    """Geometry of a Gemma-4 "assistant" MTP drafter (.g4mtp). The attention geometry must equal
+    its target's donor layers: num_kv_heads/head_dim those of the target's sliding layers,
+    global_kv_heads/global_head_dim those of its full-attention layers."""
+    num_layers: int
+    backbone: int          # the target's d_model
+    hidden: int
+    intermediate: int
+    vocab_size: int
+    num_q_heads: int
+    num_kv_heads: int
+    head_dim: int
+    global_head_dim: int
+    global_kv_heads: int
+    sliding_window: int = 1024
+    global_layer_mask: int = 0
+
+    @classmethod
+    def for_target(cls, t: ModelSpec, num_layers=4, hidden=128, intermediate=512, num_q_heads=4, global_mask=None):
+        return cls(num_layers=num_layers, backbone=t.d_model, hidden=hidden, intermediate=intermediate,
+                   vocab_size=t.vocab_size, num_q_heads=num_q_heads, num_kv_heads=t.num_kv_heads,
+                   head_dim=t.head_dim, global_head_dim=t.global_head_dim or 512,
+                   global_kv_heads=t.global_kv_heads or 4, sliding_window=t.sliding_window,
+                   global_layer_mask=(1 << (num_layers - 1)) if global_mask is None else global_mask)
+
+    def q_head_dim(self, l: int) -> int:
+        return self.global_head_dim if (self.global_layer_mask >> l) & 1 else self.head_dim
+
+
+# The 31B's assistant (tools/convert_hf_assistant.py:49-66 defaults): 4 layers, the last one
+# full-attention.
+GEMMA4_31B_ASSISTANT = MtpSpec(num_layers=4, backbone=5376, hidden=1024, intermediate=8192, vocab_size=262144,
+                               num_q_heads=32, num_kv_heads=16, head_dim=256, global_head_dim=512,
+                               global_kv_heads=4, sliding_window=1024, global_layer_mask=0b1000)
+
+
+def build_mtp_container(spec: MtpSpec, seed: int = 0, centered: bool = False) -> bytes:
+    """Full .g4mtp bytes: header, embedding (tied LM head) [V][hidden], pre-projection
+    [hidden][2*backbone], post-projection [backbone][hidden], final norm [hidden], then the layers
+    (tools/convert_hf_assistant.py:114-176; per-layer layout of src/mtp_runner.cpp:175-234: four
+    [hidden] norms, q_norm [q_head_dim], layer_scalar, then q, o, gate, up, down, each 16-byte
+    aligned). Every section is padded to 4096 bytes."""
+    rng = np.random.default_rng(seed)
+    h, bb, I, V = spec.hidden, spec.backbone, spec.intermediate, spec.vocab_size
+
+    def block(rows, cols):
+        p, s_, b_ = random_quant_block(rng, rows, cols, centered)
+        return p.tobytes() + s_.tobytes() + b_.tobytes()
+
+    sections = []
+    for rows, cols in [(V, h), (h, 2 * bb), (bb, h)]:
+        sec = bytearray(block(rows, cols))
+        _pad(sec, ALIGNMENT)
+        sections.append(bytes(sec))
+    norm = bytearray(_norm(rng, h).tobytes())
+    _pad(norm, ALIGNMENT)
+    sections.append(bytes(norm))
+    scalar = f32_to_bf16_bits(np.array([1.0 / np.sqrt(2.0 * spec.num_layers)], dtype=np.float32))
+    layers = []
+    for l in range(spec.num_layers):
+        qhd = spec.q_head_dim(l)
+        qd = spec.num_q_heads * qhd
+        ld = bytearray()
+        for _ in range(4):
+            ld += _norm(rng, h).tobytes()
+        ld += _norm(rng, qhd).tobytes()
+        ld += scalar.tobytes()
+        for rows, cols in [(qd, h), (h, qd), (I, h), (I, h), (h, I)]:
+            _pad(ld, 16)
+            ld += block(rows, cols)
+        _pad(ld, ALIGNMENT)
+        layers.append(bytes(ld))
+    offs, cur = [], HEADER_SIZE
+    for sec in sections:
+        offs.append((cur, len(sec)))
+        cur += len(sec)
+    lo, ls = [0] * MTP_MAX_LAYERS, [0] * MTP_MAX_LAYERS
+    for l, ld in enumerate(layers):
+        lo[l], ls[l] = cur, len(ld)
+        cur += len(ld)
+    payload = b"".join(sections) + b"".join(layers)
+    header = struct.pack(
+        MTP_HEADER_FMT, MTP_MAGIC, MTP_VERSION, QUANT_AFFINE_INT4_G64, spec.num_layers, bb, h, I, V,
+        spec.num_q_heads, spec.num_kv_heads, spec.head_dim, spec.global_head_dim, spec.global_kv_heads,
+        spec.sliding_window, spec.global_layer_mask, GROUP, 1, offs[0][0], offs[0][1], offs[1][0], offs[1][1],
+        offs[2][0], offs[2][1], offs[3][0], offs[3][1], *lo, *ls, hashlib.sha256(payload).digest(), b"\x00" * 3800)
+    assert len(header) == HEADER_SIZE
+    return header + payload
+
+
+def write_mtp_container(path, spec: MtpSpec, seed: int = 0, centered: bool = False) -> Path:
+    path = Path(path)
+    path.parent.mkdir(parents=True, exist_ok=True)
+    tmp = path.with_suffix(path.suffix + ".tmp")
+    tmp.write_bytes(build_mtp_container(spec, seed, centered))
+    tmp.replace(path)
+    return path
+
+
 def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
     """Round-to-nearest-even float32 -> bf16 bit patterns (uint16)."""
     u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
