@@ -328,6 +328,7 @@ def mtp_drafter(eng, prompt, stream, args):
     drafter of the 31B assistant's geometry: 4 layers, hidden 1024, attending the target's last
     sliding and full-attention layers) in place of the E2B-shaped one. Same oracle drafter and
     mismatch rate, so only the drafting cost differs."""
+    from g4dense_b200 import Engine
     eng.close()
     m = Engine(preset="gemma4-31b", seed=0, draft_preset="gemma4-31b-assistant", draft_seed=2,
                draft_k=VERIFY_WIDTH, max_context=4096)

@@ -125,7 +125,7 @@ g4b::GenerationOptions to_gen(const EngineHandle* e, const G4DenseGenerationOpti
         g.sampling.has_seed = o->has_seed != 0;
         g.sampling.seed = o->seed;
     }
-    g.speculative_enabled = e->draft_k > 0 && e->engine->draft() != nullptr;
+    g.speculative_enabled = e->draft_k > 0 && (e->engine->draft() != nullptr || e->engine->mtp() != nullptr);
     g.draft_k = (uint32_t)std::max(0, e->draft_k);
     g.stop_token = e->stop_token;
     g.replay = e->replay;
