@@ -80,13 +80,17 @@ def test_device_draw_rejects_bad_arguments(built_lib):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("params", [(0.8, 1.0, 0), (0.7, 0.9, 40), (1.5, 1.0, 4)])
+@pytest.mark.parametrize("params", [(0.8, 1.0, 0, 1.0), (0.7, 0.9, 40, 1.0), (1.5, 1.0, 4, 1.0),
+                                    (0.9, 1.0, 0, 1.3), (1.2, 0.95, 64, 0.8)])
 def test_sampled_loop_device_equals_host(built_lib, config0, params):
-    t, p, k = params
+    """The device draw (with the repetition penalty applied on the device when it is not 1)
+    against the host draw over the copied logits row: the same stream."""
+    t, p, k, pen = params
     prompt = np.random.default_rng(11).integers(0, 4096, 20)
+    prompt[5:9] = prompt[0]  # repeated ids: the penalty compounds
     e = engine(config0["target_centered"])
-    dev = e.generate(prompt, 40, temperature=t, top_p=p, top_k=k, seed=17)
+    dev = e.generate(prompt, 40, temperature=t, top_p=p, top_k=k, seed=17, repetition_penalty=pen)
     e.set_device_sampling(False)
-    host = e.generate(prompt, 40, temperature=t, top_p=p, top_k=k, seed=17)
+    host = e.generate(prompt, 40, temperature=t, top_p=p, top_k=k, seed=17, repetition_penalty=pen)
     assert dev.tolist() == host.tolist()
     e.close()

@@ -67,6 +67,13 @@ size_t g4b_sample_workspace_bytes();
 cudaError_t g4b_sample_launch(const float* logits, int V, float temperature, float top_p, int top_k,
                               unsigned long long seed, void* work, unsigned* out, cudaStream_t st);
 
+// Repetition penalty on a device logits row from history counts (count [V], the distinct ids
+// ids[0..*n)), and appending tokens (device ids) to those counts.
+cudaError_t g4b_rep_penalty(float* logits, const uint32_t* count, const uint32_t* ids, const int* n, float penalty,
+                            float limit, cudaStream_t st);
+cudaError_t g4b_rep_append(uint32_t* count, uint32_t* ids, int* n, const uint32_t* toks, int ntok, int V,
+                           cudaStream_t st);
+
 // ---- side.cu: INT8 G64 GEMV (one row per warp) and the attention output gate
 namespace g4b {
 cudaError_t gemv_int8_launch(const uint8_t* W, const uint16_t* S, const uint16_t* B, const float* x, float* out,

@@ -856,17 +856,47 @@ void DeviceModel::run_plain(int M, int base_pos, const uint32_t* tokens, bool wa
     enqueue(M, PassKind::Plain, want_logits, nullptr);
 }
 
-uint32_t DeviceModel::sample_device(int row, float temperature, float top_p, int top_k, uint64_t seed) {
+void DeviceModel::rep_reset(const uint32_t* toks, int n) {
+    const int V = v_local_;
+    if (!rep_count_) {
+        rep_count_ = static_cast<uint32_t*>(dmalloc((size_t)V * 4));
+        rep_ids_ = static_cast<uint32_t*>(dmalloc((size_t)V * 4));
+        rep_stage_ = static_cast<uint32_t*>(dmalloc((size_t)opt_.max_context * 4));
+        rep_n_ = static_cast<int*>(dmalloc(sizeof(int)));
+    }
+    if (n > opt_.max_context) throw std::invalid_argument("repetition history exceeds the context");
+    cuda_check(cudaMemsetAsync(rep_count_, 0, (size_t)V * 4, stream_), "memset");
+    cuda_check(cudaMemsetAsync(rep_n_, 0, sizeof(int), stream_), "memset");
+    cuda_check(cudaMemcpyAsync(rep_stage_, toks, (size_t)n * 4, cudaMemcpyHostToDevice, stream_), "history");
+    h2d_bytes_ += (uint64_t)n * 4;
+    cuda_check(g4b_rep_append(rep_count_, rep_ids_, rep_n_, rep_stage_, n, V, stream_), "history");
+    cuda_check(cudaStreamSynchronize(stream_), "history");  // the pageable source may be reused
+}
+
+uint32_t DeviceModel::sample_device(int row, float temperature, float top_p, int top_k, uint64_t seed,
+                                    float penalty) {
     if (opt_.tp > 1) throw std::runtime_error("device sampling needs the full vocabulary on one rank");
     if (!sample_work_) {
         sample_work_ = dmalloc(g4b_sample_workspace_bytes());
         sample_out_ = static_cast<uint32_t*>(dmalloc(sizeof(uint32_t)));
     }
     const int V = v_local_;
+    const bool pen = penalty != 1.0f;
+    if (pen && !rep_count_) throw std::runtime_error("repetition penalty without a history (rep_reset)");
+    if (pen) {
+        const float cap = h_.final_logit_softcapping;
+        cuda_check(g4b_rep_penalty(logits_ + (size_t)row * V, rep_count_, rep_ids_, rep_n_, penalty,
+                                   cap > 0.f ? cap * 0.9999f : 0.f, stream_),
+                   "repetition penalty");
+    }
     cuda_check(g4b_sample_launch(logits_ + (size_t)row * V, V, temperature, top_p, top_k, seed, sample_work_,
                                  sample_out_, stream_),
                "sample");
     launches_ += 2;
+    if (pen) {
+        cuda_check(g4b_rep_append(rep_count_, rep_ids_, rep_n_, sample_out_, 1, V, stream_), "history");
+        launches_ += 2;
+    }
     cuda_check(cudaMemcpyAsync(&res_host_->tokens[0], sample_out_, sizeof(uint32_t), cudaMemcpyDeviceToHost, stream_),
                "sampled token");
     d2h_bytes_ += sizeof(uint32_t);

@@ -117,7 +117,11 @@ class DeviceModel {
     // Draws a token on the device from logits row `row` of the last pass that asked for logits
     // (sample_token, src/sampling.cpp:92-169, with the given seed) and returns it (synchronizes
     // the stream; 4 bytes come back instead of the logits row).
-    uint32_t sample_device(int row, float temperature, float top_p, int top_k, uint64_t seed);
+    // With penalty != 1 the row is first penalised for the history set by rep_reset and the
+    // draws since (apply_repetition_penalty, src/sampling.cpp:74-90), and the drawn token joins it.
+    uint32_t sample_device(int row, float temperature, float top_p, int top_k, uint64_t seed, float penalty = 1.0f);
+    // Sets the device-side repetition history to `toks` (the prompt).
+    void rep_reset(const uint32_t* toks, int n);
     void check_device_error();  // throws if a kernel's bounded wait gave up
     void clear_kv();
 
@@ -200,6 +204,8 @@ class DeviceModel {
     float* logits_ = nullptr;
     void* sample_work_ = nullptr;      // device sampler workspace (allocated on first use)
     uint32_t* sample_out_ = nullptr;   // device: the sampled token
+    uint32_t *rep_count_ = nullptr, *rep_ids_ = nullptr, *rep_stage_ = nullptr;  // repetition history
+    int* rep_n_ = nullptr;
     HeadResult* res_dev_ = nullptr;
     StepParams* sp_dev_ = nullptr;
     uint32_t* chain_dev_ = nullptr;

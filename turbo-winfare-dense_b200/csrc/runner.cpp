@@ -140,7 +140,7 @@ std::vector<uint32_t> Engine::generate(const std::vector<uint32_t>& prompt, cons
         draft_->reset();
         draft_->catch_up(history);
     }
-    const bool dev_sample = !greedy && !spec && opt.device_sampling && sp.repetition_penalty == 1.0f;
+    const bool dev_sample = !greedy && !spec && opt.device_sampling;
     const uint32_t first = prefill(history, opt, dev_sample ? nullptr : &logits);
     if (spec && draft_) order(draft_->model().stream(), T.stream());  // decode starts after both prefills
     mtp_row_ = last_row_;  // the MTP drafter's first round starts from the prompt's last hidden state
@@ -365,7 +365,9 @@ std::vector<uint32_t> Engine::generate(const std::vector<uint32_t>& prompt, cons
             const int pos = (int)history.size() - 1;
             uint32_t nx = next_greedy;
             if (dev_sample) {
-                nx = T.sample_device(last_row_, sp.temperature, sp.top_p, sp.top_k, seed_for(sp, pos));
+                if (step == 0 && sp.repetition_penalty != 1.0f) T.rep_reset(history.data(), (int)history.size());
+                nx = T.sample_device(last_row_, sp.temperature, sp.top_p, sp.top_k, seed_for(sp, pos),
+                                     sp.repetition_penalty);
             } else if (!greedy) {
                 if (sp.repetition_penalty != 1.0f)
                     apply_repetition_penalty(logits.data(), V, history, sp.repetition_penalty,

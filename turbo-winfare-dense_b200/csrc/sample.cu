@@ -24,6 +24,7 @@
 #include <cuda_runtime.h>
 
 #include <cmath>
+#include <algorithm>
 #include <cstdint>
 
 #include "kernels.h"
@@ -213,9 +214,52 @@ __global__ void __launch_bounds__(256) sample_finish_kernel(const float* __restr
     }
 }
 
+// Repetition penalty (apply_repetition_penalty, src/sampling.cpp:74-90) on the device. The
+// reference walks the history in order and, for every occurrence of an id, divides a positive
+// logit by the penalty (or multiplies a negative one), clamping to +-0.9999 * softcap. Each id's
+// value depends only on its own occurrences, so applying the step count[id] times to every
+// distinct id gives the same floats in any id order.
+__global__ void rep_penalty_kernel(float* __restrict__ logits, const uint32_t* __restrict__ count,
+                                   const uint32_t* __restrict__ ids, const int* __restrict__ n, float penalty,
+                                   float limit) {
+    const int nd = *n;
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < nd; i += gridDim.x * blockDim.x) {
+        const uint32_t id = ids[i];
+        float v = logits[id];
+        for (uint32_t k = count[id]; k > 0; --k) {
+            v = (v > 0.0f) ? (v / penalty) : (v * penalty);
+            if (limit > 0.0f) v = fminf(fmaxf(v, -limit), limit);
+        }
+        logits[id] = v;
+    }
+}
+
+// Adds tokens to the history counts; an id seen for the first time joins the distinct list.
+__global__ void rep_append_kernel(uint32_t* __restrict__ count, uint32_t* __restrict__ ids, int* __restrict__ n,
+                                  const uint32_t* __restrict__ toks, int ntok, int V) {
+    for (int i = blockIdx.x * blockDim.x + threadIdx.x; i < ntok; i += gridDim.x * blockDim.x) {
+        const uint32_t id = toks[i];
+        if (id >= (uint32_t)V) continue;  // out-of-range ids are ignored, as in the reference
+        if (atomicAdd(&count[id], 1u) == 0u) ids[atomicAdd(n, 1)] = id;
+    }
+}
+
 }  // namespace g4b
 
 using namespace g4b;
+
+cudaError_t g4b_rep_penalty(float* logits, const uint32_t* count, const uint32_t* ids, const int* n, float penalty,
+                            float limit, cudaStream_t st) {
+    rep_penalty_kernel<<<64, 256, 0, st>>>(logits, count, ids, n, penalty, limit);
+    return cudaGetLastError();
+}
+
+cudaError_t g4b_rep_append(uint32_t* count, uint32_t* ids, int* n, const uint32_t* toks, int ntok, int V,
+                           cudaStream_t st) {
+    if (ntok <= 0) return cudaSuccess;
+    rep_append_kernel<<<std::min(148, (ntok + 255) / 256), 256, 0, st>>>(count, ids, n, toks, ntok, V);
+    return cudaGetLastError();
+}
 
 size_t g4b_sample_workspace_bytes() { return sizeof(SampleWork); }
 

@@ -245,12 +245,13 @@ class Engine:
         if lib().g4dense_engine_set_device_sampling(self.h, 1 if on else 0):
             _eng_err("g4dense_engine_set_device_sampling")
 
-    def generate(self, prompt, max_tokens, temperature=0.0, top_p=1.0, top_k=0, seed=None, callback=None):
+    def generate(self, prompt, max_tokens, temperature=0.0, top_p=1.0, top_k=0, seed=None, callback=None,
+                 repetition_penalty=1.0):
         o = GenOptions()
         lib().g4dense_options_default(ctypes.byref(o))
         o.max_tokens = max_tokens
         o.temperature, o.top_p, o.top_k = temperature, top_p, top_k
-        o.repetition_penalty = 1.0
+        o.repetition_penalty = repetition_penalty
         o.has_seed = 0 if seed is None else 1
         o.seed = 0 if seed is None else seed
         p = np.ascontiguousarray(prompt, np.uint32)
