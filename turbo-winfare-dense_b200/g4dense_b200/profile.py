@@ -1,10 +1,11 @@
 """Profiling drivers: run one piece of the hot path inside a CUDA profiler range so an external
 profiler started with `--profile-from-start off` sees exactly that piece.
 
-    python -m g4dense_b200.profile pass  --which target|draft --batch M --pos P [--layers L]
+    python -m g4dense_b200.profile pass  --which target|draft|mtp --batch M --pos P [--layers L]
         one forward pass of the 31B-shaped target (or the E2B-shaped drafter) with M rows at
         positions P..P+M-1 (attention spans P earlier cache entries), after 5 timed warm
-        passes; prints their mean CUDA-event time.
+        passes; prints their mean CUDA-event time. `mtp`: one step of the 31B assistant's MTP
+        drafter (M = 1) attending the target's P cached positions.
     python -m g4dense_b200.profile gemms [--only NAME] [--batch M]
         each distinct verify-GEMM shape of the 31B pass once (the kernel as the pass runs it:
         split-K slots left for the consuming epilogue), through the g4b_qmat C-ABI.
@@ -41,15 +42,20 @@ def _profiler():
 
 def run_pass(which, batch, pos, layers=0):
     from .api import Engine
+    slot = 0
     if which == "target":
         preset = "gemma4-31b" + (f":layers={layers}" if layers else "")
         e = Engine(preset=preset, seed=0, max_context=4096, device=0)
+    elif which == "mtp":
+        e = Engine(preset="gemma4-31b", seed=0, draft_preset="gemma4-31b-assistant", draft_seed=2, max_context=4096,
+                   device=0)
+        slot = 2
     else:
         e = Engine(preset="gemma4-e2b", seed=1, max_context=4096, device=0)
-    ms = e.time_pass(0, batch, 5, pos=pos)
+    ms = e.time_pass(slot, batch, 5, pos=pos)
     start, stop = _profiler()
     start()
-    e.time_pass(0, batch, 1, pos=pos)
+    e.time_pass(slot, batch, 1, pos=pos)
     stop()
     e.close()
     print(json.dumps({"which": which, "batch": batch, "pos": pos, "ms_per_pass": ms}))
@@ -132,7 +138,7 @@ def main(argv=None):
     ap = argparse.ArgumentParser(prog="python -m g4dense_b200.profile")
     sub = ap.add_subparsers(dest="cmd", required=True)
     p = sub.add_parser("pass")
-    p.add_argument("--which", choices=["target", "draft"], default="target")
+    p.add_argument("--which", choices=["target", "draft", "mtp"], default="target")
     p.add_argument("--batch", type=int, default=5)
     p.add_argument("--pos", type=int, default=768)
     p.add_argument("--layers", type=int, default=0, help="target layers (0 = all 60); a small case for ncu")
