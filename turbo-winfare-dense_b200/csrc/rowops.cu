@@ -9,7 +9,7 @@
 //   rowepi       post-attention: h += rmsnorm(o)*w_post_attn; x = rmsnorm(h)*w_pre_ffn
 //                (:560-567); post-FFN: h = (h + rmsnorm(down)*w_post_ffn) * layer_scalar,
 //                then the next layer's input norm or the final norm (:583-629). One CTA
-//                (narrow rows) or one 16-CTA cluster (wide rows, DSMEM reduction) per row:
+//                (narrow rows) or one 12-CTA cluster (wide rows, DSMEM reduction) per row:
 //                slot sums and statistics, the two RMS factors, then every column.
 //   geglu        gelu_tanh(gate) * up (:568-581, GeGLU.hlsl)
 #include <cooperative_groups.h>
@@ -207,15 +207,17 @@ __global__ void __launch_bounds__(256, 3) qkv_epi_kernel(QkvEpiArgs a) {
 // ---------------------------------------------------------------- norm/residual epilogues
 
 // Narrow rows (d <= 1024, and prefill rows up to d = 6144): one CTA per row, the statistics
-// reduced in the CTA. Wider verify rows: one 16-CTA cluster per row; CTA r owns groups
-// [r*gpc, (r+1)*gpc) (gpc = ceil(groups / 16)), each warp up to kEpiGroupsPerWarp of them, and
+// reduced in the CTA. Wider verify rows: one 12-CTA cluster per row; CTA r owns groups
+// [r*gpc, (r+1)*gpc) (gpc = ceil(groups / 12)), each warp up to kEpiGroupsPerWarp of them, and
 // the cluster adds the CTA sums in rank order through distributed shared memory, so every CTA
 // derives the same two RMS factors. In both forms a warp holds its columns in registers from
 // start to finish: phase 1 sums the split-K slots and the sums of y^2, h^2, h*c and c^2
 // (c = y * w1); phase 2 finishes the columns.
-constexpr int kEpiClusters = 16;     // non-portable cluster size (B200 allows 16)
+// 12 CTAs: measured against 8 and 16 on the 31B verify pass and the E2B drafter step (both
+// about 0.6 % faster than with 16); a non-portable size, which B200 allows up to 16.
+constexpr int kEpiClusters = 12;
 constexpr int kEpiWarps = 8;         // warps per CTA in the cluster form
-constexpr int kEpiGroupsPerWarp = 2;  // d <= 16 CTAs x 8 warps x 2 groups x 64 = 16384
+constexpr int kEpiGroupsPerWarp = 2;  // d <= 12 CTAs x 8 warps x 2 groups x 64 = 12288
 constexpr int kEpiMaxWarps = 32;
 
 __device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
@@ -575,12 +577,12 @@ cudaError_t g4b_rowepi(const GemmOut& o, const TpGather& tg, const float* h_in, 
     if (tg.n < 1 || tg.n > kMaxTp) return cudaErrorInvalidValue;
     const int ngp = (d + 127) / 128 * 2;
     // Rows of up to 16 groups (d <= 1024): one CTA per row, one warp per group. Wider verify
-    // rows spread their slot sums over a 16-CTA cluster (measured faster from d = 1536 up).
+    // rows spread their slot sums over a 12-CTA cluster (measured faster from d = 1536 up).
     if (ngp <= 16)
         return launch(rowepi_kernel<false>, dim3(1, M), dim3(ngp * 32), 0, st, pdl, o, tg, h_in, h_out, w1, out_scale,
                       w2, d, bfrag, M, frag_row0, x_out);
     // A prefill chunk has rows enough to fill the GPU: one CTA per row (each warp up to three
-    // groups) instead of a 16-CTA cluster per row.
+    // groups) instead of a 12-CTA cluster per row.
     if (M > kMaxM && ngp <= kEpiMaxWarps)
         return launch(rowepi_kernel<false>, dim3(1, M), dim3(ngp * 32), 0, st, pdl, o, tg, h_in, h_out, w1, out_scale,
                       w2, d, bfrag, M, frag_row0, x_out);
