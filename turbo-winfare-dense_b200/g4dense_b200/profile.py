@@ -2,6 +2,7 @@
 profiler started with `--profile-from-start off` sees exactly that piece.
 
     python -m g4dense_b200.profile pass  --which target|draft|mtp --batch M --pos P [--layers L]
+                                         [--ctx C] [--kv-bf16]
         one forward pass of the 31B-shaped target (or the E2B-shaped drafter) with M rows at
         positions P..P+M-1 (attention spans P earlier cache entries), after 5 timed warm
         passes; prints their mean CUDA-event time. `mtp`: one step of the 31B assistant's MTP
@@ -40,12 +41,12 @@ def _profiler():
     return cu.cuProfilerStart, cu.cuProfilerStop
 
 
-def run_pass(which, batch, pos, layers=0):
+def run_pass(which, batch, pos, layers=0, ctx=4096, kv_bf16=False):
     from .api import Engine
     slot = 0
     if which == "target":
         preset = "gemma4-31b" + (f":layers={layers}" if layers else "")
-        e = Engine(preset=preset, seed=0, max_context=4096, device=0)
+        e = Engine(preset=preset, seed=0, max_context=ctx, kv_bf16=kv_bf16, device=0)
     elif which == "mtp":
         e = Engine(preset="gemma4-31b", seed=0, draft_preset="gemma4-31b-assistant", draft_seed=2, max_context=4096,
                    device=0)
@@ -139,6 +140,8 @@ def main(argv=None):
     sub = ap.add_subparsers(dest="cmd", required=True)
     p = sub.add_parser("pass")
     p.add_argument("--which", choices=["target", "draft", "mtp"], default="target")
+    p.add_argument("--ctx", type=int, default=4096, help="KV capacity (target)")
+    p.add_argument("--kv-bf16", action="store_true", help="bf16 KV cache (target, long-context mode)")
     p.add_argument("--batch", type=int, default=5)
     p.add_argument("--pos", type=int, default=768)
     p.add_argument("--layers", type=int, default=0, help="target layers (0 = all 60); a small case for ncu")
@@ -151,7 +154,7 @@ def main(argv=None):
     pg.add_argument("--reps", type=int, default=20)
     a = ap.parse_args(argv)
     if a.cmd == "pass":
-        run_pass(a.which, a.batch, a.pos, a.layers)
+        run_pass(a.which, a.batch, a.pos, a.layers, a.ctx, a.kv_bf16)
     elif a.cmd == "pgemm":
         run_pgemm(a.only, a.batch, a.reps)
     else:
