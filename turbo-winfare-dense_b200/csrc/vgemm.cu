@@ -4,7 +4,7 @@
 //
 // The op is HBM-bound (0.5625 B per weight; 3.5-56 flop/B for M = 1..16), so the kernel is
 // organised around streaming the packed weights once at full bandwidth:
-//   * each warp owns a 4-stage ring of 4608-byte k-tile blocks in shared memory, filled by
+//   * each warp owns a 2- or 4-stage ring of 4608-byte k-tile blocks in shared memory, filled by
 //     TMA bulk copies (cp.async.bulk, one per block, completion on a per-stage mbarrier).
 //     The first stages are issued before griddepcontrol.wait, so under programmatic
 //     dependent launch the weight stream starts while the previous kernel is still draining;
@@ -35,7 +35,13 @@ namespace g4b {
 constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
 constexpr int kCtaRows = kWarps * kWarpRows;  // 256
-constexpr int kStages = 3;                    // weight ring depth per warp
+// Weight ring depth per warp, by mode, as measured against 3 stages for both: the packed fp16
+// mode (1..4 rows: the drafter's one-row steps, a few units per CTA) gains from the deeper
+// prefetch before the PDL wait (E2B drafter step 1.411 -> 1.377 ms with 4 stages); the digit
+// modes (5..16 rows) run faster with fewer weight bytes in flight ahead of each CTA (31B 5-row
+// verify pass 6.07 -> 5.84 ms with 2; occupancy stays 3 CTAs per SM, set by registers).
+template <int NT>
+__host__ __device__ constexpr int ring_stages() { return NT == 0 ? 4 : 2; }
 constexpr int kBlockU4 = kKTileBytes / 16;    // 288 uint4 per block
 
 // y[m][crg*256 + j] = sum over slots s = 0..ns-1, in slot order, of part[crg][s][m][j]. One
@@ -117,6 +123,7 @@ template <int NB, int NACC, bool PACKED, int NT>
 __global__ void __launch_bounds__(kThreads, (NACC == 2 || NT == 6) ? 2 : 3) vgemm_kernel(VgemmParams p) {
     extern __shared__ __align__(128) unsigned char smem_raw[];
     using BS = BStage<NB, NACC, NT>;
+    constexpr int kStages = ring_stages<NT>();
     constexpr int kFragU4 = BS::frag_u4;
     constexpr int kGsumF4 = BS::gsum_f4;
     constexpr int kBufU4 = kFragU4 + kGsumF4;
@@ -335,6 +342,7 @@ __global__ void __launch_bounds__(kThreads, (NACC == 2 || NT == 6) ? 2 : 3) vgem
 template <int NB, int NACC, int NT>
 static constexpr size_t smem_bytes() {
     using BS = BStage<NB, NACC, NT>;
+    constexpr int kStages = ring_stages<NT>();
     return (size_t)kWarps * kStages * kKTileBytes + 2 * ((size_t)BS::frag_u4 * 16 + (size_t)BS::gsum_f4 * 16) +
            (kWarps * kStages + 2) * sizeof(uint64_t);
 }
