@@ -35,13 +35,14 @@ namespace g4b {
 constexpr int kWarps = 4;
 constexpr int kThreads = kWarps * 32;
 constexpr int kCtaRows = kWarps * kWarpRows;  // 256
-// Weight ring depth per warp, by mode, as measured against 3 stages for both: the packed fp16
-// mode (1..4 rows: the drafter's one-row steps, a few units per CTA) gains from the deeper
-// prefetch before the PDL wait (E2B drafter step 1.411 -> 1.377 ms with 4 stages); the digit
-// modes (5..16 rows) run faster with fewer weight bytes in flight ahead of each CTA (31B 5-row
-// verify pass 6.07 -> 5.84 ms with 2; occupancy stays 3 CTAs per SM, set by registers).
+// Weight ring depth per warp, by mode, as measured against 3 stages: the packed fp16 mode
+// (1..4 rows: the drafter's one-row steps, a few units per CTA) gains from the deeper prefetch
+// before the PDL wait (E2B drafter step 1.411 -> 1.377 ms with 4 stages); the 5..8-row digit
+// modes run faster with fewer weight bytes in flight ahead of each CTA (31B 5-row verify pass
+// 6.07 -> 5.84 ms with 2; occupancy stays 3 CTAs per SM, set by registers); the 9..16-row mode
+// (2 CTAs per SM) again prefers 4 (9-row pass 9.27 -> 9.00 ms, 16-row 9.50 -> 9.27 ms).
 template <int NT>
-__host__ __device__ constexpr int ring_stages() { return NT == 0 ? 4 : 2; }
+__host__ __device__ constexpr int ring_stages() { return (NT == 0 || NT == 6) ? 4 : 2; }
 constexpr int kBlockU4 = kKTileBytes / 16;    // 288 uint4 per block
 
 // y[m][crg*256 + j] = sum over slots s = 0..ns-1, in slot order, of part[crg][s][m][j]. One
