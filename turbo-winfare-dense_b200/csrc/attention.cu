@@ -577,11 +577,13 @@ static cudaError_t launch_attn(const AttnArgs& a, void* bfrag, cudaStream_t st, 
     // chunk has hundreds of clusters already, so its keys are split in two only, which keeps the
     // per-CTA loops long and the cross-CTA combine cheap.
     int splits = a.M > kMaxM ? 2 : attn_splits<BF16, HD>(a.kvh * chunks);
-    // A sliding layer's key range is bounded by its window whatever the context, so 8 splits
-    // already leave each CTA at most two 64-key tiles of a 1024-key window; more only add
-    // combine work (measured: 31B 5-row verify pass 5.85 -> 5.78 ms, long-context passes
-    // unchanged). Full-attention layers keep the widest split that fits one wave.
-    if (a.window > 0 && a.window <= 1024) splits = std::min(splits, 8);
+    // A sliding layer's key range is bounded by its window whatever the context, so when there
+    // are clusters enough to fill the GPU (8 or more), 8 splits already leave each CTA at most
+    // two 64-key tiles of a 1024-key window; more only add combine work (measured: 31B 5-row
+    // verify pass 5.85 -> 5.78 ms, long-context passes unchanged). With few clusters (the
+    // drafter's single KV head) the wide split stays: capped, a 3-row drafter pass went 1.44 ->
+    // 1.53 ms. Full-attention layers keep the widest split that fits one wave.
+    if (a.window > 0 && a.window <= 1024 && a.kvh * chunks >= 8) splits = std::min(splits, 8);
     cudaLaunchAttribute attr[2];
     cudaLaunchConfig_t cfg = attn_config<BF16, HD>(a, splits, st, attr, pdl);
     return cudaLaunchKernelEx(&cfg, attention_kernel<BF16, HD>, a, bfrag);
