@@ -64,7 +64,7 @@ def check_gemm(N, K, M, seed=0, centered=False, x_scale=1.0):
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("M", [1, 2, 4, 5, 8, 9, 16])
+@pytest.mark.parametrize("M", [1, 2, 4, 5, 8, 9, 10, 11, 16])
 def test_vgemm_small_shapes(built_lib, M):
     # N not a multiple of 256 (partial CTA row group), K with a padded half k-tile.
     check_gemm(320, 192, M, seed=M)
@@ -73,7 +73,7 @@ def test_vgemm_small_shapes(built_lib, M):
 
 @pytest.mark.gpu
 @pytest.mark.parametrize("K,N", [(5376, 1024), (21504, 256), (1536, 6144)])
-@pytest.mark.parametrize("M", [1, 5, 16])
+@pytest.mark.parametrize("M", [1, 5, 9, 16])
 def test_vgemm_model_shapes(built_lib, K, N, M):
     check_gemm(N, K, M, seed=K + N + M)
 

@@ -81,6 +81,7 @@ __host__ __device__ inline BMode bmode_for(int M) {
     if (M <= 4) return {1, 1, true, 0};
     if (M <= 5) return {0, 0, false, 2};
     if (M <= 8) return {0, 0, false, 3};
+    if (M <= 10) return {0, 0, false, 4};
     return {0, 0, false, 6};
 }
 __host__ __device__ inline size_t bfrag_frag_bytes(int K, int M) {
@@ -94,11 +95,17 @@ __host__ __device__ inline size_t bfrag_gsum_bytes(int K, int M) {
 // Digit modes: the (n-tile, column) of digit d of activation row m. Columns are arranged so
 // that the quad thread t holding accumulator columns 2t, 2t+1 holds all three digits of rows
 // t, 4+t (and 8+t, 12+t with six tiles); with two tiles, row 4's digits sit in column 2d+1 of
-// tile 1 (threads 0..2) and are gathered with two shuffles.
+// tile 1 (threads 0..2) and are gathered with two shuffles; with four tiles (9..10 rows), rows
+// 8 and 9 sit in columns 2d and 2d+1 of tile 3 and are gathered the same way.
 __host__ __device__ inline void digit_col(int nt_count, int m, int d, int& nt, int& col) {
     if (nt_count == 2 && m == 4) {
         nt = 1;
         col = 2 * d + 1;
+        return;
+    }
+    if (nt_count == 4 && m >= 8) {  // rows 8 and 9: tile 3, columns 2d (row 8) and 2d+1 (row 9)
+        nt = 3;
+        col = 2 * d + (m - 8);
         return;
     }
     const int blk = m >> 3, mm = m & 7, tt = mm & 3;

@@ -39,8 +39,9 @@ constexpr int kCtaRows = kWarps * kWarpRows;  // 256
 // (1..4 rows: the drafter's one-row steps, a few units per CTA) gains from the deeper prefetch
 // before the PDL wait (E2B drafter step 1.411 -> 1.377 ms with 4 stages); the 5..8-row digit
 // modes run faster with fewer weight bytes in flight ahead of each CTA (31B 5-row verify pass
-// 6.07 -> 5.84 ms with 2; occupancy stays 3 CTAs per SM, set by registers); the 9..16-row mode
-// (2 CTAs per SM) again prefers 4 (9-row pass 9.27 -> 9.00 ms, 16-row 9.50 -> 9.27 ms).
+// 6.07 -> 5.84 ms with 2; occupancy stays 3 CTAs per SM, set by registers; the four-tile
+// 9..10-row mode too: 8.46 ms against 8.57 with 4); the six-tile 11..16-row mode (2 CTAs per SM)
+// again prefers 4 (16-row pass 9.50 -> 9.27 ms).
 template <int NT>
 __host__ __device__ constexpr int ring_stages() { return (NT == 0 || NT == 6) ? 4 : 2; }
 constexpr int kBlockU4 = kKTileBytes / 16;    // 288 uint4 per block
@@ -241,15 +242,16 @@ __global__ void __launch_bounds__(kThreads, (NACC == 2 || NT == 6) ? 2 : 3) vgem
         const int nmax = direct ? p.N - crg * kCtaRows : kCtaRows;
         if constexpr (NT > 0) {
             // Thread t holds activation rows t, 4+t (8+t, 12+t); with two tiles its second
-            // row is row 4, valid on thread 0 only. No 2^24 factor: digits are integers.
+            // row is row 4, with four tiles its third and fourth are rows 8 and 9, valid on
+            // thread 0 only. No 2^24 factor: digits are integers.
 #pragma unroll
             for (int r = 0; r < kTilesPerWarp; ++r)
 #pragma unroll
                 for (int j = 0; j < kJ; ++j)
 #pragma unroll
                     for (int h = 0; h < 2; ++h) {
-                        const int m = (NT == 2 && j == 1) ? 4 : 4 * j + t;
-                        const bool mine = NT != 2 || j == 0 || t == 0;
+                        const int m = (NT == 2 && j == 1) ? 4 : (NT == 4 && j >= 2) ? 6 + j : 4 * j + t;
+                        const bool mine = (NT != 2 || j == 0 || t == 0) && (NT != 4 || j < 2 || t == 0);
                         const int nl = warp * kWarpRows + r * 16 + g + 8 * h;
                         if (act && !failed && mine && m < p.M && nl < nmax) dst[(size_t)m * ld + nl] = accd[r][j][h];
                         accd[r][j][h] = 0.f;
@@ -388,6 +390,7 @@ int vgemm_grid(int M, int n_crg, int ktiles) {
     if (md.packed) per_sm = max_ctas_per_sm<1, 1, true, 0>();
     else if (md.nt == 2) per_sm = max_ctas_per_sm<0, 0, false, 2>();
     else if (md.nt == 3) per_sm = max_ctas_per_sm<0, 0, false, 3>();
+    else if (md.nt == 4) per_sm = max_ctas_per_sm<0, 0, false, 4>();
     else per_sm = max_ctas_per_sm<0, 0, false, 6>();
     const long long T = (long long)n_crg * ktiles;
     return (int)std::min<long long>(T, (long long)sm_count() * per_sm);
@@ -420,5 +423,6 @@ cudaError_t vgemm_launch(const VgemmParams& p, cudaStream_t st, bool pdl) {
     if (md.packed) return launch_t<1, 1, true, 0>(p, st, pdl);
     if (md.nt == 2) return launch_t<0, 0, false, 2>(p, st, pdl);
     if (md.nt == 3) return launch_t<0, 0, false, 3>(p, st, pdl);
+    if (md.nt == 4) return launch_t<0, 0, false, 4>(p, st, pdl);
     return launch_t<0, 0, false, 6>(p, st, pdl);
 }

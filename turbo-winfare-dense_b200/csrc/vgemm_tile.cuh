@@ -101,7 +101,7 @@ __device__ __forceinline__ void mma_u8s8(int (&d)[4], uint32_t a0, uint32_t a1, 
 // Activation rows a quad thread t holds in the digit modes (format 5 of common.cuh).
 template <int NT>
 struct DigitRows {
-    static constexpr int J = NT == 6 ? 4 : 2;
+    static constexpr int J = (NT == 6 || NT == 4) ? 4 : 2;
 };
 
 // Digit modes (M = 5..16): one k-tile for one warp, 4 row tiles x 128 k. The nibble words of
@@ -148,11 +148,12 @@ __device__ __forceinline__ void compute_ktile_digits(const uint4* __restrict__ b
         // Group epilogue. Digit columns of the thread's rows (digit_col in common.cuh):
         // row t: (tile 3b, cols 2t, 2t+1) = d0, d1; (tile 3b+1, col 2t) = d2
         // row 4+t: (tile 3b+1, col 2t+1) = d0; (tile 3b+2, cols 2t, 2t+1) = d1, d2
-        // two tiles: row 4 in (tile 1, col 2d+1) of thread d, gathered by shuffles.
+        // two tiles: row 4 in (tile 1, col 2d+1) of thread d, gathered by shuffles;
+        // four tiles: rows 8, 9 in (tile 3, cols 2d, 2d+1) of thread d, gathered the same way.
         float2 ey[J];
 #pragma unroll
         for (int j = 0; j < J; ++j) {
-            const int m = (NT == 2 && j == 1) ? 4 : 4 * j + t;
+            const int m = (NT == 2 && j == 1) ? 4 : (NT == 4 && j >= 2) ? 6 + j : 4 * j + t;
             ey[j] = gsm[G * kMaxM + m];
         }
 #pragma unroll
@@ -174,6 +175,14 @@ __device__ __forceinline__ void compute_ktile_digits(const uint4* __restrict__ b
                     const int c = ci[r][1][2 * h + 1];  // thread d holds digit d of row 4
                     const int c1 = __shfl_down_sync(0xffffffffu, c, 1), c2 = __shfl_down_sync(0xffffffffu, c, 2);
                     P[1] = fmaf((float)c2, 65536.0f, (float)(c + 256 * c1));
+                }
+                if constexpr (NT == 4) {
+#pragma unroll
+                    for (int q = 0; q < 2; ++q) {  // thread d holds digit d of rows 8 (q = 0) and 9
+                        const int c = ci[r][3][2 * h + q];
+                        const int c1 = __shfl_down_sync(0xffffffffu, c, 1), c2 = __shfl_down_sync(0xffffffffu, c, 2);
+                        P[2 + q] = fmaf((float)c2, 65536.0f, (float)(c + 256 * c1));
+                    }
                 }
 #pragma unroll
                 for (int j = 0; j < J; ++j)
