@@ -115,9 +115,7 @@ def reference_sample(steps, warmup):
     """Times the reference's CpuReferenceRunner on a 2-layer 31B-shaped container."""
     from g4dense_b200 import container as C
     from oracle import oracle as O
-    spec = C.ModelSpec(num_layers=2, d_model=5376, d_ff=21504, num_q_heads=32, num_kv_heads=16, head_dim=256,
-                       vocab_size=262144, sliding_window=1024, global_layer_mask=0b10, global_head_dim=512,
-                       global_kv_heads=4)
+    spec = C.GEMMA4_31B_TWO_LAYERS
     with tempfile.TemporaryDirectory(dir="/tmp") as d:
         path = C.write_container(Path(d) / "b31_2layer.g4dense", spec, seed=0)
         if O.reference_available():
@@ -198,8 +196,7 @@ def run_b200(args, rank, world):
 
     for _ in range(args.warmup):
         one()
-    clk_path = str(REPO / "gpurun_out" / f"clocks_rank{rank}.csv") if (REPO / "gpurun_out").is_dir() else \
-        f"/tmp/g4b_clocks_{rank}.csv"
+    clk_path = f"/tmp/g4b_clocks_{os.getpid()}_{rank}.csv"
     clk = clocks_start(clk_path) if rank == 0 else None
     if world > 1:
         dist.barrier()

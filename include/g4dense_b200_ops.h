@@ -43,19 +43,25 @@ G4B_API int g4b_qmat_run(g4b_qmat* q, int M, float* out, int ldo, void* stream);
 /* The verify GEMM kernel (M <= 16) without its in-kernel split-K sum, leaving the partials in
  * the matrix's workspace (for timing the weight stream alone). */
 G4B_API int g4b_qmat_run_partial(g4b_qmat* q, int M, void* stream);
-/* g4b_qmat_run without any allocation: the same kernel, grid and slot order (bit-identical
- * output), but the split-K scratch -- partial slots and per-row-group arrival counters -- is a
- * fixed static device buffer inside the library (8 MiB of slots, 4096 row groups) instead of the
- * matrix's own workspace. No counterpart in the reference, whose shaders take their scratch from
- * buffers bound by the host. For callers that must not allocate device memory at call time:
- * code running inside a caching allocator's callbacks or on a device whose memory a pool has
- * fully reserved, and latency-sensitive loops where cudaMalloc/cudaFree would synchronize the
- * device. Rejects (non-zero return, message in g4b_last_error) a matrix whose launch at this M
- * needs more than 8 MiB of slots or more than 4096 row groups (N > 1048576). The counters are
- * cleared on `stream` before the launch. The symbol addresses are looked up once per device on
- * the first call; make that first call before any stream capture. The scratch is shared by every
- * caller on a device: overlapping calls (other streams, other threads) race and must be ordered
- * by the caller. */
+/* g4b_qmat_run for M = 1..16 (the verify GEMM only) without any allocation: the same kernel,
+ * grid and slot order (bit-identical output), but the split-K scratch -- partial slots and
+ * per-row-group arrival counters -- is a fixed static device buffer inside the library (8 MiB of
+ * slots, 4096 row groups) instead of the matrix's own workspace. No counterpart in the reference,
+ * whose shaders take their scratch from buffers bound by the host. For callers that must not
+ * allocate device memory at call time: code running inside a caching allocator's callbacks or on
+ * a device whose memory a pool has fully reserved, and latency-sensitive loops where
+ * cudaMalloc/cudaFree would synchronize the device.
+ *   - Rejects (non-zero return, message in g4b_last_error) M outside 1..16 (17..128 rows need
+ *     g4b_qmat_run's tensor-core path), and a matrix whose launch at this M needs more than
+ *     8 MiB of slots or more than 4096 row groups (N > 1048576).
+ *   - The static buffer lives in a module that CUDA loads lazily; loading it reserves its
+ *     device memory. g4b_qmat_create loads it on the matrix's device (it allocates anyway), so
+ *     this call itself allocates nothing. It must run on the device the matrix was created on.
+ *   - The counters are cleared on `stream` before the launch.
+ *   - The scratch is shared by every caller on a device: overlapping calls (other streams,
+ *     other threads) race and must be ordered by the caller.
+ *   - Not valid across a device or primary-context reset: the cached scratch address dies
+ *     with the context. Create the matrix again after a reset. */
 G4B_API int g4b_qmat_run_noalloc(g4b_qmat* q, int M, float* out, int ldo, void* stream);
 /* Synchronizes and reports whether any launch on q hit a bounded-wait timeout. */
 G4B_API int g4b_qmat_check_error(g4b_qmat* q);

@@ -11,6 +11,7 @@ Only tests/, __graft_entry__.smoke() and bench.py's CPU-baseline leg may import 
 from __future__ import annotations
 
 import ctypes
+import os
 import subprocess
 from pathlib import Path
 
@@ -44,9 +45,11 @@ def build_restated() -> Path:
     return RESTATED_SO
 
 
-def build_reference(ref_root: str = "/root/reference") -> Path | None:
-    """Builds oracle/_ref when the reference checkout is present; returns the .so or None."""
-    if Path(ref_root).is_dir():
+def build_reference(ref_root: str | None = None) -> Path | None:
+    """Builds oracle/_ref from the reference checkout `ref_root` (default: the REF_ROOT
+    environment variable) when that directory exists; returns the .so or None."""
+    ref_root = ref_root or os.environ.get("REF_ROOT")
+    if ref_root and Path(ref_root).is_dir():
         subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REF_ROOT={ref_root}"], check=True)
     return REF_SO if REF_SO.exists() else None
 

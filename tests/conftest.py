@@ -43,21 +43,16 @@ def config0(tmp_path_factory):
         "target_centered": C.write_container(d / "target_c.g4dense", C.CONFIG0_TARGET, seed=0, centered=True),
         "draft_centered": C.write_container(d / "draft_c.g4dense", C.CONFIG0_DRAFT, seed=1, centered=True),
     }
+    paths["near_draft"] = C.perturbed_copy(paths["target"], d / "near_draft.g4dense", C.CONFIG0_TARGET, 0.0,
+                                           seed=C.NEAR_DRAFT_SEED, embed_frac=C.NEAR_DRAFT_EMBED_FRAC)
     return paths
-
-
-# Gemma-4-31B attention geometry at toy width: sliding layers with head_dim 256 and GQA 2
-# over a 48-key window (the KV ring wraps), one full-attention layer with head_dim 512, a
-# single KV head (GQA 4) and V taken from the raw K.
-GEOM31 = dict(num_layers=3, d_model=256, d_ff=512, num_q_heads=4, num_kv_heads=2, head_dim=256, vocab_size=4096,
-              sliding_window=48, global_layer_mask=0b010, global_head_dim=512, global_kv_heads=1)
 
 
 @pytest.fixture(scope="session")
 def geom31(tmp_path_factory):
     from g4dense_b200 import container as C
     d = tmp_path_factory.mktemp("geom31")
-    spec = C.ModelSpec(**GEOM31)
+    spec = C.GEOM31_TEST
     return {
         "baseline": C.write_container(d / "g31.g4dense", spec, seed=5),
         "centered": C.write_container(d / "g31_c.g4dense", spec, seed=5, centered=True),

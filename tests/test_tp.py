@@ -1,9 +1,16 @@
-"""Tensor parallelism: 2 ranks, one GPU each, run the config-0 target with query heads, FFN
-columns and the vocabulary split (KV heads replicated where there are fewer than ranks); the
-o-projection and down-projection partials are summed across ranks over peer memory and the LM
-head's per-chunk bests all-gathered over NCCL. Greedy token streams and round records must equal
-the oracle's (the reference has no multi-GPU path; its single-process CPU runner is the oracle).
-A 200-token prompt also runs the tensor-core prefill (chunks of 128 and 72 rows) under TP."""
+"""Tensor parallelism: 2, 4 or 8 ranks, one GPU each, run container.TP_TEST_TARGET (8 query
+heads; 8 KV heads on the sliding layers, split by rank; 2 KV heads on the full-attention layer,
+replicated at TP = 8 as the 31B's four-head global layers are) with query heads, FFN columns and
+the vocabulary split. The o-projection and down-projection partials are summed across ranks over
+peer memory and the LM head's per-chunk bests all-gathered over NCCL.
+
+Zero-mean weights and pinned prompts (container.TP_PINNED*), whose oracle margins along the whole
+stream stay clear of the FP16 K/V rounding noise, so greedy token streams and round records must
+equal the oracle's exactly (the reference has no multi-GPU path; its single-process CPU runner,
+restated in oracle/ and pinned to the reference by tests/test_oracle.py, is the oracle). Cases:
+no drafter; the target drafting for itself (every draft accepted); the config-3 replay drafter at
+a 0.25 mismatch rate (accepts and rejects mixed); and a 300-token prompt that also runs the
+tensor-core prefill (chunks of 128, 128 and 44 rows) under TP."""
 from __future__ import annotations
 
 import json
@@ -28,23 +35,50 @@ def gpu_count():
         return 0
 
 
-@pytest.mark.parametrize("spec,plen", [("no_spec", 24), ("spec_k5", 24), ("spec_k5", 200)])
-def test_tp2_streams_match_oracle(built_lib, config0, tmp_path, spec, plen):
-    if gpu_count() < 2:
-        pytest.skip("needs 2 GPUs")
-    tgt, drf = config0["target"], config0["draft"]
-    n = 48
-    prompt = np.random.default_rng(0).integers(0, 4096, plen)
-    D = O.RestatedModel(drf) if spec == "spec_k5" else None
-    want_tokens, want_rounds = O.spec_generate(O.RestatedModel(tgt), D, prompt, n, verify_width=5)
+@pytest.fixture(scope="module")
+def tp_model(tmp_path_factory):
+    from g4dense_b200 import container as C
+    return C.write_container(tmp_path_factory.mktemp("tp") / "tp_target.g4dense", C.TP_TEST_TARGET,
+                             seed=C.TP_TEST_SEED, centered=True)
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+@pytest.mark.parametrize("case", ["no_spec", "self_k5", "replay_k5", "long_self_k5"])
+def test_tp_streams_match_oracle(built_lib, config0, tp_model, tmp_path, world, case):
+    if gpu_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    from g4dense_b200 import container as C
+    long = case.startswith("long")
+    prompt = C.tp_pinned_prompt(long)
+    n = C.TP_PINNED_LONG[2] if long else C.TP_PINNED[2]
+    T = O.RestatedModel(tp_model)
+    extra, gate = [], 24
+    if case == "no_spec":
+        dpath = None
+    elif case == "replay_k5":
+        dpath = config0["draft_centered"]
+        stream, _ = O.spec_generate(T, None, prompt, n)
+        np.save(tmp_path / "replay.npy", np.asarray(stream, np.uint32))
+        extra, gate = [str(tmp_path / "replay.npy"), "0.25", "9"], -1
+    else:
+        dpath = tp_model
+    D = O.RestatedModel(dpath) if dpath else None
+    want_tokens, want_rounds = O.spec_generate(
+        T, D, prompt, n, verify_width=5, gate_window=gate,
+        replay_stream=stream if extra else None, mismatch_rate=0.25 if extra else 0.0, mismatch_seed=9)
+    if case == "replay_k5":
+        assert any(0 < r[1] < r[0] for r in want_rounds)
+    np.save(tmp_path / "prompt.npy", np.asarray(prompt, np.uint32))
     cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           "--nproc-per-node=2", "--master-addr=127.0.0.1", "--master-port=29533",
-           os.path.join(REPO, "tests", "tp_worker.py"), str(tgt), str(drf) if D else "-", "5", str(plen), str(n),
-           str(tmp_path)]
+           f"--nproc-per-node={world}", "--master-addr=127.0.0.1", f"--master-port={29533 + world}",
+           os.path.join(REPO, "tests", "tp_worker.py"), str(tp_model), str(dpath) if dpath else "-", "5",
+           str(tmp_path / "prompt.npy"), str(n), str(tmp_path)] + extra
     env = dict(os.environ, NCCL_NVLS_ENABLE="0")
     r = subprocess.run(cmd, capture_output=True, text=True, env=env)
     assert r.returncode == 0, r.stderr[-3000:]
-    for rank in range(2):
+    for rank in range(world):
         got = json.loads((tmp_path / f"rank{rank}.json").read_text())
         assert got["tokens"] == want_tokens.tolist(), f"rank {rank} tokens"
         assert [tuple(x) for x in got["rounds"]] == [tuple(x) for x in want_rounds], f"rank {rank} rounds"
+    print(f"TP={world} {case} prompt {len(prompt)}: compared {len(want_tokens)} tokens and {len(want_rounds)} "
+          f"rounds on each of {world} ranks")

@@ -33,12 +33,28 @@ def test_noalloc_matches_run_on_two_calls(built_lib, N, K, M):
     q.prepare(x)
     ref = torch.empty(M, N, device="cuda")
     q.run(M, ref)
+    outs = [torch.full((M, N), float("nan"), device="cuda") for _ in range(2)]
+    torch.cuda.synchronize()
+    free0, alloc0 = torch.cuda.mem_get_info()[0], torch.cuda.memory_allocated()
     for call in range(2):
-        got = torch.full((M, N), float("nan"), device="cuda")
-        q.run_noalloc(M, got)
+        q.run_noalloc(M, outs[call])
         torch.cuda.synchronize()
+    # The property the entry point exists for: the calls reserve no device memory.
+    assert torch.cuda.mem_get_info()[0] == free0 and torch.cuda.memory_allocated() == alloc0
+    for call, got in enumerate(outs):
         assert torch.equal(got, ref), f"call {call}: max |diff| {(got - ref).abs().max().item()}"
     q.check_error()
+    q.close()
+
+
+def test_noalloc_rejects_prefill_rows(built_lib):
+    import torch
+    q = make_qmat(256, 128, seed=3)
+    x = torch.randn(17, 128, device="cuda")
+    q.prepare(x)
+    out = torch.empty(17, 256, device="cuda")
+    with pytest.raises(RuntimeError, match="M must be 1..16"):
+        q.run_noalloc(17, out)
     q.close()
 
 

@@ -1,7 +1,8 @@
 """One rank of the tensor-parallel parity test (launched by test_tp.py under torchrun).
 
-argv: target container, drafter container ("-" for none), verify width, prompt length,
-tokens to generate, output directory. Writes rank<r>.json with the greedy stream and the
+argv: target container, drafter container ("-" for none), verify width, prompt (.npy of token
+ids), tokens to generate, output directory, and optionally a replay stream (.npy) with its
+mismatch rate and seed for the config-3 oracle drafter. Writes rank<r>.json with the greedy stream and the
 per-round records."""
 import json
 import os
@@ -33,7 +34,11 @@ def main():
     nid = t.cpu().numpy().tobytes()
     e = Engine(target=target, draft=None if draft == "-" else draft, draft_k=int(width) if draft != "-" else 0,
                tp_rank=rank, tp_size=world, nccl_id=nid, device=local)
-    prompt = np.random.default_rng(0).integers(0, 4096, int(plen))
+    prompt = np.load(plen)
+    if len(sys.argv) > 7:
+        e.set_gate(0.45, -1)
+        e.set_decode_options(replay=np.load(sys.argv[7]), mismatch_rate=float(sys.argv[8]),
+                             mismatch_seed=int(sys.argv[9]))
     toks = e.generate(prompt, int(n))
     rounds = e.rounds()
     e.close()

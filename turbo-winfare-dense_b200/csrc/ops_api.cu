@@ -23,6 +23,42 @@ int fail_msg(const char* msg) {
 }
 }  // namespace
 
+namespace {
+// Library-owned split-K scratch of g4b_qmat_run_noalloc: 8 MiB of partial slots and one
+// arrival counter per 256-row group. Static device memory is part of the module image, so
+// using it allocates nothing at call time.
+constexpr size_t kNoAllocPartFloats = (size_t)2 << 20;  // 8 MiB
+constexpr int kNoAllocCounters = 4096;                 // N <= 4096 * 256 rows
+__device__ __align__(256) float g_noalloc_part[kNoAllocPartFloats];
+__device__ __align__(256) unsigned g_noalloc_cnt[kNoAllocCounters];
+
+struct NoAllocScratch {
+    float* part = nullptr;
+    unsigned* cnt = nullptr;
+};
+constexpr int kMaxDevices = 64;
+std::mutex g_noalloc_mu;
+NoAllocScratch g_noalloc[kMaxDevices];  // symbol addresses per device ordinal
+
+// Looks up the device addresses of the static scratch on `dev` (the current device) and caches
+// them. The first lookup on a device loads the module holding the arrays, which reserves their
+// device memory; g4b_qmat_create calls this so that the no-alloc call itself never does. A
+// later lookup allocates nothing and refreshes the cache (the addresses are only valid for the
+// primary context they were taken in).
+cudaError_t noalloc_scratch_setup(int dev) {
+    if (dev < 0 || dev >= kMaxDevices) return cudaErrorInvalidDevice;
+    void* part = nullptr;
+    void* cnt = nullptr;
+    cudaError_t e;
+    if ((e = cudaGetSymbolAddress(&part, g_noalloc_part)) != cudaSuccess) return e;
+    if ((e = cudaGetSymbolAddress(&cnt, g_noalloc_cnt)) != cudaSuccess) return e;
+    std::lock_guard<std::mutex> lock(g_noalloc_mu);
+    g_noalloc[dev].part = static_cast<float*>(part);
+    g_noalloc[dev].cnt = static_cast<unsigned*>(cnt);
+    return cudaSuccess;
+}
+}  // namespace
+
 struct g4b_qmat {
     int N, K, ktiles, n_wrg, n_crg;
     void* w;          // repacked weights
@@ -36,6 +72,7 @@ struct g4b_qmat {
     float* ppart;
     unsigned* pcnt;
     int n_tiles, pmax_slots;
+    int dev;          // device the matrix lives on
 };
 
 extern "C" {
@@ -46,7 +83,15 @@ int g4b_qmat_create(const uint32_t* W, const uint16_t* S, const uint16_t* B, int
                     g4b_qmat** out) {
     if (!out || !W || !S || !B || N <= 0 || K <= 0 || K % 64) return fail_msg("g4b_qmat_create: bad arguments");
     cudaStream_t st = (cudaStream_t)stream;
+    int dev = 0;
+    cudaError_t e0 = cudaGetDevice(&dev);
+    if (e0 != cudaSuccess) return fail(e0, "g4b_qmat_create: cudaGetDevice");
+    // Loads the module that holds g4b_qmat_run_noalloc's static scratch on this device now,
+    // while allocating is allowed: under lazy module loading the first symbol lookup reserves
+    // that module's device memory.
+    if ((e0 = noalloc_scratch_setup(dev)) != cudaSuccess) return fail(e0, "g4b_qmat_create: static scratch set-up");
     auto* q = new g4b_qmat{};
+    q->dev = dev;
     q->N = N;
     q->K = K;
     q->ktiles = vgemm_ktiles(K);
@@ -157,45 +202,22 @@ int g4b_qmat_run(g4b_qmat* q, int M, float* out, int ldo, void* stream) {
 
 // ---------------------------------------------------------------- allocation-free run
 
-namespace {
-// Library-owned split-K scratch of g4b_qmat_run_noalloc: 8 MiB of partial slots and one
-// arrival counter per 256-row group. Static device memory is part of the module image, so
-// using it allocates nothing at call time.
-constexpr size_t kNoAllocPartFloats = (size_t)2 << 20;  // 8 MiB
-constexpr int kNoAllocCounters = 4096;                 // N <= 4096 * 256 rows
-__device__ __align__(256) float g_noalloc_part[kNoAllocPartFloats];
-__device__ __align__(256) unsigned g_noalloc_cnt[kNoAllocCounters];
-
-struct NoAllocScratch {
-    float* part = nullptr;
-    unsigned* cnt = nullptr;
-};
-constexpr int kMaxDevices = 64;
-std::mutex g_noalloc_mu;
-NoAllocScratch g_noalloc[kMaxDevices];  // symbol addresses, looked up once per device
-}  // namespace
 
 int g4b_qmat_run_noalloc(g4b_qmat* q, int M, float* out, int ldo, void* stream) {
-    if (!q || !out || M < 1 || M > g4b::kMaxM || ldo < q->N) return fail_msg("g4b_qmat_run_noalloc: bad arguments");
+    if (!q || !out || ldo < q->N) return fail_msg("g4b_qmat_run_noalloc: bad arguments");
+    if (M < 1 || M > g4b::kMaxM)
+        return fail_msg("g4b_qmat_run_noalloc: M must be 1..16 (the verify GEMM only; 17..128 rows need "
+                        "g4b_qmat_run's tensor-core path and its allocated workspace)");
     int dev = 0;
     cudaError_t e = cudaGetDevice(&dev);
     if (e != cudaSuccess) return fail(e, "g4b_qmat_run_noalloc: cudaGetDevice");
-    if (dev < 0 || dev >= kMaxDevices) return fail_msg("g4b_qmat_run_noalloc: device ordinal out of range");
+    if (dev != q->dev) return fail_msg("g4b_qmat_run_noalloc: the current device is not the matrix's device");
     NoAllocScratch sc;
     {
         std::lock_guard<std::mutex> lock(g_noalloc_mu);
-        NoAllocScratch& slot = g_noalloc[dev];
-        if (!slot.part) {
-            void* part = nullptr;
-            void* cnt = nullptr;
-            if ((e = cudaGetSymbolAddress(&part, g_noalloc_part)) != cudaSuccess ||
-                (e = cudaGetSymbolAddress(&cnt, g_noalloc_cnt)) != cudaSuccess)
-                return fail(e, "g4b_qmat_run_noalloc: cudaGetSymbolAddress");
-            slot.part = static_cast<float*>(part);
-            slot.cnt = static_cast<unsigned*>(cnt);
-        }
-        sc = slot;
+        sc = g_noalloc[dev];
     }
+    if (!sc.part) return fail_msg("g4b_qmat_run_noalloc: static scratch not set up on this device");
     VgemmParams p = qmat_params(q, M);
     // Exactly the slots this launch needs (the matrix's own workspace is sized for every M).
     const int slots = vgemm_max_slots(p.out.grid, q->n_crg, q->ktiles);

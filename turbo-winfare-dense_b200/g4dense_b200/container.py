@@ -90,9 +90,59 @@ CONFIG0_DRAFT = ModelSpec(num_layers=2, d_model=128, d_ff=512, num_q_heads=2, nu
 GEMMA4_31B = ModelSpec(num_layers=60, d_model=5376, d_ff=21504, num_q_heads=32, num_kv_heads=16,
                        head_dim=256, vocab_size=262144, sliding_window=1024,
                        global_layer_mask=0x0820820820820820, global_head_dim=512, global_kv_heads=4)
+# Two layers of the 31B at full width (one sliding, one global) with the full 262144-row embedding
+# and LM head: the CPU-baseline sample and the full-shape parity case.
+GEMMA4_31B_TWO_LAYERS = dataclasses.replace(GEMMA4_31B, num_layers=2, global_layer_mask=0b10)
 # Gemma-4-E2B-shaped drafter used by BASELINE config 3 (no PLE, no KV sharing).
 E2B_DRAFT = ModelSpec(num_layers=35, d_model=1536, d_ff=6144, num_q_heads=8, num_kv_heads=1,
                       head_dim=256, vocab_size=262144, sliding_window=512)
+
+
+# Gemma-4-31B attention geometry at toy width (a test aid): sliding layers with head_dim 256 and
+# GQA 2 over a 48-key window (the KV ring wraps), one full-attention layer with head_dim 512, a
+# single KV head (GQA 4) and V taken from the raw K.
+GEOM31_TEST = ModelSpec(num_layers=3, d_model=256, d_ff=512, num_q_heads=4, num_kv_heads=2, head_dim=256,
+                        vocab_size=4096, sliding_window=48, global_layer_mask=0b010, global_head_dim=512,
+                        global_kv_heads=1)
+
+# Tensor-parallel test geometry at config-0 scale (a test aid): 8 query heads and 8 KV heads on
+# the sliding layers split evenly at TP 2/4/8; the full-attention layer (head_dim 128) has 2 KV
+# heads, so TP = 8 replicates them as the 31B's four-head global layers are replicated at TP = 8.
+# A 64-key window, wrapped by long prompts.
+TP_TEST_TARGET = ModelSpec(num_layers=4, d_model=256, d_ff=1024, num_q_heads=8, num_kv_heads=8, head_dim=64,
+                           vocab_size=4096, sliding_window=64, global_layer_mask=0b0100, global_head_dim=128,
+                           global_kv_heads=2)
+
+# Config-0 decode cases whose oracle greedy streams have no near-tie: prompt seeds found by
+# scanning the oracle's top-2 margins (seeds 100.. in order) on the zero-mean ("centered")
+# config-0 target (seed 0) and drafter (seed 1). Along each stream every target margin is at
+# least 0.09 and every drafter margin at least 0.02, above the FP16 K/V rounding noise of the
+# GPU-vs-CPU comparison, so streams and round records can be compared exactly.
+PINNED_PROMPT_SEED, PINNED_PROMPT_LEN, PINNED_TOKENS = 158, 32, 64
+PINNED_LONG_PROMPT_SEED, PINNED_LONG_PROMPT_LEN, PINNED_LONG_TOKENS = 114, 300, 32
+# The drafter of the sampled-decoding parity cases: the BASELINE-distribution config-0 target with
+# 20% of its embedding nibbles re-drawn (perturbed_copy), so rejection sampling both accepts and
+# rejects drafts.
+NEAR_DRAFT_EMBED_FRAC, NEAR_DRAFT_SEED = 0.2, 7
+SAMPLED_PARAMS = (0.8, 0.95, 64, 5)  # temperature, top_p, top_k, seed
+
+
+# The same for TP_TEST_TARGET (zero-mean, seed TP_TEST_SEED): (prompt seed, prompt length, tokens).
+# Target margins along the streams are at least 0.10, the config-0 drafter's at least 0.03.
+TP_TEST_SEED = 3
+TP_PINNED = (137, 32, 64)
+TP_PINNED_LONG = (132, 300, 32)
+
+
+def tp_pinned_prompt(long: bool = False) -> np.ndarray:
+    seed, n, _ = TP_PINNED_LONG if long else TP_PINNED
+    return np.random.default_rng(seed).integers(0, 4096, n)
+
+
+def pinned_prompt(long: bool = False) -> np.ndarray:
+    if long:
+        return np.random.default_rng(PINNED_LONG_PROMPT_SEED).integers(0, 4096, PINNED_LONG_PROMPT_LEN)
+    return np.random.default_rng(PINNED_PROMPT_SEED).integers(0, 4096, PINNED_PROMPT_LEN)
 
 
 # A target with both layer kinds at config-0 scale: the MTP drafter's tests need a sliding and a
@@ -213,8 +263,10 @@ def write_mtp_container(path, spec: MtpSpec, seed: int = 0, centered: bool = Fal
 
 def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
     """Round-to-nearest-even float32 -> bf16 bit patterns (uint16)."""
-    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
-    rounded = (u + 0x7FFF + ((u >> 16) & 1)) >> 16
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)
+    if not np.isfinite(x).all():
+        u = u.astype(np.uint64)  # NaN/inf bit patterns could wrap in 32 bits
+    rounded = (u + np.uint32(0x7FFF) + ((u >> 16) & np.uint32(1))) >> 16
     return rounded.astype(np.uint16)
 
 
@@ -253,64 +305,131 @@ def _pad(buf: bytearray, align: int):
         buf += b"\x00" * (align - rem)
 
 
-def build_container(spec: ModelSpec, seed: int = 0, centered: bool = False) -> bytes:
-    """Returns the full container bytes for `spec` drawn from seed `seed` (see
-    random_quant_block for ``centered``)."""
+def _container_sections(spec: ModelSpec, seed: int, centered: bool):
+    """Yields the payload in file order: the embedding block, then each layer block (each
+    already padded to 4096 bytes), drawing from `default_rng(seed)` in the documented order."""
     rng = np.random.default_rng(seed)
     d, V = spec.d_model, spec.vocab_size
 
-    embed = bytearray()
-    p, s, b = random_quant_block(rng, V, d, centered)
-    embed += p.tobytes() + s.tobytes() + b.tobytes()
-    embed += _norm(rng, d).tobytes()
-    _pad(embed, ALIGNMENT)
+    def quant_bytes(rows, cols):
+        p, s_, b_ = random_quant_block(rng, rows, cols, centered)
+        return [p.tobytes(), s_.tobytes(), b_.tobytes()]
 
-    layers = []
+    def padded(parts, align):
+        n = sum(len(x) for x in parts)
+        return parts + [b"\x00" * ((-n) % align)]
+
+    yield padded(quant_bytes(V, d) + [_norm(rng, d).tobytes()], ALIGNMENT)
     scalar = f32_to_bf16_bits(np.array([1.0 / np.sqrt(2.0 * spec.num_layers)], dtype=np.float32))
     for l in range(spec.num_layers):
         hd, _, _, _ = spec.layer_geometry(l)
-        ld = bytearray()
-        for _ in range(4):
-            ld += _norm(rng, d).tobytes()
-        ld += _norm(rng, hd).tobytes()
-        ld += _norm(rng, hd).tobytes()
-        ld += scalar.tobytes()
+        parts = [_norm(rng, d).tobytes() for _ in range(4)]
+        parts += [_norm(rng, hd).tobytes(), _norm(rng, hd).tobytes(), scalar.tobytes()]
         for _, rows, cols in spec.layer_projections(l):
-            _pad(ld, 16)
-            p, s, b = random_quant_block(rng, rows, cols, centered)
-            ld += p.tobytes() + s.tobytes() + b.tobytes()
-        _pad(ld, ALIGNMENT)
-        layers.append(bytes(ld))
+            n = sum(len(x) for x in parts)
+            parts.append(b"\x00" * ((-n) % 16))
+            parts += quant_bytes(rows, cols)
+        yield padded(parts, ALIGNMENT)
 
-    payload = bytearray(embed)
+
+def _header(spec: ModelSpec, embed_len: int, layer_lens, sha: bytes) -> bytes:
     offsets = [0] * 60
     sizes = [0] * 60
-    cur = HEADER_SIZE + len(payload)
-    for l, ld in enumerate(layers):
-        offsets[l] = cur
-        sizes[l] = len(ld)
-        payload += ld
-        cur += len(ld)
-    sha = hashlib.sha256(bytes(payload)).digest()
+    cur = HEADER_SIZE + embed_len
+    for l, n in enumerate(layer_lens):
+        offsets[l], sizes[l] = cur, n
+        cur += n
     layer_d_ff = [spec.d_ff] * spec.num_layers + [0] * (60 - spec.num_layers)
     header = struct.pack(
-        HEADER_FMT, MAGIC, VERSION, QUANT_AFFINE_INT4_G64, spec.num_layers, d, spec.d_ff,
-        spec.num_q_heads, spec.num_kv_heads, spec.head_dim, V, spec.sliding_window, GROUP,
+        HEADER_FMT, MAGIC, VERSION, QUANT_AFFINE_INT4_G64, spec.num_layers, spec.d_model, spec.d_ff,
+        spec.num_q_heads, spec.num_kv_heads, spec.head_dim, spec.vocab_size, spec.sliding_window, GROUP,
         1, 1, spec.global_layer_mask, spec.rope_theta_local, spec.rope_theta_global, 1.0,
-        spec.softcap, HEADER_SIZE, len(embed), HEADER_SIZE, len(embed), *offsets, *sizes, sha,
+        spec.softcap, HEADER_SIZE, embed_len, HEADER_SIZE, embed_len, *offsets, *sizes, sha,
         spec.global_head_dim or (spec.head_dim if spec.global_layer_mask == 0 else 512),
         spec.global_kv_heads or (spec.num_kv_heads if spec.global_layer_mask == 0 else 4),
         0, 0, 0, 0, 0, 0, *layer_d_ff, 0, 0, 0.0, 0.0, b"\x00" * 2696)
-    return header + bytes(payload)
+    assert len(header) == HEADER_SIZE
+    return header
+
+
+def _write_sections(f, spec: ModelSpec, seed: int, centered: bool) -> bytes:
+    """Writes header placeholder + payload to the open file `f`; returns the real header."""
+    f.write(b"\x00" * HEADER_SIZE)
+    sha = hashlib.sha256()
+    lens = []
+    for parts in _container_sections(spec, seed, centered):
+        for x in parts:
+            f.write(x)
+            sha.update(x)
+        lens.append(sum(len(x) for x in parts))
+    return _header(spec, lens[0], lens[1:], sha.digest())
+
+
+def build_container(spec: ModelSpec, seed: int = 0, centered: bool = False) -> bytes:
+    """Returns the full container bytes for `spec` drawn from seed `seed` (see
+    random_quant_block for ``centered``)."""
+    import io
+    buf = io.BytesIO()
+    header = _write_sections(buf, spec, seed, centered)
+    data = buf.getbuffer()
+    data[:HEADER_SIZE] = header
+    return bytes(data)
 
 
 def write_container(path, spec: ModelSpec, seed: int = 0, centered: bool = False) -> Path:
+    """Streams the container for `spec` to `path` (written to a temporary name, then renamed)."""
     path = Path(path)
     path.parent.mkdir(parents=True, exist_ok=True)
-    data = build_container(spec, seed, centered)
     tmp = path.with_suffix(path.suffix + ".tmp")
-    tmp.write_bytes(data)
+    with open(tmp, "wb") as f:
+        header = _write_sections(f, spec, seed, centered)
+        f.seek(0)
+        f.write(header)
     tmp.replace(path)
+    return path
+
+
+def layer_weight_ranges(spec: ModelSpec, l: int):
+    """[(name, start, nbytes)] of each projection's packed nibble words inside layer l's block,
+    following the writer's layout: six bf16 norms, the bf16 layer_scalar, then per projection a
+    16-byte pad relative to the layer start and W, scales, biases."""
+    hd, _, _, _ = spec.layer_geometry(l)
+    off = 4 * spec.d_model * 2 + 2 * hd * 2 + 2
+    out = []
+    for name, rows, cols in spec.layer_projections(l):
+        off += (-off) % 16
+        w = rows * cols // 2
+        out.append((name, off, w))
+        off += w + 2 * (rows * cols // GROUP) * 2
+    return out
+
+
+def perturbed_copy(src, dst, spec: ModelSpec, frac: float, seed: int, embed_frac: float = 0.0) -> Path:
+    """A test aid: a copy of container `src` (written for `spec`) in which a fraction `frac` of
+    every layer projection's nibble bytes, and a fraction `embed_frac` of the tied embedding's
+    nibble bytes, is re-drawn uniformly; norms, scales and biases stay as they are. Used as a
+    drafter close to its target, so that speculative rounds accept some drafts and reject others.
+    The header's payload sha256 is recomputed."""
+    data = bytearray(Path(src).read_bytes())
+    h = read_header(src)
+    rng = np.random.default_rng(seed)
+
+    def redraw(start, n, f):
+        region = np.frombuffer(data, np.uint8, n, start).copy()
+        hit = rng.random(n) < f
+        region[hit] = rng.integers(0, 256, int(hit.sum()), dtype=np.uint8)
+        data[start:start + n] = region.tobytes()
+
+    if embed_frac > 0:
+        redraw(h["embed_offset"], spec.vocab_size * spec.d_model // 2, embed_frac)
+    for l in range(spec.num_layers):
+        base = h["layer_offsets"][l]
+        for _, start, n in layer_weight_ranges(spec, l):
+            redraw(base + start, n, frac)
+    sha_off = struct.calcsize("<IIIIIIIIIIIIIIQffffQQQQ60Q60Q")
+    data[sha_off:sha_off + 32] = hashlib.sha256(bytes(data[HEADER_SIZE:])).digest()
+    path = Path(dst)
+    path.write_bytes(bytes(data))
     return path
 
 
