@@ -21,6 +21,11 @@ copies and the per-round result reads included). `roofline` = the verify GEMM (t
 kernel): algorithmic bytes of one 5-row verify pass's GEMMs / their CUDA-event time, against
 the measured HBM copy bandwidth in MEASURED_PEAKS.json.
 
+The line also carries BASELINE config 1 (`config1`: the verify GEMM alone at its (K, N) x M grid,
+GB/s per cell) and config 4 (`long_context`: 32768-token bf16 KV after a 30000-token prefill,
+verify width 9, greedy and temperature-0.8 rejection sampling, at the run's TP size), and the
+speculative weight-bytes bound of the measured rounds.
+
 `--impl reference` times the reference's own CPU code (oracle/_ref, src/cpu_reference.cpp built
 unmodified) on a bounded sample of the same workload on the host: a 31B-shaped container with
 one sliding and one global layer plus the full embedding / LM head, one position per step,
@@ -48,6 +53,11 @@ UNIT = "tok/s"
 PROMPT_LEN, GEN_LEN, VERIFY_WIDTH, MISMATCH = 512, 256, 5, 0.25
 # Weight bytes of one 31B verify pass (50 sliding + 10 global layers + LM head, INT4 G64).
 B31_PASS_BYTES = 50 * 269.40e6 + 10 * 300.37e6 + 792.72e6
+# Weight bytes of one E2B-shaped drafter step (35 layers + LM head).
+E2B_STEP_BYTES = 35 * 19.91e6 + 226.5e6
+# (K, N) of the verify-GEMM sweep and its verify widths.
+CONFIG1_SHAPES = [(5376, 21504), (21504, 5376), (5376, 8192), (5376, 262144)]
+CONFIG1_M = [1, 2, 5, 8, 16]
 
 
 def peaks():
@@ -133,19 +143,23 @@ def reference_sample(steps, warmup):
         dt = (time.perf_counter() - t0) / steps
     sample_bytes = 269.40e6 + 300.37e6 + 792.72e6
     t_token = dt * B31_PASS_BYTES / sample_bytes
-    return {"value": 1.0 / t_token, "unit": UNIT, "cores": 1, "kind": kind,
+    return {"value": 1.0 / t_token, "unit": UNIT, "cores": 1, "nproc": os.cpu_count(), "kind": kind,
+            "measured_s_per_sample_position": dt, "extrapolation_factor": B31_PASS_BYTES / sample_bytes,
             "sample": f"{steps} position(s) of a 2-layer (1 sliding + 1 global) 31B-shaped container with the full "
-                      f"262144x5376 embedding/LM head: {dt:.2f} s per position, extrapolated to 60 layers by weight "
-                      f"bytes ({B31_PASS_BYTES / sample_bytes:.2f}x) = {t_token:.1f} s/token; greedy autoregressive "
-                      f"decode, single-threaded"}
+                      f"262144x5376 embedding/LM head: {dt:.2f} s per position (measured), extrapolated to 60 layers "
+                      f"by weight bytes ({B31_PASS_BYTES / sample_bytes:.2f}x) = {t_token:.1f} s/token; greedy "
+                      f"autoregressive decode; the reference's CPU runner is single-threaded (src/cpu_reference.cpp "
+                      f"has no threading), so 1 of the host's {os.cpu_count()} cores is used"}
 
 
 def run_reference(args, rank, world):
     if rank != 0:
         return 0
     cb = reference_sample(args.steps, args.warmup)
+    # One step = one timed sample position; ms_per_step is what was measured per step (the
+    # value is that time extrapolated to the 60-layer model, as cpu_baseline.sample states).
     line = {"metric": METRIC, "value": cb["value"], "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 / cb["value"],
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * cb["measured_s_per_sample_position"],
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32", "data": "synthetic",
             "config": {"workload": "config3: 31B-shaped target greedy decode on the reference CPU path"},
             "cpu_baseline": cb,
@@ -164,14 +178,19 @@ def run_b200(args, rank, world):
 
     local = int(os.environ.get("LOCAL_RANK", rank))
     torch.cuda.set_device(local)
-    nid = None
-    if world > 1:
+
+    def nccl_id():
+        """A fresh NCCL unique id from rank 0 for one tensor-parallel engine (None at TP = 1)."""
+        if world == 1:
+            return None
         buf = np.zeros(128, np.uint8)
         if rank == 0:
             lib().g4dense_nccl_unique_id(buf.ctypes.data)
         t = torch.from_numpy(buf).cuda()
         dist.broadcast(t, 0)
-        nid = t.cpu().numpy().tobytes()
+        return t.cpu().numpy().tobytes()
+
+    nid = nccl_id()
     t_load = time.perf_counter()
     eng = Engine(preset="gemma4-31b", seed=0, draft_preset="gemma4-e2b", draft_seed=1, draft_k=VERIFY_WIDTH,
                  max_context=4096, tp_rank=rank, tp_size=world, nccl_id=nid, device=local)
@@ -242,6 +261,14 @@ def run_b200(args, rank, world):
             if ln.startswith("traffic_bytes_per_pass:"):
                 traffic = int(ln.split(":")[1])
 
+    # Speculative weight-bytes bound: per round the target streams its weights once (split over
+    # the ranks) and the drafter its weights K-1 times (on one GPU, serially); the tokens a round
+    # yields are the accepted drafts plus one.
+    rounds = max(1.0, sum(s["rounds"] for s in stats))
+    tok_per_round = sum(s["emitted"] - 1 for s in stats) / rounds
+    round_s = (B31_PASS_BYTES / world + (VERIFY_WIDTH - 1) * E2B_STEP_BYTES) / (peaks()[0] * 1e9)
+    spec_bound = tok_per_round / round_s
+
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": dec_ms / args.steps, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
@@ -269,39 +296,91 @@ def run_b200(args, rank, world):
         "spec_stream_equals_greedy": all(matches),
         "acceptance": sum(s["accepted"] for s in stats) / max(1.0, sum(s["drafted"] for s in stats)),
         "weights_bound_tok_s_tp": peak * 1e9 / (B31_PASS_BYTES / world),
+        "speculative_weights_bound": {
+            "tok_s": spec_bound, "frac": value / spec_bound, "tokens_per_round": tok_per_round,
+            "round_bytes": B31_PASS_BYTES / world + (VERIFY_WIDTH - 1) * E2B_STEP_BYTES,
+            "how": "(31B pass bytes / TP + (K-1) x E2B step bytes) / measured HBM peak per round; tokens per round "
+                   "= decoded tokens / rounds of the timed requests"},
         "load_s": load_s,
     }
     if clocks:
         line["clocks"] = clocks
     if world == 1:
-        line["mtp_drafter"] = mtp_drafter(eng, prompt, stream, args)
-    long_ctx = args.long_context and world == 1  # (a second TP engine would need its own NCCL id)
-    if long_ctx:
+        line["mtp_drafter"] = mtp_drafter(eng, prompt, stream, args)  # closes eng
+        line["config1"] = config1_sweep()
+    else:
         eng.close()
-        line["long_context"] = long_context(args, eng_factory=lambda: Engine(
+    if not args.no_long_context:
+        line["long_context"] = long_context(args, eng_factory=lambda nid2: Engine(
             preset="gemma4-31b", seed=0, draft_preset="gemma4-e2b", draft_seed=1, draft_k=9, max_context=32768,
-            kv_bf16=True, device=local), world=world)
+            kv_bf16=True, tp_rank=rank, tp_size=world, nccl_id=nid2, device=local), nccl_id=nccl_id)
     if rank != 0:
-        if not long_ctx:
-            eng.close()
         return 0
     if world == 1 and not args.no_cpu_baseline:
         try:
-            line["cpu_baseline"] = reference_sample(1, 1)
+            line["cpu_baseline"] = reference_sample(2, 1)
         except Exception as e:  # the baseline is reported, never required
             line["cpu_baseline"] = {"value": None, "error": str(e)[:200]}
     print(json.dumps(line), flush=True)
-    if not long_ctx:
-        eng.close()
     return 0
 
 
-def long_context(args, eng_factory, world):
-    """BASELINE config 4 at TP 1: 32768-token bf16 KV filled by a 30000-token prefill, verify width
-    9 (k = 8), greedy (natural drafter, gate off) and temperature-0.8 rejection sampling."""
+def config1_sweep(reps=10):
+    """the verify GEMM alone on bf16 activations ~N(0, 1) (held as fp32 values)
+    of M rows times INT4 G64 weights [N, K] with the container's distributions, fp32 output, for
+    every (K, N) and M. Each cell is one launch of g4b_qmat_run (the kernel that streams the
+    weights and sums its split-K slots in-kernel) timed with CUDA events on its stream, after a
+    256 MiB write that evicts the 126 MB L2, so every launch reads its weights from HBM. GB/s =
+    algorithmic bytes (N*K/2 packed nibbles + N*K/16 scale/bias bytes + 2*M*K bf16 activations +
+    4*M*N outputs) / median launch time."""
+    import torch
+    from g4dense_b200 import QMat
+    dev = torch.device("cuda")
+    st = torch.cuda.current_stream()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=dev)
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(1)
+    peak = peaks()[0]
+    cells = []
+    for K, N in CONFIG1_SHAPES:
+        W = torch.randint(-2 ** 31, 2 ** 31, (N, K // 8), dtype=torch.int32, device=dev, generator=gen)
+        S = (torch.randn((N, K // 64), device=dev, generator=gen).abs() * 0.02).to(torch.bfloat16).view(torch.int16)
+        B = (torch.randn((N, K // 64), device=dev, generator=gen) * 0.01).to(torch.bfloat16).view(torch.int16)
+        q = QMat(W, S, B, stream=st)
+        del W, S, B
+        for M in CONFIG1_M:
+            x = torch.randn((M, K), device=dev, generator=gen).to(torch.bfloat16).float()
+            out = torch.empty((M, N), device=dev)
+            q.prepare(x, stream=st)
+            ms = []
+            for r in range(reps + 2):
+                flush.fill_(r & 255)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                e0.record(st)
+                q.run(M, out, stream=st)
+                e1.record(st)
+                e1.synchronize()
+                if r >= 2:
+                    ms.append(e0.elapsed_time(e1))
+            q.check_error()
+            t = float(np.median(ms))
+            nbytes = N * K // 2 + N * K // 16 + 2 * M * K + 4 * M * N
+            gbs = nbytes / (t / 1000.0) / 1e9
+            cells.append({"M": M, "K": K, "N": N, "us": t * 1000.0, "GB_s": gbs, "frac": gbs / peak})
+        q.close()
+    del flush
+    torch.cuda.empty_cache()
+    return {"cells": cells, "peak_gbs": peak,
+            "how": "one g4b_qmat_run launch per cell after a 256 MiB L2-evicting write, CUDA events, median of 10"}
+
+
+def long_context(args, eng_factory, nccl_id):
+    """32768-token bf16 KV filled by a 30000-token prefill, verify width 9
+    (k = 8), greedy (natural drafter, gate off) and temperature-0.8 rejection sampling, at the
+    run's TP size (sampled verify logits are all-gathered from the ranks' vocabulary slices)."""
     import gc
     gc.collect()
-    eng = eng_factory()
+    eng = eng_factory(nccl_id())
     prompt = np.random.default_rng(4).integers(0, 262144, 30000).astype(np.uint32)
     eng.set_gate(0.45, -1)
     out = {"prompt_tokens": 30000, "kv_context": 32768, "kv": "bf16", "verify_width": 9}
@@ -309,12 +388,11 @@ def long_context(args, eng_factory, world):
     s = eng.stats()
     out["greedy"] = {"tokens": int(s["emitted"]), "decode_tok_s": (s["emitted"] - 1) / (s["decode_gpu_ms"] / 1000.0),
                      "prefill_s": s["ttft_ms"] / 1000.0, "acceptance": s["accepted"] / max(1.0, s["drafted"])}
-    if world == 1:
-        eng.generate(prompt, 16, temperature=0.8, seed=7)
-        s = eng.stats()
-        out["sampled_t0.8"] = {"tokens": int(s["emitted"]),
-                               "decode_tok_s": (s["emitted"] - 1) / (s["decode_gpu_ms"] / 1000.0),
-                               "acceptance": s["accepted"] / max(1.0, s["drafted"])}
+    eng.generate(prompt, 16, temperature=0.8, seed=7)
+    s = eng.stats()
+    out["sampled_t0.8"] = {"tokens": int(s["emitted"]),
+                           "decode_tok_s": (s["emitted"] - 1) / (s["decode_gpu_ms"] / 1000.0),
+                           "acceptance": s["accepted"] / max(1.0, s["drafted"])}
     out["verify_pass_ms_at_30000"] = eng.time_pass(0, 9, 3, pos=30000)
     eng.close()
     return out
@@ -354,7 +432,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="b200", choices=["b200", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--long-context", action="store_true", help="also run BASELINE config 4 (about a minute more)")
+    ap.add_argument("--no-long-context", action="store_true", help="skip BASELINE config 4 (about a minute)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

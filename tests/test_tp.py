@@ -9,8 +9,11 @@ stream stay clear of the FP16 K/V rounding noise, so greedy token streams and ro
 equal the oracle's exactly (the reference has no multi-GPU path; its single-process CPU runner,
 restated in oracle/ and pinned to the reference by tests/test_oracle.py, is the oracle). Cases:
 no drafter; the target drafting for itself (every draft accepted); the config-3 replay drafter at
-a 0.25 mismatch rate (accepts and rejects mixed); and a 300-token prompt that also runs the
-tensor-core prefill (chunks of 128, 128 and 44 rows) under TP."""
+a 0.25 mismatch rate (accepts and rejects mixed); a 300-token prompt that also runs the
+tensor-core prefill (chunks of 128, 128 and 44 rows) under TP; and temperature-0.8 speculative
+decoding with rejection sampling, whose verify logits are all-gathered from the ranks' vocabulary
+slices before the reference's acceptance test runs (BASELINE-distribution weights, which the GPU
+reproduces to ~1e-5, with a near drafter so that drafts are both accepted and rejected)."""
 from __future__ import annotations
 
 import json
@@ -42,6 +45,46 @@ def tp_model(tmp_path_factory):
                              seed=C.TP_TEST_SEED, centered=True)
 
 
+@pytest.fixture(scope="module")
+def tp_sampled_pair(tmp_path_factory):
+    from g4dense_b200 import container as C
+    d = tmp_path_factory.mktemp("tp_sampled")
+    tgt = C.write_container(d / "tp_base.g4dense", C.TP_TEST_TARGET, seed=C.TP_TEST_SEED)
+    near = C.perturbed_copy(tgt, d / "tp_near.g4dense", C.TP_TEST_TARGET, 0.0, seed=C.NEAR_DRAFT_SEED,
+                            embed_frac=C.NEAR_DRAFT_EMBED_FRAC)
+    return tgt, near
+
+
+def _run_ranks(world, tmp_path, args, env_extra=None):
+    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
+           f"--nproc-per-node={world}", "--master-addr=127.0.0.1", f"--master-port={29533 + world}",
+           os.path.join(REPO, "tests", "tp_worker.py")] + args
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0", **(env_extra or {}))
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env)
+    assert r.returncode == 0, r.stderr[-3000:]
+    return [json.loads((tmp_path / f"rank{rank}.json").read_text()) for rank in range(world)]
+
+
+@pytest.mark.parametrize("world", [2, 4, 8])
+def test_tp_sampled_spec_matches_oracle(built_lib, tp_sampled_pair, tmp_path, world):
+    if gpu_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    from g4dense_b200 import container as C
+    tgt, near = tp_sampled_pair
+    t, tp, tk, seed = C.SAMPLED_PARAMS
+    prompt = C.tp_pinned_prompt()
+    want_tokens, want_rounds = O.spec_generate(O.RestatedModel(tgt), O.RestatedModel(near), prompt, 48, verify_width=5,
+                                               sampling=O.Sampling(t, tp, tk, 1.0, 1, seed))
+    np.save(tmp_path / "prompt.npy", np.asarray(prompt, np.uint32))
+    got = _run_ranks(world, tmp_path, [str(tgt), str(near), "5", str(tmp_path / "prompt.npy"), "48", str(tmp_path)],
+                     {"G4B_TEST_SAMPLING": f"{t},{tp},{tk},{seed}"})
+    for rank, g in enumerate(got):
+        assert g["tokens"] == want_tokens.tolist(), f"rank {rank} tokens"
+        assert [tuple(x) for x in g["rounds"]] == [tuple(x) for x in want_rounds], f"rank {rank} rounds"
+    print(f"TP={world} sampled: compared {len(want_tokens)} tokens and {len(want_rounds)} rounds "
+          f"({sum(r[1] for r in want_rounds)}/{sum(r[0] for r in want_rounds)} drafts accepted) on each rank")
+
+
 @pytest.mark.parametrize("world", [2, 4, 8])
 @pytest.mark.parametrize("case", ["no_spec", "self_k5", "replay_k5", "long_self_k5"])
 def test_tp_streams_match_oracle(built_lib, config0, tp_model, tmp_path, world, case):
@@ -69,15 +112,9 @@ def test_tp_streams_match_oracle(built_lib, config0, tp_model, tmp_path, world, 
     if case == "replay_k5":
         assert any(0 < r[1] < r[0] for r in want_rounds)
     np.save(tmp_path / "prompt.npy", np.asarray(prompt, np.uint32))
-    cmd = ["timeout", "-k", "30", "300", sys.executable, "-m", "torch.distributed.run", "--nnodes=1",
-           f"--nproc-per-node={world}", "--master-addr=127.0.0.1", f"--master-port={29533 + world}",
-           os.path.join(REPO, "tests", "tp_worker.py"), str(tp_model), str(dpath) if dpath else "-", "5",
-           str(tmp_path / "prompt.npy"), str(n), str(tmp_path)] + extra
-    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
-    r = subprocess.run(cmd, capture_output=True, text=True, env=env)
-    assert r.returncode == 0, r.stderr[-3000:]
-    for rank in range(world):
-        got = json.loads((tmp_path / f"rank{rank}.json").read_text())
+    ranks = _run_ranks(world, tmp_path, [str(tp_model), str(dpath) if dpath else "-", "5",
+                                         str(tmp_path / "prompt.npy"), str(n), str(tmp_path)] + extra)
+    for rank, got in enumerate(ranks):
         assert got["tokens"] == want_tokens.tolist(), f"rank {rank} tokens"
         assert [tuple(x) for x in got["rounds"]] == [tuple(x) for x in want_rounds], f"rank {rank} rounds"
     print(f"TP={world} {case} prompt {len(prompt)}: compared {len(want_tokens)} tokens and {len(want_rounds)} "

@@ -2,7 +2,8 @@
 
 argv: target container, drafter container ("-" for none), verify width, prompt (.npy of token
 ids), tokens to generate, output directory, and optionally a replay stream (.npy) with its
-mismatch rate and seed for the config-3 oracle drafter. Writes rank<r>.json with the greedy stream and the
+mismatch rate and seed for the config-3 oracle drafter. G4B_TEST_SAMPLING="temperature,top_p,
+top_k,seed" selects sampled decoding. Writes rank<r>.json with the greedy stream and the
 per-round records."""
 import json
 import os
@@ -39,7 +40,12 @@ def main():
         e.set_gate(0.45, -1)
         e.set_decode_options(replay=np.load(sys.argv[7]), mismatch_rate=float(sys.argv[8]),
                              mismatch_seed=int(sys.argv[9]))
-    toks = e.generate(prompt, int(n))
+    samp = os.environ.get("G4B_TEST_SAMPLING")  # "temperature,top_p,top_k,seed"
+    if samp:
+        t, tp, tk, seed = samp.split(",")
+        toks = e.generate(prompt, int(n), temperature=float(t), top_p=float(tp), top_k=int(tk), seed=int(seed))
+    else:
+        toks = e.generate(prompt, int(n))
     rounds = e.rounds()
     e.close()
     Path(out, f"rank{rank}.json").write_text(json.dumps({"tokens": toks.tolist(), "rounds": rounds}))

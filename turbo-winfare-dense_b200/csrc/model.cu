@@ -798,6 +798,40 @@ void DeviceModel::head(int M, bool want_logits, uint32_t* chain_out, StepParams*
                "head_finalize");
 }
 
+void DeviceModel::logits_to_host(int row0, int rows, float* dst) {
+    const size_t VL = (size_t)v_local_;
+    if (row0 < 0 || rows < 1 || row0 + rows > kMaxM) throw std::invalid_argument("logits_to_host: rows");
+    if (opt_.tp == 1) {
+        cuda_check(cudaMemcpyAsync(dst, logits_ + (size_t)row0 * VL, (size_t)rows * VL * 4, cudaMemcpyDeviceToHost,
+                                   stream_),
+                   "logits");
+        d2h_bytes_ += (uint64_t)rows * VL * 4;
+        cuda_check(cudaStreamSynchronize(stream_), "logits");
+        return;
+    }
+#ifdef G4B_HAVE_NCCL
+    if (!logits_gather_) logits_gather_ = static_cast<float*>(dmalloc((size_t)opt_.tp * kMaxM * VL * 4));
+    const size_t n = (size_t)rows * VL;
+    if (ncclAllGather(logits_ + (size_t)row0 * VL, logits_gather_, n, ncclFloat, (ncclComm_t)opt_.nccl_comm,
+                      stream_) != ncclSuccess)
+        throw std::runtime_error("ncclAllGather (logits) failed");
+    logits_stage_.resize((size_t)opt_.tp * n);
+    cuda_check(cudaMemcpyAsync(logits_stage_.data(), logits_gather_, logits_stage_.size() * 4, cudaMemcpyDeviceToHost,
+                               stream_),
+               "logits");
+    d2h_bytes_ += logits_stage_.size() * 4;
+    cuda_check(cudaStreamSynchronize(stream_), "logits");
+    // Gathered as [rank][row][vocab slice]; rank r's slice starts at vocabulary id r * VL.
+    const size_t V = VL * opt_.tp;
+    for (int r = 0; r < opt_.tp; ++r)
+        for (int i = 0; i < rows; ++i)
+            std::memcpy(dst + (size_t)i * V + (size_t)r * VL, logits_stage_.data() + (size_t)r * n + (size_t)i * VL,
+                        VL * 4);
+#else
+    throw std::runtime_error("logits_to_host: tensor parallelism needs NCCL");
+#endif
+}
+
 void DeviceModel::enqueue(int M, PassKind kind, bool want_logits, uint32_t* chain_out) {
     if (!loaded_) throw std::runtime_error("model not loaded");
     if (M < 1 || M > max_rows())

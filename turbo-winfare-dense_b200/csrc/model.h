@@ -97,6 +97,11 @@ class DeviceModel {
     StepParams* step_params(int slot) { return sp_dev_ + slot; }
     HeadResult* result_dev() { return res_dev_; }
     float* logits_dev() { return logits_; }  // [16][vocab_local] when a pass asked for them
+    // Copies `rows` full-vocabulary logits rows from row `row0` of the last pass that asked for
+    // logits into host `dst` ([rows][vocab]) and synchronizes the stream. Under tensor
+    // parallelism every rank's vocabulary slice is all-gathered first (every rank must call it,
+    // in the same order) and the slices are placed in rank order.
+    void logits_to_host(int row0, int rows, float* dst);
     uint32_t* chain_dev() { return chain_dev_; }
 
     // Enqueues one pass of M rows on the model's stream (graph-replayed when enabled): 1..16
@@ -202,6 +207,8 @@ class DeviceModel {
     unsigned* pcnt_ = nullptr; // prefill GEMM tile arrival counters
     float2* chunk_best_ = nullptr;
     float* logits_ = nullptr;
+    float* logits_gather_ = nullptr;  // [tp][16][vocab_local]: all-gathered logits rows (tp > 1)
+    std::vector<float> logits_stage_;
     void* sample_work_ = nullptr;      // device sampler workspace (allocated on first use)
     uint32_t* sample_out_ = nullptr;   // device: the sampled token
     uint32_t *rep_count_ = nullptr, *rep_ids_ = nullptr, *rep_stage_ = nullptr;  // repetition history

@@ -60,17 +60,11 @@ void Engine::forward_batch(const uint32_t* ids, uint32_t batch, uint32_t base, f
         throw std::invalid_argument("forward_batch: batch must be 1.." + std::to_string(target_->max_rows()));
     if (batch > (uint32_t)kBatchRows && out_logits && all_positions)
         throw std::invalid_argument("forward_batch: a batch of more than 16 rows returns the last row's logits only");
-    if (out_logits && target_->options().tp > 1)
-        throw std::invalid_argument("forward_batch: host logits are not gathered across tensor-parallel ranks");
     if (base + batch > (uint32_t)target_->max_context()) throw std::invalid_argument("forward_batch: context exceeds max_context");
     target_->run_plain((int)batch, (int)base, ids, out_logits != nullptr);
     if (out_logits) {
-        const size_t V = target_->vocab_local();
-        const size_t row0 = all_positions ? 0 : (size_t)DeviceModel::result_row((int)batch);
-        const size_t rows = all_positions ? batch : 1;
-        cuda_check(cudaMemcpyAsync(out_logits, target_->logits_dev() + row0 * V, rows * V * sizeof(float),
-                                   cudaMemcpyDeviceToHost, target_->stream()),
-                   "logits");
+        const int row0 = all_positions ? 0 : DeviceModel::result_row((int)batch);
+        target_->logits_to_host(row0, all_positions ? (int)batch : 1, out_logits);
     }
     cuda_check(cudaStreamSynchronize(target_->stream()), "forward_batch");
 }
@@ -94,11 +88,8 @@ uint32_t Engine::prefill(const std::vector<uint32_t>& toks, const GenerationOpti
     const int row = DeviceModel::result_row(m_last);
     last_row_ = row;
     if (!greedy && last) {
-        const size_t V = target_->vocab_local();
-        last->resize(V);
-        cuda_check(cudaMemcpy(last->data(), target_->logits_dev() + (size_t)row * V, V * sizeof(float),
-                              cudaMemcpyDeviceToHost),
-                   "logits");
+        last->resize(target_->header().vocab_size);
+        target_->logits_to_host(row, 1, last->data());
     }
     return r.argmax[row];
 }
@@ -112,8 +103,6 @@ std::vector<uint32_t> Engine::generate(const std::vector<uint32_t>& prompt, cons
     const bool greedy = sp.is_greedy();
     DeviceModel& T = *target_;
     const uint32_t V = T.header().vocab_size;
-    if (!greedy && T.options().tp > 1)
-        throw std::invalid_argument("sampled decoding needs full logits; tensor-parallel runs decode greedily");
     std::vector<uint32_t> history;
     for (uint32_t t : prompt) {
         if (t >= V) {
@@ -140,7 +129,9 @@ std::vector<uint32_t> Engine::generate(const std::vector<uint32_t>& prompt, cons
         draft_->reset();
         draft_->catch_up(history);
     }
-    const bool dev_sample = !greedy && !spec && opt.device_sampling;
+    // The device draw needs the whole vocabulary on one GPU; tensor-parallel ranks gather the
+    // logits rows and draw on the host.
+    const bool dev_sample = !greedy && !spec && opt.device_sampling && T.options().tp == 1;
     const uint32_t first = prefill(history, opt, dev_sample ? nullptr : &logits);
     if (spec && draft_) order(draft_->model().stream(), T.stream());  // decode starts after both prefills
     mtp_row_ = last_row_;  // the MTP drafter's first round starts from the prompt's last hidden state
@@ -195,7 +186,7 @@ std::vector<uint32_t> Engine::generate(const std::vector<uint32_t>& prompt, cons
                 uint32_t nx = r.argmax[0];
                 if (!greedy) {
                     verify.resize(V);
-                    cuda_check(cudaMemcpy(verify.data(), T.logits_dev(), V * 4, cudaMemcpyDeviceToHost), "logits");
+                    T.logits_to_host(0, 1, verify.data());
                     nx = sample_token(verify.data(), V, sp, seed_for(sp, (int)history.size()));
                 }
                 history.push_back(nx);
@@ -310,10 +301,7 @@ std::vector<uint32_t> Engine::generate(const std::vector<uint32_t>& prompt, cons
                 batch.insert(batch.end(), drafts.begin(), drafts.end());
                 T.run_plain((int)K, (int)len - 1, batch.data(), true);
                 verify.resize((size_t)K * V);
-                cuda_check(cudaMemcpyAsync(verify.data(), T.logits_dev(), (size_t)K * V * 4, cudaMemcpyDeviceToHost,
-                                           T.stream()),
-                           "logits");
-                cuda_check(cudaStreamSynchronize(T.stream()), "sync");
+                T.logits_to_host(0, (int)K, verify.data());
                 std::vector<const float*> per_pos;
                 for (uint32_t i = 0; i < K; ++i) per_pos.push_back(verify.data() + (size_t)i * V);
                 const SpeculativeEvaluation ev =
@@ -385,7 +373,7 @@ std::vector<uint32_t> Engine::generate(const std::vector<uint32_t>& prompt, cons
             next_greedy = r.argmax[0];
             if (!greedy) {
                 logits.resize(V);
-                cuda_check(cudaMemcpy(logits.data(), T.logits_dev(), V * 4, cudaMemcpyDeviceToHost), "logits");
+                T.logits_to_host(0, 1, logits.data());
             }
         }
     }
