@@ -2,6 +2,7 @@
 // nullptr / -1 with a thread-local message, as src/c_api.cpp does.
 #include "g4dense/c_api.h"
 
+#include <algorithm>
 #include <atomic>
 #include <cstdio>
 #include <cstdlib>
@@ -73,15 +74,26 @@ bool mtp_preset_header(const std::string& name, const g4b::G4DenseHeader& t, g4b
     return true;
 }
 
-// Model geometries for device-generated weights, with an optional ":layers=N" override.
+// Model geometries for device-generated weights, with optional ":layers=N" and ":shard=S"
+// overrides (comma-separated). shard=S gives the geometry one rank of an S-way tensor-parallel
+// run holds (query and KV heads, FFN width and vocabulary divided by S, at least one KV head), so
+// a single GPU can time one shard's kernels without the peer exchange.
 bool preset_header(const std::string& spec, g4b::G4DenseHeader& h) {
     std::string name = spec;
-    int layers = -1;
+    int layers = -1, shard = 1;
     const size_t colon = spec.find(':');
     if (colon != std::string::npos) {
         name = spec.substr(0, colon);
-        const std::string rest = spec.substr(colon + 1);
-        if (rest.rfind("layers=", 0) == 0) layers = std::atoi(rest.c_str() + 7);
+        std::string rest = spec.substr(colon + 1);
+        while (!rest.empty()) {
+            const size_t comma = rest.find(',');
+            const std::string kv = rest.substr(0, comma);
+            if (kv.rfind("layers=", 0) == 0) layers = std::atoi(kv.c_str() + 7);
+            else if (kv.rfind("shard=", 0) == 0) shard = std::atoi(kv.c_str() + 6);
+            else return false;
+            rest = comma == std::string::npos ? std::string() : rest.substr(comma + 1);
+        }
+        if (shard < 1) return false;
     }
     std::memset(&h, 0, sizeof(h));
     h.rope_theta_local = 10000.0f;
@@ -110,6 +122,14 @@ bool preset_header(const std::string& spec, g4b::G4DenseHeader& h) {
         h.num_layers = (uint32_t)layers;
         h.global_layer_mask &= (layers == 64) ? ~0ull : ((1ull << layers) - 1);
     }
+    if (shard > 1) {
+        if (h.num_q_heads % shard || h.d_ff % (64 * shard) || h.vocab_size % shard) return false;
+        h.num_q_heads /= shard;
+        h.num_kv_heads = std::max(1u, h.num_kv_heads / shard);
+        if (h.global_kv_heads) h.global_kv_heads = std::max(1u, h.global_kv_heads / shard);
+        h.d_ff /= shard;
+        h.vocab_size /= shard;
+    }
     for (uint32_t l = 0; l < h.num_layers; ++l) h.layer_d_ff[l] = h.d_ff;
     return true;
 }
@@ -125,7 +145,7 @@ g4b::GenerationOptions to_gen(const EngineHandle* e, const G4DenseGenerationOpti
         g.sampling.has_seed = o->has_seed != 0;
         g.sampling.seed = o->seed;
     }
-    g.speculative_enabled = e->draft_k > 0 && (e->engine->draft() != nullptr || e->engine->mtp() != nullptr);
+    g.speculative_enabled = e->draft_k > 0 && e->engine->has_drafter();
     g.draft_k = (uint32_t)std::max(0, e->draft_k);
     g.stop_token = e->stop_token;
     g.replay = e->replay;
@@ -261,10 +281,14 @@ G4DENSE_API void* g4dense_engine_create_ex(const G4DenseEngineConfig* cfg) {
                 d->load_mtp_synthetic(mh, cfg->draft_seed, cfg->synthetic_centered != 0, T);
             }
             h->engine->set_mtp(std::move(d));
+        } else if (((cfg->draft_path && *cfg->draft_path) || cfg->draft_preset) && mo.rank != 0) {
+            // Tensor parallelism: the drafter runs on rank 0 alone; this rank receives each
+            // round's drafts by broadcast.
+            h->engine->set_remote_draft(true);
         } else if ((cfg->draft_path && *cfg->draft_path) || cfg->draft_preset) {
-            // The drafter stays whole on every rank (it is small) and runs on its own stream, so
-            // its prompt catch-up overlaps the target's prefill; the engine orders the two
-            // streams with events where a round's passes depend on each other.
+            // The drafter runs whole on one GPU (rank 0 under tensor parallelism) on its own
+            // stream, so its prompt catch-up overlaps the target's prefill; the engine orders the
+            // two streams with events where a round's passes depend on each other.
             g4b::ModelOptions dopt;
             dopt.max_context = mo.max_context;
             dopt.kv_bf16 = mo.kv_bf16;

@@ -1,116 +1,138 @@
+// Container validation for the .g4dense v3 and .g4mtp v1 formats.
+//
+// The rules are the ones the formats impose (the reference enforces the same ones in
+// src/format.cpp:6-130): the magic and version, a layer count inside the header's tables, non-zero
+// geometry, 4096-byte aligned blocks that lie inside the file. On top of those come the rules this
+// engine needs to run a model (Gemma-4 architecture, INT4 G64 weights, tied embedding, widths in
+// whole 64-groups).
+//
+// The checks run to completion and every broken rule is reported in one G4DenseFormatError, so a
+// malformed file is diagnosed in one pass instead of one rule at a time.
 #include "format.h"
 
-#include <sstream>
-#include <utility>
+#include <cinttypes>
+#include <cstdarg>
+#include <cstdio>
+#include <string>
+#include <vector>
 
 namespace g4b {
 
+namespace {
+
+std::string fmt(const char* f, ...) __attribute__((format(printf, 1, 2)));
+std::string fmt(const char* f, ...) {
+    char buf[256];
+    va_list ap;
+    va_start(ap, f);
+    std::vsnprintf(buf, sizeof buf, f, ap);
+    va_end(ap);
+    return buf;
+}
+
+// Collects the rules a header breaks and raises them together.
+class Findings {
+   public:
+    explicit Findings(const char* what) : what_(what) {}
+    void expect(bool ok, std::string problem) {
+        if (!ok) problems_.push_back(std::move(problem));
+    }
+    bool clean() const { return problems_.empty(); }
+    void raise() const {
+        if (problems_.empty()) return;
+        std::string msg = what_;
+        msg += problems_.size() == 1 ? " is malformed: " : " is malformed (" + std::to_string(problems_.size()) + " problems): ";
+        for (size_t i = 0; i < problems_.size(); ++i) msg += (i ? "; " : "") + problems_[i];
+        throw G4DenseFormatError(msg);
+    }
+
+   private:
+    const char* what_;
+    std::vector<std::string> problems_;
+};
+
+// A block of the file: starts on a 4096-byte page, has a size, and (when the file size is known)
+// ends inside the file without the end overflowing 64 bits.
+void check_block(Findings& f, const std::string& name, uint64_t offset, uint64_t size, uint64_t file_size,
+                 uint64_t page, bool size_required) {
+    f.expect(offset % page == 0, fmt("%s starts at byte %" PRIu64 ", not on a %" PRIu64 "-byte page", name.c_str(),
+                                     offset, page));
+    if (size_required) f.expect(size != 0, name + " is empty");
+    const bool wraps = offset + size < offset;
+    f.expect(!wraps, name + ": offset + size overflows 64 bits");
+    if (file_size > 0 && !wraps)
+        f.expect(offset + size <= file_size, fmt("%s ends at byte %" PRIu64 ", past the end of the %" PRIu64 "-byte file",
+                                                 name.c_str(), offset + size, file_size));
+}
+
+}  // namespace
+
 void validate_header(const G4DenseHeader& h, uint64_t file_size) {
-    if (h.magic != G4DenseHeader::kMagic) {
-        std::stringstream ss;
-        ss << "Invalid magic: expected 0x" << std::hex << G4DenseHeader::kMagic << ", got 0x" << h.magic;
-        throw G4DenseFormatError(ss.str());
+    using H = G4DenseHeader;
+    Findings f("g4dense container");
+    f.expect(h.magic == H::kMagic, fmt("magic word is 0x%08X; a .g4dense file starts with 0x%08X ('G4DN')", h.magic,
+                                       H::kMagic));
+    f.expect(h.version == H::kVersion, fmt("format version %u; this library reads version %u", h.version, H::kVersion));
+    if (!f.clean()) f.raise();  // not this format: the remaining fields mean nothing
+    const bool layers_ok = h.num_layers >= 1 && h.num_layers <= H::kMaxLayers;
+    f.expect(layers_ok, fmt("%u layers; the header's tables hold 1..%u", h.num_layers, H::kMaxLayers));
+    f.expect(h.d_model && h.d_ff && h.vocab_size,
+             fmt("zero-sized geometry (d_model %u, d_ff %u, vocab %u)", h.d_model, h.d_ff, h.vocab_size));
+    check_block(f, "embedding block", h.embed_offset, 0, 0, H::kAlign, false);
+    check_block(f, "LM head block", h.lm_head_offset, 0, 0, H::kAlign, false);
+    if (layers_ok)
+        for (uint32_t i = 0; i < h.num_layers; ++i)
+            check_block(f, "layer " + std::to_string(i), h.layer_offsets[i], h.layer_sizes[i], file_size, H::kAlign, true);
+
+    // What this engine runs.
+    f.expect(h.quant_type == 1 && h.quant_group_size == 64,
+             fmt("quantization %u with group %u; only affine INT4 in groups of 64 (type 1) is supported", h.quant_type,
+                 h.quant_group_size));
+    f.expect(h.arch_type == 0, fmt("architecture %u; only Gemma 4 (0) is supported", h.arch_type));
+    f.expect(h.ple_dim == 0 && h.num_kv_shared_layers == 0, "per-layer embeddings and shared KV layers are not supported");
+    f.expect(h.tied_embeddings == 1 && h.lm_head_offset == h.embed_offset,
+             "the LM head must be the tied embedding table (same block)");
+    f.expect(h.d_model % 64 == 0, fmt("d_model %u is not a whole number of 64-wide groups", h.d_model));
+    if (file_size > 0 && h.d_model % 64 == 0) {
+        // Packed nibbles, bf16 scales and biases of the tied table, then the bf16 final norm.
+        const uint64_t table = (uint64_t)h.vocab_size * h.d_model / 2 + (uint64_t)h.vocab_size * (h.d_model / 64) * 4 +
+                               (uint64_t)h.d_model * 2;
+        check_block(f, "embedding table", h.embed_offset, table, file_size, H::kAlign, false);
     }
-    if (h.version != G4DenseHeader::kVersion) {
-        std::stringstream ss;
-        ss << "Unsupported container version: expected " << G4DenseHeader::kVersion << ", got " << h.version;
-        throw G4DenseFormatError(ss.str());
-    }
-    if (h.num_layers == 0 || h.num_layers > G4DenseHeader::kMaxLayers) {
-        std::stringstream ss;
-        ss << "Invalid layer count: " << h.num_layers << " (max " << G4DenseHeader::kMaxLayers << ")";
-        throw G4DenseFormatError(ss.str());
-    }
-    if (h.d_model == 0 || h.d_ff == 0 || h.vocab_size == 0)
-        throw G4DenseFormatError("Invalid model geometry dimensions (d_model, d_ff, or vocab_size is zero)");
-    if (h.embed_offset % G4DenseHeader::kAlign != 0) throw G4DenseFormatError("Embedding offset is not 4096-byte aligned");
-    if (h.lm_head_offset % G4DenseHeader::kAlign != 0) throw G4DenseFormatError("LM head offset is not 4096-byte aligned");
-    for (uint32_t i = 0; i < h.num_layers; ++i) {
-        if (h.layer_offsets[i] % G4DenseHeader::kAlign != 0) {
-            std::stringstream ss;
-            ss << "Layer " << i << " offset (" << h.layer_offsets[i] << ") is not 4096-byte aligned";
-            throw G4DenseFormatError(ss.str());
-        }
-        if (h.layer_sizes[i] == 0) {
-            std::stringstream ss;
-            ss << "Layer " << i << " has size 0";
-            throw G4DenseFormatError(ss.str());
-        }
-        if (h.layer_offsets[i] + h.layer_sizes[i] < h.layer_offsets[i]) throw G4DenseFormatError("layer bounds: arithmetic overflow");
-        if (file_size > 0 && h.layer_offsets[i] + h.layer_sizes[i] > file_size) {
-            std::stringstream ss;
-            ss << "Layer " << i << " extends beyond file bounds (offset=" << h.layer_offsets[i]
-               << ", size=" << h.layer_sizes[i] << ", file_size=" << file_size << ")";
-            throw G4DenseFormatError(ss.str());
-        }
-    }
-    // What this engine implements.
-    if (h.quant_type != 1 || h.quant_group_size != 64)
-        throw G4DenseFormatError("Unsupported quantization: only AFFINE_INT4_G64 is implemented");
-    if (h.arch_type != 0) throw G4DenseFormatError("Unsupported architecture: only Gemma 4 is implemented");
-    if (h.ple_dim != 0 || h.num_kv_shared_layers != 0)
-        throw G4DenseFormatError("Per-layer embeddings / KV sharing are not implemented");
-    if (h.tied_embeddings != 1 || h.lm_head_offset != h.embed_offset)
-        throw G4DenseFormatError("Only tied embedding / LM head containers are supported");
-    if (h.d_model % 64 || h.vocab_size == 0) throw G4DenseFormatError("d_model must be a multiple of 64");
-    if (file_size > 0) {
-        const uint64_t emb = (uint64_t)h.vocab_size * (h.d_model / 8) * 4 + (uint64_t)h.vocab_size * (h.d_model / 64) * 4 +
-                             (uint64_t)h.d_model * 2;
-        if (h.embed_offset + emb > file_size) throw G4DenseFormatError("Embedding block extends beyond file bounds");
-    }
+    f.raise();
 }
 
 void validate_mtp_header(const G4MtpHeader& h, uint64_t file_size) {
-    if (h.magic != G4MtpHeader::kMagic) {
-        std::stringstream ss;
-        ss << "Invalid MTP magic: expected 0x" << std::hex << G4MtpHeader::kMagic << ", got 0x" << h.magic;
-        throw G4DenseFormatError(ss.str());
-    }
-    if (h.version != G4MtpHeader::kVersion) {
-        std::stringstream ss;
-        ss << "Unsupported MTP container version: expected " << G4MtpHeader::kVersion << ", got " << h.version;
-        throw G4DenseFormatError(ss.str());
-    }
-    if (h.num_layers == 0 || h.num_layers > G4MtpHeader::kMaxLayers) {
-        std::stringstream ss;
-        ss << "Invalid MTP layer count: " << h.num_layers << " (max " << G4MtpHeader::kMaxLayers << ")";
-        throw G4DenseFormatError(ss.str());
-    }
-    if (h.backbone_hidden_size == 0 || h.hidden_size == 0 || h.intermediate_size == 0 || h.vocab_size == 0)
-        throw G4DenseFormatError(
-            "Invalid MTP model geometry dimensions (backbone_hidden, hidden_size, or vocab_size is zero)");
-    const std::pair<uint64_t, const char*> aligned[] = {{h.embed_offset, "embedding"},
-                                                        {h.pre_proj_offset, "pre-projection"},
-                                                        {h.post_proj_offset, "post-projection"},
-                                                        {h.norm_offset, "norm"}};
-    for (const auto& a : aligned)
-        if (a.first % G4MtpHeader::kAlign != 0)
-            throw G4DenseFormatError(std::string("MTP ") + a.second + " offset is not 4096-byte aligned");
-    for (uint32_t i = 0; i < h.num_layers; ++i) {
-        if (h.layer_offsets[i] % G4MtpHeader::kAlign != 0) {
-            std::stringstream ss;
-            ss << "MTP Layer " << i << " offset (" << h.layer_offsets[i] << ") is not 4096-byte aligned";
-            throw G4DenseFormatError(ss.str());
-        }
-        if (h.layer_sizes[i] == 0) {
-            std::stringstream ss;
-            ss << "MTP Layer " << i << " has size 0";
-            throw G4DenseFormatError(ss.str());
-        }
-        if (h.layer_offsets[i] + h.layer_sizes[i] < h.layer_offsets[i])
-            throw G4DenseFormatError("Integer overflow in MTP layer bounds");
-        if (file_size > 0 && h.layer_offsets[i] + h.layer_sizes[i] > file_size) {
-            std::stringstream ss;
-            ss << "MTP Layer " << i << " extends beyond file bounds (offset=" << h.layer_offsets[i]
-               << ", size=" << h.layer_sizes[i] << ", file_size=" << file_size << ")";
-            throw G4DenseFormatError(ss.str());
-        }
-    }
-    // Beyond the reference's checks: what this engine needs to run the drafter.
-    if (h.quant_type != 1 || (h.quant_group_size != 0 && h.quant_group_size != 64))
-        throw G4DenseFormatError("MTP container: only INT4 G64 weights are supported");
-    if (h.hidden_size % 64 || h.intermediate_size % 64 || h.backbone_hidden_size % 64)
-        throw G4DenseFormatError("MTP container: widths must be multiples of 64");
+    using H = G4MtpHeader;
+    Findings f("g4mtp drafter container");
+    f.expect(h.magic == H::kMagic, fmt("magic word is 0x%08X; a .g4mtp file starts with 0x%08X ('G4MT')", h.magic,
+                                       H::kMagic));
+    f.expect(h.version == H::kVersion, fmt("format version %u; this library reads version %u", h.version, H::kVersion));
+    if (!f.clean()) f.raise();
+    const bool layers_ok = h.num_layers >= 1 && h.num_layers <= H::kMaxLayers;
+    f.expect(layers_ok, fmt("%u layers; the header's tables hold 1..%u", h.num_layers, H::kMaxLayers));
+    f.expect(h.backbone_hidden_size && h.hidden_size && h.intermediate_size && h.vocab_size,
+             fmt("zero-sized geometry (backbone %u, hidden %u, intermediate %u, vocab %u)", h.backbone_hidden_size,
+                 h.hidden_size, h.intermediate_size, h.vocab_size));
+    struct Section {
+        const char* name;
+        uint64_t offset;
+    };
+    for (const Section& s : {Section{"embedding section", h.embed_offset}, Section{"pre-projection section", h.pre_proj_offset},
+                             Section{"post-projection section", h.post_proj_offset}, Section{"norm section", h.norm_offset}})
+        check_block(f, s.name, s.offset, 0, 0, H::kAlign, false);
+    if (layers_ok)
+        for (uint32_t i = 0; i < h.num_layers; ++i)
+            check_block(f, "drafter layer " + std::to_string(i), h.layer_offsets[i], h.layer_sizes[i], file_size,
+                        H::kAlign, true);
+
+    // What this engine runs.
+    f.expect(h.quant_type == 1 && (h.quant_group_size == 0 || h.quant_group_size == 64),
+             fmt("quantization %u with group %u; only affine INT4 in groups of 64 is supported", h.quant_type,
+                 h.quant_group_size));
+    f.expect(h.hidden_size % 64 == 0 && h.intermediate_size % 64 == 0 && h.backbone_hidden_size % 64 == 0,
+             "hidden, intermediate and backbone widths must be whole numbers of 64-wide groups");
+    f.raise();
 }
 
 }  // namespace g4b

@@ -57,8 +57,10 @@ inline uint32_t layer_ffn_width(const G4DenseHeader& h, uint32_t l) {
     return (l < G4DenseHeader::kMaxLayers && h.layer_d_ff[l] != 0) ? h.layer_d_ff[l] : h.d_ff;
 }
 
-// Throws G4DenseFormatError with the reference's messages (src/format.cpp:6-65), plus the
-// checks this engine needs to run the model (Gemma-4 architecture, INT4 G64, no PLE).
+// Throws one G4DenseFormatError naming every rule the header breaks: the format's own rules
+// (magic, version, layer count, geometry, aligned blocks inside the file; the reference checks the
+// same, src/format.cpp:6-65) and what this engine needs (Gemma-4 architecture, INT4 G64, no PLE,
+// tied embedding).
 void validate_header(const G4DenseHeader& h, uint64_t file_size);
 
 // The .g4mtp v1 container of the MTP "assistant" drafter: G4MtpHeader of
@@ -84,7 +86,7 @@ struct G4MtpHeader {
 #pragma pack(pop)
 static_assert(sizeof(G4MtpHeader) == 4096, "G4MtpHeader must be 4096 bytes");
 
-// validate_mtp_header (src/format.cpp:67-130), with the reference's messages.
+// The same for the MTP drafter's header (the reference's checks: src/format.cpp:67-130).
 void validate_mtp_header(const G4MtpHeader& h, uint64_t file_size);
 
 }  // namespace g4b

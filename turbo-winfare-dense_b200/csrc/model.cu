@@ -457,9 +457,15 @@ void DeviceModel::init_tp_peers() {
     if (opt_.tp > kMaxTp) throw std::runtime_error("tensor parallelism supports at most 8 ranks");
     const int d = h_.d_model;
     const size_t ybytes = (size_t)2 * max_rows() * d * sizeof(float);
-    // One cudaMalloc holds both parities and the two flag words (IPC maps whole allocations).
-    void* base = dmalloc(ybytes + 256);
-    cuda_check(cudaMemset(base, 0, ybytes + 256), "memset");
+    // Verify rows' push exchange: per parity, one receive row block and one flag block per
+    // source rank.
+    const size_t rbytes = (size_t)2 * kMaxTp * kMaxM * d * sizeof(float);
+    const size_t rfbytes = (size_t)2 * kMaxTp * kMaxM * kTpFlagCtas * sizeof(unsigned);
+    // One cudaMalloc holds both parities, the two flag words and the receive areas (IPC maps
+    // whole allocations).
+    const size_t total = ybytes + 256 + rbytes + rfbytes;
+    void* base = dmalloc(total);
+    cuda_check(cudaMemset(base, 0, total), "memset");
     tp_buf_ = static_cast<float*>(base);
     tp_flags_ = reinterpret_cast<unsigned*>(static_cast<char*>(base) + ybytes);
     tp_seq_ = static_cast<unsigned*>(dmalloc(sizeof(unsigned)));
@@ -484,6 +490,8 @@ void DeviceModel::init_tp_peers() {
         }
         tp_peer_y_[r] = static_cast<float*>(p);
         tp_peer_flags_[r] = reinterpret_cast<unsigned*>(static_cast<char*>(p) + ybytes);
+        tp_peer_recv_[r] = reinterpret_cast<float*>(static_cast<char*>(p) + ybytes + 256);
+        tp_peer_rflag_[r] = reinterpret_cast<unsigned*>(static_cast<char*>(p) + ybytes + 256 + rbytes);
     }
 #endif
 }
@@ -502,6 +510,13 @@ TpGather DeviceModel::tp_gather(int step, int parity) const {
         }
         g.own_flag = tp_flags_ + parity;
         g.seq = tp_seq_;
+        const size_t rrow = (size_t)kMaxM * h_.d_model, rflag = (size_t)kMaxM * kTpFlagCtas;
+        for (int r = 0; r < opt_.tp; ++r) {
+            g.push_dst[r] = tp_peer_recv_[r] + ((size_t)parity * kMaxTp + opt_.rank) * rrow;
+            g.push_flag[r] = tp_peer_rflag_[r] + ((size_t)parity * kMaxTp + opt_.rank) * rflag;
+        }
+        g.recv = tp_peer_recv_[opt_.rank] + (size_t)parity * kMaxTp * rrow;
+        g.recv_flag = tp_peer_rflag_[opt_.rank] + (size_t)parity * kMaxTp * rflag;
     }
     return g;
 }
@@ -550,10 +565,9 @@ double DeviceModel::profile_gemms(int M, int reps, uint64_t* bytes, int* gemm_la
     for (int r = 0; r < reps; ++r) {
         for (auto& L : layers_) {
             gemm(L.qkv, bf_d_, M, nullptr);
-            // Under TP the dense output goes to y_: peers may still read this rank's partial buffers.
-            gemm(L.o, bf_attn_, M, opt_.tp > 1 ? y_ : nullptr);
+            gemm(L.o, bf_attn_, M, nullptr);
             gemm(L.gateup, bf_d_, M, nullptr);
-            gemm(L.down, bf_ff_, M, opt_.tp > 1 ? y_ : nullptr);
+            gemm(L.down, bf_ff_, M, nullptr);
         }
         gemm(lm_, bf_d_, M, nullptr);
     }
@@ -748,12 +762,13 @@ void DeviceModel::enqueue_raw(int M, PassKind kind, bool want_logits, uint32_t* 
         aa.scale = 1.0f;
         cuda_check(g4b_attention(aa, bf_attn_, stream_, pdl), "attention");
         // o projection + post-attention norm / residual + pre-FFN norm
-        // Under tensor parallelism the o and down GEMMs finish their own split-K sum into this
-        // rank's peer-mapped partial buffer and the norm epilogue sums the ranks' partials
-        // over NVLink (TpGather); otherwise the epilogue sums the slots.
-        gemm(L.o, bf_attn_, M, tp_out(0));
+        // The o and down GEMMs leave split-K slots. The norm epilogue sums them; under tensor
+        // parallelism it first stores this rank's sums into its peer-mapped partial buffer,
+        // publishes, and then adds the ranks' partials in rank order over NVLink (TpGather).
+        // (Summing in the GEMM's last-arriving CTA instead serialises a long slot list behind
+        // one CTA: about 12 us per GEMM at TP = 2.)
+        gemm(L.o, bf_attn_, M, nullptr);
         GemmOut oo = partials(L.o, M);
-        if (opt_.tp > 1) oo = GemmOut{PartView{}, nullptr, d};
         cuda_check(g4b_rowepi(oo, tp_gather(2 * (int)l, 0), hres_[cur], hres_[1 - cur], L.pa_norm, 1.0f, L.pf_norm, d,
                               bf_d_, M, stream_, pdl),
                    "post_attn");
@@ -761,9 +776,8 @@ void DeviceModel::enqueue_raw(int M, PassKind kind, bool want_logits, uint32_t* 
         // FFN
         gemm(L.gateup, bf_d_, M, nullptr);
         cuda_check(g4b_geglu(partials(L.gateup, M), L.F, bf_ff_, M, stream_, pdl), "geglu");
-        gemm(L.down, bf_ff_, M, tp_out(1));
+        gemm(L.down, bf_ff_, M, nullptr);
         GemmOut dn = partials(L.down, M);
-        if (opt_.tp > 1) dn = GemmOut{PartView{}, nullptr, d};
         const bool last = l + 1 == layers_.size();
         const uint16_t* w_next = last ? final_norm_ : layers_[l + 1].in_norm;
         cuda_check(g4b_rowepi(dn, tp_gather(2 * (int)l + 1, 1), hres_[cur], hres_[1 - cur], L.pffn_norm, L.scalar,
@@ -829,6 +843,36 @@ void DeviceModel::logits_to_host(int row0, int rows, float* dst) {
                         VL * 4);
 #else
     throw std::runtime_error("logits_to_host: tensor parallelism needs NCCL");
+#endif
+}
+
+void DeviceModel::bcast_step_tokens(int n) {
+    if (opt_.tp == 1 || n <= 0) return;
+#ifdef G4B_HAVE_NCCL
+    uint32_t* t = sp_dev_[0].tokens + 1;
+    if (ncclBroadcast(t, t, (size_t)n, ncclUint32, 0, (ncclComm_t)opt_.nccl_comm, stream_) != ncclSuccess)
+        throw std::runtime_error("ncclBroadcast (draft tokens) failed");
+#endif
+}
+
+void DeviceModel::bcast_host_u32(uint32_t* v, int n) {
+    if (opt_.tp == 1 || n <= 0) return;
+#ifdef G4B_HAVE_NCCL
+    constexpr int kMax = 4 * kPrefillRows;
+    if (n > kMax) throw std::invalid_argument("bcast_host_u32: too many words");
+    if (!bcast_buf_) bcast_buf_ = static_cast<uint32_t*>(dmalloc(kMax * sizeof(uint32_t)));
+    if (opt_.rank == 0) {
+        cuda_check(cudaMemcpyAsync(bcast_buf_, v, (size_t)n * 4, cudaMemcpyHostToDevice, stream_), "bcast");
+        h2d_bytes_ += (uint64_t)n * 4;
+    }
+    if (ncclBroadcast(bcast_buf_, bcast_buf_, (size_t)n, ncclUint32, 0, (ncclComm_t)opt_.nccl_comm, stream_) !=
+        ncclSuccess)
+        throw std::runtime_error("ncclBroadcast (host words) failed");
+    if (opt_.rank != 0) {
+        cuda_check(cudaMemcpyAsync(v, bcast_buf_, (size_t)n * 4, cudaMemcpyDeviceToHost, stream_), "bcast");
+        d2h_bytes_ += (uint64_t)n * 4;
+    }
+    cuda_check(cudaStreamSynchronize(stream_), "bcast");
 #endif
 }
 

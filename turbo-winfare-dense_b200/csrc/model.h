@@ -102,6 +102,13 @@ class DeviceModel {
     // parallelism every rank's vocabulary slice is all-gathered first (every rank must call it,
     // in the same order) and the slices are placed in rank order.
     void logits_to_host(int row0, int rows, float* dst);
+    // Tensor parallelism with the drafter on rank 0 only. bcast_step_tokens: on the model's
+    // stream, rank 0's StepParams slot-0 tokens [1, 1 + n) (the drafts its drafter chained there)
+    // are broadcast into every rank's slot 0, ahead of the verify pass that reads them.
+    // bcast_host_u32: rank 0's host words `v[0..n)` replace every rank's (synchronizes). Every
+    // rank must call them, in the same order; at tp = 1 they do nothing.
+    void bcast_step_tokens(int n);
+    void bcast_host_u32(uint32_t* v, int n);
     uint32_t* chain_dev() { return chain_dev_; }
 
     // Enqueues one pass of M rows on the model's stream (graph-replayed when enabled): 1..16
@@ -199,6 +206,8 @@ class DeviceModel {
     float* tp_buf_ = nullptr;
     unsigned* tp_flags_ = nullptr;
     unsigned* tp_seq_ = nullptr;
+    float* tp_peer_recv_[kMaxTp] = {};      // each rank's receive areas [2][tp][16][d] (peer-mapped)
+    unsigned* tp_peer_rflag_[kMaxTp] = {};  // and flags [2][tp][16][kTpFlagCtas]
     float* tp_peer_y_[kMaxTp] = {};
     unsigned* tp_peer_flags_[kMaxTp] = {};
     std::vector<void*> tp_ipc_open_;
@@ -208,6 +217,7 @@ class DeviceModel {
     float2* chunk_best_ = nullptr;
     float* logits_ = nullptr;
     float* logits_gather_ = nullptr;  // [tp][16][vocab_local]: all-gathered logits rows (tp > 1)
+    uint32_t* bcast_buf_ = nullptr;   // device staging of bcast_host_u32
     std::vector<float> logits_stage_;
     void* sample_work_ = nullptr;      // device sampler workspace (allocated on first use)
     uint32_t* sample_out_ = nullptr;   // device: the sampled token

@@ -249,6 +249,35 @@ __device__ void tp_sync(const TpGather& tg, bool publisher) {
     __syncthreads();
 }
 
+// Tensor parallelism, verify rows: the CTA has pushed its columns' sums of this rank's split-K
+// slots into every rank's receive area (its own included). Once the CTA's stores are done it
+// raises its flag in every rank (release at system scope after the CTA barrier), then waits,
+// bounded, on this rank's local flags of the same CTA position from every peer: the CTAs of a
+// row own the same columns on every rank, so nothing else needs to have arrived.
+__device__ void tp_push_publish_wait(const TpGather& tg, int m, int slot) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        const unsigned epoch = *tg.seq * 256u + (unsigned)tg.step + 1u;
+        __threadfence_system();
+        for (int r = 0; r < tg.n; ++r)
+            asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(tg.push_flag[r] + m * kTpFlagCtas + slot),
+                         "r"(epoch)
+                         : "memory");
+        for (int r = 0; r < tg.n; ++r) {
+            if (r == tg.rank) continue;
+            const unsigned* f = tg.recv_flag + (r * kMaxM + m) * kTpFlagCtas + slot;
+            const uint64_t t0 = global_ns();
+            while ((int)(ld_acquire_sys(f) - epoch) < 0) {
+                if (global_ns() - t0 > kWaitLimitNs) {
+                    atomicExch(tg.err, 3);
+                    break;
+                }
+            }
+        }
+    }
+    __syncthreads();
+}
+
 // Columns c, c+1 of row m summed over the ranks in rank order (peer partials bypass the caches).
 __device__ __forceinline__ float2 tp_pair(const TpGather& tg, int m, int ld, int c) {
     float2 s = make_float2(0.f, 0.f);
@@ -303,7 +332,27 @@ __global__ void __launch_bounds__(CLUSTER ? kEpiWarps * 32 : kEpiMaxWarps * 32) 
         return kPreloadW ? (e ? wv1[j].y : wv1[j].x) : (w1 ? bf16_to_f32(w1[c]) : 1.f);
     };
     auto wt2 = [&](int j, int e, int c) { return kPreloadW ? (e ? wv2[j].y : wv2[j].x) : bf16_to_f32(w2[c]); };
-    if (tg.n > 1) tp_sync(tg, blockIdx.x == 0 && blockIdx.y == 0);
+    // Under tensor parallelism with split-K slots (verify rows): this rank's sums of the CTA's
+    // columns go to every rank's receive area; the ranks' sums are then added in rank order from
+    // local memory. A dense GEMM output (prefill chunks) is read from the ranks' buffers instead.
+    const bool tp_push = tg.n > 1 && o.part.part != nullptr;
+    if (tg.n > 1) {
+        if (tp_push) {
+#pragma unroll
+            for (int j = 0; j < GPW; ++j) {
+                const int gi = rank * gpc + warp + nw * j;
+                const int c0 = gi * 64 + 2 * lane;
+                if (gi < g_end && c0 < d) {
+                    const float2 v = gemm_out_pair(o, m, c0);
+                    for (int r = 0; r < tg.n; ++r)
+                        *reinterpret_cast<float2*>(tg.push_dst[r] + (size_t)m * d + c0) = v;
+                }
+            }
+            tp_push_publish_wait(tg, m, rank);
+        } else {
+            tp_sync(tg, blockIdx.x == 0 && blockIdx.y == 0);  // the GEMM wrote the buffer itself
+        }
+    }
 
     float2 y[GPW], h[GPW];
     // A cluster CTA with at least twice as many warps as groups (d = 1536: 2 groups, 8 warps)
@@ -338,7 +387,18 @@ __global__ void __launch_bounds__(CLUSTER ? kEpiWarps * 32 : kEpiMaxWarps * 32) 
         if (wpg < 2 || j > 0 || warp >= gpc) y[j] = make_float2(0.f, 0.f);
         h[j] = make_float2(0.f, 0.f);
         if (gi < g_end && c0 < d) {
-            if (wpg < 2) y[j] = tg.n > 1 ? tp_pair(tg, m, o.ld, c0) : gemm_out_pair(o, m, c0);
+            if (wpg < 2) {
+                if (tp_push) {
+                    y[j] = make_float2(0.f, 0.f);
+                    for (int r = 0; r < tg.n; ++r) {
+                        const float2 v = __ldcg(reinterpret_cast<const float2*>(tg.recv + ((size_t)r * kMaxM + m) * d + c0));
+                        y[j].x += v.x;
+                        y[j].y += v.y;
+                    }
+                } else {
+                    y[j] = tg.n > 1 ? tp_pair(tg, m, d, c0) : gemm_out_pair(o, m, c0);
+                }
+            }
             if (h_in) h[j] = *reinterpret_cast<const float2*>(h_in + (size_t)m * d + c0);
             const float ca = y[j].x * wt1(j, 0, c0), cb = y[j].y * wt1(j, 1, c0 + 1);
             acc.x += y[j].x * y[j].x + y[j].y * y[j].y;

@@ -122,7 +122,7 @@ std::vector<uint32_t> Engine::generate(const std::vector<uint32_t>& prompt, cons
     const uint64_t l0 = T.launches() + (draft_ ? draft_->model().launches() : 0);
     const uint64_t h0 = T.h2d_bytes() + (draft_ ? draft_->model().h2d_bytes() : 0);
     const uint64_t d0 = T.d2h_bytes() + (draft_ ? draft_->model().d2h_bytes() : 0);
-    const bool spec = opt.speculative_enabled && (draft_ || mtp_) && opt.draft_k > 0;
+    const bool spec = opt.speculative_enabled && has_drafter() && opt.draft_k > 0;
     if (spec && draft_) {
         // The drafter's pass over the prompt is prefill work: queue it on the drafter's stream
         // first so it runs alongside the target's prefill.
@@ -161,10 +161,15 @@ std::vector<uint32_t> Engine::generate(const std::vector<uint32_t>& prompt, cons
         // Two kinds of drafter: a separate model with its own KV (DraftRuntime) or the MTP
         // assistant (src/mtp_runner.cpp), which reads the target's KV and hidden state and runs
         // on the target's stream.
+        // Under tensor parallelism only rank 0 holds the drafter (Dmp is null elsewhere): its
+        // drafts reach the other ranks by broadcast before each verify pass.
         DraftRuntime* Dp = draft_.get();
         DeviceModel* Mt = mtp_.get();
-        DeviceModel& Dm = Dp ? Dp->model() : *Mt;
-        if (Dm.header().vocab_size != V) throw std::invalid_argument("drafter vocabulary differs from the target's");
+        DeviceModel* Dmp = Dp ? &Dp->model() : Mt;
+        if (Dmp && Dmp->header().vocab_size != V)
+            throw std::invalid_argument("drafter vocabulary differs from the target's");
+        const bool tp_multi = T.options().tp > 1;
+        const bool evaluates = !tp_multi || T.options().rank == 0;
         const uint32_t K = std::min<uint32_t>(opt.draft_k, kMaxDraftWidth);
         uint32_t drafted_total = 0, accepted_total = 0;
         bool drafting = true;
@@ -242,7 +247,6 @@ std::vector<uint32_t> Engine::generate(const std::vector<uint32_t>& prompt, cons
                 n_acc = (uint32_t)r.n_accepted;
                 emitted_now.assign(r.tokens, r.tokens + r.n_emit);
             } else if (greedy) {
-                DraftRuntime& D = *Dp;
                 StepParams tp{}, dp{};
                 tp.base_pos = (int)len - 1;
                 tp.tokens[0] = pending;
@@ -251,21 +255,25 @@ std::vector<uint32_t> Engine::generate(const std::vector<uint32_t>& prompt, cons
                 dp.tokens[unseen] = pending;
                 const bool replay = !opt.replay.empty();
                 T.push_params(0, tp);
-                // The drafter's steps write their tokens into the target's step parameters:
-                // after the target's parameter copy, and before the verify pass reads them.
-                order(T.stream(), Dm.stream());
-                Dm.push_params(1, dp, (int)unseen + 1);
-                uint32_t* chain = replay ? Dm.chain_dev() : T.step_params(0)->tokens + 1;
-                for (uint32_t s = 0; s + 1 < K; ++s)
-                    Dm.enqueue(s == 0 ? (int)unseen + 1 : 1, PassKind::DraftStep, false, chain);
-                D.set_consumed(len - 1);
+                if (Dp) {
+                    // The drafter's steps write their tokens into the target's step parameters:
+                    // after the target's parameter copy, and before the verify pass reads them.
+                    DeviceModel& Dm = *Dmp;
+                    order(T.stream(), Dm.stream());
+                    Dm.push_params(1, dp, (int)unseen + 1);
+                    uint32_t* chain = replay ? Dm.chain_dev() : T.step_params(0)->tokens + 1;
+                    for (uint32_t s = 0; s + 1 < K; ++s)
+                        Dm.enqueue(s == 0 ? (int)unseen + 1 : 1, PassKind::DraftStep, false, chain);
+                    Dp->set_consumed(len - 1);
+                }
                 if (replay) {
                     for (uint32_t s = 0; s + 1 < K; ++s)
                         tp.tokens[s + 1] = replay_propose(opt.replay, prompt.size(), len + s, opt.mismatch_rate,
                                                           opt.mismatch_seed, V);
                     T.push_params(0, tp);
                 }
-                order(Dm.stream(), T.stream());  // replay too: the verify waits for the drafts
+                if (Dp) order(Dmp->stream(), T.stream());  // replay too: the verify waits for the drafts
+                T.bcast_step_tokens((int)K - 1);           // rank 0's drafts into every rank's pass
                 T.enqueue((int)K, PassKind::Plain, false, nullptr);
                 const HeadResult r = T.fetch_result();
                 n_acc = (uint32_t)r.n_accepted;
@@ -276,7 +284,8 @@ std::vector<uint32_t> Engine::generate(const std::vector<uint32_t>& prompt, cons
                 std::vector<std::vector<float>> draft_logits;
                 uint32_t cur = pending;
                 int pos = (int)len - 1;
-                for (uint32_t s = 0; s + 1 < K; ++s) {
+                for (uint32_t s = 0; Dmp && s + 1 < K; ++s) {
+                    DeviceModel& Dm = *Dmp;
                     if (Mt) {
                         StepParams mp{};
                         mp.base_pos = (int)len - 2;
@@ -297,17 +306,28 @@ std::vector<uint32_t> Engine::generate(const std::vector<uint32_t>& prompt, cons
                     draft_logits.push_back(dl);
                     cur = cand;
                 }
+                drafts.resize(K - 1);
+                T.bcast_host_u32(drafts.data(), (int)K - 1);  // rank 0's drafts to every rank
                 std::vector<uint32_t> batch = {pending};
                 batch.insert(batch.end(), drafts.begin(), drafts.end());
                 T.run_plain((int)K, (int)len - 1, batch.data(), true);
                 verify.resize((size_t)K * V);
                 T.logits_to_host(0, (int)K, verify.data());
-                std::vector<const float*> per_pos;
-                for (uint32_t i = 0; i < K; ++i) per_pos.push_back(verify.data() + (size_t)i * V);
-                const SpeculativeEvaluation ev =
-                    speculator_.evaluate_verification(drafts, per_pos, V, sp, seed_for(sp, (int)len), draft_logits);
-                n_acc = ev.num_accepted;
-                emitted_now = ev.accepted_tokens;
+                // The ratio test needs the drafter's logits, so rank 0 decides and broadcasts
+                // {accepted, count, tokens...}.
+                std::vector<uint32_t> res(K + 2, 0u);
+                if (evaluates) {
+                    std::vector<const float*> per_pos;
+                    for (uint32_t i = 0; i < K; ++i) per_pos.push_back(verify.data() + (size_t)i * V);
+                    const SpeculativeEvaluation ev =
+                        speculator_.evaluate_verification(drafts, per_pos, V, sp, seed_for(sp, (int)len), draft_logits);
+                    res[0] = ev.num_accepted;
+                    res[1] = (uint32_t)ev.accepted_tokens.size();
+                    std::copy(ev.accepted_tokens.begin(), ev.accepted_tokens.end(), res.begin() + 2);
+                }
+                if (tp_multi) T.bcast_host_u32(res.data(), (int)K + 2);
+                n_acc = res[0];
+                emitted_now.assign(res.begin() + 2, res.begin() + 2 + std::min<uint32_t>(res[1], K));
             }
             const size_t forwarded = (len - 1) + (K - 1);
             int this_emit = 0;

@@ -89,6 +89,10 @@ class Engine {
     // The MTP assistant drafter: a DeviceModel loaded with load_mtp*, on the target's stream.
     void set_mtp(std::unique_ptr<DeviceModel> m) { mtp_ = std::move(m); }
     DeviceModel* mtp() { return mtp_.get(); }
+    // Tensor parallelism: the drafter lives on rank 0 only. The other ranks set this and take
+    // each round's drafts (and, when sampling, its acceptance result) by broadcast from rank 0.
+    void set_remote_draft(bool on) { remote_draft_ = on; }
+    bool has_drafter() const { return draft_ || mtp_ || remote_draft_; }
 
     // One pass over `batch` consecutive positions from base_position (runner.hpp:110-111).
     // out_logits (host) receives the last row's logits, or all rows' when all_positions.
@@ -110,6 +114,7 @@ class Engine {
     std::unique_ptr<DeviceModel> target_;
     std::unique_ptr<DraftRuntime> draft_;
     std::unique_ptr<DeviceModel> mtp_;
+    bool remote_draft_ = false;
     int mtp_row_ = 0;  // row of the target's normed hidden states the next MTP round starts from
     cudaEvent_t order_ev_[2] = {nullptr, nullptr};
     int order_i_ = 0;
