@@ -457,13 +457,11 @@ void DeviceModel::init_tp_peers() {
     if (opt_.tp > kMaxTp) throw std::runtime_error("tensor parallelism supports at most 8 ranks");
     const int d = h_.d_model;
     const size_t ybytes = (size_t)2 * max_rows() * d * sizeof(float);
-    // Verify rows' push exchange: per parity, one receive row block and one flag block per
-    // source rank.
-    const size_t rbytes = (size_t)2 * kMaxTp * kMaxM * d * sizeof(float);
-    const size_t rfbytes = (size_t)2 * kMaxTp * kMaxM * kTpFlagCtas * sizeof(unsigned);
-    // One cudaMalloc holds both parities, the two flag words and the receive areas (IPC maps
+    // Verify rows' push exchange: per parity, one block of {value, epoch} words per source rank.
+    const size_t rbytes = (size_t)2 * kMaxTp * kMaxM * d * sizeof(uint2);
+    // One cudaMalloc holds both parities, the two flag words and the receive words (IPC maps
     // whole allocations).
-    const size_t total = ybytes + 256 + rbytes + rfbytes;
+    const size_t total = ybytes + 256 + rbytes;
     void* base = dmalloc(total);
     cuda_check(cudaMemset(base, 0, total), "memset");
     tp_buf_ = static_cast<float*>(base);
@@ -490,8 +488,7 @@ void DeviceModel::init_tp_peers() {
         }
         tp_peer_y_[r] = static_cast<float*>(p);
         tp_peer_flags_[r] = reinterpret_cast<unsigned*>(static_cast<char*>(p) + ybytes);
-        tp_peer_recv_[r] = reinterpret_cast<float*>(static_cast<char*>(p) + ybytes + 256);
-        tp_peer_rflag_[r] = reinterpret_cast<unsigned*>(static_cast<char*>(p) + ybytes + 256 + rbytes);
+        tp_peer_recv_[r] = reinterpret_cast<uint2*>(static_cast<char*>(p) + ybytes + 256);
     }
 #endif
 }
@@ -510,13 +507,10 @@ TpGather DeviceModel::tp_gather(int step, int parity) const {
         }
         g.own_flag = tp_flags_ + parity;
         g.seq = tp_seq_;
-        const size_t rrow = (size_t)kMaxM * h_.d_model, rflag = (size_t)kMaxM * kTpFlagCtas;
-        for (int r = 0; r < opt_.tp; ++r) {
+        const size_t rrow = (size_t)kMaxM * h_.d_model;
+        for (int r = 0; r < opt_.tp; ++r)
             g.push_dst[r] = tp_peer_recv_[r] + ((size_t)parity * kMaxTp + opt_.rank) * rrow;
-            g.push_flag[r] = tp_peer_rflag_[r] + ((size_t)parity * kMaxTp + opt_.rank) * rflag;
-        }
         g.recv = tp_peer_recv_[opt_.rank] + (size_t)parity * kMaxTp * rrow;
-        g.recv_flag = tp_peer_rflag_[opt_.rank] + (size_t)parity * kMaxTp * rflag;
     }
     return g;
 }

@@ -206,8 +206,7 @@ class DeviceModel {
     float* tp_buf_ = nullptr;
     unsigned* tp_flags_ = nullptr;
     unsigned* tp_seq_ = nullptr;
-    float* tp_peer_recv_[kMaxTp] = {};      // each rank's receive areas [2][tp][16][d] (peer-mapped)
-    unsigned* tp_peer_rflag_[kMaxTp] = {};  // and flags [2][tp][16][kTpFlagCtas]
+    uint2* tp_peer_recv_[kMaxTp] = {};  // each rank's receive words [2][tp][16][d] {value, epoch} (peer-mapped)
     float* tp_peer_y_[kMaxTp] = {};
     unsigned* tp_peer_flags_[kMaxTp] = {};
     std::vector<void*> tp_ipc_open_;

@@ -159,7 +159,6 @@ struct QkvEpiArgs {
 // so all ranks compute identical sums. Two buffer/flag parities alternate between the o and the
 // down projection, so a buffer is rewritten only after every rank has consumed it.
 constexpr int kMaxTp = 8;
-constexpr int kTpFlagCtas = 16;  // flag slots per row: one per norm-epilogue CTA of the row
 struct TpGather {
     const float* y[kMaxTp];        // each rank's partial buffer for this step (peer-mapped)
     const unsigned* flag[kMaxTp];  // each rank's flag word for this step's parity (peer-mapped)
@@ -167,12 +166,11 @@ struct TpGather {
     const unsigned* seq;           // passes completed on this rank (advanced by head_finalize)
     int n, rank, step;             // ranks (1: no gather), this rank, step index within a pass
     int* err;                      // set to 3 if a peer's flag never arrived
-    // Verify rows (M <= 16) whose GEMM left split-K slots: each norm-epilogue CTA pushes its
-    // columns' sums into every rank's receive area and raises a per-CTA flag there.
-    float* push_dst[kMaxTp];       // rank r's receive rows for data from this rank ([16][d], peer-mapped)
-    unsigned* push_flag[kMaxTp];   // rank r's flags for data from this rank ([16][kTpFlagCtas], peer-mapped)
-    const float* recv;             // this rank's receive area for the parity: [source rank][16][d]
-    const unsigned* recv_flag;     // and its flags: [source rank][16][kTpFlagCtas]
+    // Verify rows (M <= 16) whose GEMM left split-K slots: each norm-epilogue thread stores its
+    // columns' sums, each value paired with the step's epoch in one 8-byte word, into every peer's
+    // receive area; readers poll their own words until the epochs match (no fences or flags).
+    uint2* push_dst[kMaxTp];       // rank r's receive words for data from this rank ([16][d], peer-mapped)
+    const uint2* recv;             // this rank's receive words for the parity: [source rank][16][d]
 };
 
 struct AttnArgs {

@@ -249,33 +249,46 @@ __device__ void tp_sync(const TpGather& tg, bool publisher) {
     __syncthreads();
 }
 
-// Tensor parallelism, verify rows: the CTA has pushed its columns' sums of this rank's split-K
-// slots into every rank's receive area (its own included). Once the CTA's stores are done it
-// raises its flag in every rank (release at system scope after the CTA barrier), then waits,
-// bounded, on this rank's local flags of the same CTA position from every peer: the CTAs of a
-// row own the same columns on every rank, so nothing else needs to have arrived.
-__device__ void tp_push_publish_wait(const TpGather& tg, int m, int slot) {
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        const unsigned epoch = *tg.seq * 256u + (unsigned)tg.step + 1u;
-        __threadfence_system();
-        for (int r = 0; r < tg.n; ++r)
-            asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(tg.push_flag[r] + m * kTpFlagCtas + slot),
-                         "r"(epoch)
-                         : "memory");
-        for (int r = 0; r < tg.n; ++r) {
-            if (r == tg.rank) continue;
-            const unsigned* f = tg.recv_flag + (r * kMaxM + m) * kTpFlagCtas + slot;
-            const uint64_t t0 = global_ns();
-            while ((int)(ld_acquire_sys(f) - epoch) < 0) {
-                if (global_ns() - t0 > kWaitLimitNs) {
-                    atomicExch(tg.err, 3);
-                    break;
-                }
+// Tensor parallelism, verify rows: values travel with their step's epoch in the same 8-byte word
+// ({value bits, epoch}), written by one 16-byte store per column pair, so a reader that sees both
+// epochs of a pair sees both values; no fence or separate flag is needed. Stores and polls are
+// volatile (relaxed, system scope) and bypass L1.
+__device__ __forceinline__ void st_volatile_v4(void* p, uint4 v) {
+    asm volatile("st.volatile.global.v4.u32 [%0], {%1, %2, %3, %4};" ::"l"(p), "r"(v.x), "r"(v.y), "r"(v.z), "r"(v.w)
+                 : "memory");
+}
+__device__ __forceinline__ uint4 ld_volatile_v4(const void* p) {
+    uint4 v;
+    asm volatile("ld.volatile.global.v4.u32 {%0, %1, %2, %3}, [%4];" : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+                 : "l"(p)
+                 : "memory");
+    return v;
+}
+// Columns c, c+1 of row m from every rank, added in rank order (this rank's own from `mine`).
+// Waits, bounded, for each peer's words of this step.
+__device__ float2 tp_ll_sum(const TpGather& tg, int m, int d, int c, float2 mine, unsigned epoch) {
+    float2 s = make_float2(0.f, 0.f);
+    for (int r = 0; r < tg.n; ++r) {
+        float2 v = mine;
+        if (r != tg.rank) {
+            const uint2* src = tg.recv + ((size_t)r * kMaxM + m) * d + c;
+            uint4 w = ld_volatile_v4(src);
+            if (w.y != epoch || w.w != epoch) {
+                const uint64_t t0 = global_ns();
+                do {
+                    w = ld_volatile_v4(src);
+                    if (global_ns() - t0 > kWaitLimitNs) {
+                        atomicExch(tg.err, 3);
+                        break;
+                    }
+                } while (w.y != epoch || w.w != epoch);
             }
+            v = make_float2(__uint_as_float(w.x), __uint_as_float(w.z));
         }
+        s.x += v.x;
+        s.y += v.y;
     }
-    __syncthreads();
+    return s;
 }
 
 // Columns c, c+1 of row m summed over the ranks in rank order (peer partials bypass the caches).
@@ -336,19 +349,23 @@ __global__ void __launch_bounds__(CLUSTER ? kEpiWarps * 32 : kEpiMaxWarps * 32) 
     // columns go to every rank's receive area; the ranks' sums are then added in rank order from
     // local memory. A dense GEMM output (prefill chunks) is read from the ranks' buffers instead.
     const bool tp_push = tg.n > 1 && o.part.part != nullptr;
+    float2 mine[GPW];
+    unsigned epoch = 0;
     if (tg.n > 1) {
         if (tp_push) {
+            epoch = *tg.seq * 256u + (unsigned)tg.step + 1u;
 #pragma unroll
             for (int j = 0; j < GPW; ++j) {
                 const int gi = rank * gpc + warp + nw * j;
                 const int c0 = gi * 64 + 2 * lane;
+                mine[j] = make_float2(0.f, 0.f);
                 if (gi < g_end && c0 < d) {
-                    const float2 v = gemm_out_pair(o, m, c0);
+                    mine[j] = gemm_out_pair(o, m, c0);
+                    const uint4 w = make_uint4(__float_as_uint(mine[j].x), epoch, __float_as_uint(mine[j].y), epoch);
                     for (int r = 0; r < tg.n; ++r)
-                        *reinterpret_cast<float2*>(tg.push_dst[r] + (size_t)m * d + c0) = v;
+                        if (r != tg.rank) st_volatile_v4(tg.push_dst[r] + (size_t)m * d + c0, w);
                 }
             }
-            tp_push_publish_wait(tg, m, rank);
         } else {
             tp_sync(tg, blockIdx.x == 0 && blockIdx.y == 0);  // the GEMM wrote the buffer itself
         }
@@ -389,12 +406,7 @@ __global__ void __launch_bounds__(CLUSTER ? kEpiWarps * 32 : kEpiMaxWarps * 32) 
         if (gi < g_end && c0 < d) {
             if (wpg < 2) {
                 if (tp_push) {
-                    y[j] = make_float2(0.f, 0.f);
-                    for (int r = 0; r < tg.n; ++r) {
-                        const float2 v = __ldcg(reinterpret_cast<const float2*>(tg.recv + ((size_t)r * kMaxM + m) * d + c0));
-                        y[j].x += v.x;
-                        y[j].y += v.y;
-                    }
+                    y[j] = tp_ll_sum(tg, m, d, c0, mine[j], epoch);
                 } else {
                     y[j] = tg.n > 1 ? tp_pair(tg, m, d, c0) : gemm_out_pair(o, m, c0);
                 }
