@@ -128,6 +128,13 @@ G4DENSE_API int g4dense_engine_set_device_sampling(void* handle, int on);
  * Additive; returns 0 or -1. */
 G4DENSE_API int g4dense_engine_mtp_draft(void* handle, unsigned int seed_token, int context_length, int hidden_row,
                                          int k, unsigned int* out_tokens, float* out_logits);
+/* DraftRuntime::generate_draft_tokens (src/draft_runtime.cpp:46-95) with greedy drafting, for an
+ * engine with a separate drafter model: k chained one-row drafter steps (k <= 64) from `token` at
+ * position `pos` over the drafter's current KV cache (each step writes its own position's K/V),
+ * each step's argmax feeding the next. out_tokens receives the k drafts; out_logits (host, may be
+ * NULL) each step's softcapped logits [k][vocab]. Additive; returns 0 or -1. */
+G4DENSE_API int g4dense_engine_draft_steps(void* handle, unsigned int token, int pos, int k, unsigned int* out_tokens,
+                                           float* out_logits);
 /* Per-round (drafted, accepted, emitted) triples of the last speculative generation. */
 G4DENSE_API int g4dense_engine_last_rounds(void* handle, int* out, int cap_triples);
 G4DENSE_API int g4dense_nccl_unique_id(void* out128);

@@ -424,6 +424,45 @@ G4DENSE_API int g4dense_engine_forward_batch(void* handle, const unsigned int* t
     }
 }
 
+// Greedy drafting by the separate drafter model, DraftRuntime::generate_draft_tokens's greedy case
+// (src/draft_runtime.cpp:46-95) on the device: k chained one-row steps from `token` at position
+// `pos` over the drafter's current KV cache, each step's argmax feeding the next. Writes the k
+// drafted tokens and, when out_logits is non-null, each step's softcapped logits [k][vocab].
+G4DENSE_API int g4dense_engine_draft_steps(void* handle, unsigned int token, int pos, int k, unsigned int* out_tokens,
+                                           float* out_logits) {
+    clear_error();
+    if (!handle || pos < 0 || k < 1 || k > 64 || !out_tokens) {
+        set_error("Invalid arguments");
+        return -1;
+    }
+    try {
+        g4b::Engine& E = *static_cast<EngineHandle*>(handle)->engine;
+        if (!E.draft()) throw std::invalid_argument("no drafter model loaded");
+        g4b::DeviceModel& m = E.draft()->model();
+        if (pos + k > m.max_context()) throw std::invalid_argument("pos + k exceeds the drafter's KV capacity");
+        const int V = (int)m.header().vocab_size;
+        g4b::StepParams p{};
+        p.base_pos = pos;
+        p.tokens[0] = token % (unsigned)V;
+        m.push_params(1, p, 1);
+        for (int s = 0; s < k; ++s) {
+            m.enqueue(1, g4b::PassKind::DraftStep, out_logits != nullptr, m.chain_dev());
+            if (out_logits)
+                g4b::cuda_check(cudaMemcpyAsync(out_logits + (size_t)s * V, m.logits_dev(), (size_t)V * 4,
+                                                cudaMemcpyDeviceToHost, m.stream()),
+                                "logits");
+        }
+        g4b::cuda_check(cudaMemcpyAsync(out_tokens, m.chain_dev(), (size_t)k * 4, cudaMemcpyDeviceToHost, m.stream()),
+                        "tokens");
+        g4b::cuda_check(cudaStreamSynchronize(m.stream()), "sync");
+        m.check_device_error();
+        return 0;
+    } catch (const std::exception& ex) {
+        set_error(ex.what());
+        return -1;
+    }
+}
+
 G4DENSE_API int g4dense_engine_mtp_draft(void* handle, unsigned int seed_token, int context_length, int hidden_row,
                                          int k, unsigned int* out_tokens, float* out_logits) {
     clear_error();
@@ -594,6 +633,38 @@ G4DENSE_API double g4dense_engine_time_pass(void* handle, int which, int batch, 
         g4b::DeviceModel* m = which == 0 ? &e->engine->target()
                                          : (e->engine->draft() ? &e->engine->draft()->model() : nullptr);
         if (!m) throw std::invalid_argument("no drafter loaded");
+        if (which == 3) {  // chained one-row drafter steps from position pos, as a speculative round runs them
+            if (batch != 1 || pos + 2 * reps + 2 > m->max_context())
+                throw std::invalid_argument("drafter steps are one row, inside the KV capacity");
+            g4b::StepParams p{};
+            p.base_pos = pos;
+            p.tokens[0] = 1;
+            m->push_params(1, p, 1);
+            for (int r = 0; r < 2; ++r) m->enqueue(1, g4b::PassKind::DraftStep, false, m->chain_dev());
+            p.base_pos = pos;
+            m->push_params(1, p, 1);
+            cudaEvent_t a, b;
+            g4b::cuda_check(cudaEventCreate(&a), "event");
+            g4b::cuda_check(cudaEventCreate(&b), "event");
+            g4b::cuda_check(cudaEventRecord(a, m->stream()), "event");
+            for (int r = 0; r < reps; ++r) {
+                if (r % 32 == 31) {  // the chain list holds 64 tokens: restart it between bursts
+                    g4b::cuda_check(cudaEventRecord(b, m->stream()), "event");
+                    g4b::cuda_check(cudaEventSynchronize(b), "event");
+                    p.base_pos = pos + r;
+                    m->push_params(1, p, 1);
+                }
+                m->enqueue(1, g4b::PassKind::DraftStep, false, m->chain_dev());
+            }
+            g4b::cuda_check(cudaEventRecord(b, m->stream()), "event");
+            g4b::cuda_check(cudaEventSynchronize(b), "event");
+            m->check_device_error();
+            float ms = 0.f;
+            cudaEventElapsedTime(&ms, a, b);
+            cudaEventDestroy(a);
+            cudaEventDestroy(b);
+            return (double)ms / reps;
+        }
         if (batch > m->max_rows()) throw std::invalid_argument("batch exceeds the model's rows per pass");
         if (pos + batch > m->max_context()) throw std::invalid_argument("pos + batch exceeds the KV capacity");
         std::vector<uint32_t> toks(batch, 1);

@@ -78,6 +78,7 @@ def _bind_engine(L):
                                                     ctypes.c_double, ctypes.c_ulonglong]
     L.g4dense_engine_set_device_sampling.argtypes = [_vp, ctypes.c_int]
     L.g4dense_engine_mtp_draft.argtypes = [_vp, ctypes.c_uint, ctypes.c_int, ctypes.c_int, ctypes.c_int, _vp, _vp]
+    L.g4dense_engine_draft_steps.argtypes = [_vp, ctypes.c_uint, ctypes.c_int, ctypes.c_int, _vp, _vp]
     L.g4b_sample_workspace.restype = ctypes.c_size_t
     L.g4b_sample_token.argtypes = [_vp, ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.c_int,
                                    ctypes.c_uint64, _vp, _vp, _vp]
@@ -287,6 +288,16 @@ class Engine:
         if lib().g4dense_engine_mtp_draft(self.h, seed_token, context_length, hidden_row, k,
                                           toks.ctypes.data_as(_vp), logits.ctypes.data_as(_vp)):
             _eng_err("g4dense_engine_mtp_draft")
+        return toks, logits
+
+    def draft_steps(self, token, pos, k, vocab=None):
+        """Greedy drafting by the separate drafter: k chained one-row steps from `token` at position
+        `pos` -> (tokens [k], logits [k][vocab] or None)."""
+        toks = np.zeros(k, np.uint32)
+        logits = None if vocab is None else np.zeros((k, vocab), np.float32)
+        if lib().g4dense_engine_draft_steps(self.h, token, pos, k, toks.ctypes.data_as(_vp),
+                                            None if logits is None else logits.ctypes.data_as(_vp)):
+            _eng_err("g4dense_engine_draft_steps")
         return toks, logits
 
     STAT_KEYS = ("emitted", "decode_gpu_ms", "ttft_ms", "total_ms", "drafted", "accepted", "rounds",

@@ -98,6 +98,13 @@ E2B_DRAFT = ModelSpec(num_layers=35, d_model=1536, d_ff=6144, num_q_heads=8, num
                       head_dim=256, vocab_size=262144, sliding_window=512)
 
 
+# A mid-size drafter (a test aid): d 512 (four k-tiles per projection), FFN 2048, GQA 4 over two KV
+# heads of 128 and a 64-key window that 200 chained steps wrap, at a size the CPU oracle runs in
+# seconds.
+MID_TEST_DRAFT = ModelSpec(num_layers=3, d_model=512, d_ff=2048, num_q_heads=8, num_kv_heads=2, head_dim=128,
+                             vocab_size=4096, sliding_window=64)
+
+
 # Gemma-4-31B attention geometry at toy width (a test aid): sliding layers with head_dim 256 and
 # GQA 2 over a 48-key window (the KV ring wraps), one full-attention layer with head_dim 512, a
 # single KV head (GQA 4) and V taken from the raw K.

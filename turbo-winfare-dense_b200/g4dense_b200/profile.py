@@ -6,7 +6,8 @@ profiler started with `--profile-from-start off` sees exactly that piece.
         one forward pass of the 31B-shaped target (or the E2B-shaped drafter) with M rows at
         positions P..P+M-1 (attention spans P earlier cache entries), after 5 timed warm
         passes; prints their mean CUDA-event time. `mtp`: one step of the 31B assistant's MTP
-        drafter (M = 1) attending the target's P cached positions.
+        drafter (M = 1) attending the target's P cached positions. `draftstep`: chained one-row
+        E2B-shaped drafter steps from position P, as a speculative round runs them.
     python -m g4dense_b200.profile gemms [--only NAME] [--batch M]
         each distinct verify-GEMM shape of the 31B pass once (the kernel as the pass runs it:
         split-K slots left for the consuming epilogue), through the g4b_qmat C-ABI.
@@ -51,9 +52,16 @@ def run_pass(which, batch, pos, layers=0, ctx=4096, kv_bf16=False):
         e = Engine(preset="gemma4-31b", seed=0, draft_preset="gemma4-31b-assistant", draft_seed=2, max_context=4096,
                    device=0)
         slot = 2
+    elif which == "draftstep":
+        # Chained one-row E2B-shaped drafter steps, as a speculative round runs them. The small
+        # target only hosts the drafter.
+        e = Engine(preset="config0-target", seed=0, draft_preset="gemma4-e2b", draft_seed=1, max_context=4096,
+                   device=0)
+        slot = 3
+        batch = 1
     else:
         e = Engine(preset="gemma4-e2b", seed=1, max_context=4096, device=0)
-    ms = e.time_pass(slot, batch, 5, pos=pos)
+    ms = e.time_pass(slot, batch, 20 if which == "draftstep" else 5, pos=pos)
     start, stop = _profiler()
     start()
     e.time_pass(slot, batch, 1, pos=pos)
@@ -139,7 +147,7 @@ def main(argv=None):
     ap = argparse.ArgumentParser(prog="python -m g4dense_b200.profile")
     sub = ap.add_subparsers(dest="cmd", required=True)
     p = sub.add_parser("pass")
-    p.add_argument("--which", choices=["target", "draft", "mtp"], default="target")
+    p.add_argument("--which", choices=["target", "draft", "mtp", "draftstep"], default="target")
     p.add_argument("--ctx", type=int, default=4096, help="KV capacity (target)")
     p.add_argument("--kv-bf16", action="store_true", help="bf16 KV cache (target, long-context mode)")
     p.add_argument("--batch", type=int, default=5)
