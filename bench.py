@@ -254,12 +254,14 @@ def run_b200(args, rank, world):
     ms, gbytes, glaunch = eng.profile_gemms(VERIFY_WIDTH, reps=5)
     achieved = gbytes / (ms / 1000.0) / 1e9
     peak, peak_kind = peaks()
-    traffic = None  # DRAM bytes per 5-row pass from the committed ncu summary
+    traffic = None  # DRAM bytes per 5-row pass from the committed ncu summary (a full, TP = 1 pass)
     tf = REPO / "profiles" / "vgemm_31b_shapes_m5.md"
     if tf.exists():
         for ln in tf.read_text().splitlines():
             if ln.startswith("traffic_bytes_per_pass:"):
                 traffic = int(ln.split(":")[1])
+    if traffic is not None and world > 1:
+        traffic = traffic // world  # one rank's shard streams 1/TP of the pass's weight bytes
 
     # Speculative weight-bytes bound: per round the target streams its weights once (split over
     # the ranks) and the drafter its weights K-1 times (on one GPU, serially); the tokens a round
@@ -285,7 +287,8 @@ def run_b200(args, rank, world):
                      "peak_kind": peak_kind, "unit": "GB/s", "frac": achieved / peak, "traffic": traffic,
                      "algorithmic_bytes_per_pass": gbytes, "launches_per_pass": glaunch,
                      "traffic_per": "pass (sum of dram__bytes_read+write over the pass's GEMM launches, ncu; "
-                                    "profiles/vgemm_31b_shapes_m5.md)",
+                                    "profiles/vgemm_31b_shapes_m5.md" + (f"; scaled to one rank's 1/{world} shard"
+                                                                         if world > 1 else "") + ")",
                      "ms_per_pass": ms},
         "prefill": {"prompt_tokens": PROMPT_LEN,
                     "ttft_ms": sum(s["ttft_ms"] for s in stats) / args.steps,
