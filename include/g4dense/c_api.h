@@ -6,13 +6,15 @@
  * returned strings stay valid until the next call on the same handle). A binding written
  * against the reference links against this library unchanged.
  *
- * The second block is additive. The reference drives its engine with text through a
- * tokenizer; this path is driven by token ids, and speculation / tensor parallelism /
- * synthetic weights are enabled through g4dense_engine_create_ex without changing any
- * existing signature.
+ * The second block is additive: generation from token ids, speculation / tensor parallelism /
+ * synthetic weights through g4dense_engine_create_ex, and the tokenizer on its own
+ * (g4dense_tokenizer_*, the reference's Tokenizer / IncrementalDetokenizer /
+ * StreamingStopMatcher), all without changing any existing signature.
  */
 #ifndef G4DENSE_C_API_H
 #define G4DENSE_C_API_H
+
+#include <stddef.h>
 
 #ifdef __cplusplus
 extern "C" {
@@ -27,9 +29,13 @@ extern "C" {
 G4DENSE_API void* g4dense_engine_create(const char* container_path);
 /* src/c_api.cpp:79-82 */
 G4DENSE_API void g4dense_engine_destroy(void* handle);
-/* Text generation (src/c_api.cpp:84-112). This path has no tokenizer (the reference's
- * tokenizer.json is not part of it), so this returns nullptr with last_error set; use
- * g4dense_engine_generate_tokens. */
+/* Text generation (src/c_api.cpp:84-112): the prompt becomes one user turn of the chat
+ * template, is encoded without a second <bos> and decoded with temperature 0.2, top_p 0.95,
+ * top_k 64 and max_tokens (512 when <= 0), stopping after a tokenizer stop id
+ * (src/runner.cpp:2060-2347). Returns the concatenated decode_single pieces of the emitted
+ * tokens (the stop token's included; "" for special tokens). Needs the engine's tokenizer
+ * (G4DenseEngineConfig.tokenizer_path, else $G4DENSE_TOKENIZER, else tokenizer.json beside the
+ * container or in the working directory); without one, nullptr with last_error set. */
 G4DENSE_API const char* g4dense_engine_generate(void* handle, const char* prompt, int max_tokens);
 /* JSON telemetry with the reference's keys for the fields this engine measures
  * (src/c_api.cpp:114-119, src/telemetry.cpp:11-48). "{}" for a null handle. */
@@ -54,8 +60,10 @@ G4DENSE_API void g4dense_options_default(G4DenseGenerationOptions* out);
 
 typedef int (*G4DenseTokenCallback)(void* user, int index, unsigned int token_id, const char* delta);
 
-/* Chat-message generation (src/c_api.cpp:121-162). Text needs a tokenizer: returns nullptr
- * with last_error set, as g4dense_engine_generate does. */
+/* src/c_api.cpp:121-162. As the reference does, the messages_json text itself is the user
+ * turn of the chat template (it is not parsed into messages); opts as given (NULL: the
+ * runner's defaults). on_token receives each emitted token with its decode_single piece;
+ * returning 0 stops generation. Returns the concatenated pieces, as g4dense_engine_generate. */
 G4DENSE_API const char* g4dense_engine_generate_ex(void* handle, const char* messages_json,
                                                    const G4DenseGenerationOptions* opts,
                                                    G4DenseTokenCallback on_token, void* user);
@@ -90,6 +98,9 @@ typedef struct {
     int device;                  /* CUDA device ordinal (-1 = current) */
     double gate_min_accept;      /* adaptive gate (default 0.45 over 24 drafts) */
     int gate_window;
+    const char* tokenizer_path;  /* tokenizer.json for the text entry points, or NULL to look for
+                                    $G4DENSE_TOKENIZER, then tokenizer.json beside the container,
+                                    then in the working directory (none found: text calls fail) */
 } G4DenseEngineConfig;
 
 G4DENSE_API void g4dense_config_default(G4DenseEngineConfig* out);
@@ -102,6 +113,13 @@ G4DENSE_API void* g4dense_engine_create_ex(const G4DenseEngineConfig* cfg);
 G4DENSE_API const char* g4dense_engine_generate_tokens(void* handle, const unsigned int* prompt_ids, int n_prompt,
                                                        const G4DenseGenerationOptions* opts,
                                                        G4DenseTokenCallback on_token, void* user);
+/* ForwardRunner::generate(prompt, options) (src/runner.cpp:2060-2347) with the choice the
+ * reference leaves to GenerationOptions::use_chat_template (include/g4dense/runner.hpp:50):
+ * use_chat_template != 0 wraps `prompt` in one user turn and encodes it without <bos>;
+ * 0 encodes it as given with <bos>. Otherwise as g4dense_engine_generate_ex. */
+G4DENSE_API const char* g4dense_engine_generate_text(void* handle, const char* prompt, int use_chat_template,
+                                                     const G4DenseGenerationOptions* opts,
+                                                     G4DenseTokenCallback on_token, void* user);
 /* Copies up to `cap` ids of the last generation into out; returns the count. */
 G4DENSE_API int g4dense_engine_last_tokens(void* handle, unsigned int* out, int cap);
 /* ForwardRunner::forward_batch (include/g4dense/runner.hpp:110-111): one pass over `batch`
@@ -158,6 +176,58 @@ G4DENSE_API double g4dense_engine_time_pass(void* handle, int which, int batch, 
  * GEMM launches per pass. A measurement hook for the verify-GEMM bandwidth metric. */
 G4DENSE_API double g4dense_engine_profile_gemms(void* handle, int batch, int reps, unsigned long long* bytes,
                                                 int* launches);
+
+/* ---- tokenizer (include/g4dense/tokenizer.hpp, include/g4dense/detokenizer.hpp) ----------
+ * Strings returned by these calls stay valid until the next call on the same object; byte
+ * lengths are written to *out_len (when non-NULL) because decoded text may hold NUL bytes. */
+
+/* Tokenizer::load_vocabulary(path) then set_architecture(arch): arch 0 = Gemma-4,
+ * 1 = Muse-Glimmer (ModelArch, include/g4dense/format.hpp:114-117). nullptr on error. */
+G4DENSE_API void* g4dense_tokenizer_open(const char* tokenizer_json_path, int arch);
+/* The tokenizer an engine loaded (owned by the engine), or nullptr when it has none. */
+G4DENSE_API void* g4dense_engine_tokenizer(void* handle);
+G4DENSE_API void g4dense_tokenizer_destroy(void* tok);
+/* Tokenizer::encode (src/tokenizer.cpp:472-520) of text[0..len). Writes up to `cap` ids and
+ * returns the full count (call again with a larger buffer when it exceeds cap), -1 on error. */
+G4DENSE_API int g4dense_tokenizer_encode(void* tok, const char* text, size_t len, int add_bos, unsigned int* out,
+                                         int cap);
+/* Tokenizer::decode / decode_single (src/tokenizer.cpp:526-632). */
+G4DENSE_API const char* g4dense_tokenizer_decode(void* tok, const unsigned int* ids, int n, int skip_special,
+                                                 size_t* out_len);
+G4DENSE_API const char* g4dense_tokenizer_decode_single(void* tok, unsigned int id, int skip_special,
+                                                        size_t* out_len);
+/* Tokenizer::apply_chat_template (src/tokenizer.cpp:638-672) of a JSON array of
+ * {"role": ..., "content": ...} objects. nullptr on error (malformed JSON, a Gemma-4 system
+ * message that is not first). */
+G4DENSE_API const char* g4dense_tokenizer_chat_template(void* tok, const char* messages_json);
+/* out[0..6) = bos, eos, pad, unk, end_of_turn, vocab_size; returns 0 or -1. */
+G4DENSE_API int g4dense_tokenizer_special_ids(void* tok, unsigned int* out6);
+/* Writes up to cap stop ids (Tokenizer::stop_token_ids); returns their count. */
+G4DENSE_API int g4dense_tokenizer_stop_ids(void* tok, unsigned int* out, int cap);
+/* 1 when `id` is a byte-fallback token (*value = its byte), else 0. */
+G4DENSE_API int g4dense_tokenizer_byte_value(void* tok, unsigned int id, unsigned char* value);
+/* 1 when `id` is marked special in added_tokens, else 0. */
+G4DENSE_API int g4dense_tokenizer_is_special(void* tok, unsigned int id);
+
+/* IncrementalDetokenizer (src/detokenizer.cpp:7-40) over a tokenizer that must outlive it. */
+G4DENSE_API void* g4dense_detokenizer_create(void* tok, int skip_special);
+G4DENSE_API const char* g4dense_detokenizer_push(void* detok, unsigned int id, size_t* out_len);
+G4DENSE_API const char* g4dense_detokenizer_finish(void* detok, size_t* out_len);
+G4DENSE_API void g4dense_detokenizer_destroy(void* detok);
+
+/* StreamingStopMatcher (src/detokenizer.cpp:44-101). */
+G4DENSE_API void* g4dense_stop_matcher_create(const char* const* stops, int n);
+G4DENSE_API const char* g4dense_stop_matcher_push(void* m, const char* text, size_t len, size_t* out_len);
+G4DENSE_API const char* g4dense_stop_matcher_finish(void* m, size_t* out_len);
+/* 1 once a stop string matched (*matched, when non-NULL, points at it), else 0. */
+G4DENSE_API int g4dense_stop_matcher_stopped(void* m, const char** matched);
+G4DENSE_API void g4dense_stop_matcher_destroy(void* m);
+
+/* utf8_repair (src/tokenizer.cpp:563-598): appends the repaired prefix of in[0..len) and
+ * returns it; *consumed = bytes of `in` used. The string stays valid until the next call on
+ * this thread. */
+G4DENSE_API const char* g4dense_utf8_repair(const char* in, size_t len, int flush_all, size_t* consumed,
+                                            size_t* out_len);
 
 #ifdef __cplusplus
 }

@@ -2,7 +2,8 @@
 // (include/g4dense/runner.hpp:25-157, src/runner.cpp:906-2347), with the model fully resident on
 // one B200 (or tensor-parallel over the ranks of the DeviceContext). The reference's Vulkan,
 // streaming and tier machinery has no counterpart: everything is resident, so tiers and the layer
-// cache are gone; its tokenizer sits outside this path, so generation takes token ids.
+// cache are gone. Text goes through the Tokenizer given at construction (or set_tokenizer);
+// generate_tokens takes token ids directly.
 #pragma once
 #include <atomic>
 #include <cstdint>
@@ -13,6 +14,7 @@
 
 #include "g4dense/device_context.hpp"
 #include "g4dense/sampling.hpp"
+#include "g4dense/tokenizer.hpp"
 
 namespace g4dense {
 
@@ -22,12 +24,12 @@ struct GenerationOptions {
     bool speculative_enabled{false};  // off by default, as in the reference
     uint32_t draft_k{6};              // verify width K (K - 1 drafts); the B200 path takes 2..16
     uint32_t active_tier_id{1};       // accepted and ignored: every layer is resident
-    bool use_chat_template{true};     // the token-id entry point never applies a template
+    bool use_chat_template{true};     // generate(): wrap the prompt in one user turn (generate_tokens: unused)
     int64_t stop_token{-1};           // additive: < 0 = none
 };
 
-// Called once per emitted token; returning false stops generation. `piece` is the token's text in
-// the reference; here it is empty (no tokenizer on this path).
+// Called once per emitted token; returning false stops generation. `piece` is
+// Tokenizer::decode_single(token) ("" from generate_tokens when the runner has no tokenizer).
 using TokenCallback = std::function<bool(uint32_t token, const std::string& piece)>;
 
 // Per-round record of speculative decoding: (drafted, accepted, emitted).
@@ -38,6 +40,9 @@ struct RoundRecord {
 class G4DENSE_CXX_API ForwardRunner {
    public:
     ForwardRunner(std::shared_ptr<DeviceContext> ctx, const std::string& container_path);
+    // The reference's constructor (include/g4dense/runner.hpp:60-62): the tokenizer serves generate().
+    ForwardRunner(std::shared_ptr<DeviceContext> ctx, std::shared_ptr<Tokenizer> tokenizer,
+                  const std::string& container_path);
     ~ForwardRunner();
     ForwardRunner(const ForwardRunner&) = delete;
     ForwardRunner& operator=(const ForwardRunner&) = delete;
@@ -56,12 +61,18 @@ class G4DENSE_CXX_API ForwardRunner {
                        bool all_positions = false);
     void forward_single_token(uint32_t token_id, uint32_t position, float* out_logits);
 
-    // The reference's text entry point: throws std::runtime_error (the tokenizer is not part of
-    // this path); use generate_tokens.
+    // The reference's text entry point (src/runner.cpp:2060-2347): the prompt is wrapped in one
+    // user turn of the chat template and encoded without another <bos> (use_chat_template), or
+    // encoded with <bos>; generation stops after any of the tokenizer's stop ids, and on_token
+    // receives each emitted token with its decode_single piece. Throws std::runtime_error without
+    // a loaded tokenizer.
     void generate(const std::string& prompt, const GenerationOptions& options, TokenCallback on_token,
                   std::atomic<bool>* cancel_flag = nullptr);
+    // Sets the tokenizer (its architecture follows the container once initialized).
+    void set_tokenizer(std::shared_ptr<Tokenizer> tokenizer);
     // Generation from token ids: prompt prefill, then the speculative round loop (when enabled and
-    // a drafter is loaded) or the plain loop. Returns the emitted tokens.
+    // a drafter is loaded) or the plain loop. Stops only on options.stop_token (no tokenizer stop
+    // ids). Returns the emitted tokens.
     std::vector<uint32_t> generate_tokens(const std::vector<uint32_t>& prompt_ids, const GenerationOptions& options,
                                           TokenCallback on_token = nullptr, std::atomic<bool>* cancel_flag = nullptr);
     // Round records of the last generate_tokens call.

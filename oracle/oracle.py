@@ -329,6 +329,39 @@ def reference_lib():
                                           ctypes.c_int, ctypes.c_float, ctypes.c_float, ctypes.c_int,
                                           ctypes.c_int, ctypes.c_uint64, ctypes.c_double, ctypes.c_int,
                                           ctypes.c_int64, _vp, _vp, ctypes.c_int, _vp]
+        sz = ctypes.POINTER(ctypes.c_size_t)
+        lib.ref_tok_open.restype = _vp
+        lib.ref_tok_open.argtypes = [ctypes.c_char_p, ctypes.c_int]
+        lib.ref_tok_close.argtypes = [_vp]
+        lib.ref_tok_encode.argtypes = [_vp, ctypes.c_char_p, ctypes.c_size_t, ctypes.c_int, _vp, ctypes.c_int]
+        lib.ref_tok_decode.restype = _vp
+        lib.ref_tok_decode.argtypes = [_vp, _vp, ctypes.c_int, ctypes.c_int, sz]
+        lib.ref_tok_decode_single.restype = _vp
+        lib.ref_tok_decode_single.argtypes = [_vp, ctypes.c_uint32, ctypes.c_int, sz]
+        lib.ref_tok_chat_template.restype = ctypes.c_char_p
+        lib.ref_tok_chat_template.argtypes = [_vp, ctypes.POINTER(ctypes.c_char_p), ctypes.POINTER(ctypes.c_char_p),
+                                              ctypes.c_int]
+        lib.ref_tok_special_ids.argtypes = [_vp, _vp]
+        lib.ref_tok_stop_ids.argtypes = [_vp, _vp, ctypes.c_int]
+        lib.ref_tok_byte_value.argtypes = [_vp, ctypes.c_uint32, ctypes.POINTER(ctypes.c_uint8)]
+        lib.ref_tok_is_special.argtypes = [_vp, ctypes.c_uint32]
+        lib.ref_detok_create.restype = _vp
+        lib.ref_detok_create.argtypes = [_vp, ctypes.c_int]
+        lib.ref_detok_push.restype = _vp
+        lib.ref_detok_push.argtypes = [_vp, ctypes.c_uint32, sz]
+        lib.ref_detok_finish.restype = _vp
+        lib.ref_detok_finish.argtypes = [_vp, sz]
+        lib.ref_detok_destroy.argtypes = [_vp]
+        lib.ref_stop_create.restype = _vp
+        lib.ref_stop_create.argtypes = [ctypes.POINTER(ctypes.c_char_p), ctypes.c_int]
+        lib.ref_stop_push.restype = _vp
+        lib.ref_stop_push.argtypes = [_vp, ctypes.c_char_p, ctypes.c_size_t, sz]
+        lib.ref_stop_finish.restype = _vp
+        lib.ref_stop_finish.argtypes = [_vp, sz]
+        lib.ref_stop_stopped.argtypes = [_vp, ctypes.POINTER(ctypes.c_char_p)]
+        lib.ref_stop_destroy.argtypes = [_vp]
+        lib.ref_utf8_repair.restype = _vp
+        lib.ref_utf8_repair.argtypes = [ctypes.c_char_p, ctypes.c_size_t, ctypes.c_int, sz, sz]
         _ref = lib
     return _ref
 
@@ -398,3 +431,103 @@ def reference_evaluate_verification(drafts, target_logits, sampling=None, base_s
     if n < 0:
         raise RuntimeError(lib.ref_last_error().decode())
     return out[:n].tolist(), int(na.value)
+
+
+class ReferenceTokenizer:
+    """The reference's own Tokenizer / IncrementalDetokenizer / StreamingStopMatcher
+    (src/tokenizer.cpp, src/detokenizer.cpp, compiled unmodified into oracle/_ref). Same method
+    shapes as g4dense_b200.api.Tokenizer; text in as bytes, out as bytes."""
+
+    def __init__(self, path=None, arch=0):
+        self.lib = reference_lib()
+        self.h = self.lib.ref_tok_open(None if path is None else str(path).encode(), arch)
+        if not self.h:
+            raise RuntimeError(self.lib.ref_last_error().decode())
+
+    def _take(self, p, n):
+        if not p:
+            raise RuntimeError(self.lib.ref_last_error().decode())
+        return ctypes.string_at(p, n.value)
+
+    def encode(self, text: bytes, add_bos=True):
+        n = self.lib.ref_tok_encode(self.h, text, len(text), 1 if add_bos else 0, None, 0)
+        if n < 0:
+            raise RuntimeError(self.lib.ref_last_error().decode())
+        out = np.zeros(max(n, 1), np.uint32)
+        self.lib.ref_tok_encode(self.h, text, len(text), 1 if add_bos else 0, _ptr(out), len(out))
+        return out[:n].tolist()
+
+    def decode(self, ids, skip_special=True):
+        a = np.ascontiguousarray(ids, np.uint32)
+        n = ctypes.c_size_t(0)
+        return self._take(self.lib.ref_tok_decode(self.h, _ptr(a), len(a), 1 if skip_special else 0,
+                                                  ctypes.byref(n)), n)
+
+    def decode_single(self, tid, skip_special=True):
+        n = ctypes.c_size_t(0)
+        return self._take(self.lib.ref_tok_decode_single(self.h, tid, 1 if skip_special else 0, ctypes.byref(n)), n)
+
+    def chat_template(self, messages):
+        """messages: [(role, content)] as bytes or str."""
+        enc = [tuple(x if isinstance(x, bytes) else x.encode() for x in m) for m in messages]
+        roles = (ctypes.c_char_p * max(1, len(enc)))(*[m[0] for m in enc])
+        contents = (ctypes.c_char_p * max(1, len(enc)))(*[m[1] for m in enc])
+        r = self.lib.ref_tok_chat_template(self.h, roles, contents, len(enc))
+        if r is None:
+            raise RuntimeError(self.lib.ref_last_error().decode())
+        return r
+
+    def special_ids(self):
+        v = np.zeros(7, np.uint32)
+        self.lib.ref_tok_special_ids(self.h, _ptr(v))
+        return dict(zip(("bos", "eos", "pad", "unk", "end_of_turn", "vocab_size", "loaded"), v.tolist()))
+
+    def stop_ids(self):
+        v = np.zeros(16, np.uint32)
+        n = self.lib.ref_tok_stop_ids(self.h, _ptr(v), len(v))
+        return v[:n].tolist()
+
+    def byte_value(self, tid):
+        b = ctypes.c_uint8(0)
+        return b.value if self.lib.ref_tok_byte_value(self.h, tid, ctypes.byref(b)) else None
+
+    def is_special(self, tid):
+        return bool(self.lib.ref_tok_is_special(self.h, tid))
+
+    def stream(self, ids, skip_special=True):
+        """IncrementalDetokenizer: [push(id) for id in ids] + [finish()]."""
+        d = self.lib.ref_detok_create(self.h, 1 if skip_special else 0)
+        n = ctypes.c_size_t(0)
+        out = [self._take(self.lib.ref_detok_push(d, int(t), ctypes.byref(n)), n) for t in ids]
+        out.append(self._take(self.lib.ref_detok_finish(d, ctypes.byref(n)), n))
+        self.lib.ref_detok_destroy(d)
+        return out
+
+    def __del__(self):
+        try:
+            if self.h:
+                self.lib.ref_tok_close(self.h)
+        except Exception:
+            pass
+
+
+def reference_stop_matcher(stops, chunks):
+    """StreamingStopMatcher: ([push(c) for c in chunks] + [finish()], stopped, matched)."""
+    lib = reference_lib()
+    arr = (ctypes.c_char_p * max(1, len(stops)))(*stops)
+    m = lib.ref_stop_create(arr, len(stops))
+    n = ctypes.c_size_t(0)
+    out = [ctypes.string_at(lib.ref_stop_push(m, c, len(c), ctypes.byref(n)), n.value) for c in chunks]
+    out.append(ctypes.string_at(lib.ref_stop_finish(m, ctypes.byref(n)), n.value))
+    matched = ctypes.c_char_p()
+    stopped = bool(lib.ref_stop_stopped(m, ctypes.byref(matched)))
+    res = (out, stopped, matched.value or b"")
+    lib.ref_stop_destroy(m)
+    return res
+
+
+def reference_utf8_repair(data: bytes, flush_all: bool):
+    lib = reference_lib()
+    used, n = ctypes.c_size_t(0), ctypes.c_size_t(0)
+    p = lib.ref_utf8_repair(data, len(data), 1 if flush_all else 0, ctypes.byref(used), ctypes.byref(n))
+    return ctypes.string_at(p, n.value), used.value

@@ -3,7 +3,11 @@
 // TEST INFRASTRUCTURE ONLY. Only tests/, __graft_entry__.smoke() and bench.py's CPU
 // baseline load it, and only as the checker. It links the unmodified reference sources
 // (src/cpu_reference.cpp, src/format.cpp, src/sampling.cpp, src/speculator.cpp,
-// src/tokenizer.cpp) compiled with oracle/shim/.
+// src/tokenizer.cpp, src/detokenizer.cpp) compiled with oracle/shim/.
+//
+// The ref_tok_* / ref_detok_* / ref_stop_* functions expose the reference's Tokenizer,
+// IncrementalDetokenizer and StreamingStopMatcher with the shapes of the engine's
+// g4dense_tokenizer_* calls, so a test can drive both with the same inputs.
 //
 // What it restates (the reference has these only on its Vulkan path):
 //   * ref_spec_generate: the decode loop of ForwardRunner::generate
@@ -24,6 +28,8 @@
 // engine) the drafter's consumed count is capped at what it actually forwarded, so the
 // missing token is fed on the next round and the drafter's cache always matches its context.
 #include "g4dense/cpu_reference.hpp"
+#include "g4dense/detokenizer.hpp"
+#include "g4dense/tokenizer.hpp"
 #include "g4dense/sampling.hpp"
 #include "g4dense/speculator.hpp"
 
@@ -349,6 +355,150 @@ int ref_spec_generate(const char* target_path, const char* draft_path, const uin
         g_err = e.what();
         return -1;
     }
+}
+
+}  // extern "C"
+
+// ---- tokenizer ---------------------------------------------------------------------------
+
+namespace {
+struct RefTok {
+    Tokenizer tok;
+    std::string out;
+};
+struct RefDetok {
+    RefDetok(const Tokenizer& t, bool skip) : d(t, skip) {}
+    IncrementalDetokenizer d;
+    std::string out;
+};
+struct RefStop {
+    StreamingStopMatcher m;
+    std::string out;
+};
+const char* hand_out(std::string& buf, std::string s, size_t* out_len) {
+    buf = std::move(s);
+    if (out_len) *out_len = buf.size();
+    return buf.c_str();
+}
+}  // namespace
+
+extern "C" {
+
+// Tokenizer::load_vocabulary(path) then set_architecture(arch) (0 Gemma-4, 1 Muse-Glimmer);
+// a null path leaves the tokenizer empty (its default-constructed state).
+void* ref_tok_open(const char* path, int arch) {
+    try {
+        auto t = std::make_unique<RefTok>();
+        if (path) t->tok.load_vocabulary(path);
+        t->tok.set_architecture(arch == 1 ? ModelArch::MUSE_GLIMMER : ModelArch::GEMMA4);
+        return t.release();
+    } catch (const std::exception& e) {
+        g_err = e.what();
+        return nullptr;
+    }
+}
+void ref_tok_close(void* h) { delete static_cast<RefTok*>(h); }
+
+int ref_tok_encode(void* h, const char* text, size_t len, int add_bos, uint32_t* out, int cap) {
+    try {
+        const auto ids = static_cast<RefTok*>(h)->tok.encode(std::string(text, len), add_bos != 0);
+        for (size_t i = 0; i < ids.size() && (int)i < cap; ++i) out[i] = ids[i];
+        return (int)ids.size();
+    } catch (const std::exception& e) {
+        g_err = e.what();
+        return -1;
+    }
+}
+
+const char* ref_tok_decode(void* h, const uint32_t* ids, int n, int skip_special, size_t* out_len) {
+    try {
+        auto* t = static_cast<RefTok*>(h);
+        return hand_out(t->out, t->tok.decode(std::vector<uint32_t>(ids, ids + n), skip_special != 0), out_len);
+    } catch (const std::exception& e) {
+        g_err = e.what();
+        return nullptr;
+    }
+}
+
+const char* ref_tok_decode_single(void* h, uint32_t id, int skip_special, size_t* out_len) {
+    auto* t = static_cast<RefTok*>(h);
+    return hand_out(t->out, t->tok.decode_single(id, skip_special != 0), out_len);
+}
+
+// apply_chat_template over n (role, content) pairs.
+const char* ref_tok_chat_template(void* h, const char* const* roles, const char* const* contents, int n) {
+    try {
+        auto* t = static_cast<RefTok*>(h);
+        std::vector<Tokenizer::ChatMessage> msgs;
+        for (int i = 0; i < n; ++i) msgs.push_back({roles[i], contents[i]});
+        return hand_out(t->out, t->tok.apply_chat_template(msgs), nullptr);
+    } catch (const std::exception& e) {
+        g_err = e.what();
+        return nullptr;
+    }
+}
+
+// out[0..6) = bos, eos, pad, unk, end_of_turn, vocab_size; out[6] = loaded.
+void ref_tok_special_ids(void* h, uint32_t* out7) {
+    const Tokenizer& t = static_cast<RefTok*>(h)->tok;
+    const uint32_t v[7] = {t.bos_id(), t.eos_id(), t.pad_id(), t.unk_id(), t.end_of_turn_id(), t.vocab_size(),
+                           t.is_loaded() ? 1u : 0u};
+    std::memcpy(out7, v, sizeof(v));
+}
+
+int ref_tok_stop_ids(void* h, uint32_t* out, int cap) {
+    const auto& s = static_cast<RefTok*>(h)->tok.stop_token_ids();
+    for (size_t i = 0; i < s.size() && (int)i < cap; ++i) out[i] = s[i];
+    return (int)s.size();
+}
+
+int ref_tok_byte_value(void* h, uint32_t id, uint8_t* value) {
+    return static_cast<RefTok*>(h)->tok.is_byte_fallback(id, *value) ? 1 : 0;
+}
+
+int ref_tok_is_special(void* h, uint32_t id) { return static_cast<RefTok*>(h)->tok.is_special_token(id) ? 1 : 0; }
+
+void* ref_detok_create(void* h, int skip_special) {
+    return new RefDetok(static_cast<RefTok*>(h)->tok, skip_special != 0);
+}
+const char* ref_detok_push(void* d, uint32_t id, size_t* out_len) {
+    auto* x = static_cast<RefDetok*>(d);
+    return hand_out(x->out, x->d.push(id), out_len);
+}
+const char* ref_detok_finish(void* d, size_t* out_len) {
+    auto* x = static_cast<RefDetok*>(d);
+    return hand_out(x->out, x->d.finish(), out_len);
+}
+void ref_detok_destroy(void* d) { delete static_cast<RefDetok*>(d); }
+
+void* ref_stop_create(const char* const* stops, int n) {
+    std::vector<std::string> v;
+    for (int i = 0; i < n; ++i) v.emplace_back(stops[i]);
+    auto* m = new RefStop;
+    m->m = StreamingStopMatcher(std::move(v));
+    return m;
+}
+const char* ref_stop_push(void* m, const char* text, size_t len, size_t* out_len) {
+    auto* x = static_cast<RefStop*>(m);
+    return hand_out(x->out, x->m.push(std::string_view(text, len)), out_len);
+}
+const char* ref_stop_finish(void* m, size_t* out_len) {
+    auto* x = static_cast<RefStop*>(m);
+    return hand_out(x->out, x->m.finish(), out_len);
+}
+int ref_stop_stopped(void* m, const char** matched) {
+    auto* x = static_cast<RefStop*>(m);
+    if (matched) *matched = x->m.matched().c_str();
+    return x->m.stopped() ? 1 : 0;
+}
+void ref_stop_destroy(void* m) { delete static_cast<RefStop*>(m); }
+
+const char* ref_utf8_repair(const char* in, size_t len, int flush_all, size_t* consumed, size_t* out_len) {
+    thread_local std::string buf;
+    std::string out;
+    const size_t used = utf8_repair(std::string_view(in, len), flush_all != 0, out);
+    if (consumed) *consumed = used;
+    return hand_out(buf, std::move(out), out_len);
 }
 
 }  // extern "C"

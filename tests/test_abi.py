@@ -84,3 +84,21 @@ def test_c_header_compiles_with_reference_layout(tmp_path):
     r = subprocess.run(["gcc", "-std=c11", "-I", str(REPO / "include"), "-o", str(tmp_path / "probe"), str(src)],
                        capture_output=True, text=True)
     assert r.returncode == 0, r.stderr
+
+
+def test_engine_config_layout_matches_header(tmp_path):
+    """The Python mirror of G4DenseEngineConfig has the C struct's size and field offsets."""
+    import subprocess
+    from g4dense_b200.api import EngineConfig
+    fields = [f[0] for f in EngineConfig._fields_]
+    src = tmp_path / "cfg.c"
+    src.write_text("#include <stdio.h>\n#include <stddef.h>\n#include \"g4dense/c_api.h\"\nint main(void) {\n"
+                   + "".join(f'  printf("%zu\\n", offsetof(G4DenseEngineConfig, {f}));\n' for f in fields)
+                   + '  printf("%zu\\n", sizeof(G4DenseEngineConfig));\n  return 0;\n}\n')
+    exe = tmp_path / "cfg"
+    r = subprocess.run(["gcc", "-std=c11", "-I", str(REPO / "include"), "-o", str(exe), str(src)],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr
+    got = [int(x) for x in subprocess.run([str(exe)], capture_output=True, text=True, check=True).stdout.split()]
+    want = [getattr(EngineConfig, f).offset for f in fields] + [ctypes.sizeof(EngineConfig)]
+    assert got == want

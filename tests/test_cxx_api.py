@@ -86,3 +86,44 @@ def test_cxx_runner_drafter_speculator_match_oracle(cxx_test_bin, config0):
         want2.append(cur)
         pos += 1
     assert got["draft2"] == want2
+
+
+@pytest.fixture(scope="module")
+def tok_api_bin(built_lib, tmp_path_factory):
+    out = tmp_path_factory.mktemp("cxxtok") / "test_tokenizer_api"
+    r = subprocess.run(["g++", "-std=c++17", "-O1", "-I", str(REPO / "include"), str(CPP / "test_tokenizer_api.cpp"),
+                        "-o", str(out), str(built_lib), f"-Wl,-rpath,{built_lib.parent}"],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr[-4000:]
+    return out
+
+
+def test_cxx_tokenizer_api(tok_api_bin, tmp_path):
+    """Tokenizer / IncrementalDetokenizer / StreamingStopMatcher through the public C++ headers,
+    with the reference's own test cases (tests/test_tokenizer.cpp, tests/test_detokenizer.cpp)."""
+    r = subprocess.run([str(tok_api_bin), "cpu", str(tmp_path)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout + r.stderr
+
+
+@pytest.mark.gpu
+def test_cxx_runner_text_generate(tok_api_bin, config0, tmp_path):
+    """ForwardRunner::generate(prompt) with a tokenizer: greedy, chat template, stop ids; tokens and
+    pieces equal the reference tokenizer + restated runner on the same container."""
+    from g4dense_b200 import synth_tokenizer as S
+    from oracle import tokenizer_oracle as TO
+    tokp = S.write_synthetic_tokenizer(tmp_path / "tokenizer.json")
+    R = O.ReferenceTokenizer(tokp) if O.reference_available() else TO.Tokenizer(tokp)
+    tgt = config0["target_centered"]
+    prompt = "stin évi chch"
+    ids = R.encode(R.chat_template([("user", prompt)]), False)
+    want, _ = O.spec_generate(O.RestatedModel(tgt), None, ids, 48)
+    want = want.tolist()
+    stops = R.stop_ids() if callable(R.stop_ids) else R.stop_ids
+    cut = next(i for i, t in enumerate(want) if t in stops)
+    want = want[:cut + 1]
+    r = subprocess.run([str(tok_api_bin), "gpu", str(tgt), str(tokp), prompt, "48"], capture_output=True, text=True,
+                       timeout=600)
+    assert r.returncode == 0, r.stdout + r.stderr[-3000:]
+    got = json.loads(r.stdout.strip().splitlines()[-1])
+    assert got["tokens"] == want
+    assert [bytes.fromhex(p) for p in got["pieces"]] == [R.decode_single(t) for t in want]

@@ -256,7 +256,7 @@ def test_callback_stop_and_telemetry(built_lib, config0):
     for key in ("tps", "ttft_ms", "speculative_acceptance_rate", "total_tokens_generated", "kv_cache_mb"):
         assert key in tel
     assert lib().g4dense_engine_generate(e.h, b"hello", 4) is None
-    assert b"tokenizer" in lib().g4dense_engine_last_error()
+    assert b"tokenizer" in lib().g4dense_engine_last_error().lower()
     e.close()
 
 

@@ -4,15 +4,18 @@
 
 #include <algorithm>
 #include <atomic>
+#include <cstdint>
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <filesystem>
 #include <memory>
 #include <sstream>
 #include <string>
 #include <vector>
 
 #include "runner.h"
+#include "tokenizer.h"
 
 #ifdef G4B_HAVE_NCCL
 #include <nccl.h>
@@ -24,8 +27,31 @@ thread_local std::string g_last_error;
 void set_error(const std::string& m) { g_last_error = m; }
 void clear_error() { g_last_error.clear(); }
 
+// A tokenizer behind the C ABI, with the buffer its returned strings live in.
+struct TokHandle {
+    g4b::Tokenizer tok;
+    bool engine_owned{false};  // the engine's own tokenizer: g4dense_tokenizer_destroy ignores it
+    std::string out;
+};
+struct DetokHandle {
+    explicit DetokHandle(const g4b::Tokenizer& t, bool skip) : d(t, skip) {}
+    g4b::IncrementalDetokenizer d;
+    std::string out;
+};
+struct StopHandle {
+    g4b::StreamingStopMatcher m;
+    std::string out;
+};
+
+const char* give(std::string& buf, std::string s, size_t* out_len) {
+    buf = std::move(s);
+    if (out_len) *out_len = buf.size();
+    return buf.c_str();
+}
+
 struct EngineHandle {
     std::unique_ptr<g4b::Engine> engine;
+    std::unique_ptr<TokHandle> tok;  // null: the text entry points fail
     std::atomic<bool> cancel{false};
     std::string last_response, last_telemetry;
     std::vector<uint32_t> last_tokens;
@@ -155,6 +181,48 @@ g4b::GenerationOptions to_gen(const EngineHandle* e, const G4DenseGenerationOpti
     g.gate_min_accept = e->gate_min_accept;
     g.gate_window = e->gate_window;
     return g;
+}
+
+// Where the engine's tokenizer comes from: the config, $G4DENSE_TOKENIZER, tokenizer.json beside
+// the container, then tokenizer.json in the working directory (the first place the reference's
+// resolve_resource_path looks, src/manifest.cpp:200-212). "" when none is found.
+std::string tokenizer_file(const G4DenseEngineConfig* cfg) {
+    if (cfg->tokenizer_path && *cfg->tokenizer_path) return cfg->tokenizer_path;
+    if (const char* env = std::getenv("G4DENSE_TOKENIZER"); env && *env) return env;
+    namespace fs = std::filesystem;
+    std::error_code ec;
+    if (cfg->container_path && *cfg->container_path) {
+        const fs::path beside = fs::path(cfg->container_path).parent_path() / "tokenizer.json";
+        if (fs::is_regular_file(beside, ec)) return beside.string();
+    }
+    if (fs::is_regular_file("tokenizer.json", ec)) return "tokenizer.json";
+    return "";
+}
+
+// ForwardRunner::generate(prompt, options) (src/runner.cpp:2060-2347): chat template or raw
+// encode, then the engine's decode loop, stopping after a tokenizer stop id; every emitted token
+// reaches on_token with its decode_single piece, and the pieces are returned concatenated.
+const char* generate_text(EngineHandle* e, const std::string& prompt, bool chat, const G4DenseGenerationOptions* o,
+                          G4DenseTokenCallback on_token, void* user) {
+    if (!e->tok) throw std::runtime_error("ForwardRunner::generate: Tokenizer is not loaded or missing");
+    const g4b::Tokenizer& tk = e->tok->tok;
+    // The template emits the literal "<bos>", so the templated text is encoded without another.
+    const std::vector<uint32_t> ids =
+        chat ? tk.encode(tk.chat_template({{"user", prompt}}), false) : tk.encode(prompt, true);
+    if (ids.empty()) throw std::runtime_error("ForwardRunner::generate: prompt encoded to empty token sequence");
+    g4b::GenerationOptions g = to_gen(e, o);
+    g.stop_tokens = tk.stop_ids();
+    e->cancel.store(false);
+    e->last_response.clear();
+    int idx = 0;
+    auto cb = [&](uint32_t t) {
+        const std::string piece = tk.decode_single(t);
+        e->last_response += piece;
+        return on_token ? on_token(user, idx++, t, piece.c_str()) != 0 : true;
+    };
+    e->last_tokens = e->engine->generate(ids, g, cb, &e->cancel);
+    e->last_stop_reason = e->engine->last_stats().stop_reason;
+    return e->last_response.c_str();
 }
 
 }  // namespace
@@ -306,6 +374,16 @@ G4DENSE_API void* g4dense_engine_create_ex(const G4DenseEngineConfig* cfg) {
         h->draft_k = cfg->draft_k;
         h->gate_min_accept = cfg->gate_min_accept;
         h->gate_window = cfg->gate_window;
+        // The runner sets the tokenizer's architecture from the container header
+        // (src/runner.cpp:265), which decides the chat template and the stop ids.
+        if (const std::string tp = tokenizer_file(cfg); !tp.empty()) {
+            auto t = std::make_unique<TokHandle>();
+            t->engine_owned = true;
+            t->tok.load(tp);
+            t->tok.set_arch(h->engine->target().header().arch_type == 1 ? g4b::Tokenizer::Arch::MuseGlimmer
+                                                                         : g4b::Tokenizer::Arch::Gemma4);
+            h->tok = std::move(t);
+        }
         return h.release();
     } catch (const std::exception& e) {
         set_error(e.what());
@@ -331,30 +409,52 @@ G4DENSE_API void g4dense_engine_destroy(void* handle) { delete static_cast<Engin
 
 G4DENSE_API const char* g4dense_engine_generate(void* handle, const char* prompt, int max_tokens) {
     clear_error();
-    (void)max_tokens;
     if (!handle || !prompt) {
         set_error("Invalid handle or null prompt");
         return nullptr;
     }
-    set_error("text prompts need the reference tokenizer (tokenizer.json), which this engine does not load; "
-              "use g4dense_engine_generate_tokens");
-    return nullptr;
+    try {
+        G4DenseGenerationOptions o;
+        g4dense_options_default(&o);  // temperature 0.2, top_p 0.95, top_k 64 (src/c_api.cpp:93-96)
+        o.max_tokens = max_tokens > 0 ? max_tokens : 512;
+        return generate_text(static_cast<EngineHandle*>(handle), prompt, true, &o, nullptr, nullptr);
+    } catch (const std::exception& ex) {
+        set_error(ex.what());
+        return nullptr;
+    }
 }
 
 G4DENSE_API const char* g4dense_engine_generate_ex(void* handle, const char* messages_json,
                                                    const G4DenseGenerationOptions* opts, G4DenseTokenCallback on_token,
                                                    void* user) {
     clear_error();
-    (void)opts;
-    (void)on_token;
-    (void)user;
     if (!handle || !messages_json) {
         set_error("Invalid handle or null messages");
         return nullptr;
     }
-    set_error("chat messages need the reference tokenizer (tokenizer.json), which this engine does not load; "
-              "use g4dense_engine_generate_tokens");
-    return nullptr;
+    try {
+        return generate_text(static_cast<EngineHandle*>(handle), messages_json, true, opts, on_token, user);
+    } catch (const std::exception& ex) {
+        set_error(ex.what());
+        return nullptr;
+    }
+}
+
+G4DENSE_API const char* g4dense_engine_generate_text(void* handle, const char* prompt, int use_chat_template,
+                                                     const G4DenseGenerationOptions* opts,
+                                                     G4DenseTokenCallback on_token, void* user) {
+    clear_error();
+    if (!handle || !prompt) {
+        set_error("Invalid handle or null prompt");
+        return nullptr;
+    }
+    try {
+        return generate_text(static_cast<EngineHandle*>(handle), prompt, use_chat_template != 0, opts, on_token,
+                             user);
+    } catch (const std::exception& ex) {
+        set_error(ex.what());
+        return nullptr;
+    }
 }
 
 G4DENSE_API const char* g4dense_engine_generate_tokens(void* handle, const unsigned int* prompt_ids, int n_prompt,
@@ -689,6 +789,187 @@ G4DENSE_API double g4dense_engine_time_pass(void* handle, int which, int batch, 
 
 G4DENSE_API void g4dense_engine_stop(void* handle) {
     if (handle) static_cast<EngineHandle*>(handle)->cancel.store(true);
+}
+
+// ---- tokenizer ---------------------------------------------------------------------------
+
+G4DENSE_API void* g4dense_tokenizer_open(const char* tokenizer_json_path, int arch) {
+    clear_error();
+    if (arch != 0 && arch != 1) {
+        set_error("unknown tokenizer architecture (0 = Gemma-4, 1 = Muse-Glimmer)");
+        return nullptr;
+    }
+    try {
+        auto t = std::make_unique<TokHandle>();
+        t->tok.load(tokenizer_json_path ? tokenizer_json_path : "");
+        t->tok.set_arch(arch == 1 ? g4b::Tokenizer::Arch::MuseGlimmer : g4b::Tokenizer::Arch::Gemma4);
+        return t.release();
+    } catch (const std::exception& e) {
+        set_error(e.what());
+        return nullptr;
+    }
+}
+
+G4DENSE_API void* g4dense_engine_tokenizer(void* handle) {
+    return handle ? static_cast<EngineHandle*>(handle)->tok.get() : nullptr;
+}
+
+G4DENSE_API void g4dense_tokenizer_destroy(void* tok) {
+    auto* t = static_cast<TokHandle*>(tok);
+    if (t && !t->engine_owned) delete t;
+}
+
+G4DENSE_API int g4dense_tokenizer_encode(void* tok, const char* text, size_t len, int add_bos, unsigned int* out,
+                                         int cap) {
+    clear_error();
+    if (!tok || (!text && len) || cap < 0 || (!out && cap)) {
+        set_error("Invalid arguments");
+        return -1;
+    }
+    try {
+        const auto ids =
+            static_cast<TokHandle*>(tok)->tok.encode(std::string_view(text ? text : "", len), add_bos != 0);
+        if (ids.size() > (size_t)INT32_MAX) throw std::length_error("too many tokens");
+        std::copy_n(ids.begin(), std::min(ids.size(), (size_t)cap), out);
+        return (int)ids.size();
+    } catch (const std::exception& e) {
+        set_error(e.what());
+        return -1;
+    }
+}
+
+G4DENSE_API const char* g4dense_tokenizer_decode(void* tok, const unsigned int* ids, int n, int skip_special,
+                                                 size_t* out_len) {
+    clear_error();
+    if (!tok || n < 0 || (!ids && n)) {
+        set_error("Invalid arguments");
+        return nullptr;
+    }
+    try {
+        auto* t = static_cast<TokHandle*>(tok);
+        return give(t->out, t->tok.decode(std::vector<uint32_t>(ids, ids + n), skip_special != 0), out_len);
+    } catch (const std::exception& e) {
+        set_error(e.what());
+        return nullptr;
+    }
+}
+
+G4DENSE_API const char* g4dense_tokenizer_decode_single(void* tok, unsigned int id, int skip_special,
+                                                        size_t* out_len) {
+    clear_error();
+    if (!tok) {
+        set_error("Invalid arguments");
+        return nullptr;
+    }
+    auto* t = static_cast<TokHandle*>(tok);
+    return give(t->out, t->tok.decode_single(id, skip_special != 0), out_len);
+}
+
+G4DENSE_API const char* g4dense_tokenizer_chat_template(void* tok, const char* messages_json) {
+    clear_error();
+    if (!tok || !messages_json) {
+        set_error("Invalid arguments");
+        return nullptr;
+    }
+    try {
+        auto* t = static_cast<TokHandle*>(tok);
+        return give(t->out, t->tok.chat_template(g4b::parse_chat_messages(messages_json)), nullptr);
+    } catch (const std::exception& e) {
+        set_error(e.what());
+        return nullptr;
+    }
+}
+
+G4DENSE_API int g4dense_tokenizer_special_ids(void* tok, unsigned int* out6) {
+    if (!tok || !out6) return -1;
+    const g4b::Tokenizer& t = static_cast<TokHandle*>(tok)->tok;
+    const unsigned int v[6] = {t.bos(), t.eos(), t.pad(), t.unk(), t.end_of_turn(), t.vocab_size()};
+    std::memcpy(out6, v, sizeof(v));
+    return 0;
+}
+
+G4DENSE_API int g4dense_tokenizer_stop_ids(void* tok, unsigned int* out, int cap) {
+    if (!tok || cap < 0 || (!out && cap)) return 0;
+    const auto& s = static_cast<TokHandle*>(tok)->tok.stop_ids();
+    std::copy_n(s.begin(), std::min(s.size(), (size_t)cap), out);
+    return (int)s.size();
+}
+
+G4DENSE_API int g4dense_tokenizer_byte_value(void* tok, unsigned int id, unsigned char* value) {
+    uint8_t b = 0;
+    if (!tok || !static_cast<TokHandle*>(tok)->tok.byte_value(id, b)) return 0;
+    if (value) *value = b;
+    return 1;
+}
+
+G4DENSE_API int g4dense_tokenizer_is_special(void* tok, unsigned int id) {
+    return tok && static_cast<TokHandle*>(tok)->tok.is_special(id) ? 1 : 0;
+}
+
+G4DENSE_API void* g4dense_detokenizer_create(void* tok, int skip_special) {
+    clear_error();
+    if (!tok) {
+        set_error("null tokenizer");
+        return nullptr;
+    }
+    return new DetokHandle(static_cast<TokHandle*>(tok)->tok, skip_special != 0);
+}
+
+G4DENSE_API const char* g4dense_detokenizer_push(void* detok, unsigned int id, size_t* out_len) {
+    if (!detok) return nullptr;
+    auto* d = static_cast<DetokHandle*>(detok);
+    return give(d->out, d->d.push(id), out_len);
+}
+
+G4DENSE_API const char* g4dense_detokenizer_finish(void* detok, size_t* out_len) {
+    if (!detok) return nullptr;
+    auto* d = static_cast<DetokHandle*>(detok);
+    return give(d->out, d->d.finish(), out_len);
+}
+
+G4DENSE_API void g4dense_detokenizer_destroy(void* detok) { delete static_cast<DetokHandle*>(detok); }
+
+G4DENSE_API void* g4dense_stop_matcher_create(const char* const* stops, int n) {
+    clear_error();
+    if (n < 0 || (!stops && n)) {
+        set_error("Invalid arguments");
+        return nullptr;
+    }
+    std::vector<std::string> v;
+    for (int i = 0; i < n; ++i) v.emplace_back(stops[i] ? stops[i] : "");
+    auto* m = new StopHandle;
+    m->m = g4b::StreamingStopMatcher(std::move(v));
+    return m;
+}
+
+G4DENSE_API const char* g4dense_stop_matcher_push(void* m, const char* text, size_t len, size_t* out_len) {
+    if (!m || (!text && len)) return nullptr;
+    auto* h = static_cast<StopHandle*>(m);
+    return give(h->out, h->m.push(std::string_view(text ? text : "", len)), out_len);
+}
+
+G4DENSE_API const char* g4dense_stop_matcher_finish(void* m, size_t* out_len) {
+    if (!m) return nullptr;
+    auto* h = static_cast<StopHandle*>(m);
+    return give(h->out, h->m.finish(), out_len);
+}
+
+G4DENSE_API int g4dense_stop_matcher_stopped(void* m, const char** matched) {
+    if (!m) return 0;
+    auto* h = static_cast<StopHandle*>(m);
+    if (matched) *matched = h->m.matched().c_str();
+    return h->m.stopped() ? 1 : 0;
+}
+
+G4DENSE_API void g4dense_stop_matcher_destroy(void* m) { delete static_cast<StopHandle*>(m); }
+
+G4DENSE_API const char* g4dense_utf8_repair(const char* in, size_t len, int flush_all, size_t* consumed,
+                                            size_t* out_len) {
+    thread_local std::string buf;
+    std::string out;
+    const size_t used = g4b::utf8_repair(std::string_view(in ? in : "", in ? len : 0), flush_all != 0, out);
+    if (consumed) *consumed = used;
+    return give(buf, std::move(out), out_len);
 }
 
 }  // extern "C"

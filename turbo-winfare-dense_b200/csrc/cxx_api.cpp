@@ -14,6 +14,7 @@
 #include "g4dense/speculator.hpp"
 #include "runner.h"
 #include "sampling.h"
+#include "tokenizer_impl.h"
 #ifdef G4B_HAVE_NCCL
 #include <nccl.h>
 #endif
@@ -229,8 +230,15 @@ struct ForwardRunner::Impl {
     std::string path;
     uint32_t max_context = 4096;
     std::unique_ptr<g4b::Engine> engine;
+    std::shared_ptr<Tokenizer> tok;
     void require() const {
         if (!engine) throw std::runtime_error("ForwardRunner: call initialize() first");
+    }
+    // The runner decides the tokenizer's architecture from the container (src/runner.cpp:265).
+    void sync_arch() {
+        if (tok && engine)
+            tok->set_architecture(engine->target().header().arch_type == 1 ? ModelArch::MUSE_GLIMMER
+                                                                           : ModelArch::GEMMA4);
     }
 };
 
@@ -239,6 +247,17 @@ ForwardRunner::ForwardRunner(std::shared_ptr<DeviceContext> ctx, const std::stri
     if (!ctx) throw std::invalid_argument("ForwardRunner: a DeviceContext is required");
     impl_->ctx = std::move(ctx);
     impl_->path = container_path;
+}
+
+ForwardRunner::ForwardRunner(std::shared_ptr<DeviceContext> ctx, std::shared_ptr<Tokenizer> tokenizer,
+                             const std::string& container_path)
+    : ForwardRunner(std::move(ctx), container_path) {
+    impl_->tok = std::move(tokenizer);
+}
+
+void ForwardRunner::set_tokenizer(std::shared_ptr<Tokenizer> tokenizer) {
+    impl_->tok = std::move(tokenizer);
+    impl_->sync_arch();
 }
 
 ForwardRunner::~ForwardRunner() {
@@ -261,6 +280,7 @@ void ForwardRunner::initialize() {
     auto t = std::make_unique<g4b::DeviceModel>(o);
     t->load_container(impl_->path);
     impl_->engine = std::make_unique<g4b::Engine>(std::move(t));
+    impl_->sync_arch();
 }
 
 void ForwardRunner::forward_batch(const uint32_t* ids, uint32_t batch, uint32_t base, float* out_logits,
@@ -274,10 +294,28 @@ void ForwardRunner::forward_single_token(uint32_t token_id, uint32_t position, f
     forward_batch(&token_id, 1, position, out_logits, false);
 }
 
-void ForwardRunner::generate(const std::string&, const GenerationOptions&, TokenCallback, std::atomic<bool>*) {
-    throw std::runtime_error(
-        "ForwardRunner::generate: text prompts need the reference's tokenizer, which is not part of this path; "
-        "use generate_tokens");
+void ForwardRunner::generate(const std::string& prompt, const GenerationOptions& o, TokenCallback on_token,
+                             std::atomic<bool>* cancel) {
+    if (!impl_->tok || !impl_->tok->is_loaded())
+        throw std::runtime_error("ForwardRunner::generate: Tokenizer is not loaded or missing");
+    impl_->require();
+    use_device(impl_->ctx->device());
+    const g4b::Tokenizer& tk = impl_->tok->impl_->t;
+    // The template emits the literal "<bos>", so the templated text is encoded without another.
+    const std::vector<uint32_t> ids =
+        o.use_chat_template ? tk.encode(tk.chat_template({{"user", prompt}}), false) : tk.encode(prompt, true);
+    if (ids.empty()) throw std::runtime_error("ForwardRunner::generate: prompt encoded to empty token sequence");
+    g4b::Engine& e = *impl_->engine;
+    g4b::GenerationOptions g;
+    g.max_tokens = o.max_tokens;
+    g.sampling = to_internal(o.sampling);
+    g.speculative_enabled = o.speculative_enabled && (e.draft() || e.mtp());
+    g.draft_k = o.draft_k;
+    g.stop_token = o.stop_token;
+    g.stop_tokens = tk.stop_ids();
+    g4b::TokenCallback cb;
+    if (on_token) cb = [&](uint32_t t) { return on_token(t, tk.decode_single(t)); };
+    e.generate(ids, g, cb, cancel);
 }
 
 std::vector<uint32_t> ForwardRunner::generate_tokens(const std::vector<uint32_t>& prompt, const GenerationOptions& o,
@@ -292,7 +330,9 @@ std::vector<uint32_t> ForwardRunner::generate_tokens(const std::vector<uint32_t>
     g.draft_k = o.draft_k;
     g.stop_token = o.stop_token;
     g4b::TokenCallback cb;
-    if (on_token) cb = [&on_token](uint32_t t) { return on_token(t, std::string()); };
+    const Tokenizer* tok = impl_->tok && impl_->tok->is_loaded() ? impl_->tok.get() : nullptr;
+    if (on_token)
+        cb = [&on_token, tok](uint32_t t) { return on_token(t, tok ? tok->decode_single(t) : std::string()); };
     return e.generate(prompt, g, cb, cancel);
 }
 

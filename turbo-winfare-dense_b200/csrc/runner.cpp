@@ -151,7 +151,8 @@ std::vector<uint32_t> Engine::generate(const std::vector<uint32_t>& prompt, cons
             stats_.stop_reason = 2;
             return false;
         }
-        if (opt.stop_token >= 0 && (int64_t)t == opt.stop_token) {
+        if ((opt.stop_token >= 0 && (int64_t)t == opt.stop_token) ||
+            std::find(opt.stop_tokens.begin(), opt.stop_tokens.end(), t) != opt.stop_tokens.end()) {
             stats_.stop_reason = 1;
             return false;
         }

@@ -26,6 +26,7 @@ struct GenerationOptions {
     bool speculative_enabled{false};  // off by default, as in the reference
     uint32_t draft_k{6};              // verify width K (K-1 drafts), clamped to [2, 8]
     int64_t stop_token{-1};           // < 0: no stop token
+    std::vector<uint32_t> stop_tokens;  // the tokenizer's stop ids (text generation)
     double gate_min_accept{0.45};     // adaptive gate (src/runner.cpp:2188-2195)
     int gate_window{24};
     // Config-3 "oracle drafter": the drafter model still runs its steps (cost), but the

@@ -47,7 +47,8 @@ class EngineConfig(ctypes.Structure):
                 ("draft_seed", ctypes.c_ulonglong), ("draft_k", ctypes.c_int), ("max_context", ctypes.c_int),
                 ("kv_bf16", ctypes.c_int), ("tp_rank", ctypes.c_int), ("tp_size", ctypes.c_int),
                 ("nccl_unique_id", ctypes.c_void_p), ("device", ctypes.c_int),
-                ("gate_min_accept", ctypes.c_double), ("gate_window", ctypes.c_int)]
+                ("gate_min_accept", ctypes.c_double), ("gate_window", ctypes.c_int),
+                ("tokenizer_path", ctypes.c_char_p)]
 
 
 TOKEN_CB = ctypes.CFUNCTYPE(ctypes.c_int, ctypes.c_void_p, ctypes.c_int, ctypes.c_uint, ctypes.c_char_p)
@@ -69,6 +70,8 @@ def _bind_engine(L):
     L.g4dense_engine_generate.argtypes = [_vp, ctypes.c_char_p, ctypes.c_int]
     L.g4dense_engine_generate_ex.restype = ctypes.c_char_p
     L.g4dense_engine_generate_ex.argtypes = [_vp, ctypes.c_char_p, _vp, TOKEN_CB, _vp]
+    L.g4dense_engine_generate_text.restype = ctypes.c_char_p
+    L.g4dense_engine_generate_text.argtypes = [_vp, ctypes.c_char_p, ctypes.c_int, _vp, TOKEN_CB, _vp]
     L.g4dense_engine_generate_tokens.restype = ctypes.c_char_p
     L.g4dense_engine_generate_tokens.argtypes = [_vp, _vp, ctypes.c_int, _vp, TOKEN_CB, _vp]
     L.g4dense_engine_last_tokens.argtypes = [_vp, _vp, ctypes.c_int]
@@ -90,6 +93,40 @@ def _bind_engine(L):
     L.g4dense_engine_set_gate.argtypes = [_vp, ctypes.c_double, ctypes.c_int]
     L.g4dense_engine_time_pass.restype = ctypes.c_double
     L.g4dense_engine_time_pass.argtypes = [_vp, ctypes.c_int, ctypes.c_int, ctypes.c_int, ctypes.c_int]
+    _sz = ctypes.POINTER(ctypes.c_size_t)
+    L.g4dense_tokenizer_open.restype = _vp
+    L.g4dense_tokenizer_open.argtypes = [ctypes.c_char_p, ctypes.c_int]
+    L.g4dense_engine_tokenizer.restype = _vp
+    L.g4dense_engine_tokenizer.argtypes = [_vp]
+    L.g4dense_tokenizer_destroy.argtypes = [_vp]
+    L.g4dense_tokenizer_encode.argtypes = [_vp, ctypes.c_char_p, ctypes.c_size_t, ctypes.c_int, _vp, ctypes.c_int]
+    L.g4dense_tokenizer_decode.restype = _vp
+    L.g4dense_tokenizer_decode.argtypes = [_vp, _vp, ctypes.c_int, ctypes.c_int, _sz]
+    L.g4dense_tokenizer_decode_single.restype = _vp
+    L.g4dense_tokenizer_decode_single.argtypes = [_vp, ctypes.c_uint, ctypes.c_int, _sz]
+    L.g4dense_tokenizer_chat_template.restype = ctypes.c_char_p
+    L.g4dense_tokenizer_chat_template.argtypes = [_vp, ctypes.c_char_p]
+    L.g4dense_tokenizer_special_ids.argtypes = [_vp, _vp]
+    L.g4dense_tokenizer_stop_ids.argtypes = [_vp, _vp, ctypes.c_int]
+    L.g4dense_tokenizer_byte_value.argtypes = [_vp, ctypes.c_uint, ctypes.POINTER(ctypes.c_ubyte)]
+    L.g4dense_tokenizer_is_special.argtypes = [_vp, ctypes.c_uint]
+    L.g4dense_detokenizer_create.restype = _vp
+    L.g4dense_detokenizer_create.argtypes = [_vp, ctypes.c_int]
+    L.g4dense_detokenizer_push.restype = _vp
+    L.g4dense_detokenizer_push.argtypes = [_vp, ctypes.c_uint, _sz]
+    L.g4dense_detokenizer_finish.restype = _vp
+    L.g4dense_detokenizer_finish.argtypes = [_vp, _sz]
+    L.g4dense_detokenizer_destroy.argtypes = [_vp]
+    L.g4dense_stop_matcher_create.restype = _vp
+    L.g4dense_stop_matcher_create.argtypes = [ctypes.POINTER(ctypes.c_char_p), ctypes.c_int]
+    L.g4dense_stop_matcher_push.restype = _vp
+    L.g4dense_stop_matcher_push.argtypes = [_vp, ctypes.c_char_p, ctypes.c_size_t, _sz]
+    L.g4dense_stop_matcher_finish.restype = _vp
+    L.g4dense_stop_matcher_finish.argtypes = [_vp, _sz]
+    L.g4dense_stop_matcher_stopped.argtypes = [_vp, ctypes.POINTER(ctypes.c_char_p)]
+    L.g4dense_stop_matcher_destroy.argtypes = [_vp]
+    L.g4dense_utf8_repair.restype = _vp
+    L.g4dense_utf8_repair.argtypes = [ctypes.c_char_p, ctypes.c_size_t, ctypes.c_int, _sz, _sz]
     L.g4dense_engine_profile_gemms.restype = ctypes.c_double
     L.g4dense_engine_profile_gemms.argtypes = [_vp, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_ulonglong),
                                                ctypes.POINTER(ctypes.c_int)]
@@ -203,7 +240,7 @@ class Engine:
 
     def __init__(self, target=None, preset=None, seed=0, centered=False, draft=None, draft_preset=None,
                  draft_seed=1, draft_k=0, max_context=4096, kv_bf16=False, tp_rank=0, tp_size=1,
-                 nccl_id=None, device=-1, gate_min_accept=0.45, gate_window=24):
+                 nccl_id=None, device=-1, gate_min_accept=0.45, gate_window=24, tokenizer_path=None):
         L = lib()
         cfg = EngineConfig()
         L.g4dense_config_default(ctypes.byref(cfg))
@@ -231,6 +268,7 @@ class Engine:
         cfg.device = device
         cfg.gate_min_accept = gate_min_accept
         cfg.gate_window = gate_window
+        cfg.tokenizer_path = cstr(tokenizer_path)
         self.h = L.g4dense_engine_create_ex(ctypes.byref(cfg))
         if not self.h:
             _eng_err("g4dense_engine_create_ex")
@@ -263,6 +301,36 @@ class Engine:
         out = np.zeros(max_tokens + 32, np.uint32)
         n = lib().g4dense_engine_last_tokens(self.h, out.ctypes.data_as(_vp), len(out))
         return out[:n].copy()
+
+    def generate_text(self, prompt, use_chat_template=True, max_tokens=512, temperature=0.0, top_p=1.0, top_k=0,
+                      seed=None, callback=None, options=None):
+        """ForwardRunner::generate(prompt, options) through g4dense_engine_generate_text: returns the
+        concatenated pieces (bytes); callback(token, piece_bytes) -> bool continues. `options`
+        (a GenOptions) overrides the keyword sampling arguments."""
+        o = options
+        if o is None:
+            o = GenOptions()
+            lib().g4dense_options_default(ctypes.byref(o))
+            o.max_tokens = max_tokens
+            o.temperature, o.top_p, o.top_k = temperature, top_p, top_k
+            o.has_seed = 0 if seed is None else 1
+            o.seed = 0 if seed is None else seed
+        cb = TOKEN_CB(lambda u, i, t, d: int(callback(t, d)) if callback else 1)
+        r = lib().g4dense_engine_generate_text(self.h, _as_bytes(prompt), 1 if use_chat_template else 0,
+                                               ctypes.byref(o), cb, None)
+        if r is None:
+            _eng_err("g4dense_engine_generate_text")
+        return r
+
+    def tokens(self, cap=1 << 16):
+        out = np.zeros(cap, np.uint32)
+        n = lib().g4dense_engine_last_tokens(self.h, out.ctypes.data_as(_vp), cap)
+        return out[:n].copy()
+
+    def tokenizer(self):
+        """The engine's own tokenizer (None when it loaded none)."""
+        t = lib().g4dense_engine_tokenizer(self.h)
+        return Tokenizer(_handle=t, _owner=self) if t else None
 
     def rounds(self, cap=4096):
         buf = np.zeros(3 * cap, np.int32)
@@ -340,3 +408,155 @@ class Engine:
             self.close()
         except Exception:
             pass
+
+
+def _as_bytes(x):
+    return x if isinstance(x, bytes) else str(x).encode()
+
+
+def _take(ptr, n):
+    if not ptr:
+        raise RuntimeError(lib().g4dense_engine_last_error().decode())
+    return ctypes.string_at(ptr, n.value)
+
+
+class Tokenizer:
+    """The engine's tokenizer (g4dense_tokenizer_*): Gemma-4 tokenizer.json BPE, chat template,
+    byte-fallback decoding. Text goes in as str or UTF-8 bytes and comes out as bytes."""
+
+    def __init__(self, path=None, arch=0, _handle=None, _owner=None):
+        self._owner = _owner
+        if _handle is not None:
+            self.h = _handle
+            return
+        self.h = lib().g4dense_tokenizer_open(None if path is None else str(path).encode(), arch)
+        if not self.h:
+            _eng_err("g4dense_tokenizer_open")
+
+    def encode(self, text, add_bos=True):
+        b = _as_bytes(text)
+        n = lib().g4dense_tokenizer_encode(self.h, b, len(b), 1 if add_bos else 0, None, 0)
+        if n < 0:
+            _eng_err("g4dense_tokenizer_encode")
+        out = np.zeros(max(n, 1), np.uint32)
+        n = lib().g4dense_tokenizer_encode(self.h, b, len(b), 1 if add_bos else 0, out.ctypes.data_as(_vp), len(out))
+        return out[:n].tolist()
+
+    def decode(self, ids, skip_special=True):
+        a = np.ascontiguousarray(ids, np.uint32)
+        n = ctypes.c_size_t(0)
+        return _take(lib().g4dense_tokenizer_decode(self.h, a.ctypes.data_as(_vp), len(a), 1 if skip_special else 0,
+                                                    ctypes.byref(n)), n)
+
+    def decode_single(self, tid, skip_special=True):
+        n = ctypes.c_size_t(0)
+        return _take(lib().g4dense_tokenizer_decode_single(self.h, tid, 1 if skip_special else 0, ctypes.byref(n)), n)
+
+    def chat_template(self, messages):
+        """messages: a JSON string, or [(role, content)] / [{"role": .., "content": ..}]."""
+        import json
+        if not isinstance(messages, (str, bytes)):
+            messages = json.dumps([m if isinstance(m, dict) else {"role": m[0], "content": m[1]} for m in messages])
+        r = lib().g4dense_tokenizer_chat_template(self.h, _as_bytes(messages))
+        if r is None:
+            _eng_err("g4dense_tokenizer_chat_template")
+        return r
+
+    def special_ids(self):
+        v = np.zeros(6, np.uint32)
+        lib().g4dense_tokenizer_special_ids(self.h, v.ctypes.data_as(_vp))
+        return dict(zip(("bos", "eos", "pad", "unk", "end_of_turn", "vocab_size"), v.tolist()))
+
+    def stop_ids(self):
+        v = np.zeros(16, np.uint32)
+        n = lib().g4dense_tokenizer_stop_ids(self.h, v.ctypes.data_as(_vp), len(v))
+        return v[:n].tolist()
+
+    def byte_value(self, tid):
+        b = ctypes.c_ubyte(0)
+        return b.value if lib().g4dense_tokenizer_byte_value(self.h, tid, ctypes.byref(b)) else None
+
+    def is_special(self, tid):
+        return bool(lib().g4dense_tokenizer_is_special(self.h, tid))
+
+    def detokenizer(self, skip_special=True):
+        return Detokenizer(self, skip_special)
+
+    def close(self):
+        if getattr(self, "h", None) and self._owner is None:
+            lib().g4dense_tokenizer_destroy(self.h)
+        self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+
+class Detokenizer:
+    """IncrementalDetokenizer: push(id) -> bytes now complete; finish() -> the rest."""
+
+    def __init__(self, tok: Tokenizer, skip_special=True):
+        self._tok = tok
+        self.h = lib().g4dense_detokenizer_create(tok.h, 1 if skip_special else 0)
+        if not self.h:
+            _eng_err("g4dense_detokenizer_create")
+
+    def push(self, tid):
+        n = ctypes.c_size_t(0)
+        return _take(lib().g4dense_detokenizer_push(self.h, tid, ctypes.byref(n)), n)
+
+    def finish(self):
+        n = ctypes.c_size_t(0)
+        return _take(lib().g4dense_detokenizer_finish(self.h, ctypes.byref(n)), n)
+
+    def __del__(self):
+        try:
+            if self.h:
+                lib().g4dense_detokenizer_destroy(self.h)
+        except Exception:
+            pass
+
+
+class StopMatcher:
+    """StreamingStopMatcher over byte strings."""
+
+    def __init__(self, stops):
+        arr = (ctypes.c_char_p * max(1, len(stops)))(*[_as_bytes(s) for s in stops])
+        self.h = lib().g4dense_stop_matcher_create(arr, len(stops))
+        if not self.h:
+            _eng_err("g4dense_stop_matcher_create")
+
+    def push(self, text):
+        b = _as_bytes(text)
+        n = ctypes.c_size_t(0)
+        return _take(lib().g4dense_stop_matcher_push(self.h, b, len(b), ctypes.byref(n)), n)
+
+    def finish(self):
+        n = ctypes.c_size_t(0)
+        return _take(lib().g4dense_stop_matcher_finish(self.h, ctypes.byref(n)), n)
+
+    @property
+    def stopped(self):
+        return bool(lib().g4dense_stop_matcher_stopped(self.h, None))
+
+    @property
+    def matched(self):
+        m = ctypes.c_char_p()
+        lib().g4dense_stop_matcher_stopped(self.h, ctypes.byref(m))
+        return m.value or b""
+
+    def __del__(self):
+        try:
+            if self.h:
+                lib().g4dense_stop_matcher_destroy(self.h)
+        except Exception:
+            pass
+
+
+def utf8_repair(data: bytes, flush_all: bool):
+    """-> (repaired bytes, bytes of `data` consumed)."""
+    used, n = ctypes.c_size_t(0), ctypes.c_size_t(0)
+    p = lib().g4dense_utf8_repair(data, len(data), 1 if flush_all else 0, ctypes.byref(used), ctypes.byref(n))
+    return ctypes.string_at(p, n.value), used.value
