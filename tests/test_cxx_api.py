@@ -112,9 +112,9 @@ def test_cxx_runner_text_generate(tok_api_bin, config0, tmp_path):
     from g4dense_b200 import synth_tokenizer as S
     from oracle import tokenizer_oracle as TO
     tokp = S.write_synthetic_tokenizer(tmp_path / "tokenizer.json")
+    prompt = S.STOP_PROMPT
     R = O.ReferenceTokenizer(tokp) if O.reference_available() else TO.Tokenizer(tokp)
     tgt = config0["target_centered"]
-    prompt = "stin évi chch"
     ids = R.encode(R.chat_template([("user", prompt)]), False)
     want, _ = O.spec_generate(O.RestatedModel(tgt), None, ids, 48)
     want = want.tolist()

@@ -297,3 +297,20 @@ def test_reference_unit_cases(built_lib, tmp_path):
         ids = (100 + rng.integers(0, 256, int(rng.integers(1, 65)))).tolist()
         d = tok.detokenizer()
         assert b"".join([d.push(t) for t in ids] + [d.finish()]) == tok.decode(ids, False)
+
+
+def test_text_prompts_have_clear_greedy_margins(config0, tok_paths):
+    """The engine's text-generation tests compare streams exactly; that is meaningful only where
+    the oracle's greedy choice is not a near-tie (top-1 minus top-2 logit >= 0.05 everywhere)."""
+    from g4dense_b200.synth_tokenizer import RAW_PROMPTS, STOP_PROMPT
+    T = TO.Tokenizer(tok_paths["pair"])
+    tgt = config0["target_centered"]
+    cases = [(T.encode(T.chat_template([("user", STOP_PROMPT)]), False), 48, True)]
+    cases += [(T.encode(p.encode(), True), 40, False) for p in RAW_PROMPTS]
+    for ids, n, must_stop in cases:
+        toks, _ = O.spec_generate(O.RestatedModel(tgt), None, ids, n)
+        toks = toks.tolist()
+        cut = next((i for i, t in enumerate(toks) if t in T.stop_ids), None)
+        assert (cut is not None) == must_stop
+        toks = toks if cut is None else toks[:cut + 1]
+        assert min(O.greedy_margins(tgt, ids, toks)) >= 0.05

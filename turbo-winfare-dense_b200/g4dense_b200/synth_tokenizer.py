@@ -41,6 +41,16 @@ SYLLABLES = ["ka", "to", "ri", "en", "the", "ing", "ion", "ar", "qu", "st", "pre
              "中", "文", "ly", "ed", "un", "re", "'s", "1", "2", "0", "9"]
 
 
+# Text prompts for the engine's text entry points on BASELINE config 0's zero-mean target (seed 0)
+# with this tokenizer: along each greedy continuation the oracle's top-1 minus top-2 logit stays
+# at or above 0.05, so the engine's stream must equal the oracle's token for token.
+# STOP_PROMPT, wrapped in the chat template, reaches a stop id at index 33 of the stream;
+# RAW_PROMPTS are encoded as given (<bos> first; 17 and 22 ids, so tensor-core prefill) and hold
+# added tokens and byte-fallback characters.
+STOP_PROMPT = "stin évi chch"
+RAW_PROMPTS = ("thequexst 🎉中totheneñalyshorarre1", "ex [multimodal]ñaé2ne🎉éing中😀edé[multimodal]sh")
+
+
 def _corpus(rng: np.random.Generator, n_words: int):
     w = 1.0 / np.arange(1, len(SYLLABLES) + 1) ** 0.8
     w /= w.sum()
