@@ -1,0 +1,568 @@
+// Long-context attention for the full-attention layers (head_dim 512, bf16 KV cache) on the
+// 5th-generation tensor cores: Attention.hlsl (shaders/Attention.hlsl:65-179) for verify
+// batches of up to 16 rows at tens of thousands of cached keys, where the KV read dominates.
+//
+// Grid: one CTA per (key split, query-head group, KV head); S splits share the batch's key range
+// [0, base + M) in 128-key tiles. A group is gqa / G query heads of the KV head, so a CTA holds
+// N <= 48 query rows (row r = m * heads + j), and every K/V tile it loads serves all of them.
+// Per tile, with warp roles:
+//   * warp 0 (one thread) streams the tile's K, then the previous tile's V, through a ring of
+//     three 32 KB slots: each slot is two TMA tensor copies of 128 keys x 64 dims in the
+//     128-byte-swizzled layout (no multicast);
+//   * warp 1 (one thread) issues the MMAs: S^T[key][row] = K Q^T into one of two TMEM buffers,
+//     with the fp32 query split into two bf16 terms (q = q1 + q2, 16 significant bits), then
+//     O^T[dim][row] += V^T P^T into four TMEM tiles of 128 dims (V read MN-major, P as two bf16
+//     terms);
+//   * warps 4..7 (TMEM lanes = keys, columns = rows) read S^T, keep the online softmax (running
+//     max and sum in fp32, exp of the fp32 scores), write P^T to shared memory and, when a row's
+//     maximum rises, rescale that row of O^T in TMEM before the tile's P V is issued;
+//   * warps 2..7 stage the query terms first.
+// Each CTA writes its unnormalised O and {max, sum} per row; a second kernel combines the splits
+// (the softmax-weighted sum) and writes the o-projection's B fragments.
+//
+// Row m of the batch sits at position base + m and sees keys [0, base + m]. Every wait is bounded
+// (2 s); a CTA that gives up records kErrAttnLc in the error word and leaves.
+#include <cuda.h>
+#include <cuda_bf16.h>
+
+#include "bfrag.cuh"
+#include "common.cuh"
+#include "kernels.h"
+#include "launch.cuh"
+#include "model_dev.h"
+#include "tcgen05.cuh"
+#include "tma.cuh"
+
+#include <algorithm>
+#include <cstdlib>
+#include <cstring>
+
+namespace g4b {
+
+namespace {
+
+constexpr int kLcHd = 512;
+constexpr int kLcKeys = 128;    // keys per tile: the M of S^T
+constexpr int kLcMaxN = 48;     // query rows per CTA
+constexpr int kLcSlots = 3;
+constexpr uint32_t kLcBoxBytes = kLcKeys * 128;      // 128 keys x 64 dims of bf16
+constexpr uint32_t kLcSlotBytes = 2 * kLcBoxBytes;   // 128 dims
+constexpr uint32_t kLcRingBytes = kLcSlots * kLcSlotBytes;
+constexpr uint32_t kLcQBytes = 2 * (kLcHd / 64) * kLcMaxN * 128;  // 2 terms x 8 dim blocks x N rows
+constexpr uint32_t kLcPBytes = 2 * 2 * kLcMaxN * 128;             // 2 terms x 2 key blocks x N rows
+constexpr int kLcThreads = 256;
+constexpr uint32_t kLcTmemCols = 512;
+constexpr int kErrAttnLc = 7;
+
+struct LcCtl {
+    uint64_t full[kLcSlots], empty[kLcSlots];
+    uint64_t s_full[2], s_free[2];
+    uint64_t q_ready, p_full, o_done, done;
+    uint32_t tmem_base;
+    int abort;
+    int changed;
+    float m_run[kLcMaxN], l_run[kLcMaxN], m_new[kLcMaxN], corr[kLcMaxN];
+    float red[4][kLcMaxN];
+};
+constexpr size_t kLcSmemBytes = 1024 + kLcRingBytes + kLcQBytes + kLcPBytes + sizeof(LcCtl);
+static_assert(kLcSmemBytes <= 232448, "long-context attention exceeds the shared-memory limit");
+
+// Bounded wait that also gives up as soon as another warp of the CTA has.
+__device__ __forceinline__ bool lc_wait(uint64_t* bar, uint32_t parity, volatile int* abort, int* err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    const uint64_t t0 = global_ns();
+    while (!mbar_try_wait_sleep(bar, parity, 1000000u)) {
+        if (*abort) return false;
+        if (global_ns() - t0 > kWaitLimitNs) {
+            *abort = 1;
+            if (err) atomicExch(err, kErrAttnLc);
+            return false;
+        }
+    }
+    return true;
+}
+
+// Barrier of the four softmax warps; returns the AND of `ok` over their 128 threads.
+__device__ __forceinline__ bool sm_bar_and(bool ok) {
+    uint32_t r;
+    asm volatile(
+        "{\n .reg .pred p, q;\n setp.ne.b32 p, %1, 0;\n bar.red.and.pred q, 1, 128, p;\n selp.u32 %0, 1, 0, q;\n}"
+        : "=r"(r)
+        : "r"((uint32_t)ok)
+        : "memory");
+    return r != 0;
+}
+__device__ __forceinline__ void sm_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+// One 3-D TMA tensor copy (x = dim, y = KV head, z = position) completing on `bar`.
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+        "[%5];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(z), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ uint16_t bf16_bits(float x) { return __bfloat16_as_ushort(__float2bfloat16_rn(x)); }
+__device__ __forceinline__ float bf16_val(uint16_t b) { return __uint_as_float((uint32_t)b << 16); }
+
+// Byte offset of element (row, col) of a [rows][64] bf16 block in the 128-byte-swizzled layout.
+__device__ __forceinline__ uint32_t sw128_off(int row, int col) {
+    return (uint32_t)row * 128 + ((uint32_t)(((col >> 3) ^ (row & 7))) << 4) + (uint32_t)(col & 7) * 2;
+}
+
+__global__ void __launch_bounds__(kLcThreads, 1)
+    attn_lc_kernel(const __grid_constant__ CUtensorMap kmap, const __grid_constant__ CUtensorMap vmap,
+                   AttnLcParams p) {
+    extern __shared__ unsigned char smem_raw[];
+    unsigned char* sm = reinterpret_cast<unsigned char*>(
+        (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~static_cast<uintptr_t>(1023));
+    unsigned char* ring = sm;
+    unsigned char* qs = ring + kLcRingBytes;
+    unsigned char* pt = qs + kLcQBytes;
+    LcCtl& c = *reinterpret_cast<LcCtl*>(pt + kLcPBytes);
+    volatile int* abort = &c.abort;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int split = blockIdx.x, grp = blockIdx.y, kvh_i = blockIdx.z;
+    const int N = p.N, hpg = p.hpg, R = p.M * hpg;
+    const int gqa = p.qh / p.kvh;
+    // base_pos stays fixed during a pass (only a pass's last kernel writes it), so it is read
+    // before waiting on the producer of the query rows.
+    const int base = p.sp->base_pos;
+    const int kmax = base + p.M;
+    const int per = ((kmax + p.S - 1) / p.S + kLcKeys - 1) / kLcKeys * kLcKeys;
+    const int ks = split * per, ke = min(kmax, ks + per);
+    const int T = ks < ke ? (ke - ks + kLcKeys - 1) / kLcKeys : 0;
+    const int cta = (kvh_i * p.G + grp) * p.S + split;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < kLcSlots; ++s) {
+            mbar_init(&c.full[s], 1);
+            mbar_init(&c.empty[s], 1);
+        }
+        for (int b = 0; b < 2; ++b) {
+            mbar_init(&c.s_full[b], 1);
+            mbar_init(&c.s_free[b], 4);
+        }
+        mbar_init(&c.q_ready, 6);
+        mbar_init(&c.p_full, 4);
+        mbar_init(&c.o_done, 1);
+        mbar_init(&c.done, 1);
+        c.abort = 0;
+        c.changed = 0;
+        for (int r = 0; r < kLcMaxN; ++r) {
+            c.m_run[r] = -INFINITY;
+            c.l_run[r] = 0.f;
+        }
+        mbar_init_fence();
+    }
+    if (warp == 1) tc::alloc(&c.tmem_base, kLcTmemCols);
+    tc::fence_before_sync();
+    __syncthreads();
+    tc::fence_after_sync();
+    const uint32_t tmem = c.tmem_base;
+    const uint32_t s_col = 0, o_col = 2 * (uint32_t)N;  // S^T buffers, then the four O^T tiles
+    pdl_launch_dependents();
+
+    if (warp == 0) {
+        // ------------------------------------------------------------------ producer
+        if (lane == 0) {
+            int q = 0;
+            bool ok = true, waited = false;
+            auto load = [&](const CUtensorMap* map, int kt, int ci) {
+                const int slot = q % kLcSlots;
+                if (q >= kLcSlots && !lc_wait(&c.empty[slot], ((q / kLcSlots) + 1) & 1, abort, p.err)) return false;
+                unsigned char* dst = ring + slot * kLcSlotBytes;
+                mbar_expect_tx(&c.full[slot], kLcSlotBytes);
+                tma_load_3d(dst, map, 128 * ci, kvh_i, kt, &c.full[slot]);
+                tma_load_3d(dst + kLcBoxBytes, map, 128 * ci + 64, kvh_i, kt, &c.full[slot]);
+                ++q;
+                return true;
+            };
+            // Order of use: K(0), then for each t >= 1 K(t) and V(t - 1), then V(T - 1). Keys
+            // below base come from earlier passes and are fetched before the producer wait.
+            for (int t = 0; t <= T && ok; ++t) {
+                if (t < T) {
+                    const int kt = ks + t * kLcKeys;
+                    if (!waited && kt + kLcKeys > base) {
+                        pdl_wait();
+                        waited = true;
+                    }
+                    for (int ci = 0; ci < 4 && ok; ++ci) ok = load(&kmap, kt, ci);
+                }
+                if (t >= 1)
+                    for (int ci = 0; ci < 4 && ok; ++ci) ok = load(&vmap, ks + (t - 1) * kLcKeys, ci);
+            }
+            // Every issued copy lands before the CTA can exit.
+            for (int i = max(0, q - kLcSlots); i < q; ++i)
+                if (!mbar_wait(&c.full[i % kLcSlots], (i / kLcSlots) & 1) && p.err) atomicExch(p.err, kErrAttnLc);
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            const uint32_t id_s = tc::idesc_bf16(kLcKeys, N, false), id_o = tc::idesc_bf16(128, N, true);
+            const uint32_t q_addr = smem_u32(qs), p_addr = smem_u32(pt), r_addr = smem_u32(ring);
+            const uint32_t blk = (uint32_t)N * 128;  // bytes of one [N rows][64] block
+            int q = 0;
+            bool ok = lc_wait(&c.q_ready, 0, abort, p.err);
+            auto issue_s = [&](int t) {
+                const int b = t & 1;
+                if (t >= 2 && !lc_wait(&c.s_free[b], ((t >> 1) - 1) & 1, abort, p.err)) return false;
+                for (int ci = 0; ci < 4; ++ci, ++q) {
+                    const int slot = q % kLcSlots;
+                    if (!lc_wait(&c.full[slot], (q / kLcSlots) & 1, abort, p.err)) return false;
+                    tc::fence_after_sync();
+                    const uint32_t sa = r_addr + slot * kLcSlotBytes;
+#pragma unroll
+                    for (int h = 0; h < 2; ++h)
+#pragma unroll
+                        for (int kk = 0; kk < 4; ++kk)
+#pragma unroll
+                            for (int term = 0; term < 2; ++term) {
+                                const uint32_t qb = q_addr + (uint32_t)(term * 8 + 2 * ci + h) * blk + kk * 32;
+                                tc::mma_ss(tmem + s_col + b * N, tc::desc_sw128(sa + h * kLcBoxBytes + kk * 32),
+                                           tc::desc_sw128(qb), id_s, (ci | h | kk | term) ? 1u : 0u);
+                            }
+                    tc::commit(&c.empty[slot]);
+                }
+                tc::commit(&c.s_full[b]);
+                return true;
+            };
+            auto issue_o = [&](int t) {
+                if (!lc_wait(&c.p_full, t & 1, abort, p.err)) return false;
+                tc::fence_after_sync();
+                for (int ci = 0; ci < 4; ++ci, ++q) {
+                    const int slot = q % kLcSlots;
+                    if (!lc_wait(&c.full[slot], (q / kLcSlots) & 1, abort, p.err)) return false;
+                    tc::fence_after_sync();
+                    const uint32_t sa = r_addr + slot * kLcSlotBytes;
+#pragma unroll
+                    for (int kk = 0; kk < 8; ++kk)
+#pragma unroll
+                        for (int term = 0; term < 2; ++term) {
+                            // V^T rows = this slot's 128 dims (two 64-dim boxes kLcBoxBytes apart),
+                            // K = keys 16 kk .. 16 kk + 15 (rows of the boxes, 8-key groups 1 KB apart).
+                            const uint64_t a = tc::desc_sw128_mn(sa + kk * 2048, kLcBoxBytes, 1024);
+                            const uint32_t pb = p_addr + (uint32_t)(term * 2 + (kk >> 2)) * blk + (kk & 3) * 32;
+                            tc::mma_ss(tmem + o_col + ci * N, a, tc::desc_sw128(pb), id_o,
+                                       (t > 0 || kk > 0 || term > 0) ? 1u : 0u);
+                        }
+                    tc::commit(&c.empty[slot]);
+                }
+                tc::commit(&c.o_done);
+                return true;
+            };
+            if (ok && T > 0) ok = issue_s(0);
+            for (int t = 1; t < T && ok; ++t) ok = issue_s(t) && issue_o(t - 1);
+            if (ok && T > 0) ok = issue_o(T - 1);
+            tc::commit(&c.done);  // every MMA has completed before tensor memory is freed
+            if (!mbar_wait(&c.done, 0) && p.err) atomicExch(p.err, kErrAttnLc);
+        }
+    } else {
+        // ------------------------------------------------------------------ query staging
+        pdl_wait();
+        for (int r = warp - 2; r < N; r += 6) {
+            float x[16];
+            if (r < R) {
+                const int m = r / hpg, qhead = kvh_i * gqa + grp * hpg + r % hpg;
+                const float4* src = reinterpret_cast<const float4*>(p.q + ((size_t)m * p.qh + qhead) * kLcHd) + 4 * lane;
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    const float4 v = src[i];
+                    x[4 * i] = v.x;
+                    x[4 * i + 1] = v.y;
+                    x[4 * i + 2] = v.z;
+                    x[4 * i + 3] = v.w;
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 16; ++i) x[i] = 0.f;
+            }
+            // dims 16 lane .. 16 lane + 15: chunks 2 lane, 2 lane + 1 of dim block lane / 4
+            const int db = lane >> 2;
+#pragma unroll
+            for (int h = 0; h < 2; ++h) {
+                uint32_t hi[4], lo[4];
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    uint16_t a0 = bf16_bits(x[8 * h + 2 * i]), a1 = bf16_bits(x[8 * h + 2 * i + 1]);
+                    uint16_t b0 = bf16_bits(x[8 * h + 2 * i] - bf16_val(a0));
+                    uint16_t b1 = bf16_bits(x[8 * h + 2 * i + 1] - bf16_val(a1));
+                    hi[i] = (uint32_t)a0 | ((uint32_t)a1 << 16);
+                    lo[i] = (uint32_t)b0 | ((uint32_t)b1 << 16);
+                }
+                const int col = (lane & 3) * 16 + 8 * h;
+                const uint32_t off = sw128_off(r, col);
+                *reinterpret_cast<uint4*>(qs + (size_t)(0 * 8 + db) * N * 128 + off) = make_uint4(hi[0], hi[1], hi[2], hi[3]);
+                *reinterpret_cast<uint4*>(qs + (size_t)(1 * 8 + db) * N * 128 + off) = make_uint4(lo[0], lo[1], lo[2], lo[3]);
+            }
+        }
+        fence_proxy_async();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&c.q_ready);
+
+        if (warp >= 4) {
+            // -------------------------------------------------------------- softmax
+            const int qd = warp - 4, tid = qd * 32 + lane;
+            const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
+            const int nch = N / 16;
+            float s[kLcMaxN];
+            bool ok = true;
+            for (int t = 0; t < T; ++t) {
+                const int b = t & 1;
+                const int key = ks + t * kLcKeys + tid;
+                ok = sm_bar_and(ok && lc_wait(&c.s_full[b], (t >> 1) & 1, abort, p.err));
+                if (!ok) break;
+                tc::fence_after_sync();
+#pragma unroll
+                for (int i = 0; i < kLcMaxN / 16; ++i)
+                    if (i < nch) {
+                        float v[16];
+                        tc::ld16(tmem + lane_base + s_col + b * N + 16 * i, v);
+                        tc::wait_ld();
+#pragma unroll
+                        for (int j = 0; j < 16; ++j) s[16 * i + j] = v[j];
+                    }
+                tc::fence_before_sync();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&c.s_free[b]);
+                // Masked, scaled scores and the tile's row maxima.
+#pragma unroll
+                for (int r = 0; r < kLcMaxN; ++r) {
+                    if (r >= N) break;
+                    const bool valid = r < R && key < ke && key <= base + r / hpg;
+                    s[r] = valid ? s[r] * p.scale : -INFINITY;
+                    const float v = warp_max(s[r]);
+                    if (lane == (r & 31)) c.red[qd][r] = v;
+                }
+                sm_bar();
+                if (tid < N) {
+                    const float mt = fmaxf(fmaxf(c.red[0][tid], c.red[1][tid]), fmaxf(c.red[2][tid], c.red[3][tid]));
+                    const float mo = c.m_run[tid], mn = fmaxf(mo, mt);
+                    c.m_new[tid] = mn;
+                    c.corr[tid] = mn == -INFINITY ? 1.f : expf(mo - mn);  // 0 while nothing was seen
+                    if (t > 0 && mn > mo) c.changed = 1;
+                }
+                // P^T reuses one buffer: the previous tile's P V must be complete (this also
+                // orders the O^T rescale below after it).
+                ok = sm_bar_and(ok && (t == 0 || lc_wait(&c.o_done, (t - 1) & 1, abort, p.err)));
+                if (!ok) break;
+                tc::fence_after_sync();
+                const bool rescale = c.changed != 0;
+                const int kb = tid >> 6, col = tid & 63;
+#pragma unroll
+                for (int r = 0; r < kLcMaxN; ++r) {
+                    if (r >= N) break;
+                    const float pr = s[r] == -INFINITY ? 0.f : expf(s[r] - c.m_new[r]);
+                    const uint16_t h1 = bf16_bits(pr), h2 = bf16_bits(pr - bf16_val(h1));
+                    const uint32_t off = sw128_off(r, col);
+                    *reinterpret_cast<uint16_t*>(pt + (size_t)(0 * 2 + kb) * N * 128 + off) = h1;
+                    *reinterpret_cast<uint16_t*>(pt + (size_t)(1 * 2 + kb) * N * 128 + off) = h2;
+                    s[r] = bf16_val(h1) + bf16_val(h2);
+                }
+                if (rescale) {
+#pragma unroll 1
+                    for (int ci = 0; ci < 4; ++ci)
+#pragma unroll
+                        for (int i = 0; i < kLcMaxN / 16; ++i)
+                            if (i < nch) {
+                                float v[16];
+                                const uint32_t ta = tmem + lane_base + o_col + ci * N + 16 * i;
+                                tc::ld16(ta, v);
+                                tc::wait_ld();
+#pragma unroll
+                                for (int j = 0; j < 16; ++j) v[j] *= c.corr[16 * i + j];
+                                tc::st16(ta, v);
+                            }
+                    tc::wait_st();
+                }
+                // Row sums of the P that the MMA multiplies (both terms).
+#pragma unroll
+                for (int r = 0; r < kLcMaxN; ++r) {
+                    if (r >= N) break;
+                    const float v = warp_sum(s[r]);
+                    if (lane == (r & 31)) c.red[qd][r] = v;
+                }
+                sm_bar();
+                if (tid < N) {
+                    c.l_run[tid] = c.l_run[tid] * c.corr[tid] + (c.red[0][tid] + c.red[1][tid]) + (c.red[2][tid] + c.red[3][tid]);
+                    c.m_run[tid] = c.m_new[tid];
+                }
+                if (tid == 0) c.changed = 0;  // every thread read it before the barrier above
+                fence_proxy_async();
+                tc::fence_before_sync();
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&c.p_full);
+            }
+            // This split's partial result: O^T (lane = dim) and {max, sum} per row.
+            ok = sm_bar_and(ok && (T == 0 || lc_wait(&c.o_done, (T - 1) & 1, abort, p.err)));
+            if (ok && T > 0) {
+                tc::fence_after_sync();
+                float* dst = p.part + (size_t)cta * N * kLcHd;
+#pragma unroll 1
+                for (int ci = 0; ci < 4; ++ci)
+#pragma unroll
+                    for (int i = 0; i < kLcMaxN / 16; ++i)
+                        if (i < nch) {
+                            float v[16];
+                            tc::ld16(tmem + lane_base + o_col + ci * N + 16 * i, v);
+                            tc::wait_ld();
+#pragma unroll
+                            for (int j = 0; j < 16; ++j)
+                                if (16 * i + j < R) __stcg(dst + (size_t)(16 * i + j) * kLcHd + 128 * ci + tid, v[j]);
+                        }
+            }
+            if (tid < N) p.ml[(size_t)cta * N + tid] = ok && T > 0 ? make_float2(c.m_run[tid], c.l_run[tid])
+                                                                : make_float2(-INFINITY, 0.f);
+        }
+    }
+
+    tc::fence_before_sync();
+    __syncthreads();
+    if (warp == 1) {
+        tc::fence_after_sync();
+        tc::dealloc(tmem, kLcTmemCols);
+    }
+}
+
+// out[row] = sum_s e^(m_s - M) O_s / sum_s e^(m_s - M) l_s, one warp per (row, 64-dim group),
+// written as the o-projection's B fragments.
+__global__ void __launch_bounds__(256) attn_lc_combine_kernel(AttnLcParams p, void* bfrag) {
+    __shared__ __half stage[8][128];
+    pdl_launch_dependents();
+    pdl_wait();
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int gqa = p.qh / p.kvh, rows = p.M * gqa;
+    const int w = blockIdx.x * 8 + warp;
+    if (w >= p.kvh * rows * 8) return;  // warp-uniform
+    const int gi = w & 7, rr = (w >> 3) % rows, kvh_i = (w >> 3) / rows;
+    const int m = rr / gqa, jj = rr % gqa, grp = jj / p.hpg, r = m * p.hpg + jj % p.hpg;
+    const int cta0 = (kvh_i * p.G + grp) * p.S;
+    float mx = -INFINITY;
+    for (int s = 0; s < p.S; ++s) {
+        const float2 ml = p.ml[(size_t)(cta0 + s) * p.N + r];
+        if (ml.y > 0.f) mx = fmaxf(mx, ml.x);
+    }
+    float n0 = 0.f, n1 = 0.f, den = 0.f;
+    for (int s = 0; s < p.S; ++s) {
+        const float2 ml = p.ml[(size_t)(cta0 + s) * p.N + r];
+        if (ml.y <= 0.f) continue;
+        const float wgt = expf(ml.x - mx);
+        const float2 o = __ldcg(reinterpret_cast<const float2*>(p.part + ((size_t)(cta0 + s) * p.N + r) * kLcHd +
+                                                               gi * 64 + 2 * lane));
+        n0 += wgt * o.x;
+        n1 += wgt * o.y;
+        den += wgt * ml.y;
+    }
+    const float inv = den > 0.f ? 1.0f / den : 0.f;
+    const int K = p.qh * kLcHd;
+    const BFragView bv = bfrag_view(bfrag, (K + 127) / 128 * 128, p.M);
+    const int qhead = kvh_i * gqa + jj;
+    bfrag_store_group(bv, p.M, m, (qhead * kLcHd) / 64 + gi, n0 * inv, n1 * inv, stage[warp]);
+}
+
+int sm_count() {
+    static int n = 0;
+    if (!n) {
+        int dev = 0;
+        cudaGetDevice(&dev);
+        cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+        if (n <= 0) n = 148;
+    }
+    return n;
+}
+
+int splits_for(int kvh, int G) { return std::max(1, sm_count() / std::max(1, kvh * G)); }
+
+}  // namespace
+
+int attn_lc_groups(int M, int gqa) {
+    if (M < 1 || M > kMaxM || gqa < 1) return 0;
+    for (int G = 1; G <= gqa; ++G)
+        if (gqa % G == 0 && M * (gqa / G) <= kLcMaxN) return G;
+    return 0;
+}
+
+void attn_lc_scratch(int qh, int kvh, size_t* part_bytes, size_t* ml_bytes) {
+    size_t pb = 0, mb = 0;
+    const int gqa = qh / kvh;
+    for (int M = 1; M <= kMaxM; ++M) {
+        const int G = attn_lc_groups(M, gqa);
+        if (!G) continue;
+        const int N = (M * (gqa / G) + 15) / 16 * 16;
+        const size_t ctas = (size_t)kvh * G * splits_for(kvh, G);
+        pb = std::max(pb, ctas * N * kLcHd * sizeof(float));
+        mb = std::max(mb, ctas * N * sizeof(float2));
+    }
+    *part_bytes = pb;
+    *ml_bytes = mb;
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link against libcuda).
+cudaError_t make_kv_tmap(KvTmap* out, const uint16_t* ring, int hd, int kvh, int cap) {
+    using EncodeFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+    static EncodeFn encode = nullptr;
+    if (!encode) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        const cudaError_t e = cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn, cudaEnableDefault, &q);
+        if (e != cudaSuccess || q != cudaDriverEntryPointSuccess || !fn) return cudaErrorNotSupported;
+        encode = reinterpret_cast<EncodeFn>(fn);
+    }
+    static_assert(sizeof(KvTmap) == sizeof(CUtensorMap), "KvTmap must hold a CUtensorMap");
+    if (hd % 64 || reinterpret_cast<uintptr_t>(ring) % 16) return cudaErrorInvalidValue;
+    const cuuint64_t dims[3] = {(cuuint64_t)hd, (cuuint64_t)kvh, (cuuint64_t)cap};
+    const cuuint64_t strides[2] = {(cuuint64_t)hd * 2, (cuuint64_t)kvh * hd * 2};
+    const cuuint32_t box[3] = {64, 1, (cuuint32_t)kLcKeys};
+    const cuuint32_t estride[3] = {1, 1, 1};
+    CUtensorMap m;
+    const CUresult r = encode(&m, CU_TENSOR_MAP_DATA_TYPE_UINT16, 3, const_cast<uint16_t*>(ring), dims, strides, box,
+                              estride, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                              CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) return cudaErrorInvalidValue;
+    std::memcpy(out, &m, sizeof(m));
+    return cudaSuccess;
+}
+
+cudaError_t attention_lc(const AttnArgs& a, const KvTmap& k, const KvTmap& v, float* part, float2* ml, int* err,
+                         void* bfrag, cudaStream_t st, bool pdl) {
+    if (a.hd != kLcHd || a.window != 0 || !a.kv_bf16 || a.kvh < 1 || a.qh % a.kvh) return cudaErrorInvalidValue;
+    const int gqa = a.qh / a.kvh, G = attn_lc_groups(a.M, gqa);
+    if (!G) return cudaErrorInvalidValue;
+    AttnLcParams p{};
+    p.q = a.q;
+    p.sp = a.sp;
+    p.part = part;
+    p.ml = ml;
+    p.err = err;
+    p.M = a.M;
+    p.qh = a.qh;
+    p.kvh = a.kvh;
+    p.G = G;
+    p.S = splits_for(a.kvh, G);
+    // G4DENSE_ATTN_LC_SPLITS lowers the split count (never raises it past what the scratch
+    // holds), so a moderate context still gives each CTA several tiles.
+    if (const char* f = std::getenv("G4DENSE_ATTN_LC_SPLITS"); f && std::atoi(f) > 0) p.S = std::min(p.S, std::atoi(f));
+    p.hpg = gqa / G;
+    p.N = (a.M * p.hpg + 15) / 16 * 16;
+    p.scale = a.scale;
+    static bool attr = false;
+    if (!attr) {
+        const cudaError_t e =
+            cudaFuncSetAttribute(attn_lc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kLcSmemBytes);
+        if (e != cudaSuccess) return e;
+        attr = true;
+    }
+    CUtensorMap km, vm;
+    std::memcpy(&km, &k, sizeof(km));
+    std::memcpy(&vm, &v, sizeof(vm));
+    cudaError_t e = launch(attn_lc_kernel, dim3(p.S, G, a.kvh), dim3(kLcThreads), kLcSmemBytes, st, pdl, km, vm, p);
+    if (e != cudaSuccess) return e;
+    const int warps = a.kvh * a.M * gqa * 8;
+    return launch(attn_lc_combine_kernel, dim3((warps + 7) / 8), dim3(256), 0, st, pdl, p, bfrag);
+}
+
+}  // namespace g4b

@@ -39,6 +39,16 @@ cudaError_t g4b_rowepi(const g4b::GemmOut& o, const g4b::TpGather& tg, const flo
 // B fragments. One 8-CTA cluster per (KV head, 16 query rows), key splits combined in DSMEM.
 cudaError_t g4b_attention(const g4b::AttnArgs& a, void* bfrag, cudaStream_t st, bool pdl);
 
+namespace g4b {
+// Long-context attention for full-attention layers with head_dim 512 and a bf16 KV cache
+// (attn_lc.cu). attn_lc_groups is 0 where a batch of M rows cannot use it.
+int attn_lc_groups(int M, int gqa);
+void attn_lc_scratch(int qh, int kvh, size_t* part_bytes, size_t* ml_bytes);
+cudaError_t make_kv_tmap(KvTmap* out, const uint16_t* ring, int hd, int kvh, int cap);
+cudaError_t attention_lc(const AttnArgs& a, const KvTmap& k, const KvTmap& v, float* part, float2* ml, int* err,
+                         void* bfrag, cudaStream_t st, bool pdl);
+}  // namespace g4b
+
 // ---- head.cu
 struct HeadResult {
     int n_emit;          // tokens emitted by greedy acceptance (accepted drafts + 1)

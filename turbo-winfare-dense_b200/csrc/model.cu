@@ -18,6 +18,7 @@
 #include <algorithm>
 #include <cmath>
 #include <cstddef>
+#include <cstdlib>
 #include <cstring>
 #include <sstream>
 
@@ -390,6 +391,28 @@ void DeviceModel::finalize_load() {
         L.v_ring = static_cast<uint16_t*>(dmalloc(n * 2));
         kv_bytes_ += n * 4;
     }
+    // Long-context mode (bf16 KV, a context of 8192 or more, or G4DENSE_ATTN_LC=1; =0 turns it
+    // off): full-attention layers of head_dim 512 run their verify-batch attention on the
+    // tensor cores (attn_lc.cu), which needs TMA maps of their rings and per-split scratch.
+    const char* lc_env = std::getenv("G4DENSE_ATTN_LC");
+    const bool lc_want = lc_env ? std::atoi(lc_env) != 0 : opt_.max_context >= 8192;
+    if (lc_want && opt_.kv_bf16 && !mtp_) {
+        size_t pb = 0, mb = 0;
+        for (auto& L : layers_) {
+            if (!L.geo.is_global || L.hd != 512 || !L.k_ring) continue;
+            cuda_check(make_kv_tmap(&L.k_tmap, L.k_ring, L.hd, L.kvh, L.cap), "K ring map");
+            cuda_check(make_kv_tmap(&L.v_tmap, L.v_ring, L.hd, L.kvh, L.cap), "V ring map");
+            L.lc = true;
+            size_t a = 0, b = 0;
+            attn_lc_scratch(L.qh, L.kvh, &a, &b);
+            pb = std::max(pb, a);
+            mb = std::max(mb, b);
+        }
+        if (pb) {
+            lc_part_ = static_cast<float*>(dmalloc(pb));
+            lc_ml_ = static_cast<float2*>(dmalloc(mb));
+        }
+    }
     init_buffers();
     clear_kv();
     cuda_check(cudaStreamSynchronize(stream_), "load");
@@ -527,14 +550,15 @@ void DeviceModel::clear_kv() {
 uint64_t DeviceModel::pass_weight_bytes() const { return weight_bytes_; }
 
 int DeviceModel::kernels_per_pass(int M) const {
-    (void)M;
     // MTP step: input, pre-projection GEMM, its epilogue; per layer the 9 below; the
     // post-projection and LM head GEMMs, head_chunks and finalize.
     if (mtp_) return 3 + 9 * (int)layers_.size() + 4;
     // embed_norm; per layer 4 GEMMs + qkv_epi + attention + 2 norm/residual epilogues +
     // geglu; LM head GEMM + head_chunks + finalize (NCCL's all-reduce kernels not counted)
     const int per_layer = 9;
-    return 1 + per_layer * (int)layers_.size() + 3;
+    int lc = 0;  // the long-context attention is two kernels (splits, then their combination)
+    for (const auto& L : layers_) lc += L.lc && attn_lc_groups(M, L.qh / L.kvh) ? 1 : 0;
+    return 1 + per_layer * (int)layers_.size() + lc + 3;
 }
 
 double DeviceModel::profile_gemms(int M, int reps, uint64_t* bytes, int* gemm_launches) {
@@ -754,7 +778,11 @@ void DeviceModel::enqueue_raw(int M, PassKind kind, bool want_logits, uint32_t* 
         aa.window = L.geo.is_global ? 0 : (int)h_.sliding_window;
         aa.kv_bf16 = opt_.kv_bf16;
         aa.scale = 1.0f;
-        cuda_check(g4b_attention(aa, bf_attn_, stream_, pdl), "attention");
+        if (L.lc && attn_lc_groups(M, L.qh / L.kvh))
+            cuda_check(attention_lc(aa, L.k_tmap, L.v_tmap, lc_part_, lc_ml_, err_dev_, bf_attn_, stream_, pdl),
+                       "attention_lc");
+        else
+            cuda_check(g4b_attention(aa, bf_attn_, stream_, pdl), "attention");
         // o projection + post-attention norm / residual + pre-FFN norm
         // The o and down GEMMs leave split-K slots. The norm epilogue sums them; under tensor
         // parallelism it first stores this rank's sums into its peer-mapped partial buffer,

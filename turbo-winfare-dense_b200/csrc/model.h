@@ -49,6 +49,9 @@ struct DevLayer {
     uint16_t *q_norm = nullptr, *k_norm = nullptr;
     uint16_t *k_ring = nullptr, *v_ring = nullptr;
     int cap = 0;
+    // Long-context mode: TMA maps of the rings for the tensor-core attention (attn_lc.cu).
+    bool lc = false;
+    KvTmap k_tmap{}, v_tmap{};
     // MTP drafter layers attend over a donor layer of the target instead of their own ring.
     const uint16_t *att_k = nullptr, *att_v = nullptr;
     int att_cap = 0, att_kvh = 0, att_window = 0;
@@ -196,6 +199,8 @@ class DeviceModel {
     float* hres_[2] = {nullptr, nullptr};
     void* bf_d_ = nullptr;     // B fragments with K = d_model
     void* bf_attn_ = nullptr;  // K = local q_heads * head_dim (max over layers)
+    float* lc_part_ = nullptr;   // long-context attention: per-split partial outputs
+    float2* lc_ml_ = nullptr;    //   and {max, sum} per row
     void* bf_ff_ = nullptr;    // K = local FFN width
     float* part_ = nullptr;
     size_t part_floats_ = 0;

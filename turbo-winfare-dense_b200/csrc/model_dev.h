@@ -183,4 +183,22 @@ struct AttnArgs {
     float scale;
 };
 
+// A TMA tensor map (CUtensorMap) of one layer's K or V ring, [cap][kvh][hd] bf16, read in boxes
+// of 128 positions x 64 dims with 128-byte swizzle.
+struct alignas(64) KvTmap {
+    unsigned char bytes[128];
+};
+
+// Long-context attention (attn_lc.cu): one CTA per (key split, query-head group, KV head).
+struct AttnLcParams {
+    const float* q;          // [M][qh][512]
+    const StepParams* sp;
+    float* part;             // [kvh][G][S][N][512] unnormalised partial outputs
+    float2* ml;              // [kvh][G][S][N] {max, sum} per row
+    int* err;
+    int M, qh, kvh;
+    int G, S, N, hpg;        // groups per KV head, key splits, rows per CTA (padded), heads per group
+    float scale;
+};
+
 }  // namespace g4b

@@ -1,8 +1,8 @@
 // Thin inline-PTX wrappers for the sm_100a 5th-generation tensor core (tcgen05): tensor-memory
 // allocation, the MMA with its accumulator in tensor memory (TMEM), completion tracking through
-// mbarriers, and TMEM <-> register moves. Only the forms the prefill GEMM uses are wrapped:
-// cta_group::1, kind::f16 (fp16 inputs, fp32 accumulate), B from shared memory, A from shared
-// or tensor memory.
+// mbarriers, and TMEM <-> register moves. Only the forms the prefill GEMM and the long-context
+// attention use are wrapped: cta_group::1, kind::f16 (fp16 or bf16 inputs, fp32 accumulate), B
+// from shared memory, A from shared (K- or MN-major) or tensor memory.
 //
 // TMEM addresses are (lane << 16) | column. A warp may only touch the 32 lanes of its
 // quadrant, lanes 32 * (warp % 4) .. +31.
@@ -94,6 +94,18 @@ __device__ __forceinline__ void st32(uint32_t taddr, const uint32_t (&r)[32]) {
         "r"(r[25]), "r"(r[26]), "r"(r[27]), "r"(r[28]), "r"(r[29]), "r"(r[30]), "r"(r[31])
         : "memory");
 }
+// 16 consecutive 32-bit columns of this thread's lane. Warp-collective; follow with wait_st().
+__device__ __forceinline__ void st16(uint32_t taddr, const float (&v)[16]) {
+    asm volatile(
+        "tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};" ::"r"(
+            taddr),
+        "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])), "r"(__float_as_uint(v[3])),
+        "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])), "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])),
+        "r"(__float_as_uint(v[8])), "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])),
+        "r"(__float_as_uint(v[11])), "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])),
+        "r"(__float_as_uint(v[14])), "r"(__float_as_uint(v[15]))
+        : "memory");
+}
 __device__ __forceinline__ void wait_st() { asm volatile("tcgen05.wait::st.sync.aligned;" ::: "memory"); }
 
 // Shared-memory matrix descriptor of a K-major operand tile in the canonical 128-byte-swizzled
@@ -106,6 +118,27 @@ __device__ __forceinline__ uint64_t desc_sw128(uint32_t addr) {
            | ((uint64_t)(1024 >> 4) << 32)     // stride byte offset: 8-row atom pitch
            | ((uint64_t)1 << 46)               // descriptor version for sm_100
            | ((uint64_t)2 << 61);              // 128-byte swizzle
+}
+
+// Shared-memory matrix descriptor of an MN-major operand tile in the 128-byte-swizzled layout:
+// each 128-byte row holds 64 consecutive M (or N) elements of one K index, rows of consecutive K
+// are 128 B apart (swizzled as above), the next 8 K rows `sbo` bytes on and the next 64 M
+// elements `lbo` bytes on. `addr` is the first row's address (1024-byte aligned atom).
+__device__ __forceinline__ uint64_t desc_sw128_mn(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+    return (uint64_t)((addr & 0x3FFFFu) >> 4)  // start address, 16-byte units
+           | ((uint64_t)(lbo >> 4) << 16)       // leading byte offset: next 64 M elements
+           | ((uint64_t)(sbo >> 4) << 32)       // stride byte offset: next 8 K rows
+           | ((uint64_t)1 << 46)               // descriptor version for sm_100
+           | ((uint64_t)2 << 61);              // 128-byte swizzle
+}
+
+// Instruction descriptor for kind::f16 with bf16 A and B, fp32 D, M x N; a_mn: A is MN-major.
+__host__ __device__ constexpr uint32_t idesc_bf16(int M, int N, bool a_mn) {
+    return (1u << 4)                        // D format: f32
+           | (1u << 7) | (1u << 10)         // A, B format: bf16
+           | ((a_mn ? 1u : 0u) << 15)       // A major-ness (0: K-major)
+           | ((uint32_t)(N >> 3) << 17)     // N / 8
+           | ((uint32_t)(M >> 4) << 24);    // M / 16
 }
 
 // Instruction descriptor for kind::f16: fp16 A and B (both K-major), fp32 D, M x N.
