@@ -13,10 +13,12 @@
 //     with the fp32 query split into two bf16 terms (q = q1 + q2, 16 significant bits), then
 //     O^T[dim][row] += V^T P^T into four TMEM tiles of 128 dims (V read MN-major, P as two bf16
 //     terms);
-//   * warps 4..7 (TMEM lanes = keys, columns = rows) read S^T, keep the online softmax (running
-//     max and sum in fp32, exp of the fp32 scores), write P^T to shared memory and, when a row's
-//     maximum rises, rescale that row of O^T in TMEM before the tile's P V is issued;
-//   * warps 2..7 stage the query terms first.
+//   * warps 4..11 (TMEM lanes = keys, columns = rows; two warps per lane quadrant, 24 rows each)
+//     read S^T, keep the online softmax (running max and sum in fp32, exp of the fp32 scores;
+//     the per-row reductions over a warp's 32 keys are butterfly reduce-scatters), write P^T to
+//     shared memory and, when a row's maximum rises, rescale that row of O^T in TMEM before the
+//     tile's P V is issued;
+//   * warps 2..11 stage the query terms first.
 // Each CTA writes its unnormalised O and {max, sum} per row; a second kernel combines the splits
 // (the softmax-weighted sum) and writes the o-projection's B fragments.
 //
@@ -50,7 +52,9 @@ constexpr uint32_t kLcSlotBytes = 2 * kLcBoxBytes;   // 128 dims
 constexpr uint32_t kLcRingBytes = kLcSlots * kLcSlotBytes;
 constexpr uint32_t kLcQBytes = 2 * (kLcHd / 64) * kLcMaxN * 128;  // 2 terms x 8 dim blocks x N rows
 constexpr uint32_t kLcPBytes = 2 * 2 * kLcMaxN * 128;             // 2 terms x 2 key blocks x N rows
-constexpr int kLcThreads = 256;
+constexpr int kLcThreads = 384;
+constexpr int kLcSoftWarps = 8;   // warps 4..11
+constexpr int kLcStageWarps = 10;  // warps 2..11
 constexpr uint32_t kLcTmemCols = 512;
 constexpr int kErrAttnLc = 7;
 
@@ -82,17 +86,55 @@ __device__ __forceinline__ bool lc_wait(uint64_t* bar, uint32_t parity, volatile
     return true;
 }
 
-// Barrier of the four softmax warps; returns the AND of `ok` over their 128 threads.
+// Barrier of the eight softmax warps; returns the AND of `ok` over their 256 threads.
 __device__ __forceinline__ bool sm_bar_and(bool ok) {
     uint32_t r;
     asm volatile(
-        "{\n .reg .pred p, q;\n setp.ne.b32 p, %1, 0;\n bar.red.and.pred q, 1, 128, p;\n selp.u32 %0, 1, 0, q;\n}"
+        "{\n .reg .pred p, q;\n setp.ne.b32 p, %1, 0;\n bar.red.and.pred q, 1, 256, p;\n selp.u32 %0, 1, 0, q;\n}"
         : "=r"(r)
         : "r"((uint32_t)ok)
         : "memory");
     return r != 0;
 }
-__device__ __forceinline__ void sm_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+__device__ __forceinline__ void sm_bar() { asm volatile("bar.sync 1, 256;" ::: "memory"); }
+
+// Reduce-scatter of 24 per-lane values over the warp (max or sum across the 32 lanes): each
+// exchange sends the half the lane gives away and combines the half it keeps, so 27 shuffles
+// replace 24 x 5. Afterwards v[0..2] hold the reductions of rows 12 b4 + 6 b3 + 3 b2 + (0..2),
+// b_i the lane's bits (the four lanes sharing bits 4..2 hold the same values).
+template <bool kMax>
+__device__ __forceinline__ void reduce_scatter24(float (&v)[24], int lane) {
+    auto op = [](float a, float b) { return kMax ? fmaxf(a, b) : a + b; };
+    {
+        const bool h = lane & 16;
+#pragma unroll
+        for (int i = 0; i < 12; ++i) {
+            const float snd = h ? v[i] : v[i + 12], kp = h ? v[i + 12] : v[i];
+            v[i] = op(kp, __shfl_xor_sync(0xffffffffu, snd, 16));
+        }
+    }
+    {
+        const bool h = lane & 8;
+#pragma unroll
+        for (int i = 0; i < 6; ++i) {
+            const float snd = h ? v[i] : v[i + 6], kp = h ? v[i + 6] : v[i];
+            v[i] = op(kp, __shfl_xor_sync(0xffffffffu, snd, 8));
+        }
+    }
+    {
+        const bool h = lane & 4;
+#pragma unroll
+        for (int i = 0; i < 3; ++i) {
+            const float snd = h ? v[i] : v[i + 3], kp = h ? v[i + 3] : v[i];
+            v[i] = op(kp, __shfl_xor_sync(0xffffffffu, snd, 4));
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < 3; ++i) {
+        v[i] = op(v[i], __shfl_xor_sync(0xffffffffu, v[i], 2));
+        v[i] = op(v[i], __shfl_xor_sync(0xffffffffu, v[i], 1));
+    }
+}
 
 // One 3-D TMA tensor copy (x = dim, y = KV head, z = position) completing on `bar`.
 __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, int x, int y, int z, uint64_t* bar) {
@@ -143,10 +185,10 @@ __global__ void __launch_bounds__(kLcThreads, 1)
         }
         for (int b = 0; b < 2; ++b) {
             mbar_init(&c.s_full[b], 1);
-            mbar_init(&c.s_free[b], 4);
+            mbar_init(&c.s_free[b], kLcSoftWarps);
         }
-        mbar_init(&c.q_ready, 6);
-        mbar_init(&c.p_full, 4);
+        mbar_init(&c.q_ready, kLcStageWarps);
+        mbar_init(&c.p_full, kLcSoftWarps);
         mbar_init(&c.o_done, 1);
         mbar_init(&c.done, 1);
         c.abort = 0;
@@ -262,7 +304,7 @@ __global__ void __launch_bounds__(kLcThreads, 1)
     } else {
         // ------------------------------------------------------------------ query staging
         pdl_wait();
-        for (int r = warp - 2; r < N; r += 6) {
+        for (int r = warp - 2; r < N; r += kLcStageWarps) {
             float x[16];
             if (r < R) {
                 const int m = r / hpg, qhead = kvh_i * gqa + grp * hpg + r % hpg;
@@ -304,38 +346,49 @@ __global__ void __launch_bounds__(kLcThreads, 1)
 
         if (warp >= 4) {
             // -------------------------------------------------------------- softmax
-            const int qd = warp - 4, tid = qd * 32 + lane;
+            const int sw = warp - 4, qd = warp & 3, half = sw >> 2;
+            const int tid = sw * 32 + lane;  // 0..255
+            const int r0 = 24 * half;        // this warp's rows r0 .. r0 + 23
+            const bool active = r0 < N;      // warp-uniform
             const uint32_t lane_base = (uint32_t)(qd * 32) << 16;
-            const int nch = N / 16;
-            float s[kLcMaxN];
+            const int rs0 = r0 + ((lane >> 4) & 1) * 12 + ((lane >> 3) & 1) * 6 + ((lane >> 2) & 1) * 3;
+            const int kb = (qd * 32 + lane) >> 6, col = (qd * 32 + lane) & 63;
+            float s[24];
             bool ok = true;
             for (int t = 0; t < T; ++t) {
                 const int b = t & 1;
-                const int key = ks + t * kLcKeys + tid;
+                const int kt = ks + t * kLcKeys, key = kt + qd * 32 + lane;
                 ok = sm_bar_and(ok && lc_wait(&c.s_full[b], (t >> 1) & 1, abort, p.err));
                 if (!ok) break;
                 tc::fence_after_sync();
+                if (active) {
+                    float v[16], w[8];
+                    tc::ld16(tmem + lane_base + s_col + b * N + r0, v);
+                    tc::ld8(tmem + lane_base + s_col + b * N + r0 + 16, w);
+                    tc::wait_ld();
 #pragma unroll
-                for (int i = 0; i < kLcMaxN / 16; ++i)
-                    if (i < nch) {
-                        float v[16];
-                        tc::ld16(tmem + lane_base + s_col + b * N + 16 * i, v);
-                        tc::wait_ld();
+                    for (int j = 0; j < 16; ++j) s[j] = v[j];
 #pragma unroll
-                        for (int j = 0; j < 16; ++j) s[16 * i + j] = v[j];
-                    }
+                    for (int j = 0; j < 8; ++j) s[16 + j] = w[j];
+                }
                 tc::fence_before_sync();
                 __syncwarp();
                 if (lane == 0) mbar_arrive(&c.s_free[b]);
-                // Masked, scaled scores and the tile's row maxima.
+                // Masked, scaled scores. A tile below every row's last key and inside the split
+                // needs the row check only.
+                const bool inside = kt + kLcKeys <= ke && kt + kLcKeys - 1 <= base;
+                float red[24];
 #pragma unroll
-                for (int r = 0; r < kLcMaxN; ++r) {
-                    if (r >= N) break;
-                    const bool valid = r < R && key < ke && key <= base + r / hpg;
-                    s[r] = valid ? s[r] * p.scale : -INFINITY;
-                    const float v = warp_max(s[r]);
-                    if (lane == (r & 31)) c.red[qd][r] = v;
+                for (int j = 0; j < 24; ++j) {
+                    const int r = r0 + j;
+                    const bool valid = r < R && (inside || (key < ke && key <= base + r / hpg));
+                    s[j] = valid ? s[j] * p.scale : -INFINITY;
+                    red[j] = s[j];
                 }
+                reduce_scatter24<true>(red, lane);
+                if (active && (lane & 3) == 0)
+#pragma unroll
+                    for (int i = 0; i < 3; ++i) c.red[qd][rs0 + i] = red[i];
                 sm_bar();
                 if (tid < N) {
                     const float mt = fmaxf(fmaxf(c.red[0][tid], c.red[1][tid]), fmaxf(c.red[2][tid], c.red[3][tid]));
@@ -350,23 +403,29 @@ __global__ void __launch_bounds__(kLcThreads, 1)
                 if (!ok) break;
                 tc::fence_after_sync();
                 const bool rescale = c.changed != 0;
-                const int kb = tid >> 6, col = tid & 63;
+                if (active) {
 #pragma unroll
-                for (int r = 0; r < kLcMaxN; ++r) {
-                    if (r >= N) break;
-                    const float pr = s[r] == -INFINITY ? 0.f : expf(s[r] - c.m_new[r]);
-                    const uint16_t h1 = bf16_bits(pr), h2 = bf16_bits(pr - bf16_val(h1));
-                    const uint32_t off = sw128_off(r, col);
-                    *reinterpret_cast<uint16_t*>(pt + (size_t)(0 * 2 + kb) * N * 128 + off) = h1;
-                    *reinterpret_cast<uint16_t*>(pt + (size_t)(1 * 2 + kb) * N * 128 + off) = h2;
-                    s[r] = bf16_val(h1) + bf16_val(h2);
+                    for (int j = 0; j < 24; ++j) {
+                        const int r = r0 + j;
+                        if (r >= N) break;
+                        const float pr = s[j] == -INFINITY ? 0.f : expf(s[j] - c.m_new[r]);
+                        const uint16_t h1 = bf16_bits(pr), h2 = bf16_bits(pr - bf16_val(h1));
+                        const uint32_t off = sw128_off(r, col);
+                        *reinterpret_cast<uint16_t*>(pt + (size_t)(0 * 2 + kb) * N * 128 + off) = h1;
+                        *reinterpret_cast<uint16_t*>(pt + (size_t)(1 * 2 + kb) * N * 128 + off) = h2;
+                        red[j] = bf16_val(h1) + bf16_val(h2);
+                    }
+                } else {
+#pragma unroll
+                    for (int j = 0; j < 24; ++j) red[j] = 0.f;
                 }
                 if (rescale) {
+                    // This warp's two O^T tiles (dims 128 ci .. +127, lane = dim) times corr[row].
 #pragma unroll 1
-                    for (int ci = 0; ci < 4; ++ci)
+                    for (int ci = half; ci < 4; ci += 2)
 #pragma unroll
                         for (int i = 0; i < kLcMaxN / 16; ++i)
-                            if (i < nch) {
+                            if (16 * i < N) {
                                 float v[16];
                                 const uint32_t ta = tmem + lane_base + o_col + ci * N + 16 * i;
                                 tc::ld16(ta, v);
@@ -378,12 +437,10 @@ __global__ void __launch_bounds__(kLcThreads, 1)
                     tc::wait_st();
                 }
                 // Row sums of the P that the MMA multiplies (both terms).
+                reduce_scatter24<false>(red, lane);
+                if (active && (lane & 3) == 0)
 #pragma unroll
-                for (int r = 0; r < kLcMaxN; ++r) {
-                    if (r >= N) break;
-                    const float v = warp_sum(s[r]);
-                    if (lane == (r & 31)) c.red[qd][r] = v;
-                }
+                    for (int i = 0; i < 3; ++i) c.red[qd][rs0 + i] = red[i];
                 sm_bar();
                 if (tid < N) {
                     c.l_run[tid] = c.l_run[tid] * c.corr[tid] + (c.red[0][tid] + c.red[1][tid]) + (c.red[2][tid] + c.red[3][tid]);
@@ -401,16 +458,17 @@ __global__ void __launch_bounds__(kLcThreads, 1)
                 tc::fence_after_sync();
                 float* dst = p.part + (size_t)cta * N * kLcHd;
 #pragma unroll 1
-                for (int ci = 0; ci < 4; ++ci)
+                for (int ci = half; ci < 4; ci += 2)
 #pragma unroll
                     for (int i = 0; i < kLcMaxN / 16; ++i)
-                        if (i < nch) {
+                        if (16 * i < N) {
                             float v[16];
                             tc::ld16(tmem + lane_base + o_col + ci * N + 16 * i, v);
                             tc::wait_ld();
 #pragma unroll
                             for (int j = 0; j < 16; ++j)
-                                if (16 * i + j < R) __stcg(dst + (size_t)(16 * i + j) * kLcHd + 128 * ci + tid, v[j]);
+                                if (16 * i + j < R)
+                                    __stcg(dst + (size_t)(16 * i + j) * kLcHd + 128 * ci + qd * 32 + lane, v[j]);
                         }
             }
             if (tid < N) p.ml[(size_t)cta * N + tid] = ok && T > 0 ? make_float2(c.m_run[tid], c.l_run[tid])
