@@ -16,8 +16,8 @@
 //   * warps 4..11 (TMEM lanes = keys, columns = rows; two warps per lane quadrant, 24 rows each)
 //     read S^T, keep the online softmax (running max and sum in fp32, exp of the fp32 scores;
 //     the per-row reductions over a warp's 32 keys are butterfly reduce-scatters), write P^T to
-//     shared memory and, when a row's maximum rises, rescale that row of O^T in TMEM before the
-//     tile's P V is issued;
+//     shared memory and, when a row's maximum rises by more than kLcLazy, rescale that row of
+//     O^T in TMEM before the tile's P V is issued;
 //   * warps 2..11 stage the query terms first.
 // Each CTA writes its unnormalised O and {max, sum} per row; a second kernel combines the splits
 // (the softmax-weighted sum) and writes the o-projection's B fragments.
@@ -57,6 +57,7 @@ constexpr int kLcSoftWarps = 8;   // warps 4..11
 constexpr int kLcStageWarps = 10;  // warps 2..11
 constexpr uint32_t kLcTmemCols = 512;
 constexpr int kErrAttnLc = 7;
+constexpr float kLcLazy = 8.0f;  // rescale threshold of the running maximum (natural-log units)
 
 struct LcCtl {
     uint64_t full[kLcSlots], empty[kLcSlots];
@@ -391,11 +392,15 @@ __global__ void __launch_bounds__(kLcThreads, 1)
                     for (int i = 0; i < 3; ++i) c.red[qd][rs0 + i] = red[i];
                 sm_bar();
                 if (tid < N) {
+                    // The row's reference maximum moves only when a score exceeds it by more than
+                    // kLcLazy (so p <= e^kLcLazy); O^T and the sum are kept relative to it, which
+                    // leaves their ratio exact and skips most rescales.
                     const float mt = fmaxf(fmaxf(c.red[0][tid], c.red[1][tid]), fmaxf(c.red[2][tid], c.red[3][tid]));
-                    const float mo = c.m_run[tid], mn = fmaxf(mo, mt);
+                    const float mo = c.m_run[tid];
+                    const float mn = (mo == -INFINITY || mt > mo + kLcLazy) ? fmaxf(mo, mt) : mo;
                     c.m_new[tid] = mn;
-                    c.corr[tid] = mn == -INFINITY ? 1.f : expf(mo - mn);  // 0 while nothing was seen
-                    if (t > 0 && mn > mo) c.changed = 1;
+                    c.corr[tid] = mn == mo ? 1.f : expf(mo - mn);  // 0 while nothing was seen
+                    if (t > 0 && mn != mo) c.changed = 1;
                 }
                 // P^T reuses one buffer: the previous tile's P V must be complete (this also
                 // orders the O^T rescale below after it).
@@ -497,21 +502,49 @@ __global__ void __launch_bounds__(256) attn_lc_combine_kernel(AttnLcParams p, vo
     const int gi = w & 7, rr = (w >> 3) % rows, kvh_i = (w >> 3) / rows;
     const int m = rr / gqa, jj = rr % gqa, grp = jj / p.hpg, r = m * p.hpg + jj % p.hpg;
     const int cta0 = (kvh_i * p.G + grp) * p.S;
+    // The splits' {max, sum} are spread over the lanes (32 splits per round); each lane's weight
+    // then reaches the whole warp by shuffle, so the partial-output loads are independent and
+    // four stay in flight. Empty splits (sum 0) never wrote a partial output and are skipped.
     float mx = -INFINITY;
-    for (int s = 0; s < p.S; ++s) {
-        const float2 ml = p.ml[(size_t)(cta0 + s) * p.N + r];
-        if (ml.y > 0.f) mx = fmaxf(mx, ml.x);
+    for (int s0 = 0; s0 < p.S; s0 += 32) {
+        const int s = s0 + lane;
+        if (s < p.S) {
+            const float2 ml = p.ml[(size_t)(cta0 + s) * p.N + r];
+            if (ml.y > 0.f) mx = fmaxf(mx, ml.x);
+        }
     }
+    mx = warp_max(mx);
     float n0 = 0.f, n1 = 0.f, den = 0.f;
-    for (int s = 0; s < p.S; ++s) {
-        const float2 ml = p.ml[(size_t)(cta0 + s) * p.N + r];
-        if (ml.y <= 0.f) continue;
-        const float wgt = expf(ml.x - mx);
-        const float2 o = __ldcg(reinterpret_cast<const float2*>(p.part + ((size_t)(cta0 + s) * p.N + r) * kLcHd +
-                                                               gi * 64 + 2 * lane));
-        n0 += wgt * o.x;
-        n1 += wgt * o.y;
-        den += wgt * ml.y;
+    const float* col = p.part + (size_t)r * kLcHd + gi * 64 + 2 * lane;
+    for (int s0 = 0; s0 < p.S; s0 += 32) {
+        const int s = s0 + lane;
+        float w = 0.f, lw = 0.f;
+        if (s < p.S) {
+            const float2 ml = p.ml[(size_t)(cta0 + s) * p.N + r];
+            if (ml.y > 0.f) {
+                w = expf(ml.x - mx);
+                lw = w * ml.y;
+            }
+        }
+        den += warp_sum(lw);
+        const int cnt = min(32, p.S - s0);
+        for (int j = 0; j < cnt; j += 4) {
+            float wj[4];
+            float2 o[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                wj[u] = __shfl_sync(0xffffffffu, w, (j + u) & 31);
+                o[u] = make_float2(0.f, 0.f);
+                if (j + u < cnt && wj[u] != 0.f)
+                    o[u] = __ldcg(reinterpret_cast<const float2*>(col + (size_t)(cta0 + s0 + j + u) * p.N * kLcHd));
+            }
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                if (j + u >= cnt) wj[u] = 0.f;
+                n0 = fmaf(wj[u], o[u].x, n0);
+                n1 = fmaf(wj[u], o[u].y, n1);
+            }
+        }
     }
     const float inv = den > 0.f ? 1.0f / den : 0.f;
     const int K = p.qh * kLcHd;
