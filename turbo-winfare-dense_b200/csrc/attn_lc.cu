@@ -402,27 +402,37 @@ __global__ void __launch_bounds__(kLcThreads, 1)
                     c.corr[tid] = mn == mo ? 1.f : expf(mo - mn);  // 0 while nothing was seen
                     if (t > 0 && mn != mo) c.changed = 1;
                 }
-                // P^T reuses one buffer: the previous tile's P V must be complete (this also
-                // orders the O^T rescale below after it).
+                sm_bar();
+                const bool rescale = c.changed != 0;
+                // P and its row sums need only this tile's scores: they are computed while the
+                // previous tile's P V may still run. Only the stores into the single P^T buffer
+                // and the O^T rescale wait for it.
+#pragma unroll
+                for (int j = 0; j < 24; ++j) {
+                    const int r = r0 + j;
+                    float pr = 0.f;
+                    if (active && r < N && s[j] != -INFINITY) pr = expf(s[j] - c.m_new[r]);
+                    const uint16_t h1 = bf16_bits(pr), h2 = bf16_bits(pr - bf16_val(h1));
+                    s[j] = pr;
+                    red[j] = bf16_val(h1) + bf16_val(h2);
+                }
+                reduce_scatter24<false>(red, lane);
+                if (active && (lane & 3) == 0)
+#pragma unroll
+                    for (int i = 0; i < 3; ++i) c.red[qd][rs0 + i] = red[i];
                 ok = sm_bar_and(ok && (t == 0 || lc_wait(&c.o_done, (t - 1) & 1, abort, p.err)));
                 if (!ok) break;
                 tc::fence_after_sync();
-                const bool rescale = c.changed != 0;
                 if (active) {
 #pragma unroll
                     for (int j = 0; j < 24; ++j) {
                         const int r = r0 + j;
                         if (r >= N) break;
-                        const float pr = s[j] == -INFINITY ? 0.f : expf(s[j] - c.m_new[r]);
-                        const uint16_t h1 = bf16_bits(pr), h2 = bf16_bits(pr - bf16_val(h1));
+                        const uint16_t h1 = bf16_bits(s[j]), h2 = bf16_bits(s[j] - bf16_val(h1));
                         const uint32_t off = sw128_off(r, col);
                         *reinterpret_cast<uint16_t*>(pt + (size_t)(0 * 2 + kb) * N * 128 + off) = h1;
                         *reinterpret_cast<uint16_t*>(pt + (size_t)(1 * 2 + kb) * N * 128 + off) = h2;
-                        red[j] = bf16_val(h1) + bf16_val(h2);
                     }
-                } else {
-#pragma unroll
-                    for (int j = 0; j < 24; ++j) red[j] = 0.f;
                 }
                 if (rescale) {
                     // This warp's two O^T tiles (dims 128 ci .. +127, lane = dim) times corr[row].
@@ -441,12 +451,6 @@ __global__ void __launch_bounds__(kLcThreads, 1)
                             }
                     tc::wait_st();
                 }
-                // Row sums of the P that the MMA multiplies (both terms).
-                reduce_scatter24<false>(red, lane);
-                if (active && (lane & 3) == 0)
-#pragma unroll
-                    for (int i = 0; i < 3; ++i) c.red[qd][rs0 + i] = red[i];
-                sm_bar();
                 if (tid < N) {
                     c.l_run[tid] = c.l_run[tid] * c.corr[tid] + (c.red[0][tid] + c.red[1][tid]) + (c.red[2][tid] + c.red[3][tid]);
                     c.m_run[tid] = c.m_new[tid];
