@@ -398,6 +398,17 @@ def long_context(args, eng_factory, nccl_id):
                            "acceptance": s["accepted"] / max(1.0, s["drafted"])}
     out["verify_pass_ms_at_30000"] = eng.time_pass(0, 9, 3, pos=30000)
     eng.close()
+    if args.gpus == 1:
+        # The same pass with the full-attention layers on the cluster attention kernel instead of
+        # the tensor-core long-context one (G4DENSE_ATTN_LC=0 is read when the engine loads).
+        gc.collect()
+        os.environ["G4DENSE_ATTN_LC"] = "0"
+        try:
+            ref = eng_factory(None)
+            out["verify_pass_ms_at_30000_cluster_attention"] = ref.time_pass(0, 9, 3, pos=30000)
+            ref.close()
+        finally:
+            del os.environ["G4DENSE_ATTN_LC"]
     return out
 
 
