@@ -7,9 +7,11 @@ verify-batch attention in long-context mode (bf16 KV, head_dim 512).
   max (top-1 and top-5 exact where the margins allow). The split count is forced down (1 and 3)
   so each CTA runs several 128-key tiles (the double-buffered scores, the output accumulated
   across tiles, the rescale when a row's maximum rises), and left at its natural value.
-* Against the cluster kernel (`csrc/attention.cu`) at the 31B's real shapes: a 6-layer cut with
-  an 8 192-token bf16 context, verify batches of 9, 1 and 16 rows; the two kernels' logits agree
-  to 2e-3 of the row's max.
+* Prefill chunks of 17..128 rows (blocks of up to 48 positions of one query head) against the
+  oracle: each chunk's last-row logits and the verify rows that read the keys the chunks wrote.
+* Against the cluster kernel (`csrc/attention.cu`) at the 31B's real shapes: a 6-layer cut whose
+  8 192-token bf16 context is prefilled in 128-row chunks, then verify batches of 9, 1 and 16
+  rows; the two kernels' logits agree to 2e-3 of the row's max.
 """
 from __future__ import annotations
 
@@ -82,3 +84,33 @@ def test_lc_matches_cluster_kernel_31b_long_context(built_lib, monkeypatch):
         for i in range(m):
             worst = max(worst, check_logits(b[i], a[i], f"batch {m} row {i}", tol=2e-3))
     print(f"tensor-core vs cluster attention at {ctx} keys: worst |diff| / max |logit| = {worst:.2e}")
+
+
+@pytest.mark.parametrize("splits", [1, 0])
+def test_lc_prefill_chunks_match_oracle(built_lib, geom31, monkeypatch, splits):
+    """Prefill chunks of 17..128 rows: the rows run as blocks of up to 48 positions of one query
+    head, each with its own causal key limit; the chunk's last-row logits and the verify rows that
+    follow (reading the keys the chunks wrote) against the oracle."""
+    from g4dense_b200 import Engine
+    monkeypatch.setenv("G4DENSE_ATTN_LC", "1")
+    if splits:
+        monkeypatch.setenv("G4DENSE_ATTN_LC_SPLITS", str(splits))
+    path = geom31["baseline"]
+    e = Engine(target=path, max_context=1024, kv_bf16=True)
+    ref = O.RestatedModel(path, max_ctx=1024, kv_mode=O.KV_BF16)
+    toks = np.random.default_rng(33).integers(0, 4096, 700)
+    want = [ref.forward(int(t), p) for p, t in enumerate(toks)]
+    pos, worst = 0, 0.0
+    for m in [128, 17, 100, 64, 9, 128, 49, 5, 96, 16, 88]:
+        m = min(m, len(toks) - pos)
+        if m > 16:
+            got = e.forward_batch(toks[pos:pos + m], pos, vocab=4096, all_positions=False)
+            worst = max(worst, check_logits(got[0], want[pos + m - 1], f"prefill chunk at {pos} (rows {m})"))
+        else:
+            got = e.forward_batch(toks[pos:pos + m], pos, vocab=4096, all_positions=True)
+            for i in range(m):
+                worst = max(worst, check_logits(got[i], want[pos + i], f"position {pos + i} (batch {m})"))
+        pos += m
+    assert pos == len(toks)
+    e.close()
+    print(f"prefill chunks, splits {splits or 'natural'}: worst |diff| / max |logit| = {worst:.2e}")

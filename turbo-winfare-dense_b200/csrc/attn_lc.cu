@@ -2,9 +2,11 @@
 // 5th-generation tensor cores: Attention.hlsl (shaders/Attention.hlsl:65-179) for verify
 // batches of up to 16 rows at tens of thousands of cached keys, where the KV read dominates.
 //
-// Grid: one CTA per (key split, query-head group, KV head); S splits share the batch's key range
-// [0, base + M) in 128-key tiles. A group is gqa / G query heads of the KV head, so a CTA holds
-// N <= 48 query rows (row r = m * heads + j), and every K/V tile it loads serves all of them.
+// Grid: one CTA per (key split, row group, KV head). A row group is gqa / G query heads of the
+// KV head over the batch's positions (verify batches, up to 48 rows: row r = m * heads + j) or,
+// for a prefill chunk, one query head over a block of up to 48 consecutive positions. S splits
+// share the group's key range [0, base + its last position] in 128-key tiles, and every K/V tile
+// a CTA loads serves all of its rows.
 // Per tile, with warp roles:
 //   * warp 0 (one thread) streams the tile's K, then the previous tile's V, through a ring of
 //     three 32 KB slots: each slot is two TMA tensor copies of 128 keys x 64 dims in the
@@ -20,7 +22,8 @@
 //     O^T in TMEM before the tile's P V is issued;
 //   * warps 2..11 stage the query terms first.
 // Each CTA writes its unnormalised O and {max, sum} per row; a second kernel combines the splits
-// (the softmax-weighted sum) and writes the o-projection's B fragments.
+// (the softmax-weighted sum) and writes the o-projection's B fragments (the wide layout for a
+// prefill chunk).
 //
 // Row m of the batch sits at position base + m and sees keys [0, base + m]. Every wait is bounded
 // (2 s); a CTA that gives up records kErrAttnLc in the error word and leaves.
@@ -167,17 +170,18 @@ __global__ void __launch_bounds__(kLcThreads, 1)
     volatile int* abort = &c.abort;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int split = blockIdx.x, grp = blockIdx.y, kvh_i = blockIdx.z;
-    const int N = p.N, hpg = p.hpg, R = p.M * hpg;
+    const int split = blockIdx.x, grp = blockIdx.y / p.BM, kvh_i = blockIdx.z;
+    const int m0 = (blockIdx.y % p.BM) * p.mb, mcnt = min(p.M - m0, p.mb);  // this group's positions
+    const int N = p.N, hpg = p.hpg, R = mcnt * hpg;
     const int gqa = p.qh / p.kvh;
     // base_pos stays fixed during a pass (only a pass's last kernel writes it), so it is read
     // before waiting on the producer of the query rows.
     const int base = p.sp->base_pos;
-    const int kmax = base + p.M;
+    const int kmax = base + m0 + mcnt;  // the group's last row sees keys up to base + m0 + mcnt - 1
     const int per = ((kmax + p.S - 1) / p.S + kLcKeys - 1) / kLcKeys * kLcKeys;
     const int ks = split * per, ke = min(kmax, ks + per);
     const int T = ks < ke ? (ke - ks + kLcKeys - 1) / kLcKeys : 0;
-    const int cta = (kvh_i * p.G + grp) * p.S + split;
+    const int cta = (kvh_i * p.G * p.BM + (int)blockIdx.y) * p.S + split;
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < kLcSlots; ++s) {
@@ -308,7 +312,7 @@ __global__ void __launch_bounds__(kLcThreads, 1)
         for (int r = warp - 2; r < N; r += kLcStageWarps) {
             float x[16];
             if (r < R) {
-                const int m = r / hpg, qhead = kvh_i * gqa + grp * hpg + r % hpg;
+                const int m = m0 + r / hpg, qhead = kvh_i * gqa + grp * hpg + r % hpg;
                 const float4* src = reinterpret_cast<const float4*>(p.q + ((size_t)m * p.qh + qhead) * kLcHd) + 4 * lane;
 #pragma unroll
                 for (int i = 0; i < 4; ++i) {
@@ -377,12 +381,12 @@ __global__ void __launch_bounds__(kLcThreads, 1)
                 if (lane == 0) mbar_arrive(&c.s_free[b]);
                 // Masked, scaled scores. A tile below every row's last key and inside the split
                 // needs the row check only.
-                const bool inside = kt + kLcKeys <= ke && kt + kLcKeys - 1 <= base;
+                const bool inside = kt + kLcKeys <= ke && kt + kLcKeys - 1 <= base + m0;
                 float red[24];
 #pragma unroll
                 for (int j = 0; j < 24; ++j) {
                     const int r = r0 + j;
-                    const bool valid = r < R && (inside || (key < ke && key <= base + r / hpg));
+                    const bool valid = r < R && (inside || (key < ke && key <= base + m0 + r / hpg));
                     s[j] = valid ? s[j] * p.scale : -INFINITY;
                     red[j] = s[j];
                 }
@@ -504,8 +508,9 @@ __global__ void __launch_bounds__(256) attn_lc_combine_kernel(AttnLcParams p, vo
     const int w = blockIdx.x * 8 + warp;
     if (w >= p.kvh * rows * 8) return;  // warp-uniform
     const int gi = w & 7, rr = (w >> 3) % rows, kvh_i = (w >> 3) / rows;
-    const int m = rr / gqa, jj = rr % gqa, grp = jj / p.hpg, r = m * p.hpg + jj % p.hpg;
-    const int cta0 = (kvh_i * p.G + grp) * p.S;
+    const int m = rr / gqa, jj = rr % gqa, grp = jj / p.hpg, mbk = m / p.mb;
+    const int r = (m - mbk * p.mb) * p.hpg + jj % p.hpg;
+    const int cta0 = (kvh_i * p.G * p.BM + grp * p.BM + mbk) * p.S;
     // The splits' {max, sum} are spread over the lanes (32 splits per round); each lane's weight
     // then reaches the whole warp by shuffle, so the partial-output loads are independent and
     // four stay in flight. Empty splits (sum 0) never wrote a partial output and are skipped.
@@ -554,7 +559,16 @@ __global__ void __launch_bounds__(256) attn_lc_combine_kernel(AttnLcParams p, vo
     const int K = p.qh * kLcHd;
     const BFragView bv = bfrag_view(bfrag, (K + 127) / 128 * 128, p.M);
     const int qhead = kvh_i * gqa + jj;
-    bfrag_store_group(bv, p.M, m, (qhead * kLcHd) / 64 + gi, n0 * inv, n1 * inv, stage[warp]);
+    if (p.M > kMaxM) {
+        // Prefill rows: one static scale per row. Every output is a convex combination of cached
+        // V rows, and V is RMS-normalised without a weight, so |o| <= sqrt(head_dim) (times the
+        // cache's rounding, well inside 1.01).
+        const float wide_e = wide_row_scale(sqrtf((float)kLcHd) * 1.01f);
+        wide_store_group(bv, m, (qhead * kLcHd) / 64 + gi, n0 * inv, n1 * inv, 1.0f / wide_e);
+        if (lane == 0 && qhead == 0 && gi == 0) bv.erow[m] = wide_e;
+    } else {
+        bfrag_store_group(bv, p.M, m, (qhead * kLcHd) / 64 + gi, n0 * inv, n1 * inv, stage[warp]);
+    }
 }
 
 int sm_count() {
@@ -568,25 +582,39 @@ int sm_count() {
     return n;
 }
 
-int splits_for(int kvh, int G) { return std::max(1, sm_count() / std::max(1, kvh * G)); }
+int splits_for(int kvh, int groups) { return std::max(1, sm_count() / std::max(1, kvh * groups)); }
+
+// Row groups of a batch of M rows: the fewest head groups whose rows (M x heads) fit a CTA; a
+// prefill chunk too long for that takes one head per group over blocks of 48 positions.
+struct LcShape {
+    int G, BM, mb;
+};
+bool lc_shape(int M, int gqa, LcShape& sh) {
+    if (M < 1 || M > kPrefillRows || gqa < 1) return false;
+    for (int G = 1; G <= gqa; ++G)
+        if (gqa % G == 0 && M * (gqa / G) <= kLcMaxN) {
+            sh = {G, 1, M};
+            return true;
+        }
+    sh = {gqa, (M + kLcMaxN - 1) / kLcMaxN, kLcMaxN};
+    return true;
+}
 
 }  // namespace
 
 int attn_lc_groups(int M, int gqa) {
-    if (M < 1 || M > kMaxM || gqa < 1) return 0;
-    for (int G = 1; G <= gqa; ++G)
-        if (gqa % G == 0 && M * (gqa / G) <= kLcMaxN) return G;
-    return 0;
+    LcShape sh;
+    return lc_shape(M, gqa, sh) ? sh.G * sh.BM : 0;
 }
 
 void attn_lc_scratch(int qh, int kvh, size_t* part_bytes, size_t* ml_bytes) {
     size_t pb = 0, mb = 0;
     const int gqa = qh / kvh;
-    for (int M = 1; M <= kMaxM; ++M) {
-        const int G = attn_lc_groups(M, gqa);
-        if (!G) continue;
-        const int N = (M * (gqa / G) + 15) / 16 * 16;
-        const size_t ctas = (size_t)kvh * G * splits_for(kvh, G);
+    for (int M = 1; M <= kPrefillRows; ++M) {
+        LcShape sh;
+        if (!lc_shape(M, gqa, sh)) continue;
+        const int N = (std::min(M, sh.mb) * (gqa / sh.G) + 15) / 16 * 16;
+        const size_t ctas = (size_t)kvh * sh.G * sh.BM * splits_for(kvh, sh.G * sh.BM);
         pb = std::max(pb, ctas * N * kLcHd * sizeof(float));
         mb = std::max(mb, ctas * N * sizeof(float2));
     }
@@ -625,8 +653,10 @@ cudaError_t make_kv_tmap(KvTmap* out, const uint16_t* ring, int hd, int kvh, int
 cudaError_t attention_lc(const AttnArgs& a, const KvTmap& k, const KvTmap& v, float* part, float2* ml, int* err,
                          void* bfrag, cudaStream_t st, bool pdl) {
     if (a.hd != kLcHd || a.window != 0 || !a.kv_bf16 || a.kvh < 1 || a.qh % a.kvh) return cudaErrorInvalidValue;
-    const int gqa = a.qh / a.kvh, G = attn_lc_groups(a.M, gqa);
-    if (!G) return cudaErrorInvalidValue;
+    const int gqa = a.qh / a.kvh;
+    LcShape sh;
+    if (!lc_shape(a.M, gqa, sh)) return cudaErrorInvalidValue;
+    const int G = sh.G;
     AttnLcParams p{};
     p.q = a.q;
     p.sp = a.sp;
@@ -637,12 +667,14 @@ cudaError_t attention_lc(const AttnArgs& a, const KvTmap& k, const KvTmap& v, fl
     p.qh = a.qh;
     p.kvh = a.kvh;
     p.G = G;
-    p.S = splits_for(a.kvh, G);
+    p.BM = sh.BM;
+    p.mb = sh.mb;
+    p.S = splits_for(a.kvh, G * sh.BM);
     // G4DENSE_ATTN_LC_SPLITS lowers the split count (never raises it past what the scratch
     // holds), so a moderate context still gives each CTA several tiles.
     if (const char* f = std::getenv("G4DENSE_ATTN_LC_SPLITS"); f && std::atoi(f) > 0) p.S = std::min(p.S, std::atoi(f));
     p.hpg = gqa / G;
-    p.N = (a.M * p.hpg + 15) / 16 * 16;
+    p.N = (std::min(a.M, sh.mb) * p.hpg + 15) / 16 * 16;
     p.scale = a.scale;
     static bool attr = false;
     if (!attr) {
@@ -654,7 +686,8 @@ cudaError_t attention_lc(const AttnArgs& a, const KvTmap& k, const KvTmap& v, fl
     CUtensorMap km, vm;
     std::memcpy(&km, &k, sizeof(km));
     std::memcpy(&vm, &v, sizeof(vm));
-    cudaError_t e = launch(attn_lc_kernel, dim3(p.S, G, a.kvh), dim3(kLcThreads), kLcSmemBytes, st, pdl, km, vm, p);
+    cudaError_t e =
+        launch(attn_lc_kernel, dim3(p.S, G * sh.BM, a.kvh), dim3(kLcThreads), kLcSmemBytes, st, pdl, km, vm, p);
     if (e != cudaSuccess) return e;
     const int warps = a.kvh * a.M * gqa * 8;
     return launch(attn_lc_combine_kernel, dim3((warps + 7) / 8), dim3(256), 0, st, pdl, p, bfrag);

@@ -701,7 +701,11 @@ void DeviceModel::enqueue_prefill(int M, bool want_logits) {
         aa.window = L.geo.is_global ? 0 : (int)h_.sliding_window;
         aa.kv_bf16 = opt_.kv_bf16;
         aa.scale = 1.0f;
-        cuda_check(g4b_attention(aa, bf_attn_, stream_, pdl), "attention");
+        if (L.lc && attn_lc_groups(M, L.qh / L.kvh))
+            cuda_check(attention_lc(aa, L.k_tmap, L.v_tmap, lc_part_, lc_ml_, err_dev_, bf_attn_, stream_, pdl),
+                       "attention_lc");
+        else
+            cuda_check(g4b_attention(aa, bf_attn_, stream_, pdl), "attention");
         float* yo = opt_.tp > 1 ? tp_out(0) : y_;
         pgemm(L.o, bf_attn_, M, yo);
         cuda_check(g4b_rowepi(GemmOut{PartView{}, yo, d}, tp_gather(2 * (int)l, 0), hres_[cur], hres_[1 - cur],

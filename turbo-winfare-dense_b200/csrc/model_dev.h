@@ -197,7 +197,8 @@ struct AttnLcParams {
     float2* ml;              // [kvh][G][S][N] {max, sum} per row
     int* err;
     int M, qh, kvh;
-    int G, S, N, hpg;        // groups per KV head, key splits, rows per CTA (padded), heads per group
+    int G, S, N, hpg;        // head groups per KV head, key splits, rows per CTA (padded), heads per group
+    int BM, mb;              // position blocks (prefill chunks) and positions per block
     float scale;
 };
 
