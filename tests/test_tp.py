@@ -13,7 +13,9 @@ a 0.25 mismatch rate (accepts and rejects mixed); a 300-token prompt that also r
 tensor-core prefill (chunks of 128, 128 and 44 rows) under TP; and temperature-0.8 speculative
 decoding with rejection sampling, whose verify logits are all-gathered from the ranks' vocabulary
 slices before the reference's acceptance test runs (BASELINE-distribution weights, which the GPU
-reproduces to ~1e-5, with a near drafter so that drafts are both accepted and rejected)."""
+reproduces to ~1e-5, with a near drafter so that drafts are both accepted and rejected). The
+long-context attention (tensor cores, bf16 KV, head_dim 512 full-attention layer) also runs under
+TP, on the 31B attention geometry, its logits compared with the oracle's."""
 from __future__ import annotations
 
 import json
@@ -119,3 +121,36 @@ def test_tp_streams_match_oracle(built_lib, config0, tp_model, tmp_path, world, 
         assert [tuple(x) for x in got["rounds"]] == [tuple(x) for x in want_rounds], f"rank {rank} rounds"
     print(f"TP={world} {case} prompt {len(prompt)}: compared {len(want_tokens)} tokens and {len(want_rounds)} "
           f"rounds on each of {world} ranks")
+
+
+@pytest.mark.parametrize("world", [2, 4])
+def test_tp_long_context_attention_matches_oracle(built_lib, geom31, tmp_path, world):
+    """The 31B attention geometry at toy width (head_dim 512 full-attention layer, one KV head,
+    replicated across ranks) with a bf16 KV cache and the tensor-core long-context attention on
+    every rank: prefill chunks and verify batches, logits gathered from the ranks' vocabulary
+    slices, within 2e-2 of the row's max of the oracle's."""
+    if gpu_count() < world:
+        pytest.skip(f"needs {world} GPUs")
+    path = geom31["baseline"]
+    chunks = [128, 128, 100, 9, 16, 128, 51, 1]
+    toks = np.random.default_rng(34).integers(0, 4096, sum(chunks))
+    np.save(tmp_path / "prompt.npy", np.asarray(toks, np.uint32))
+    _run_ranks(world, tmp_path, [str(path), "-", "5", str(tmp_path / "prompt.npy"), "0", str(tmp_path)],
+               {"G4DENSE_ATTN_LC": "1", "G4B_TEST_LC_LOGITS": ",".join(map(str, chunks)), "G4B_TEST_VOCAB": "4096"})
+    ref = O.RestatedModel(path, max_ctx=1024, kv_mode=O.KV_BF16)
+    want = [ref.forward(int(t), p) for p, t in enumerate(toks)]
+    data = np.load(tmp_path / "logits.npz")
+    pos, worst = 0, 0.0
+    for i, m in enumerate(chunks):
+        got = data[f"arr_{i}"]
+        rows = range(m) if m <= 16 else [m - 1]
+        for j, r in enumerate(rows):
+            g, w = got[j], want[pos + r]
+            d = np.abs(g.astype(np.float64) - w).max() / np.abs(w).max()
+            assert np.isfinite(g).all() and d <= 2e-2, f"TP={world} pass {i} row {r}: {d:.3e}"
+            worst = max(worst, d)
+            srt = np.sort(w)
+            if srt[-1] - srt[-2] >= 2e-2 * np.abs(w).max():
+                assert int(np.argmax(g)) == int(np.argmax(w)), f"TP={world} pass {i} row {r}: argmax"
+        pos += m
+    print(f"TP={world} long-context attention: worst |diff| / max |logit| = {worst:.2e}")

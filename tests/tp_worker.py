@@ -4,7 +4,10 @@ argv: target container, drafter container ("-" for none), verify width, prompt (
 ids), tokens to generate, output directory, and optionally a replay stream (.npy) with its
 mismatch rate and seed for the config-3 oracle drafter. G4B_TEST_SAMPLING="temperature,top_p,
 top_k,seed" selects sampled decoding. Writes rank<r>.json with the greedy stream and the
-per-round records."""
+per-round records. G4B_TEST_LC_LOGITS="m1,m2,..." instead feeds the prompt as forward passes of
+those row counts on a bf16-KV engine (max_context 1024) and rank 0 writes logits.npz: each pass's
+logits over G4B_TEST_VOCAB ids (every row of passes up to 16 rows, the last row of a prefill
+chunk)."""
 import json
 import os
 import sys
@@ -33,9 +36,23 @@ def main():
     t = torch.from_numpy(buf).cuda()
     dist.broadcast(t, 0)
     nid = t.cpu().numpy().tobytes()
+    chunks = os.environ.get("G4B_TEST_LC_LOGITS")
+    extra = {"kv_bf16": True, "max_context": 1024} if chunks else {}
     e = Engine(target=target, draft=None if draft == "-" else draft, draft_k=int(width) if draft != "-" else 0,
-               tp_rank=rank, tp_size=world, nccl_id=nid, device=local)
+               tp_rank=rank, tp_size=world, nccl_id=nid, device=local, **extra)
     prompt = np.load(plen)
+    if chunks:
+        vocab, pos, outs = int(os.environ["G4B_TEST_VOCAB"]), 0, []
+        for m in (int(x) for x in chunks.split(",")):
+            outs.append(e.forward_batch(prompt[pos:pos + m], pos, vocab=vocab, all_positions=m <= 16))
+            pos += m
+        e.close()
+        if rank == 0:
+            np.savez(Path(out, "logits.npz"), *outs)
+        Path(out, f"rank{rank}.json").write_text(json.dumps({"tokens": [], "rounds": []}))
+        dist.barrier()
+        dist.destroy_process_group()
+        return
     if len(sys.argv) > 7:
         e.set_gate(0.45, -1)
         e.set_decode_options(replay=np.load(sys.argv[7]), mismatch_rate=float(sys.argv[8]),
