@@ -229,6 +229,13 @@ G4DENSE_API void g4dense_stop_matcher_destroy(void* m);
 G4DENSE_API const char* g4dense_utf8_repair(const char* in, size_t len, int flush_all, size_t* consumed,
                                             size_t* out_len);
 
+/* Checks the header of the container at `path` against the file's size with the rules the
+ * engine's loader applies (the reference's validate_header / validate_mtp_header,
+ * src/format.cpp:6-130, plus what this engine needs to run the model). Needs no GPU and does not
+ * read the payload. Returns 1 for a valid .g4dense, 2 for a valid .g4mtp, or -1 with every broken
+ * rule in g4dense_engine_last_error(). */
+G4DENSE_API int g4dense_container_validate(const char* path);
+
 #ifdef __cplusplus
 }
 #endif

@@ -9,11 +9,13 @@
 #include <cstdlib>
 #include <cstring>
 #include <filesystem>
+#include <fstream>
 #include <memory>
 #include <sstream>
 #include <string>
 #include <vector>
 
+#include "format.h"
 #include "runner.h"
 #include "tokenizer.h"
 
@@ -970,6 +972,38 @@ G4DENSE_API const char* g4dense_utf8_repair(const char* in, size_t len, int flus
     const size_t used = g4b::utf8_repair(std::string_view(in ? in : "", in ? len : 0), flush_all != 0, out);
     if (consumed) *consumed = used;
     return give(buf, std::move(out), out_len);
+}
+
+G4DENSE_API int g4dense_container_validate(const char* path) {
+    clear_error();
+    try {
+        if (!path) throw std::invalid_argument("container path is NULL");
+        std::ifstream f(path, std::ios::binary | std::ios::ate);
+        if (!f) throw g4b::G4DenseFormatError(std::string("cannot open container ") + path);
+        const uint64_t size = static_cast<uint64_t>(f.tellg());
+        unsigned char raw[4096];
+        static_assert(sizeof(raw) == sizeof(g4b::G4DenseHeader) && sizeof(raw) == sizeof(g4b::G4MtpHeader),
+                      "both headers fill one 4096-byte page");
+        if (size < sizeof(raw)) throw g4b::G4DenseFormatError("container file too small for header");
+        f.seekg(0);
+        if (!f.read(reinterpret_cast<char*>(raw), sizeof(raw)))
+            throw g4b::G4DenseFormatError(std::string("cannot read the header of ") + path);
+        uint32_t magic;
+        std::memcpy(&magic, raw, sizeof magic);
+        if (magic == g4b::G4MtpHeader::kMagic) {
+            g4b::G4MtpHeader h;
+            std::memcpy(&h, raw, sizeof h);
+            g4b::validate_mtp_header(h, size);
+            return 2;
+        }
+        g4b::G4DenseHeader h;
+        std::memcpy(&h, raw, sizeof h);
+        g4b::validate_header(h, size);
+        return 1;
+    } catch (const std::exception& e) {
+        set_error(e.what());
+        return -1;
+    }
 }
 
 }  // extern "C"

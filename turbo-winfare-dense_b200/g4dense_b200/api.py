@@ -127,6 +127,7 @@ def _bind_engine(L):
     L.g4dense_stop_matcher_destroy.argtypes = [_vp]
     L.g4dense_utf8_repair.restype = _vp
     L.g4dense_utf8_repair.argtypes = [ctypes.c_char_p, ctypes.c_size_t, ctypes.c_int, _sz, _sz]
+    L.g4dense_container_validate.argtypes = [ctypes.c_char_p]
     L.g4dense_engine_profile_gemms.restype = ctypes.c_double
     L.g4dense_engine_profile_gemms.argtypes = [_vp, ctypes.c_int, ctypes.c_int, ctypes.POINTER(ctypes.c_ulonglong),
                                                ctypes.POINTER(ctypes.c_int)]
@@ -560,3 +561,12 @@ def utf8_repair(data: bytes, flush_all: bool):
     used, n = ctypes.c_size_t(0), ctypes.c_size_t(0)
     p = lib().g4dense_utf8_repair(data, len(data), 1 if flush_all else 0, ctypes.byref(used), ctypes.byref(n))
     return ctypes.string_at(p, n.value), used.value
+
+
+def validate_container(path) -> str:
+    """Checks a container's header against its file with the engine loader's rules (no GPU
+    needed). Returns "g4dense" or "g4mtp"; raises ValueError listing every broken rule."""
+    rc = lib().g4dense_container_validate(str(path).encode())
+    if rc < 0:
+        raise ValueError(lib().g4dense_engine_last_error().decode())
+    return {1: "g4dense", 2: "g4mtp"}[rc]
