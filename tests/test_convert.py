@@ -166,3 +166,24 @@ def test_cli_reports_errors(tmp_path, capsys):
     ack = S.write_checkpoint(tmp_path / "ack", S.assistant_config(mspec), S.assistant_tensors(mspec, 0), prefix="")
     assert V.main(["--assistant", "--input-dir", str(ack), "--output-file", str(tmp_path / "a.g4mtp")]) == 0
     assert (tmp_path / "a.g4mtp").read_bytes() == C.build_mtp_container(mspec, 0)
+
+
+def test_small_chunks_give_the_same_container(tmp_path, monkeypatch):
+    """Tensors are copied in bounded chunks; a chunk far smaller than every tensor (so each is
+    copied in many pieces, ragged last piece included) writes the same bytes."""
+    config, tensors, prefix, shards, _ = CASES["model"]["global_layers_bare_names"]
+    ck = S.write_checkpoint(tmp_path / "ck", config, tensors, prefix, shards)
+    whole = V.convert(ck, tmp_path / "whole.g4dense").read_bytes()
+    monkeypatch.setattr(V._Span, "CHUNK", 1000)
+    assert V.convert(ck, tmp_path / "chunked.g4dense").read_bytes() == whole
+    assert hashlib.sha256(whole).hexdigest() == GOLDEN["model"]["global_layers_bare_names"]["sha256"]
+
+
+def test_shard_shorter_than_its_index_is_refused(tmp_path):
+    spec = C.CONFIG0_DRAFT
+    ck = S.write_checkpoint(tmp_path / "ck", S.gemma4_config(spec), S.gemma4_tensors(spec, 0))
+    shard = next(ck.glob("*.safetensors"))
+    shard.write_bytes(shard.read_bytes()[:-10])
+    with pytest.raises(V.CheckpointError, match="outside shard"):
+        V.convert(ck, tmp_path / "m.g4dense")
+    assert not (tmp_path / "m.g4dense").exists()

@@ -21,8 +21,9 @@ Every block is zero-padded to 4096 bytes and the header holds the payload's SHA-
 
 Tensors are looked up as the reference does (the bare name, then under "model.",
 "language_model." and "model.language_model."), and config.json fields take the same
-per-architecture defaults, so a checkpoint becomes the same container. Shards are streamed tensor
-by tensor and the header is written last, so a 17 GB checkpoint is never held in memory.
+per-architecture defaults, so a checkpoint becomes the same container. Tensor bytes are copied
+from the shards in chunks of at most 64 MiB and hashed on the way; the header is written last. The
+converter's memory use is bounded by one chunk, whatever the checkpoint's size.
 
 The engine itself runs Gemma-4 dense models without per-layer embeddings or shared KV; its loader
 rejects the other containers with the reason (validate_header). Mixture-of-experts checkpoints are
@@ -65,6 +66,29 @@ class CheckpointError(ValueError):
     pass
 
 
+class _Span:
+    """One tensor's bytes inside a shard; copied out in chunks of at most 64 MiB."""
+
+    CHUNK = 64 << 20
+
+    def __init__(self, key: str, path: Path, offset: int, length: int):
+        self.key, self.path, self.offset, self.length = key, path, offset, length
+
+    def __len__(self) -> int:
+        return self.length
+
+    def chunks(self):
+        with open(self.path, "rb") as f:
+            f.seek(self.offset)
+            left = self.length
+            while left:
+                data = f.read(min(left, self.CHUNK))
+                if not data:
+                    raise CheckpointError(f"tensor {self.key}: shard {self.path} ends early")
+                left -= len(data)
+                yield data
+
+
 class _Tensors:
     """The tensors of every shard: name -> (file, absolute byte offset, byte length, shape).
     A name is looked up under each of `prefixes` in turn."""
@@ -76,6 +100,7 @@ class _Tensors:
         if not shards:
             raise CheckpointError(f"no .safetensors shards in {directory}")
         for shard in shards:
+            size = shard.stat().st_size
             with open(shard, "rb") as f:
                 raw = f.read(8)
                 if len(raw) != 8:
@@ -86,6 +111,8 @@ class _Tensors:
                 if name == "__metadata__":
                     continue
                 lo, hi = info["data_offsets"]
+                if not 0 <= lo <= hi or 8 + n + hi > size:
+                    raise CheckpointError(f"tensor {name}: bytes {lo}..{hi} lie outside shard {shard}")
                 self.where[name] = (shard, 8 + n + lo, hi - lo, info["shape"])
 
     def key(self, name):
@@ -101,19 +128,15 @@ class _Tensors:
         k = self.key(name)
         return None if k is None else self.where[k][3]
 
-    def read(self, name, optional=False) -> bytes:
+    def read(self, name, optional=False):
+        """The tensor's bytes as a _Span (b"" for a missing optional tensor)."""
         k = self.key(name)
         if k is None:
             if optional:
                 return b""
             raise CheckpointError(f"tensor {name} is not in the checkpoint")
         path, off, length, _ = self.where[k]
-        with open(path, "rb") as f:
-            f.seek(off)
-            data = f.read(length)
-        if len(data) != length:
-            raise CheckpointError(f"tensor {k}: truncated shard {path}")
-        return data
+        return _Span(k, path, off, length)
 
     def quantized(self, name, scales_optional=True):
         """[packed weight, scales, biases] of one quantized matrix; missing scales/biases are empty."""
@@ -224,12 +247,14 @@ class _BlockWriter:
         f.write(b"\x00" * HEADER_SIZE)
 
     def __call__(self, parts) -> int:
-        """Writes one block, zero-padded to the container alignment; returns its size."""
+        """Writes one block (byte strings and tensor spans), zero-padded to the container
+        alignment; returns its size."""
         n = 0
-        for b in parts:
-            self.f.write(b)
-            self.sha.update(b)
-            n += len(b)
+        for part in parts:
+            for b in (part.chunks() if isinstance(part, _Span) else (part,)):
+                self.f.write(b)
+                self.sha.update(b)
+            n += len(part)
         tail = b"\x00" * ((-n) % ALIGNMENT)
         self.f.write(tail)
         self.sha.update(tail)

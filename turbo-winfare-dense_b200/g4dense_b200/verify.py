@@ -33,9 +33,9 @@ class ContainerError(ValueError):
     pass
 
 
-def _blocks_model(f) -> tuple:
+def _blocks_model(raw: bytes) -> tuple:
     """(kind, fields, [(name, offset, size)], declared digest) of a .g4dense header."""
-    h = struct.unpack(HEADER_FMT, f)
+    h = struct.unpack(HEADER_FMT, raw)
     layers = h[3]
     if not 1 <= layers <= 60:
         raise ContainerError(f"{layers} layers; the header's tables hold 1..60")
@@ -48,8 +48,9 @@ def _blocks_model(f) -> tuple:
     return "g4dense", fields, blocks, h[143], VERSION
 
 
-def _blocks_assistant(f) -> tuple:
-    h = struct.unpack(MTP_HEADER_FMT, f)
+def _blocks_assistant(raw: bytes) -> tuple:
+    """The same for a .g4mtp header."""
+    h = struct.unpack(MTP_HEADER_FMT, raw)
     layers = h[3]
     if not 1 <= layers <= MTP_MAX_LAYERS:
         raise ContainerError(f"{layers} layers; the header's tables hold 1..{MTP_MAX_LAYERS}")
