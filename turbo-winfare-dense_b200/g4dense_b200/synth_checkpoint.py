@@ -242,6 +242,34 @@ def assistant_cases() -> dict:
     }
 
 
+def forward_cases() -> dict:
+    """Checkpoints on which the reference's independent NumPy forward pass
+    (tools/numpy_reference.py) pins converter + oracle: name -> (config, tensors, prompt ids).
+    Zero-mean ("centered") weights, vocabulary 1024 to keep the committed logits small, names
+    under "model." as that tool reads them. The cases: the config-0 shape; full-attention layers
+    (head_dim 128, rotating all 64 pairs, which a partial_rotary_factor of 1.0 tells the NumPy
+    pass); the same with a 4-key sliding window that the prompt wraps twice; and head_dim-512
+    full-attention layers with GQA 2, on the default factor of 0.25 (64 of 256 pairs)."""
+    import dataclasses
+    from .container import CONFIG0_TARGET
+
+    base = dataclasses.replace(CONFIG0_TARGET, vocab_size=1024)
+    glob = dataclasses.replace(base, global_layer_mask=0b1010, global_head_dim=128, global_kv_heads=1)
+    wide = dataclasses.replace(base, num_kv_heads=2, global_layer_mask=0b0100, global_head_dim=512,
+                               global_kv_heads=1)
+    cases = {}
+    for name, spec, seed, prompt, prf in (
+            ("config0_shape", base, 30, [2, 105, 17, 900, 1023, 3], None),
+            ("global_layers", glob, 31, [2, 7, 300, 1000, 55, 9], 1.0),
+            ("window_wrap", dataclasses.replace(glob, sliding_window=4), 32, [2, 7, 300, 1000, 55, 9, 77, 512, 4], 1.0),
+            ("global_hd512_gqa2", wide, 33, [2, 640, 31, 8, 999, 100], None)):
+        cfg = gemma4_config(spec)
+        if prf is not None:
+            cfg["text_config"]["rope_parameters"]["full_attention"]["partial_rotary_factor"] = prf
+        cases[name] = (cfg, gemma4_tensors(spec, seed, centered=True), prompt)
+    return cases
+
+
 def write_checkpoint(directory, config: dict, tensors: dict, prefix: str = "model.language_model.",
                      shards: int = 1) -> Path:
     """Writes config.json and the tensors as `shards` safetensors files (round-robin by name),
