@@ -454,3 +454,80 @@ def read_header(path) -> dict:
     h["layer_sizes"] = list(v[83:143])
     h["global_head_dim"], h["global_kv_heads"] = v[144], v[145]
     return h
+
+
+# ------------------------------------------- the reference's own test fixture (tiny.g4dense)
+
+# Geometry of the fixture the reference's GPU tests run on (tools/make_synthetic_model.py:73-95,
+# Gemma-4 variant): 4 sliding layers, d 256, FFN 512, 4 query heads over 2 KV heads of 64, a
+# 1024-token vocabulary and a 512-key window.
+REFERENCE_TINY = ModelSpec(num_layers=4, d_model=256, d_ff=512, num_q_heads=4, num_kv_heads=2, head_dim=64,
+                           vocab_size=1024, sliding_window=512, global_head_dim=64, global_kv_heads=2)
+
+
+def _bf16_truncated(x: np.ndarray) -> bytes:
+    """float32 -> bf16 by dropping the low 16 bits (the fixture generator truncates; it does not
+    round)."""
+    return (np.ascontiguousarray(x, dtype=np.float32).view(np.uint32) >> 16).astype(np.uint16).tobytes()
+
+
+def minmax_quant_g64(w: np.ndarray) -> bytes:
+    """Affine INT4 G64 by each group's range, as the fixture generator quantizes real-valued
+    weights (tools/make_synthetic_model.py:30-67): scale = (max - min) / 15 (1 where the range is
+    0), bias = min, q = clip(round((w - min) / scale), 0, 15) with round-half-to-even, in float32.
+    Returns the packed words, scales and biases in the container's order."""
+    rows, cols = w.shape
+    g = w.reshape(rows, cols // GROUP, GROUP)
+    lo, hi = g.min(axis=-1, keepdims=True), g.max(axis=-1, keepdims=True)
+    scale = (hi - lo) / np.float32(15.0)
+    scale = np.where(scale == 0, np.float32(1.0), scale).astype(np.float32)
+    q = np.clip(np.round((g - lo) / scale), 0, 15).astype(np.uint32).reshape(rows, cols)
+    words = np.zeros((rows, cols // 8), dtype=np.uint32)
+    for nib in range(8):
+        words |= q[:, nib::8] << np.uint32(4 * nib)
+    return words.tobytes() + _bf16_truncated(scale) + _bf16_truncated(lo)
+
+
+def reference_tiny_container(seed: int = 42) -> bytes:
+    """The reference's tests/fixtures/tiny.g4dense, byte for byte (its generator,
+    tools/make_synthetic_model.py, with the default seed 42 and the Gemma-4 architecture).
+
+    Weights are N(0, 0.02) from the legacy global NumPy generator seeded with `seed`, drawn in
+    this order: the embedding [V][d]; then per layer q, k, v, o, gate, up, down. Each is quantized
+    by minmax_quant_g64. Every norm weight is 1, layer_scalar is 1/sqrt(2L), and both are bf16 by
+    truncation. Blocks follow the container layout and are padded to 4096 bytes. The header also
+    records attn_out_dim = d, qk_scale_factor = output_multiplier = 1 and the per-layer FFN widths."""
+    spec = REFERENCE_TINY
+    rng = np.random.RandomState(seed)
+    d, f, V, L = spec.d_model, spec.d_ff, spec.vocab_size, spec.num_layers
+    qd, kvd = spec.num_q_heads * spec.head_dim, spec.num_kv_heads * spec.head_dim
+
+    def gauss(rows, cols):
+        return (rng.randn(rows, cols).astype(np.float32) * np.float32(0.02)).astype(np.float32)
+
+    ones = lambda n: _bf16_truncated(np.ones(n, dtype=np.float32))  # noqa: E731
+    embed = bytearray(minmax_quant_g64(gauss(V, d)) + ones(d))
+    _pad(embed, ALIGNMENT)
+    scalar = _bf16_truncated(np.array([1.0 / np.sqrt(2.0 * L)], dtype=np.float32))
+    layers = []
+    for _ in range(L):
+        mats = [gauss(qd, d), gauss(kvd, d), gauss(kvd, d), gauss(d, qd), gauss(f, d), gauss(f, d), gauss(d, f)]
+        # the four [d] norms, q_norm and k_norm [head_dim], layer_scalar
+        block = bytearray(ones(d) + ones(d) + ones(d) + ones(d) + ones(spec.head_dim) + ones(spec.head_dim) + scalar)
+        for m in mats:
+            _pad(block, 16)
+            block += minmax_quant_g64(m)
+        _pad(block, ALIGNMENT)
+        layers.append(bytes(block))
+    payload = bytes(embed) + b"".join(layers)
+    offsets, sizes, cur = [0] * 60, [0] * 60, HEADER_SIZE + len(embed)
+    for l, b in enumerate(layers):
+        offsets[l], sizes[l] = cur, len(b)
+        cur += len(b)
+    header = struct.pack(
+        HEADER_FMT, MAGIC, VERSION, QUANT_AFFINE_INT4_G64, L, d, f, spec.num_q_heads, spec.num_kv_heads,
+        spec.head_dim, V, spec.sliding_window, GROUP, 1, 1, 0, spec.rope_theta_local, spec.rope_theta_global, 1.0,
+        spec.softcap, HEADER_SIZE, len(embed), HEADER_SIZE, len(embed), *offsets, *sizes,
+        hashlib.sha256(payload).digest(), spec.global_head_dim, spec.global_kv_heads, 0, 0, 0, 0, 0, 0,
+        *([f] * L + [0] * (60 - L)), 0, d, 1.0, 1.0, b"\x00" * 2696)
+    return header + payload
