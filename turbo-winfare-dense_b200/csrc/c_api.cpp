@@ -51,6 +51,20 @@ const char* give(std::string& buf, std::string s, size_t* out_len) {
     return buf.c_str();
 }
 
+// Runs `body` so that no exception (an allocation failure included) crosses the C ABI: on one,
+// the message goes to the thread's last error and `failed` is returned.
+template <class R, class F>
+R guarded(R failed, F&& body) {
+    try {
+        return body();
+    } catch (const std::exception& e) {
+        set_error(e.what());
+    } catch (...) {
+        set_error("unknown C++ exception");
+    }
+    return failed;
+}
+
 struct EngineHandle {
     std::unique_ptr<g4b::Engine> engine;
     std::unique_ptr<TokHandle> tok;  // null: the text entry points fail
@@ -260,6 +274,10 @@ G4DENSE_API void g4dense_config_default(G4DenseEngineConfig* c) {
 
 G4DENSE_API int g4dense_nccl_unique_id(void* out128) {
     clear_error();
+    if (!out128) {
+        set_error("Null output buffer");
+        return -1;
+    }
 #ifdef G4B_HAVE_NCCL
     ncclUniqueId id;
     if (ncclGetUniqueId(&id) != ncclSuccess) {
@@ -394,10 +412,11 @@ G4DENSE_API void* g4dense_engine_create_ex(const G4DenseEngineConfig* cfg) {
 }
 
 G4DENSE_API void* g4dense_engine_create(const char* container_path) {
+    clear_error();
     G4DenseEngineConfig c;
     g4dense_config_default(&c);
-    const std::string path = (container_path && *container_path) ? container_path : "gemma-4-31b-dense.g4dense";
-    c.container_path = path.c_str();
+    // The default name is a literal, so no allocation is needed for the path.
+    c.container_path = (container_path && *container_path) ? container_path : "gemma-4-31b-dense.g4dense";
     // Speculation is opt-in, as in the reference; these environment variables enable it
     // without changing the signature.
     if (const char* d = std::getenv("G4DENSE_DRAFT_MODEL")) c.draft_path = d;
@@ -611,12 +630,14 @@ G4DENSE_API int g4dense_engine_set_decode_options(void* handle, long long stop_t
         return -1;
     }
     auto* e = static_cast<EngineHandle*>(handle);
-    e->stop_token = stop_token;
-    if (draft_k >= 0) e->draft_k = draft_k;
-    e->replay.assign(replay, replay ? replay + replay_len : replay);
-    e->mismatch_rate = mismatch_rate;
-    e->mismatch_seed = mismatch_seed;
-    return 0;
+    return guarded(-1, [&] {
+        e->replay.assign(replay, replay ? replay + replay_len : replay);
+        e->stop_token = stop_token;
+        if (draft_k >= 0) e->draft_k = draft_k;
+        e->mismatch_rate = mismatch_rate;
+        e->mismatch_seed = mismatch_seed;
+        return 0;
+    });
 }
 
 G4DENSE_API int g4dense_engine_set_device_sampling(void* handle, int on) {
@@ -864,7 +885,7 @@ G4DENSE_API const char* g4dense_tokenizer_decode_single(void* tok, unsigned int 
         return nullptr;
     }
     auto* t = static_cast<TokHandle*>(tok);
-    return give(t->out, t->tok.decode_single(id, skip_special != 0), out_len);
+    return guarded<const char*>(nullptr, [&] { return give(t->out, t->tok.decode_single(id, skip_special != 0), out_len); });
 }
 
 G4DENSE_API const char* g4dense_tokenizer_chat_template(void* tok, const char* messages_json) {
@@ -914,19 +935,19 @@ G4DENSE_API void* g4dense_detokenizer_create(void* tok, int skip_special) {
         set_error("null tokenizer");
         return nullptr;
     }
-    return new DetokHandle(static_cast<TokHandle*>(tok)->tok, skip_special != 0);
+    return guarded<void*>(nullptr, [&] { return new DetokHandle(static_cast<TokHandle*>(tok)->tok, skip_special != 0); });
 }
 
 G4DENSE_API const char* g4dense_detokenizer_push(void* detok, unsigned int id, size_t* out_len) {
     if (!detok) return nullptr;
     auto* d = static_cast<DetokHandle*>(detok);
-    return give(d->out, d->d.push(id), out_len);
+    return guarded<const char*>(nullptr, [&] { return give(d->out, d->d.push(id), out_len); });
 }
 
 G4DENSE_API const char* g4dense_detokenizer_finish(void* detok, size_t* out_len) {
     if (!detok) return nullptr;
     auto* d = static_cast<DetokHandle*>(detok);
-    return give(d->out, d->d.finish(), out_len);
+    return guarded<const char*>(nullptr, [&] { return give(d->out, d->d.finish(), out_len); });
 }
 
 G4DENSE_API void g4dense_detokenizer_destroy(void* detok) { delete static_cast<DetokHandle*>(detok); }
@@ -937,23 +958,26 @@ G4DENSE_API void* g4dense_stop_matcher_create(const char* const* stops, int n) {
         set_error("Invalid arguments");
         return nullptr;
     }
-    std::vector<std::string> v;
-    for (int i = 0; i < n; ++i) v.emplace_back(stops[i] ? stops[i] : "");
-    auto* m = new StopHandle;
-    m->m = g4b::StreamingStopMatcher(std::move(v));
-    return m;
+    return guarded<void*>(nullptr, [&] {
+        std::vector<std::string> v;
+        for (int i = 0; i < n; ++i) v.emplace_back(stops[i] ? stops[i] : "");
+        auto m = std::make_unique<StopHandle>();
+        m->m = g4b::StreamingStopMatcher(std::move(v));
+        return static_cast<void*>(m.release());
+    });
 }
 
 G4DENSE_API const char* g4dense_stop_matcher_push(void* m, const char* text, size_t len, size_t* out_len) {
     if (!m || (!text && len)) return nullptr;
     auto* h = static_cast<StopHandle*>(m);
-    return give(h->out, h->m.push(std::string_view(text ? text : "", len)), out_len);
+    return guarded<const char*>(nullptr,
+                                [&] { return give(h->out, h->m.push(std::string_view(text ? text : "", len)), out_len); });
 }
 
 G4DENSE_API const char* g4dense_stop_matcher_finish(void* m, size_t* out_len) {
     if (!m) return nullptr;
     auto* h = static_cast<StopHandle*>(m);
-    return give(h->out, h->m.finish(), out_len);
+    return guarded<const char*>(nullptr, [&] { return give(h->out, h->m.finish(), out_len); });
 }
 
 G4DENSE_API int g4dense_stop_matcher_stopped(void* m, const char** matched) {
@@ -968,10 +992,12 @@ G4DENSE_API void g4dense_stop_matcher_destroy(void* m) { delete static_cast<Stop
 G4DENSE_API const char* g4dense_utf8_repair(const char* in, size_t len, int flush_all, size_t* consumed,
                                             size_t* out_len) {
     thread_local std::string buf;
-    std::string out;
-    const size_t used = g4b::utf8_repair(std::string_view(in ? in : "", in ? len : 0), flush_all != 0, out);
-    if (consumed) *consumed = used;
-    return give(buf, std::move(out), out_len);
+    return guarded<const char*>(nullptr, [&] {
+        std::string out;
+        const size_t used = g4b::utf8_repair(std::string_view(in ? in : "", in ? len : 0), flush_all != 0, out);
+        if (consumed) *consumed = used;
+        return give(buf, std::move(out), out_len);
+    });
 }
 
 G4DENSE_API int g4dense_container_validate(const char* path) {
