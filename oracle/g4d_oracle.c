@@ -243,10 +243,16 @@ typedef struct {
 
 typedef struct {
     uint32_t hd, qh, kvh, is_global;
+    uint32_t ffn;        /* this layer's FFN width (layer_ffn_width, include/g4dense/format.hpp:189-196) */
+    uint32_t has_v;      /* 0: V is the raw K (a full-attention layer of a model without per-layer inputs) */
+    uint32_t shared;     /* 1: reads the K/V of layer `donor` and has no k, v or k_norm of its own */
+    uint32_t donor;
     const uint16_t *in_norm, *post_attn_norm, *pre_ffn_norm, *post_ffn_norm, *q_norm, *k_norm;
+    const uint16_t* post_ple_norm; /* per-layer-input models only */
     float layer_scalar;
-    qmat q, k, v, o, gate, up, down; /* v.rows == 0 on global layers */
-    float* kcache; /* [max_ctx][kvh*hd] */
+    qmat q, k, v, o, gate, up, down; /* k/v.rows == 0 where absent */
+    qmat ple_gate, ple_proj;         /* [ple_dim][d], [d][ple_dim]; rows == 0 without per-layer inputs */
+    float* kcache; /* [max_ctx][kvh*hd]; NULL on a shared layer */
     float* vcache;
 } layer_t;
 
@@ -259,7 +265,26 @@ struct g4o_model {
     layer_t* layers;
     qmat embed; /* the tied embedding / LM head */
     const uint16_t* final_norm;
+    /* Per-layer inputs (E2B/E4B): the [ple_vocab][L*ple_dim] table, the [L*ple_dim][d]
+     * projection of the token embedding and the bf16 [ple_dim] norm of each layer's slice. */
+    qmat ple_table, ple_model_proj;
+    const uint16_t* ple_norm;
 };
+
+/* is_kv_shared_layer / kv_donor_layer, include/g4dense/format.hpp:210-227: the last
+ * num_kv_shared_layers layers read the cache of the last non-shared layer of their own type. */
+static uint32_t kv_shared_layer(const g4o_header* h, uint32_t l) {
+    return h->num_kv_shared_layers && h->num_kv_shared_layers <= h->num_layers &&
+           l >= h->num_layers - h->num_kv_shared_layers;
+}
+
+static uint32_t kv_donor(const g4o_header* h, uint32_t l) {
+    if (!kv_shared_layer(h, l)) return l;
+    const uint64_t want = (h->global_layer_mask >> l) & 1ull;
+    for (uint32_t d = h->num_layers - h->num_kv_shared_layers; d-- > 0;)
+        if (((h->global_layer_mask >> d) & 1ull) == want) return d;
+    return 0;
+}
 
 /* resolve_layer_geometry, include/g4dense/format.hpp:229-241 */
 static void layer_geo(const g4o_header* h, uint32_t l, layer_t* L) {
@@ -278,6 +303,19 @@ static void layer_geo(const g4o_header* h, uint32_t l, layer_t* L) {
 static const uint8_t* parse_qmat(const uint8_t* layer, const uint8_t* p, uint32_t rows, uint32_t cols,
                                  qmat* q) {
     p += (16u - ((size_t)(p - layer) & 15u)) & 15u;
+    const size_t wb = (size_t)rows * (cols / 8) * 4, sb = (size_t)rows * (cols / 64) * 2;
+    q->w = (const uint32_t*)p;
+    q->s = (const uint16_t*)(p + wb);
+    q->b = (const uint16_t*)(p + wb + sb);
+    q->rows = rows;
+    q->cols = cols;
+    q->cached = NULL;
+    return p + wb + 2 * sb;
+}
+
+/* A quantized matrix stored back to back (W, scales, biases) with no alignment padding, as the
+ * per-layer-input block is (tools/convert_hf_to_g4dense.py:180-190). */
+static const uint8_t* packed_qmat(const uint8_t* p, uint32_t rows, uint32_t cols, qmat* q) {
     const size_t wb = (size_t)rows * (cols / 8) * 4, sb = (size_t)rows * (cols / 64) * 2;
     q->w = (const uint32_t*)p;
     q->s = (const uint16_t*)(p + wb);
@@ -347,10 +385,31 @@ g4o_model* g4o_open(const char* path, int kv_mode, uint32_t max_ctx, int cache_d
     m->embed.cols = d;
     m->embed.cached = NULL;
     m->final_norm = (const uint16_t*)((const uint8_t*)m->embed.b + (size_t)V * (d / 64) * 2);
+    const uint32_t ple = h->ple_dim, ple_rows = h->num_layers * h->ple_dim;
+    if (ple) {
+        /* The per-layer-input block (src/runner.cpp:446-482): the table, the projection, the
+         * norm, back to back. */
+        if (!h->ple_offset || !h->ple_vocab || ple % 64 || h->ple_offset + h->ple_size > m->size) {
+            set_err("g4o_open: invalid per-layer-input block");
+            munmap(p, m->size);
+            free(m);
+            return NULL;
+        }
+        const uint8_t* b = packed_qmat(m->base + h->ple_offset, h->ple_vocab, ple_rows, &m->ple_table);
+        b = packed_qmat(b, ple_rows, d, &m->ple_model_proj);
+        m->ple_norm = (const uint16_t*)b;
+    }
+    (void)f;
     m->layers = (layer_t*)calloc(h->num_layers, sizeof(layer_t));
     for (uint32_t l = 0; l < h->num_layers; ++l) {
         layer_t* L = &m->layers[l];
         layer_geo(h, l, L);
+        L->ffn = (l < 60 && h->layer_d_ff[l]) ? h->layer_d_ff[l] : h->d_ff;
+        L->shared = kv_shared_layer(h, l);
+        L->donor = kv_donor(h, l);
+        /* V has its own projection except on full-attention layers of a model without per-layer
+         * inputs (src/runner.cpp:351-360). */
+        L->has_v = !L->shared && (!L->is_global || ple);
         const uint8_t* lp = m->base + h->layer_offsets[l];
         const uint16_t* n = (const uint16_t*)lp;
         L->in_norm = n;
@@ -358,17 +417,26 @@ g4o_model* g4o_open(const char* path, int kv_mode, uint32_t max_ctx, int cache_d
         L->pre_ffn_norm = n + 2 * d;
         L->post_ffn_norm = n + 3 * d;
         L->q_norm = n + 4 * d;
-        L->k_norm = L->q_norm + L->hd;
-        L->layer_scalar = g4o_bf16_to_f32(*(L->k_norm + L->hd));
-        const uint8_t* q = (const uint8_t*)(L->k_norm + L->hd + 1);
+        n = L->q_norm + L->hd;
+        L->k_norm = L->shared ? NULL : n;
+        if (!L->shared) n += L->hd;
+        L->layer_scalar = g4o_bf16_to_f32(*n++);
+        if (ple) {
+            L->post_ple_norm = n;
+            n += d;
+        }
+        const uint8_t* q = (const uint8_t*)n;
         q = parse_qmat(lp, q, L->qh * L->hd, d, &L->q);
-        q = parse_qmat(lp, q, L->kvh * L->hd, d, &L->k);
-        if (!L->is_global) q = parse_qmat(lp, q, L->kvh * L->hd, d, &L->v);
-        else memset(&L->v, 0, sizeof(qmat));
+        if (!L->shared) q = parse_qmat(lp, q, L->kvh * L->hd, d, &L->k);
+        if (L->has_v) q = parse_qmat(lp, q, L->kvh * L->hd, d, &L->v);
         q = parse_qmat(lp, q, d, L->qh * L->hd, &L->o);
-        q = parse_qmat(lp, q, f, d, &L->gate);
-        q = parse_qmat(lp, q, f, d, &L->up);
-        q = parse_qmat(lp, q, d, f, &L->down);
+        q = parse_qmat(lp, q, L->ffn, d, &L->gate);
+        q = parse_qmat(lp, q, L->ffn, d, &L->up);
+        q = parse_qmat(lp, q, d, L->ffn, &L->down);
+        if (ple) {
+            q = parse_qmat(lp, q, ple, d, &L->ple_gate);
+            q = parse_qmat(lp, q, d, ple, &L->ple_proj);
+        }
         if ((size_t)(q - m->base) > m->size) {
             set_err("g4o_open: layer exceeds file");
             g4o_close(m);
@@ -377,11 +445,17 @@ g4o_model* g4o_open(const char* path, int kv_mode, uint32_t max_ctx, int cache_d
         if (cache_dequant) {
             cache_q(&L->q); cache_q(&L->k); cache_q(&L->v); cache_q(&L->o);
             cache_q(&L->gate); cache_q(&L->up); cache_q(&L->down);
+            cache_q(&L->ple_gate); cache_q(&L->ple_proj);
         }
-        L->kcache = (float*)malloc(sizeof(float) * (size_t)max_ctx * L->kvh * L->hd);
-        L->vcache = (float*)malloc(sizeof(float) * (size_t)max_ctx * L->kvh * L->hd);
+        if (!L->shared) {
+            L->kcache = (float*)malloc(sizeof(float) * (size_t)max_ctx * L->kvh * L->hd);
+            L->vcache = (float*)malloc(sizeof(float) * (size_t)max_ctx * L->kvh * L->hd);
+        }
     }
-    if (cache_dequant) cache_q(&m->embed);
+    if (cache_dequant) {
+        cache_q(&m->embed);
+        cache_q(&m->ple_model_proj);
+    }
     return m;
 }
 
@@ -393,10 +467,12 @@ void g4o_close(g4o_model* m) {
         layer_t* L = &m->layers[l];
         free_q(&L->q); free_q(&L->k); free_q(&L->v); free_q(&L->o);
         free_q(&L->gate); free_q(&L->up); free_q(&L->down);
+        free_q(&L->ple_gate); free_q(&L->ple_proj);
         free(L->kcache);
         free(L->vcache);
     }
     free_q(&m->embed);
+    free_q(&m->ple_model_proj);
     free(m->layers);
     munmap((void*)m->base, m->size);
     free(m);
@@ -447,12 +523,16 @@ int g4o_forward(g4o_model* m, uint32_t token, uint32_t pos, float* logits, float
         if (V < 262144) token %= V;
         else { set_err("Token ID exceeds vocab size"); return -1; }
     }
+    /* gbuf/ubuf hold the widest FFN row, and gbuf also the per-layer-input gate [ple_dim]. */
+    uint32_t widest = f > h->ple_dim ? f : h->ple_dim;
+    for (uint32_t l = 0; l < h->num_layers; ++l)
+        if (m->layers[l].ffn > widest) widest = m->layers[l].ffn;
     float* hidden = (float*)malloc(sizeof(float) * d);
     float* norm = (float*)malloc(sizeof(float) * d);
     float* attn = (float*)malloc(sizeof(float) * d);
     float* ffn = (float*)malloc(sizeof(float) * d);
-    float* gbuf = (float*)malloc(sizeof(float) * f);
-    float* ubuf = (float*)malloc(sizeof(float) * f);
+    float* gbuf = (float*)malloc(sizeof(float) * widest);
+    float* ubuf = (float*)malloc(sizeof(float) * widest);
     float* wn = (float*)malloc(sizeof(float) * d);
 
     /* embedding dequant x sqrt(d): src/cpu_reference.cpp:260-291 */
@@ -460,6 +540,29 @@ int g4o_forward(g4o_model* m, uint32_t token, uint32_t pos, float* logits, float
                  m->embed.b + (size_t)token * (d / 64), 1, d, hidden);
     const float es = sqrtf((float)d);
     for (uint32_t i = 0; i < d; ++i) hidden[i] *= es;
+
+    /* Per-layer inputs, src/runner.cpp:960-1085: the token's row of the per-layer table times
+     * sqrt(ple_dim), plus the projection of the scaled embedding with each layer's ple_dim slice
+     * RMS-normalised (its hidden^-0.5 factor cancels in that norm and is not applied), both
+     * times 2^-0.5. */
+    const uint32_t ple = h->ple_dim, ple_rows = h->num_layers * ple;
+    float* combined = NULL;
+    if (ple) {
+        combined = (float*)malloc(sizeof(float) * ple_rows);
+        float* tokrow = (float*)malloc(sizeof(float) * ple_rows);
+        const uint32_t pt = token % h->ple_vocab;
+        dequant_int4(m->ple_table.w + (size_t)pt * (ple_rows / 8), m->ple_table.s + (size_t)pt * (ple_rows / 64),
+                     m->ple_table.b + (size_t)pt * (ple_rows / 64), 1, ple_rows, tokrow);
+        const float ps = sqrtf((float)ple);
+        for (uint32_t i = 0; i < ple_rows; ++i) tokrow[i] *= ps;
+        qgemv(&m->ple_model_proj, hidden, combined);
+        float* pw = (float*)malloc(sizeof(float) * ple);
+        bf16_vec(m->ple_norm, ple, pw);
+        for (uint32_t l = 0; l < h->num_layers; ++l) rms_norm_f(combined + (size_t)l * ple, pw, ple, 1e-6f, combined + (size_t)l * ple);
+        for (uint32_t i = 0; i < ple_rows; ++i) combined[i] = (combined[i] + tokrow[i]) * 0.70710678118654752f;
+        free(pw);
+        free(tokrow);
+    }
 
     for (uint32_t l = 0; l < h->num_layers; ++l) {
         layer_t* L = &m->layers[l];
@@ -471,13 +574,13 @@ int g4o_forward(g4o_model* m, uint32_t token, uint32_t pos, float* logits, float
         float* kn = (float*)malloc(sizeof(float) * hd);
         float* head_out = (float*)calloc(qrows, sizeof(float));
         bf16_vec(L->q_norm, hd, qn);
-        bf16_vec(L->k_norm, hd, kn);
+        if (!L->shared) bf16_vec(L->k_norm, hd, kn);
 
         bf16_vec(L->in_norm, d, wn);
         rms_norm_f(hidden, wn, d, 1e-6f, norm);
         qgemv(&L->q, norm, qb);
-        qgemv(&L->k, norm, kb);
-        if (!L->is_global) qgemv(&L->v, norm, vb);
+        if (!L->shared) qgemv(&L->k, norm, kb);
+        if (L->has_v) qgemv(&L->v, norm, vb);
 
         const float theta = L->is_global ? h->rope_theta_global : h->rope_theta_local;
         const uint32_t rotated = L->is_global ? 64u : hd / 2;
@@ -486,27 +589,32 @@ int g4o_forward(g4o_model* m, uint32_t token, uint32_t pos, float* logits, float
             rms_norm_f(qv, qn, hd, 1e-6f, qv);
             rope(qv, hd, rotated, theta, pos);
         }
-        for (uint32_t hh = 0; hh < L->kvh; ++hh) {
-            float* kv = kb + (size_t)hh * hd;
-            float* vv = vb + (size_t)hh * hd;
-            /* V = unweighted norm of v, or of RAW k on layers without v_proj (:473-477) */
-            rms_norm_f(L->is_global ? kv : vv, NULL, hd, 1e-6f, vv);
-            rms_norm_f(kv, kn, hd, 1e-6f, kv);
-            rope(kv, hd, rotated, theta, pos);
+        if (!L->shared) {
+            for (uint32_t hh = 0; hh < L->kvh; ++hh) {
+                float* kv = kb + (size_t)hh * hd;
+                float* vv = vb + (size_t)hh * hd;
+                /* V = unweighted norm of v, or of RAW k on layers without v_proj (:473-477) */
+                rms_norm_f(L->has_v ? vv : kv, NULL, hd, 1e-6f, vv);
+                rms_norm_f(kv, kn, hd, 1e-6f, kv);
+                rope(kv, hd, rotated, theta, pos);
+            }
+            /* KV cache at reduced precision (:495-498) */
+            float* kd = L->kcache + (size_t)pos * kvrows;
+            float* vd = L->vcache + (size_t)pos * kvrows;
+            for (uint32_t i = 0; i < kvrows; ++i) {
+                kd[i] = kv_round(m->kv_mode, kb[i]);
+                vd[i] = kv_round(m->kv_mode, vb[i]);
+            }
         }
-        /* KV cache at reduced precision (:495-498) */
-        float* kd = L->kcache + (size_t)pos * kvrows;
-        float* vd = L->vcache + (size_t)pos * kvrows;
-        for (uint32_t i = 0; i < kvrows; ++i) {
-            kd[i] = kv_round(m->kv_mode, kb[i]);
-            vd[i] = kv_round(m->kv_mode, vb[i]);
-        }
+        /* A shared layer attends over its donor's cache, which the donor (an earlier layer of the
+         * same type and geometry) has already written for this position (src/runner.cpp:1240-1250). */
+        const layer_t* C = &m->layers[L->donor];
         const uint32_t total = pos + 1;
         const uint32_t win = L->is_global ? total : (total < h->sliding_window ? total : h->sliding_window);
         float* scores = (float*)malloc(sizeof(float) * win);
         const uint32_t gqa = L->qh / L->kvh;
         for (uint32_t hh = 0; hh < L->qh; ++hh)
-            attend_row(qb + (size_t)hh * hd, L->kcache, L->vcache, L->kvh, hh / gqa, hd,
+            attend_row(qb + (size_t)hh * hd, C->kcache, C->vcache, L->kvh, hh / gqa, hd,
                        total - win, total, 1.0f, scores, head_out + (size_t)hh * hd);
         free(scores);
 
@@ -519,11 +627,25 @@ int g4o_forward(g4o_model* m, uint32_t token, uint32_t pos, float* logits, float
         rms_norm_f(hidden, wn, d, 1e-6f, norm);
         qgemv(&L->gate, norm, gbuf);
         qgemv(&L->up, norm, ubuf);
-        for (uint32_t i = 0; i < f; ++i) gbuf[i] = g4o_gelu_tanh(gbuf[i]) * ubuf[i];
+        for (uint32_t i = 0; i < L->ffn; ++i) gbuf[i] = g4o_gelu_tanh(gbuf[i]) * ubuf[i];
         qgemv(&L->down, gbuf, ffn);
         bf16_vec(L->post_ffn_norm, d, wn);
         rms_norm_f(ffn, wn, d, 1e-6f, ffn);
-        for (uint32_t i = 0; i < d; ++i) hidden[i] = (hidden[i] + ffn[i]) * L->layer_scalar;
+        if (!ple) {
+            for (uint32_t i = 0; i < d; ++i) hidden[i] = (hidden[i] + ffn[i]) * L->layer_scalar;
+        } else {
+            /* The per-layer-input block sits between the FFN residual add and layer_scalar
+             * (src/runner.cpp:1745-1825): gelu(gate . h) * this layer's slice, projected back to d,
+             * normalised, added; the scalar multiplies the sum. */
+            for (uint32_t i = 0; i < d; ++i) hidden[i] = hidden[i] + ffn[i];
+            qgemv(&L->ple_gate, hidden, gbuf);
+            const float* slice = combined + (size_t)l * ple;
+            for (uint32_t i = 0; i < ple; ++i) gbuf[i] = g4o_gelu_tanh(gbuf[i]) * slice[i];
+            qgemv(&L->ple_proj, gbuf, ffn);
+            bf16_vec(L->post_ple_norm, d, wn);
+            rms_norm_f(ffn, wn, d, 1e-6f, ffn);
+            for (uint32_t i = 0; i < d; ++i) hidden[i] = (hidden[i] + ffn[i]) * L->layer_scalar;
+        }
 
         free(qb); free(kb); free(vb); free(qn); free(kn); free(head_out);
     }
@@ -539,7 +661,7 @@ int g4o_forward(g4o_model* m, uint32_t token, uint32_t pos, float* logits, float
         if (cap > 0.0f)
             for (uint32_t v = 0; v < V; ++v) logits[v] = cap * tanhf(logits[v] / cap);
     }
-    free(hidden); free(norm); free(attn); free(ffn); free(gbuf); free(ubuf); free(wn);
+    free(hidden); free(norm); free(attn); free(ffn); free(gbuf); free(ubuf); free(wn); free(combined);
     return 0;
 }
 

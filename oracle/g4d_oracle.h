@@ -8,7 +8,12 @@
  * Differences from the reference's CPU oracle, all additive:
  *   - the KV cache can be truncated (the reference can only append, so callers replay);
  *   - KV rounding mode is selectable (FP16 = the reference; BF16 for the bf16-KV config);
- *   - the speculative loop of src/runner.cpp:2120-2347 is restated over this forward pass.
+ *   - the speculative loop of src/runner.cpp:2120-2347 is restated over this forward pass;
+ *   - per-layer FFN widths, per-layer inputs and layers that read another layer's K/V (the
+ *     E2B/E4B architecture) follow the reference's GPU runner (src/runner.cpp:271-370, 960-1085,
+ *     1240-1336, 1745-1825), which is the only C++ code of the reference that runs them. That
+ *     path is pinned against the reference's NumPy forward pass (tools/numpy_reference.py) on
+ *     synthetic checkpoints; a container without these features takes the unchanged path above.
  */
 #ifndef G4D_ORACLE_H
 #define G4D_ORACLE_H

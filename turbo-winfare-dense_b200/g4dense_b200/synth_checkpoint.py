@@ -8,8 +8,10 @@ must reproduce that container's payload. Quantized matrices are MLX affine INT4 
 `[rows][cols/64]`. Full-attention layers carry no v_proj (their V is the raw K), as in the
 container. `assistant_tensors(spec, seed)` does the same for an MTP assistant drafter and
 `container.build_mtp_container`. `converter_cases()` and `assistant_cases()` are the checkpoints
-the converters are pinned on against the reference's converters. `write_checkpoint` lays any
-tensor dict out as safetensors shards under a name prefix.
+the converters are pinned on against the reference's converters. `e2b_tensors` draws an
+E2B-style model (per-layer inputs, shared-KV layers), and `forward_cases()` lists the
+checkpoints on which the reference's NumPy forward pass pins converter and oracle.
+`write_checkpoint` lays any tensor dict out as safetensors shards under a name prefix.
 """
 from __future__ import annotations
 
@@ -242,6 +244,50 @@ def assistant_cases() -> dict:
     }
 
 
+def e2b_tensors(spec: ModelSpec, ple_dim: int, kv_shared: int, seed: int, wide_shared_ffn: bool = False) -> dict:
+    """Tensors of an E2B-style model: `spec`'s layers plus per-layer inputs of width `ple_dim`
+    (the [vocab][L*ple_dim] table, its projection from the embedding and the slice norm; per layer
+    the gate [ple_dim][d], the projection [d][ple_dim] and their output norm), with the last
+    `kv_shared` layers reading another layer's K/V (no k/v projections, no k_norm). Every layer has
+    its own v (V is the raw K only without per-layer inputs). `wide_shared_ffn` doubles the FFN
+    of the shared layers, as E2B does. Zero-mean weights."""
+    rng = np.random.default_rng(seed)
+    d, L = spec.d_model, spec.num_layers
+
+    def q(name, rows, cols):
+        return quant_tensors(name, *random_quant_block(rng, rows, cols, True))
+
+    out = q("embed_tokens", spec.vocab_size, d)
+    out["norm.weight"] = _bf16(_norm(rng, d))
+    out.update(q("model.embed_tokens_per_layer", spec.vocab_size, L * ple_dim))
+    out.update(q("model.per_layer_model_projection", L * ple_dim, d))
+    out["model.per_layer_projection_norm.weight"] = _bf16(_norm(rng, ple_dim))
+    scalar = f32_to_bf16_bits(np.array([1.0 / np.sqrt(2.0 * L)], dtype=np.float32))
+    for l in range(L):
+        hd, qh, kvh, _ = spec.layer_geometry(l)
+        shared = l >= L - kv_shared
+        ffn = spec.d_ff * (2 if shared and wide_shared_ffn else 1)
+        pre = f"layers.{l}."
+        for n in ("input_layernorm", "post_attention_layernorm", "pre_feedforward_layernorm",
+                  "post_feedforward_layernorm", "post_per_layer_input_norm"):
+            out[pre + n + ".weight"] = _bf16(_norm(rng, d))
+        out[pre + "self_attn.q_norm.weight"] = _bf16(_norm(rng, hd))
+        if not shared:
+            out[pre + "self_attn.k_norm.weight"] = _bf16(_norm(rng, hd))
+        out[pre + "layer_scalar"] = _bf16(scalar)
+        out.update(q(pre + "self_attn.q_proj", qh * hd, d))
+        if not shared:
+            out.update(q(pre + "self_attn.k_proj", kvh * hd, d))
+            out.update(q(pre + "self_attn.v_proj", kvh * hd, d))
+        out.update(q(pre + "self_attn.o_proj", d, qh * hd))
+        out.update(q(pre + "mlp.gate_proj", ffn, d))
+        out.update(q(pre + "mlp.up_proj", ffn, d))
+        out.update(q(pre + "mlp.down_proj", d, ffn))
+        out.update(q(pre + "per_layer_input_gate", ple_dim, d))
+        out.update(q(pre + "per_layer_projection", d, ple_dim))
+    return out
+
+
 def forward_cases() -> dict:
     """Checkpoints on which the reference's independent NumPy forward pass
     (tools/numpy_reference.py) pins converter + oracle: name -> (config, tensors, prompt ids).
@@ -267,6 +313,19 @@ def forward_cases() -> dict:
         if prf is not None:
             cfg["text_config"]["rope_parameters"]["full_attention"]["partial_rotary_factor"] = prf
         cases[name] = (cfg, gemma4_tensors(spec, seed, centered=True), prompt)
+    # E2B-style: per-layer inputs 64 wide and the last two layers sharing K/V. The first is all
+    # sliding with double-wide FFNs on the shared layers; the second alternates sliding and
+    # full-attention layers, so each shared layer takes its own type's donor (layers 2 and 3).
+    six = dataclasses.replace(glob, num_layers=6, global_layer_mask=0b101010)
+    for name, spec, seed, prompt, prf, wide in (
+            ("e2b_ple_shared_kv", base, 34, [2, 686, 824, 23, 827, 480], None, True),
+            ("e2b_ple_shared_kv_global", six, 35, [2, 90, 1, 333, 812, 64, 7], 1.0, False)):
+        cfg = gemma4_config(spec)
+        cfg["text_config"].update(hidden_size_per_layer_input=64, vocab_size_per_layer_input=spec.vocab_size,
+                                  num_kv_shared_layers=2)
+        if prf is not None:
+            cfg["text_config"]["rope_parameters"]["full_attention"]["partial_rotary_factor"] = prf
+        cases[name] = (cfg, e2b_tensors(spec, 64, 2, seed, wide_shared_ffn=wide), prompt)
     return cases
 
 
