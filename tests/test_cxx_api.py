@@ -49,6 +49,17 @@ def test_format_validators(tmp_path):
     assert r.returncode == 0, r.stdout + r.stderr
 
 
+def test_tensor_parallel_shard_plan(tmp_path):
+    """The engine's split of each layer across tp = 1, 2, 4, 8 ranks (csrc/shard.h), on the host."""
+    out = tmp_path / "test_shard"
+    csrc = REPO / "turbo-winfare-dense_b200" / "csrc"
+    r = subprocess.run(["g++", "-std=c++17", "-O1", "-Wall", "-I", str(csrc), str(CPP / "test_shard.cpp"), "-o", str(out)],
+                       capture_output=True, text=True)
+    assert r.returncode == 0, r.stderr[-4000:]
+    r = subprocess.run([str(out)], capture_output=True, text=True)
+    assert r.returncode == 0, r.stdout + r.stderr
+
+
 @pytest.mark.gpu
 def test_cxx_runner_drafter_speculator_match_oracle(cxx_test_bin, config0):
     from g4dense_b200 import container as C

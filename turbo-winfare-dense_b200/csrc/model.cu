@@ -24,6 +24,7 @@
 
 #include "common.cuh"
 #include "pgemm.h"
+#include "shard.h"
 #include "synth.h"
 #include "vgemm.h"
 
@@ -122,26 +123,6 @@ struct RowRange {
     const QPtr* m;
     int r0, n;
 };
-
-// Local shard description of one layer.
-struct Shard {
-    int q0, qh_l, kv0, kvh_l, f0, F_l;
-};
-
-Shard make_shard(const LayerGeometry& g, int F, int rank, int tp) {
-    Shard s;
-    if (g.q_heads % tp) throw std::runtime_error("q_heads must divide by the tensor-parallel size");
-    if (F % tp || (F / tp) % 64) throw std::runtime_error("FFN width / tp must be a multiple of 64");
-    s.qh_l = g.q_heads / tp;
-    s.q0 = rank * s.qh_l;
-    const int gqa = g.q_heads / g.kv_heads;
-    s.kv0 = s.q0 / gqa;
-    s.kvh_l = (s.q0 + s.qh_l - 1) / gqa + 1 - s.kv0;
-    if (s.qh_l % s.kvh_l) throw std::runtime_error("uneven GQA split across ranks");
-    s.F_l = F / tp;
-    s.f0 = rank * s.F_l;
-    return s;
-}
 
 // Host gather of rows (several ranges, concatenated) and a 64-aligned column slice.
 void gather_host(const std::vector<RowRange>& ranges, int col0, int Kl, std::vector<uint32_t>& W,
