@@ -253,7 +253,8 @@ def test_callback_stop_and_telemetry(built_lib, config0):
     assert len(out) == 3 and seen == out.tolist()
     assert lib().g4dense_engine_last_stop_reason(e.h) == 2
     tel = e.telemetry()
-    for key in ("tps", "ttft_ms", "speculative_acceptance_rate", "total_tokens_generated", "kv_cache_mb"):
+    for key in ("tps", "ttft_ms", "speculative_acceptance_rate", "total_tokens_generated", "kv_cache_mb",
+                "pinned_layers", "lm_head_mb", "draft_k", "context_tokens"):
         assert key in tel
     assert lib().g4dense_engine_generate(e.h, b"hello", 4) is None
     assert b"tokenizer" in lib().g4dense_engine_last_error().lower()

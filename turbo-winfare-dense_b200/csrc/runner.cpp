@@ -123,6 +123,7 @@ std::vector<uint32_t> Engine::generate(const std::vector<uint32_t>& prompt, cons
     const uint64_t h0 = T.h2d_bytes() + (draft_ ? draft_->model().h2d_bytes() : 0);
     const uint64_t d0 = T.d2h_bytes() + (draft_ ? draft_->model().d2h_bytes() : 0);
     const bool spec = opt.speculative_enabled && has_drafter() && opt.draft_k > 0;
+    stats_.draft_k = spec ? std::min<uint32_t>(opt.draft_k, kMaxDraftWidth) : 0;
     if (spec && draft_) {
         // The drafter's pass over the prompt is prefill work: queue it on the drafter's stream
         // first so it runs alongside the target's prefill.
@@ -411,6 +412,7 @@ std::vector<uint32_t> Engine::generate(const std::vector<uint32_t>& prompt, cons
     stats_.launches = T.launches() + (draft_ ? draft_->model().launches() : 0) - l0;
     stats_.h2d_bytes += T.h2d_bytes() + (draft_ ? draft_->model().h2d_bytes() : 0) - h0;
     stats_.d2h_bytes += T.d2h_bytes() + (draft_ ? draft_->model().d2h_bytes() : 0) - d0 + out.size() * sizeof(uint32_t);
+    stats_.context_tokens = history.size();
     return out;
 }
 
@@ -432,7 +434,7 @@ std::string Engine::telemetry_json() const {
     ss << "  \"speculative_acceptance_rate\": " << rate << ",\n";
     ss << "  \"max_context\": " << target_->max_context() << ",\n";
     ss << "  \"gpu_name\": \"" << prop.name << "\",\n";
-    ss << "  \"has_draft\": " << (draft_ ? "true" : "false") << ",\n";
+    ss << "  \"has_draft\": " << (draft_ || mtp_ ? "true" : "false") << ",\n";
     ss << "  \"speculative_drafted\": " << s.drafted << ",\n";
     ss << "  \"speculative_accepted\": " << s.accepted << ",\n";
     ss << "  \"drafting_gated\": " << (s.gated ? "true" : "false") << ",\n";
@@ -440,7 +442,12 @@ std::string Engine::telemetry_json() const {
     ss << "  \"kv_cache_mb\": " << (double)target_->kv_bytes() / 1048576.0 << ",\n";
     ss << "  \"layer_mb\": " << (double)target_->weight_bytes() / 1048576.0 / std::max(1u, h.num_layers) << ",\n";
     ss << "  \"total_layers\": " << h.num_layers << ",\n";
+    ss << "  \"pinned_layers\": " << h.num_layers << ",\n";  // every layer is resident in HBM
     ss << "  \"streamed_layers\": 0,\n";
+    ss << "  \"lm_head_mb\": "
+       << ((double)h.vocab_size * h.d_model / 2 + (double)h.vocab_size * (h.d_model / 64) * 4) / 1048576.0 << ",\n";
+    ss << "  \"draft_k\": " << s.draft_k << ",\n";
+    ss << "  \"context_tokens\": " << s.context_tokens << ",\n";
     ss << "  \"speculative_rounds\": " << s.rounds << ",\n";
     ss << "  \"gated_steps\": " << s.gated_steps << ",\n";
     ss << "  \"tensor_parallel\": " << target_->options().tp << ",\n";

@@ -47,6 +47,8 @@ struct GenStats {
     uint64_t launches{0};           // kernels enqueued by this generation (target + drafter)
     uint64_t h2d_bytes{0}, d2h_bytes{0};  // host<->device copies of this generation
     bool gated{false};
+    uint32_t draft_k{0};          // verify width of the speculative rounds (0 without speculation)
+    uint64_t context_tokens{0};   // prompt + emitted tokens held by the KV cache at the end
     std::vector<int> round_info;  // (drafted, accepted, emitted) per verify round
     int stop_reason{0};           // 0 max_tokens, 1 stop token, 2 callback, 3 cancelled
 };
