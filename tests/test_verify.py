@@ -83,3 +83,16 @@ def test_assistant_damage_is_reported(tmp_path):
     _patch(b, 4, struct.pack("<I", 3))
     with pytest.raises(W.ContainerError, match="g4mtp format version 3"):
         W.verify_container(b)
+
+
+def test_per_layer_input_block_is_checked(tmp_path):
+    """A container with per-layer inputs (E2B-style) verifies, and its per-layer-input block is one
+    of the blocks checked: moved off its page, it is reported."""
+    config, tensors, prompt = S.forward_cases()["e2b_ple_shared_kv"]
+    ck = S.write_checkpoint(tmp_path / "ck", config, tensors, prefix="model.")
+    out = V.convert(ck, tmp_path / "e2b.g4dense")
+    assert W.verify_container(out)["kind"] == "g4dense"
+    ple_offset = struct.calcsize("<IIIIIIIIIIIIIIQffffQQQQ60Q60Q32sIIIIII")
+    _patch(out, ple_offset, struct.pack("<Q", struct.unpack_from("<Q", out.read_bytes(), ple_offset)[0] + 8))
+    with pytest.raises(W.ContainerError, match="per-layer-input block starts"):
+        W.verify_container(out)

@@ -3,7 +3,7 @@ tools/verify_assistant_weights.py of the reference check, in one tool that recog
 by its magic word.
 
 * the magic word and format version;
-* each block (the embedding, LM head and per-layer blocks of a model; the embedding, pre-/post-
+* each block (the embedding, LM head, per-layer-input and layer blocks of a model; the embedding, pre-/post-
   projection, norm and layer sections of an assistant) starts on a 4096-byte boundary, is not
   empty and ends inside the file (for a model, as tools/verify_weights.py:52-62 checks its layers);
 * the SHA-256 of everything after the 4096-byte header equals the header's payload digest
@@ -41,6 +41,8 @@ def _blocks_model(raw: bytes) -> tuple:
         raise ContainerError(f"{layers} layers; the header's tables hold 1..60")
     offsets, sizes = h[23:83], h[83:143]
     blocks = [("embedding block", h[19], h[20]), ("LM head block", h[21], h[22])]
+    if h[146]:  # per-layer inputs (E2B/E4B): their block sits between the head and the layers
+        blocks.append(("per-layer-input block", h[150], h[151]))
     blocks += [(f"layer {l}", offsets[l], sizes[l]) for l in range(layers)]
     fields = {"version": h[1], "layers": layers, "d_model": h[4], "d_ff": h[5], "q_heads": h[6], "kv_heads": h[7],
               "head_dim": h[8], "vocab_size": h[9], "sliding_window": h[10], "global_layer_mask": h[14],
