@@ -43,15 +43,17 @@ static G4DenseHeader good() {
     h.quant_group_size = 64;
     h.tied_embeddings = 1;
     h.embed_offset = h.lm_head_offset = 4096;
+    // Each layer's tensors take 536 848 bytes (norms, then q, k, v, o, gate, up, down on 16-byte
+    // boundaries): 140 pages hold them.
     h.layer_offsets[0] = 4096 * 200;
-    h.layer_sizes[0] = 4096 * 10;
-    h.layer_offsets[1] = 4096 * 210;
-    h.layer_sizes[1] = 4096 * 10;
+    h.layer_sizes[0] = 4096 * 140;
+    h.layer_offsets[1] = 4096 * 340;
+    h.layer_sizes[1] = 4096 * 140;
     return h;
 }
 
 int main() {
-    const uint64_t size = 4096 * 220;
+    const uint64_t size = 4096 * 480;
     CHECK(error_of(good(), size).empty());
 
     G4DenseHeader h = good();
@@ -61,9 +63,9 @@ int main() {
     CHECK(e.find("magic") != std::string::npos && e.find("layers") == std::string::npos);
 
     h = good();
-    h.layer_offsets[1] = 4096 * 210 + 8;       // unaligned (still ending inside the file)
-    h.layer_sizes[1] = 4096 * 10 - 8;
-    h.layer_sizes[0] = 4096 * 100;             // past the end of the file
+    h.layer_offsets[1] = 4096 * 340 + 8;       // unaligned (still ending inside the file)
+    h.layer_sizes[1] = 4096 * 140 - 8;
+    h.layer_sizes[0] = 4096 * 1000;            // past the end of the file
     h.quant_group_size = 32;                   // unsupported grouping
     e = error_of(h, size);
     CHECK(e.find("3 problems") != std::string::npos);
@@ -74,6 +76,30 @@ int main() {
     h = good();
     h.layer_offsets[0] = ~0ull - 4095;         // offset + size wraps
     CHECK(error_of(h, size).find("overflows") != std::string::npos);
+
+    // The kernels' per-layer rules, and tensors that must fit in their layer's block.
+    h = good();
+    h.layer_sizes[1] = 4096 * 131;             // 536 576 bytes: 272 short
+    e = error_of(h, size);
+    CHECK(e.find("layer 1 holds 536576 bytes; its tensors need 536848") != std::string::npos);
+    h = good();
+    h.head_dim = 96;
+    CHECK(error_of(h, size).find("head_dim 96") != std::string::npos);
+    h = good();
+    h.d_ff = 1000;
+    CHECK(error_of(h, size).find("FFN width 1000") != std::string::npos);
+    h = good();
+    h.layer_d_ff[1] = 1040;                    // a per-layer width overrides d_ff
+    CHECK(error_of(h, size).find("layer 1: FFN width 1040") != std::string::npos);
+    h = good();
+    h.num_q_heads = 6;
+    h.num_kv_heads = 4;
+    CHECK(error_of(h, size).find("whole groups") != std::string::npos);
+    h = good();
+    h.global_layer_mask = 0b10;                // layer 1 full-attention with head_dim 64
+    h.global_head_dim = 64;
+    h.global_kv_heads = 1;
+    CHECK(error_of(h, size).find("too small for the 64 rotated pairs") != std::string::npos);
 
     G4MtpHeader m;
     std::memset(&m, 0, sizeof m);

@@ -5,7 +5,8 @@ The cases follow the reference's tests/test_format.cpp: a valid model and assist
 accepted; a bad magic word, a block off its 4096-byte page and a file too short for its blocks
 are rejected. Added: the layer-count bounds, the format version, and what this engine refuses to
 run with the reason (Muse-Glimmer, per-layer embeddings, an untied head, another quantization, a
-width that is not whole 64-groups). Several broken rules are reported together.
+width that is not whole 64-groups, a head_dim the kernels lack, a layer block shorter than its
+tensors). Several broken rules are reported together.
 """
 from __future__ import annotations
 
@@ -21,7 +22,7 @@ from g4dense_b200 import synth_checkpoint as S
 # Field indices of struct.unpack(C.HEADER_FMT) and struct.unpack(C.MTP_HEADER_FMT).
 MAGIC, VERSION, QUANT, LAYERS, D_MODEL, D_FF = 0, 1, 2, 3, 4, 5
 GROUP, TIED, EMBED_OFF, LM_OFF, LAYER_OFF, LAYER_SIZE = 11, 13, 19, 21, 23, 83
-PLE_DIM, ARCH = 146, 212
+PLE_DIM, LAYER_D_FF, ARCH = 146, 152, 212
 M_LAYERS, M_HIDDEN, M_PRE_OFF, M_LAYER_OFF = 3, 5, 19, 25
 
 
@@ -94,9 +95,12 @@ F = C.HEADER_FMT
     ({f"f{ARCH}": 1}, ["architecture 1"]),
     ({f"f{PLE_DIM}": 256}, ["per-layer embeddings"]),
     ({f"f{QUANT}": 2, f"f{ARCH}": 1}, ["(2 problems)", "quantization 2", "architecture 1"]),
+    ({f"f{LAYER_SIZE + 1}": 4096}, ["layer 1 holds 4096 bytes; its tensors need"]),
+    ({"f8": 96}, ["head_dim 96"]),
+    ({f"f{LAYER_D_FF}": 1000}, ["layer 0: FFN width 1000"]),  # the per-layer width the engine uses
 ], ids=["magic", "version", "layer_misaligned", "embed_misaligned", "no_layers", "61_layers", "empty_layer",
         "quant_type", "group", "zero_width", "width_not_64", "untied", "lm_head_elsewhere", "muse", "ple",
-        "two_problems"])
+        "two_problems", "layer_too_short", "head_dim", "ffn_width"])
 def test_model_header_rejections(changes, phrases, tmp_path):
     _rejects(_edit(_model(tmp_path), F, **changes), *phrases)
 

@@ -65,6 +65,53 @@ void check_block(Findings& f, const std::string& name, uint64_t offset, uint64_t
                                                  name.c_str(), offset + size, file_size));
 }
 
+// Bytes a layer's tensors take inside its block, in the layout the loader parses
+// (src/cpu_reference.cpp:324-395): the bf16 norms (four [d], q_norm and k_norm [head_dim]) and the
+// layer scalar, then q, k, v (absent on full-attention layers), o, gate, up and down, each starting
+// on a 16-byte boundary of the block with its packed nibbles, bf16 scales and bf16 biases.
+uint64_t layer_payload_bytes(const G4DenseHeader& h, uint32_t l) {
+    const LayerGeometry g = resolve_layer_geometry(h, l);
+    const uint64_t d = h.d_model, F = layer_ffn_width(h, l), hd = g.head_dim;
+    uint64_t n = (4 * d + 2 * hd + 1) * 2;
+    auto matrix = [&n](uint64_t rows, uint64_t cols) {
+        n = (n + 15) / 16 * 16;
+        n += rows * (cols / 8) * 4 + 2 * rows * (cols / 64) * 2;
+    };
+    matrix((uint64_t)g.q_heads * hd, d);
+    matrix((uint64_t)g.kv_heads * hd, d);
+    if (!g.is_global) matrix((uint64_t)g.kv_heads * hd, d);
+    matrix(d, (uint64_t)g.q_heads * hd);
+    matrix(F, d);
+    matrix(F, d);
+    matrix(d, F);
+    return n;
+}
+
+// The per-layer rules of the kernels: attention is built for head dims 64, 128, 256 and 512, a
+// full-attention layer rotates 64 pairs, query heads come in whole GQA groups, and every GEMM's
+// reduction runs over whole 64-wide groups. Then the layer's tensors must fit in its block.
+void check_layers(Findings& f, const G4DenseHeader& h, uint64_t file_size) {
+    for (uint32_t l = 0; l < h.num_layers; ++l) {
+        const LayerGeometry g = resolve_layer_geometry(h, l);
+        const uint32_t F = layer_ffn_width(h, l), hd = g.head_dim;
+        const std::string name = std::string(g.is_global ? "full-attention " : "sliding ") + "layer " + std::to_string(l);
+        bool ok = true;
+        auto rule = [&](bool c, const std::string& problem) {
+            f.expect(c, name + ": " + problem);
+            ok = ok && c;
+        };
+        rule(hd == 64 || hd == 128 || hd == 256 || hd == 512, fmt("head_dim %u; the kernels take 64, 128, 256 or 512", hd));
+        rule(!g.is_global || hd >= 128, fmt("head_dim %u is too small for the 64 rotated pairs", hd));
+        rule(g.kv_heads > 0 && g.q_heads > 0 && g.q_heads % g.kv_heads == 0,
+             fmt("%u query heads do not form whole groups over %u KV heads", g.q_heads, g.kv_heads));
+        rule(F > 0 && F % 64 == 0, fmt("FFN width %u is not a whole number of 64-wide groups", F));
+        if (!ok || file_size == 0) continue;  // the size below is only meaningful for a sound geometry
+        const uint64_t need = layer_payload_bytes(h, l);
+        f.expect(need <= h.layer_sizes[l], fmt("%s holds %" PRIu64 " bytes; its tensors need %" PRIu64, name.c_str(),
+                                               h.layer_sizes[l], need));
+    }
+}
+
 }  // namespace
 
 void validate_header(const G4DenseHeader& h, uint64_t file_size) {
@@ -93,6 +140,9 @@ void validate_header(const G4DenseHeader& h, uint64_t file_size) {
     f.expect(h.tied_embeddings == 1 && h.lm_head_offset == h.embed_offset,
              "the LM head must be the tied embedding table (same block)");
     f.expect(h.d_model % 64 == 0, fmt("d_model %u is not a whole number of 64-wide groups", h.d_model));
+    // The layer rules assume the layout this engine reads (Gemma 4, no per-layer inputs).
+    if (layers_ok && h.arch_type == 0 && h.ple_dim == 0 && h.num_kv_shared_layers == 0 && h.d_model % 64 == 0)
+        check_layers(f, h, file_size);
     if (file_size > 0 && h.d_model % 64 == 0) {
         // Packed nibbles, bf16 scales and biases of the tied table, then the bf16 final norm.
         const uint64_t table = (uint64_t)h.vocab_size * h.d_model / 2 + (uint64_t)h.vocab_size * (h.d_model / 64) * 4 +
