@@ -14,6 +14,8 @@
  *     1240-1336, 1745-1825), which is the only C++ code of the reference that runs them. That
  *     path is pinned against the reference's NumPy forward pass (tools/numpy_reference.py) on
  *     synthetic checkpoints; a container without these features takes the unchanged path above.
+ *
+ * The MTP drafter's restatement (g4o_mtp_*) is the exception to the pinning: parity unpinned.
  */
 #ifndef G4D_ORACLE_H
 #define G4D_ORACLE_H
@@ -71,7 +73,10 @@ void g4o_attention(const float* q, const float* K, const float* V, uint32_t M, u
                    uint32_t kvh, uint32_t hd, uint32_t n_pos, uint32_t window, float scale,
                    float* out);
 
-/* ---- MTP "assistant" drafter (.g4mtp v1; src/mtp_runner.cpp) ---- */
+/* ---- MTP "assistant" drafter (.g4mtp v1; src/mtp_runner.cpp) ----
+ * PARITY UNPINNED: the reference runs its MTP drafter only as Vulkan compute and has no CPU
+ * implementation, golden vectors or known answers for it, so this restatement of
+ * src/mtp_runner.cpp:263-843 is checked against nothing of the reference's own. */
 typedef struct g4o_mtp g4o_mtp;
 g4o_mtp* g4o_mtp_open(const char* path);
 void g4o_mtp_close(g4o_mtp* m);
