@@ -229,19 +229,6 @@ def greedy_margins(path, prompt, tokens):
     return out
 
 
-def check_stream(got, want, margins, noise=0.05):
-    """Greedy streams must be identical until the oracle reaches a near-tie (top-2 margin
-    below the FP16-KV rounding noise, `noise`); a divergence is accepted only there.
-    Returns the number of positions compared."""
-    got, want = [int(t) for t in got], [int(t) for t in want]
-    for i, (a, b) in enumerate(zip(got, want)):
-        if a != b:
-            assert margins[i] < noise, f"stream diverges at {i} where the oracle's margin is {margins[i]:.4f}"
-            return i
-    assert len(got) == len(want), (len(got), len(want))
-    return len(got)
-
-
 def int4_gemm(W, S, B, x):
     """Restated GemmInt4Batch: W u32 [N][K/8], S/B u16 [N][K/64], x f32 [M][K] -> [M][N]."""
     lib = restated_lib()
